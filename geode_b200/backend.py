@@ -1,0 +1,233 @@
+"""Python driver of libgeode_cuda.so's backend (include/geode_cuda.h): adopts a geode-pack's tensors into a gcuda
+handle and exposes verify / keep / accept / state. It mirrors what the C++ host (libgeode_host.so) does for the
+engine; the tests and the benchmark use it to reach the backend from Python. No CPU fallback: every call goes to
+the CUDA library, and a missing library or device raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+from typing import Optional
+
+import numpy as np
+
+from . import cuda_lib
+
+
+class GShape(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_layers", "vocab")] + [("eps", C.c_float)] + \
+               [(n, C.c_int) for n in ("n_heads", "n_kv_heads", "head_dim", "rope_dim")] + [("rope_theta", C.c_float)] + \
+               [(n, C.c_int) for n in ("gdn_k_heads", "gdn_v_heads", "gdn_k_dim", "gdn_v_dim", "conv_kernel",
+                                       "n_experts", "top_k", "moe_ff", "shared_ff", "dense", "context", "max_tokens")]
+
+
+class GLayer(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("attn", "in_norm", "post_norm", "qkv", "z", "out", "a", "b", "A_log", "dt_bias",
+                                       "conv", "gnorm", "q", "k", "v", "o", "q_norm", "k_norm", "sh_gate", "sh_up",
+                                       "sh_down", "router", "shared_gate", "experts")]
+
+
+class GSampling(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int)]
+
+
+def _sig(L):
+    vp, i32, i64, f32, sz = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
+    sigs = {
+        "gcuda_open": (vp, [i32, C.c_char_p, i32]),
+        "gcuda_close": (None, [vp]),
+        "gcuda_last_error": (i32, [vp, C.c_char_p, i32]),
+        "gcuda_adopt_q4": (i32, [vp, vp, i64, i64, sz, f32]),
+        "gcuda_adopt_raw": (i32, [vp, vp, sz]),
+        "gcuda_adopt_embedding": (i32, [vp, vp, i64, i64, f32]),
+        "gcuda_adopt_experts": (i32, [vp, vp, i32, sz, vp]),
+        "gcuda_setup": (i32, [vp, vp, vp, i32, i32, i32]),
+        "gcuda_verify": (i32, [vp, vp, i32, vp, vp]),
+        "gcuda_verify_device": (i32, [vp, vp, i32]),
+        "gcuda_keep": (i32, [vp, i32]),
+        "gcuda_position": (i32, [vp]),
+        "gcuda_reset": (i32, [vp]),
+        "gcuda_accept": (i32, [vp, vp, vp, vp, i32, vp, vp, vp]),  # g, sampling, uniforms, stops, n_stops, kept, next, samples
+        "gcuda_spec_reject": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, C.c_uint64, vp, vp]),
+        "gcuda_state_get": (i32, [vp, vp, vp, vp, vp, i32]),
+        "gcuda_state_put": (i32, [vp, vp, vp, vp, vp, i32]),
+        "gcuda_device_logits": (vp, [vp]),
+        "gcuda_last_ms": (f32, [vp]),
+        "gcuda_launches": (C.c_uint64, [vp]),
+        "gcuda_debug_read": (i32, [vp, i32, vp, sz]),
+        "gcuda_debug_step_eager": (i32, [vp, vp, i32, i32]),
+    }
+    for name, (res, args) in sigs.items():
+        if hasattr(L, name):
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class GcudaError(RuntimeError):
+    pass
+
+
+class Backend:
+    """One gcuda handle over a geode-pack directory."""
+
+    def __init__(self, pack_dir: str, context: int, max_tokens: int = 5, device: int = 0):
+        self.L = L = cuda_lib()
+        _sig(L)
+        err = C.create_string_buffer(512)
+        self.g = L.gcuda_open(device, err, 512)
+        if not self.g:
+            raise GcudaError("gcuda_open: " + err.value.decode())
+        with open(os.path.join(pack_dir, "geode.json")) as f:
+            m = json.load(f)
+        self.manifest = m
+        files = {fi["name"]: np.memmap(os.path.join(pack_dir, fi["name"]), dtype=np.uint8, mode="r") for fi in m["files"]}
+        c = m["config"]
+        dense = m["arch"] == "qwen35"
+        T = m["tensors"]
+
+        def check(rc, what):
+            if rc < 0:
+                raise GcudaError(f"{what}: {self.error()}")
+            return rc
+
+        def tensor_bytes(name):
+            t = T[name]
+            buf = files[t["file"]]
+            n = int(np.prod(t["shape"]))
+            if t["type"] == "f32":
+                size = 4 * n
+            elif t["type"] == "bf16":
+                size = 2 * n
+            else:
+                size = t["shape"][0] * int(np.prod(t["shape"][1:])) // 16 * 9
+            return np.ascontiguousarray(buf[t["offset"]: t["offset"] + size]), t
+
+        def q4(name):
+            b, t = tensor_bytes(name)
+            rows, cols = t["shape"][0], int(np.prod(t["shape"][1:]))
+            return check(L.gcuda_adopt_q4(self.g, _ptr(b), rows, cols, cols // 16 * 9, t.get("global", 1.0)), name)
+
+        def raw(name):
+            b, _ = tensor_bytes(name)
+            return check(L.gcuda_adopt_raw(self.g, _ptr(b), b.nbytes), name)
+
+        attn = [t == "full_attention" for t in c["layer_types"]]
+        layers = (GLayer * c["num_hidden_layers"])()
+        for l in range(c["num_hidden_layers"]):
+            p = f"layers.{l}."
+            x = layers[l]
+            for f_ in GLayer._fields_:
+                setattr(x, f_[0], -1)
+            x.attn = 1 if attn[l] else 0
+            x.in_norm, x.post_norm = raw(p + "input_layernorm.weight"), raw(p + "post_attention_layernorm.weight")
+            if attn[l]:
+                x.q, x.k, x.v, x.o = (q4(p + f"self_attn.{n}_proj.weight") for n in "qkvo")
+                x.q_norm, x.k_norm = raw(p + "self_attn.q_norm.weight"), raw(p + "self_attn.k_norm.weight")
+            else:
+                x.qkv = q4(p + "linear_attn.in_proj_qkv.weight")
+                x.z = q4(p + "linear_attn.in_proj_z.weight")
+                x.out = q4(p + "linear_attn.out_proj.weight")
+                x.a, x.b = raw(p + "linear_attn.in_proj_a.weight"), raw(p + "linear_attn.in_proj_b.weight")
+                x.A_log, x.dt_bias = raw(p + "linear_attn.A_log"), raw(p + "linear_attn.dt_bias")
+                x.conv, x.gnorm = raw(p + "linear_attn.conv1d.weight"), raw(p + "linear_attn.norm.weight")
+            if dense:
+                x.sh_gate, x.sh_up, x.sh_down = (q4(p + f"mlp.{n}_proj.weight") for n in ("gate", "up", "down"))
+            else:
+                x.sh_gate, x.sh_up, x.sh_down = (q4(p + f"mlp.shared_expert.{n}_proj.weight") for n in ("gate", "up", "down"))
+                x.router, x.shared_gate = raw(p + "mlp.gate.weight"), raw(p + "mlp.shared_expert_gate.weight")
+                e = m["experts"]["layers"][l]
+                buf = files[e["file"]]
+                E = c["num_experts"]
+                blocks = np.ascontiguousarray(buf[e["offset"]: e["offset"] + E * e["stride"]])
+                sc, _ = tensor_bytes(p + "mlp.experts.scales")
+                x.experts = check(L.gcuda_adopt_experts(self.g, _ptr(blocks), E, e["stride"], _ptr(sc)), p + "experts")
+        eb, et = tensor_bytes("embed_tokens.weight")
+        embed = check(L.gcuda_adopt_embedding(self.g, _ptr(eb), et["shape"][0], et["shape"][1], et.get("global", 1.0)), "embed")
+        head = q4("lm_head.weight")
+        norm = raw("norm.weight")
+        rope = c.get("rope_parameters", {})
+        s = GShape(hidden=c["hidden_size"], n_layers=c["num_hidden_layers"], vocab=c["vocab_size"],
+                   eps=c.get("rms_norm_eps", 1e-6), n_heads=c["num_attention_heads"], n_kv_heads=c["num_key_value_heads"],
+                   head_dim=c["head_dim"], rope_dim=int(c["head_dim"] * rope.get("partial_rotary_factor", 1.0)),
+                   rope_theta=rope.get("rope_theta", 10000.0), gdn_k_heads=c.get("linear_num_key_heads", 0),
+                   gdn_v_heads=c.get("linear_num_value_heads", 0), gdn_k_dim=c.get("linear_key_head_dim", 0),
+                   gdn_v_dim=c.get("linear_value_head_dim", 0), conv_kernel=c.get("linear_conv_kernel_dim", 0),
+                   n_experts=c.get("num_experts", 0), top_k=c.get("num_experts_per_tok", 0),
+                   moe_ff=c.get("moe_intermediate_size", 0),
+                   shared_ff=c["intermediate_size"] if dense else c["shared_expert_intermediate_size"],
+                   dense=1 if dense else 0, context=context, max_tokens=max_tokens)
+        self.shape = s
+        check(L.gcuda_setup(self.g, C.addressof(s), C.addressof(layers), embed, head, norm), "setup")
+        self.vocab, self.hidden = s.vocab, s.hidden
+        self.n_attn = sum(attn)
+        self.n_gdn = s.n_layers - self.n_attn
+
+    def error(self) -> str:
+        buf = C.create_string_buffer(1024)
+        self.L.gcuda_last_error(self.g, buf, 1024)
+        return buf.value.decode()
+
+    def _rc(self, rc, what):
+        if rc != 0:
+            raise GcudaError(f"{what} ({rc}): {self.error()}")
+
+    def close(self):
+        if getattr(self, "g", None):
+            self.L.gcuda_close(self.g)
+            self.g = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def pos(self) -> int:
+        return self.L.gcuda_position(self.g)
+
+    def verify(self, toks, logits: bool = True, hidden: bool = False):
+        toks = np.ascontiguousarray(np.asarray(toks, dtype=np.int32))
+        n = len(toks)
+        lg = np.zeros((n, self.vocab), np.float32) if logits else None
+        hd = np.zeros((n, self.hidden), np.float32) if hidden else None
+        self._rc(self.L.gcuda_verify(self.g, _ptr(toks), n, _ptr(lg) if lg is not None else None,
+                                     _ptr(hd) if hd is not None else None), "verify")
+        self._last_n = n
+        return lg, hd
+
+    def keep(self, kept: int):
+        self._rc(self.L.gcuda_keep(self.g, kept), "keep")
+
+    def reset(self):
+        self._rc(self.L.gcuda_reset(self.g), "reset")
+
+    def state_put(self, conv, gdn, kv, kvs, pos: int):
+        self._rc(self.L.gcuda_state_put(self.g, _ptr(conv), _ptr(gdn), _ptr(kv), _ptr(kvs), pos), "state_put")
+
+    def state_get(self, conv, gdn, kv, kvs, positions: int):
+        self._rc(self.L.gcuda_state_get(self.g, _ptr(conv), _ptr(gdn), _ptr(kv), _ptr(kvs), positions), "state_get")
+
+    def accept(self, temperature=0.0, top_p=1.0, top_k=0, uniforms=None, stops=()):
+        """The acceptance of the last verified batch (its own tokens are the drafts): (kept, next, samples)."""
+        n = self._last_n
+        u = np.ascontiguousarray(np.zeros(n) if uniforms is None else np.asarray(uniforms, dtype=np.float64))
+        st = np.ascontiguousarray(np.asarray(list(stops) or [0], dtype=np.int32))
+        kept, nxt = C.c_int(0), C.c_int(0)
+        samples = np.zeros(n, np.int32)
+        sp = GSampling(temperature, top_p, top_k)
+        self._rc(self.L.gcuda_accept(self.g, C.addressof(sp), _ptr(u), _ptr(st), len(stops), C.byref(kept),
+                                     C.byref(nxt), _ptr(samples)), "accept")
+        return kept.value, nxt.value, samples
+
+    def last_ms(self) -> float:
+        return self.L.gcuda_last_ms(self.g)
+
+    def launches(self) -> int:
+        return int(self.L.gcuda_launches(self.g))

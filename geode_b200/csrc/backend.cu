@@ -1,0 +1,980 @@
+// backend.cu - the gcuda_* backend of geode_cuda.h: weights adopted into device memory, the conversation's device
+// state, and the verify step (Model::verify_n's Adreno branch, engine/src/model.cpp:1529-1592, redone for sm_100a)
+// recorded once per batch size as a CUDA graph of dependent launches.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/geode_cuda.h"
+#include "gemv_kernels.cuh"
+#include "launch.hpp"
+#include "ops_impl.cuh"
+#include "accept.cuh"
+
+using namespace gcu;
+
+namespace {
+
+enum TensorKind { kQ4Tiled = 0, kRaw = 1 };
+
+struct DevTensor {
+    void *d = nullptr;
+    size_t bytes = 0;
+    int64_t rows = 0, cols = 0;
+    float global = 1.0f;
+    int kind = kRaw;
+};
+
+struct DevExperts {
+    uint8_t *d = nullptr;
+    int n = 0;
+    size_t stride = 0;
+    float *scales = nullptr;   // device [n][2]
+    std::vector<float> host_scales;
+};
+
+struct ActBuf {
+    int8_t *q = nullptr;
+    float *scale = nullptr;
+    int32_t *bsum = nullptr;
+    int cols = 0, n = 0;
+    ActSet set() const { return ActSet{q, scale, bsum, cols, n, cols, cols / 16}; }
+};
+
+struct LayerPlan {
+    int gi = -1, ai = -1;                 // index among GDN / attention layers
+    int u_in = 0, n_in = 0;               // unit table range: the mixer's input products
+    int u_out = 0, n_out = 0;             // the mixer's output product
+    int u_mlp = 0, n_mlp = 0, u_dn = 0, n_dn = 0;   // dense MLP
+    uint16_t *ab_w = nullptr;             // GDN a|b rows (bf16 [2 nv][H])
+    uint16_t *router_w = nullptr;         // MoE router rows + the shared gate row ([E+1][H])
+};
+
+}  // namespace
+
+struct gcuda {
+    int device = 0;
+    cudaStream_t st = nullptr;
+    std::string err;
+    std::vector<DevTensor> tensors;
+    std::vector<DevExperts> experts;
+    bool ready = false;
+    gcuda_shape sh{};
+    std::vector<gcuda_layer> layers;
+    std::vector<LayerPlan> plan;
+    int embed = -1, lm_head = -1, final_norm = -1;
+    int n_gdn = 0, n_attn = 0, conv_dim = 0, vd = 0, kd = 0, qw = 0, kvrow = 0, corew = 0;
+    // state
+    float *conv = nullptr, *gdn = nullptr, *conv_bk = nullptr, *gdn_bk = nullptr;
+    size_t conv_n = 0, gdn_n = 0;   // floats per copy (all GDN layers)
+    int8_t *kc = nullptr, *vc = nullptr;
+    float *ks = nullptr, *vs = nullptr;
+    // scratch
+    int *d_toks = nullptr, *d_pos = nullptr;
+    uint32_t *d_status = nullptr;
+    float *x = nullptr, *hf = nullptr, *big = nullptr, *zb = nullptr, *ab = nullptr, *kb = nullptr, *vb = nullptr,
+          *qn = nullptr, *rlog = nullptr, *eout = nullptr, *shout = nullptr, *part = nullptr, *logits = nullptr,
+          *hid = nullptr, *core_f = nullptr, *inv_freq = nullptr;
+    ActBuf hq, core, amid, shact;
+    RouteOut *route = nullptr;
+    GemvUnit *units = nullptr;
+    int n_units = 0, lm_u = 0;
+    int nchunks = 0;
+    // graphs per batch size
+    cudaGraphExec_t graph[kMaxTok + 1] = {};
+    int pos = 0, last_batch = 0;
+    int last_toks[kMaxTok] = {};
+    double *d_u = nullptr;
+    int *d_samples = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.0f;
+    bool pdl = true;
+    std::vector<void *> allocs;
+};
+
+namespace {
+
+int fail(gcuda *g, int code, const std::string &msg) {
+    if (g) g->err = msg;
+    return code;
+}
+
+int cuda_fail(gcuda *g, cudaError_t e, const char *what) {
+    return fail(g, e == cudaErrorMemoryAllocation ? GCUDA_E_MEMORY : GCUDA_E_CUDA,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+template <typename T>
+bool dalloc(gcuda *g, T **p, size_t count) {
+    void *q = nullptr;
+    if (count == 0) count = 1;
+    const cudaError_t e = cudaMalloc(&q, count * sizeof(T));
+    if (e != cudaSuccess) {
+        cuda_fail(g, e, "cudaMalloc");
+        return false;
+    }
+    cudaMemsetAsync(q, 0, count * sizeof(T), g->st);
+    g->allocs.push_back(q);
+    *p = static_cast<T *>(q);
+    return true;
+}
+
+bool act_alloc(gcuda *g, ActBuf &a, int n, int cols) {
+    a.n = n;
+    a.cols = cols;
+    return dalloc(g, &a.q, static_cast<size_t>(n) * cols) && dalloc(g, &a.scale, static_cast<size_t>(n) * cols / 16) &&
+           dalloc(g, &a.bsum, static_cast<size_t>(n) * cols / 16);
+}
+
+const DevTensor *tensor(gcuda *g, int id, int kind) {
+    if (id < 0 || id >= static_cast<int>(g->tensors.size())) return nullptr;
+    const DevTensor &t = g->tensors[static_cast<size_t>(id)];
+    return t.kind == kind ? &t : nullptr;
+}
+
+// units of a plain matrix: rows / 32 units of adjacent tile pairs, outputs y + row (ystride between tokens)
+void plain_units(std::vector<GemvUnit> &out, const DevTensor &m, float *y, int ystride, int mode) {
+    const size_t tb = static_cast<size_t>(tile_bytes(static_cast<int>(m.cols)));
+    const int64_t units = (m.rows + 31) / 32;
+    for (int64_t u = 0; u < units; ++u) {
+        GemvUnit U{};
+        U.w0 = static_cast<const uint8_t *>(m.d) + (2 * u) * tb;
+        U.w1 = U.w0 + tb;
+        U.g0 = U.g1 = m.global;
+        U.y0 = y + 32 * u;
+        U.y1 = U.y0 + 16;
+        U.ngroups = static_cast<int>(m.cols / 64);
+        U.ystride = ystride;
+        U.mode = mode;
+        U.tok_mask = 0xFF;
+        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = t;
+        out.push_back(U);
+    }
+}
+
+// silu(gate) * up units: gate tile i with up tile i (rows multiples of 16), into act rows t
+void swiglu_units(std::vector<GemvUnit> &out, const DevTensor &gt, const DevTensor &up, const ActBuf &a) {
+    const size_t tb = static_cast<size_t>(tile_bytes(static_cast<int>(gt.cols)));
+    for (int64_t i = 0; i < gt.rows / 16; ++i) {
+        GemvUnit U{};
+        U.w0 = static_cast<const uint8_t *>(gt.d) + i * tb;
+        U.w1 = static_cast<const uint8_t *>(up.d) + i * tb;
+        U.g0 = gt.global;
+        U.g1 = up.global;
+        U.ngroups = static_cast<int>(gt.cols / 64);
+        U.mode = kSwiglu;
+        U.tok_mask = 0xFF;
+        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = t;
+        U.aq = a.q;
+        U.as = a.scale;
+        U.ab = a.bsum;
+        U.acols = a.cols;
+        U.arow0 = static_cast<int>(16 * i);
+        out.push_back(U);
+    }
+}
+
+int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl) {
+    StaticGemv p{};
+    p.units = g->units + u0;
+    p.n_units = nu;
+    p.act = act.set();
+    p.ncols = n;
+    p.status = g->d_status;
+    return launch_static_gemv(p, g->st, pdl);
+}
+
+#define LAUNCH_OK(call)                                                        \
+    do {                                                                       \
+        const cudaError_t e_ = (call);                                         \
+        if (e_ != cudaSuccess) return cuda_fail(g, e_, #call);                 \
+    } while (0)
+#define RC_OK(call)                                                            \
+    do {                                                                       \
+        const int r_ = (call);                                                 \
+        if (r_ != GCUDA_OK) return g->err.empty() ? fail(g, r_, #call) : r_;   \
+    } while (0)
+
+// The verify step for n tokens on g->st (toks in g->d_toks, the position in g->d_pos).
+int enqueue_step(gcuda *g, int n) {
+    const gcuda_shape &s = g->sh;
+    const int H = s.hidden;
+    const bool pdl = g->pdl;
+    const DevTensor *emb = tensor(g, g->embed, kRaw);
+    {
+        const dim3 grid((H + 255) / 256, n);
+        LAUNCH_OK(launch_ex(k_embed, grid, dim3(256), 0, g->st, false, static_cast<const uint8_t *>(emb->d),
+                            static_cast<int64_t>(s.vocab), H, emb->global, static_cast<const int *>(g->d_toks), n, g->x,
+                            g->d_status));
+    }
+    auto norm = [&](const float *w, bool combine, float *hf_out) -> int {
+        NormArgs a{};
+        a.x = g->x;
+        a.w = w;
+        a.eps = s.eps;
+        a.H = H;
+        a.n = n;
+        a.hf = hf_out;
+        a.q = g->hq.q;
+        a.scale = g->hq.scale;
+        a.bsum = g->hq.bsum;
+        if (combine) {
+            a.sh = g->shout;
+            a.gs = g->route->gs;
+            a.eout = g->eout;
+            a.wk = g->route->w;
+            a.K = s.top_k;
+        }
+        LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(256), 0, g->st, pdl, a));
+        return GCUDA_OK;
+    };
+    auto raw = [&](int id) -> const float * {
+        const DevTensor *t = tensor(g, id, kRaw);
+        return t ? static_cast<const float *>(t->d) : nullptr;
+    };
+    RC_OK(norm(raw(g->layers[0].in_norm), false, g->hf));
+    for (int l = 0; l < s.n_layers; ++l) {
+        const gcuda_layer &L = g->layers[static_cast<size_t>(l)];
+        const LayerPlan &P = g->plan[static_cast<size_t>(l)];
+        if (!L.attn) {
+            RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
+            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3((2 * s.gdn_v_heads * n * 8 + 255) / 256), dim3(256), 0, g->st, pdl,
+                                static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H,
+                                static_cast<const float *>(g->hf), H, n, g->ab, 2 * s.gdn_v_heads));
+            GdnArgs a{};
+            a.proj = g->big;
+            a.z = g->zb;
+            a.ab = g->ab;
+            a.convw = raw(L.conv);
+            a.A_log = raw(L.A_log);
+            a.dt_bias = raw(L.dt_bias);
+            a.gnorm = raw(L.gnorm);
+            const size_t conv_l = static_cast<size_t>(g->conv_dim) * (s.conv_kernel - 1);
+            const size_t st_l = static_cast<size_t>(s.gdn_v_heads) * s.gdn_v_dim * s.gdn_k_dim;
+            a.conv_st = g->conv + P.gi * conv_l;
+            a.state = g->gdn + P.gi * st_l;
+            a.conv_bk = g->conv_bk + P.gi * conv_l;
+            a.state_bk = g->gdn_bk + P.gi * st_l;
+            a.bk_conv_stride = g->conv_n;
+            a.bk_state_stride = g->gdn_n;
+            a.n = n;
+            a.nk = s.gdn_k_heads;
+            a.nv = s.gdn_v_heads;
+            a.dk = s.gdn_k_dim;
+            a.dv = s.gdn_v_dim;
+            a.K = s.conv_kernel;
+            a.eps = s.eps;
+            a.q = g->core.q;
+            a.scale = g->core.scale;
+            a.bsum = g->core.bsum;
+            a.core_f = g->core_f;
+            cudaLaunchConfig_t cfg{};
+            const int S = s.gdn_v_dim / 16;
+            cfg.gridDim = dim3(s.gdn_v_heads * S);
+            cfg.blockDim = dim3(128);
+            cfg.stream = g->st;
+            cudaLaunchAttribute attr[2];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = S;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            attr[1].val.programmaticStreamSerializationAllowed = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = pdl ? 2 : 1;
+            cudaError_t e;
+            if (s.gdn_k_dim == 128) e = cudaLaunchKernelEx(&cfg, k_gdn<128>, a);
+            else if (s.gdn_k_dim == 64) e = cudaLaunchKernelEx(&cfg, k_gdn<64>, a);
+            else e = cudaLaunchKernelEx(&cfg, k_gdn<32>, a);
+            count_launch();
+            LAUNCH_OK(e);
+            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl));
+        } else {
+            RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
+            AttnPrepArgs pa{};
+            pa.qg = g->big;
+            pa.kb = g->kb;
+            pa.vb = g->vb;
+            pa.q_norm = raw(L.q_norm);
+            pa.k_norm = raw(L.k_norm);
+            pa.inv_freq = g->inv_freq;
+            pa.pos = g->d_pos;
+            pa.n = n;
+            pa.nh = s.n_heads;
+            pa.nkv = s.n_kv_heads;
+            pa.hd = s.head_dim;
+            pa.half = s.rope_dim / 2;
+            pa.eps = s.eps;
+            pa.qn = g->qn;
+            const size_t kvl = static_cast<size_t>(s.context) * g->kvrow;
+            pa.kc = g->kc + P.ai * kvl;
+            pa.vc = g->vc + P.ai * kvl;
+            pa.ks = g->ks + P.ai * static_cast<size_t>(s.context) * s.n_kv_heads;
+            pa.vs = g->vs + P.ai * static_cast<size_t>(s.context) * s.n_kv_heads;
+            pa.ctx = s.context;
+            pa.status = g->d_status;
+            const int items = n * (s.n_heads + 2 * s.n_kv_heads);
+            LAUNCH_OK(launch_ex(k_attn_prep, dim3((items + 3) / 4), dim3(128), 4 * s.head_dim * sizeof(float), g->st, pdl, pa));
+            AttnArgs aa{};
+            aa.qn = g->qn;
+            aa.kc = pa.kc;
+            aa.vc = pa.vc;
+            aa.ks = pa.ks;
+            aa.vs = pa.vs;
+            aa.pos = g->d_pos;
+            aa.n = n;
+            aa.nh = s.n_heads;
+            aa.nkv = s.n_kv_heads;
+            aa.ctx = s.context;
+            aa.scale = 1.0f / std::sqrt(static_cast<float>(s.head_dim));
+            aa.part = g->part;
+            aa.nchunks = g->nchunks;
+            const dim3 grid(g->nchunks, s.n_kv_heads);
+            if (s.head_dim == 256) {
+                LAUNCH_OK(launch_ex(k_attn_decode<256>, grid, dim3(128), attn_smem_bytes<256>(), g->st, pdl, aa));
+            } else if (s.head_dim == 128) {
+                LAUNCH_OK(launch_ex(k_attn_decode<128>, grid, dim3(128), attn_smem_bytes<128>(), g->st, pdl, aa));
+            } else {
+                LAUNCH_OK(launch_ex(k_attn_decode<64>, grid, dim3(128), attn_smem_bytes<64>(), g->st, pdl, aa));
+            }
+            MergeArgs ma{};
+            ma.part = g->part;
+            ma.qg = g->big;
+            ma.pos = g->d_pos;
+            ma.n = n;
+            ma.nh = s.n_heads;
+            ma.hd = s.head_dim;
+            ma.nchunks = g->nchunks;
+            ma.q = g->core.q;
+            ma.scale = g->core.scale;
+            ma.bsum = g->core.bsum;
+            ma.core_f = g->core_f;
+            LAUNCH_OK(launch_ex(k_attn_merge, dim3((n * s.n_heads + 3) / 4), dim3(128), 0, g->st, pdl, ma));
+            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl));
+        }
+        // x += mix happened in the output product's epilogue; h = rmsnorm(x, post_norm)
+        RC_OK(norm(raw(L.post_norm), false, g->hf));
+        const float *next_norm = l + 1 < s.n_layers ? raw(g->layers[static_cast<size_t>(l) + 1].in_norm) : raw(g->final_norm);
+        float *next_hf = l + 1 < s.n_layers ? g->hf : g->hid;
+        if (s.dense) {
+            RC_OK(launch_units(g, P.u_mlp, P.n_mlp, g->hq, n, pdl));
+            RC_OK(launch_units(g, P.u_dn, P.n_dn, g->shact, n, pdl));
+            RC_OK(norm(next_norm, false, next_hf));
+        } else {
+            const int E = s.n_experts;
+            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3(((E + 1) * n * 8 + 255) / 256), dim3(256), 0, g->st, pdl,
+                                static_cast<const uint16_t *>(P.router_w), E + 1, H, static_cast<const float *>(g->hf), H,
+                                n, g->rlog, E + 1));
+            LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(32 * kMaxTok), kMaxTok * E * sizeof(float), g->st, pdl,
+                                static_cast<const float *>(g->rlog), n, E, s.top_k, g->route));
+            const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
+            const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
+                            *sd = tensor(g, L.sh_down, kQ4Tiled);
+            ExpertsArgs ea{};
+            ea.route = g->route;
+            ea.experts = X.d;
+            ea.stride = X.stride;
+            ea.scales = X.scales;
+            ea.sh_gate = static_cast<const uint8_t *>(sg->d);
+            ea.sh_up = static_cast<const uint8_t *>(su->d);
+            ea.sh_down = static_cast<const uint8_t *>(sd->d);
+            ea.sh_g0 = sg->global;
+            ea.sh_g1 = su->global;
+            ea.sh_g2 = sd->global;
+            ea.H = H;
+            ea.ff = s.moe_ff;
+            ea.sff = s.shared_ff;
+            ea.K = s.top_k;
+            ea.n = n;
+            ea.hq = g->hq.set();
+            ea.amid = g->amid.set();
+            ea.shact = g->shact.set();
+            ea.eout = g->eout;
+            ea.shout = g->shout;
+            ea.status = g->d_status;
+            const size_t smem = experts_smem_bytes(H, s.moe_ff, s.shared_ff);
+            ea.pass = kGateUp;
+            LAUNCH_OK(launch_ex(k_gemv_experts, dim3(sm_count()), dim3(kGemvWarps * 32), smem, g->st, pdl, ea));
+            ea.pass = kDown;
+            LAUNCH_OK(launch_ex(k_gemv_experts, dim3(sm_count()), dim3(kGemvWarps * 32), smem, g->st, pdl, ea));
+            RC_OK(norm(next_norm, true, next_hf));
+        }
+    }
+    // the logits of every row (engine/src/model.cpp:5397-5410): hq holds rmsnorm(x, final_norm) quantized
+    RC_OK(launch_units(g, g->lm_u, static_cast<int>((s.vocab + 31) / 32), g->hq, n, pdl));
+    return GCUDA_OK;
+}
+
+int set_attrs(gcuda *g) {
+    const gcuda_shape &s = g->sh;
+    const size_t gsm = std::max(gemv_smem_bytes(s.hidden), std::max(gemv_smem_bytes(g->corew),
+                                                                     gemv_smem_bytes(std::max(16 * 4, s.shared_ff))));
+    LAUNCH_OK(cudaFuncSetAttribute(k_gemv_static, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
+    if (!s.dense)
+        LAUNCH_OK(cudaFuncSetAttribute(k_gemv_experts, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(experts_smem_bytes(s.hidden, s.moe_ff, s.shared_ff))));
+    LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<256>())));
+    LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<128>())));
+    LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<64>())));
+    LAUNCH_OK(cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxTok * s.n_experts * sizeof(float) + 16)));
+    return GCUDA_OK;
+}
+
+int record_graphs(gcuda *g) {
+    for (int n = 1; n <= g->sh.max_tokens; ++n) {
+        cudaGraph_t graph = nullptr;
+        LAUNCH_OK(cudaStreamBeginCapture(g->st, cudaStreamCaptureModeThreadLocal));
+        const int rc = enqueue_step(g, n);
+        const cudaError_t e = cudaStreamEndCapture(g->st, &graph);
+        if (rc != GCUDA_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e != cudaSuccess) return cuda_fail(g, e, "cudaStreamEndCapture");
+        const cudaError_t ei = cudaGraphInstantiate(&g->graph[n], graph, 0);
+        cudaGraphDestroy(graph);
+        if (ei != cudaSuccess) return cuda_fail(g, ei, "cudaGraphInstantiate");
+    }
+    return GCUDA_OK;
+}
+
+int check_status(gcuda *g) {
+    uint32_t st = 0;
+    LAUNCH_OK(cudaMemcpyAsync(&st, g->d_status, 4, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    if (st) {
+        cudaMemsetAsync(g->d_status, 0, 4, g->st);
+        std::string why;
+        if (st & kErrWaitTimeout) why += " a bounded wait gave up;";
+        if (st & kErrBadToken) why += " a token id out of range;";
+        if (st & kErrBadShape) why += " a position past the context;";
+        return fail(g, GCUDA_E_DEVICE, "device status" + why);
+    }
+    return GCUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+gcuda *gcuda_open(int device, char *err, int err_len) {
+    auto put = [&](const std::string &m) {
+        if (err && err_len > 0) {
+            std::strncpy(err, m.c_str(), static_cast<size_t>(err_len - 1));
+            err[err_len - 1] = 0;
+        }
+    };
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+        put("no CUDA device " + std::to_string(device));
+        return nullptr;
+    }
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, device);
+    if (prop.major != 10) {
+        put(std::string("not an sm_100 device: ") + prop.name);
+        return nullptr;
+    }
+    auto *g = new gcuda;
+    g->device = device;
+    cudaSetDevice(device);
+    if (cudaStreamCreateWithFlags(&g->st, cudaStreamNonBlocking) != cudaSuccess) {
+        put("cudaStreamCreate failed");
+        delete g;
+        return nullptr;
+    }
+    cudaEventCreate(&g->ev0);
+    cudaEventCreate(&g->ev1);
+    if (!dalloc(g, &g->d_status, 1)) {
+        put(g->err);
+        gcuda_close(g);
+        return nullptr;
+    }
+    return g;
+}
+
+void gcuda_close(gcuda *g) {
+    if (!g) return;
+    cudaSetDevice(g->device);
+    if (g->st) cudaStreamSynchronize(g->st);
+    for (auto &ge : g->graph)
+        if (ge) cudaGraphExecDestroy(ge);
+    for (auto &t : g->tensors)
+        if (t.d) cudaFree(t.d);
+    for (auto &x : g->experts) {
+        if (x.d) cudaFree(x.d);
+        if (x.scales) cudaFree(x.scales);
+    }
+    for (void *p : g->allocs) cudaFree(p);
+    if (g->ev0) cudaEventDestroy(g->ev0);
+    if (g->ev1) cudaEventDestroy(g->ev1);
+    if (g->st) cudaStreamDestroy(g->st);
+    delete g;
+}
+
+int gcuda_last_error(gcuda *g, char *buf, int len) {
+    if (!g) return GCUDA_E_ARG;
+    if (buf && len > 0) {
+        std::strncpy(buf, g->err.c_str(), static_cast<size_t>(len - 1));
+        buf[len - 1] = 0;
+    }
+    return g->err.empty() ? 0 : 1;
+}
+
+int gcuda_adopt_q4(gcuda *g, const uint8_t *data, int64_t rows, int64_t cols, size_t row_bytes, float global) {
+    if (!g || !data || rows <= 0 || cols <= 0 || cols % 64 || row_bytes != static_cast<size_t>(cols / 16) * 9)
+        return fail(g, GCUDA_E_ARG, "adopt_q4: a q4 [rows][cols] with cols a multiple of 64");
+    cudaSetDevice(g->device);
+    const size_t src_bytes = static_cast<size_t>(rows) * row_bytes;
+    const size_t tiled = gcuda_op_q4_tiled_bytes(rows, cols);
+    void *stage = nullptr, *dst = nullptr;
+    cudaError_t e = cudaMalloc(&dst, tiled);
+    if (e != cudaSuccess) return cuda_fail(g, e, "adopt_q4 cudaMalloc");
+    e = cudaMalloc(&stage, src_bytes);
+    if (e != cudaSuccess) {
+        cudaFree(dst);
+        return cuda_fail(g, e, "adopt_q4 cudaMalloc (staging)");
+    }
+    e = cudaMemcpyAsync(stage, data, src_bytes, cudaMemcpyHostToDevice, g->st);
+    if (e == cudaSuccess && gcuda_op_q4_relayout(static_cast<uint8_t *>(stage), rows, cols, static_cast<uint8_t *>(dst), g->st) != 0)
+        e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g->st);
+    cudaFree(stage);
+    if (e != cudaSuccess) {
+        cudaFree(dst);
+        return cuda_fail(g, e, "adopt_q4");
+    }
+    DevTensor t;
+    t.d = dst;
+    t.bytes = tiled;
+    t.rows = rows;
+    t.cols = cols;
+    t.global = global;
+    t.kind = kQ4Tiled;
+    g->tensors.push_back(t);
+    return static_cast<int>(g->tensors.size()) - 1;
+}
+
+int gcuda_adopt_raw(gcuda *g, const void *data, size_t bytes) {
+    if (!g || !data || bytes == 0) return fail(g, GCUDA_E_ARG, "adopt_raw: no data");
+    cudaSetDevice(g->device);
+    void *dst = nullptr;
+    cudaError_t e = cudaMalloc(&dst, bytes);
+    if (e != cudaSuccess) return cuda_fail(g, e, "adopt_raw cudaMalloc");
+    e = cudaMemcpy(dst, data, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dst);
+        return cuda_fail(g, e, "adopt_raw");
+    }
+    DevTensor t;
+    t.d = dst;
+    t.bytes = bytes;
+    t.kind = kRaw;
+    g->tensors.push_back(t);
+    return static_cast<int>(g->tensors.size()) - 1;
+}
+
+// Internal: the embedding keeps the pack's row layout (rows are gathered, not streamed) with its global.
+int gcuda_adopt_embedding(gcuda *g, const uint8_t *data, int64_t rows, int64_t cols, float global) {
+    const int id = gcuda_adopt_raw(g, data, static_cast<size_t>(rows) * static_cast<size_t>(cols / 16) * 9);
+    if (id >= 0) {
+        g->tensors[static_cast<size_t>(id)].rows = rows;
+        g->tensors[static_cast<size_t>(id)].cols = cols;
+        g->tensors[static_cast<size_t>(id)].global = global;
+    }
+    return id;
+}
+
+int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, const float *scales) {
+    if (!g || !blocks || n <= 0 || !scales) return fail(g, GCUDA_E_ARG, "adopt_experts: no data");
+    cudaSetDevice(g->device);
+    DevExperts X;
+    X.n = n;
+    X.stride = stride;
+    X.host_scales.assign(scales, scales + 2 * n);
+    cudaError_t e = cudaMalloc(&X.d, static_cast<size_t>(n) * stride);
+    if (e != cudaSuccess) return cuda_fail(g, e, "adopt_experts cudaMalloc");
+    e = cudaMalloc(&X.scales, sizeof(float) * 2 * n);
+    if (e == cudaSuccess) e = cudaMemcpy(X.scales, scales, sizeof(float) * 2 * n, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(X.d);
+        return cuda_fail(g, e, "adopt_experts");
+    }
+    // the blocks stay raw until gcuda_setup knows hidden and ff (then each is relaid in place: see setup)
+    e = cudaMemcpy(X.d, blocks, static_cast<size_t>(n) * stride, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(g, e, "adopt_experts copy");
+    g->experts.push_back(X);
+    return static_cast<int>(g->experts.size()) - 1;
+}
+
+int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, int embed, int lm_head, int final_norm) {
+    if (!g || !shape || !layers) return fail(g, GCUDA_E_ARG, "setup: no shape");
+    if (g->ready) return fail(g, GCUDA_E_STATE, "setup: already set up");
+    cudaSetDevice(g->device);
+    const gcuda_shape &s = *shape;
+    if (s.max_tokens < 1 || s.max_tokens > kMaxTok || s.hidden % 64 || s.n_layers <= 0 || s.context <= 0 ||
+        (!s.dense && (s.top_k < 1 || s.top_k > 8 || s.n_experts > 1024 || s.moe_ff % 64 || s.shared_ff % 64)) ||
+        (s.dense && s.shared_ff % 64) || s.head_dim % 64 || (s.head_dim != 64 && s.head_dim != 128 && s.head_dim != 256) ||
+        s.n_heads % std::max(1, s.n_kv_heads) || s.max_tokens * (s.n_heads / std::max(1, s.n_kv_heads)) > 32)
+        return fail(g, GCUDA_E_ARG, "setup: an unsupported geometry");
+    g->sh = s;
+    g->layers.assign(layers, layers + s.n_layers);
+    g->embed = embed;
+    g->lm_head = lm_head;
+    g->final_norm = final_norm;
+    const int H = s.hidden, T = s.max_tokens;
+    g->kd = s.gdn_k_heads * s.gdn_k_dim;
+    g->vd = s.gdn_v_heads * s.gdn_v_dim;
+    g->conv_dim = 2 * g->kd + g->vd;
+    g->qw = s.n_heads * 2 * s.head_dim;
+    g->kvrow = s.n_kv_heads * s.head_dim;
+    g->corew = std::max(g->vd, s.n_heads * s.head_dim);
+    for (const auto &L : g->layers) (L.attn ? g->n_attn : g->n_gdn)++;
+    if (g->n_gdn && (s.gdn_v_dim % 16 || s.gdn_v_dim / 16 > 8 || (s.gdn_k_dim != 32 && s.gdn_k_dim != 64 && s.gdn_k_dim != 128) ||
+                     s.gdn_v_heads % std::max(1, s.gdn_k_heads) || s.conv_kernel < 1 || s.conv_kernel > 9))
+        return fail(g, GCUDA_E_ARG, "setup: an unsupported Gated DeltaNet geometry");
+    // the routed experts relaid into tiles, block by block: [gate_up tiles][down tiles], the same bytes
+    if (!s.dense) {
+        const size_t want = static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9 + static_cast<size_t>(H) * (s.moe_ff / 16) * 9;
+        for (auto &X : g->experts) {
+            if (X.stride != want) return fail(g, GCUDA_E_ARG, "setup: an expert block of unexpected size");
+            uint8_t *tmp = nullptr;
+            cudaError_t e = cudaMalloc(&tmp, X.stride);
+            if (e != cudaSuccess) return cuda_fail(g, e, "setup cudaMalloc");
+            const size_t gu_tiled = gcuda_op_q4_tiled_bytes(2 * s.moe_ff, H);
+            for (int i = 0; i < X.n; ++i) {
+                uint8_t *blk = X.d + static_cast<size_t>(i) * X.stride;
+                cudaMemcpyAsync(tmp, blk, X.stride, cudaMemcpyDeviceToDevice, g->st);
+                gcuda_op_q4_relayout(tmp, 2 * s.moe_ff, H, blk, g->st);
+                gcuda_op_q4_relayout(tmp + static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9, H, s.moe_ff, blk + gu_tiled, g->st);
+            }
+            e = cudaStreamSynchronize(g->st);
+            cudaFree(tmp);
+            if (e != cudaSuccess) return cuda_fail(g, e, "setup relayout experts");
+        }
+    }
+    // state
+    g->conv_n = static_cast<size_t>(g->n_gdn) * g->conv_dim * std::max(0, s.conv_kernel - 1);
+    g->gdn_n = static_cast<size_t>(g->n_gdn) * s.gdn_v_heads * s.gdn_v_dim * s.gdn_k_dim;
+    const size_t kv = static_cast<size_t>(g->n_attn) * s.context * g->kvrow;
+    const size_t kvs = static_cast<size_t>(g->n_attn) * s.context * s.n_kv_heads;
+    g->nchunks = (s.context + kAttnChunk - 1) / kAttnChunk;
+    const int E = s.dense ? 0 : s.n_experts, K = s.dense ? 1 : s.top_k;
+    const int ffw = s.dense ? 64 : s.moe_ff;
+    if (!dalloc(g, &g->conv, g->conv_n) || !dalloc(g, &g->gdn, g->gdn_n) ||
+        !dalloc(g, &g->conv_bk, g->conv_n * (T - 1 > 0 ? T - 1 : 1)) || !dalloc(g, &g->gdn_bk, g->gdn_n * (T - 1 > 0 ? T - 1 : 1)) ||
+        !dalloc(g, &g->kc, kv) || !dalloc(g, &g->vc, kv) || !dalloc(g, &g->ks, kvs) || !dalloc(g, &g->vs, kvs) ||
+        !dalloc(g, &g->d_toks, kMaxTok) || !dalloc(g, &g->d_pos, 1) || !dalloc(g, &g->x, static_cast<size_t>(T) * H) ||
+        !dalloc(g, &g->hf, static_cast<size_t>(T) * H) || !dalloc(g, &g->hid, static_cast<size_t>(T) * H) ||
+        !dalloc(g, &g->big, static_cast<size_t>(T) * std::max(g->conv_dim, g->qw)) ||
+        !dalloc(g, &g->zb, static_cast<size_t>(T) * std::max(1, g->vd)) ||
+        !dalloc(g, &g->ab, static_cast<size_t>(T) * std::max(1, 2 * s.gdn_v_heads)) ||
+        !dalloc(g, &g->kb, static_cast<size_t>(T) * g->kvrow) || !dalloc(g, &g->vb, static_cast<size_t>(T) * g->kvrow) ||
+        !dalloc(g, &g->qn, static_cast<size_t>(T) * s.n_heads * s.head_dim) ||
+        !dalloc(g, &g->rlog, static_cast<size_t>(T) * (E + 1)) || !dalloc(g, &g->eout, static_cast<size_t>(T) * K * H) ||
+        !dalloc(g, &g->shout, static_cast<size_t>(T) * H) ||
+        !dalloc(g, &g->part, static_cast<size_t>(T) * s.n_heads * g->nchunks * (s.head_dim + 2)) ||
+        !dalloc(g, &g->logits, static_cast<size_t>(T) * s.vocab) || !dalloc(g, &g->core_f, static_cast<size_t>(T) * g->corew) ||
+        !dalloc(g, &g->inv_freq, std::max(1, s.rope_dim / 2)) || !dalloc(g, &g->route, 1) ||
+        !dalloc(g, &g->d_u, kMaxTok) || !dalloc(g, &g->d_samples, kMaxTok) ||
+        !act_alloc(g, g->hq, T, H) || !act_alloc(g, g->core, T, g->corew) ||
+        !act_alloc(g, g->amid, T * K, ffw) || !act_alloc(g, g->shact, T, s.shared_ff))
+        return GCUDA_E_MEMORY;
+    // inv_freq as the reference computes it (engine/src/model.cpp:737-740), host powf
+    {
+        std::vector<float> inv(static_cast<size_t>(std::max(1, s.rope_dim / 2)));
+        for (int i = 0; i < s.rope_dim / 2; ++i)
+            inv[static_cast<size_t>(i)] = 1.0f / std::pow(s.rope_theta, static_cast<float>(2 * i) / static_cast<float>(s.rope_dim));
+        cudaMemcpy(g->inv_freq, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice);
+    }
+    // the unit tables and the small merged weight buffers
+    std::vector<GemvUnit> U;
+    g->plan.assign(static_cast<size_t>(s.n_layers), LayerPlan{});
+    int gi = 0, ai = 0;
+    auto q4 = [&](int id) { return tensor(g, id, kQ4Tiled); };
+    for (int l = 0; l < s.n_layers; ++l) {
+        const gcuda_layer &L = g->layers[static_cast<size_t>(l)];
+        LayerPlan &P = g->plan[static_cast<size_t>(l)];
+        if (!tensor(g, L.in_norm, kRaw) || !tensor(g, L.post_norm, kRaw))
+            return fail(g, GCUDA_E_ARG, "setup: layer " + std::to_string(l) + " lacks its norms");
+        if (!L.attn) {
+            P.gi = gi++;
+            const DevTensor *qkv = q4(L.qkv), *z = q4(L.z), *out = q4(L.out);
+            const DevTensor *a = tensor(g, L.a, kRaw), *b = tensor(g, L.b, kRaw);
+            if (!qkv || !z || !out || !a || !b || !tensor(g, L.conv, kRaw) || !tensor(g, L.A_log, kRaw) ||
+                !tensor(g, L.dt_bias, kRaw) || !tensor(g, L.gnorm, kRaw) || qkv->rows != g->conv_dim || z->rows != g->vd ||
+                out->rows != H || out->cols != g->vd)
+                return fail(g, GCUDA_E_ARG, "setup: GDN layer " + std::to_string(l) + " tensors");
+            P.u_in = static_cast<int>(U.size());
+            plain_units(U, *qkv, g->big, g->conv_dim, kStore);
+            plain_units(U, *z, g->zb, g->vd, kStore);
+            P.n_in = static_cast<int>(U.size()) - P.u_in;
+            P.u_out = static_cast<int>(U.size());
+            plain_units(U, *out, g->x, H, kAccumulate);
+            P.n_out = static_cast<int>(U.size()) - P.u_out;
+            if (!dalloc(g, &P.ab_w, static_cast<size_t>(2 * s.gdn_v_heads) * H)) return GCUDA_E_MEMORY;
+            cudaMemcpy(P.ab_w, a->d, a->bytes, cudaMemcpyDeviceToDevice);
+            cudaMemcpy(P.ab_w + static_cast<size_t>(s.gdn_v_heads) * H, b->d, b->bytes, cudaMemcpyDeviceToDevice);
+        } else {
+            P.ai = ai++;
+            const DevTensor *q = q4(L.q), *k = q4(L.k), *v = q4(L.v), *o = q4(L.o);
+            if (!q || !k || !v || !o || !tensor(g, L.q_norm, kRaw) || !tensor(g, L.k_norm, kRaw) || q->rows != g->qw ||
+                k->rows != g->kvrow || v->rows != g->kvrow || o->rows != H || o->cols != s.n_heads * s.head_dim)
+                return fail(g, GCUDA_E_ARG, "setup: attention layer " + std::to_string(l) + " tensors");
+            P.u_in = static_cast<int>(U.size());
+            plain_units(U, *q, g->big, g->qw, kStore);
+            plain_units(U, *k, g->kb, g->kvrow, kStore);
+            plain_units(U, *v, g->vb, g->kvrow, kStore);
+            P.n_in = static_cast<int>(U.size()) - P.u_in;
+            P.u_out = static_cast<int>(U.size());
+            plain_units(U, *o, g->x, H, kAccumulate);
+            P.n_out = static_cast<int>(U.size()) - P.u_out;
+        }
+        const DevTensor *sg = q4(L.sh_gate), *su = q4(L.sh_up), *sd = q4(L.sh_down);
+        if (!sg || !su || !sd || sg->rows != s.shared_ff || su->rows != s.shared_ff || sd->rows != H)
+            return fail(g, GCUDA_E_ARG, "setup: layer " + std::to_string(l) + " MLP tensors");
+        if (s.dense) {
+            P.u_mlp = static_cast<int>(U.size());
+            swiglu_units(U, *sg, *su, g->shact);
+            P.n_mlp = static_cast<int>(U.size()) - P.u_mlp;
+            P.u_dn = static_cast<int>(U.size());
+            plain_units(U, *sd, g->x, H, kAccumulate);
+            P.n_dn = static_cast<int>(U.size()) - P.u_dn;
+        } else {
+            const DevTensor *r = tensor(g, L.router, kRaw), *gt = tensor(g, L.shared_gate, kRaw);
+            if (!r || !gt || L.experts < 0 || L.experts >= static_cast<int>(g->experts.size()) ||
+                g->experts[static_cast<size_t>(L.experts)].n != s.n_experts)
+                return fail(g, GCUDA_E_ARG, "setup: MoE layer " + std::to_string(l) + " tensors");
+            if (!dalloc(g, &P.router_w, static_cast<size_t>(s.n_experts + 1) * H)) return GCUDA_E_MEMORY;
+            cudaMemcpy(P.router_w, r->d, r->bytes, cudaMemcpyDeviceToDevice);
+            cudaMemcpy(P.router_w + static_cast<size_t>(s.n_experts) * H, gt->d, gt->bytes, cudaMemcpyDeviceToDevice);
+        }
+    }
+    const DevTensor *head = q4(lm_head);
+    if (!head || head->rows != s.vocab || !tensor(g, final_norm, kRaw) || !tensor(g, embed, kRaw))
+        return fail(g, GCUDA_E_ARG, "setup: lm_head / norm / embedding");
+    g->lm_u = static_cast<int>(U.size());
+    plain_units(U, *head, g->logits, s.vocab, kStore);
+    g->n_units = static_cast<int>(U.size());
+    if (!dalloc(g, &g->units, U.size())) return GCUDA_E_MEMORY;
+    cudaMemcpy(g->units, U.data(), U.size() * sizeof(GemvUnit), cudaMemcpyHostToDevice);
+    RC_OK(set_attrs(g));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    RC_OK(record_graphs(g));
+    g->ready = true;
+    g->pos = 0;
+    return GCUDA_OK;
+}
+
+int gcuda_verify_device(gcuda *g, const int *d_toks, int n) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "verify before setup");
+    if (n < 1 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "a verified batch of " + std::to_string(n) + " tokens");
+    if (g->pos + n > g->sh.context) return fail(g, GCUDA_E_ARG, "the context is full");
+    cudaSetDevice(g->device);
+    if (d_toks != g->d_toks) LAUNCH_OK(cudaMemcpyAsync(g->d_toks, d_toks, sizeof(int) * n, cudaMemcpyDeviceToDevice, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaEventRecord(g->ev0, g->st));
+    LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
+    LAUNCH_OK(cudaEventRecord(g->ev1, g->st));
+    RC_OK(check_status(g));
+    cudaEventElapsedTime(&g->last_ms, g->ev0, g->ev1);
+    LAUNCH_OK(cudaMemcpy(g->last_toks, g->d_toks, sizeof(int) * n, cudaMemcpyDeviceToHost));
+    g->pos += n;
+    g->last_batch = n;
+    return GCUDA_OK;
+}
+
+int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "verify before setup");
+    if (!toks || n < 1 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "a verified batch of " + std::to_string(n) + " tokens");
+    if (g->pos + n > g->sh.context) return fail(g, GCUDA_E_ARG, "the context is full");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
+    RC_OK(gcuda_verify_device(g, g->d_toks, n));
+    if (logits) LAUNCH_OK(cudaMemcpyAsync(logits, g->logits, sizeof(float) * n * g->sh.vocab, cudaMemcpyDeviceToHost, g->st));
+    if (hidden) LAUNCH_OK(cudaMemcpyAsync(hidden, g->hid, sizeof(float) * n * g->sh.hidden, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    return GCUDA_OK;
+}
+
+int gcuda_accept(gcuda *g, const gcuda_sampling *sp, const double *uniforms, const int *stops, int n_stops, int *kept,
+                 int *next, int *samples) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "accept before setup");
+    if (!sp || !kept || !next || g->last_batch < 1) return fail(g, GCUDA_E_STATE, "accept without a verified batch");
+    cudaSetDevice(g->device);
+    const int n = g->last_batch;
+    const bool greedy = sp->temperature <= 0.0f;
+    if (!greedy) {
+        if (!uniforms) return fail(g, GCUDA_E_ARG, "accept: sampling needs the uniforms");
+        LAUNCH_OK(cudaMemcpyAsync(g->d_u, uniforms, sizeof(double) * n, cudaMemcpyHostToDevice, g->st));
+    }
+    SampleArgs a{};
+    a.logits = g->logits;
+    a.V = g->sh.vocab;
+    a.n = n;
+    a.temperature = sp->temperature;
+    a.top_p = sp->top_p;
+    a.top_k = sp->top_k;
+    a.u = g->d_u;
+    a.out = g->d_samples;
+    LAUNCH_OK(launch_ex(k_sample_rows, dim3(n), dim3(kSampleThreads), 0, g->st, false, a));
+    int ys[kMaxTok];
+    LAUNCH_OK(cudaMemcpyAsync(ys, g->d_samples, sizeof(int) * n, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    // engine/src/geode.cpp:327-350: draft i+1 stands while row i's sample is that draft and no stop token
+    int k = 1, nx = -1;
+    for (int i = 0; i < n; ++i) {
+        bool stop = false;
+        for (int j = 0; j < n_stops && stops; ++j) stop |= stops[j] == ys[i];
+        if (i + 1 < n && ys[i] == g->last_toks[i + 1] && !stop) {
+            ++k;
+            continue;
+        }
+        nx = ys[i];
+        break;
+    }
+    *kept = k;
+    *next = nx;
+    // the loop samples rows 0 .. kept-1 (the last of them ends it); the rows after were never drawn
+    if (samples)
+        for (int i = 0; i < n; ++i) samples[i] = i < k ? ys[i] : -1;
+    return GCUDA_OK;
+}
+
+int gcuda_keep(gcuda *g, int kept) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "keep before setup");
+    if (kept < 1 || kept >= g->last_batch)
+        return fail(g, GCUDA_E_ARG, "keeping " + std::to_string(kept) + " of a batch of " + std::to_string(g->last_batch));
+    cudaSetDevice(g->device);
+    const size_t b = static_cast<size_t>(kept - 1);
+    if (g->conv_n)
+        LAUNCH_OK(cudaMemcpyAsync(g->conv, g->conv_bk + b * g->conv_n, g->conv_n * sizeof(float), cudaMemcpyDeviceToDevice, g->st));
+    if (g->gdn_n)
+        LAUNCH_OK(cudaMemcpyAsync(g->gdn, g->gdn_bk + b * g->gdn_n, g->gdn_n * sizeof(float), cudaMemcpyDeviceToDevice, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    g->pos -= g->last_batch - kept;
+    g->last_batch = 0;
+    return GCUDA_OK;
+}
+
+int gcuda_position(gcuda *g) { return g ? g->pos : GCUDA_E_ARG; }
+
+int gcuda_reset(gcuda *g) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "reset before setup");
+    cudaSetDevice(g->device);
+    if (g->conv_n) cudaMemsetAsync(g->conv, 0, g->conv_n * sizeof(float), g->st);
+    if (g->gdn_n) cudaMemsetAsync(g->gdn, 0, g->gdn_n * sizeof(float), g->st);
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    g->pos = 0;
+    g->last_batch = 0;
+    return GCUDA_OK;
+}
+
+const float *gcuda_device_logits(gcuda *g) { return g ? g->logits : nullptr; }
+float gcuda_last_ms(gcuda *g) { return g ? g->last_ms : 0.0f; }
+uint64_t gcuda_launches(gcuda *) { return launch_counter().load(); }
+
+// state bridge: the reference's layouts <-> the device's ([vh][dv][dk] recurrent states, [pos][nkv][hd] KV)
+int gcuda_state_get(gcuda *g, float *conv, float *gdn, int8_t *kv, float *kv_scale, int positions) {
+    if (!g || !g->ready || positions < 0 || positions > g->sh.context) return fail(g, GCUDA_E_ARG, "state_get");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    const gcuda_shape &s = g->sh;
+    if (conv && g->conv_n) LAUNCH_OK(cudaMemcpy(conv, g->conv, g->conv_n * sizeof(float), cudaMemcpyDeviceToHost));
+    if (gdn && g->gdn_n) {
+        std::vector<float> d(g->gdn_n);
+        LAUNCH_OK(cudaMemcpy(d.data(), g->gdn, g->gdn_n * sizeof(float), cudaMemcpyDeviceToHost));
+        const int nv = s.gdn_v_heads, dv = s.gdn_v_dim, dk = s.gdn_k_dim;
+        for (size_t l = 0; l < static_cast<size_t>(g->n_gdn); ++l)
+            for (int h = 0; h < nv; ++h)
+                for (int j = 0; j < dv; ++j)
+                    for (int i = 0; i < dk; ++i) {
+                        const size_t src = ((l * nv + h) * dv + j) * dk + i;
+                        const size_t dst = (l * nv + h) * static_cast<size_t>(dv) * dk + static_cast<size_t>(j / 16) * dk * 16 +
+                                           static_cast<size_t>(i) * 16 + (j % 16);
+                        gdn[dst] = d[src];
+                    }
+    }
+    const size_t row = g->kvrow, nkv = s.n_kv_heads;
+    for (int a = 0; a < g->n_attn && positions > 0; ++a) {
+        const size_t base = static_cast<size_t>(a) * s.context;
+        if (kv) {
+            LAUNCH_OK(cudaMemcpy(kv + (static_cast<size_t>(a) * 2 + 0) * positions * row, g->kc + base * row, positions * row, cudaMemcpyDeviceToHost));
+            LAUNCH_OK(cudaMemcpy(kv + (static_cast<size_t>(a) * 2 + 1) * positions * row, g->vc + base * row, positions * row, cudaMemcpyDeviceToHost));
+        }
+        if (kv_scale) {
+            LAUNCH_OK(cudaMemcpy(kv_scale + (static_cast<size_t>(a) * 2 + 0) * positions * nkv, g->ks + base * nkv, positions * nkv * 4, cudaMemcpyDeviceToHost));
+            LAUNCH_OK(cudaMemcpy(kv_scale + (static_cast<size_t>(a) * 2 + 1) * positions * nkv, g->vs + base * nkv, positions * nkv * 4, cudaMemcpyDeviceToHost));
+        }
+    }
+    return GCUDA_OK;
+}
+
+int gcuda_state_put(gcuda *g, const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, int pos) {
+    if (!g || !g->ready || pos < 0 || pos > g->sh.context) return fail(g, GCUDA_E_ARG, "state_put");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    const gcuda_shape &s = g->sh;
+    if (conv && g->conv_n) LAUNCH_OK(cudaMemcpy(g->conv, conv, g->conv_n * sizeof(float), cudaMemcpyHostToDevice));
+    if (gdn && g->gdn_n) {
+        std::vector<float> d(g->gdn_n);
+        const int nv = s.gdn_v_heads, dv = s.gdn_v_dim, dk = s.gdn_k_dim;
+        for (size_t l = 0; l < static_cast<size_t>(g->n_gdn); ++l)
+            for (int h = 0; h < nv; ++h)
+                for (int j = 0; j < dv; ++j)
+                    for (int i = 0; i < dk; ++i)
+                        d[((l * nv + h) * dv + j) * dk + i] =
+                            gdn[(l * nv + h) * static_cast<size_t>(dv) * dk + static_cast<size_t>(j / 16) * dk * 16 +
+                                static_cast<size_t>(i) * 16 + (j % 16)];
+        LAUNCH_OK(cudaMemcpy(g->gdn, d.data(), g->gdn_n * sizeof(float), cudaMemcpyHostToDevice));
+    }
+    const size_t row = g->kvrow, nkv = s.n_kv_heads;
+    for (int a = 0; a < g->n_attn && pos > 0; ++a) {
+        const size_t base = static_cast<size_t>(a) * s.context;
+        if (kv) {
+            LAUNCH_OK(cudaMemcpy(g->kc + base * row, kv + (static_cast<size_t>(a) * 2 + 0) * pos * row, pos * row, cudaMemcpyHostToDevice));
+            LAUNCH_OK(cudaMemcpy(g->vc + base * row, kv + (static_cast<size_t>(a) * 2 + 1) * pos * row, pos * row, cudaMemcpyHostToDevice));
+        }
+        if (kv_scale) {
+            LAUNCH_OK(cudaMemcpy(g->ks + base * nkv, kv_scale + (static_cast<size_t>(a) * 2 + 0) * pos * nkv, pos * nkv * 4, cudaMemcpyHostToDevice));
+            LAUNCH_OK(cudaMemcpy(g->vs + base * nkv, kv_scale + (static_cast<size_t>(a) * 2 + 1) * pos * nkv, pos * nkv * 4, cudaMemcpyHostToDevice));
+        }
+    }
+    g->pos = pos;
+    g->last_batch = 0;
+    return GCUDA_OK;
+}
+
+// Tests: the device copies of the last step's intermediate rows (what: 0 x [n][H], 1 hf, 2 core_f, 3 route, 4 hid)
+int gcuda_debug_read(gcuda *g, int what, void *out, size_t bytes) {
+    if (!g || !g->ready) return GCUDA_E_STATE;
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    const void *src = what == 0 ? static_cast<const void *>(g->x) : what == 1 ? g->hf : what == 2 ? g->core_f
+                      : what == 3 ? static_cast<const void *>(g->route) : g->hid;
+    LAUNCH_OK(cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost));
+    return GCUDA_OK;
+}
+
+// Tests / measuring: launch the step without the graph (every kernel on the stream, PDL as configured)
+int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl) {
+    if (!g || !g->ready || n < 1 || n > g->sh.max_tokens) return GCUDA_E_ARG;
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    const bool keep = g->pdl;
+    g->pdl = pdl != 0;
+    const int rc = enqueue_step(g, n);
+    g->pdl = keep;
+    if (rc != GCUDA_OK) return rc;
+    RC_OK(check_status(g));
+    g->pos += n;
+    g->last_batch = n;
+    return GCUDA_OK;
+}
+
+}  // extern "C"

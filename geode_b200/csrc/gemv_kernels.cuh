@@ -1,0 +1,340 @@
+// gemv_kernels.cuh - the launchable GEMV kernels over q4_gemv.cuh's unit stream, the load-time relayout, and the
+// activation quantizer.
+#pragma once
+
+#include "relay_core.cuh"
+
+namespace gcu {
+
+// ------------------------------------------------------------------------------------------- relayout ----
+// pack rows [rows][cols/2 codes | cols/16 scales] -> 16-row tiles (q4_gemv.cuh's tile layout). rows_pad: rows
+// rounded up to 32; padding rows get level codes of level -1 and scale byte 0 (they contribute 0).
+// One thread per (tile, group, lane) word quadruple.
+__global__ void k_relayout_q4(const uint8_t *__restrict__ src, int64_t rows, int64_t rows_pad, int cols,
+                              uint8_t *__restrict__ dst) {
+    const int ng = cols / 64;
+    const int64_t tiles = rows_pad / 16;
+    const int64_t total = tiles * ng * 32;
+    const size_t rb = static_cast<size_t>(cols / 16) * 9;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int lane = static_cast<int>(i % 32);
+        const int g = static_cast<int>((i / 32) % ng);
+        const int64_t tile = i / (32 * ng);
+        const int gid = lane >> 2, tig = lane & 3;
+        const int64_t r0 = tile * 16 + gid, r1 = r0 + 8;
+        uint8_t *out = dst + static_cast<size_t>(tile) * (ng * kGroupBytes) + static_cast<size_t>(g) * kGroupBytes;
+        uint32_t words[4];
+        for (int j = 0; j < 4; ++j) {
+            const int b = 4 * g + j;
+            uint32_t w = 0;
+            for (int i2 = 0; i2 < 4; ++i2) {
+                const int col = 16 * b + 4 * tig + i2;   // value index within the row
+                uint32_t c0 = 7, c1 = 7;                   // padding: affine 7 = level -1 (scale 0)
+                if (r0 < rows) {
+                    const uint8_t byte = src[static_cast<size_t>(r0) * rb + col / 2];
+                    const uint32_t c = (col & 1) ? (byte >> 4) : (byte & 15);
+                    c0 = c < 8 ? c + 8 : 15 - c;
+                }
+                if (r1 < rows) {
+                    const uint8_t byte = src[static_cast<size_t>(r1) * rb + col / 2];
+                    const uint32_t c = (col & 1) ? (byte >> 4) : (byte & 15);
+                    c1 = c < 8 ? c + 8 : 15 - c;
+                }
+                w |= (c0 | (c1 << 4)) << (8 * i2);
+            }
+            words[j] = w;
+        }
+        *reinterpret_cast<uint4 *>(out + lane * 16) = make_uint4(words[0], words[1], words[2], words[3]);
+        // the scales: lane l < 16 writes row l's four bytes
+        if (lane < 16) {
+            const int64_t r = tile * 16 + lane;
+            uint32_t s = 0;
+            if (r < rows)
+                for (int j = 0; j < 4; ++j)
+                    s |= static_cast<uint32_t>(src[static_cast<size_t>(r) * rb + static_cast<size_t>(cols / 2) + 4 * g + j]) << (8 * j);
+            *reinterpret_cast<uint32_t *>(out + 512 + lane * 4) = s;
+        }
+    }
+}
+
+// Row r of a tiled matrix back to floats: (level * 1) * (e4m3 * global) (engine/src/kernels.cpp:1214-1228) - the
+// dequantized weights, for the bit-exactness check of the device copy. One thread per value.
+__global__ void k_dequant_rows(const uint8_t *__restrict__ tiles, int cols, float global, const int64_t *__restrict__ rows,
+                               int nrows, float *__restrict__ out) {
+    const int ng = cols / 64;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < static_cast<int64_t>(nrows) * cols;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int k = static_cast<int>(i % cols);
+        const int64_t r = rows[i / cols];
+        const int64_t tile = r / 16;
+        const int rr = static_cast<int>(r % 16), gid = rr & 7, hi = rr >> 3;
+        const int b = k / 16, g = b / 4, j = b % 4, kk = k % 16, tig = kk / 4, i2 = kk % 4;
+        const uint8_t *grp = tiles + static_cast<size_t>(tile) * ng * kGroupBytes + static_cast<size_t>(g) * kGroupBytes;
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(grp + (4 * gid + tig) * 16 + 4 * j);
+        const uint32_t c = (w >> (8 * i2 + 4 * hi)) & 15;
+        const int level = 2 * static_cast<int>(c) - 15;
+        const uint8_t sb = grp[512 + rr * 4 + j];
+        const float e4 = e4m3x2_to_float2(sb).x;
+        out[i] = __fmul_rn(__fmul_rn(static_cast<float>(level), 1.0f), __fmul_rn(e4, global));
+    }
+}
+
+// ------------------------------------------------------------------------------------------- quantize ----
+// n vectors of cols floats (rows xstride apart) -> an ActSet (quantize_activation, engine/src/kernels.cpp:1254-1295).
+// One half-warp per block of 16 values.
+__global__ void k_quantize(const float *__restrict__ x, int n, int cols, int xstride, int8_t *__restrict__ q,
+                           float *__restrict__ scale, int32_t *__restrict__ bsum) {
+    const int nb = cols / 16;
+    const int64_t total = static_cast<int64_t>(n) * nb * 16;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int k = static_cast<int>(i % 16);
+        const int64_t blk = i / 16;
+        const int t = static_cast<int>(blk / nb), b = static_cast<int>(blk % nb);
+        const float v = x[static_cast<size_t>(t) * xstride + b * 16 + k];
+        float amax = fabsf(v);
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(v, inv))));
+        int s = qv;
+        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        q[static_cast<size_t>(t) * cols + b * 16 + k] = static_cast<int8_t>(qv);
+        if (k == 0) {
+            scale[static_cast<size_t>(t) * nb + b] = __fdiv_rn(amax, 127.0f);
+            bsum[static_cast<size_t>(t) * nb + b] = s;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------- the static GEMV ----
+// A table of units (built on the host), or one plain matrix, against one ActSet; slots take units round-robin.
+struct StaticGemv {
+    const GemvUnit *units;   // a unit table, or NULL: one plain matrix (below), units made on the fly
+    int n_units;
+    // the plain matrix: tiles (rows / 32 units of two adjacent tiles), y [ncols][ystride]
+    const uint8_t *tiles;
+    float global;
+    float *y;
+    int ystride, mode;
+    ActSet act;
+    int ncols;          // token columns (<= kMaxTok)
+    uint32_t *status;
+};
+
+__host__ __device__ inline size_t gemv_smem_bytes(int cols) {
+    const int wpu = warps_per_unit(cols);
+    return static_cast<size_t>(kGemvWarps) * warp_smem_bytes((cols / 64) / wpu);
+}
+__host__ __device__ inline int gemv_slots(int cols) { return kGemvWarps / warps_per_unit(cols); }
+
+__global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5;
+    const int cols = p.act.cols, wpu = warps_per_unit(cols), sg = (cols / 64) / wpu, nslots = kGemvWarps / wpu;
+    if (warp >= nslots * wpu) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
+    RelayCtx c = make_ctx(smem, sg, wpu);
+    c.sg = sg;
+    const int slot = warp / wpu;
+    const size_t tb = static_cast<size_t>(cols / 64) * kGroupBytes;
+    auto get = [&](int i, GemvUnit &U) -> bool {
+        const int u = blockIdx.x * nslots + slot + i * gridDim.x * nslots;
+        if (u >= p.n_units) return false;
+        if (p.units) {
+            U = p.units[u];
+            U.tok_mask &= (1 << p.ncols) - 1;
+            return true;
+        }
+        U.w0 = p.tiles + (2 * static_cast<size_t>(u)) * tb;
+        U.w1 = U.w0 + tb;
+        U.g0 = U.g1 = p.global;
+        U.y0 = p.y + 32 * static_cast<size_t>(u);
+        U.y1 = U.y0 + 16;
+        U.ngroups = cols / 64;
+        U.ystride = p.ystride;
+        U.mode = p.mode;
+        U.tok_mask = (1 << p.ncols) - 1;
+        U.act_id = 0;
+        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = t;
+        return true;
+    };
+    bool staged = false;
+    auto restage = [&](const GemvUnit &) {
+        if (staged) return;
+        int sel[kMaxTok];
+        for (int t = 0; t < kMaxTok; ++t) sel[t] = t < p.ncols ? t : -1;
+        stage_slice(p.act, sel, c.part * sg, sg, c.img);
+        __syncwarp();
+        staged = true;
+    };
+    auto prelude = [&]() {
+        // (the weights do not depend on the previous kernel: their first stages are already requested)
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;");
+    };
+    relay_units(get, c, restage, p.status, [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid,
+                                              int tig) { epi_store(U, y0, y1, gid, tig); }, true, prelude);
+}
+
+}  // namespace gcu
+
+#include "layer_kernels.cuh"
+
+namespace gcu {
+
+// ------------------------------------------------------------------------------------------- the expert GEMVs ----
+// The MoE's routed experts over the union the router picked (engine/src/model.cpp:4496-4543), with the shared expert
+// as one more entry. Units are made on the device from the RouteOut:
+//   kGateUp: per union expert, ff/16 units (gate tile i with up tile i), the shared expert's sff/16 after them;
+//            silu(g) * u quantized into the pick's row of amid (slot t * K + k), or the token's row of shact.
+//            Every unit multiplies h (hq, staged once per CTA).
+//   kDown:   per union expert, hidden/32 units (two down tiles), output rows of eout at the pick's slot; the shared
+//            expert's down units after them into shout. A warp restages its activation image when its expert
+//            changes (the picks' amid rows, or shact).
+// Warps take contiguous ranges of units (so a warp restages rarely).
+enum ExpertPass : int { kGateUp = 0, kDown = 1 };
+
+struct ExpertsArgs {
+    int pass;
+    const RouteOut *route;
+    const uint8_t *experts;     // this layer's tiled expert blocks, expert e at experts + e * stride
+    size_t stride;
+    const float *scales;        // [E][2]
+    const uint8_t *sh_gate, *sh_up, *sh_down;   // the shared expert's tiled matrices
+    float sh_g0, sh_g1, sh_g2;
+    int H, ff, sff, K, n;
+    ActSet hq, amid, shact;     // amid: [n*K][ff], shact: [n][sff]
+    float *eout, *shout;        // [n*K][H], [n][H]
+    uint32_t *status;
+};
+
+__host__ __device__ inline size_t experts_smem_bytes(int H, int ff, int sff) {
+    int sgm = 0;
+    for (int cols : {H, ff, sff}) {
+        const int sg = (cols / 64) / warps_per_unit(cols);
+        sgm = sg > sgm ? sg : sgm;
+    }
+    return static_cast<size_t>(kGemvWarps) * warp_smem_bytes(sgm);
+}
+
+__global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5;
+    const bool gu = p.pass == kGateUp;
+    // gate_up multiplies hidden-wide h; down multiplies ff-wide (sff for the shared expert) activations
+    const int cols = gu ? p.H : p.ff;
+    const int wpu = warps_per_unit(cols), sg = (cols / 64) / wpu, nslots = kGemvWarps / wpu;
+    if (gu ? false : p.sff != p.ff) {
+        // (one K for the whole pass: the shared expert's width must match the routed experts')
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.status, kErrBadShape);
+    }
+    int sgm = 0;
+    for (int cc : {p.H, p.ff, p.sff}) {
+        const int s2 = (cc / 64) / warps_per_unit(cc);
+        sgm = s2 > sgm ? s2 : sgm;
+    }
+    if (warp >= nslots * wpu) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
+    RelayCtx c = make_ctx(smem, sgm, wpu);
+    c.sg = sg;
+    const int slot = warp / wpu;
+    auto prelude = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;");
+    };
+    const RouteOut &R = *p.route;
+    int nu = 0, per_ex = 0, total = 0, u0 = 0, u1 = 0;
+    const int all = (1 << p.n) - 1;
+    const size_t tbH = static_cast<size_t>(tile_bytes(p.H)), tbF = static_cast<size_t>(tile_bytes(p.ff)),
+                 tbS = static_cast<size_t>(tile_bytes(p.sff));
+    bool ranged = false;
+    auto range = [&]() {
+        // (read after the dependent-launch wait: the route is the previous kernel's output)
+        nu = R.n_union;
+        per_ex = gu ? p.ff / 16 : p.H / 32;
+        const int sh_units = gu ? p.sff / 16 : p.H / 32;
+        total = nu * per_ex + sh_units;
+        const int nslots_all = gridDim.x * nslots, gs = blockIdx.x * nslots + slot;
+        const int per = (total + nslots_all - 1) / nslots_all;
+        u0 = gs * per;
+        u1 = min(total, u0 + per);
+        ranged = true;
+    };
+    auto get = [&](int i, GemvUnit &U) -> bool {
+        if (!ranged) range();
+        const int u = u0 + i;
+        if (u >= u1) return false;
+        const int s = u / per_ex;
+        const bool shared = s >= nu;
+        const int j = shared ? u - nu * per_ex : u % per_ex;
+        const int e = shared ? 0 : R.ex[s];
+        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = shared ? t : R.slot[s][t];
+        U.tok_mask = shared ? all : R.mask[s];
+        U.act_id = shared ? -1 : s;
+        if (gu) {
+            if (shared) {
+                U.w0 = p.sh_gate + j * tbH;
+                U.w1 = p.sh_up + j * tbH;
+                U.g0 = p.sh_g0;
+                U.g1 = p.sh_g1;
+                U.aq = const_cast<int8_t *>(p.shact.q);
+                U.as = const_cast<float *>(p.shact.scale);
+                U.ab = const_cast<int32_t *>(p.shact.bsum);
+                U.acols = p.sff;
+            } else {
+                const uint8_t *base = p.experts + static_cast<size_t>(e) * p.stride;
+                U.w0 = base + j * tbH;
+                U.w1 = base + (p.ff / 16 + j) * tbH;
+                U.g0 = U.g1 = p.scales[2 * e];
+                U.aq = const_cast<int8_t *>(p.amid.q);
+                U.as = const_cast<float *>(p.amid.scale);
+                U.ab = const_cast<int32_t *>(p.amid.bsum);
+                U.acols = p.ff;
+            }
+            U.arow0 = 16 * j;
+            U.ngroups = p.H / 64;
+            U.mode = kSwiglu;
+            U.act_id = 0;   // every gate_up unit multiplies h
+        } else {
+            if (shared) {
+                U.w0 = p.sh_down + (2 * j) * tbS;
+                U.w1 = U.w0 + tbS;
+                U.g0 = U.g1 = p.sh_g2;
+                U.y0 = p.shout + 32 * j;
+                U.ngroups = p.sff / 64;
+            } else {
+                const uint8_t *base = p.experts + static_cast<size_t>(e) * p.stride + (2 * p.ff / 16) * tbH;
+                U.w0 = base + (2 * j) * tbF;
+                U.w1 = U.w0 + tbF;
+                U.g0 = U.g1 = p.scales[2 * e + 1];
+                U.y0 = p.eout + 32 * j;
+                U.ngroups = p.ff / 64;
+            }
+            U.y1 = U.y0 + 16;
+            U.ystride = p.H;
+            U.mode = kStore;
+        }
+        return true;
+    };
+    int staged = -2;
+    auto restage = [&](const GemvUnit &U) {
+        if (U.act_id == staged) return;
+        __syncwarp();
+        int sel[kMaxTok];
+        for (int t = 0; t < kMaxTok; ++t)
+            sel[t] = t < p.n && ((U.tok_mask >> t) & 1) ? (gu ? t : U.slot[t]) : -1;
+        const ActSet &a = gu ? p.hq : (U.act_id < 0 ? p.shact : p.amid);
+        stage_slice(a, sel, c.part * sg, sg, c.img);
+        __syncwarp();
+        staged = U.act_id;
+    };
+    relay_units(get, c, restage, p.status, [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid,
+                                              int tig) { epi_store(U, y0, y1, gid, tig); }, false, prelude);
+}
+
+}  // namespace gcu

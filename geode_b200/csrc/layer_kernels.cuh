@@ -1,0 +1,704 @@
+// layer_kernels.cuh - the verify step's per-layer kernels besides the weight GEMVs: the embedding, the residual
+// norms with their int8 quantization, the Gated DeltaNet recurrence, gated attention over the int8 KV cache, the
+// router's top-k with the union of the picked experts, and the MoE combine.
+#pragma once
+
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "q4_gemv.cuh"
+#include "small_kernels.cuh"
+
+namespace gcu {
+
+namespace cg = cooperative_groups;
+
+// ------------------------------------------------------------------------------------------- embedding ----
+// x[t] = dequant_row(embed, toks[t]) (engine/src/pack.cpp:353-363, engine/src/kernels.cpp:1214-1228) from the
+// pack-layout table; a token out of range raises kErrBadToken and leaves zeros.
+__global__ void k_embed(const uint8_t *__restrict__ table, int64_t vocab, int H, float global, const int *__restrict__ toks,
+                        int n, float *__restrict__ x, uint32_t *status) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const size_t rb = static_cast<size_t>(H / 16) * 9;
+    const int t = blockIdx.y;
+    if (t >= n) return;
+    const int tok = toks[t];
+    const bool ok = tok >= 0 && tok < vocab;
+    if (!ok && threadIdx.x == 0 && blockIdx.x == 0) atomicOr(status, kErrBadToken);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        if (ok) {
+            const uint8_t *row = table + static_cast<size_t>(tok) * rb;
+            const uint8_t byte = row[i / 2];
+            const int c = (i & 1) ? (byte >> 4) : (byte & 15);
+            const int level = c < 8 ? 2 * c + 1 : -(2 * (c - 8) + 1);
+            const float e4 = e4m3x2_to_float2(row[H / 2 + i / 16]).x;
+            v = __fmul_rn(__fmul_rn(static_cast<float>(level), 1.0f), __fmul_rn(e4, global));
+        }
+        x[static_cast<size_t>(t) * H + i] = v;
+    }
+}
+
+// ------------------------------------------------------------------------------------------- norm + quantize ----
+// Per token (one CTA each, 256 threads): h = x * (1 / sqrt(ss / H + eps)) * (1 + w), ss the sum of squares in double
+// (engine/src/kernels.cpp:1520-1529); then h quantized per 16 values (quantize_activation). hf may be NULL.
+// Optionally first x += add0 * gs + sum_k w_k * add_k (the MoE combine, below).
+__device__ inline void block_norm_quant(float *xr, int H, const float *__restrict__ w, float eps, float *hf, int8_t *q,
+                                        float *scale, int32_t *bsum) {
+    __shared__ double red[32];
+    double ss = 0.0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(red[0] / H), eps)));
+    // 16 consecutive values per half-warp: thread i of the CTA handles value i (+ blockDim steps)
+    for (int i0 = 0; i0 < H; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const float h = i < H ? __fmul_rn(__fmul_rn(xr[i], inv), __fadd_rn(1.0f, w[i])) : 0.0f;
+        if (hf && i < H) hf[i] = h;
+        float amax = fabsf(h);
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(h, iv))));
+        int s = qv;
+        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (i < H) {
+            q[i] = static_cast<int8_t>(qv);
+            if ((i & 15) == 0) {
+                scale[i / 16] = __fdiv_rn(amax, 127.0f);
+                bsum[i / 16] = s;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+struct NormArgs {
+    float *x;                 // [n][H] residual
+    const float *w;           // norm weight [H]
+    float eps;
+    int H, n;
+    float *hf;                // [n][H] or NULL
+    int8_t *q;                // [n][H]
+    float *scale;             // [n][H/16]
+    int32_t *bsum;
+    // the MoE combine, when sh != NULL: x += gs[t] * sh[t] + sum_k w[t][k] * eout[t*K + k] (rank order)
+    const float *sh, *gs, *eout, *wk;
+    int K;
+    float *trace_moe;         // [n][H] or NULL: the MoE output (tests)
+};
+
+__global__ void k_norm_quant(NormArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int t = blockIdx.x;
+    if (t >= a.n) return;
+    float *xr = a.x + static_cast<size_t>(t) * a.H;
+    if (a.sh) {
+        // engine/src/model.cpp:4554-4585 then 5363-5365: out = gs * shared; out += w_k * y_k (k in order, w == 0
+        // skipped); x += out
+        for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+            float o = __fmul_rn(a.gs[t], a.sh[static_cast<size_t>(t) * a.H + i]);
+            for (int k = 0; k < a.K; ++k) {
+                const float wv = a.wk[t * a.K + k];
+                if (wv == 0.0f) continue;
+                o = __fadd_rn(o, __fmul_rn(wv, a.eout[(static_cast<size_t>(t) * a.K + k) * a.H + i]));
+            }
+            if (a.trace_moe) a.trace_moe[static_cast<size_t>(t) * a.H + i] = o;
+            xr[i] = __fadd_rn(xr[i], o);
+        }
+        __syncthreads();
+    }
+    block_norm_quant(xr, a.H, a.w, a.eps, a.hf ? a.hf + static_cast<size_t>(t) * a.H : nullptr,
+                     a.q + static_cast<size_t>(t) * a.H, a.scale + static_cast<size_t>(t) * (a.H / 16),
+                     a.bsum + static_cast<size_t>(t) * (a.H / 16));
+}
+
+// ------------------------------------------------------------------------------------------- Gated DeltaNet ----
+// Model::gdn (engine/src/model.cpp:3527-3688) after its products, for the n tokens of the batch, as one kernel.
+// Grid: nv value heads x S = dv/16 strips, one cluster (S CTAs) per value head; 128 threads per CTA. Thread
+// (j = tid / 8, rg = tid % 8) holds the recurrent state's column j of the strip, rows rg*R .. rg*R+R-1 (R = dk/8)
+// in registers for the whole batch; the column sums over rows reduce across the 8 rg lanes by shuffles.
+// The state layout: [layer][vh][dv column j][dk row i] (a column contiguous). The gated RMSNorm's sum over the
+// head's dv outputs crosses the cluster through distributed shared memory (fixed order: identical on every CTA).
+// Rollback: after each token t < n-1 the conv and recurrent states are written to backup slot t.
+struct GdnArgs {
+    const float *proj;    // [n][conv_dim] (qkv product, before the convolution)
+    const float *z;       // [n][vd]
+    const float *ab;      // [n][2 nv]: a then b
+    const float *convw;   // [conv_dim][K]
+    const float *A_log, *dt_bias, *gnorm;
+    float *conv_st;       // [conv_dim][K-1] (this layer)
+    float *state;         // [nv][dv][dk] (this layer)
+    float *conv_bk;       // backups: slot t at conv_bk + t * bk_conv_stride (this layer's part)
+    float *state_bk;
+    size_t bk_conv_stride, bk_state_stride;
+    int n, nk, nv, dk, dv, K;
+    float eps;
+    int8_t *q;            // the core ActSet [n][vd]
+    float *scale;
+    int32_t *bsum;
+    float *core_f;        // [n][vd] or NULL (tests)
+};
+
+template <int DK>
+__global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
+    constexpr int R = DK / 8;
+    __shared__ float s_q[kMaxTok][DK], s_k[kMaxTok][DK], s_v[kMaxTok][16], s_o[kMaxTok][16];
+    __shared__ float s_beta[kMaxTok], s_decay[kMaxTok], s_ss[kMaxTok], s_red[kMaxTok][4];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = a.dv / 16;
+    const int vh = blockIdx.x / S, s = blockIdx.x % S;
+    const int rep = a.nv / a.nk, kh = vh / rep;
+    const int kd = a.nk * a.dk, vd = a.nv * a.dv;
+    const int tid = threadIdx.x, n = a.n;
+    const int K = a.K;
+    const bool write_qk = (vh % rep == 0) && s == 0;
+    // 1. the convolution (and silu_fast) of this CTA's channels: q and k of key head kh, v columns of the strip
+    const int nch = 2 * DK + 16;
+    for (int c = tid; c < nch; c += blockDim.x) {
+        int ch;
+        if (c < DK) ch = kh * DK + c;                       // q
+        else if (c < 2 * DK) ch = kd + kh * DK + (c - DK);  // k
+        else ch = 2 * kd + vh * a.dv + s * 16 + (c - 2 * DK);
+        const bool writer = c >= 2 * DK || write_qk;
+        const float *w = a.convw + static_cast<size_t>(ch) * K;
+        float st[8];
+        for (int k = 0; k < K - 1; ++k) st[k] = a.conv_st[static_cast<size_t>(ch) * (K - 1) + k];
+        for (int t = 0; t < n; ++t) {
+            const float in = a.proj[static_cast<size_t>(t) * (2 * kd + vd) + ch];
+            float acc = 0.0f;
+            for (int k = 0; k < K - 1; ++k) acc = __fadd_rn(acc, __fmul_rn(w[k], st[k]));
+            acc = __fadd_rn(acc, __fmul_rn(w[K - 1], in));
+            for (int k = 0; k + 1 < K - 1; ++k) st[k] = st[k + 1];
+            if (K > 1) st[K - 2] = in;
+            const float y = silu_fast_exact(acc);
+            if (c < DK) s_q[t][c] = y;
+            else if (c < 2 * DK) s_k[t][c - DK] = y;
+            else s_v[t][c - 2 * DK] = y;
+            if (writer && t + 1 < n)
+                for (int k = 0; k < K - 1; ++k)
+                    a.conv_bk[t * a.bk_conv_stride + static_cast<size_t>(ch) * (K - 1) + k] = st[k];
+        }
+        if (writer)
+            for (int k = 0; k < K - 1; ++k) a.conv_st[static_cast<size_t>(ch) * (K - 1) + k] = st[k];
+    }
+    // gates (engine/src/model.cpp:3604-3611): beta = sigmoid(b), decay = exp(-exp(A_log) * softplus(a + dt_bias))
+    if (tid < n) {
+        const float av = a.ab[static_cast<size_t>(tid) * 2 * a.nv + vh], bv = a.ab[static_cast<size_t>(tid) * 2 * a.nv + a.nv + vh];
+        s_beta[tid] = sigmoid_cr(bv);
+        const float x = __fadd_rn(av, a.dt_bias[vh]);
+        const float sp = x > 20.0f ? x : static_cast<float>(log1p(exp(static_cast<double>(x))));
+        s_decay[tid] = expf_cr(__fmul_rn(-expf_cr(a.A_log[vh]), sp));
+    }
+    __syncthreads();
+    // 2. q, k L2-normalised over dk (eps 1e-6), q times 1/sqrt(dk): one warp per (token, q|k)
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        const float qscale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(DK)));
+        for (int item = warp; item < 2 * n; item += 4) {
+            const int t = item >> 1;
+            float *v = (item & 1) ? s_k[t] : s_q[t];
+            float ss = 0.0f;
+            for (int i = lane; i < DK; i += 32) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+            ss = warp_sum(ss);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
+            __syncwarp();
+            for (int i = lane; i < DK; i += 32)
+                v[i] = (item & 1) ? __fmul_rn(v[i], inv) : __fmul_rn(__fmul_rn(v[i], inv), qscale);
+        }
+    }
+    __syncthreads();
+    // 3. the delta rule, token by token (engine/src/model.cpp:3501-3524)
+    const int j = tid >> 3, rg = tid & 7;
+    const int col = s * 16 + j;
+    float *Sg = a.state + (static_cast<size_t>(vh) * a.dv + col) * DK + rg * R;
+    float Sr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) Sr[r] = Sg[r];
+    for (int t = 0; t < n; ++t) {
+        const float decay = s_decay[t], beta = s_beta[t];
+        float mem = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            Sr[r] = __fmul_rn(Sr[r], decay);
+            mem = __fmaf_rn(Sr[r], s_k[t][rg * R + r], mem);
+        }
+        mem += __shfl_xor_sync(0xffffffffu, mem, 1);
+        mem += __shfl_xor_sync(0xffffffffu, mem, 2);
+        mem += __shfl_xor_sync(0xffffffffu, mem, 4);
+        const float delta = __fmul_rn(__fsub_rn(s_v[t][j], mem), beta);
+        float o = 0.0f;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            Sr[r] = __fmaf_rn(s_k[t][rg * R + r], delta, Sr[r]);
+            o = __fmaf_rn(Sr[r], s_q[t][rg * R + r], o);
+        }
+        o += __shfl_xor_sync(0xffffffffu, o, 1);
+        o += __shfl_xor_sync(0xffffffffu, o, 2);
+        o += __shfl_xor_sync(0xffffffffu, o, 4);
+        if (rg == 0) s_o[t][j] = o;
+        if (t + 1 < n) {
+            float *bk = a.state_bk + t * a.bk_state_stride + (static_cast<size_t>(vh) * a.dv + col) * DK + rg * R;
+#pragma unroll
+            for (int r = 0; r < R; ++r) bk[r] = Sr[r];
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) Sg[r] = Sr[r];
+    __syncthreads();
+    // 4. gated RMSNorm over the head's dv outputs: o / rms(o) * w * silu_fast(z) (engine/src/model.cpp:3670-3682)
+    if (tid < n) {
+        float ss = 0.0f;
+        for (int jj = 0; jj < 16; ++jj) ss = __fmaf_rn(s_o[tid][jj], s_o[tid][jj], ss);
+        s_ss[tid] = ss;
+    }
+    cluster.sync();
+    if (tid < n) {
+        float tot = 0.0f;
+        for (int r = 0; r < S; ++r) {
+            const float *peer = cluster.map_shared_rank(s_ss, r);
+            tot = __fadd_rn(tot, peer[tid]);
+        }
+        s_red[tid][0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.dv)), a.eps)));
+    }
+    cluster.sync();   // (no CTA leaves while a peer still reads its s_ss)
+    // one warp per token: 16 values = lanes 0..15 (lanes 16..31 idle copies), quantized as one block
+    {
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int t = warp; t < n; t += 4) {
+            const int jj = lane & 15;
+            const int c = vh * a.dv + s * 16 + jj;
+            const float zv = a.z[static_cast<size_t>(t) * vd + c];
+            const float h = __fmul_rn(__fmul_rn(__fmul_rn(s_o[t][jj], s_red[t][0]), a.gnorm[s * 16 + jj]), silu_fast_exact(zv));
+            if (a.core_f && lane < 16) a.core_f[static_cast<size_t>(t) * vd + c] = h;
+            float amax = fabsf(h);
+            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(h, iv))));
+            int sm = qv;
+            for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+            if (lane < 16) a.q[static_cast<size_t>(t) * vd + c] = static_cast<int8_t>(qv);
+            if (lane == 0) {
+                a.scale[static_cast<size_t>(t) * (vd / 16) + c / 16] = __fdiv_rn(amax, 127.0f);
+                a.bsum[static_cast<size_t>(t) * (vd / 16) + c / 16] = sm;
+            }
+        }
+    }
+}
+
+}  // namespace gcu
+
+namespace gcu {
+
+// ------------------------------------------------------------------------------------------- attention ----
+// Model::attention's per-head steps (engine/src/model.cpp:3705-3733) and the KV store (3782-3797): queries and keys
+// through the zero-centred head RMSNorm and partial rotary (rotate-half over the first rope_dim dims, angle
+// pos * inv_freq[i]); keys and values to int8 rows (amax / 127, round half even, engine/src/model.cpp:3767-3774)
+// at positions pos .. pos + n - 1. One warp per (token, vector); q rows -> qn [n][nh][hd] f32.
+struct AttnPrepArgs {
+    const float *qg;     // [n][nh][2 hd] (query | gate)
+    const float *kb, *vb;   // [n][nkv * hd]
+    const float *q_norm, *k_norm, *inv_freq;
+    const int *pos;
+    int n, nh, nkv, hd, half;
+    float eps;
+    float *qn;           // [n][nh][hd]
+    int8_t *kc, *vc;     // this layer's cache [ctx][nkv][hd]
+    float *ks, *vs;      // [ctx][nkv]
+    int ctx;
+    uint32_t *status;
+};
+
+__global__ void k_attn_prep(AttnPrepArgs a) {
+    extern __shared__ float sv[];   // per warp hd floats
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int per = a.nh + 2 * a.nkv;
+    const int p0 = *a.pos;
+    float *v = sv + warp * a.hd;
+    for (int item = blockIdx.x * nw + warp; item < a.n * per; item += gridDim.x * nw) {
+        const int t = item / per, w = item % per;
+        const int p = p0 + t;
+        if (p >= a.ctx) {
+            if (lane == 0) atomicOr(a.status, kErrBadShape);
+            continue;
+        }
+        const float *src;
+        const float *nw8 = nullptr;
+        if (w < a.nh) src = a.qg + (static_cast<size_t>(t) * a.nh + w) * 2 * a.hd, nw8 = a.q_norm;
+        else if (w < a.nh + a.nkv) src = a.kb + static_cast<size_t>(t) * a.nkv * a.hd + (w - a.nh) * a.hd, nw8 = a.k_norm;
+        else src = a.vb + static_cast<size_t>(t) * a.nkv * a.hd + (w - a.nh - a.nkv) * a.hd;
+        for (int i = lane; i < a.hd; i += 32) v[i] = src[i];
+        __syncwarp();
+        if (nw8) {
+            double ss = 0.0;
+            for (int i = lane; i < a.hd; i += 32) ss += static_cast<double>(v[i]) * v[i];
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ss / a.hd), a.eps)));
+            for (int i = lane; i < a.hd; i += 32) v[i] = __fmul_rn(__fmul_rn(v[i], inv), __fadd_rn(1.0f, nw8[i]));
+            __syncwarp();
+            for (int i = lane; i < a.half; i += 32) {
+                const float f = __fmul_rn(static_cast<float>(p), a.inv_freq[i]);
+                float sn, cs;
+                sincosf(f, &sn, &cs);
+                const float x1 = v[i], x2 = v[i + a.half];
+                v[i] = __fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn));
+                v[i + a.half] = __fadd_rn(__fmul_rn(x2, cs), __fmul_rn(x1, sn));
+            }
+            __syncwarp();
+        }
+        if (w < a.nh) {
+            float *dst = a.qn + (static_cast<size_t>(t) * a.nh + w) * a.hd;
+            for (int i = lane; i < a.hd; i += 32) dst[i] = v[i];
+        } else {
+            const bool isk = w < a.nh + a.nkv;
+            const int kh = isk ? w - a.nh : w - a.nh - a.nkv;
+            float amax = 0.0f;
+            for (int i = lane; i < a.hd; i += 32) amax = fmaxf(amax, fabsf(v[i]));
+            amax = warp_max(amax);
+            const float inv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            int8_t *dst = (isk ? a.kc : a.vc) + (static_cast<size_t>(p) * a.nkv + kh) * a.hd;
+            for (int i = lane; i < a.hd; i += 32)
+                dst[i] = static_cast<int8_t>(max(-127, min(127, __float2int_rn(__fmul_rn(v[i], inv)))));
+            if (lane == 0) (isk ? a.ks : a.vs)[static_cast<size_t>(p) * a.nkv + kh] = __fdiv_rn(amax, 127.0f);
+        }
+        __syncwarp();
+    }
+}
+
+// Flash-decoding over the int8 cache (the arithmetic of attend / attend_heads, engine/src/model.cpp:3815-4019,
+// regrouped): one CTA per (KV head, chunk of kChunk positions); its rows are the n tokens x G query heads sharing the
+// KV head (<= 32 rows, two m16 tiles). Per sub-chunk of 64 positions: K and V rows widened to f16 in shared memory
+// (int8 is exact in f16), scores Q.K^T on the tensor cores (mma.sync f16, f32 accumulate) times (1/sqrt(hd) *
+// k_scale[p]), causal mask p <= pos + t, an online softmax, P (times v_scale[p], as the reference folds it into the
+// weights) in f16, O += P.V. Partial (O, max, sum) per (token, head, chunk) for k_attn_merge.
+constexpr int kAttnSub = 64;
+constexpr int kAttnChunk = 256;
+
+struct AttnArgs {
+    const float *qn;       // [n][nh][hd]
+    const int8_t *kc, *vc; // [ctx][nkv][hd]
+    const float *ks, *vs;  // [ctx][nkv]
+    const int *pos;
+    int n, nh, nkv, ctx;
+    float scale;           // 1 / sqrt(hd)
+    float *part;           // [n][nh][nchunks][hd + 2]
+    int nchunks;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
+    constexpr int QS = HD + 8;            // f16 row stride (elements) of Q, K, V tiles
+    constexpr int PS = kAttnSub + 8;
+    constexpr int NT_O = HD / 32;         // O n-tiles (8 dims) per warp
+    extern __shared__ __align__(16) uint8_t sm[];
+    __half *Qs = reinterpret_cast<__half *>(sm);
+    __half *Ks = Qs + 32 * QS;
+    __half *Vs = Ks + kAttnSub * QS;
+    __half *Ps = Vs + kAttnSub * QS;
+    float *Ss = reinterpret_cast<float *>(Ps + 32 * PS);
+    float *row_m = Ss + 32 * kAttnSub;
+    float *row_l = row_m + 32;
+    float *row_f = row_l + 32;
+    float *ksc = row_f + 32;
+    float *vsc = ksc + kAttnSub;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
+    const int kh = blockIdx.y, chunk = blockIdx.x;
+    const int G = a.nh / a.nkv, rows = a.n * G;
+    const int pos = *a.pos, plim = pos + a.n;   // positions < plim exist
+    const int c0 = chunk * kAttnChunk;
+    if (c0 >= plim) return;
+    // Q rows r = t * G + g -> f16
+    for (int i = tid; i < 32 * HD; i += blockDim.x) {
+        const int r = i / HD, d = i % HD;
+        float q = 0.0f;
+        if (r < rows) q = a.qn[(static_cast<size_t>(r / G) * a.nh + kh * G + r % G) * HD + d];
+        Qs[r * QS + d] = __float2half_rn(q);
+    }
+    if (tid < 32) {
+        row_m[tid] = -INFINITY;
+        row_l[tid] = 0.0f;
+    }
+    float o[2][NT_O][4];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int j = 0; j < NT_O; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[m][j][e] = 0.0f;
+    for (int s0 = c0; s0 < min(c0 + kAttnChunk, plim); s0 += kAttnSub) {
+        __syncthreads();
+        // K, V rows of the sub-chunk -> f16 (zeros past the end)
+        for (int i = tid; i < kAttnSub * HD / 4; i += blockDim.x) {
+            const int p = i / (HD / 4), d4 = (i % (HD / 4)) * 4, gp = s0 + p;
+            char4 kv = make_char4(0, 0, 0, 0), vv = make_char4(0, 0, 0, 0);
+            if (gp < plim) {
+                kv = *reinterpret_cast<const char4 *>(a.kc + (static_cast<size_t>(gp) * a.nkv + kh) * HD + d4);
+                vv = *reinterpret_cast<const char4 *>(a.vc + (static_cast<size_t>(gp) * a.nkv + kh) * HD + d4);
+            }
+            __half2 *kd = reinterpret_cast<__half2 *>(Ks + p * QS + d4);
+            __half2 *vd = reinterpret_cast<__half2 *>(Vs + p * QS + d4);
+            kd[0] = __halves2half2(__int2half_rn(kv.x), __int2half_rn(kv.y));
+            kd[1] = __halves2half2(__int2half_rn(kv.z), __int2half_rn(kv.w));
+            vd[0] = __halves2half2(__int2half_rn(vv.x), __int2half_rn(vv.y));
+            vd[1] = __halves2half2(__int2half_rn(vv.z), __int2half_rn(vv.w));
+        }
+        if (tid < kAttnSub) {
+            const int gp = s0 + tid;
+            ksc[tid] = gp < plim ? a.ks[static_cast<size_t>(gp) * a.nkv + kh] : 0.0f;
+            vsc[tid] = gp < plim ? a.vs[static_cast<size_t>(gp) * a.nkv + kh] : 0.0f;
+        }
+        __syncthreads();
+        // S = Q K^T: warp w -> positions 16 w .. 16 w + 15 (two n8 tiles), both m tiles
+        {
+            float sacc[2][2][4] = {};
+#pragma unroll
+            for (int kk = 0; kk < HD / 16; ++kk) {
+                uint32_t bq[4];
+                // B: rows = positions (n), k contiguous: matrices (n 0-7,k 0-7), (n 0-7,k 8-15), (n 8-15,k 0-7), (n 8-15,k 8-15)
+                {
+                    const int mi = lane >> 3, rr = lane & 7;
+                    const int n = 16 * warp + rr + 8 * (mi >> 1), k = 16 * kk + 8 * (mi & 1);
+                    ldsm_x4(bq, Ks + n * QS + k);
+                }
+#pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                    uint32_t aq[4];
+                    const int mi = lane >> 3, rr = lane & 7;
+                    const int r = 16 * m + rr + 8 * (mi & 1), k = 16 * kk + 8 * (mi >> 1);
+                    ldsm_x4(aq, Qs + r * QS + k);
+                    const uint32_t b0[2] = {bq[0], bq[1]}, b1[2] = {bq[2], bq[3]};
+                    mma_f16_16816(sacc[m][0], aq, b0);
+                    mma_f16_16816(sacc[m][1], aq, b1);
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int r = 16 * m + gid + 8 * (e >> 1), c = 16 * warp + 8 * nt + 2 * tig + (e & 1);
+                        const int gp = s0 + c, t = r / G;
+                        float v = __fmul_rn(sacc[m][nt][e], __fmul_rn(a.scale, ksc[c]));
+                        if (r >= rows || gp > pos + t) v = -INFINITY;
+                        Ss[r * kAttnSub + c] = v;
+                    }
+        }
+        __syncthreads();
+        // online softmax: warp w -> rows 8 w .. 8 w + 7, lanes over 64 columns (2 each)
+        for (int rr = 0; rr < 8; ++rr) {
+            const int r = 8 * warp + rr;
+            const float s_a = Ss[r * kAttnSub + lane], s_b = Ss[r * kAttnSub + lane + 32];
+            const float mx = warp_max(fmaxf(s_a, s_b));
+            const float m_old = row_m[r], m_new = fmaxf(m_old, mx);
+            const float ea = s_a == -INFINITY ? 0.0f : expf_cr(__fsub_rn(s_a, m_new));
+            const float eb = s_b == -INFINITY ? 0.0f : expf_cr(__fsub_rn(s_b, m_new));
+            const float sum = warp_sum(__fadd_rn(ea, eb));
+            const float f = m_old == -INFINITY ? 0.0f : expf_cr(__fsub_rn(m_old, m_new));
+            Ps[r * PS + lane] = __float2half_rn(__fmul_rn(ea, vsc[lane]));
+            Ps[r * PS + lane + 32] = __float2half_rn(__fmul_rn(eb, vsc[lane + 32]));
+            __syncwarp();
+            if (lane == 0) {
+                row_l[r] = __fadd_rn(__fmul_rn(row_l[r], f), sum);
+                row_m[r] = m_new;
+                row_f[r] = f;
+            }
+        }
+        __syncthreads();
+        // O = O * f + P V: warp w -> dims [w * HD/4, (w+1) * HD/4)
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const float f0 = row_f[16 * m + gid], f1 = row_f[16 * m + gid + 8];
+#pragma unroll
+            for (int j = 0; j < NT_O; ++j) {
+                o[m][j][0] *= f0;
+                o[m][j][1] *= f0;
+                o[m][j][2] *= f1;
+                o[m][j][3] *= f1;
+            }
+        }
+#pragma unroll
+        for (int kk = 0; kk < kAttnSub / 16; ++kk) {
+            uint32_t ap[2][4];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int r = 16 * m + rr + 8 * (mi & 1), k = 16 * kk + 8 * (mi >> 1);
+                ldsm_x4(ap[m], Ps + r * PS + k);
+            }
+#pragma unroll
+            for (int j = 0; j < NT_O; j += 2) {
+                // V rows = k (positions), dims = n: .trans gives the col-major fragments; matrices (k 0-7, n tile j),
+                // (k 8-15, tile j), (k 0-7, tile j+1), (k 8-15, tile j+1)
+                uint32_t bv[4];
+                const int mi = lane >> 3, rr = lane & 7;
+                const int k = 16 * kk + rr + 8 * (mi & 1), n = warp * (HD / 4) + 8 * (j + (mi >> 1));
+                ldsm_x4_t(bv, Vs + k * QS + n);
+                const uint32_t b0[2] = {bv[0], bv[1]}, b1[2] = {bv[2], bv[3]};
+#pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                    mma_f16_16816(o[m][j], ap[m], b0);
+                    mma_f16_16816(o[m][j + 1], ap[m], b1);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // partial results: rows < rows
+    const size_t pstride = HD + 2;
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int j = 0; j < NT_O; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int r = 16 * m + gid + 8 * (e >> 1);
+                if (r >= rows) continue;
+                const int d = warp * (HD / 4) + 8 * j + 2 * tig + (e & 1);
+                const int t = r / G, h = kh * G + r % G;
+                a.part[((static_cast<size_t>(t) * a.nh + h) * a.nchunks + chunk) * pstride + d] = o[m][j][e];
+            }
+    if (tid < rows) {
+        const int t = tid / G, h = kh * G + tid % G;
+        float *pp = a.part + ((static_cast<size_t>(t) * a.nh + h) * a.nchunks + chunk) * pstride;
+        pp[HD] = row_m[tid];
+        pp[HD + 1] = row_l[tid];
+    }
+}
+
+template <int HD>
+constexpr size_t attn_smem_bytes() {
+    return (32 * (HD + 8) + 2 * kAttnSub * (HD + 8) + 32 * (kAttnSub + 8)) * 2 + (32 * kAttnSub + 3 * 32 + 2 * kAttnSub) * 4;
+}
+
+// The chunks joined (engine/src/model.cpp:3832-3853): M = max m_c, O = sum O_c exp(m_c - M), L = sum l_c exp(m_c - M),
+// o = O * (1 / L) * sigmoid(gate); quantized per 16 into the core ActSet. One warp per (token, head).
+struct MergeArgs {
+    const float *part;
+    const float *qg;     // gates: [n][nh][2 hd] second half
+    const int *pos;
+    int n, nh, hd, nchunks;
+    int8_t *q;
+    float *scale;
+    int32_t *bsum;
+    float *core_f;       // [n][nh * hd] or NULL
+};
+
+__global__ void k_attn_merge(MergeArgs a) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int pos = *a.pos;
+    const int W = a.nh * a.hd;
+    for (int item = blockIdx.x * nw + warp; item < a.n * a.nh; item += gridDim.x * nw) {
+        const int t = item / a.nh, h = item % a.nh;
+        const int nc = min(a.nchunks, (pos + t) / kAttnChunk + 1);
+        const float *pp = a.part + (static_cast<size_t>(t) * a.nh + h) * a.nchunks * (a.hd + 2);
+        float M = -INFINITY;
+        for (int c = 0; c < nc; ++c) M = fmaxf(M, pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd]);
+        float L = 0.0f;
+        for (int c = 0; c < nc; ++c) {
+            const float mc = pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd];
+            if (mc == -INFINITY) continue;
+            L = __fadd_rn(L, __fmul_rn(pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd + 1], expf_cr(__fsub_rn(mc, M))));
+        }
+        const float inv = __fdiv_rn(1.0f, L);
+        const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
+        // 16-value blocks: a half-warp per block, lanes over the head's dims
+        for (int d0 = 0; d0 < a.hd; d0 += 32) {
+            const int d = d0 + lane;
+            float acc = 0.0f;
+            for (int c = 0; c < nc; ++c) {
+                const float mc = pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd];
+                if (mc == -INFINITY) continue;
+                acc = __fadd_rn(acc, __fmul_rn(pp[static_cast<size_t>(c) * (a.hd + 2) + d], expf_cr(__fsub_rn(mc, M))));
+            }
+            const float v = __fmul_rn(__fmul_rn(acc, inv), sigmoid_cr(gate[d]));
+            const int col = h * a.hd + d;
+            if (a.core_f) a.core_f[static_cast<size_t>(t) * W + col] = v;
+            float amax = fabsf(v);
+            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(v, iv))));
+            int sm = qv;
+            for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+            a.q[static_cast<size_t>(t) * W + col] = static_cast<int8_t>(qv);
+            if ((lane & 15) == 0) {
+                a.scale[static_cast<size_t>(t) * (W / 16) + col / 16] = __fdiv_rn(amax, 127.0f);
+                a.bsum[static_cast<size_t>(t) * (W / 16) + col / 16] = sm;
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------- routing ----
+// route_topk per token (engine/src/model.cpp:4021-4065), the shared expert's gate sigmoid(w . h)
+// (engine/src/model.cpp:4564-4567; its dot product is the router's last row here), and the union of the picked
+// experts (engine/src/model.cpp:4183-4196): ascending expert ids, each with the tokens that picked it and the
+// pick's slot t * K + k. One CTA, a warp per token.
+constexpr int kMaxUnion = 64;
+struct RouteOut {
+    int n_union;
+    int ex[kMaxUnion];
+    int mask[kMaxUnion];
+    int slot[kMaxUnion][kMaxTok];
+    int ids[kMaxTok * 8];
+    float w[kMaxTok * 8];
+    float gs[kMaxTok];
+};
+
+__global__ void k_route(const float *__restrict__ logits, int n, int E, int K, RouteOut *out) {
+    extern __shared__ float ps[];   // E floats per warp
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < n) {
+        route_row(logits + static_cast<size_t>(warp) * (E + 1), E, K, ps + warp * E, out->ids + warp * K, out->w + warp * K);
+        if (lane == 0) out->gs[warp] = sigmoid_cr(logits[static_cast<size_t>(warp) * (E + 1) + E]);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int nu = 0;
+        // picks sorted by expert (ties by token, then rank: the reference's std::sort of (expert, token, rank))
+        for (;;) {
+            int best = 0x7fffffff;
+            for (int i = 0; i < n * K; ++i) {
+                const int e = out->ids[i];
+                bool seen = false;
+                for (int u = 0; u < nu; ++u) seen |= out->ex[u] == e;
+                if (!seen && e < best) best = e;
+            }
+            if (best == 0x7fffffff || nu >= kMaxUnion) break;
+            out->ex[nu] = best;
+            int m = 0;
+            for (int t = 0; t < kMaxTok; ++t) out->slot[nu][t] = 0;
+            for (int i = 0; i < n * K; ++i)
+                if (out->ids[i] == best) {
+                    m |= 1 << (i / K);
+                    out->slot[nu][i / K] = i;
+                }
+            out->mask[nu] = m;
+            ++nu;
+        }
+        out->n_union = nu;
+    }
+}
+
+}  // namespace gcu

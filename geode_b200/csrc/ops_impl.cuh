@@ -1,0 +1,85 @@
+// ops_impl.cuh - the operator layer of geode_cuda.h (gcuda_op_*): single kernels on caller-owned device buffers.
+// (Included once, by backend.cu: the kernels live in one translation unit.)
+#pragma once
+#include <cuda_runtime.h>
+
+#include "../../include/geode_cuda.h"
+#include "gemv_kernels.cuh"
+#include "small_kernels.cuh"
+#include "launch.hpp"
+
+using namespace gcu;
+
+extern "C" {
+
+size_t gcuda_op_q4_tiled_bytes(int64_t rows, int64_t cols) {
+    const int64_t rows_pad = (rows + 31) / 32 * 32;
+    return static_cast<size_t>(rows_pad / 16) * static_cast<size_t>(tile_bytes(static_cast<int>(cols)));
+}
+
+int gcuda_op_q4_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint8_t *d_tiles, void *stream) {
+    if (!d_pack || !d_tiles || rows <= 0 || cols <= 0 || cols % 64) return GCUDA_E_ARG;
+    const int64_t rows_pad = (rows + 31) / 32 * 32;
+    const int64_t work = rows_pad / 16 * (cols / 64) * 32;
+    const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 32));
+    k_relayout_q4<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_pack, rows, rows_pad, static_cast<int>(cols), d_tiles);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_quantize(const float *d_x, int n, int cols, int8_t *d_q, float *d_scale, int32_t *d_bsum, void *stream) {
+    if (!d_x || n <= 0 || cols <= 0 || cols % 64) return GCUDA_E_ARG;
+    const int64_t work = static_cast<int64_t>(n) * cols;
+    const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 16));
+    k_quantize<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_x, n, cols, cols, d_q, d_scale, d_bsum);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float global, const int8_t *d_q,
+                     const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream) {
+    if (!d_tiles || rows <= 0 || rows % 32 || cols <= 0 || cols % 64 || n < 1 || n > kMaxTok) return GCUDA_E_ARG;
+    StaticGemv p{};
+    p.units = nullptr;
+    p.n_units = static_cast<int>(rows / 32);
+    p.tiles = d_tiles;
+    p.global = global;
+    p.y = d_y;
+    p.ystride = static_cast<int>(rows);
+    p.mode = kStore;
+    p.act = ActSet{d_q, d_scale, d_bsum, static_cast<int>(cols), n, static_cast<int>(cols), static_cast<int>(cols / 16)};
+    p.ncols = n;
+    p.status = device_status();
+    return launch_static_gemv(p, static_cast<cudaStream_t>(stream), false);
+}
+
+int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, const int64_t *d_rows, int nrows,
+                        float *d_out, void *stream) {
+    if (!d_tiles || cols % 64 || nrows <= 0) return GCUDA_E_ARG;
+    const int64_t work = static_cast<int64_t>(nrows) * cols;
+    const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 16));
+    k_dequant_rows<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_tiles, static_cast<int>(cols), global, d_rows,
+                                                                        nrows, d_out);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_bf16_gemv(const uint16_t *d_w, int rows, int cols, const float *d_x, int n, float *d_y, void *stream) {
+    if (!d_w || rows <= 0 || cols % 8 || n < 1) return GCUDA_E_ARG;
+    const int64_t work = static_cast<int64_t>(rows) * n * 8;
+    const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 8));
+    k_bf16_gemv<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_w, rows, cols, d_x, cols, n, d_y, rows);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, float *d_weights, void *stream) {
+    if (!d_logits || n < 1 || E < 1 || E > 1024 || K < 1 || K > E) return GCUDA_E_ARG;
+    const int warps = 4;
+    k_route_topk<<<(n + warps - 1) / warps, warps * 32, warps * E * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+        d_logits, n, E, K, d_ids, d_weights);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+}  // extern "C"

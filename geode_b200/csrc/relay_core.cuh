@@ -1,0 +1,293 @@
+// relay_core.cuh - the q4 GEMV engine: a unit (two 16-row tiles x all K) is split by K over the WPU warps of a
+// "slot"; warp `part` owns groups [part * SG, (part + 1) * SG) (SG = K / 64 / WPU, a group = 4 blocks of 16 values).
+// Each warp streams its slices of successive units through its own ring of TMA bulk-copy stages, computes its first
+// kPre groups' products p = float(isum) * (e4m3 * ascale) ahead, then takes the running f32 chain from warp part-1
+// (a rendezvous on a named barrier), adds its products in block order, and hands the chain to warp part+1; the last
+// warp writes the result. The additions happen in exactly the reference's order (engine/src/kernels.cpp:1316-1319),
+// so the result is bit for bit matvec_rows_q_ref's, while a 2048-row matrix still spreads over every SM.
+#pragma once
+
+#include "q4_gemv.cuh"
+
+namespace gcu {
+
+constexpr int kRelayStages = 6;   // ring stages per warp, one group of both tiles each
+constexpr int kStageBytesR = 2 * kGroupBytes;
+constexpr int kPre = 1;           // groups computed before the predecessor's hand-off
+
+// f32x2 (sm_100): two IEEE operations per instruction, each lane rounded on its own
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return static_cast<uint64_t>(hi) << 32 | lo; }
+__device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+
+// E4M3 byte -> float, exactly, on the integer and FMA pipes: the low 7 bits placed as an f32 exponent/mantissa
+// (bits 20..26) give 2^(e-127) (1 + m/8) for e >= 1 and the denormal m 2^-129 for e = 0; times 2^120 that is the
+// E4M3 value 2^(e-7) (1 + m/8), resp. m 2^-9 (engine/src/kernels.cpp:39-52). The sign is bit 7. (0x7F / 0xFF, the
+// format's NaN, decode as +-480 here; the quantizer never emits them.)
+__device__ __forceinline__ float e4m3_alu(uint32_t b) {
+    return __fmul_rn(__uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20)), 0x1p120f);
+}
+
+// Shared memory per warp: the ring, its barriers, one group's scales as (e, e) float pairs, the warp's activation
+// image for its K-slice, and the relay mailbox (2 parities x 32 lanes x 4 float pairs).
+__host__ __device__ inline int slice_tstride(int sg) { return sg * 64 + (sg % 2 == 0 ? 64 : 0); }
+__host__ __device__ inline int warp_act_bytes(int sg) { return kMaxTok * slice_tstride(sg) + sg * 4 * 64; }
+__host__ __device__ inline int warp_smem_bytes(int sg) {
+    const int b = kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8 + warp_act_bytes(sg) + 2 * 32 * 32;
+    return (b + 127) / 128 * 128;
+}
+// warps per unit for K: a slice of two groups where K allows (at most 16 warps)
+__host__ __device__ inline int warps_per_unit(int cols) {
+    int g = cols / 64, w = g / 2;
+    if (w < 1) w = 1;
+    if (w > 16) w = 16;
+    while (g % w) --w;
+    return w;
+}
+
+// The warp's activation image for groups [g0, g0 + sg) of up to kMaxTok vectors (sel[t] = the ActSet row of token
+// column t, -1 = zeros): act word (t, gl, tig, j) at t * tstride + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
+// .. + 3); cs per (gl, tig) 64 bytes: cinit(2 tig)[4], cinit(2 tig + 1)[4], then (ascale(2 tig), ascale(2 tig + 1)) per
+// block. cinit = 1.5 * 2^23 - 15 * bsum.
+__device__ inline void stage_slice(const ActSet &a, const int *sel, int g0, int sg, uint8_t *img) {
+    const int lane = threadIdx.x & 31, ts = slice_tstride(sg);
+    const int words = kMaxTok * sg * 16;
+    for (int i = lane; i < words; i += 32) {
+        const int t = i / (sg * 16), w = i % (sg * 16), gl = w / 16, j = (w / 4) % 4, tig = w % 4;
+        const int src = sel[t];
+        uint32_t v = 0;
+        if (src >= 0)
+            v = *reinterpret_cast<const uint32_t *>(a.q + static_cast<size_t>(src) * a.qstride + (g0 + gl) * 64 + 16 * j + 4 * tig);
+        *reinterpret_cast<uint32_t *>(img + t * ts + (gl * 4 + tig) * 16 + 4 * j) = v;
+    }
+    int32_t *cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts);
+    for (int i = lane; i < kMaxTok * sg * 4; i += 32) {
+        const int t = i / (sg * 4), bl = i % (sg * 4), gl = bl / 4, j = bl % 4;
+        const int src = sel[t];
+        const int b = (g0 + gl) * 4 + j;
+        int32_t ci = static_cast<int32_t>(kBiasBits);
+        float sc = 0.0f;
+        if (src >= 0) {
+            ci -= 15 * a.bsum[static_cast<size_t>(src) * a.sstride + b];
+            sc = a.scale[static_cast<size_t>(src) * a.sstride + b];
+        }
+        int32_t *base = cs + (gl * 4 + t / 2) * 16;
+        base[(t % 2) * 4 + j] = ci;
+        reinterpret_cast<float *>(base)[8 + 2 * j + (t % 2)] = sc;
+    }
+}
+
+// One group's products for both tiles: p[j][0..3] = tile A (row gid: tokens pair, row gid+8: pair), tile B likewise.
+// e4p: the group's scales as [tile][block][gid][e(gid), e(gid), e(gid+8), e(gid+8)] floats.
+__device__ __forceinline__ void group_products(const uint8_t *stage, const float *e4p, const uint8_t *act, const uint8_t *cs,
+                                               int lane, uint64_t (&p)[4][4]) {
+    const int gid = lane >> 2;
+    const uint4 wa = ld_shared_v4(stage + lane * 16);
+    const uint4 wb = ld_shared_v4(stage + kGroupBytes + lane * 16);
+    const uint4 av = ld_shared_v4(act);
+    const uint4 ci0 = ld_shared_v4(cs);
+    const uint4 ci1 = ld_shared_v4(cs + 16);
+    const uint4 s01 = ld_shared_v4(cs + 32);   // (as0, as1) for blocks 0, 1
+    const uint4 s23 = ld_shared_v4(cs + 48);   // blocks 2, 3
+    const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w}, wB[4] = {wb.x, wb.y, wb.z, wb.w};
+    const uint32_t bv[4] = {av.x, av.y, av.z, av.w};
+    const int32_t c0[4] = {static_cast<int32_t>(ci0.x), static_cast<int32_t>(ci0.y), static_cast<int32_t>(ci0.z), static_cast<int32_t>(ci0.w)};
+    const int32_t c1[4] = {static_cast<int32_t>(ci1.x), static_cast<int32_t>(ci1.y), static_cast<int32_t>(ci1.z), static_cast<int32_t>(ci1.w)};
+    const uint64_t sp[4] = {pack2(s01.x, s01.y), pack2(s01.z, s01.w), pack2(s23.x, s23.y), pack2(s23.z, s23.w)};
+    const uint64_t bias2 = pack2(__float_as_uint(kBiasF), __float_as_uint(kBiasF));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        int32_t dA[4], dB[4];
+        const int32_t cinit[4] = {c0[j], c1[j], c0[j], c1[j]};
+        mma_s8_16816(dA, (wA[j] << 1) & 0x1E1E1E1Eu, (wA[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
+        mma_s8_16816(dB, (wB[j] << 1) & 0x1E1E1E1Eu, (wB[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
+        const uint4 eA = ld_shared_v4(e4p + ((0 * 4 + j) * 8 + gid) * 4);
+        const uint4 eB = ld_shared_v4(e4p + ((1 * 4 + j) * 8 + gid) * 4);
+        // float(isum) = bits(bias + isum) - bias; p = float(isum) * (e4m3 * ascale)
+        const uint64_t FAg = f2_sub(pack2(dA[0], dA[1]), bias2), FAh = f2_sub(pack2(dA[2], dA[3]), bias2);
+        const uint64_t FBg = f2_sub(pack2(dB[0], dB[1]), bias2), FBh = f2_sub(pack2(dB[2], dB[3]), bias2);
+        p[j][0] = f2_mul(FAg, f2_mul(pack2(eA.x, eA.y), sp[j]));
+        p[j][1] = f2_mul(FAh, f2_mul(pack2(eA.z, eA.w), sp[j]));
+        p[j][2] = f2_mul(FBg, f2_mul(pack2(eB.x, eB.y), sp[j]));
+        p[j][3] = f2_mul(FBh, f2_mul(pack2(eB.z, eB.w), sp[j]));
+    }
+}
+
+struct RelayCtx {
+    uint8_t *ring;     // kRelayStages stages
+    uint64_t *bar;
+    float *e4p;        // 2 tiles x 16 rows x 4 blocks x (e, e)
+    uint8_t *img;      // activation image of the slice
+    uint64_t *mail;    // [2][32][4] pairs: this slot's hand-off from the predecessor
+    uint64_t *mail_next;   // the successor's mailbox
+    int part, wpu, sg;
+    int bar_in, bar_out;   // named barrier ids (0: none)
+};
+
+// The units of one slot: get(i, U) the i-th (false past the end); restage(U) fills ctx.img for U's act_id when it
+// changes (called by every lane); epi(U, y0, y1, gid, tig) by the last warp. `early`: the first weight stages may be
+// requested before prelude() (the units do not depend on the previous kernel); prelude() holds CTA barriers.
+template <typename GetUnit, typename Restage, typename Epi, typename Prelude>
+__device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &restage, uint32_t *status, const Epi &epi,
+                            bool early, const Prelude &prelude) {
+    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int sg = c.sg;
+    const uint32_t gbytes = kGroupBytes;
+    // producer: items (unit i, group gl) in order
+    int pu = 0, pg = 0, issued = 0;
+    const uint8_t *pw0 = nullptr, *pw1 = nullptr;
+    bool p_ok = false;
+    auto fetch = [&](int i) {
+        GemvUnit T;
+        p_ok = get(i, T);
+        pw0 = T.w0;
+        pw1 = T.w1;
+    };
+    auto issue = [&]() {
+        if (!p_ok) return;
+        const int s = issued % kRelayStages;
+        if (lane == 0) {
+            fence_proxy_async();
+            uint8_t *dst = c.ring + s * kStageBytesR;
+            const size_t off = static_cast<size_t>(c.part * sg + pg) * gbytes;
+            mbar_expect_tx(&c.bar[s], 2 * gbytes);
+            bulk_g2s(dst, pw0 + off, gbytes, &c.bar[s]);
+            bulk_g2s(dst + gbytes, pw1 + off, gbytes, &c.bar[s]);
+        }
+        ++issued;
+        if (++pg == sg) {
+            pg = 0;
+            fetch(++pu);
+        }
+    };
+    if (early) {
+        fetch(0);
+        for (int i = 0; i < kRelayStages - 1; ++i) issue();
+        prelude();
+    } else {
+        prelude();
+        fetch(0);
+        for (int i = 0; i < kRelayStages - 1; ++i) issue();
+    }
+    const int ts = slice_tstride(sg);
+    int consumed = 0;
+    GemvUnit U;
+    bool ok = true;
+    for (int u = 0; get(u, U); ++u) {
+        restage(U);
+        const uint8_t *act = c.img + gid * ts + tig * 16;
+        const uint8_t *cs = c.img + kMaxTok * ts + tig * 64;
+        // one group: wait, the scales to (e, e) pairs, the products
+        auto group = [&](int gl, uint64_t (&p)[4][4]) -> bool {
+            if (!ok) return false;   // (after a wait gave up: no more waits; the chain still runs, the status says why)
+            const int s = consumed % kRelayStages;
+            if (!mbar_wait_bounded(&c.bar[s], (consumed / kRelayStages) & 1, status)) return false;
+            const uint8_t *st = c.ring + s * kStageBytesR;
+            {   // 2 tiles x 64 scale bytes (row w's four blocks in a word): one word per lane, to (e, e) pairs
+                const int tile = lane >> 4, w = lane & 15;
+                const uint32_t word = *reinterpret_cast<const uint32_t *>(st + tile * kGroupBytes + 512 + 4 * w);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float e = e4m3_alu((word >> (8 * j)) & 0xFFu);
+                    *reinterpret_cast<float2 *>(c.e4p + ((tile * 4 + j) * 8 + (w & 7)) * 4 + (w >> 3) * 2) = make_float2(e, e);
+                }
+            }
+            __syncwarp();
+            group_products(st, c.e4p, act + gl * 64, cs + gl * 256, lane, p);
+            ++consumed;
+            __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
+            issue();
+            return true;
+        };
+        uint64_t pre[kPre][4][4];
+        const int npre = sg < kPre ? sg : kPre;
+#pragma unroll
+        for (int gl = 0; gl < kPre; ++gl)
+            if (gl < npre && !group(gl, pre[gl])) ok = false;
+        // the chain so far
+        uint64_t acc[4];
+        const int par = u & 1;
+        if (c.part == 0) {
+            acc[0] = acc[1] = acc[2] = acc[3] = 0;
+        } else {
+            asm volatile("bar.sync %0, 64;" ::"r"(c.bar_in) : "memory");
+            const uint64_t *m = c.mail + (par * 32 + lane) * 4;
+            acc[0] = m[0], acc[1] = m[1], acc[2] = m[2], acc[3] = m[3];
+        }
+#pragma unroll
+        for (int gl = 0; gl < kPre; ++gl)
+            if (gl < npre)
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], pre[gl][j][q]);
+        for (int gl = npre; gl < sg; ++gl) {
+            uint64_t p[4][4];
+            if (!group(gl, p)) ok = false;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[j][q]);
+        }
+        if (c.part + 1 < c.wpu) {
+            uint64_t *m = c.mail_next + (par * 32 + lane) * 4;
+            m[0] = acc[0], m[1] = acc[1], m[2] = acc[2], m[3] = acc[3];
+            asm volatile("bar.sync %0, 64;" ::"r"(c.bar_out) : "memory");
+        } else {
+            // y = acc * global * 1 (engine/src/kernels.cpp:1320); y0: tile A (gid: t 2tig, 2tig+1; gid+8: ...), y1: B
+            float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
+            float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                y0[i] = __fmul_rn(y0[i], U.g0);
+                y1[i] = __fmul_rn(y1[i], U.g1);
+            }
+            epi(U, y0, y1, gid, tig);
+        }
+    }
+    // copies still in flight after a failed wait: waited for (bounded) before the shared memory is released
+    for (; !ok && consumed < issued; ++consumed) mbar_wait_bounded(&c.bar[consumed % kRelayStages], (consumed / kRelayStages) & 1, nullptr);
+    return ok;
+}
+
+// The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu.
+__device__ inline RelayCtx make_ctx(uint8_t *smem_warps, int sg_max, int wpu) {
+    const int warp = threadIdx.x >> 5;
+    const int wb = warp_smem_bytes(sg_max);
+    uint8_t *base = smem_warps + static_cast<size_t>(warp) * wb;
+    RelayCtx c;
+    c.ring = base;
+    c.bar = reinterpret_cast<uint64_t *>(base + kRelayStages * kStageBytesR);
+    c.e4p = reinterpret_cast<float *>(base + kRelayStages * kStageBytesR + kRelayStages * 8);
+    c.img = base + kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8;
+    c.mail = reinterpret_cast<uint64_t *>(c.img + warp_act_bytes(sg_max));
+    c.wpu = wpu;
+    c.part = warp % wpu;
+    c.sg = 0;
+    const int slot = warp / wpu;
+    c.bar_in = c.part > 0 ? 1 + slot * (wpu - 1) + (c.part - 1) : 0;
+    c.bar_out = c.part + 1 < wpu ? 1 + slot * (wpu - 1) + c.part : 0;
+    c.mail_next = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(c.mail) + wb);   // the next warp's mailbox
+    if ((threadIdx.x & 31) == 0)
+        for (int s = 0; s < kRelayStages; ++s) mbar_init(&c.bar[s], 1);
+    fence_barrier_init();
+    __syncwarp();
+    return c;
+}
+
+}  // namespace gcu

@@ -1,0 +1,156 @@
+/* geode_cuda.h - libgeode_cuda.so: the CUDA (B200, sm_100a) backend of the engine's speculative-decoding verify
+ * step, as a C ABI with no CUDA or torch type in it, so the engine can dlopen it beside its CPU, Adreno and Hexagon
+ * backends exactly as it opens libgeode_npu.so (engine/src/model.cpp:2255-2320, npu/host/npu_api.h:12-40).
+ *
+ * Two layers:
+ *   1. The backend (gcuda_*): an opaque handle that owns the model's weights in device memory (adopted from the
+ *      pack's bytes), the conversation's device state (Gated DeltaNet conv / recurrent states, the int8 KV cache)
+ *      and the verify step. It replaces the Adreno branch of Model::verify_n / verify_keep
+ *      (engine/src/model.cpp:1529-1592, 1594-1634) and the acceptance of geode_generate
+ *      (engine/src/geode.cpp:327-350).
+ *   2. Operators (gcuda_op_*): the kernels one at a time on caller-owned device buffers (a CUDA stream passed as
+ *      void *), the products Model::matmul / matmul_bf16 / quantize_activation / route_topk compute
+ *      (engine/src/model.cpp:3336-3495, engine/src/kernels.cpp:1254-1322, engine/src/model.cpp:4021-4065).
+ *
+ * Conventions (as npu_api.h): 0 = ok, negative = an error; the message of the last error via gcuda_last_error.
+ * A handle is driven by one thread at a time (engine/include/geode/geode.h:6-7); it runs on one device and one
+ * CUDA stream of its own. Host buffers passed in are read or written before the call returns; adopted weights
+ * are copied to the device (the caller's bytes are not kept).
+ */
+#ifndef GEODE_CUDA_H
+#define GEODE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GCUDA_OK 0
+#define GCUDA_E_ARG (-1)      /* a bad argument (shape, id, batch size, position) */
+#define GCUDA_E_CUDA (-2)     /* a CUDA runtime error */
+#define GCUDA_E_DEVICE (-3)   /* a kernel reported an error (a bounded wait that gave up, a bad token id) */
+#define GCUDA_E_MEMORY (-4)   /* device memory exhausted */
+#define GCUDA_E_STATE (-5)    /* a call out of order (verify before setup, keep without a verified batch) */
+
+typedef struct gcuda gcuda;
+
+/* ------------------------------------------------------------------------------------------- the backend ---- */
+
+/* The model geometry (engine/src/pack.hpp:31-60 ModelConfig; dense = arch "qwen35"). */
+typedef struct {
+    int hidden, n_layers, vocab;
+    float eps;
+    int n_heads, n_kv_heads, head_dim, rope_dim;
+    float rope_theta;
+    int gdn_k_heads, gdn_v_heads, gdn_k_dim, gdn_v_dim, conv_kernel;
+    int n_experts, top_k, moe_ff, shared_ff;
+    int dense;
+    int context;      /* KV positions to hold (Model's context_length, engine/src/model.hpp:295) */
+    int max_tokens;   /* the largest verified batch (spec_tokens, engine/src/model.hpp:197), 2..8 */
+} gcuda_shape;
+
+/* One layer's tensors, as ids returned by the gcuda_adopt_* calls (-1 where the layer has none); the pack's names
+ * (engine/src/model.cpp:94-156). */
+typedef struct {
+    int attn;
+    int in_norm, post_norm;
+    int qkv, z, out, a, b, A_log, dt_bias, conv, gnorm; /* linear_attn.* (Gated DeltaNet) */
+    int q, k, v, o, q_norm, k_norm;                     /* self_attn.* (gated attention) */
+    int sh_gate, sh_up, sh_down;                        /* mlp.shared_expert.* (or the dense mlp.*) */
+    int router, shared_gate;                            /* mlp.gate, mlp.shared_expert_gate (bf16) */
+    int experts;                                        /* gcuda_adopt_experts */
+} gcuda_layer;
+
+/* Opens device `device` (its own stream). NULL with the reason in err when CUDA or the device is unusable. */
+gcuda *gcuda_open(int device, char *err, int err_len);
+void gcuda_close(gcuda *g);
+/* The last error's message (0 = none). */
+int gcuda_last_error(gcuda *g, char *buf, int len);
+
+/* A q4 matrix in the pack's layout (rows x cols; each row cols/2 code bytes, then cols/16 E4M3 scale bytes, level
+ * 2c+1 for c < 8, -(2(c-8)+1) above), copied to the device in the GEMV's tile layout (the same bytes, permuted
+ * within 16-row tiles). cols a multiple of 64. Its id (>= 0), or < 0. Mirrors gnpu_adopt_q4 (npu/host/npu_api.h:34). */
+int gcuda_adopt_q4(gcuda *g, const uint8_t *data, int64_t rows, int64_t cols, size_t row_bytes, float global);
+/* f32 or bf16 parameters (norm weights, conv taps, A_log, dt_bias, router / gate / a / b rows), copied as they are. */
+int gcuda_adopt_raw(gcuda *g, const void *data, size_t bytes);
+/* One layer's routed experts: n blocks of stride bytes (gate_up [2 ff][hidden] then down [hidden][ff], q4,
+ * engine/src/pack.cpp:333-337) and their globals scales[n][2] (mlp.experts.scales). Its id, or < 0. */
+int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, const float *scales);
+/* The model: the geometry, the layers, the embedding (q4), lm_head (q4) and norm.weight ids. Allocates the state
+ * (context positions) and the scratch, and records the verify step as CUDA graphs. */
+int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, int embed, int lm_head, int final_norm);
+
+/* Model::verify_n (engine/src/model.cpp:1483): n tokens (toks[0] the last accepted token, then the drafts) at the
+ * next positions through every layer; logits [n][vocab] (host; NULL: left on the device) and hidden [n][hidden]
+ * (the rows after the final norm, the MTP layer's input; NULL: not wanted). The position moves on by n. */
+int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden);
+/* Model::verify_keep (engine/src/model.cpp:1594): keep the first `kept` (1 .. n-1) of the last verified batch - the
+ * Gated DeltaNet states as after token kept-1, the position back by n - kept. */
+int gcuda_keep(gcuda *g, int kept);
+int gcuda_position(gcuda *g);
+/* The conversation from the start (position 0, zero states). */
+int gcuda_reset(gcuda *g);
+
+/* Sampling parameters (engine/src/sampler.hpp:11-15). */
+typedef struct {
+    float temperature; /* 0 = greedy */
+    float top_p;       /* 1 = off */
+    int top_k;         /* 0 = off (then 1024 candidates, engine/src/sampler.cpp:11) */
+} gcuda_sampling;
+
+/* The acceptance of geode_generate (engine/src/geode.cpp:327-350) on the last verified batch's logits (on the
+ * device): row i sampled with uniforms[i] (the draw Sampler::sample makes for row i, in [0,1); ignored when
+ * greedy); draft i+1 stands while row i's sample equals toks[i+1] and is not in stops. Returns kept (1 .. n) in
+ * *kept, the first sample that is no draft in *next, and every row's sample in samples[n] (NULL: not wanted). */
+int gcuda_accept(gcuda *g, const gcuda_sampling *s, const double *uniforms, const int *stops, int n_stops, int *kept,
+                 int *next, int *samples);
+/* Speculative (rejection) sampling (Leviathan et al. 2023) over S sequences x (k+1) target rows and k draft rows of V
+ * logits already on the device (target [S][k+1][V], draft [S][k][V]), Philox4x32-10 uniforms (key seed, counter
+ * (sequence, row)); accepted[S] and next[S] on the host. Not in the reference: no counterpart there. */
+int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, const int *drafts, int S, int k, int V,
+                      const gcuda_sampling *s, uint64_t seed, int *accepted, int *next);
+
+/* The conversation's state to and from the host, in the reference's own buffer layouts (engine/src/model.hpp:548-555):
+ * conv [n_gdn][conv_dim][K-1] f32, gdn [n_gdn][nv][dv/16][dk][16] f32, kv [n_attn][2][positions][nkv*hd] int8,
+ * kv_scale [n_attn][2][positions][nkv] f32 for positions 0..pos-1; pos the new position (put). */
+int gcuda_state_get(gcuda *g, float *conv, float *gdn, int8_t *kv, float *kv_scale, int positions);
+int gcuda_state_put(gcuda *g, const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, int pos);
+
+/* Device pointers of the last batch's results (the verify step's outputs stay resident): logits [max_tokens][vocab]. */
+const float *gcuda_device_logits(gcuda *g);
+/* The verify step with the tokens already on the device (d_toks: n int32) and the results left there - the resident
+ * form of gcuda_verify for callers that keep their batches on the GPU. */
+int gcuda_verify_device(gcuda *g, const int *d_toks, int n);
+/* Milliseconds of the last gcuda_verify / gcuda_verify_device on the device (CUDA events on the handle's stream). */
+float gcuda_last_ms(gcuda *g);
+/* Kernels this library launched since the handle opened. */
+uint64_t gcuda_launches(gcuda *g);
+
+/* ------------------------------------------------------------------------------------------- operators ---- */
+/* All on caller-owned device memory, enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ * They return once enqueued. */
+
+/* tiles: the bytes gcuda_op_q4_tiled_bytes gives; the pack's rows -> the GEMV's tile layout */
+size_t gcuda_op_q4_tiled_bytes(int64_t rows, int64_t cols);
+int gcuda_op_q4_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint8_t *d_tiles, void *stream);
+/* quantize_activation for n rows of cols floats (engine/src/kernels.cpp:1254-1295): q [n][cols], scale and bsum
+ * [n][cols/16] */
+int gcuda_op_quantize(const float *d_x, int n, int cols, int8_t *d_q, float *d_scale, int32_t *d_bsum, void *stream);
+/* y[t][r] = matvec_rows_q_ref (engine/src/kernels.cpp:1304-1322) of the tiled matrix with n (<= 8) quantized rows;
+ * bit for bit the reference's int8 product. y [n][rows]. */
+int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float global, const int8_t *d_q,
+                     const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream);
+/* dequant_row (engine/src/kernels.cpp:1214-1228) of nrows rows (d_rows int64) of a tiled matrix: out [nrows][cols] */
+int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, const int64_t *d_rows, int nrows,
+                        float *d_out, void *stream);
+/* matvec_rows_bf16_multi (engine/src/kernels.cpp:1449-1518), bit for bit: y [n][rows] = W [rows][cols] x [n][cols] */
+int gcuda_op_bf16_gemv(const uint16_t *d_w, int rows, int cols, const float *d_x, int n, float *d_y, void *stream);
+/* route_topk (engine/src/model.cpp:4021-4065) for n rows of E logits: ids [n][K], weights [n][K] */
+int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, float *d_weights, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -284,6 +284,18 @@ def oracle_matvec_q(lib, packed: np.ndarray, rows: int, cols: int, glob: float, 
     return ys
 
 
+class GoMt64(C.Structure):
+    _fields_ = [("mt", C.c_uint64 * 312), ("mti", C.c_int)]
+
+
+def oracle_uniforms(lib, seed: int, n: int) -> np.ndarray:
+    """The first n draws the reference's Sampler makes from mt19937_64(seed): generate_canonical<double, 53>."""
+    g = GoMt64()
+    lib.go_mt64_seed(C.byref(g), C.c_uint64(seed))
+    lib.go_canonical.argtypes = [C.c_void_p]
+    return np.array([lib.go_canonical(C.byref(g)) for _ in range(n)], dtype=np.float64)
+
+
 def oracle_route_topk(lib, logits: np.ndarray, K: int):
     logits = np.ascontiguousarray(logits, np.float32)
     E = logits.shape[-1]

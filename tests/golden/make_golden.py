@@ -1,0 +1,130 @@
+"""Regenerates the golden fixtures in this folder from the REFERENCE engine's own code (oracle/_ref/libgeode_ref.so,
+compiled from the reference sources by oracle/Makefile): every output here was computed by the reference, not by the
+restatement, so tests/test_oracle.py pins the restatement to the reference wherever the reference build is absent
+(the GPU box). Run from the repository root: python tests/golden/make_golden.py
+
+- kernels.npz: the E4M3 table, quantize_activation, matvec_rows_q_multi, matvec_rows_bf16_multi, route_topk, rmsnorm,
+  fast_exp (engine/src/kernels.cpp, engine/src/model.cpp:4021), the q4 block quantizer (engine/src/yue2_q4.cpp:88) and
+  the sampler's uniform stream (std::mt19937_64 + generate_canonical, engine/src/sampler.cpp:45);
+- accept.npz: the acceptance rule (engine/src/geode.cpp:327-350) around geode::Sampler, greedy and sampled;
+- model_moe.npz / model_dense.npz: Model::forward_batch over a prompt and a 5-token verify batch on a tiny synthetic
+  pack (written by geode_b200/synth.py with the seed stored), every logit and the per-layer trace.
+"""
+import ctypes as C
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+from geode_b200 import synth  # noqa: E402
+import oracle_py as op  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def kernels(R):
+    rng = np.random.default_rng(20261201)
+    g = {}
+    g["e4m3"] = np.array([R.ref_e4m3_value(b) for b in range(256)], np.float32)
+    x = (rng.standard_normal(512) * 3).astype(np.float32)
+    x[:16] = 0.0
+    q, s, b = np.zeros(512, np.int8), np.zeros(32, np.float32), np.zeros(32, np.int32)
+    R.ref_quantize_activation(x.ctypes.data, 512, q.ctypes.data, s.ctypes.data, b.ctypes.data)
+    g.update(act_x=x, act_q=q, act_scale=s, act_bsum=b)
+    w, gl = synth.q4_quantize((rng.standard_normal((32, 512)) * 0.02).astype(np.float32))
+    xs = rng.standard_normal((5, 512)).astype(np.float32)
+    y = np.zeros((5, 32), np.float32)
+    R.ref_matvec_q(w.ctypes.data, 32, 512, C.c_float(gl), 6, 5, xs.ctypes.data, y.ctypes.data)
+    g.update(w_packed=w, w_rows=32, w_cols=512, w_global=np.float32(gl), w_x=xs, w_y=y)
+    bw = synth.bf16_bits((rng.standard_normal((33, 256)) * 0.05).astype(np.float32))
+    bx = rng.standard_normal((5, 256)).astype(np.float32)
+    by = np.zeros((5, 33), np.float32)
+    R.ref_matvec_bf16_multi(bw.ctypes.data, 33, 256, 5, bx.ctypes.data, by.ctypes.data)
+    g.update(bf_w=bw, bf_x=bx, bf_y=by)
+    lg = (rng.standard_normal((8, 256)) * 2).astype(np.float32)
+    ids, wt = np.zeros((8, 8), np.int32), np.zeros((8, 8), np.float32)
+    for t in range(8):
+        R.ref_route_topk(lg[t].ctypes.data, 256, 8, ids[t].ctypes.data, wt[t].ctypes.data)
+    g.update(rt_logits=lg, rt_k=8, rt_ids=ids, rt_w=wt)
+    rx = (rng.standard_normal(2048) * 4).astype(np.float32)
+    rw = (rng.standard_normal(2048) * 0.1).astype(np.float32)
+    ry = np.zeros(2048, np.float32)
+    R.ref_rmsnorm(rx.ctypes.data, rw.ctypes.data, ry.ctypes.data, 2048, C.c_float(1e-6), 1)
+    g.update(rn_x=rx, rn_w=rw, rn_y=ry)
+    fx = np.concatenate([rng.standard_normal(200) * 20, [-100.0, 100.0, 0.0, -87.0, 88.0, 1e-8]]).astype(np.float32)
+    g.update(fe_x=fx, fe_y=np.array([R.ref_fast_exp(float(v)) for v in fx], np.float32))
+    u = np.zeros(16, np.float64)
+    R.ref_uniforms(C.c_uint64(1234), 16, u.ctypes.data)
+    g.update(mt_seed=1234, mt_u=u)
+    # the q4 quantizer: blocks through the reference's q4_block, assembled into the pack's row layout
+    qw = (rng.standard_normal((8, 256)) * 0.02).astype(np.float32)
+    qw[0, :16] = 0.0
+    s2 = np.float32(np.float32(np.abs(qw).max()) * np.float32(1.25) / np.float32(15.0 * 448.0))
+    packed = np.zeros((8, 256 // 16 * 9), np.uint8)
+    for r in range(8):
+        for blk in range(16):
+            sb = C.c_uint8(0)
+            codes = np.zeros(16, np.uint8)
+            R.ref_q4_block(np.ascontiguousarray(qw[r, 16 * blk: 16 * blk + 16]).ctypes.data, C.c_float(s2), C.byref(sb),
+                           codes.ctypes.data)
+            packed[r, 8 * blk: 8 * blk + 8] = codes[0::2] | (codes[1::2] << 4)
+            packed[r, 128 + blk] = sb.value
+    g.update(qz_w=qw, qz_s2=s2, qz_packed=packed)
+    np.savez_compressed(os.path.join(OUT, "kernels.npz"), **g)
+
+
+def accept(R):
+    rng = np.random.default_rng(77)
+    V = 4096
+    cases = [(0.0, 1.0, 0), (0.7, 0.95, 20), (0.7, 1.0, 0), (1.3, 0.8, 40), (0.5, 0.9, 0), (0.0, 1.0, 0)]
+    rows = (rng.standard_normal((len(cases), 5, V)) * 3).astype(np.float32)
+    batch = rng.integers(0, V, (len(cases), 5)).astype(np.int32)
+    params, kept, nxt, samples = [], [], [], []
+    for c, (T, P, K) in enumerate(cases):
+        for i in range(c % 5):   # planted drafts that stand (greedy rows)
+            batch[c, i + 1] = int(np.argmax(rows[c, i]))
+        seed = int(rng.integers(0, 2 ** 40))
+        n = C.c_int(0)
+        s = np.zeros(5, np.int32)
+        k = R.ref_accept(rows[c].ctypes.data, 5, V, batch[c].ctypes.data, T, P, K, C.c_uint64(seed), None, 0, C.byref(n),
+                         s.ctypes.data)
+        params.append((T, P, K, seed))
+        kept.append(k)
+        nxt.append(n.value)
+        samples.append(s)
+    np.savez_compressed(os.path.join(OUT, "accept.npz"), rows=rows, batch=batch, params=np.array(params, np.float64),
+                        kept=np.array(kept), next=np.array(nxt), samples=np.array(samples))
+
+
+def model(arch, name, seed=21, attn_block=64):
+    shape = synth.tiny_shape(arch, n_layers=4, ctx=640)
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_pack(d, shape, seed=seed)
+        ref = op.Reference(d, threads=4, ctx=shape.ctx, attn_block=attn_block)
+        rng = np.random.default_rng(seed + 1)
+        prompt = rng.integers(0, shape.vocab, 100).astype(np.int32)
+        toks = rng.integers(0, shape.vocab, 5).astype(np.int32)
+        r1 = ref.forward(prompt)
+        r2 = ref.forward(toks, trace=True)
+        out = dict(seed=seed, attn_block=attn_block, prompt=prompt, toks=toks, prompt_logits=r1["logits"],
+                   logits=r2["logits"])
+        for k in ("x", "mixer", "moe", "out", "ids", "weights"):
+            out["trace_" + k] = r2["trace"][k]
+        ref.close()
+    np.savez_compressed(os.path.join(OUT, name + ".npz"), **out)
+
+
+if __name__ == "__main__":
+    if not op.have_reference():
+        sys.exit("build the reference first: make -C oracle ref")
+    R = op.reference_lib()
+    kernels(R)
+    accept(R)
+    model("qwen35moe", "model_moe")
+    model("qwen35", "model_dense")
+    print("written to", OUT)

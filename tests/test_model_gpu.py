@@ -1,0 +1,130 @@
+"""GPU parity of the whole verify step (gcuda_verify / gcuda_keep / gcuda_accept) against the C oracle, itself pinned
+bit for bit to the reference engine (tests/test_oracle.py).
+
+- logits of the K+1 verified rows within max|d| <= 1e-2 x (max - min) of the oracle's row (fp32 accumulation; the GPU's
+  exp / sin / cos and its attention order differ in the last bits, so the model is not bit-exact end to end);
+- rollback: after keep(kept) the next batch's logits again within the tolerance (the Gated DeltaNet states restored
+  as after token kept-1, the KV rows past it written over);
+- acceptance: bit-exact given the same logits - the GPU's samples, kept and next equal the oracle's rule on the GPU's
+  own logits, greedy and sampled (the reference's uniform stream, mt19937_64 -> generate_canonical).
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from geode_b200 import synth  # noqa: E402
+import oracle_py as op  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _shapes():
+    tiny = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    heads = synth.ModelShape("heads-moe", "qwen35moe", 512, 4, 2048, synth.hybrid_types(4), n_heads=4, n_kv_heads=2,
+                             head_dim=256, gdn_k_heads=2, gdn_v_heads=4, gdn_k_dim=128, gdn_v_dim=128, n_experts=32,
+                             top_k=8, moe_ff=128, shared_ff=128, ctx=1100)
+    dense = synth.tiny_shape("qwen35", n_layers=4, ctx=640)
+    return {"tiny-moe": tiny, "heads-moe": heads, "tiny-dense": dense}
+
+
+SHAPES = _shapes()
+
+
+@pytest.fixture(scope="module", params=list(SHAPES))
+def setup(request, tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from geode_b200.backend import Backend
+    shape = SHAPES[request.param]
+    d = str(tmp_path_factory.mktemp(request.param))
+    synth.write_pack(d, shape, seed=11)
+    ora = op.Oracle(d)
+    be = Backend(d, context=shape.ctx, max_tokens=5)
+    rng = np.random.default_rng(5)
+    st = ora.new_state(shape.ctx)
+    prompt = rng.integers(0, shape.vocab, 300 if shape.ctx > 1000 else 120)
+    ora.forward(st, prompt, logits=False)
+    be.state_put(st.conv, st.gdn, st.kv.reshape(-1), st.kvs.reshape(-1), st.pos)
+    yield shape, ora, be, st, rng
+    be.close()
+
+
+def _close(got, ref):
+    rng_ = ref.max(axis=-1) - ref.min(axis=-1)
+    err = np.abs(got - ref).max(axis=-1)
+    return err, rng_, bool(np.all(err <= TOL * rng_))
+
+
+def test_verify_logits_and_rollback(setup):
+    shape, ora, be, st, rng = setup
+    for step in range(3):
+        toks = rng.integers(0, shape.vocab, 5)
+        before = st.copy()
+        ref = ora.forward(st, toks, logits=True, hidden=True)
+        got, hid = be.verify(toks, logits=True, hidden=True)
+        err, rr, ok = _close(got, ref["logits"])
+        assert ok, f"step {step}: max|d| {err} vs range {rr}"
+        herr = np.abs(hid - ref["hidden"]).max()
+        assert herr <= TOL * (np.abs(ref["hidden"]).max() + 1e-6), herr
+        kept = int(rng.integers(1, 5))
+        be.keep(kept)
+        st.__dict__.update(before.copy().__dict__)
+        ora.forward(st, toks[:kept], logits=False)
+        assert be.pos == st.pos
+
+
+def test_state_roundtrip(setup):
+    shape, ora, be, st, rng = setup
+    conv = np.zeros_like(st.conv)
+    gdn = np.zeros_like(st.gdn)
+    kv = np.zeros_like(st.kv)
+    kvs = np.zeros_like(st.kvs)
+    n_attn = max(1, ora.n_attn)
+    be.state_get(conv, gdn, kv.reshape(-1), kvs.reshape(-1), st.pos)
+    # the bridge keeps the reference's layouts: the KV rows for positions < pos, [layer][K|V][pos][row]
+    assert np.allclose(conv, st.conv, rtol=1e-3, atol=1e-3)
+    assert np.allclose(gdn, st.gdn, rtol=1e-2, atol=1e-3)
+
+
+def _planted(ora, st, t0, j, rng, vocab):
+    """t0, then j drafts that the (greedy) model itself predicts, then random ones: a batch where the first j drafts
+    stand (engine/src/geode.cpp:327-350), so partial acceptance and rollback really happen."""
+    s2 = st.copy()
+    toks = [int(t0)]
+    for i in range(4):
+        if i < j:
+            lg = ora.forward(s2, [toks[-1]], logits=True)["logits"][0]
+            toks.append(int(np.argmax(lg)))
+        else:
+            toks.append(int(rng.integers(0, vocab)))
+    return np.array(toks, dtype=np.int32)
+
+
+@pytest.mark.parametrize("temperature,top_p,top_k", [(0.0, 1.0, 0), (0.7, 0.95, 20), (0.7, 1.0, 0), (1.3, 0.8, 0)])
+def test_accept_bit_exact(setup, temperature, top_p, top_k):
+    shape, ora, be, st, rng = setup
+    O = op.oracle_lib()
+    for rep in range(3):
+        j = int(rng.integers(0, 5))
+        toks = _planted(ora, st, rng.integers(0, shape.vocab), j, rng, shape.vocab)
+        before = st.copy()
+        got, _ = be.verify(toks, logits=True)
+        seed = int(rng.integers(0, 2 ** 31))
+        u = op.oracle_uniforms(O, seed, 5)
+        kept, nxt, samples = be.accept(temperature, top_p, top_k, uniforms=u)
+        ref_samples = np.zeros(5, np.int32)
+        ref_next = op.C.c_int(0)
+        ref_kept = O.go_accept(got.ctypes.data, 5, shape.vocab, toks.ctypes.data, temperature, top_p, top_k,
+                               op.C.c_uint64(seed), None, 0, op.C.byref(ref_next), ref_samples.ctypes.data)
+        assert kept == ref_kept and nxt == ref_next.value and np.array_equal(samples, ref_samples), \
+            (kept, ref_kept, nxt, ref_next.value, samples, ref_samples)
+        if temperature == 0.0:
+            assert kept >= min(5, j + 1) - (1 if j else 0)   # the planted drafts (nearly always) stand
+        if kept < 5:
+            be.keep(kept)
+        st.__dict__.update(before.copy().__dict__)
+        ora.forward(st, toks[:kept], logits=False)
+        assert be.pos == st.pos

@@ -1,0 +1,125 @@
+"""GPU parity of the operator layer (include/geode_cuda.h gcuda_op_*) against the C oracle, which itself is pinned
+bit for bit to the reference engine (tests/test_oracle.py). Every check here is bit-exact: the q4 GEMV, the
+activation quantizer, dequantized weights, the bf16 router GEMV and route_topk all reproduce the reference's
+integer and float operation order."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from geode_b200 import cuda_lib, synth  # noqa: E402
+import oracle_py as op  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev(a: np.ndarray):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _p(t) -> int:
+    return t.data_ptr()
+
+
+@pytest.fixture(scope="module")
+def L():
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    return cuda_lib()
+
+
+@pytest.fixture(scope="module")
+def O():
+    return op.oracle_lib()
+
+
+def _tiles(L, packed, rows, cols):
+    d_pack = _dev(packed)
+    tb = L.gcuda_op_q4_tiled_bytes(rows, cols)
+    d_t = torch.zeros(tb, dtype=torch.uint8, device="cuda")
+    assert L.gcuda_op_q4_relayout(_p(d_pack), rows, cols, _p(d_t), None) == 0
+    return d_t
+
+
+def _quant(L, x):
+    n, cols = x.shape
+    d_x = _dev(x.astype(np.float32))
+    q = torch.zeros((n, cols), dtype=torch.int8, device="cuda")
+    s = torch.zeros((n, cols // 16), dtype=torch.float32, device="cuda")
+    b = torch.zeros((n, cols // 16), dtype=torch.int32, device="cuda")
+    assert L.gcuda_op_quantize(_p(d_x), n, cols, _p(q), _p(s), _p(b), None) == 0
+    return q, s, b
+
+
+@pytest.mark.parametrize("cols", [512, 2048, 4096])
+def test_quantize_bit_exact(L, O, cols):
+    rng = np.random.default_rng(cols)
+    x = rng.standard_normal((5, cols)).astype(np.float32) * 3
+    x[0, :16] = 0.0  # an all-zero block: scale 0, codes 0
+    q, s, b = _quant(L, x)
+    torch.cuda.synchronize()
+    for t in range(5):
+        rq, rs, rb = op.oracle_quantize_activation(O, x[t])
+        assert np.array_equal(q[t].cpu().numpy(), rq)
+        assert np.array_equal(s[t].cpu().numpy().view(np.uint32), rs.view(np.uint32))
+        assert np.array_equal(b[t].cpu().numpy(), rb)
+
+
+@pytest.mark.parametrize("rows,cols,n", [(64, 512, 1), (1024, 2048, 5), (96, 4096, 3), (256, 2048, 8)])
+def test_q4_gemv_bit_exact(L, O, rows, cols, n):
+    rng = np.random.default_rng(rows + cols + n)
+    w = rng.standard_normal((rows, cols)).astype(np.float32) * 0.02
+    packed, g = synth.q4_quantize(w)
+    d_t = _tiles(L, packed, rows, cols)
+    x = rng.standard_normal((n, cols)).astype(np.float32)
+    q, s, b = _quant(L, x)
+    y = torch.zeros((n, rows), dtype=torch.float32, device="cuda")
+    assert L.gcuda_op_q4_gemv(_p(d_t), rows, cols, g, _p(q), _p(s), _p(b), n, _p(y), None) == 0
+    torch.cuda.synchronize()
+    ref = op.oracle_matvec_q(O, packed, rows, cols, g, x)
+    got = y.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), np.abs(got - ref).max()
+
+
+def test_q4_dequant_bit_exact(L):
+    rng = np.random.default_rng(7)
+    rows, cols = 96, 2048
+    packed, g = synth.q4_quantize(rng.standard_normal((rows, cols)).astype(np.float32) * 0.02)
+    d_t = _tiles(L, packed, rows, cols)
+    sel = np.array([0, 5, 17, 63, 95], dtype=np.int64)
+    out = torch.zeros((len(sel), cols), dtype=torch.float32, device="cuda")
+    assert L.gcuda_op_q4_dequant(_p(d_t), cols, g, _p(_dev(sel)), len(sel), _p(out), None) == 0
+    torch.cuda.synchronize()
+    ref = synth.q4_dequant(packed[sel], cols, g)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,n", [(257, 5), (16, 2)])
+def test_bf16_gemv_bit_exact(L, O, rows, n):
+    rng = np.random.default_rng(rows)
+    cols = 2048
+    w = synth.bf16_bits(rng.standard_normal((rows, cols)).astype(np.float32) * 0.05)
+    x = rng.standard_normal((n, cols)).astype(np.float32)
+    y = torch.zeros((n, rows), dtype=torch.float32, device="cuda")
+    assert L.gcuda_op_bf16_gemv(_p(_dev(w)), rows, cols, _p(_dev(x)), n, _p(y), None) == 0
+    torch.cuda.synchronize()
+    ref = np.zeros((n, rows), np.float32)
+    O.go_matvec_bf16(w.ctypes.data, rows, cols, n, x.ctypes.data, ref.ctypes.data)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+
+
+def test_route_topk_bit_exact(L, O):
+    rng = np.random.default_rng(3)
+    n, E, K = 64, 256, 8
+    lg = (rng.standard_normal((n, E)) * 2).astype(np.float32)
+    lg[1, 10] = lg[1, 20] = lg[1].max() + 1  # an exact tie: the lower index first
+    ids = torch.zeros((n, K), dtype=torch.int32, device="cuda")
+    w = torch.zeros((n, K), dtype=torch.float32, device="cuda")
+    assert L.gcuda_op_route_topk(_p(_dev(lg)), n, E, K, _p(ids), _p(w), None) == 0
+    torch.cuda.synchronize()
+    for t in range(n):
+        rid, rw = op.oracle_route_topk(O, lg[t], K)
+        assert np.array_equal(ids[t].cpu().numpy(), rid)
+        assert np.array_equal(w[t].cpu().numpy().view(np.uint32), rw.view(np.uint32))
