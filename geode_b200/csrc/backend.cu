@@ -78,7 +78,7 @@ struct gcuda {
     uint32_t *d_status = nullptr;
     float *x = nullptr, *hf = nullptr, *big = nullptr, *zb = nullptr, *ab = nullptr, *kb = nullptr, *vb = nullptr,
           *qn = nullptr, *rlog = nullptr, *eout = nullptr, *shout = nullptr, *part = nullptr, *logits = nullptr,
-          *hid = nullptr, *core_f = nullptr, *inv_freq = nullptr;
+          *hid = nullptr, *core_f = nullptr, *inv_freq = nullptr, *convd = nullptr;
     ActBuf hq, core, amid, shact;
     RouteOut *route = nullptr;
     GemvUnit *units = nullptr;
@@ -178,11 +178,14 @@ void swiglu_units(std::vector<GemvUnit> &out, const DevTensor &gt, const DevTens
     }
 }
 
-int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl) {
+// act_cols: the width of the activation rows the units multiply (0: the buffer's own width); the rows are packed
+// at that width (a narrower writer, e.g. the Gated DeltaNet core, packs them so)
+int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, int act_cols = 0) {
     StaticGemv p{};
     p.units = g->units + u0;
     p.n_units = nu;
     p.act = act.set();
+    if (act_cols > 0) p.act = ActSet{act.q, act.scale, act.bsum, act_cols, act.n, act_cols, act_cols / 16};
     p.ncols = n;
     p.status = g->d_status;
     return launch_static_gemv(p, g->st, pdl);
@@ -272,6 +275,9 @@ int enqueue_step(gcuda *g, int n) {
             a.scale = g->core.scale;
             a.bsum = g->core.bsum;
             a.core_f = g->core_f;
+            LAUNCH_OK(launch_ex(k_gdn_conv, dim3((g->conv_dim + 127) / 128), dim3(128), 0, g->st, pdl, a, g->conv_dim,
+                                g->convd));
+            a.proj = g->convd;
             cudaLaunchConfig_t cfg{};
             const int S = s.gdn_v_dim / 16;
             cfg.gridDim = dim3(s.gdn_v_heads * S);
@@ -292,7 +298,7 @@ int enqueue_step(gcuda *g, int n) {
             else e = cudaLaunchKernelEx(&cfg, k_gdn<32>, a);
             count_launch();
             LAUNCH_OK(e);
-            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl));
+            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, g->vd));
         } else {
             RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
             AttnPrepArgs pa{};
@@ -354,7 +360,7 @@ int enqueue_step(gcuda *g, int n) {
             ma.bsum = g->core.bsum;
             ma.core_f = g->core_f;
             LAUNCH_OK(launch_ex(k_attn_merge, dim3((n * s.n_heads + 3) / 4), dim3(128), 0, g->st, pdl, ma));
-            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl));
+            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, s.n_heads * s.head_dim));
         }
         // x += mix happened in the output product's epilogue; h = rmsnorm(x, post_norm)
         RC_OK(norm(raw(L.post_norm), false, g->hf));
@@ -672,6 +678,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         !dalloc(g, &g->hf, static_cast<size_t>(T) * H) || !dalloc(g, &g->hid, static_cast<size_t>(T) * H) ||
         !dalloc(g, &g->big, static_cast<size_t>(T) * std::max(g->conv_dim, g->qw)) ||
         !dalloc(g, &g->zb, static_cast<size_t>(T) * std::max(1, g->vd)) ||
+        !dalloc(g, &g->convd, static_cast<size_t>(T) * std::max(1, g->conv_dim)) ||
         !dalloc(g, &g->ab, static_cast<size_t>(T) * std::max(1, 2 * s.gdn_v_heads)) ||
         !dalloc(g, &g->kb, static_cast<size_t>(T) * g->kvrow) || !dalloc(g, &g->vb, static_cast<size_t>(T) * g->kvrow) ||
         !dalloc(g, &g->qn, static_cast<size_t>(T) * s.n_heads * s.head_dim) ||
@@ -955,7 +962,8 @@ int gcuda_debug_read(gcuda *g, int what, void *out, size_t bytes) {
     cudaSetDevice(g->device);
     LAUNCH_OK(cudaStreamSynchronize(g->st));
     const void *src = what == 0 ? static_cast<const void *>(g->x) : what == 1 ? g->hf : what == 2 ? g->core_f
-                      : what == 3 ? static_cast<const void *>(g->route) : g->hid;
+                      : what == 3 ? static_cast<const void *>(g->route) : what == 4 ? g->hid : what == 5 ? g->convd
+                      : what == 6 ? g->ab : what == 7 ? g->zb : g->big;
     LAUNCH_OK(cudaMemcpy(out, src, bytes, cudaMemcpyDeviceToHost));
     return GCUDA_OK;
 }

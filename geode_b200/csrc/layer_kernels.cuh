@@ -147,6 +147,32 @@ struct GdnArgs {
     float *core_f;        // [n][vd] or NULL (tests)
 };
 
+// The causal depthwise convolution over [state (K-1 earlier inputs) | the n tokens] and silu_fast, for every channel
+// (engine/src/model.cpp:3555-3583), one thread per channel: conv outputs [n][conv_dim]; the state after each token
+// t < n-1 to backup slot t, the last to the state. (Its own kernel: the q and k channels are read by several value
+// heads, so the state may change only after every reader has read it.)
+__global__ void k_gdn_conv(GdnArgs a, int conv_dim, float *__restrict__ out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= conv_dim) return;
+    const int K = a.K;
+    const float *w = a.convw + static_cast<size_t>(ch) * K;
+    float st[8];
+    for (int k = 0; k < K - 1; ++k) st[k] = a.conv_st[static_cast<size_t>(ch) * (K - 1) + k];
+    for (int t = 0; t < a.n; ++t) {
+        const float in = a.proj[static_cast<size_t>(t) * conv_dim + ch];
+        float acc = 0.0f;
+        for (int k = 0; k < K - 1; ++k) acc = __fadd_rn(acc, __fmul_rn(w[k], st[k]));
+        acc = __fadd_rn(acc, __fmul_rn(w[K - 1], in));
+        for (int k = 0; k + 1 < K - 1; ++k) st[k] = st[k + 1];
+        if (K > 1) st[K - 2] = in;
+        out[static_cast<size_t>(t) * conv_dim + ch] = silu_fast_exact(acc);
+        if (t + 1 < a.n)
+            for (int k = 0; k < K - 1; ++k) a.conv_bk[t * a.bk_conv_stride + static_cast<size_t>(ch) * (K - 1) + k] = st[k];
+    }
+    for (int k = 0; k < K - 1; ++k) a.conv_st[static_cast<size_t>(ch) * (K - 1) + k] = st[k];
+}
+
 template <int DK>
 __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     constexpr int R = DK / 8;
@@ -159,36 +185,14 @@ __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     const int rep = a.nv / a.nk, kh = vh / rep;
     const int kd = a.nk * a.dk, vd = a.nv * a.dv;
     const int tid = threadIdx.x, n = a.n;
-    const int K = a.K;
-    const bool write_qk = (vh % rep == 0) && s == 0;
-    // 1. the convolution (and silu_fast) of this CTA's channels: q and k of key head kh, v columns of the strip
-    const int nch = 2 * DK + 16;
-    for (int c = tid; c < nch; c += blockDim.x) {
-        int ch;
-        if (c < DK) ch = kh * DK + c;                       // q
-        else if (c < 2 * DK) ch = kd + kh * DK + (c - DK);  // k
-        else ch = 2 * kd + vh * a.dv + s * 16 + (c - 2 * DK);
-        const bool writer = c >= 2 * DK || write_qk;
-        const float *w = a.convw + static_cast<size_t>(ch) * K;
-        float st[8];
-        for (int k = 0; k < K - 1; ++k) st[k] = a.conv_st[static_cast<size_t>(ch) * (K - 1) + k];
-        for (int t = 0; t < n; ++t) {
-            const float in = a.proj[static_cast<size_t>(t) * (2 * kd + vd) + ch];
-            float acc = 0.0f;
-            for (int k = 0; k < K - 1; ++k) acc = __fadd_rn(acc, __fmul_rn(w[k], st[k]));
-            acc = __fadd_rn(acc, __fmul_rn(w[K - 1], in));
-            for (int k = 0; k + 1 < K - 1; ++k) st[k] = st[k + 1];
-            if (K > 1) st[K - 2] = in;
-            const float y = silu_fast_exact(acc);
-            if (c < DK) s_q[t][c] = y;
-            else if (c < 2 * DK) s_k[t][c - DK] = y;
-            else s_v[t][c - 2 * DK] = y;
-            if (writer && t + 1 < n)
-                for (int k = 0; k < K - 1; ++k)
-                    a.conv_bk[t * a.bk_conv_stride + static_cast<size_t>(ch) * (K - 1) + k] = st[k];
-        }
-        if (writer)
-            for (int k = 0; k < K - 1; ++k) a.conv_st[static_cast<size_t>(ch) * (K - 1) + k] = st[k];
+    // 1. this CTA's conv outputs (k_gdn_conv, in a.proj): q and k of key head kh, the v columns of the strip
+    const int cd = 2 * kd + vd;
+    for (int c = tid; c < n * (2 * DK + 16); c += blockDim.x) {
+        const int t = c / (2 * DK + 16), cc = c % (2 * DK + 16);
+        const float *row = a.proj + static_cast<size_t>(t) * cd;
+        if (cc < DK) s_q[t][cc] = row[kh * DK + cc];
+        else if (cc < 2 * DK) s_k[t][cc - DK] = row[kd + kh * DK + (cc - DK)];
+        else s_v[t][cc - 2 * DK] = row[2 * kd + vh * a.dv + s * 16 + (cc - 2 * DK)];
     }
     // gates (engine/src/model.cpp:3604-3611): beta = sigmoid(b), decay = exp(-exp(A_log) * softplus(a + dt_bias))
     if (tid < n) {
