@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Benchmark of the speculative-decoding verify step at the Qwen3.6-35B-A3B shape (BASELINE cfg 3): 40 layers in the
+3:1 Gated DeltaNet : gated attention pattern, hidden 2048, 256 routed experts top-8 + a shared expert (ff 512), vocab
+248320, q4 weights (the engine's E4M3-scaled 16-value blocks), 1 accepted token + 4 drafts verified per step against
+a context of 8192 positions.
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+A step = the verify forward of 5 tokens (every row's logits), the greedy acceptance of the rows and the rollback of
+the Gated DeltaNet states to the last accepted token, chained on the device (gcuda_step_device). `value`: verified
+tokens/s of the whole job with the weights resident in HBM; `e2e`: the same through the C ABI with host buffers
+(gcuda_verify: tokens in, every logit out to pinned host memory; gcuda_accept; gcuda_keep). Weights are random q4
+bytes made on the device (the weights' values do not change the bytes streamed); the 8192-position KV cache and the
+recurrent states are random. `--impl reference` times the reference engine's own CPU path (oracle/_ref, compiled
+from the reference sources) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "verify tok/s at 35B-A3B shape, 4 drafts, 1/2/4/8 B200; % of HBM roofline"
+UNIT = "verified tokens/s"
+CTX = 8192
+NTOK = 5
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def step_bytes(shape, union_per_layer: float, ctx: float, n: int = NTOK) -> dict:
+    """Algorithmic bytes of one verify step: every weight byte the step must read once (q4 at 9/16 byte per value,
+    the routed experts actually picked), the KV rows attended and written, the recurrent and conv states read and
+    written, the logits written. Rollback copies are excluded (implementation overhead)."""
+    s = shape
+    H = s.hidden
+    q4 = lambda r, c: r * c * 9 // 16
+    kd, vd = s.gdn_k_heads * s.gdn_k_dim, s.gdn_v_heads * s.gdn_v_dim
+    conv_dim = 2 * kd + vd
+    kv_pos = 2 * (s.n_kv_heads * s.head_dim + 4 * s.n_kv_heads)
+    expert = q4(2 * s.moe_ff, H) + q4(H, s.moe_ff)
+    b = {"dense": 0, "experts": 0, "kv": 0, "state": 0, "logits": 0}
+    for t in s.layer_types:
+        b["dense"] += 2 * H * 4
+        if t == "full_attention":
+            b["dense"] += q4(2 * s.n_heads * s.head_dim, H) + 2 * q4(s.n_kv_heads * s.head_dim, H) + \
+                q4(H, s.n_heads * s.head_dim) + 2 * s.head_dim * 4
+            b["kv"] += int(ctx * kv_pos) + n * kv_pos
+        else:
+            b["dense"] += q4(conv_dim, H) + 2 * q4(vd, H) + 2 * s.gdn_v_heads * H * 2 + conv_dim * s.conv_kernel * 4 + \
+                s.gdn_v_dim * 4 + 2 * s.gdn_v_heads * 4
+            b["state"] += 2 * s.gdn_v_heads * s.gdn_k_dim * s.gdn_v_dim * 4 + 2 * conv_dim * (s.conv_kernel - 1) * 4
+        if s.dense:
+            b["dense"] += 2 * q4(s.shared_ff, H) + q4(H, s.shared_ff)
+        else:
+            b["dense"] += (s.n_experts + 1) * H * 2 + 2 * q4(s.shared_ff, H) + q4(H, s.shared_ff)
+            b["experts"] += int(round(union_per_layer * expert))
+    b["dense"] += q4(s.vocab, H) + H * 4 + n * (H // 16) * 9
+    b["logits"] = n * s.vocab * 4
+    b["total"] = sum(v for k, v in b.items())
+    return b
+
+
+class Clocks:
+    """nvidia-smi sampled every 200 ms while running: median SM clock, max clock, the throttle reasons seen."""
+
+    def __init__(self, index: int):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        q = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+            "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.th = threading.Thread(target=self._read, daemon=True)
+            self.th.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], 0.0, set()
+        for r in self.rows:
+            try:
+                sm.append(float(r[0]))
+                mx = max(mx, float(r[1]))
+                for i, nm in enumerate(names):
+                    if r[4 + i].lower().startswith("active"):
+                        reasons.add(nm)
+            except Exception:
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------- the CPU path ----
+def cpu_reference(steps: int = 3, layers: int = 4, threads: int = 0) -> dict:
+    """The reference engine's own CPU verify path (oracle/_ref: Model::forward_batch with every row's logits, then the
+    acceptance rule around geode::Sampler) on a bounded sample of the cfg-3 workload: the same shapes (hidden 2048,
+    256 experts top-8, vocab 248320, the 8192-position int8 KV cache), `layers` of the 40 layers (3 GDN : 1 attention
+    as in the model). The per-step time is scaled to 40 layers from the reference's own stage timer: lm_head once,
+    the rest x 40 / layers."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_py as op  # (the baseline leg only: the reference's code timed on the host)
+    from geode_b200 import synth
+
+    kind = "reference" if op.have_reference() else "port"
+    shape = synth.baseline_shape(3)
+    shape.n_layers = layers
+    shape.layer_types = synth.hybrid_types(layers)
+    threads = threads or os.cpu_count() or 1
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_pack(d, shape, seed=1, fill="random")
+        if kind != "reference":
+            return {"kind": "port", "value": None, "unit": UNIT, "cores": 1,
+                    "sample": "the reference build is missing: no CPU number"}
+        ref = op.Reference(d, threads=threads, ctx=CTX + 64)
+        ref.forward([1, 2, 3])
+        ref.save_state(os.path.join(d, "t.state"))
+        op.write_long_state(os.path.join(d, "t.state"), os.path.join(d, "l.state"), CTX)
+        lib = op.reference_lib()
+        rng = np.random.default_rng(3)
+        times, heads = [], []
+        import ctypes as C
+
+        def head_ms():
+            p = ref.profile()
+            i = p.index("lm_head ") + len("lm_head ")
+            return float(p[i:].split(" ")[0])
+
+        for it in range(steps + 1):
+            ref.load_state(os.path.join(d, "l.state"))
+            toks = rng.integers(0, shape.vocab, NTOK).astype(np.int32)
+            h0 = head_ms()
+            t0 = time.perf_counter()
+            out = ref.forward(toks, all_logits=True)
+            nxt = C.c_int(0)
+            samples = np.zeros(NTOK, np.int32)
+            lib.ref_accept(out["logits"].ctypes.data, NTOK, shape.vocab, toks.ctypes.data, 0.0, 1.0, 0, C.c_uint64(1),
+                           None, 0, C.byref(nxt), samples.ctypes.data)
+            t1 = time.perf_counter()
+            if it > 0:   # (the first is the warm-up: it reads every routed expert into the cache)
+                times.append(t1 - t0)
+                heads.append(head_ms() - h0)
+        ref.close()
+    t = statistics.median(times)
+    th = statistics.median(heads) / 1e3
+    t40 = th + (t - th) * 40 / layers
+    return {"kind": kind, "value": NTOK / t40, "unit": UNIT, "cores": threads,
+            "sample": f"{layers} of 40 layers (3 GDN : 1 attention) + lm_head, ctx {CTX}, greedy acceptance; median of "
+                      f"{steps} steps after 1 warm-up = {t * 1e3:.0f} ms (lm_head {th * 1e3:.0f} ms), scaled to 40 layers = "
+                      f"{t40 * 1e3:.0f} ms/step"}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    t0 = time.perf_counter()
+    cb = cpu_reference(steps=max(1, min(args.steps, 3)))
+    if cb.get("value") is None:
+        print(json.dumps({"impl": "reference", "unavailable": cb["sample"]}))
+        return 0
+    v = cb["value"]
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": NTOK / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4xint8->f32", "data": "synthetic",
+            "config": {"workload": "cfg3: MoE 35B-A3B shape verify, 1+4 tokens, ctx 8192, greedy", "global_batch": NTOK,
+                       "seq_len": CTX, "parallelism": "cpu"},
+            "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line))
+    return 0
+
+
+# ------------------------------------------------------------------------------------------- the GPU path ----
+def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
+    """The dominant kernel's roofline, measured live: the q4 GEMV (k_gemv_static, the kernel of every dense product and
+    the LM head) on the LM head's shape, 248320 x 2048, 5 token rows; CUDA events on its stream."""
+    import torch
+    rows, cols, n = 248320, 2048, NTOK
+    tb = L.gcuda_op_q4_tiled_bytes(rows, cols)
+    pack = torch.randint(0, 256, (rows, cols // 16 * 9), dtype=torch.uint8, device="cuda")
+    pack[:, cols // 2:] = torch.randint(0x30, 0x49, (rows, cols // 16), dtype=torch.uint8, device="cuda")
+    tiles = torch.empty(tb, dtype=torch.uint8, device="cuda")
+    L.gcuda_op_q4_relayout(pack.data_ptr(), rows, cols, tiles.data_ptr(), None)
+    del pack
+    x = torch.randn(n, cols, device="cuda")
+    q = torch.empty(n, cols, dtype=torch.int8, device="cuda")
+    sc = torch.empty(n, cols // 16, device="cuda")
+    bs = torch.empty(n, cols // 16, dtype=torch.int32, device="cuda")
+    y = torch.empty(n, rows, device="cuda")
+    L.gcuda_op_quantize(x.data_ptr(), n, cols, q.data_ptr(), sc.data_ptr(), bs.data_ptr(), None)
+    st = torch.cuda.current_stream()
+    for _ in range(3):
+        L.gcuda_op_q4_gemv(tiles.data_ptr(), rows, cols, 1e-3, q.data_ptr(), sc.data_ptr(), bs.data_ptr(), n, y.data_ptr(),
+                           st.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        L.gcuda_op_q4_gemv(tiles.data_ptr(), rows, cols, 1e-3, q.data_ptr(), sc.data_ptr(), bs.data_ptr(), n, y.data_ptr(),
+                           st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    alg = rows * cols * 9 // 16 + n * cols + n * (cols // 16) * 8 + n * rows * 4
+    ach = alg / (ms * 1e-3) / 1e9
+    return {"kernel": "k_gemv_static (q4 GEMV, lm_head 248320x2048, 5 rows)", "bound": "hbm", "achieved": ach,
+            "peak": peak_gbs, "unit": "GB/s", "frac": ach / peak_gbs, "traffic": None, "ms": ms,
+            "algorithmic_bytes": alg}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=40)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=40, help="(smaller cases for profiling)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from geode_b200 import synth
+    from geode_b200.backend import synthetic
+    from geode_b200 import cuda_lib
+
+    peak, peak_kind = measured_peaks()
+    shape = synth.baseline_shape(3)
+    if args.layers != 40:
+        shape.n_layers = args.layers
+        shape.layer_types = synth.hybrid_types(args.layers)
+    context = CTX + args.warmup + args.steps + args.e2e_steps + 64
+    t_build = time.perf_counter()
+    be = synthetic(shape, context=context, max_tokens=NTOK, device=local, seed=rank)
+    be.randomize_state(CTX, seed=7 + rank)
+    t_build = time.perf_counter() - t_build
+    rng = np.random.default_rng(rank)
+    toks = rng.integers(0, shape.vocab, NTOK).astype(np.int32)
+    launches0 = be.launches()
+
+    # ---- value: the device-resident step, K steps back to back
+    stream = torch.cuda.ExternalStream(be.stream())
+    be.begin_device_loop(toks)
+    for _ in range(args.warmup):
+        be.step_device(NTOK)
+    be.sync_step()
+    be.begin_device_loop(toks)   # (counters from zero for the timed steps)
+    pos0 = be.pos
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lc0 = be.launches()
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            be.step_device(NTOK)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    steps_done, union_sum, _ = be.sync_step()
+    launches_timed = be.launches() - lc0
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    n_moe = 0 if shape.dense else shape.n_layers
+    union_layer = union_sum / max(1, steps_done * n_moe) if n_moe else 0.0
+    mean_ctx = (pos0 + be.pos) / 2
+    b = step_bytes(shape, union_layer, mean_ctx)
+    value = world * NTOK * args.steps / (ms * 1e-3)
+
+    # ---- e2e: the C ABI with host buffers, every step synchronous (tokens in, logits out, accept, keep)
+    pinned = torch.empty((NTOK, shape.vocab), dtype=torch.float32, pin_memory=True).numpy()
+    for i in range(3):
+        be.verify(toks, logits=False)
+        kept, nxt, _ = be.accept(0.0)
+        if kept < NTOK:
+            be.keep(kept)
+    import ctypes as C
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(args.e2e_steps):
+        be._rc(be.L.gcuda_verify(be.g, toks.ctypes.data, NTOK, pinned.ctypes.data, None), "verify")
+        be._last_n = NTOK
+        kept, nxt, _ = be.accept(0.0)
+        if kept < NTOK:
+            be.keep(kept)
+        toks[0] = nxt
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * NTOK * args.e2e_steps / e2e_s
+
+    roof = gemv_roofline(cuda_lib(), peak)
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cb = cpu_reference()
+        except Exception as ex:   # (the baseline must not sink the GPU number)
+            cb = {"kind": "reference", "value": None, "unit": UNIT, "cores": os.cpu_count(), "sample": f"failed: {ex}"}
+    step_ach = b["total"] / (ms_step * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4xint8->f32", "data": "synthetic (random q4 codes / E4M3 scales made on the device; random 8192-position KV)",
+        "config": {"workload": "cfg3: MoE 35B-A3B shape verify (40 layers, 256 experts top-8 + shared, vocab 248320), "
+                               "1 accepted + 4 drafts, ctx 8192, greedy acceptance + GDN rollback",
+                   "global_batch": NTOK * world, "seq_len": CTX, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "l2": "inputs larger than L2 (20 GB of weights per GPU; no flush)", "layers": shape.n_layers},
+        "roofline": roof,
+        "step_roofline": {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,
+                          "peak_kind": peak_kind, "algorithmic_bytes_per_step": b, "experts_per_layer": union_layer,
+                          "mean_context": mean_ctx},
+        "cpu_baseline": cb,
+        "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": NTOK * 4,
+                "d2h_bytes_per_step": NTOK * shape.vocab * 4 + NTOK * 4, "steps": args.e2e_steps},
+        "gpu_launches": int(launches_timed),
+        "clocks": clk.summary(),
+        "build_s": t_build,
+        "peak_kind": peak_kind,
+    }
+    if rank == 0:
+        print(json.dumps(line))
+    be.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -57,6 +57,15 @@ def _sig(L):
         "gcuda_launches": (C.c_uint64, [vp]),
         "gcuda_debug_read": (i32, [vp, i32, vp, sz]),
         "gcuda_debug_step_eager": (i32, [vp, vp, i32, i32]),
+        "gcuda_synth_q4": (i32, [vp, i64, i64, f32, C.c_uint64]),
+        "gcuda_synth_raw": (i32, [vp, sz, i32, f32, f32, C.c_uint64]),
+        "gcuda_synth_embedding": (i32, [vp, i64, i64, f32, C.c_uint64]),
+        "gcuda_synth_experts": (i32, [vp, i32, i32, i32, f32, C.c_uint64]),
+        "gcuda_state_randomize": (i32, [vp, i32, C.c_uint64]),
+        "gcuda_step_device": (i32, [vp, i32]),
+        "gcuda_begin_device_loop": (i32, [vp, vp, i32]),
+        "gcuda_sync_step": (i32, [vp, vp, vp, vp]),
+        "gcuda_stream": (vp, [vp]),
     }
     for name, (res, args) in sigs.items():
         if hasattr(L, name):
@@ -74,15 +83,17 @@ class GcudaError(RuntimeError):
 
 
 class Backend:
-    """One gcuda handle over a geode-pack directory."""
+    """One gcuda handle over a geode-pack directory (or, with pack_dir None, a synthetic model: see synthetic())."""
 
-    def __init__(self, pack_dir: str, context: int, max_tokens: int = 5, device: int = 0):
+    def __init__(self, pack_dir: Optional[str], context: int, max_tokens: int = 5, device: int = 0):
         self.L = L = cuda_lib()
         _sig(L)
         err = C.create_string_buffer(512)
         self.g = L.gcuda_open(device, err, 512)
         if not self.g:
             raise GcudaError("gcuda_open: " + err.value.decode())
+        if pack_dir is None:
+            return
         with open(os.path.join(pack_dir, "geode.json")) as f:
             m = json.load(f)
         self.manifest = m
@@ -226,8 +237,88 @@ class Backend:
                                      C.byref(nxt), _ptr(samples)), "accept")
         return kept.value, nxt.value, samples
 
+    def randomize_state(self, pos: int, seed: int = 1):
+        self._rc(self.L.gcuda_state_randomize(self.g, pos, C.c_uint64(seed)), "state_randomize")
+
+    def begin_device_loop(self, toks):
+        toks = np.ascontiguousarray(np.asarray(toks, dtype=np.int32))
+        self._rc(self.L.gcuda_begin_device_loop(self.g, _ptr(toks), len(toks)), "begin_device_loop")
+
+    def step_device(self, n: int):
+        self._rc(self.L.gcuda_step_device(self.g, n), "step_device")
+
+    def sync_step(self):
+        steps, usum, kept = C.c_int(0), C.c_int(0), C.c_int(0)
+        self._rc(self.L.gcuda_sync_step(self.g, C.byref(steps), C.byref(usum), C.byref(kept)), "sync_step")
+        return steps.value, usum.value, kept.value
+
+    def stream(self) -> int:
+        return int(self.L.gcuda_stream(self.g) or 0)
+
     def last_ms(self) -> float:
         return self.L.gcuda_last_ms(self.g)
 
     def launches(self) -> int:
         return int(self.L.gcuda_launches(self.g))
+
+
+def synthetic(shape, context: int, max_tokens: int = 5, device: int = 0, seed: int = 0) -> Backend:
+    """A backend over a model of `shape` (geode_b200.synth.ModelShape) whose q4 weights are random bytes made on the
+    device (gcuda_synth_*: random codes, E4M3 scales 0x30..0x48) - the same bytes a pack of that shape streams, for
+    measuring at full size without writing ~20 GB of pack first."""
+    be = Backend(None, context, max_tokens, device)
+    L, g = be.L, be.g
+    k = [seed]
+
+    def nxt():
+        k[0] += 1
+        return C.c_uint64(k[0] * 0x9E3779B9 + 17)
+
+    def chk(rc, what):
+        if rc < 0:
+            raise GcudaError(f"{what}: {be.error()}")
+        return rc
+
+    s = shape
+    H = s.hidden
+    q4 = lambda rows, cols: chk(L.gcuda_synth_q4(g, rows, cols, 0.02 / 14.7, nxt()), "synth_q4")
+    f32 = lambda count, mean, std: chk(L.gcuda_synth_raw(g, count, 0, mean, std, nxt()), "synth_raw")
+    bf16 = lambda count, std: chk(L.gcuda_synth_raw(g, count, 1, 0.0, std, nxt()), "synth_raw")
+    layers = (GLayer * s.n_layers)()
+    for l in range(s.n_layers):
+        x = layers[l]
+        for f_ in GLayer._fields_:
+            setattr(x, f_[0], -1)
+        attn = s.layer_types[l] == "full_attention"
+        x.attn = 1 if attn else 0
+        x.in_norm, x.post_norm = f32(H, 0.0, 0.1), f32(H, 0.0, 0.1)
+        if attn:
+            x.q, x.k = q4(s.n_heads * s.head_dim * 2, H), q4(s.n_kv_heads * s.head_dim, H)
+            x.v, x.o = q4(s.n_kv_heads * s.head_dim, H), q4(H, s.n_heads * s.head_dim)
+            x.q_norm, x.k_norm = f32(s.head_dim, 0.0, 0.1), f32(s.head_dim, 0.0, 0.1)
+        else:
+            vd = s.gdn_v_heads * s.gdn_v_dim
+            x.qkv, x.z, x.out = q4(s.conv_dim, H), q4(vd, H), q4(H, vd)
+            x.a, x.b = bf16(s.gdn_v_heads * H, 0.05), bf16(s.gdn_v_heads * H, 0.05)
+            x.A_log, x.dt_bias = f32(s.gdn_v_heads, 1.4, 0.5), f32(s.gdn_v_heads, 0.0, 0.1)
+            x.conv, x.gnorm = f32(s.conv_dim * s.conv_kernel, 0.0, 0.3), f32(s.gdn_v_dim, 1.0, 0.1)
+        if s.dense:
+            x.sh_gate, x.sh_up, x.sh_down = q4(s.shared_ff, H), q4(s.shared_ff, H), q4(H, s.shared_ff)
+        else:
+            x.sh_gate, x.sh_up, x.sh_down = q4(s.shared_ff, H), q4(s.shared_ff, H), q4(H, s.shared_ff)
+            x.router, x.shared_gate = bf16(s.n_experts * H, 0.05), bf16(H, 0.05)
+            x.experts = chk(L.gcuda_synth_experts(g, s.n_experts, H, s.moe_ff, 0.02 / 14.7, nxt()), "synth_experts")
+    embed = chk(L.gcuda_synth_embedding(g, s.vocab, H, 1.0 / 14.7, nxt()), "synth_embedding")
+    head = q4(s.vocab, H)
+    norm = f32(H, 0.0, 0.1)
+    gs = GShape(hidden=H, n_layers=s.n_layers, vocab=s.vocab, eps=s.eps, n_heads=s.n_heads, n_kv_heads=s.n_kv_heads,
+                head_dim=s.head_dim, rope_dim=s.rope_dim, rope_theta=s.rope_theta, gdn_k_heads=s.gdn_k_heads,
+                gdn_v_heads=s.gdn_v_heads, gdn_k_dim=s.gdn_k_dim, gdn_v_dim=s.gdn_v_dim, conv_kernel=s.conv_kernel,
+                n_experts=s.n_experts, top_k=s.top_k, moe_ff=s.moe_ff, shared_ff=s.shared_ff, dense=1 if s.dense else 0,
+                context=context, max_tokens=max_tokens)
+    be.shape = gs
+    chk(L.gcuda_setup(g, C.addressof(gs), C.addressof(layers), embed, head, norm), "setup")
+    be.vocab, be.hidden = gs.vocab, gs.hidden
+    be.n_attn = s.n_attn
+    be.n_gdn = s.n_gdn
+    return be

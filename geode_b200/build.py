@@ -19,6 +19,7 @@ CUDA_SO = os.path.join(PKG, "libgeode_cuda.so")
 HOST_SO = os.path.join(PKG, "libgeode_host.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+CUDA_FLAGS = ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC"]
 
 
 def _stale(target, sources):
@@ -41,7 +42,7 @@ def build_cuda(force: bool = False) -> str:
     for s in srcs:
         o = os.path.join(bdir, os.path.basename(s) + ".o")
         objs.append(o)
-        cmd = [NVCC, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-c", s, "-o", o]
+        cmd = [NVCC, *ARCH, *CUDA_FLAGS, "-c", s, "-o", o]
         procs.append((cmd, subprocess.Popen(cmd)))
     for cmd, p in procs:
         if p.wait() != 0:

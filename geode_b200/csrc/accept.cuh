@@ -103,6 +103,35 @@ __device__ void row_topk(const float *__restrict__ row, int V, int k, float *cv,
         }
 }
 
+// Greedy rows split over many CTAs: each reduces its slice to the first maximum and merges it into best[r], a 64-bit
+// key (order-preserving value bits, then the complement of the index: the largest value, the lowest index first).
+__global__ void k_argmax_partial(const float *__restrict__ logits, int V, unsigned long long *best) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int r = blockIdx.y;
+    const float *row = logits + static_cast<size_t>(r) * V;
+    const int per = (V + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(V, lo + per);
+    unsigned long long k = 0;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = row[i];
+        if (v != v) continue;   // (NaN: never the maximum)
+        const unsigned long long key = (static_cast<unsigned long long>(fkey(v)) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(i));
+        k = key > k ? key : k;
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
+        k = ok > k ? ok : k;
+    }
+    if ((threadIdx.x & 31) == 0 && k) atomicMax(&best[r], k);
+}
+// best -> the rows' samples; best reset for the next use
+__global__ void k_argmax_finish(unsigned long long *best, int n, int *out) {
+    const int r = threadIdx.x;
+    if (r >= n) return;
+    const unsigned long long k = best[r];
+    out[r] = k ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFu)) : 0;
+    best[r] = 0;
+}
+
 struct SampleArgs {
     const float *logits;   // [n][V]
     int V, n;

@@ -31,6 +31,7 @@ struct DevTensor {
 
 struct DevExperts {
     uint8_t *d = nullptr;
+    bool tiled = false;   // already in the GEMV's tile layout (synthesized on the device)
     int n = 0;
     size_t stride = 0;
     float *scales = nullptr;   // device [n][2]
@@ -86,10 +87,13 @@ struct gcuda {
     int nchunks = 0;
     // graphs per batch size
     cudaGraphExec_t graph[kMaxTok + 1] = {};
+    uint64_t graph_kernels[kMaxTok + 1] = {};   // kernels one launch of graph[n] runs
     int pos = 0, last_batch = 0;
     int last_toks[kMaxTok] = {};
+    StepState *step = nullptr;     // the device-side loop's decision and counters
     double *d_u = nullptr;
     int *d_samples = nullptr;
+    unsigned long long *d_best = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
     bool pdl = true;
@@ -232,7 +236,7 @@ int enqueue_step(gcuda *g, int n) {
             a.wk = g->route->w;
             a.K = s.top_k;
         }
-        LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(256), 0, g->st, pdl, a));
+        LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(512), 0, g->st, pdl, a));
         return GCUDA_OK;
     };
     auto raw = [&](int id) -> const float * {
@@ -245,7 +249,7 @@ int enqueue_step(gcuda *g, int n) {
         const LayerPlan &P = g->plan[static_cast<size_t>(l)];
         if (!L.attn) {
             RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
-            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3((2 * s.gdn_v_heads * n * 8 + 255) / 256), dim3(256), 0, g->st, pdl,
+            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3((2 * s.gdn_v_heads + 31) / 32), dim3(256), sizeof(float) * n * H, g->st, pdl,
                                 static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H,
                                 static_cast<const float *>(g->hf), H, n, g->ab, 2 * s.gdn_v_heads));
             GdnArgs a{};
@@ -372,11 +376,11 @@ int enqueue_step(gcuda *g, int n) {
             RC_OK(norm(next_norm, false, next_hf));
         } else {
             const int E = s.n_experts;
-            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3(((E + 1) * n * 8 + 255) / 256), dim3(256), 0, g->st, pdl,
+            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3((E + 1 + 31) / 32), dim3(256), sizeof(float) * n * H, g->st, pdl,
                                 static_cast<const uint16_t *>(P.router_w), E + 1, H, static_cast<const float *>(g->hf), H,
                                 n, g->rlog, E + 1));
             LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(32 * kMaxTok), kMaxTok * E * sizeof(float), g->st, pdl,
-                                static_cast<const float *>(g->rlog), n, E, s.top_k, g->route));
+                                static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum));
             const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
             const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
                             *sd = tensor(g, L.sh_down, kQ4Tiled);
@@ -402,11 +406,14 @@ int enqueue_step(gcuda *g, int n) {
             ea.eout = g->eout;
             ea.shout = g->shout;
             ea.status = g->d_status;
-            const size_t smem = experts_smem_bytes(H, s.moe_ff, s.shared_ff);
-            ea.pass = kGateUp;
-            LAUNCH_OK(launch_ex(k_gemv_experts, dim3(sm_count()), dim3(kGemvWarps * 32), smem, g->st, pdl, ea));
-            ea.pass = kDown;
-            LAUNCH_OK(launch_ex(k_gemv_experts, dim3(sm_count()), dim3(kGemvWarps * 32), smem, g->st, pdl, ea));
+            for (int pass : {static_cast<int>(kGateUp), static_cast<int>(kDown)}) {
+                RelayShape r;
+                if (!plan_experts(pass, H, s.moe_ff, s.shared_ff, s.n_experts, s.top_k, n, sm_count(), r)) return GCUDA_E_ARG;
+                ea.pass = pass;
+                ea.wpu = r.wpu;
+                ea.nslots = r.nslots;
+                LAUNCH_OK(launch_ex(k_gemv_experts, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
+            }
             RC_OK(norm(next_norm, true, next_hf));
         }
     }
@@ -417,16 +424,12 @@ int enqueue_step(gcuda *g, int n) {
 
 int set_attrs(gcuda *g) {
     const gcuda_shape &s = g->sh;
-    const size_t gsm = std::max(gemv_smem_bytes(s.hidden), std::max(gemv_smem_bytes(g->corew),
-                                                                     gemv_smem_bytes(std::max(16 * 4, s.shared_ff))));
-    LAUNCH_OK(cudaFuncSetAttribute(k_gemv_static, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
-    if (!s.dense)
-        LAUNCH_OK(cudaFuncSetAttribute(k_gemv_experts, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(experts_smem_bytes(s.hidden, s.moe_ff, s.shared_ff))));
+    if (gemv_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<256>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<128>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<64>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxTok * s.n_experts * sizeof(float) + 16)));
+    LAUNCH_OK(cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxTok * s.hidden * sizeof(float))));
     return GCUDA_OK;
 }
 
@@ -434,7 +437,10 @@ int record_graphs(gcuda *g) {
     for (int n = 1; n <= g->sh.max_tokens; ++n) {
         cudaGraph_t graph = nullptr;
         LAUNCH_OK(cudaStreamBeginCapture(g->st, cudaStreamCaptureModeThreadLocal));
+        const uint64_t k0 = launch_counter().load();
         const int rc = enqueue_step(g, n);
+        g->graph_kernels[n] = launch_counter().load() - k0;
+        launch_counter().fetch_sub(g->graph_kernels[n]);   // (recorded, not run)
         const cudaError_t e = cudaStreamEndCapture(g->st, &graph);
         if (rc != GCUDA_OK) {
             if (graph) cudaGraphDestroy(graph);
@@ -648,6 +654,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         const size_t want = static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9 + static_cast<size_t>(H) * (s.moe_ff / 16) * 9;
         for (auto &X : g->experts) {
             if (X.stride != want) return fail(g, GCUDA_E_ARG, "setup: an expert block of unexpected size");
+            if (X.tiled) continue;
             uint8_t *tmp = nullptr;
             cudaError_t e = cudaMalloc(&tmp, X.stride);
             if (e != cudaSuccess) return cuda_fail(g, e, "setup cudaMalloc");
@@ -687,7 +694,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         !dalloc(g, &g->part, static_cast<size_t>(T) * s.n_heads * g->nchunks * (s.head_dim + 2)) ||
         !dalloc(g, &g->logits, static_cast<size_t>(T) * s.vocab) || !dalloc(g, &g->core_f, static_cast<size_t>(T) * g->corew) ||
         !dalloc(g, &g->inv_freq, std::max(1, s.rope_dim / 2)) || !dalloc(g, &g->route, 1) ||
-        !dalloc(g, &g->d_u, kMaxTok) || !dalloc(g, &g->d_samples, kMaxTok) ||
+        !dalloc(g, &g->d_u, kMaxTok) || !dalloc(g, &g->d_samples, kMaxTok) || !dalloc(g, &g->step, 1) || !dalloc(g, &g->d_best, kMaxTok) ||
         !act_alloc(g, g->hq, T, H) || !act_alloc(g, g->core, T, g->corew) ||
         !act_alloc(g, g->amid, T * K, ffw) || !act_alloc(g, g->shact, T, s.shared_ff))
         return GCUDA_E_MEMORY;
@@ -786,6 +793,7 @@ int gcuda_verify_device(gcuda *g, const int *d_toks, int n) {
     LAUNCH_OK(cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
     LAUNCH_OK(cudaEventRecord(g->ev0, g->st));
     LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
+    count_launch(g->graph_kernels[n]);
     LAUNCH_OK(cudaEventRecord(g->ev1, g->st));
     RC_OK(check_status(g));
     cudaEventElapsedTime(&g->last_ms, g->ev0, g->ev1);
@@ -828,7 +836,13 @@ int gcuda_accept(gcuda *g, const gcuda_sampling *sp, const double *uniforms, con
     a.top_k = sp->top_k;
     a.u = g->d_u;
     a.out = g->d_samples;
-    LAUNCH_OK(launch_ex(k_sample_rows, dim3(n), dim3(kSampleThreads), 0, g->st, false, a));
+    if (greedy) {
+        LAUNCH_OK(launch_ex(k_argmax_partial, dim3(64, n), dim3(256), 0, g->st, false, static_cast<const float *>(g->logits),
+                            g->sh.vocab, g->d_best));
+        LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, false, g->d_best, n, g->d_samples));
+    } else {
+        LAUNCH_OK(launch_ex(k_sample_rows, dim3(n), dim3(kSampleThreads), 0, g->st, false, a));
+    }
     int ys[kMaxTok];
     LAUNCH_OK(cudaMemcpyAsync(ys, g->d_samples, sizeof(int) * n, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
@@ -984,5 +998,165 @@ int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl) {
     g->last_batch = n;
     return GCUDA_OK;
 }
+
+// ------------------------------------------------------------------------------------------- synthetic weights ----
+namespace {
+int grid_for(size_t work) { return static_cast<int>(std::min<size_t>((work + 255) / 256, 148 * 64)); }
+}  // namespace
+
+int gcuda_synth_q4(gcuda *g, int64_t rows, int64_t cols, float global, uint64_t seed) {
+    if (!g || rows <= 0 || cols % 64) return fail(g, GCUDA_E_ARG, "synth_q4: cols a multiple of 64");
+    cudaSetDevice(g->device);
+    const size_t bytes = gcuda_op_q4_tiled_bytes(rows, cols);
+    void *d = nullptr;
+    cudaError_t e = cudaMalloc(&d, bytes);
+    if (e != cudaSuccess) return cuda_fail(g, e, "synth_q4 cudaMalloc");
+    k_synth_tiled<<<grid_for(bytes / 8), 256, 0, g->st>>>(static_cast<uint8_t *>(d), bytes, seed);
+    count_launch();
+    DevTensor t;
+    t.d = d;
+    t.bytes = bytes;
+    t.rows = rows;
+    t.cols = cols;
+    t.global = global;
+    t.kind = kQ4Tiled;
+    g->tensors.push_back(t);
+    return static_cast<int>(g->tensors.size()) - 1;
+}
+
+int gcuda_synth_raw(gcuda *g, size_t count, int dtype, float mean, float stdv, uint64_t seed) {
+    if (!g || count == 0 || dtype < 0 || dtype > 1) return fail(g, GCUDA_E_ARG, "synth_raw");
+    cudaSetDevice(g->device);
+    void *d = nullptr;
+    const size_t bytes = count * (dtype == 0 ? 4 : 2);
+    cudaError_t e = cudaMalloc(&d, bytes);
+    if (e != cudaSuccess) return cuda_fail(g, e, "synth_raw cudaMalloc");
+    k_synth_values<<<grid_for(count), 256, 0, g->st>>>(d, count, dtype, mean, stdv, seed);
+    count_launch();
+    DevTensor t;
+    t.d = d;
+    t.bytes = bytes;
+    t.kind = kRaw;
+    g->tensors.push_back(t);
+    return static_cast<int>(g->tensors.size()) - 1;
+}
+
+int gcuda_synth_embedding(gcuda *g, int64_t rows, int64_t cols, float global, uint64_t seed) {
+    if (!g || rows <= 0 || cols % 16) return fail(g, GCUDA_E_ARG, "synth_embedding");
+    cudaSetDevice(g->device);
+    const size_t bytes = static_cast<size_t>(rows) * (cols / 16) * 9;
+    void *d = nullptr;
+    cudaError_t e = cudaMalloc(&d, bytes);
+    if (e != cudaSuccess) return cuda_fail(g, e, "synth_embedding cudaMalloc");
+    k_synth_rows<<<grid_for(bytes), 256, 0, g->st>>>(static_cast<uint8_t *>(d), rows, static_cast<int>(cols), seed);
+    count_launch();
+    DevTensor t;
+    t.d = d;
+    t.bytes = bytes;
+    t.rows = rows;
+    t.cols = cols;
+    t.global = global;
+    t.kind = kRaw;
+    g->tensors.push_back(t);
+    return static_cast<int>(g->tensors.size()) - 1;
+}
+
+int gcuda_synth_experts(gcuda *g, int n, int hidden, int ff, float global, uint64_t seed) {
+    if (!g || n <= 0 || hidden % 64 || ff % 64) return fail(g, GCUDA_E_ARG, "synth_experts");
+    cudaSetDevice(g->device);
+    DevExperts X;
+    X.n = n;
+    X.tiled = true;
+    X.stride = static_cast<size_t>(2 * ff) * (hidden / 16) * 9 + static_cast<size_t>(hidden) * (ff / 16) * 9;
+    X.host_scales.assign(static_cast<size_t>(2 * n), global);
+    cudaError_t e = cudaMalloc(&X.d, static_cast<size_t>(n) * X.stride);
+    if (e != cudaSuccess) return cuda_fail(g, e, "synth_experts cudaMalloc");
+    e = cudaMalloc(&X.scales, sizeof(float) * 2 * n);
+    if (e == cudaSuccess) e = cudaMemcpy(X.scales, X.host_scales.data(), sizeof(float) * 2 * n, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return cuda_fail(g, e, "synth_experts");
+    k_synth_tiled<<<grid_for(static_cast<size_t>(n) * X.stride / 8), 256, 0, g->st>>>(X.d, static_cast<size_t>(n) * X.stride, seed);
+    count_launch();
+    g->experts.push_back(X);
+    return static_cast<int>(g->experts.size()) - 1;
+}
+
+int gcuda_state_randomize(gcuda *g, int pos, uint64_t seed) {
+    if (!g || !g->ready || pos < 0 || pos > g->sh.context) return fail(g, GCUDA_E_ARG, "state_randomize");
+    cudaSetDevice(g->device);
+    const gcuda_shape &s = g->sh;
+    for (int a = 0; a < g->n_attn; ++a) {
+        const size_t base = static_cast<size_t>(a) * s.context;
+        const size_t rows = static_cast<size_t>(pos) * g->kvrow, sc = static_cast<size_t>(pos) * s.n_kv_heads;
+        k_synth_kv<<<grid_for(rows), 256, 0, g->st>>>(g->kc + base * g->kvrow, rows, g->ks + base * s.n_kv_heads, sc, 0.5f, seed + 2 * a);
+        k_synth_kv<<<grid_for(rows), 256, 0, g->st>>>(g->vc + base * g->kvrow, rows, g->vs + base * s.n_kv_heads, sc, 0.5f, seed + 2 * a + 1);
+        count_launch(2);
+    }
+    if (g->conv_n) k_synth_values<<<grid_for(g->conv_n), 256, 0, g->st>>>(g->conv, g->conv_n, 0, 0.0f, 0.3f, seed ^ 0xC0);
+    if (g->gdn_n) k_synth_values<<<grid_for(g->gdn_n), 256, 0, g->st>>>(g->gdn, g->gdn_n, 0, 0.0f, 0.02f, seed ^ 0xD0);
+    count_launch(2);
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    g->pos = pos;
+    g->last_batch = 0;
+    return GCUDA_OK;
+}
+
+// The device-resident speculative step, enqueued without waiting: the verify graph for n tokens at the device
+// position, the greedy acceptance of every row (k_sample_rows), the decision (k_decide: kept, next, position += kept,
+// toks[0] = next) and the rollback of the Gated DeltaNet states (k_rollback). The drafts toks[1..n-1] are the
+// caller's (gcuda_set_drafts); gcuda_sync_step reads the decision and the position back.
+int gcuda_step_device(gcuda *g, int n) {
+    if (!g || !g->ready || n < 2 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "step_device: 2 .. max_tokens");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
+    count_launch(g->graph_kernels[n]);
+    SampleArgs a{};
+    a.logits = g->logits;
+    a.V = g->sh.vocab;
+    a.n = n;
+    a.temperature = 0.0f;
+    a.top_p = 1.0f;
+    a.u = g->d_u;
+    a.out = g->d_samples;
+    (void)a;
+    LAUNCH_OK(launch_ex(k_argmax_partial, dim3(64, n), dim3(256), 0, g->st, false, static_cast<const float *>(g->logits),
+                        g->sh.vocab, g->d_best));
+    LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, g->pdl, g->d_best, n, g->d_samples));
+    LAUNCH_OK(launch_ex(k_decide, dim3(1), dim3(32), 0, g->st, g->pdl, static_cast<const int *>(g->d_samples), g->d_toks, n,
+                        g->d_pos, g->step));
+    LAUNCH_OK(launch_ex(k_rollback, dim3(sm_count() * 4), dim3(256), 0, g->st, g->pdl, g->conv,
+                        static_cast<const float *>(g->conv_bk), g->conv_n, g->gdn, static_cast<const float *>(g->gdn_bk),
+                        g->gdn_n, n, static_cast<const StepState *>(g->step)));
+    return GCUDA_OK;
+}
+
+// Before a device loop: the position to the device, the batch's tokens (n), the counters zeroed.
+int gcuda_begin_device_loop(gcuda *g, const int *toks, int n) {
+    if (!g || !g->ready || !toks || n < 1 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "begin_device_loop");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaMemsetAsync(g->step, 0, sizeof(StepState), g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    return GCUDA_OK;
+}
+
+// After a device loop: the position back to the host; steps, the expert-union sum over the routed layers and the
+// last kept count.
+int gcuda_sync_step(gcuda *g, int *steps, int *union_sum, int *last_kept) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "sync_step");
+    cudaSetDevice(g->device);
+    StepState ss{};
+    LAUNCH_OK(cudaMemcpyAsync(&ss, g->step, sizeof(ss), cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(&g->pos, g->d_pos, sizeof(int), cudaMemcpyDeviceToHost, g->st));
+    RC_OK(check_status(g));
+    if (steps) *steps = ss.steps;
+    if (union_sum) *union_sum = ss.n_union_sum;
+    if (last_kept) *last_kept = ss.kept;
+    g->last_batch = 0;
+    return GCUDA_OK;
+}
+
+// The stream the handle enqueues on (a cudaStream_t), for callers that time it with their own events.
+void *gcuda_stream(gcuda *g) { return g ? static_cast<void *>(g->st) : nullptr; }
 
 }  // extern "C"

@@ -108,7 +108,9 @@ __global__ void k_quantize(const float *__restrict__ x, int n, int cols, int xst
 }
 
 // ------------------------------------------------------------------------------------------- the static GEMV ----
-// A table of units (built on the host), or one plain matrix, against one ActSet; slots take units round-robin.
+// A table of units (built on the host), or one plain matrix, against one ActSet; slots take units round-robin. Every
+// unit multiplies the same activations, so the CTA stages one image of all K (after the previous kernel ends) and
+// every warp reads its groups from it.
 struct StaticGemv {
     const GemvUnit *units;   // a unit table, or NULL: one plain matrix (below), units made on the fly
     int n_units;
@@ -119,25 +121,31 @@ struct StaticGemv {
     int ystride, mode;
     ActSet act;
     int ncols;          // token columns (<= kMaxTok)
+    int wpu, nslots;    // the launch shape (plan_static)
     uint32_t *status;
 };
 
-__host__ __device__ inline size_t gemv_smem_bytes(int cols) {
-    const int wpu = warps_per_unit(cols);
-    return static_cast<size_t>(kGemvWarps) * warp_smem_bytes((cols / 64) / wpu);
+inline bool plan_static(int cols, int n_units, int sms, RelayShape &r) {
+    return plan_relay(cols, choose_wpu(cols, n_units, sms), false, static_cast<size_t>(act_smem_bytes(cols)), r);
 }
-__host__ __device__ inline int gemv_slots(int cols) { return kGemvWarps / warps_per_unit(cols); }
 
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
-    const int cols = p.act.cols, wpu = warps_per_unit(cols), sg = (cols / 64) / wpu, nslots = kGemvWarps / wpu;
-    if (warp >= nslots * wpu) {
+    const int cols = p.act.cols, wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
+    uint8_t *img = smem;
+    auto prelude = [&]() {
+        // (the weights do not depend on the previous kernel: their first stages are already requested)
         asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;");
+        stage_full(p.act, p.ncols, img);
+        __syncthreads();
+    };
+    if (warp >= nslots * wpu) {   // (a warp without a slot helps stage the image)
+        prelude();
         return;
     }
-    RelayCtx c = make_ctx(smem, sg, wpu);
-    c.sg = sg;
+    RelayCtx c = make_ctx(smem + act_smem_bytes(cols), wpu, sg, 0, img, act_tstride(cols));
     const int slot = warp / wpu;
     const size_t tb = static_cast<size_t>(cols / 64) * kGroupBytes;
     auto get = [&](int i, GemvUnit &U) -> bool {
@@ -161,22 +169,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p
         for (int t = 0; t < kMaxTok; ++t) U.slot[t] = t;
         return true;
     };
-    bool staged = false;
-    auto restage = [&](const GemvUnit &) {
-        if (staged) return;
-        int sel[kMaxTok];
-        for (int t = 0; t < kMaxTok; ++t) sel[t] = t < p.ncols ? t : -1;
-        stage_slice(p.act, sel, c.part * sg, sg, c.img);
-        __syncwarp();
-        staged = true;
-    };
-    auto prelude = [&]() {
-        // (the weights do not depend on the previous kernel: their first stages are already requested)
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        asm volatile("griddepcontrol.launch_dependents;");
-    };
-    relay_units(get, c, restage, p.status, [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid,
-                                              int tig) { epi_store(U, y0, y1, gid, tig); }, true, prelude);
+    relay_units(get, c, [](const GemvUnit &) {}, p.status, [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4],
+                                                               int gid, int tig) { epi_store(U, y0, y1, gid, tig); },
+                true, prelude);
 }
 
 }  // namespace gcu
@@ -208,16 +203,18 @@ struct ExpertsArgs {
     int H, ff, sff, K, n;
     ActSet hq, amid, shact;     // amid: [n*K][ff], shact: [n][sff]
     float *eout, *shout;        // [n*K][H], [n][H]
+    int wpu, nslots;            // the launch shape (plan_experts)
     uint32_t *status;
 };
 
-__host__ __device__ inline size_t experts_smem_bytes(int H, int ff, int sff) {
-    int sgm = 0;
-    for (int cols : {H, ff, sff}) {
-        const int sg = (cols / 64) / warps_per_unit(cols);
-        sgm = sg > sgm ? sg : sgm;
-    }
-    return static_cast<size_t>(kGemvWarps) * warp_smem_bytes(sgm);
+// gate_up: the CTA's image of h in front of the warps; down: every warp its own image (the units' activations differ).
+// units: the expected count (the union is known on the device only): n*K picks at most, E experts at most.
+inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, RelayShape &r) {
+    const int picks = n * K < E ? n * K : E;
+    if (pass == kGateUp)
+        return plan_relay(H, choose_wpu(H, picks * (ff / 16) + sff / 16, sms), false,
+                          static_cast<size_t>(act_smem_bytes(H)), r);
+    return plan_relay(ff, choose_wpu(ff, (picks + 1) * (H / 32), sms), true, 0, r);
 }
 
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs p) {
@@ -226,27 +223,28 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs
     const bool gu = p.pass == kGateUp;
     // gate_up multiplies hidden-wide h; down multiplies ff-wide (sff for the shared expert) activations
     const int cols = gu ? p.H : p.ff;
-    const int wpu = warps_per_unit(cols), sg = (cols / 64) / wpu, nslots = kGemvWarps / wpu;
-    if (gu ? false : p.sff != p.ff) {
+    const int wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
+    if (!gu && p.sff != p.ff) {
         // (one K for the whole pass: the shared expert's width must match the routed experts')
         if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.status, kErrBadShape);
     }
-    int sgm = 0;
-    for (int cc : {p.H, p.ff, p.sff}) {
-        const int s2 = (cc / 64) / warps_per_unit(cc);
-        sgm = s2 > sgm ? s2 : sgm;
-    }
-    if (warp >= nslots * wpu) {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        return;
-    }
-    RelayCtx c = make_ctx(smem, sgm, wpu);
-    c.sg = sg;
-    const int slot = warp / wpu;
+    uint8_t *img = gu ? smem : nullptr;
     auto prelude = [&]() {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         asm volatile("griddepcontrol.launch_dependents;");
+        if (gu) {
+            stage_full(p.hq, p.n, img);
+            __syncthreads();
+        }
     };
+    if (warp >= nslots * wpu) {
+        if (gu) prelude();
+        else asm volatile("griddepcontrol.wait;" ::: "memory");
+        return;
+    }
+    RelayCtx c = gu ? make_ctx(smem + act_smem_bytes(p.H), wpu, sg, 0, img, act_tstride(p.H))
+                    : make_ctx(smem, wpu, sg, sg, nullptr, 0);
+    const int slot = warp / wpu;
     const RouteOut &R = *p.route;
     int nu = 0, per_ex = 0, total = 0, u0 = 0, u1 = 0;
     const int all = (1 << p.n) - 1;
@@ -323,13 +321,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs
     };
     int staged = -2;
     auto restage = [&](const GemvUnit &U) {
-        if (U.act_id == staged) return;
+        if (gu || U.act_id == staged) return;   // (gate_up: the CTA's image of h, staged in the prelude)
         __syncwarp();
         int sel[kMaxTok];
-        for (int t = 0; t < kMaxTok; ++t)
-            sel[t] = t < p.n && ((U.tok_mask >> t) & 1) ? (gu ? t : U.slot[t]) : -1;
-        const ActSet &a = gu ? p.hq : (U.act_id < 0 ? p.shact : p.amid);
-        stage_slice(a, sel, c.part * sg, sg, c.img);
+        for (int t = 0; t < kMaxTok; ++t) sel[t] = t < p.n && ((U.tok_mask >> t) & 1) ? U.slot[t] : -1;
+        stage_slice(U.act_id < 0 ? p.shact : p.amid, sel, c.part * sg, sg, c.own_img);
         __syncwarp();
         staged = U.act_id;
     };

@@ -63,19 +63,27 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
     return e;
 }
 
-inline int launch_static_gemv(const StaticGemv &p, cudaStream_t st, bool pdl) {
-    const size_t smem = gemv_smem_bytes(p.act.cols);
-    static size_t opted = 0;
-    if (smem > opted) {
-        if (cudaFuncSetAttribute(k_gemv_static, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-            cudaSuccess)
-            return GCUDA_E_CUDA;
-        opted = smem;
-    }
-    const int units_per_cta = gemv_slots(p.act.cols);
-    const int grid = std::max(1, std::min(sm_count(), (p.n_units + units_per_cta - 1) / units_per_cta));
-    return launch_ex(k_gemv_static, dim3(grid), dim3(kGemvWarps * 32), smem, st, pdl, p) == cudaSuccess ? GCUDA_OK
-                                                                                                          : GCUDA_E_CUDA;
+// The GEMV kernels' shared-memory opt-in: the largest any launch shape takes (plan_relay caps it there).
+inline int gemv_opt_in() {
+    static const int rc = [] {
+        if (cudaFuncSetAttribute(k_gemv_static, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess)
+            return static_cast<int>(GCUDA_E_CUDA);
+        return static_cast<int>(GCUDA_OK);
+    }();
+    return rc;
+}
+
+// p.wpu / p.nslots are set here (plan_static); the grid is one CTA per SM at most
+inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
+    RelayShape r;
+    if (!plan_static(p.act.cols, p.n_units, sm_count(), r)) return GCUDA_E_ARG;
+    if (gemv_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
+    p.wpu = r.wpu;
+    p.nslots = r.nslots;
+    const int grid = std::max(1, std::min(sm_count(), (p.n_units + r.nslots - 1) / r.nslots));
+    return launch_ex(k_gemv_static, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p) == cudaSuccess ? GCUDA_OK
+                                                                                                            : GCUDA_E_CUDA;
 }
 
 }  // namespace gcu

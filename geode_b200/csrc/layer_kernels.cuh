@@ -514,10 +514,11 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
             const float s_a = Ss[r * kAttnSub + lane], s_b = Ss[r * kAttnSub + lane + 32];
             const float mx = warp_max(fmaxf(s_a, s_b));
             const float m_old = row_m[r], m_new = fmaxf(m_old, mx);
-            const float ea = s_a == -INFINITY ? 0.0f : expf_cr(__fsub_rn(s_a, m_new));
-            const float eb = s_b == -INFINITY ? 0.0f : expf_cr(__fsub_rn(s_b, m_new));
-            const float sum = warp_sum(__fadd_rn(ea, eb));
-            const float f = m_old == -INFINITY ? 0.0f : expf_cr(__fsub_rn(m_old, m_new));
+            // (the attention's softmax is not bit-exact across the regrouped blocks anyway: the fast exp)
+            const float ea = s_a == -INFINITY ? 0.0f : __expf(s_a - m_new);
+            const float eb = s_b == -INFINITY ? 0.0f : __expf(s_b - m_new);
+            const float sum = warp_sum(ea + eb);
+            const float f = m_old == -INFINITY ? 0.0f : __expf(m_old - m_new);
             Ps[r * PS + lane] = __float2half_rn(__fmul_rn(ea, vsc[lane]));
             Ps[r * PS + lane + 32] = __float2half_rn(__fmul_rn(eb, vsc[lane + 32]));
             __syncwarp();
@@ -608,32 +609,53 @@ struct MergeArgs {
 };
 
 __global__ void k_attn_merge(MergeArgs a) {
+    __shared__ float s_f[4][64];   // per warp: each chunk's factor exp(m_c - M) (nchunks <= 64 per pass)
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int pos = *a.pos;
     const int W = a.nh * a.hd;
+    const size_t cs = a.hd + 2;
     for (int item = blockIdx.x * nw + warp; item < a.n * a.nh; item += gridDim.x * nw) {
         const int t = item / a.nh, h = item % a.nh;
         const int nc = min(a.nchunks, (pos + t) / kAttnChunk + 1);
-        const float *pp = a.part + (static_cast<size_t>(t) * a.nh + h) * a.nchunks * (a.hd + 2);
+        const float *pp = a.part + (static_cast<size_t>(t) * a.nh + h) * a.nchunks * cs;
         float M = -INFINITY;
-        for (int c = 0; c < nc; ++c) M = fmaxf(M, pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd]);
+        for (int c = lane; c < nc; c += 32) M = fmaxf(M, pp[c * cs + a.hd]);
+        M = warp_max(M);
         float L = 0.0f;
-        for (int c = 0; c < nc; ++c) {
-            const float mc = pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd];
-            if (mc == -INFINITY) continue;
-            L = __fadd_rn(L, __fmul_rn(pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd + 1], expf_cr(__fsub_rn(mc, M))));
+        for (int c0 = 0; c0 < nc; c0 += 64) {
+            for (int c = c0 + lane; c < min(nc, c0 + 64); c += 32) {
+                const float mc = pp[c * cs + a.hd];
+                const float f = mc == -INFINITY ? 0.0f : __expf(mc - M);
+                s_f[warp][c - c0] = f;
+                L += pp[c * cs + a.hd + 1] * f;
+            }
+            __syncwarp();
         }
-        const float inv = __fdiv_rn(1.0f, L);
+        L = warp_sum(L);
+        const float inv = 1.0f / L;
         const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
-        // 16-value blocks: a half-warp per block, lanes over the head's dims
         for (int d0 = 0; d0 < a.hd; d0 += 32) {
             const int d = d0 + lane;
             float acc = 0.0f;
-            for (int c = 0; c < nc; ++c) {
-                const float mc = pp[static_cast<size_t>(c) * (a.hd + 2) + a.hd];
-                if (mc == -INFINITY) continue;
-                acc = __fadd_rn(acc, __fmul_rn(pp[static_cast<size_t>(c) * (a.hd + 2) + d], expf_cr(__fsub_rn(mc, M))));
+            for (int c0 = 0; c0 < nc; c0 += 64) {
+                if (c0 > 0) {   // (more than 64 chunks: the factors of the next 64)
+                    __syncwarp();
+                    for (int c = c0 + lane; c < min(nc, c0 + 64); c += 32) {
+                        const float mc = pp[c * cs + a.hd];
+                        s_f[warp][c - c0] = mc == -INFINITY ? 0.0f : __expf(mc - M);
+                    }
+                    __syncwarp();
+                }
+                for (int c = c0; c < min(nc, c0 + 64); ++c) acc = fmaf(pp[c * cs + d], s_f[warp][c - c0], acc);
+            }
+            if (nc > 64) {   // restore the first 64 factors for the next dims
+                __syncwarp();
+                for (int c = lane; c < min(nc, 64); c += 32) {
+                    const float mc = pp[c * cs + a.hd];
+                    s_f[warp][c] = mc == -INFINITY ? 0.0f : __expf(mc - M);
+                }
+                __syncwarp();
             }
             const float v = __fmul_rn(__fmul_rn(acc, inv), sigmoid_cr(gate[d]));
             const int col = h * a.hd + d;
@@ -650,6 +672,7 @@ __global__ void k_attn_merge(MergeArgs a) {
                 a.bsum[static_cast<size_t>(t) * (W / 16) + col / 16] = sm;
             }
         }
+        __syncwarp();
     }
 }
 
@@ -669,8 +692,9 @@ struct RouteOut {
     float gs[kMaxTok];
 };
 
-__global__ void k_route(const float *__restrict__ logits, int n, int E, int K, RouteOut *out) {
+__global__ void k_route(const float *__restrict__ logits, int n, int E, int K, RouteOut *out, int *union_acc) {
     extern __shared__ float ps[];   // E floats per warp
+    __shared__ int s_ids[kMaxTok * 8], s_first[kMaxTok * 8], s_rank[kMaxTok * 8];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < n) {
@@ -678,31 +702,147 @@ __global__ void k_route(const float *__restrict__ logits, int n, int E, int K, R
         if (lane == 0) out->gs[warp] = sigmoid_cr(logits[static_cast<size_t>(warp) * (E + 1) + E]);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int nu = 0;
-        // picks sorted by expert (ties by token, then rank: the reference's std::sort of (expert, token, rank))
-        for (;;) {
-            int best = 0x7fffffff;
-            for (int i = 0; i < n * K; ++i) {
-                const int e = out->ids[i];
-                bool seen = false;
-                for (int u = 0; u < nu; ++u) seen |= out->ex[u] == e;
-                if (!seen && e < best) best = e;
-            }
-            if (best == 0x7fffffff || nu >= kMaxUnion) break;
-            out->ex[nu] = best;
-            int m = 0;
-            for (int t = 0; t < kMaxTok; ++t) out->slot[nu][t] = 0;
-            for (int i = 0; i < n * K; ++i)
-                if (out->ids[i] == best) {
-                    m |= 1 << (i / K);
-                    out->slot[nu][i / K] = i;
-                }
-            out->mask[nu] = m;
-            ++nu;
-        }
-        out->n_union = nu;
+    // the union, in parallel over the n*K picks (pick p = t*K + k): a pick is its expert's first when no earlier pick
+    // has the expert; its expert's union slot = the number of distinct smaller experts
+    const int P = n * K, p = threadIdx.x;
+    if (p < P) s_ids[p] = out->ids[p];
+    __syncthreads();
+    if (p < P) {
+        const int e = s_ids[p];
+        bool first = true;
+        for (int q = 0; q < p; ++q) first &= s_ids[q] != e;
+        s_first[p] = first ? 1 : 0;
     }
+    __syncthreads();
+    if (p < P) {
+        const int e = s_ids[p];
+        int r = 0;
+        for (int q = 0; q < P; ++q) r += s_first[q] && s_ids[q] < e;
+        s_rank[p] = r;
+    }
+    __syncthreads();
+    if (p < P && s_first[p]) {
+        const int u = s_rank[p], e = s_ids[p];
+        out->ex[u] = e;
+        int m = 0;
+        for (int t = 0; t < kMaxTok; ++t) out->slot[u][t] = 0;
+        for (int q = 0; q < P; ++q)
+            if (s_ids[q] == e) {
+                m |= 1 << (q / K);
+                out->slot[u][q / K] = q;
+            }
+        out->mask[u] = m;
+    }
+    if (p == 0) {
+        int nu = 0;
+        for (int q = 0; q < P; ++q) nu += s_first[q];
+        out->n_union = nu;
+        if (union_acc) atomicAdd(union_acc, nu);
+    }
+}
+
+}  // namespace gcu
+
+namespace gcu {
+
+// ------------------------------------------------------------------------------------------- synthetic weights ----
+// Seeded random bytes for measuring runs whose values do not matter (the self-test weights of
+// engine/src/gpu_check.cpp:51-63: random codes, E4M3 scales in 0x30..0x48), written straight into device memory.
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {   // splitmix64's finalizer
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+__device__ __forceinline__ float unit_f(uint64_t h) { return static_cast<float>(h >> 40) * (1.0f / 16777216.0f); }
+__device__ __forceinline__ float normal_f(uint64_t h) {   // Box-Muller
+    const float u1 = fmaxf(unit_f(h), 1e-7f), u2 = unit_f(mix64(h));
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+// tiled q4 bytes: codes random, the scale bytes (offsets 512..575 of every 576-byte group) in 0x30..0x48
+__global__ void k_synth_tiled(uint8_t *p, size_t bytes, uint64_t seed) {
+    for (size_t i = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) * 8; i < bytes;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x * 8) {
+        const uint64_t h = mix64(seed ^ (i * 0x100000001B3ull));
+        uint8_t b[8];
+        for (int k = 0; k < 8; ++k) {
+            const size_t at = i + k;
+            const uint8_t r = static_cast<uint8_t>(h >> (8 * k));
+            b[k] = (at % kGroupBytes) >= 512 ? static_cast<uint8_t>(0x30 + r % 25) : r;
+        }
+        if (i + 8 <= bytes) *reinterpret_cast<uint2 *>(p + i) = *reinterpret_cast<uint2 *>(b);
+        else
+            for (int k = 0; i + k < bytes; ++k) p[i + k] = b[k];
+    }
+}
+
+// pack-layout q4 rows (the embedding table): codes random, each row's last cols/16 bytes scales
+__global__ void k_synth_rows(uint8_t *p, int64_t rows, int cols, uint64_t seed) {
+    const size_t rb = static_cast<size_t>(cols / 16) * 9, total = static_cast<size_t>(rows) * rb;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total; i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint8_t r = static_cast<uint8_t>(mix64(seed ^ i));
+        p[i] = (i % rb) >= static_cast<size_t>(cols / 2) ? static_cast<uint8_t>(0x30 + r % 25) : r;
+    }
+}
+
+// f32 (dtype 0) or bf16 (1) values mean + std * N(0, 1)
+__global__ void k_synth_values(void *p, size_t count, int dtype, float mean, float stdv, uint64_t seed) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < count; i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const float v = mean + stdv * normal_f(mix64(seed ^ (i * 0x9E3779B97F4A7C15ull)));
+        if (dtype == 0) static_cast<float *>(p)[i] = v;
+        else static_cast<uint16_t *>(p)[i] = static_cast<uint16_t>((__float_as_uint(v) + 0x7FFFu + ((__float_as_uint(v) >> 16) & 1u)) >> 16);
+    }
+}
+
+// int8 KV rows with their scales, for a synthetic context: values uniform in +-127, scales std * |N(0,1)| / 127
+__global__ void k_synth_kv(int8_t *kv, size_t n, float *sc, size_t ns, float stdv, uint64_t seed) {
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        kv[i] = static_cast<int8_t>(static_cast<int>(mix64(seed ^ i) % 255) - 127);
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < ns; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        sc[i] = stdv * fabsf(normal_f(mix64(~seed ^ i))) / 127.0f + 1e-4f;
+}
+
+// ------------------------------------------------------------------------------------------- device-side step ----
+// The acceptance decision on the device (engine/src/geode.cpp:327-350) for a chained device-resident loop: from the
+// rows' samples and the batch's tokens, kept and next; the next batch starts with `next` (its drafts: the caller's);
+// the position moves on by kept; the Gated DeltaNet states roll back to backup kept-1 when kept < n (k_rollback).
+struct StepState {
+    int kept, next, n_union_sum, steps;
+};
+__global__ void k_decide(const int *samples, int *toks, int n, int *pos, StepState *ss) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    int k = 1, nx = samples[n - 1];
+    for (int i = 0; i < n; ++i) {
+        if (i + 1 < n && samples[i] == toks[i + 1]) {
+            ++k;
+            continue;
+        }
+        nx = samples[i];
+        break;
+    }
+    ss->kept = k;
+    ss->next = nx;
+    ss->steps += 1;
+    *pos += k;
+    toks[0] = nx;
+}
+
+// state = backup[kept - 1] when kept < n (a grid-stride copy of the conv and recurrent states)
+__global__ void k_rollback(float *conv, const float *conv_bk, size_t conv_n, float *gdn, const float *gdn_bk, size_t gdn_n,
+                           int n, const StepState *ss) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int kept = ss->kept;
+    if (kept >= n) return;
+    const size_t b = static_cast<size_t>(kept - 1);
+    const float4 *cs = reinterpret_cast<const float4 *>(conv_bk + b * conv_n);
+    const float4 *gs = reinterpret_cast<const float4 *>(gdn_bk + b * gdn_n);
+    float4 *cd = reinterpret_cast<float4 *>(conv), *gd = reinterpret_cast<float4 *>(gdn);
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < conv_n / 4; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        cd[i] = cs[i];
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < gdn_n / 4; i += static_cast<size_t>(gridDim.x) * blockDim.x)
+        gd[i] = gs[i];
 }
 
 }  // namespace gcu

@@ -13,7 +13,7 @@ namespace gcu {
 
 constexpr int kRelayStages = 6;   // ring stages per warp, one group of both tiles each
 constexpr int kStageBytesR = 2 * kGroupBytes;
-constexpr int kPre = 1;           // groups computed before the predecessor's hand-off
+constexpr int kPre = 2;           // groups computed before the predecessor's hand-off
 
 // f32x2 (sm_100): two IEEE operations per instruction, each lane rounded on its own
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
@@ -31,6 +31,15 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// a * b rounded once, as mul.rn.f32x2 - written as fma(a, b, z) with z a +0 pair the compiler cannot see is zero, so
+// that no later pass contracts the product with the add that consumes it (ptxas was seen to fuse a mul.rn.f32x2 /
+// add.rn.f32x2 pair). fma(a, b, +0) = round(a b), except that a -0 product becomes +0; the chains here start at +0
+// and only add, so they never hold -0 and adding either zero leaves them unchanged.
+__device__ __forceinline__ uint64_t f2_mul_sep(uint64_t a, uint64_t b, uint64_t z) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(z));
+    return d;
+}
 __device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return static_cast<uint64_t>(hi) << 32 | lo; }
 __device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
 __device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
@@ -43,21 +52,57 @@ __device__ __forceinline__ float e4m3_alu(uint32_t b) {
     return __fmul_rn(__uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20)), 0x1p120f);
 }
 
-// Shared memory per warp: the ring, its barriers, one group's scales as (e, e) float pairs, the warp's activation
-// image for its K-slice, and the relay mailbox (2 parities x 32 lanes x 4 float pairs).
+// Shared memory per warp: the ring, its barriers, one group's scales as (e, e) float pairs, the relay mailbox
+// (2 parities x 32 lanes x 4 float pairs) and, for launches whose units multiply different activations, the warp's own
+// activation image of its K-slice (else the CTA shares one image of all K).
 __host__ __device__ inline int slice_tstride(int sg) { return sg * 64 + (sg % 2 == 0 ? 64 : 0); }
 __host__ __device__ inline int warp_act_bytes(int sg) { return kMaxTok * slice_tstride(sg) + sg * 4 * 64; }
-__host__ __device__ inline int warp_smem_bytes(int sg) {
-    const int b = kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8 + warp_act_bytes(sg) + 2 * 32 * 32;
+__host__ __device__ inline int warp_base_bytes() {
+    return kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8 + 2 * 32 * 32;
+}
+__host__ __device__ inline int warp_smem_bytes(int sg_own) {   // sg_own: the own image's groups (0: none)
+    const int b = warp_base_bytes() + (sg_own ? warp_act_bytes(sg_own) : 0);
     return (b + 127) / 128 * 128;
 }
-// warps per unit for K: a slice of two groups where K allows (at most 16 warps)
-__host__ __device__ inline int warps_per_unit(int cols) {
-    int g = cols / 64, w = g / 2;
+// the whole-K image the CTA shares (act_tstride: token stride of the full image)
+__host__ __device__ inline int act_tstride(int cols) { return (cols / 64) * 64 + ((cols / 64) % 2 == 0 ? 64 : 0); }
+__host__ __device__ inline int act_smem_bytes(int cols) { return (kMaxTok * act_tstride(cols) + (cols / 64) * 4 * 64 + 127) / 128 * 128; }
+// warps per unit: long slices (8 groups) for launches with units for every warp of the GPU several times over, short
+// ones (2 groups: the chain crosses the unit quickly) for latency-bound small matrices; always a divisor of K/64
+__host__ __device__ inline int choose_wpu(int cols, int n_units, int sms) {
+    const int g = cols / 64;
+    int w = n_units >= 3 * sms ? g / 8 : g / 2;
     if (w < 1) w = 1;
     if (w > 16) w = 16;
     while (g % w) --w;
     return w;
+}
+
+constexpr int kMaxDynSmem = 227 * 1024;
+
+// A launch's shape: wpu warps per unit, nslots units at a time per CTA, the dynamic shared memory. The warps' regions
+// (own: the groups of a per-warp image, 0 for none) follow `front` bytes (the CTA's shared image, or 0). Slots are
+// dropped, then shorter chains taken, until it fits. False if no shape fits.
+struct RelayShape {
+    int wpu, nslots, sg;
+    size_t smem;
+};
+inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelayShape &r) {
+    const int g = cols / 64;
+    if (g < 1 || wpu < 1) return false;
+    for (; wpu >= 1; --wpu) {
+        if (g % wpu) continue;
+        const int sg = g / wpu;
+        const size_t wb = static_cast<size_t>(warp_smem_bytes(own_images ? sg : 0));
+        for (int ns = kGemvWarps / wpu; ns >= 1; --ns) {
+            const size_t sm = front + static_cast<size_t>(ns * wpu) * wb;
+            if (sm <= static_cast<size_t>(kMaxDynSmem)) {
+                r = RelayShape{wpu, ns, sg, sm};
+                return true;
+            }
+        }
+    }
+    return false;
 }
 
 // The warp's activation image for groups [g0, g0 + sg) of up to kMaxTok vectors (sel[t] = the ActSet row of token
@@ -92,10 +137,38 @@ __device__ inline void stage_slice(const ActSet &a, const int *sel, int g0, int 
     }
 }
 
-// One group's products for both tiles: p[j][0..3] = tile A (row gid: tokens pair, row gid+8: pair), tile B likewise.
+// The CTA's image of all K for the first ncols vectors of an ActSet (zeros for the columns after them, up to kMaxTok),
+// the same layout as a slice image with groups g = 0 .. K/64-1 and token stride act_tstride(K). Every thread of the CTA.
+__device__ inline void stage_full(const ActSet &a, int ncols, uint8_t *img) {
+    const int cols = a.cols, ts = act_tstride(cols), nb = cols / 16, wpr = cols / 4;
+    for (int i = threadIdx.x; i < kMaxTok * wpr; i += blockDim.x) {
+        const int t = i / wpr, w = i % wpr;
+        const int b = w / 4, tig = w % 4, g = b / 4, j = b % 4;
+        uint32_t v = 0;
+        if (t < ncols) v = *reinterpret_cast<const uint32_t *>(a.q + static_cast<size_t>(t) * a.qstride + 4 * w);
+        *reinterpret_cast<uint32_t *>(img + t * ts + (g * 4 + tig) * 16 + j * 4) = v;
+    }
+    int32_t *cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts);
+    for (int i = threadIdx.x; i < nb * kMaxTok; i += blockDim.x) {
+        const int b = i / kMaxTok, t = i % kMaxTok, g = b / 4, j = b % 4;
+        int32_t ci = static_cast<int32_t>(kBiasBits);
+        float sc = 0.0f;
+        if (t < ncols) {
+            ci -= 15 * a.bsum[static_cast<size_t>(t) * a.sstride + b];
+            sc = a.scale[static_cast<size_t>(t) * a.sstride + b];
+        }
+        int32_t *base = cs + (g * 4 + t / 2) * 16;
+        base[(t % 2) * 4 + j] = ci;
+        reinterpret_cast<float *>(base)[8 + 2 * j + (t % 2)] = sc;
+    }
+}
+
+// One group of both tiles: for block j = 0..3 the products p[0..3] = tile A (row gid: the token pair (2 tig,
+// 2 tig + 1), row gid + 8: the pair), tile B likewise, handed to sink(j, p) in block order.
 // e4p: the group's scales as [tile][block][gid][e(gid), e(gid), e(gid+8), e(gid+8)] floats.
+template <typename Sink>
 __device__ __forceinline__ void group_products(const uint8_t *stage, const float *e4p, const uint8_t *act, const uint8_t *cs,
-                                               int lane, uint64_t (&p)[4][4]) {
+                                               int lane, uint64_t zero, const Sink &sink) {
     const int gid = lane >> 2;
     const uint4 wa = ld_shared_v4(stage + lane * 16);
     const uint4 wb = ld_shared_v4(stage + kGroupBytes + lane * 16);
@@ -121,10 +194,11 @@ __device__ __forceinline__ void group_products(const uint8_t *stage, const float
         // float(isum) = bits(bias + isum) - bias; p = float(isum) * (e4m3 * ascale)
         const uint64_t FAg = f2_sub(pack2(dA[0], dA[1]), bias2), FAh = f2_sub(pack2(dA[2], dA[3]), bias2);
         const uint64_t FBg = f2_sub(pack2(dB[0], dB[1]), bias2), FBh = f2_sub(pack2(dB[2], dB[3]), bias2);
-        p[j][0] = f2_mul(FAg, f2_mul(pack2(eA.x, eA.y), sp[j]));
-        p[j][1] = f2_mul(FAh, f2_mul(pack2(eA.z, eA.w), sp[j]));
-        p[j][2] = f2_mul(FBg, f2_mul(pack2(eB.x, eB.y), sp[j]));
-        p[j][3] = f2_mul(FBh, f2_mul(pack2(eB.z, eB.w), sp[j]));
+        const uint64_t p[4] = {f2_mul_sep(FAg, f2_mul(pack2(eA.x, eA.y), sp[j]), zero),
+                               f2_mul_sep(FAh, f2_mul(pack2(eA.z, eA.w), sp[j]), zero),
+                               f2_mul_sep(FBg, f2_mul(pack2(eB.x, eB.y), sp[j]), zero),
+                               f2_mul_sep(FBh, f2_mul(pack2(eB.z, eB.w), sp[j]), zero)};
+        sink(j, p);
     }
 }
 
@@ -132,11 +206,14 @@ struct RelayCtx {
     uint8_t *ring;     // kRelayStages stages
     uint64_t *bar;
     float *e4p;        // 2 tiles x 16 rows x 4 blocks x (e, e)
-    uint8_t *img;      // activation image of the slice
+    uint8_t *img;      // the activation image: token t's bytes at t * img_ts, this warp's groups from g_off
+    int img_ts, g_off;
+    uint8_t *own_img;  // the warp's own slice image (launches with per-unit activations), or NULL
     uint64_t *mail;    // [2][32][4] pairs: this slot's hand-off from the predecessor
     uint64_t *mail_next;   // the successor's mailbox
     int part, wpu, sg;
     int bar_in, bar_out;   // named barrier ids (0: none)
+    uint64_t zero;         // a +0 pair from runtime values (f2_mul_sep)
 };
 
 // The units of one slot: get(i, U) the i-th (false past the end); restage(U) fills ctx.img for U's act_id when it
@@ -184,16 +261,19 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
         fetch(0);
         for (int i = 0; i < kRelayStages - 1; ++i) issue();
     }
-    const int ts = slice_tstride(sg);
     int consumed = 0;
-    GemvUnit U;
     bool ok = true;
-    for (int u = 0; get(u, U); ++u) {
-        restage(U);
-        const uint8_t *act = c.img + gid * ts + tig * 16;
-        const uint8_t *cs = c.img + kMaxTok * ts + tig * 64;
-        // one group: wait, the scales to (e, e) pairs, the products
-        auto group = [&](int gl, uint64_t (&p)[4][4]) -> bool {
+    for (int u = 0;; ++u) {
+        {   // (the unit is read again for the epilogue: nothing of it stays live across the groups)
+            GemvUnit U;
+            if (!get(u, U)) break;
+            restage(U);
+        }
+        const int ts = c.img_ts;
+        const uint8_t *act = c.img + gid * ts + tig * 16 + c.g_off * 64;
+        const uint8_t *cs = c.img + kMaxTok * ts + tig * 64 + c.g_off * 256;
+        // one group: wait, the scales to (e, e) pairs, the products into sink(j, p[4])
+        auto group = [&](int gl, const auto &sink) -> bool {
             if (!ok) return false;   // (after a wait gave up: no more waits; the chain still runs, the status says why)
             const int s = consumed % kRelayStages;
             if (!mbar_wait_bounded(&c.bar[s], (consumed / kRelayStages) & 1, status)) return false;
@@ -208,17 +288,22 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
                 }
             }
             __syncwarp();
-            group_products(st, c.e4p, act + gl * 64, cs + gl * 256, lane, p);
+            group_products(st, c.e4p, act + gl * 64, cs + gl * 256, lane, c.zero, sink);
             ++consumed;
             __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
             issue();
             return true;
         };
+        // the first kPre groups before the predecessor's hand-off, kept as products
         uint64_t pre[kPre][4][4];
         const int npre = sg < kPre ? sg : kPre;
 #pragma unroll
         for (int gl = 0; gl < kPre; ++gl)
-            if (gl < npre && !group(gl, pre[gl])) ok = false;
+            if (gl < npre && !group(gl, [&](int j, const uint64_t (&p)[4]) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) pre[gl][j][q] = p[q];
+                }))
+                ok = false;
         // the chain so far
         uint64_t acc[4];
         const int par = u & 1;
@@ -236,20 +321,21 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
                 for (int j = 0; j < 4; ++j)
 #pragma unroll
                     for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], pre[gl][j][q]);
-        for (int gl = npre; gl < sg; ++gl) {
-            uint64_t p[4][4];
-            if (!group(gl, p)) ok = false;
+        // the rest straight into the chain, block by block
+        auto chain = [&](int, const uint64_t (&p)[4]) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[j][q]);
-        }
+            for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[q]);
+        };
+        for (int gl = npre; gl < sg; ++gl)
+            if (!group(gl, chain)) ok = false;
         if (c.part + 1 < c.wpu) {
             uint64_t *m = c.mail_next + (par * 32 + lane) * 4;
             m[0] = acc[0], m[1] = acc[1], m[2] = acc[2], m[3] = acc[3];
             asm volatile("bar.sync %0, 64;" ::"r"(c.bar_out) : "memory");
         } else {
             // y = acc * global * 1 (engine/src/kernels.cpp:1320); y0: tile A (gid: t 2tig, 2tig+1; gid+8: ...), y1: B
+            GemvUnit U;
+            get(u, U);
             float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
             float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
 #pragma unroll
@@ -265,24 +351,35 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
     return ok;
 }
 
-// The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu.
-__device__ inline RelayCtx make_ctx(uint8_t *smem_warps, int sg_max, int wpu) {
+// The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu. smem_warps: the warps'
+// regions (warp_smem_bytes(sg_own) each); img / img_ts: the CTA's shared image (or NULL: the warp's own, sg_own groups).
+__device__ inline RelayCtx make_ctx(uint8_t *smem_warps, int wpu, int sg, int sg_own, uint8_t *img, int img_ts) {
     const int warp = threadIdx.x >> 5;
-    const int wb = warp_smem_bytes(sg_max);
+    const int wb = warp_smem_bytes(sg_own);
     uint8_t *base = smem_warps + static_cast<size_t>(warp) * wb;
     RelayCtx c;
     c.ring = base;
     c.bar = reinterpret_cast<uint64_t *>(base + kRelayStages * kStageBytesR);
     c.e4p = reinterpret_cast<float *>(base + kRelayStages * kStageBytesR + kRelayStages * 8);
-    c.img = base + kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8;
-    c.mail = reinterpret_cast<uint64_t *>(c.img + warp_act_bytes(sg_max));
+    c.mail = reinterpret_cast<uint64_t *>(base + kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8);
+    c.own_img = sg_own ? reinterpret_cast<uint8_t *>(c.mail) + 2 * 32 * 32 : nullptr;
+    c.mail_next = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(c.mail) + wb);   // the next warp's mailbox
     c.wpu = wpu;
+    c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);   // (wpu >= 1: always 0)
     c.part = warp % wpu;
-    c.sg = 0;
+    c.sg = sg;
+    if (img) {
+        c.img = img;
+        c.img_ts = img_ts;
+        c.g_off = c.part * sg;
+    } else {
+        c.img = c.own_img;
+        c.img_ts = slice_tstride(sg);
+        c.g_off = 0;
+    }
     const int slot = warp / wpu;
     c.bar_in = c.part > 0 ? 1 + slot * (wpu - 1) + (c.part - 1) : 0;
     c.bar_out = c.part + 1 < wpu ? 1 + slot * (wpu - 1) + c.part : 0;
-    c.mail_next = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(c.mail) + wb);   // the next warp's mailbox
     if ((threadIdx.x & 31) == 0)
         for (int s = 0; s < kRelayStages; ++s) mbar_init(&c.bar[s], 1);
     fence_barrier_init();

@@ -24,19 +24,35 @@ __device__ __forceinline__ void bf16_dot8(const uint16_t *__restrict__ w, const 
     out = a;
 }
 
-__global__ void k_bf16_gemv(const uint16_t *__restrict__ w, int rows, int cols, const float *__restrict__ x, int xstride,
-                            int n, float *__restrict__ y, int ystride) {
+// 32 rows per CTA, 8 lanes (j) per row; every lane carries all n tokens' partial sums (the row's bf16 is read once
+// for them), x staged in shared memory. Bits as bf16_dot8's. Dynamic smem: n * cols floats.
+__global__ void __launch_bounds__(256) k_bf16_gemv(const uint16_t *__restrict__ w, int rows, int cols,
+                                                   const float *__restrict__ x, int xstride, int n, float *__restrict__ y,
+                                                   int ystride) {
+    extern __shared__ float xs[];
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int64_t total = static_cast<int64_t>(rows) * n * 8;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < (total + 31) / 32 * 32;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const bool live = i < total;
-        const int64_t k = live ? i : total - 1;
-        const int j = static_cast<int>(k % 8);
-        const int t = static_cast<int>((k / 8) % n);
-        const int r = static_cast<int>(k / 8 / n);
-        float v;
-        bf16_dot8(w + static_cast<size_t>(r) * cols, x + static_cast<size_t>(t) * xstride, cols, j, v);
+    for (int i = threadIdx.x; i < n * cols; i += blockDim.x) xs[i] = x[static_cast<size_t>(i / cols) * xstride + i % cols];
+    __syncthreads();
+    const int j = threadIdx.x & 7, r = blockIdx.x * 32 + (threadIdx.x >> 3);
+    const bool live = r < rows;
+    const uint16_t *wr = w + static_cast<size_t>(live ? r : 0) * cols;
+    float a[kMaxTok];
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) a[t] = 0.0f;
+#pragma unroll 4
+    for (int c = j; c < cols; c += 8) {
+        const float wf = __uint_as_float(static_cast<uint32_t>(wr[c]) << 16);
+#pragma unroll
+        for (int t = 0; t < kMaxTok; ++t)
+            if (t < n) a[t] = __fadd_rn(a[t], __fmul_rn(wf, xs[t * cols + c]));
+    }
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) {
+        if (t >= n) break;
+        float v = a[t];
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));   // j < 4: a_j + a_{j+4}
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));   // (a0+a4)+(a1+a5), (a2+a6)+(a3+a7)
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
         if (live && j == 0) y[static_cast<size_t>(t) * ystride + r] = v;
     }
 }

@@ -380,6 +380,12 @@ class Reference:
             raise RuntimeError("reference forward failed: " + err.value.decode())
         return out
 
+    def profile(self) -> str:
+        buf = C.create_string_buffer(8192)
+        self.lib.ref_profile.argtypes = [C.c_void_p, C.c_char_p, C.c_int]
+        self.lib.ref_profile(self.h, buf, 8192)
+        return buf.value.decode()
+
     def save_state(self, path: str):
         err = C.create_string_buffer(512)
         if self.lib.ref_save_state(self.h, path.encode(), err, 512) != 0:
@@ -409,3 +415,44 @@ def reference_lib():
                                C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
     lib.ref_uniforms.argtypes = [C.c_uint64, C.c_int, C.c_void_p]
     return lib
+
+
+# ------------------------------------------------------------------------------------------ state files ----
+# The reference's conversation file (engine/src/state.cpp:5-17, 45-65, 192-207): a 4096-byte header (StateHeader, an
+# FNV-1a checksum of its bytes last), the fixed part (gen, images, last hidden, conv states, GDN states, gen), then the
+# KV cache in blocks of 256 positions: [K, V][attention layer][256][kv_row] int8, then [K, V][layer][256][kv_heads] f32.
+_HDR = np.dtype([("magic", "S8"), ("version", "<u4"), ("header_size", "<u4"), ("fingerprint", "<u8"), ("conv_id", "<u8"),
+                 ("gen", "<u8"), ("position", "<i4"), ("extra", "<i4"), ("rope_delta", "<i4"), ("n_images", "<u4"),
+                 ("image_cap", "<u4"), ("kv_elem", "<u4"), ("n_attn", "<u4"), ("kv_heads", "<u4"), ("kv_row", "<u4"),
+                 ("hidden", "<u4"), ("has_hidden", "<u4"), ("block", "<u4"), ("conv_n", "<u8"), ("gdn_n", "<u8"),
+                 ("fixed_offset", "<u8"), ("fixed_bytes", "<u8"), ("kv_offset", "<u8"), ("block_bytes", "<u8"),
+                 ("checksum", "<u8")])
+
+
+def _fnv(data: bytes, h: int = 1469598103934665603) -> int:
+    for b in data:
+        h = ((h ^ b) * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+def write_long_state(template: str, out: str, position: int, seed: int = 0):
+    """A state file at `position` with random int8 KV rows (scales |N(0, 0.5)| / 127), from a template the reference
+    saved for the same model (its header and fixed part kept; the position, the KV blocks and the checksum new)."""
+    with open(template, "rb") as f:
+        data = bytearray(f.read())
+    h = np.frombuffer(bytes(data[:_HDR.itemsize]), dtype=_HDR)[0].copy()
+    assert h["magic"] == b"GEODESTA" and h["kv_elem"] == 1, "an int8-KV state of the reference"
+    h["position"] = position
+    raw = bytearray(h.tobytes())
+    raw[136:144] = _fnv(bytes(raw[:136])).to_bytes(8, "little")
+    rng = np.random.default_rng(seed)
+    B, n_attn, row, heads = int(h["block"]), int(h["n_attn"]), int(h["kv_row"]), int(h["kv_heads"])
+    blocks = (position + B - 1) // B
+    with open(out, "wb") as f:
+        f.write(raw)
+        f.write(bytes(data[len(raw): int(h["kv_offset"])]))
+        for b in range(blocks):
+            kv = rng.integers(-127, 128, 2 * n_attn * B * row, dtype=np.int8)
+            sc = (np.abs(rng.standard_normal(2 * n_attn * B * heads)) * 0.5 / 127 + 1e-4).astype(np.float32)
+            f.write(kv.tobytes())
+            f.write(sc.tobytes())

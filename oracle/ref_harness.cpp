@@ -65,6 +65,13 @@ void ref_close(void *h) { delete static_cast<Ref *>(h); }
 
 int ref_position(void *h) { return static_cast<Ref *>(h)->model.position(); }
 
+// Model::profile (engine/src/model.cpp:5041): the stage times since open, one line
+void ref_profile(void *h, char *buf, int len) {
+    const std::string p = static_cast<Ref *>(h)->model.profile();
+    std::strncpy(buf, p.c_str(), static_cast<size_t>(len - 1));
+    buf[len - 1] = 0;
+}
+
 // trace: the next forward_batch records every layer's rows for its n tokens
 void ref_trace(void *h, int on, int layers, int tokens) {
     Ref *r = static_cast<Ref *>(h);
