@@ -249,9 +249,8 @@ int enqueue_step(gcuda *g, int n) {
         const LayerPlan &P = g->plan[static_cast<size_t>(l)];
         if (!L.attn) {
             RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
-            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3((2 * s.gdn_v_heads + 31) / 32), dim3(256), sizeof(float) * n * H, g->st, pdl,
-                                static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H,
-                                static_cast<const float *>(g->hf), H, n, g->ab, 2 * s.gdn_v_heads));
+            RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H, g->hf, H, n, g->ab,
+                                   2 * s.gdn_v_heads, g->d_status, g->st, pdl));
             GdnArgs a{};
             a.proj = g->big;
             a.z = g->zb;
@@ -363,7 +362,7 @@ int enqueue_step(gcuda *g, int n) {
             ma.scale = g->core.scale;
             ma.bsum = g->core.bsum;
             ma.core_f = g->core_f;
-            LAUNCH_OK(launch_ex(k_attn_merge, dim3((n * s.n_heads + 3) / 4), dim3(128), 0, g->st, pdl, ma));
+            LAUNCH_OK(launch_ex(k_attn_merge, dim3(n * s.n_heads), dim3(s.head_dim), sizeof(float) * g->nchunks, g->st, pdl, ma));
             RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, s.n_heads * s.head_dim));
         }
         // x += mix happened in the output product's epilogue; h = rmsnorm(x, post_norm)
@@ -376,9 +375,8 @@ int enqueue_step(gcuda *g, int n) {
             RC_OK(norm(next_norm, false, next_hf));
         } else {
             const int E = s.n_experts;
-            LAUNCH_OK(launch_ex(k_bf16_gemv, dim3((E + 1 + 31) / 32), dim3(256), sizeof(float) * n * H, g->st, pdl,
-                                static_cast<const uint16_t *>(P.router_w), E + 1, H, static_cast<const float *>(g->hf), H,
-                                n, g->rlog, E + 1));
+            RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.router_w), E + 1, H, g->hf, H, n, g->rlog, E + 1,
+                                   g->d_status, g->st, pdl));
             LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(32 * kMaxTok), kMaxTok * E * sizeof(float), g->st, pdl,
                                 static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum));
             const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
@@ -412,7 +410,10 @@ int enqueue_step(gcuda *g, int n) {
                 ea.pass = pass;
                 ea.wpu = r.wpu;
                 ea.nslots = r.nslots;
-                LAUNCH_OK(launch_ex(k_gemv_experts, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
+                if (r.wpu == 1)
+                    LAUNCH_OK(launch_ex(k_gemv_experts<true>, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
+                else
+                    LAUNCH_OK(launch_ex(k_gemv_experts<false>, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
             }
             RC_OK(norm(next_norm, true, next_hf));
         }
@@ -429,7 +430,6 @@ int set_attrs(gcuda *g) {
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<128>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<64>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_route, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxTok * s.n_experts * sizeof(float) + 16)));
-    LAUNCH_OK(cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kMaxTok * s.hidden * sizeof(float))));
     return GCUDA_OK;
 }
 

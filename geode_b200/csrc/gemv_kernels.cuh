@@ -108,7 +108,7 @@ __global__ void k_quantize(const float *__restrict__ x, int n, int cols, int xst
 }
 
 // ------------------------------------------------------------------------------------------- the static GEMV ----
-// A table of units (built on the host), or one plain matrix, against one ActSet; slots take units round-robin. Every
+// A table of units (built on the host), or one plain matrix, against one ActSet; units are dealt to the CTAs in turn. Every
 // unit multiplies the same activations, so the CTA stages one image of all K (after the previous kernel ends) and
 // every warp reads its groups from it.
 struct StaticGemv {
@@ -126,9 +126,11 @@ struct StaticGemv {
 };
 
 inline bool plan_static(int cols, int n_units, int sms, RelayShape &r) {
-    return plan_relay(cols, choose_wpu(cols, n_units, sms), false, static_cast<size_t>(act_smem_bytes(cols)), r);
+    return plan_gemv(cols, choose_wpu(cols, n_units, sms), false, static_cast<size_t>(act_smem_bytes(cols)), r);
 }
 
+// kStream: the launch shape has one warp per unit (stream_units), else the relay (relay_units)
+template <bool kStream>
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
@@ -145,11 +147,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p
         prelude();
         return;
     }
-    RelayCtx c = make_ctx(smem + act_smem_bytes(cols), wpu, sg, 0, img, act_tstride(cols));
     const int slot = warp / wpu;
     const size_t tb = static_cast<size_t>(cols / 64) * kGroupBytes;
     auto get = [&](int i, GemvUnit &U) -> bool {
-        const int u = blockIdx.x * nslots + slot + i * gridDim.x * nslots;
+        // CTA-major: unit u on CTA u % grid, so every SM holds the same count (+-1) whatever the slots' share
+        const int u = blockIdx.x + gridDim.x * (slot + nslots * i);
         if (u >= p.n_units) return false;
         if (p.units) {
             U = p.units[u];
@@ -169,9 +171,21 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p
         for (int t = 0; t < kMaxTok; ++t) U.slot[t] = t;
         return true;
     };
-    relay_units(get, c, [](const GemvUnit &) {}, p.status, [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4],
-                                                               int gid, int tig) { epi_store(U, y0, y1, gid, tig); },
-                true, prelude);
+    auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
+        epi_store(U, y0, y1, gid, tig);
+    };
+    if constexpr (kStream) {
+        StreamCtx c;
+        c.e4p = reinterpret_cast<float *>(smem + act_smem_bytes(cols) + static_cast<size_t>(warp) * stream_warp_bytes(0));
+        c.img = img;
+        c.img_ts = act_tstride(cols);
+        c.ngroups = cols / 64;
+        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
+        stream_units(get, c, [](const GemvUnit &) {}, epi, true, prelude);
+    } else {
+        RelayCtx c = make_ctx(smem + act_smem_bytes(cols), wpu, sg, 0, img, act_tstride(cols));
+        relay_units(get, c, [](const GemvUnit &) {}, p.status, epi, true, prelude);
+    }
 }
 
 }  // namespace gcu
@@ -212,11 +226,12 @@ struct ExpertsArgs {
 inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, RelayShape &r) {
     const int picks = n * K < E ? n * K : E;
     if (pass == kGateUp)
-        return plan_relay(H, choose_wpu(H, picks * (ff / 16) + sff / 16, sms), false,
-                          static_cast<size_t>(act_smem_bytes(H)), r);
-    return plan_relay(ff, choose_wpu(ff, (picks + 1) * (H / 32), sms), true, 0, r);
+        return plan_gemv(H, choose_wpu(H, picks * (ff / 16) + sff / 16, sms), false,
+                         static_cast<size_t>(act_smem_bytes(H)), r);
+    return plan_gemv(ff, choose_wpu(ff, (picks + 1) * (H / 32), sms), true, 0, r);
 }
 
+template <bool kStream>
 __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
@@ -242,8 +257,6 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs
         else asm volatile("griddepcontrol.wait;" ::: "memory");
         return;
     }
-    RelayCtx c = gu ? make_ctx(smem + act_smem_bytes(p.H), wpu, sg, 0, img, act_tstride(p.H))
-                    : make_ctx(smem, wpu, sg, sg, nullptr, 0);
     const int slot = warp / wpu;
     const RouteOut &R = *p.route;
     int nu = 0, per_ex = 0, total = 0, u0 = 0, u1 = 0;
@@ -257,7 +270,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs
         per_ex = gu ? p.ff / 16 : p.H / 32;
         const int sh_units = gu ? p.sff / 16 : p.H / 32;
         total = nu * per_ex + sh_units;
-        const int nslots_all = gridDim.x * nslots, gs = blockIdx.x * nslots + slot;
+        // ranges CTA-major (range r on CTA r % grid): a launch with fewer ranges than slots still spreads over every SM
+        const int nslots_all = gridDim.x * nslots, gs = blockIdx.x + gridDim.x * slot;
         const int per = (total + nslots_all - 1) / nslots_all;
         u0 = gs * per;
         u1 = min(total, u0 + per);
@@ -319,18 +333,38 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs
         }
         return true;
     };
-    int staged = -2;
+    int staged = -2, part = 0;
+    uint8_t *own = nullptr;   // the warp's own image (down)
     auto restage = [&](const GemvUnit &U) {
         if (gu || U.act_id == staged) return;   // (gate_up: the CTA's image of h, staged in the prelude)
         __syncwarp();
         int sel[kMaxTok];
         for (int t = 0; t < kMaxTok; ++t) sel[t] = t < p.n && ((U.tok_mask >> t) & 1) ? U.slot[t] : -1;
-        stage_slice(U.act_id < 0 ? p.shact : p.amid, sel, c.part * sg, sg, c.own_img);
+        stage_slice(U.act_id < 0 ? p.shact : p.amid, sel, part * sg, sg, own);
         __syncwarp();
         staged = U.act_id;
     };
-    relay_units(get, c, restage, p.status, [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid,
-                                              int tig) { epi_store(U, y0, y1, gid, tig); }, false, prelude);
+    auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
+        epi_store(U, y0, y1, gid, tig);
+    };
+    if constexpr (kStream) {
+        // per warp: 1 KB of scale pairs, then (down) the warp's own image of all K
+        uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(gu ? 0 : sg);
+        StreamCtx c;
+        c.e4p = reinterpret_cast<float *>(wbase);
+        c.img = gu ? img : wbase + 1024;
+        c.img_ts = gu ? act_tstride(p.H) : slice_tstride(sg);
+        c.ngroups = cols / 64;
+        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
+        own = gu ? nullptr : wbase + 1024;
+        stream_units(get, c, restage, epi, false, prelude);
+    } else {
+        RelayCtx c = gu ? make_ctx(smem + act_smem_bytes(p.H), wpu, sg, 0, img, act_tstride(p.H))
+                        : make_ctx(smem, wpu, sg, sg, nullptr, 0);
+        own = c.own_img;
+        part = c.part;
+        relay_units(get, c, restage, p.status, epi, false, prelude);
+    }
 }
 
 }  // namespace gcu

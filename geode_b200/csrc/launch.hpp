@@ -66,8 +66,11 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
 // The GEMV kernels' shared-memory opt-in: the largest any launch shape takes (plan_relay caps it there).
 inline int gemv_opt_in() {
     static const int rc = [] {
-        if (cudaFuncSetAttribute(k_gemv_static, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) != cudaSuccess)
+        const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+        if (cudaFuncSetAttribute(k_gemv_static<true>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_static<false>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts<true>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts<false>, a, kMaxDynSmem) != cudaSuccess)
             return static_cast<int>(GCUDA_E_CUDA);
         return static_cast<int>(GCUDA_OK);
     }();
@@ -82,8 +85,27 @@ inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     p.wpu = r.wpu;
     p.nslots = r.nslots;
     const int grid = std::max(1, std::min(sm_count(), (p.n_units + r.nslots - 1) / r.nslots));
-    return launch_ex(k_gemv_static, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p) == cudaSuccess ? GCUDA_OK
-                                                                                                            : GCUDA_E_CUDA;
+    const cudaError_t e = r.wpu == 1 ? launch_ex(k_gemv_static<true>, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p)
+                                     : launch_ex(k_gemv_static<false>, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p);
+    return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+// The bf16 GEMV (router, Gated DeltaNet a/b): kBf16Rows rows per CTA. w and x 16-byte aligned, cols and xstride
+// multiples of 8 and 4, n <= kMaxTok.
+inline int launch_bf16_gemv(const uint16_t *w, int rows, int cols, const float *x, int xstride, int n, float *y,
+                            int ystride, uint32_t *status, cudaStream_t st, bool pdl) {
+    if (!w || !x || !y || rows <= 0 || cols <= 0 || cols % 8 || xstride % 4 || n < 1 || n > kMaxTok ||
+        (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
+        return GCUDA_E_ARG;
+    const size_t smem = bf16_gemv_smem(cols, n);
+    if (smem > static_cast<size_t>(kMaxDynSmem)) return GCUDA_E_ARG;
+    static const bool opted =
+        cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) == cudaSuccess;
+    if (!opted) return GCUDA_E_CUDA;
+    return launch_ex(k_bf16_gemv, dim3((rows + kBf16Rows - 1) / kBf16Rows), dim3(kBf16Rows * 32), smem, st, pdl, w, rows,
+                     cols, x, xstride, n, y, ystride, status) == cudaSuccess
+               ? GCUDA_OK
+               : GCUDA_E_CUDA;
 }
 
 }  // namespace gcu

@@ -103,12 +103,19 @@ __global__ void k_norm_quant(NormArgs a) {
     if (a.sh) {
         // engine/src/model.cpp:4554-4585 then 5363-5365: out = gs * shared; out += w_k * y_k (k in order, w == 0
         // skipped); x += out
+        // (every pick's row loaded first, independent loads; then the sum in rank order; K <= 8, checked at set-up)
         for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
             float o = __fmul_rn(a.gs[t], a.sh[static_cast<size_t>(t) * a.H + i]);
-            for (int k = 0; k < a.K; ++k) {
+            float yk[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                yk[k] = k < a.K ? a.eout[(static_cast<size_t>(t) * a.K + k) * a.H + i] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                if (k >= a.K) break;
                 const float wv = a.wk[t * a.K + k];
                 if (wv == 0.0f) continue;
-                o = __fadd_rn(o, __fmul_rn(wv, a.eout[(static_cast<size_t>(t) * a.K + k) * a.H + i]));
+                o = __fadd_rn(o, __fmul_rn(wv, yk[k]));
             }
             if (a.trace_moe) a.trace_moe[static_cast<size_t>(t) * a.H + i] = o;
             xr[i] = __fadd_rn(xr[i], o);
@@ -596,7 +603,7 @@ constexpr size_t attn_smem_bytes() {
 }
 
 // The chunks joined (engine/src/model.cpp:3832-3853): M = max m_c, O = sum O_c exp(m_c - M), L = sum l_c exp(m_c - M),
-// o = O * (1 / L) * sigmoid(gate); quantized per 16 into the core ActSet. One warp per (token, head).
+// o = O * (1 / L) * sigmoid(gate); quantized per 16 into the core ActSet.
 struct MergeArgs {
     const float *part;
     const float *qg;     // gates: [n][nh][2 hd] second half
@@ -608,71 +615,65 @@ struct MergeArgs {
     float *core_f;       // [n][nh * hd] or NULL
 };
 
+// One CTA per (token, head), one thread per dim (blockDim = hd, a multiple of 32): the chunks' factors in shared
+// memory, then every dim's sum over the chunks with independent loads. Dynamic smem: nchunks floats.
 __global__ void k_attn_merge(MergeArgs a) {
-    __shared__ float s_f[4][64];   // per warp: each chunk's factor exp(m_c - M) (nchunks <= 64 per pass)
+    extern __shared__ float s_f[];
+    __shared__ float s_red[32];
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int pos = *a.pos;
     const int W = a.nh * a.hd;
     const size_t cs = a.hd + 2;
-    for (int item = blockIdx.x * nw + warp; item < a.n * a.nh; item += gridDim.x * nw) {
-        const int t = item / a.nh, h = item % a.nh;
-        const int nc = min(a.nchunks, (pos + t) / kAttnChunk + 1);
-        const float *pp = a.part + (static_cast<size_t>(t) * a.nh + h) * a.nchunks * cs;
-        float M = -INFINITY;
-        for (int c = lane; c < nc; c += 32) M = fmaxf(M, pp[c * cs + a.hd]);
-        M = warp_max(M);
-        float L = 0.0f;
-        for (int c0 = 0; c0 < nc; c0 += 64) {
-            for (int c = c0 + lane; c < min(nc, c0 + 64); c += 32) {
-                const float mc = pp[c * cs + a.hd];
-                const float f = mc == -INFINITY ? 0.0f : __expf(mc - M);
-                s_f[warp][c - c0] = f;
-                L += pp[c * cs + a.hd + 1] * f;
-            }
-            __syncwarp();
-        }
-        L = warp_sum(L);
-        const float inv = 1.0f / L;
-        const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
-        for (int d0 = 0; d0 < a.hd; d0 += 32) {
-            const int d = d0 + lane;
-            float acc = 0.0f;
-            for (int c0 = 0; c0 < nc; c0 += 64) {
-                if (c0 > 0) {   // (more than 64 chunks: the factors of the next 64)
-                    __syncwarp();
-                    for (int c = c0 + lane; c < min(nc, c0 + 64); c += 32) {
-                        const float mc = pp[c * cs + a.hd];
-                        s_f[warp][c - c0] = mc == -INFINITY ? 0.0f : __expf(mc - M);
-                    }
-                    __syncwarp();
-                }
-                for (int c = c0; c < min(nc, c0 + 64); ++c) acc = fmaf(pp[c * cs + d], s_f[warp][c - c0], acc);
-            }
-            if (nc > 64) {   // restore the first 64 factors for the next dims
-                __syncwarp();
-                for (int c = lane; c < min(nc, 64); c += 32) {
-                    const float mc = pp[c * cs + a.hd];
-                    s_f[warp][c] = mc == -INFINITY ? 0.0f : __expf(mc - M);
-                }
-                __syncwarp();
-            }
-            const float v = __fmul_rn(__fmul_rn(acc, inv), sigmoid_cr(gate[d]));
-            const int col = h * a.hd + d;
-            if (a.core_f) a.core_f[static_cast<size_t>(t) * W + col] = v;
-            float amax = fabsf(v);
-            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(v, iv))));
-            int sm = qv;
-            for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-            a.q[static_cast<size_t>(t) * W + col] = static_cast<int8_t>(qv);
-            if ((lane & 15) == 0) {
-                a.scale[static_cast<size_t>(t) * (W / 16) + col / 16] = __fdiv_rn(amax, 127.0f);
-                a.bsum[static_cast<size_t>(t) * (W / 16) + col / 16] = sm;
-            }
-        }
-        __syncwarp();
+    const int t = blockIdx.x / a.nh, h = blockIdx.x % a.nh;
+    const int nc = min(a.nchunks, (pos + t) / kAttnChunk + 1);
+    const float *pp = a.part + (static_cast<size_t>(t) * a.nh + h) * a.nchunks * cs;
+    // M = max m_c
+    float M = -INFINITY;
+    for (int c = tid; c < nc; c += blockDim.x) M = fmaxf(M, pp[c * cs + a.hd]);
+    M = warp_max(M);
+    if (lane == 0) s_red[warp] = M;
+    __syncthreads();
+    M = s_red[0];
+    for (int w = 1; w < nw; ++w) M = fmaxf(M, s_red[w]);
+    __syncthreads();
+    // f_c = exp(m_c - M), L = sum l_c f_c
+    float L = 0.0f;
+    for (int c = tid; c < nc; c += blockDim.x) {
+        const float mc = pp[c * cs + a.hd];
+        const float f = mc == -INFINITY ? 0.0f : __expf(mc - M);
+        s_f[c] = f;
+        L += pp[c * cs + a.hd + 1] * f;
+    }
+    L = warp_sum(L);
+    if (lane == 0) s_red[warp] = L;
+    __syncthreads();
+    L = 0.0f;
+    for (int w = 0; w < nw; ++w) L += s_red[w];
+    const int d = tid;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    int c = 0;
+#pragma unroll 4
+    for (; c + 1 < nc; c += 2) {
+        acc0 = fmaf(pp[c * cs + d], s_f[c], acc0);
+        acc1 = fmaf(pp[(c + 1) * cs + d], s_f[c + 1], acc1);
+    }
+    if (c < nc) acc0 = fmaf(pp[c * cs + d], s_f[c], acc0);
+    const float acc = acc0 + acc1;
+    const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
+    const float v = __fmul_rn(__fmul_rn(acc, 1.0f / L), sigmoid_cr(gate[d]));
+    const int col = h * a.hd + d;
+    if (a.core_f) a.core_f[static_cast<size_t>(t) * W + col] = v;
+    float amax = fabsf(v);
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+    const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(v, iv))));
+    int sm = qv;
+    for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    a.q[static_cast<size_t>(t) * W + col] = static_cast<int8_t>(qv);
+    if ((lane & 15) == 0) {
+        a.scale[static_cast<size_t>(t) * (W / 16) + col / 16] = __fdiv_rn(amax, 127.0f);
+        a.bsum[static_cast<size_t>(t) * (W / 16) + col / 16] = sm;
     }
 }
 

@@ -65,14 +65,8 @@ int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, cons
 }
 
 int gcuda_op_bf16_gemv(const uint16_t *d_w, int rows, int cols, const float *d_x, int n, float *d_y, void *stream) {
-    if (!d_w || rows <= 0 || cols % 8 || n < 1) return GCUDA_E_ARG;
-    if (n > kMaxTok) return GCUDA_E_ARG;
-    const size_t smem = sizeof(float) * static_cast<size_t>(n) * cols;
-    if (smem > 48 * 1024 && cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
-        return GCUDA_E_CUDA;
-    k_bf16_gemv<<<(rows + 31) / 32, 256, smem, static_cast<cudaStream_t>(stream)>>>(d_w, rows, cols, d_x, cols, n, d_y, rows);
-    count_launch();
-    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+    return launch_bf16_gemv(d_w, rows, cols, d_x, cols, n, d_y, rows, device_status(), static_cast<cudaStream_t>(stream),
+                            false);
 }
 
 int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, float *d_weights, void *stream) {

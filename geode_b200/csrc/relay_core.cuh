@@ -67,13 +67,15 @@ __host__ __device__ inline int warp_smem_bytes(int sg_own) {   // sg_own: the ow
 // the whole-K image the CTA shares (act_tstride: token stride of the full image)
 __host__ __device__ inline int act_tstride(int cols) { return (cols / 64) * 64 + ((cols / 64) % 2 == 0 ? 64 : 0); }
 __host__ __device__ inline int act_smem_bytes(int cols) { return (kMaxTok * act_tstride(cols) + (cols / 64) * 4 * 64 + 127) / 128 * 128; }
-// warps per unit: long slices (8 groups) for launches with units for every warp of the GPU several times over, short
-// ones (2 groups: the chain crosses the unit quickly) for latency-bound small matrices; always a divisor of K/64
+// warps per unit: as many as keep every unit of the launch in flight at once on the GPU's sms x kGemvWarps warps (a
+// launch with more units than warps gets one warp per unit: no relay), at most K/128 (two groups per warp: both
+// computed before the hand-off) and 16; always a divisor of K/64
 __host__ __device__ inline int choose_wpu(int cols, int n_units, int sms) {
     const int g = cols / 64;
-    int w = n_units >= 3 * sms ? g / 8 : g / 2;
-    if (w < 1) w = 1;
+    int w = n_units > 0 ? (kGemvWarps * sms) / n_units : 16;
+    if (w > g / 2) w = g / 2;
     if (w > 16) w = 16;
+    if (w < 1) w = 1;
     while (g % w) --w;
     return w;
 }
@@ -87,6 +89,9 @@ struct RelayShape {
     int wpu, nslots, sg;
     size_t smem;
 };
+// per warp on the streaming path: 1 KB of scale pairs, then the warp's own image (own groups, 0 for none)
+__host__ __device__ inline int stream_warp_bytes(int own) { return 1024 + (own ? (warp_act_bytes(own) + 127) / 128 * 128 : 0); }
+
 inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelayShape &r) {
     const int g = cols / 64;
     if (g < 1 || wpu < 1) return false;
@@ -105,73 +110,82 @@ inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelaySh
     return false;
 }
 
-// The warp's activation image for groups [g0, g0 + sg) of up to kMaxTok vectors (sel[t] = the ActSet row of token
-// column t, -1 = zeros): act word (t, gl, tig, j) at t * tstride + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
-// .. + 3); cs per (gl, tig) 64 bytes: cinit(2 tig)[4], cinit(2 tig + 1)[4], then (ascale(2 tig), ascale(2 tig + 1)) per
-// block. cinit = 1.5 * 2^23 - 15 * bsum.
-__device__ inline void stage_slice(const ActSet &a, const int *sel, int g0, int sg, uint8_t *img) {
-    const int lane = threadIdx.x & 31, ts = slice_tstride(sg);
-    const int words = kMaxTok * sg * 16;
-    for (int i = lane; i < words; i += 32) {
-        const int t = i / (sg * 16), w = i % (sg * 16), gl = w / 16, j = (w / 4) % 4, tig = w % 4;
-        const int src = sel[t];
-        uint32_t v = 0;
-        if (src >= 0)
-            v = *reinterpret_cast<const uint32_t *>(a.q + static_cast<size_t>(src) * a.qstride + (g0 + gl) * 64 + 16 * j + 4 * tig);
-        *reinterpret_cast<uint32_t *>(img + t * ts + (gl * 4 + tig) * 16 + 4 * j) = v;
-    }
-    int32_t *cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts);
-    for (int i = lane; i < kMaxTok * sg * 4; i += 32) {
-        const int t = i / (sg * 4), bl = i % (sg * 4), gl = bl / 4, j = bl % 4;
-        const int src = sel[t];
-        const int b = (g0 + gl) * 4 + j;
-        int32_t ci = static_cast<int32_t>(kBiasBits);
-        float sc = 0.0f;
-        if (src >= 0) {
-            ci -= 15 * a.bsum[static_cast<size_t>(src) * a.sstride + b];
-            sc = a.scale[static_cast<size_t>(src) * a.sstride + b];
+// The activation image of groups [g0, g0 + ng) of up to kMaxTok vectors (src(t) = the ActSet row of token column t, -1 =
+// zeros), token stride ts: act word (t, gl, tig, j) at t * ts + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
+// .. + 3); cs per (gl, tig) 64 bytes at kMaxTok * ts + (gl * 4 + tig) * 64: cinit(2 tig)[4], cinit(2 tig + 1)[4], then
+// (ascale(2 tig), ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 15 * bsum. Threads `me` of `nthr` share the work;
+// every thread issues its loads (16 bytes: one block of one token) in batches before it stores.
+template <typename Src>
+__device__ inline void stage_image(const ActSet &a, const Src &src, int g0, int ng, int ts, uint8_t *img, int me, int nthr) {
+    constexpr int kBatch = 4;
+    const int items = kMaxTok * ng * 4;   // (token, block)
+    for (int base = me; base < items; base += nthr * kBatch) {
+        uint4 v[kBatch];
+        int32_t bs[kBatch];
+        float sc[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * nthr;
+            v[u] = make_uint4(0, 0, 0, 0);
+            bs[u] = 0;
+            sc[u] = 0.0f;
+            if (i < items) {
+                const int t = i / (ng * 4), bl = i % (ng * 4), r = src(t);
+                if (r >= 0) {
+                    const size_t b = static_cast<size_t>(g0) * 4 + bl;
+                    v[u] = *reinterpret_cast<const uint4 *>(a.q + static_cast<size_t>(r) * a.qstride + 16 * b);
+                    bs[u] = a.bsum[static_cast<size_t>(r) * a.sstride + b];
+                    sc[u] = a.scale[static_cast<size_t>(r) * a.sstride + b];
+                }
+            }
         }
-        int32_t *base = cs + (gl * 4 + t / 2) * 16;
-        base[(t % 2) * 4 + j] = ci;
-        reinterpret_cast<float *>(base)[8 + 2 * j + (t % 2)] = sc;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            const int i = base + u * nthr;
+            if (i >= items) break;
+            const int t = i / (ng * 4), bl = i % (ng * 4), gl = bl / 4, j = bl % 4;
+            uint8_t *row = img + t * ts + gl * 64 + 4 * j;   // word (t, gl, tig, j) at + tig * 16
+            *reinterpret_cast<uint32_t *>(row) = v[u].x;
+            *reinterpret_cast<uint32_t *>(row + 16) = v[u].y;
+            *reinterpret_cast<uint32_t *>(row + 32) = v[u].z;
+            *reinterpret_cast<uint32_t *>(row + 48) = v[u].w;
+            int32_t *base_cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts) + (gl * 4 + t / 2) * 16;
+            base_cs[(t % 2) * 4 + j] = static_cast<int32_t>(kBiasBits) - 15 * bs[u];
+            reinterpret_cast<float *>(base_cs)[8 + 2 * j + (t % 2)] = sc[u];
+        }
     }
 }
 
-// The CTA's image of all K for the first ncols vectors of an ActSet (zeros for the columns after them, up to kMaxTok),
-// the same layout as a slice image with groups g = 0 .. K/64-1 and token stride act_tstride(K). Every thread of the CTA.
+// a warp's own image of its K-slice (sel[t]: the ActSet row of column t, -1 = zeros)
+__device__ inline void stage_slice(const ActSet &a, const int *sel, int g0, int sg, uint8_t *img) {
+    stage_image(a, [&](int t) { return sel[t]; }, g0, sg, slice_tstride(sg), img, threadIdx.x & 31, 32);
+}
+
+// The CTA's image of all K for the first ncols vectors (zeros after them), token stride act_tstride(K). Every thread.
 __device__ inline void stage_full(const ActSet &a, int ncols, uint8_t *img) {
-    const int cols = a.cols, ts = act_tstride(cols), nb = cols / 16, wpr = cols / 4;
-    for (int i = threadIdx.x; i < kMaxTok * wpr; i += blockDim.x) {
-        const int t = i / wpr, w = i % wpr;
-        const int b = w / 4, tig = w % 4, g = b / 4, j = b % 4;
-        uint32_t v = 0;
-        if (t < ncols) v = *reinterpret_cast<const uint32_t *>(a.q + static_cast<size_t>(t) * a.qstride + 4 * w);
-        *reinterpret_cast<uint32_t *>(img + t * ts + (g * 4 + tig) * 16 + j * 4) = v;
-    }
-    int32_t *cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts);
-    for (int i = threadIdx.x; i < nb * kMaxTok; i += blockDim.x) {
-        const int b = i / kMaxTok, t = i % kMaxTok, g = b / 4, j = b % 4;
-        int32_t ci = static_cast<int32_t>(kBiasBits);
-        float sc = 0.0f;
-        if (t < ncols) {
-            ci -= 15 * a.bsum[static_cast<size_t>(t) * a.sstride + b];
-            sc = a.scale[static_cast<size_t>(t) * a.sstride + b];
-        }
-        int32_t *base = cs + (g * 4 + t / 2) * 16;
-        base[(t % 2) * 4 + j] = ci;
-        reinterpret_cast<float *>(base)[8 + 2 * j + (t % 2)] = sc;
+    stage_image(a, [&](int t) { return t < ncols ? t : -1; }, 0, a.cols / 64, act_tstride(a.cols), img,
+                static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x));
+}
+
+// A group's scale word of (tile lane >> 4, row lane & 15) - the row's four blocks - to (e, e) float pairs in e4p, the
+// layout group_products reads: [tile][block][gid][e(gid), e(gid), e(gid + 8), e(gid + 8)].
+__device__ __forceinline__ void decode_scales(uint32_t word, int lane, float *e4p) {
+    const int tile = lane >> 4, w = lane & 15;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float e = e4m3_alu((word >> (8 * j)) & 0xFFu);
+        *reinterpret_cast<float2 *>(e4p + ((tile * 4 + j) * 8 + (w & 7)) * 4 + (w >> 3) * 2) = make_float2(e, e);
     }
 }
 
 // One group of both tiles: for block j = 0..3 the products p[0..3] = tile A (row gid: the token pair (2 tig,
 // 2 tig + 1), row gid + 8: the pair), tile B likewise, handed to sink(j, p) in block order.
 // e4p: the group's scales as [tile][block][gid][e(gid), e(gid), e(gid+8), e(gid+8)] floats.
+// wa / wb: the lane's 16 code bytes of tiles A and B.
 template <typename Sink>
-__device__ __forceinline__ void group_products(const uint8_t *stage, const float *e4p, const uint8_t *act, const uint8_t *cs,
-                                               int lane, uint64_t zero, const Sink &sink) {
+__device__ __forceinline__ void group_products(const uint4 wa, const uint4 wb, const float *e4p, const uint8_t *act,
+                                               const uint8_t *cs, int lane, uint64_t zero, const Sink &sink) {
     const int gid = lane >> 2;
-    const uint4 wa = ld_shared_v4(stage + lane * 16);
-    const uint4 wb = ld_shared_v4(stage + kGroupBytes + lane * 16);
     const uint4 av = ld_shared_v4(act);
     const uint4 ci0 = ld_shared_v4(cs);
     const uint4 ci1 = ld_shared_v4(cs + 16);
@@ -278,17 +292,12 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
             const int s = consumed % kRelayStages;
             if (!mbar_wait_bounded(&c.bar[s], (consumed / kRelayStages) & 1, status)) return false;
             const uint8_t *st = c.ring + s * kStageBytesR;
-            {   // 2 tiles x 64 scale bytes (row w's four blocks in a word): one word per lane, to (e, e) pairs
-                const int tile = lane >> 4, w = lane & 15;
-                const uint32_t word = *reinterpret_cast<const uint32_t *>(st + tile * kGroupBytes + 512 + 4 * w);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float e = e4m3_alu((word >> (8 * j)) & 0xFFu);
-                    *reinterpret_cast<float2 *>(c.e4p + ((tile * 4 + j) * 8 + (w & 7)) * 4 + (w >> 3) * 2) = make_float2(e, e);
-                }
-            }
+            // 2 tiles x 64 scale bytes (row w's four blocks in a word): one word per lane, to (e, e) pairs
+            decode_scales(*reinterpret_cast<const uint32_t *>(st + (lane >> 4) * kGroupBytes + 512 + 4 * (lane & 15)), lane,
+                          c.e4p);
             __syncwarp();
-            group_products(st, c.e4p, act + gl * 64, cs + gl * 256, lane, c.zero, sink);
+            group_products(ld_shared_v4(st + lane * 16), ld_shared_v4(st + kGroupBytes + lane * 16), c.e4p, act + gl * 64,
+                           cs + gl * 256, lane, c.zero, sink);
             ++consumed;
             __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
             issue();
@@ -349,6 +358,130 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
     // copies still in flight after a failed wait: waited for (bounded) before the shared memory is released
     for (; !ok && consumed < issued; ++consumed) mbar_wait_bounded(&c.bar[consumed % kRelayStages], (consumed / kRelayStages) & 1, nullptr);
     return ok;
+}
+
+// A launch's shape for either path: one warp per unit streams (every warp of the CTA a slot), else the relay.
+inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, RelayShape &r) {
+    if (wpu == 1) {
+        const int g = cols / 64;
+        const size_t sm = front + static_cast<size_t>(kGemvWarps) * stream_warp_bytes(own_images ? g : 0);
+        if (g >= 1 && sm <= static_cast<size_t>(kMaxDynSmem)) {
+            r = RelayShape{1, kGemvWarps, g, sm};
+            return true;
+        }
+    }
+    return plan_relay(cols, wpu, own_images, front, r);
+}
+
+// ------------------------------------------------------------------------------------------- streaming ----
+// The path for launches with a warp per unit (wpu = 1, no relay): the warp reads its units' weights straight into
+// registers with coalesced 16-byte loads (a group: the lane's 16 code bytes of both tiles and one scale word), kStreamDepth
+// groups ahead of the one it multiplies, and adds every product into the chain as it comes. No shared-memory ring, no
+// waits: the loads complete like any other.
+constexpr int kStreamDepth = 4;
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const uint8_t *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream_u32(const uint8_t *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+struct StreamCtx {
+    float *e4p;           // this warp's 1 KB of (e, e) pairs
+    const uint8_t *img;   // the activation image (token stride img_ts), groups from 0
+    int img_ts;
+    int ngroups;          // K / 64
+    uint64_t zero;        // a +0 pair from runtime values (f2_mul_sep)
+};
+
+// get(i, U): the warp's i-th unit (false past the end); restage(U) (every lane) before a unit's first group; epi(U, y0,
+// y1, gid, tig) after its last. `early`: the first loads go out before prelude() (weights do not depend on the previous
+// kernel).
+template <typename GetUnit, typename Restage, typename Epi, typename Prelude>
+__device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Restage &restage, const Epi &epi, bool early,
+                             const Prelude &prelude) {
+    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int G = c.ngroups;
+    // producer cursor
+    int pu = 0, pg = 0;
+    const uint8_t *pw0 = nullptr, *pw1 = nullptr;
+    bool p_ok;
+    {
+        GemvUnit T;
+        p_ok = get(0, T);
+        pw0 = T.w0;
+        pw1 = T.w1;
+    }
+    uint4 ra[kStreamDepth], rb[kStreamDepth];
+    uint32_t rs[kStreamDepth];
+    auto load = [&](int k) {
+        if (!p_ok) return;
+        const size_t off = static_cast<size_t>(pg) * kGroupBytes;
+        ra[k] = ldg_stream_v4(pw0 + off + lane * 16);
+        rb[k] = ldg_stream_v4(pw1 + off + lane * 16);
+        rs[k] = ldg_stream_u32((lane < 16 ? pw0 : pw1) + off + 512 + 4 * (lane & 15));
+        if (++pg == G) {
+            pg = 0;
+            GemvUnit T;
+            p_ok = get(++pu, T);
+            pw0 = T.w0;
+            pw1 = T.w1;
+        }
+    };
+    if (!early) prelude();
+#pragma unroll
+    for (int k = 0; k < kStreamDepth; ++k) load(k);
+    if (early) prelude();
+    // consumer cursor
+    int cu = 0, cg = 0;
+    bool c_ok;
+    {
+        GemvUnit U;
+        c_ok = get(0, U);
+        if (c_ok) restage(U);
+    }
+    uint64_t acc[4] = {0, 0, 0, 0};
+    auto chain = [&](int, const uint64_t (&p)[4]) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[q]);
+    };
+    const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
+    const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * 64;
+    while (c_ok) {
+#pragma unroll
+        for (int k = 0; k < kStreamDepth; ++k) {
+            if (c_ok) {
+                decode_scales(rs[k], lane, c.e4p);
+                __syncwarp();
+                group_products(ra[k], rb[k], c.e4p, act0 + cg * 64, cs0 + cg * 256, lane, c.zero, chain);
+                __syncwarp();   // every lane done with the scale pairs before the next group's
+                load(k);
+                if (++cg == G) {
+                    // y = acc * global * 1 (engine/src/kernels.cpp:1320)
+                    GemvUnit U;
+                    get(cu, U);
+                    float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
+                    float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        y0[i] = __fmul_rn(y0[i], U.g0);
+                        y1[i] = __fmul_rn(y1[i], U.g1);
+                    }
+                    epi(U, y0, y1, gid, tig);
+                    acc[0] = acc[1] = acc[2] = acc[3] = 0;
+                    cg = 0;
+                    c_ok = get(++cu, U);
+                    if (c_ok) restage(U);
+                }
+            }
+        }
+    }
 }
 
 // The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu. smem_warps: the warps'

@@ -24,37 +24,85 @@ __device__ __forceinline__ void bf16_dot8(const uint16_t *__restrict__ w, const 
     out = a;
 }
 
-// 32 rows per CTA, 8 lanes (j) per row; every lane carries all n tokens' partial sums (the row's bf16 is read once
-// for them), x staged in shared memory. Bits as bf16_dot8's. Dynamic smem: n * cols floats.
-__global__ void __launch_bounds__(256) k_bf16_gemv(const uint16_t *__restrict__ w, int rows, int cols,
-                                                   const float *__restrict__ x, int xstride, int n, float *__restrict__ y,
-                                                   int ystride) {
-    extern __shared__ float xs[];
+// kBf16Rows rows per CTA, one warp per row: lane (j = lane & 7, tg = lane >> 3) carries partial sum j of tokens tg and
+// tg + 4. The CTA's rows (contiguous) arrive by one bulk copy issued before the wait for the previous kernel (weights do
+// not depend on it); x is staged after it, token rows padded by 8 floats (the four tg lanes hit different banks).
+// Bits as bf16_dot8's. w 16-byte aligned, cols % 8 == 0. Dynamic smem: bf16_gemv_smem(cols, n).
+constexpr int kBf16Rows = 8;
+__host__ __device__ inline size_t bf16_gemv_smem(int cols, int n) {
+    return 16 + static_cast<size_t>(kBf16Rows) * cols * 2 + static_cast<size_t>(n) * (cols + 8) * 4;
+}
+
+__global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__restrict__ w, int rows, int cols,
+                                                               const float *__restrict__ x, int xstride, int n,
+                                                               float *__restrict__ y, int ystride, uint32_t *status) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    uint64_t *bar = reinterpret_cast<uint64_t *>(sm);
+    uint16_t *ws = reinterpret_cast<uint16_t *>(sm + 16);
+    float *xs = reinterpret_cast<float *>(sm + 16 + static_cast<size_t>(kBf16Rows) * cols * 2);
+    const int r0 = blockIdx.x * kBf16Rows, nr = min(kBf16Rows, rows - r0);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_barrier_init();
+        const uint32_t bytes = static_cast<uint32_t>(nr) * cols * 2;
+        mbar_expect_tx(bar, bytes);
+        bulk_g2s(ws, w + static_cast<size_t>(r0) * cols, bytes, bar);
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int i = threadIdx.x; i < n * cols; i += blockDim.x) xs[i] = x[static_cast<size_t>(i / cols) * xstride + i % cols];
+    const int xs_stride = cols + 8;
+    {   // (loads issued in batches before their stores: one round trip per batch, not per load)
+        constexpr int kB = 8;
+        const int items = n * (cols / 4);
+        for (int base = threadIdx.x; base < items; base += blockDim.x * kB) {
+            float4 v[kB];
+#pragma unroll
+            for (int u = 0; u < kB; ++u) {
+                const int i = base + u * blockDim.x;
+                if (i < items)
+                    v[u] = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(i / (cols / 4)) * xstride + 4 * (i % (cols / 4)));
+            }
+#pragma unroll
+            for (int u = 0; u < kB; ++u) {
+                const int i = base + u * blockDim.x;
+                if (i < items) *reinterpret_cast<float4 *>(xs + (i / (cols / 4)) * xs_stride + 4 * (i % (cols / 4))) = v[u];
+            }
+        }
+    }
     __syncthreads();
-    const int j = threadIdx.x & 7, r = blockIdx.x * 32 + (threadIdx.x >> 3);
-    const bool live = r < rows;
-    const uint16_t *wr = w + static_cast<size_t>(live ? r : 0) * cols;
-    float a[kMaxTok];
-#pragma unroll
-    for (int t = 0; t < kMaxTok; ++t) a[t] = 0.0f;
-#pragma unroll 4
-    for (int c = j; c < cols; c += 8) {
-        const float wf = __uint_as_float(static_cast<uint32_t>(wr[c]) << 16);
-#pragma unroll
-        for (int t = 0; t < kMaxTok; ++t)
-            if (t < n) a[t] = __fadd_rn(a[t], __fmul_rn(wf, xs[t * cols + c]));
+    const bool landed = mbar_wait_bounded(bar, 0, status);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, tg = lane >> 3;
+    if (landed && warp < nr) {
+        const uint16_t *wr = ws + static_cast<size_t>(warp) * cols;
+        const float *x0 = xs + tg * xs_stride, *x1 = xs + (tg + 4) * xs_stride;
+        float a0 = 0.0f, a1 = 0.0f;
+        if (tg + 4 < n) {
+#pragma unroll 8
+            for (int c = j; c < cols; c += 8) {
+                const float wf = __uint_as_float(static_cast<uint32_t>(wr[c]) << 16);
+                a0 = __fadd_rn(a0, __fmul_rn(wf, x0[c]));
+                a1 = __fadd_rn(a1, __fmul_rn(wf, x1[c]));
+            }
+        } else if (tg < n) {
+#pragma unroll 8
+            for (int c = j; c < cols; c += 8) {
+                const float wf = __uint_as_float(static_cast<uint32_t>(wr[c]) << 16);
+                a0 = __fadd_rn(a0, __fmul_rn(wf, x0[c]));
+            }
+        }
+        // (a lane group of 8 shares tg: the shuffles below stay inside it)
+        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 4));   // j < 4: a_j + a_{j+4}
+        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));   // (a0+a4)+(a1+a5), (a2+a6)+(a3+a7)
+        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 4));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+        if (j == 0) {
+            if (tg < n) y[static_cast<size_t>(tg) * ystride + r0 + warp] = a0;
+            if (tg + 4 < n) y[static_cast<size_t>(tg + 4) * ystride + r0 + warp] = a1;
+        }
     }
-#pragma unroll
-    for (int t = 0; t < kMaxTok; ++t) {
-        if (t >= n) break;
-        float v = a[t];
-        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));   // j < 4: a_j + a_{j+4}
-        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));   // (a0+a4)+(a1+a5), (a2+a6)+(a3+a7)
-        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
-        if (live && j == 0) y[static_cast<size_t>(t) * ystride + r] = v;
-    }
+    if (!landed) mbar_wait_bounded(bar, 0, nullptr);   // (the copy may still land: not before the CTA ends)
+    asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // route_topk (engine/src/model.cpp:4021-4065) for one token row, by one warp: softmax (max, exp, a float sum in
