@@ -410,10 +410,12 @@ int enqueue_step(gcuda *g, int n) {
                 ea.pass = pass;
                 ea.wpu = r.wpu;
                 ea.nslots = r.nslots;
-                if (r.wpu == 1)
-                    LAUNCH_OK(launch_ex(k_gemv_experts<true>, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
+                if (r.stages == kWideStages)
+                    LAUNCH_OK(launch_ex(k_gemv_experts<kWideStages>, dim3(sm_count()), dim3(kStreamWarps * 32), r.smem, g->st, pdl, ea));
+                else if (r.stages == kDeepStages)
+                    LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kStreamWarps * 32), r.smem, g->st, pdl, ea));
                 else
-                    LAUNCH_OK(launch_ex(k_gemv_experts<false>, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
+                    LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
             }
             RC_OK(norm(next_norm, true, next_hf));
         }

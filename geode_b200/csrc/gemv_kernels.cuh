@@ -126,12 +126,13 @@ struct StaticGemv {
 };
 
 inline bool plan_static(int cols, int n_units, int sms, RelayShape &r) {
-    return plan_gemv(cols, choose_wpu(cols, n_units, sms), false, static_cast<size_t>(act_smem_bytes(cols)), r);
+    return plan_gemv(cols, choose_wpu(cols, n_units, sms), false, static_cast<size_t>(act_smem_bytes(cols)),
+                     (n_units + sms - 1) / sms, r);
 }
 
-// kStream: the launch shape has one warp per unit (stream_units), else the relay (relay_units)
-template <bool kStream>
-__global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p) {
+// kStages: the streaming path's ring depth (the launch shape has one warp per unit, stream_units), 0: the relay
+template <int kStages>
+__global__ void __launch_bounds__((kStages ? kStreamWarps : kGemvWarps) * 32, 1) k_gemv_static(StaticGemv p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
     const int cols = p.act.cols, wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
@@ -174,14 +175,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_static(StaticGemv p
     auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
         epi_store(U, y0, y1, gid, tig);
     };
-    if constexpr (kStream) {
+    if constexpr (kStages > 0) {
         StreamCtx c;
-        c.e4p = reinterpret_cast<float *>(smem + act_smem_bytes(cols) + static_cast<size_t>(warp) * stream_warp_bytes(0));
+        uint8_t *wbase = smem + act_smem_bytes(cols) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, 0);
+        c.e4p = reinterpret_cast<float *>(wbase);
+        c.ring = wbase + 1024;
         c.img = img;
         c.img_ts = act_tstride(cols);
         c.ngroups = cols / 64;
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
-        stream_units(get, c, [](const GemvUnit &) {}, epi, true, prelude);
+        stream_units<kStages>(get, c, [](const GemvUnit &) {}, epi, true, prelude);
     } else {
         RelayCtx c = make_ctx(smem + act_smem_bytes(cols), wpu, sg, 0, img, act_tstride(cols));
         relay_units(get, c, [](const GemvUnit &) {}, p.status, epi, true, prelude);
@@ -225,14 +228,17 @@ struct ExpertsArgs {
 // units: the expected count (the union is known on the device only): n*K picks at most, E experts at most.
 inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, RelayShape &r) {
     const int picks = n * K < E ? n * K : E;
-    if (pass == kGateUp)
-        return plan_gemv(H, choose_wpu(H, picks * (ff / 16) + sff / 16, sms), false,
-                         static_cast<size_t>(act_smem_bytes(H)), r);
-    return plan_gemv(ff, choose_wpu(ff, (picks + 1) * (H / 32), sms), true, 0, r);
+    if (pass == kGateUp) {
+        const int units = picks * (ff / 16) + sff / 16;
+        return plan_gemv(H, choose_wpu(H, units, sms), false, static_cast<size_t>(act_smem_bytes(H)),
+                         (units + sms - 1) / sms, r);
+    }
+    const int units = (picks + 1) * (H / 32);
+    return plan_gemv(ff, choose_wpu(ff, units, sms), true, 0, (units + sms - 1) / sms, r);
 }
 
-template <bool kStream>
-__global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs p) {
+template <int kStages>
+__global__ void __launch_bounds__((kStages ? kStreamWarps : kGemvWarps) * 32, 1) k_gemv_experts(ExpertsArgs p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
     const bool gu = p.pass == kGateUp;
@@ -347,17 +353,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 1) k_gemv_experts(ExpertsArgs
     auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
         epi_store(U, y0, y1, gid, tig);
     };
-    if constexpr (kStream) {
-        // per warp: 1 KB of scale pairs, then (down) the warp's own image of all K
-        uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(gu ? 0 : sg);
+    if constexpr (kStages > 0) {
+        // per warp: 1 KB of scale pairs, the ring, then (down) the warp's own image of all K
+        uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, gu ? 0 : sg);
+        uint8_t *own_img = wbase + 1024 + kStages * kStageBytesR;
         StreamCtx c;
         c.e4p = reinterpret_cast<float *>(wbase);
-        c.img = gu ? img : wbase + 1024;
+        c.ring = wbase + 1024;
+        c.img = gu ? img : own_img;
         c.img_ts = gu ? act_tstride(p.H) : slice_tstride(sg);
         c.ngroups = cols / 64;
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
-        own = gu ? nullptr : wbase + 1024;
-        stream_units(get, c, restage, epi, false, prelude);
+        own = gu ? nullptr : own_img;
+        stream_units<kStages>(get, c, restage, epi, false, prelude);
     } else {
         RelayCtx c = gu ? make_ctx(smem + act_smem_bytes(p.H), wpu, sg, 0, img, act_tstride(p.H))
                         : make_ctx(smem, wpu, sg, sg, nullptr, 0);

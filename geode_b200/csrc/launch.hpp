@@ -67,10 +67,12 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
 inline int gemv_opt_in() {
     static const int rc = [] {
         const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-        if (cudaFuncSetAttribute(k_gemv_static<true>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_static<false>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<true>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<false>, a, kMaxDynSmem) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemv_static<0>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_static<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_static<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts<0>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) != cudaSuccess)
             return static_cast<int>(GCUDA_E_CUDA);
         return static_cast<int>(GCUDA_OK);
     }();
@@ -85,8 +87,13 @@ inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     p.wpu = r.wpu;
     p.nslots = r.nslots;
     const int grid = std::max(1, std::min(sm_count(), (p.n_units + r.nslots - 1) / r.nslots));
-    const cudaError_t e = r.wpu == 1 ? launch_ex(k_gemv_static<true>, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p)
-                                     : launch_ex(k_gemv_static<false>, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p);
+    cudaError_t e;
+    if (r.stages == kWideStages)
+        e = launch_ex(k_gemv_static<kWideStages>, dim3(grid), dim3(kStreamWarps * 32), r.smem, st, pdl, p);
+    else if (r.stages == kDeepStages)
+        e = launch_ex(k_gemv_static<kDeepStages>, dim3(grid), dim3(kStreamWarps * 32), r.smem, st, pdl, p);
+    else
+        e = launch_ex(k_gemv_static<0>, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p);
     return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }
 

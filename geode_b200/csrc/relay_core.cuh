@@ -55,8 +55,10 @@ __device__ __forceinline__ float e4m3_alu(uint32_t b) {
 // Shared memory per warp: the ring, its barriers, one group's scales as (e, e) float pairs, the relay mailbox
 // (2 parities x 32 lanes x 4 float pairs) and, for launches whose units multiply different activations, the warp's own
 // activation image of its K-slice (else the CTA shares one image of all K).
+// an image's per-(group, tig) entry of accumulator inits and activation scales (kCsEntry bytes, below)
+constexpr int kCsEntry = 96;
 __host__ __device__ inline int slice_tstride(int sg) { return sg * 64 + (sg % 2 == 0 ? 64 : 0); }
-__host__ __device__ inline int warp_act_bytes(int sg) { return kMaxTok * slice_tstride(sg) + sg * 4 * 64; }
+__host__ __device__ inline int warp_act_bytes(int sg) { return kMaxTok * slice_tstride(sg) + sg * 4 * kCsEntry; }
 __host__ __device__ inline int warp_base_bytes() {
     return kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8 + 2 * 32 * 32;
 }
@@ -66,7 +68,7 @@ __host__ __device__ inline int warp_smem_bytes(int sg_own) {   // sg_own: the ow
 }
 // the whole-K image the CTA shares (act_tstride: token stride of the full image)
 __host__ __device__ inline int act_tstride(int cols) { return (cols / 64) * 64 + ((cols / 64) % 2 == 0 ? 64 : 0); }
-__host__ __device__ inline int act_smem_bytes(int cols) { return (kMaxTok * act_tstride(cols) + (cols / 64) * 4 * 64 + 127) / 128 * 128; }
+__host__ __device__ inline int act_smem_bytes(int cols) { return (kMaxTok * act_tstride(cols) + (cols / 64) * 4 * kCsEntry + 127) / 128 * 128; }
 // warps per unit: as many as keep every unit of the launch in flight at once on the GPU's sms x kGemvWarps warps (a
 // launch with more units than warps gets one warp per unit: no relay), at most K/128 (two groups per warp: both
 // computed before the hand-off) and 16; always a divisor of K/64
@@ -88,10 +90,8 @@ constexpr int kMaxDynSmem = 227 * 1024;
 struct RelayShape {
     int wpu, nslots, sg;
     size_t smem;
+    int stages = 0;   // the streaming path's ring depth (0: the relay)
 };
-// per warp on the streaming path: 1 KB of scale pairs, then the warp's own image (own groups, 0 for none)
-__host__ __device__ inline int stream_warp_bytes(int own) { return 1024 + (own ? (warp_act_bytes(own) + 127) / 128 * 128 : 0); }
-
 inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelayShape &r) {
     const int g = cols / 64;
     if (g < 1 || wpu < 1) return false;
@@ -102,7 +102,7 @@ inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelaySh
         for (int ns = kGemvWarps / wpu; ns >= 1; --ns) {
             const size_t sm = front + static_cast<size_t>(ns * wpu) * wb;
             if (sm <= static_cast<size_t>(kMaxDynSmem)) {
-                r = RelayShape{wpu, ns, sg, sm};
+                r = RelayShape{wpu, ns, sg, sm, 0};
                 return true;
             }
         }
@@ -112,9 +112,10 @@ inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelaySh
 
 // The activation image of groups [g0, g0 + ng) of up to kMaxTok vectors (src(t) = the ActSet row of token column t, -1 =
 // zeros), token stride ts: act word (t, gl, tig, j) at t * ts + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
-// .. + 3); cs per (gl, tig) 64 bytes at kMaxTok * ts + (gl * 4 + tig) * 64: cinit(2 tig)[4], cinit(2 tig + 1)[4], then
-// (ascale(2 tig), ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 15 * bsum. Threads `me` of `nthr` share the work;
-// every thread issues its loads (16 bytes: one block of one token) in batches before it stores.
+// .. + 3); cs per (gl, tig) kCsEntry bytes at kMaxTok * ts + (gl * 4 + tig) * kCsEntry: for each block j the mma's
+// accumulator quad (cinit(2 tig), cinit(2 tig + 1), cinit(2 tig), cinit(2 tig + 1)), then (ascale(2 tig),
+// ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 15 * bsum. Threads `me` of `nthr` share the work; every thread
+// issues its loads (16 bytes: one block of one token) in batches before it stores.
 template <typename Src>
 __device__ inline void stage_image(const ActSet &a, const Src &src, int g0, int ng, int ts, uint8_t *img, int me, int nthr) {
     constexpr int kBatch = 4;
@@ -149,9 +150,11 @@ __device__ inline void stage_image(const ActSet &a, const Src &src, int g0, int 
             *reinterpret_cast<uint32_t *>(row + 16) = v[u].y;
             *reinterpret_cast<uint32_t *>(row + 32) = v[u].z;
             *reinterpret_cast<uint32_t *>(row + 48) = v[u].w;
-            int32_t *base_cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts) + (gl * 4 + t / 2) * 16;
-            base_cs[(t % 2) * 4 + j] = static_cast<int32_t>(kBiasBits) - 15 * bs[u];
-            reinterpret_cast<float *>(base_cs)[8 + 2 * j + (t % 2)] = sc[u];
+            int32_t *base_cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts + (gl * 4 + t / 2) * kCsEntry);
+            const int32_t ci = static_cast<int32_t>(kBiasBits) - 15 * bs[u];
+            base_cs[4 * j + (t % 2)] = ci;
+            base_cs[4 * j + (t % 2) + 2] = ci;
+            reinterpret_cast<float *>(base_cs)[16 + 2 * j + (t % 2)] = sc[u];
         }
     }
 }
@@ -187,20 +190,18 @@ __device__ __forceinline__ void group_products(const uint4 wa, const uint4 wb, c
                                                const uint8_t *cs, int lane, uint64_t zero, const Sink &sink) {
     const int gid = lane >> 2;
     const uint4 av = ld_shared_v4(act);
-    const uint4 ci0 = ld_shared_v4(cs);
-    const uint4 ci1 = ld_shared_v4(cs + 16);
-    const uint4 s01 = ld_shared_v4(cs + 32);   // (as0, as1) for blocks 0, 1
-    const uint4 s23 = ld_shared_v4(cs + 48);   // blocks 2, 3
+    const uint4 s01 = ld_shared_v4(cs + 64);   // (as0, as1) for blocks 0, 1
+    const uint4 s23 = ld_shared_v4(cs + 80);   // blocks 2, 3
     const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w}, wB[4] = {wb.x, wb.y, wb.z, wb.w};
     const uint32_t bv[4] = {av.x, av.y, av.z, av.w};
-    const int32_t c0[4] = {static_cast<int32_t>(ci0.x), static_cast<int32_t>(ci0.y), static_cast<int32_t>(ci0.z), static_cast<int32_t>(ci0.w)};
-    const int32_t c1[4] = {static_cast<int32_t>(ci1.x), static_cast<int32_t>(ci1.y), static_cast<int32_t>(ci1.z), static_cast<int32_t>(ci1.w)};
     const uint64_t sp[4] = {pack2(s01.x, s01.y), pack2(s01.z, s01.w), pack2(s23.x, s23.y), pack2(s23.z, s23.w)};
     const uint64_t bias2 = pack2(__float_as_uint(kBiasF), __float_as_uint(kBiasF));
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         int32_t dA[4], dB[4];
-        const int32_t cinit[4] = {c0[j], c1[j], c0[j], c1[j]};
+        const uint4 cq = ld_shared_v4(cs + 16 * j);   // the block's accumulator quad
+        const int32_t cinit[4] = {static_cast<int32_t>(cq.x), static_cast<int32_t>(cq.y), static_cast<int32_t>(cq.z),
+                                  static_cast<int32_t>(cq.w)};
         mma_s8_16816(dA, (wA[j] << 1) & 0x1E1E1E1Eu, (wA[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
         mma_s8_16816(dB, (wB[j] << 1) & 0x1E1E1E1Eu, (wB[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
         const uint4 eA = ld_shared_v4(e4p + ((0 * 4 + j) * 8 + gid) * 4);
@@ -285,7 +286,7 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
         }
         const int ts = c.img_ts;
         const uint8_t *act = c.img + gid * ts + tig * 16 + c.g_off * 64;
-        const uint8_t *cs = c.img + kMaxTok * ts + tig * 64 + c.g_off * 256;
+        const uint8_t *cs = c.img + kMaxTok * ts + tig * kCsEntry + c.g_off * 4 * kCsEntry;
         // one group: wait, the scales to (e, e) pairs, the products into sink(j, p[4])
         auto group = [&](int gl, const auto &sink) -> bool {
             if (!ok) return false;   // (after a wait gave up: no more waits; the chain still runs, the status says why)
@@ -297,7 +298,7 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
                           c.e4p);
             __syncwarp();
             group_products(ld_shared_v4(st + lane * 16), ld_shared_v4(st + kGroupBytes + lane * 16), c.e4p, act + gl * 64,
-                           cs + gl * 256, lane, c.zero, sink);
+                           cs + gl * 4 * kCsEntry, lane, c.zero, sink);
             ++consumed;
             __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
             issue();
@@ -360,40 +361,48 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
     return ok;
 }
 
-// A launch's shape for either path: one warp per unit streams (every warp of the CTA a slot), else the relay.
-inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, RelayShape &r) {
+// ------------------------------------------------------------------------------------------- streaming ----
+// The path for launches with a warp per unit (wpu = 1, no relay): each warp (up to kStreamWarps) copies its units'
+// groups (both tiles' 576 bytes) into its own ring of shared-memory stages with 16-byte cp.async copies, the
+// stages ahead of the one it multiplies in flight, and adds every product into the chain as it comes. The copies hold
+// no registers (so the CTA runs more warps) and their waits (cp.async.wait_group) always end: the copies land like
+// any load.
+constexpr int kStreamWarps = 24;
+// ring depths: kDeepStages for launches with few units per SM (fewer warps, each with more copies in flight)
+constexpr int kWideStages = 6, kDeepStages = 12;
+
+// per warp: 1 KB of scale pairs, the ring, then the warp's own image (own groups, 0 for none)
+__host__ __device__ inline int stream_warp_bytes(int stages, int own) {
+    return 1024 + stages * kStageBytesR + (own ? (warp_act_bytes(own) + 127) / 128 * 128 : 0);
+}
+
+// A launch's shape for either path: one warp per unit streams, else the relay. units_per_cta: the units a CTA takes
+// (all CTAs take the same share, +-1).
+inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, int units_per_cta, RelayShape &r) {
     if (wpu == 1) {
         const int g = cols / 64;
-        const size_t sm = front + static_cast<size_t>(kGemvWarps) * stream_warp_bytes(own_images ? g : 0);
-        if (g >= 1 && sm <= static_cast<size_t>(kMaxDynSmem)) {
-            r = RelayShape{1, kGemvWarps, g, sm};
+        const int stages = units_per_cta >= kStreamWarps ? kWideStages : kDeepStages;
+        const size_t wb = static_cast<size_t>(stream_warp_bytes(stages, own_images ? g : 0));
+        int ns = units_per_cta < kStreamWarps ? (units_per_cta > 0 ? units_per_cta : 1) : kStreamWarps;
+        while (ns >= 1 && front + ns * wb > static_cast<size_t>(kMaxDynSmem)) --ns;
+        if (g >= 1 && ns >= 1) {
+            r = RelayShape{1, ns, g, front + ns * wb, stages};
             return true;
         }
     }
     return plan_relay(cols, wpu, own_images, front, r);
 }
 
-// ------------------------------------------------------------------------------------------- streaming ----
-// The path for launches with a warp per unit (wpu = 1, no relay): the warp reads its units' weights straight into
-// registers with coalesced 16-byte loads (a group: the lane's 16 code bytes of both tiles and one scale word), kStreamDepth
-// groups ahead of the one it multiplies, and adds every product into the chain as it comes. No shared-memory ring, no
-// waits: the loads complete like any other.
-constexpr int kStreamDepth = 4;
-
-__device__ __forceinline__ uint4 ldg_stream_v4(const uint8_t *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
-    return v;
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
-__device__ __forceinline__ uint32_t ldg_stream_u32(const uint8_t *p) {
-    uint32_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
-}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 struct StreamCtx {
     float *e4p;           // this warp's 1 KB of (e, e) pairs
+    uint8_t *ring;        // this warp's ring of stages of kStageBytesR
     const uint8_t *img;   // the activation image (token stride img_ts), groups from 0
     int img_ts;
     int ngroups;          // K / 64
@@ -401,15 +410,16 @@ struct StreamCtx {
 };
 
 // get(i, U): the warp's i-th unit (false past the end); restage(U) (every lane) before a unit's first group; epi(U, y0,
-// y1, gid, tig) after its last. `early`: the first loads go out before prelude() (weights do not depend on the previous
-// kernel).
-template <typename GetUnit, typename Restage, typename Epi, typename Prelude>
+// y1, gid, tig) after its last. `early`: the first copies go out before prelude() (weights do not depend on the
+// previous kernel).
+template <int kStreamStages, typename GetUnit, typename Restage, typename Epi, typename Prelude>
 __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Restage &restage, const Epi &epi, bool early,
                              const Prelude &prelude) {
     const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
     const int G = c.ngroups;
-    // producer cursor
-    int pu = 0, pg = 0;
+    // producer cursor: every issue() commits one copy group (empty past the end), so at the consumption of item i
+    // exactly kStreamStages - 1 groups were committed after i's
+    int pu = 0, pg = 0, pslot = 0;
     const uint8_t *pw0 = nullptr, *pw1 = nullptr;
     bool p_ok;
     {
@@ -418,28 +428,32 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
         pw0 = T.w0;
         pw1 = T.w1;
     }
-    uint4 ra[kStreamDepth], rb[kStreamDepth];
-    uint32_t rs[kStreamDepth];
-    auto load = [&](int k) {
-        if (!p_ok) return;
-        const size_t off = static_cast<size_t>(pg) * kGroupBytes;
-        ra[k] = ldg_stream_v4(pw0 + off + lane * 16);
-        rb[k] = ldg_stream_v4(pw1 + off + lane * 16);
-        rs[k] = ldg_stream_u32((lane < 16 ? pw0 : pw1) + off + 512 + 4 * (lane & 15));
-        if (++pg == G) {
-            pg = 0;
-            GemvUnit T;
-            p_ok = get(++pu, T);
-            pw0 = T.w0;
-            pw1 = T.w1;
+    auto issue = [&]() {
+        if (p_ok) {
+            uint8_t *dst = c.ring + pslot * kStageBytesR;
+            const size_t off = static_cast<size_t>(pg) * kGroupBytes;
+            cp_async16(dst + lane * 16, pw0 + off + lane * 16);
+            cp_async16(dst + kGroupBytes + lane * 16, pw1 + off + lane * 16);
+            if (lane < 8) {   // the 2 x 64 scale bytes
+                const int t = lane >> 2, k = lane & 3;
+                cp_async16(dst + t * kGroupBytes + 512 + 16 * k, (t ? pw1 : pw0) + off + 512 + 16 * k);
+            }
+            if (++pg == G) {
+                pg = 0;
+                GemvUnit T;
+                p_ok = get(++pu, T);
+                pw0 = T.w0;
+                pw1 = T.w1;
+            }
         }
+        cp_async_commit();
+        pslot = pslot + 1 == kStreamStages ? 0 : pslot + 1;
     };
     if (!early) prelude();
-#pragma unroll
-    for (int k = 0; k < kStreamDepth; ++k) load(k);
+    for (int k = 0; k < kStreamStages - 1; ++k) issue();
     if (early) prelude();
     // consumer cursor
-    int cu = 0, cg = 0;
+    int cu = 0, cg = 0, cslot = 0;
     bool c_ok;
     {
         GemvUnit U;
@@ -452,36 +466,38 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
         for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[q]);
     };
     const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
-    const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * 64;
+    const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry;
     while (c_ok) {
+        cp_async_wait<kStreamStages - 2>();   // this item's copies (kStreamStages - 2 newer groups may still fly)
+        __syncwarp();                         // ... and every lane's
+        const uint8_t *st = c.ring + cslot * kStageBytesR;
+        decode_scales(*reinterpret_cast<const uint32_t *>(st + (lane >> 4) * kGroupBytes + 512 + 4 * (lane & 15)), lane,
+                      c.e4p);
+        __syncwarp();
+        group_products(ld_shared_v4(st + lane * 16), ld_shared_v4(st + kGroupBytes + lane * 16), c.e4p, act0 + cg * 64,
+                       cs0 + cg * 4 * kCsEntry, lane, c.zero, chain);
+        __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
+        issue();
+        cslot = cslot + 1 == kStreamStages ? 0 : cslot + 1;
+        if (++cg == G) {
+            // y = acc * global * 1 (engine/src/kernels.cpp:1320)
+            GemvUnit U;
+            get(cu, U);
+            float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
+            float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
 #pragma unroll
-        for (int k = 0; k < kStreamDepth; ++k) {
-            if (c_ok) {
-                decode_scales(rs[k], lane, c.e4p);
-                __syncwarp();
-                group_products(ra[k], rb[k], c.e4p, act0 + cg * 64, cs0 + cg * 256, lane, c.zero, chain);
-                __syncwarp();   // every lane done with the scale pairs before the next group's
-                load(k);
-                if (++cg == G) {
-                    // y = acc * global * 1 (engine/src/kernels.cpp:1320)
-                    GemvUnit U;
-                    get(cu, U);
-                    float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
-                    float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        y0[i] = __fmul_rn(y0[i], U.g0);
-                        y1[i] = __fmul_rn(y1[i], U.g1);
-                    }
-                    epi(U, y0, y1, gid, tig);
-                    acc[0] = acc[1] = acc[2] = acc[3] = 0;
-                    cg = 0;
-                    c_ok = get(++cu, U);
-                    if (c_ok) restage(U);
-                }
+            for (int i = 0; i < 4; ++i) {
+                y0[i] = __fmul_rn(y0[i], U.g0);
+                y1[i] = __fmul_rn(y1[i], U.g1);
             }
+            epi(U, y0, y1, gid, tig);
+            acc[0] = acc[1] = acc[2] = acc[3] = 0;
+            cg = 0;
+            c_ok = get(++cu, U);
+            if (c_ok) restage(U);
         }
     }
+    cp_async_wait<0>();   // (no copy in flight when the warp leaves: the stages are released with the CTA)
 }
 
 // The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu. smem_warps: the warps'
