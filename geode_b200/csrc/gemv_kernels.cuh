@@ -132,7 +132,7 @@ inline bool plan_static(int cols, int n_units, int sms, RelayShape &r) {
 
 // kStages: the streaming path's ring depth (the launch shape has one warp per unit, stream_units), 0: the relay
 template <int kStages>
-__global__ void __launch_bounds__((kStages ? kStreamWarps : kGemvWarps) * 32, 1) k_gemv_static(StaticGemv p) {
+__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kGemvWarps) * 32, 1) k_gemv_static(StaticGemv p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
     const int cols = p.act.cols, wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__((kStages ? kStreamWarps : kGemvWarps) * 32, 1)
         StreamCtx c;
         uint8_t *wbase = smem + act_smem_bytes(cols) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, 0);
         c.e4p = reinterpret_cast<float *>(wbase);
-        c.ring = wbase + 1024;
+        c.ring = wbase + 2048;
         c.img = img;
         c.img_ts = act_tstride(cols);
         c.ngroups = cols / 64;
@@ -238,7 +238,7 @@ inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, 
 }
 
 template <int kStages>
-__global__ void __launch_bounds__((kStages ? kStreamWarps : kGemvWarps) * 32, 1) k_gemv_experts(ExpertsArgs p) {
+__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kGemvWarps) * 32, 1) k_gemv_experts(ExpertsArgs p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
     const bool gu = p.pass == kGateUp;
@@ -354,12 +354,12 @@ __global__ void __launch_bounds__((kStages ? kStreamWarps : kGemvWarps) * 32, 1)
         epi_store(U, y0, y1, gid, tig);
     };
     if constexpr (kStages > 0) {
-        // per warp: 1 KB of scale pairs, the ring, then (down) the warp's own image of all K
+        // per warp: 2 KB of scale pairs, the ring, then (down) the warp's own image of all K
         uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, gu ? 0 : sg);
-        uint8_t *own_img = wbase + 1024 + kStages * kStageBytesR;
+        uint8_t *own_img = wbase + 2048 + kStages * kStageBytesR;
         StreamCtx c;
         c.e4p = reinterpret_cast<float *>(wbase);
-        c.ring = wbase + 1024;
+        c.ring = wbase + 2048;
         c.img = gu ? img : own_img;
         c.img_ts = gu ? act_tstride(p.H) : slice_tstride(sg);
         c.ngroups = cols / 64;

@@ -373,17 +373,21 @@ constexpr int kWideStages = 6, kDeepStages = 12;
 
 // per warp: 1 KB of scale pairs, the ring, then the warp's own image (own groups, 0 for none)
 __host__ __device__ inline int stream_warp_bytes(int stages, int own) {
-    return 1024 + stages * kStageBytesR + (own ? (warp_act_bytes(own) + 127) / 128 * 128 : 0);
+    return 2048 + stages * kStageBytesR + (own ? (warp_act_bytes(own) + 127) / 128 * 128 : 0);
 }
+// warps per CTA on the streaming path: kStreamWarps (80 registers a thread) for wide launches, kDeepWarps (128) else
+constexpr int kDeepWarps = 16;
+__host__ __device__ constexpr int stream_warps(int stages) { return stages == kDeepStages ? kDeepWarps : kStreamWarps; }
 
 // A launch's shape for either path: one warp per unit streams, else the relay. units_per_cta: the units a CTA takes
 // (all CTAs take the same share, +-1).
 inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, int units_per_cta, RelayShape &r) {
-    if (wpu == 1) {
+    if (wpu == 1 && (cols / 64) % 2 == 0) {
         const int g = cols / 64;
         const int stages = units_per_cta >= kStreamWarps ? kWideStages : kDeepStages;
         const size_t wb = static_cast<size_t>(stream_warp_bytes(stages, own_images ? g : 0));
-        int ns = units_per_cta < kStreamWarps ? (units_per_cta > 0 ? units_per_cta : 1) : kStreamWarps;
+        int ns = stream_warps(stages);
+        if (units_per_cta > 0 && units_per_cta < ns) ns = units_per_cta;
         while (ns >= 1 && front + ns * wb > static_cast<size_t>(kMaxDynSmem)) --ns;
         if (g >= 1 && ns >= 1) {
             r = RelayShape{1, ns, g, front + ns * wb, stages};
@@ -393,67 +397,77 @@ inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, int unit
     return plan_relay(cols, wpu, own_images, front, r);
 }
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 struct StreamCtx {
-    float *e4p;           // this warp's 1 KB of (e, e) pairs
+    float *e4p;           // this warp's 2 KB of (e, e) pairs (two groups)
     uint8_t *ring;        // this warp's ring of stages of kStageBytesR
     const uint8_t *img;   // the activation image (token stride img_ts), groups from 0
     int img_ts;
-    int ngroups;          // K / 64
+    int ngroups;          // K / 64 (even)
     uint64_t zero;        // a +0 pair from runtime values (f2_mul_sep)
 };
 
 // get(i, U): the warp's i-th unit (false past the end); restage(U) (every lane) before a unit's first group; epi(U, y0,
 // y1, gid, tig) after its last. `early`: the first copies go out before prelude() (weights do not depend on the
-// previous kernel).
+// previous kernel). Groups go two at a time (K / 64 even), both copies waited for, both groups' scales decoded, then
+// both groups' products: two independent streams of tensor-core and f32 work for the scheduler.
 template <int kStreamStages, typename GetUnit, typename Restage, typename Epi, typename Prelude>
 __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Restage &restage, const Epi &epi, bool early,
                              const Prelude &prelude) {
+    static_assert(kStreamStages % 2 == 0 && kStreamStages >= 4, "stages in pairs");
     const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
     const int G = c.ngroups;
-    // producer cursor: every issue() commits one copy group (empty past the end), so at the consumption of item i
-    // exactly kStreamStages - 1 groups were committed after i's
-    int pu = 0, pg = 0, pslot = 0;
-    const uint8_t *pw0 = nullptr, *pw1 = nullptr;
+    // producer: this lane's copy sources in the current unit (codes of both tiles; lanes < 8 one 16-byte piece of the
+    // scales), advanced a group (576 bytes) per copy. Every issue() commits one copy group (empty past the end): the
+    // prologue kStreamStages - 2, then two per pair consumed, so when the pair (i, i + 1) is taken exactly
+    // kStreamStages - 4 groups were committed after i + 1's. Item k lives in stage k % kStreamStages.
+    const uint32_t ring_s = smem_addr(c.ring);
+    const uint32_t st_end = ring_s + kStreamStages * kStageBytesR;
+    const int sc_t = (lane >> 2) & 1, sc_k = lane & 3;   // (lanes < 8)
+    const uint32_t d_code = lane * 16, d_sc = sc_t * kGroupBytes + 512 + 16 * sc_k;
+    int pu = 0, pg = 0;
+    uint32_t pdst = ring_s;
+    const uint8_t *s0 = nullptr, *s1 = nullptr, *s2 = nullptr;
     bool p_ok;
-    {
+    auto unit_src = [&](int i) {
         GemvUnit T;
-        p_ok = get(0, T);
-        pw0 = T.w0;
-        pw1 = T.w1;
-    }
+        p_ok = get(i, T);
+        if (p_ok) {
+            s0 = T.w0 + lane * 16;
+            s1 = T.w1 + lane * 16;
+            s2 = (sc_t ? T.w1 : T.w0) + 512 + 16 * sc_k;
+        }
+    };
+    unit_src(0);
     auto issue = [&]() {
         if (p_ok) {
-            uint8_t *dst = c.ring + pslot * kStageBytesR;
-            const size_t off = static_cast<size_t>(pg) * kGroupBytes;
-            cp_async16(dst + lane * 16, pw0 + off + lane * 16);
-            cp_async16(dst + kGroupBytes + lane * 16, pw1 + off + lane * 16);
-            if (lane < 8) {   // the 2 x 64 scale bytes
-                const int t = lane >> 2, k = lane & 3;
-                cp_async16(dst + t * kGroupBytes + 512 + 16 * k, (t ? pw1 : pw0) + off + 512 + 16 * k);
-            }
+            cp_async16(pdst + d_code, s0);
+            cp_async16(pdst + kGroupBytes + d_code, s1);
+            if (lane < 8) cp_async16(pdst + d_sc, s2);
+            s0 += kGroupBytes;
+            s1 += kGroupBytes;
+            s2 += kGroupBytes;
             if (++pg == G) {
                 pg = 0;
-                GemvUnit T;
-                p_ok = get(++pu, T);
-                pw0 = T.w0;
-                pw1 = T.w1;
+                unit_src(++pu);
             }
         }
         cp_async_commit();
-        pslot = pslot + 1 == kStreamStages ? 0 : pslot + 1;
+        pdst += kStageBytesR;
+        if (pdst == st_end) pdst = ring_s;
     };
     if (!early) prelude();
-    for (int k = 0; k < kStreamStages - 1; ++k) issue();
+    for (int k = 0; k < kStreamStages - 2; ++k) issue();
     if (early) prelude();
-    // consumer cursor
-    int cu = 0, cg = 0, cslot = 0;
+    // consumer
+    int cu = 0, cg = 0;
+    const uint8_t *st = c.ring;
     bool c_ok;
     {
         GemvUnit U;
@@ -467,19 +481,26 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
     };
     const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
     const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry;
+    const uint8_t *ring_end = c.ring + kStreamStages * kStageBytesR;
     while (c_ok) {
-        cp_async_wait<kStreamStages - 2>();   // this item's copies (kStreamStages - 2 newer groups may still fly)
-        __syncwarp();                         // ... and every lane's
-        const uint8_t *st = c.ring + cslot * kStageBytesR;
-        decode_scales(*reinterpret_cast<const uint32_t *>(st + (lane >> 4) * kGroupBytes + 512 + 4 * (lane & 15)), lane,
-                      c.e4p);
+        // items i, i + 1: kStreamStages - 4 groups committed after i + 1's may still fly
+        cp_async_wait<kStreamStages - 4>();
+        __syncwarp();
+        const uint8_t *st1 = st + kStageBytesR;
+        const int sc_off = (lane >> 4) * kGroupBytes + 512 + 4 * (lane & 15);
+        decode_scales(*reinterpret_cast<const uint32_t *>(st + sc_off), lane, c.e4p);
+        decode_scales(*reinterpret_cast<const uint32_t *>(st1 + sc_off), lane, c.e4p + 256);
         __syncwarp();
         group_products(ld_shared_v4(st + lane * 16), ld_shared_v4(st + kGroupBytes + lane * 16), c.e4p, act0 + cg * 64,
                        cs0 + cg * 4 * kCsEntry, lane, c.zero, chain);
-        __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
+        group_products(ld_shared_v4(st1 + lane * 16), ld_shared_v4(st1 + kGroupBytes + lane * 16), c.e4p + 256,
+                       act0 + (cg + 1) * 64, cs0 + (cg + 1) * 4 * kCsEntry, lane, c.zero, chain);
+        __syncwarp();   // every lane done with the stages and the scale pairs before they are refilled
         issue();
-        cslot = cslot + 1 == kStreamStages ? 0 : cslot + 1;
-        if (++cg == G) {
+        issue();
+        st = st1 + kStageBytesR == ring_end ? c.ring : st1 + kStageBytesR;
+        cg += 2;
+        if (cg == G) {
             // y = acc * global * 1 (engine/src/kernels.cpp:1320)
             GemvUnit U;
             get(cu, U);
