@@ -415,7 +415,7 @@ int enqueue_step(gcuda *g, int n) {
                 else if (r.stages == kDeepStages)
                     LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
                 else
-                    LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kGemvWarps * 32), r.smem, g->st, pdl, ea));
+                    LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kFanThreads), r.smem, g->st, pdl, ea));
             }
             RC_OK(norm(next_norm, true, next_hf));
         }

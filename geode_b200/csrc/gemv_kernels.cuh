@@ -126,13 +126,12 @@ struct StaticGemv {
 };
 
 inline bool plan_static(int cols, int n_units, int sms, RelayShape &r) {
-    return plan_gemv(cols, choose_wpu(cols, n_units, sms), false, static_cast<size_t>(act_smem_bytes(cols)),
-                     (n_units + sms - 1) / sms, r);
+    return plan_gemv(cols, cols, false, static_cast<size_t>(act_smem_bytes(cols)), (n_units + sms - 1) / sms, r);
 }
 
-// kStages: the streaming path's ring depth (the launch shape has one warp per unit, stream_units), 0: the relay
+// kStages: the streaming path's ring depth (a warp per unit, stream_units), 0: the fan-in (fan_units)
 template <int kStages>
-__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kGemvWarps) * 32, 1) k_gemv_static(StaticGemv p) {
+__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) * 32, 1) k_gemv_static(StaticGemv p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
     const int cols = p.act.cols, wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
@@ -186,8 +185,14 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kGemvWarps)
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
         stream_units<kStages>(get, c, [](const GemvUnit &) {}, epi, true, prelude);
     } else {
-        RelayCtx c = make_ctx(smem + act_smem_bytes(cols), wpu, sg, 0, img, act_tstride(cols));
-        relay_units(get, c, [](const GemvUnit &) {}, p.status, epi, true, prelude);
+        FanCtx c;
+        c.img = img;
+        c.img_ts = act_tstride(cols);
+        c.prod = smem + act_smem_bytes(cols);
+        c.e4p = reinterpret_cast<float *>(c.prod + 2 * kFanSlotBytes);
+        c.ngroups = cols / 64;
+        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(nslots) >> 31);
+        fan_units(get, c, [](const GemvUnit &) { return false; }, [](const GemvUnit &, int, int) {}, epi, true, prelude);
     }
 }
 
@@ -230,15 +235,14 @@ inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, 
     const int picks = n * K < E ? n * K : E;
     if (pass == kGateUp) {
         const int units = picks * (ff / 16) + sff / 16;
-        return plan_gemv(H, choose_wpu(H, units, sms), false, static_cast<size_t>(act_smem_bytes(H)),
-                         (units + sms - 1) / sms, r);
+        return plan_gemv(H, H, false, static_cast<size_t>(act_smem_bytes(H)), (units + sms - 1) / sms, r);
     }
     const int units = (picks + 1) * (H / 32);
-    return plan_gemv(ff, choose_wpu(ff, units, sms), true, 0, (units + sms - 1) / sms, r);
+    return plan_gemv(ff, ff, true, 0, (units + sms - 1) / sms, r);
 }
 
 template <int kStages>
-__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kGemvWarps) * 32, 1) k_gemv_experts(ExpertsArgs p) {
+__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) * 32, 1) k_gemv_experts(ExpertsArgs p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
     const bool gu = p.pass == kGateUp;
@@ -367,11 +371,28 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kGemvWarps)
         own = gu ? nullptr : own_img;
         stream_units<kStages>(get, c, restage, epi, false, prelude);
     } else {
-        RelayCtx c = gu ? make_ctx(smem + act_smem_bytes(p.H), wpu, sg, 0, img, act_tstride(p.H))
-                        : make_ctx(smem, wpu, sg, sg, nullptr, 0);
-        own = c.own_img;
-        part = c.part;
-        relay_units(get, c, restage, p.status, epi, false, prelude);
+        // one image for the CTA: h (gate_up, staged in the prelude), or the unit's picks' rows (down, restaged by the
+        // producers when the expert changes)
+        uint8_t *fimg = smem;
+        FanCtx c;
+        c.img = fimg;
+        c.img_ts = gu ? act_tstride(p.H) : act_tstride(p.ff);
+        c.prod = smem + act_smem_bytes(cols);
+        c.e4p = reinterpret_cast<float *>(c.prod + 2 * kFanSlotBytes);
+        c.ngroups = cols / 64;
+        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(nslots) >> 31);
+        int fan_staged = -2;
+        auto changes = [&](const GemvUnit &U) {
+            if (gu || U.act_id == fan_staged) return false;
+            fan_staged = U.act_id;
+            return true;
+        };
+        auto fan_restage = [&](const GemvUnit &U, int me, int nthr) {
+            stage_image(U.act_id < 0 ? p.shact : p.amid,
+                        [&](int t) { return t < p.n && ((U.tok_mask >> t) & 1) ? static_cast<int>(U.slot[t]) : -1; }, 0,
+                        cols / 64, act_tstride(cols), fimg, me, nthr);
+        };
+        fan_units(get, c, changes, fan_restage, epi, false, prelude);
     }
 }
 

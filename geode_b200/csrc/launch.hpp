@@ -93,7 +93,7 @@ inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     else if (r.stages == kDeepStages)
         e = launch_ex(k_gemv_static<kDeepStages>, dim3(grid), dim3(kDeepWarps * 32), r.smem, st, pdl, p);
     else
-        e = launch_ex(k_gemv_static<0>, dim3(grid), dim3(kGemvWarps * 32), r.smem, st, pdl, p);
+        e = launch_ex(k_gemv_static<0>, dim3(grid), dim3(kFanThreads), r.smem, st, pdl, p);
     return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }
 

@@ -361,6 +361,19 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
     return ok;
 }
 
+// the fan-in path's shape (fan_units below)
+constexpr int kFanProducers = 16;
+constexpr int kFanWarps = kFanProducers + 1;
+constexpr int kFanThreads = kFanWarps * 32;
+constexpr int kFanGroupBytes = 32 * 16 * 8;                      // a group's products: 32 lanes x 16 f32 pairs
+constexpr int kFanSlotBytes = kFanProducers * kFanGroupBytes;
+constexpr int kBarFull = 1, kBarEmpty = 3, kBarProducers = 5;    // (+ slot)
+
+// image (img_cols wide), then two product slots, then a KB of scale pairs per producer
+__host__ __device__ inline size_t fan_smem_bytes(int img_cols) {
+    return static_cast<size_t>(act_smem_bytes(img_cols)) + 2 * kFanSlotBytes + kFanProducers * 1024;
+}
+
 // ------------------------------------------------------------------------------------------- streaming ----
 // The path for launches with a warp per unit (wpu = 1, no relay): each warp (up to kStreamWarps) copies its units'
 // groups (both tiles' 576 bytes) into its own ring of shared-memory stages with 16-byte cp.async copies, the
@@ -379,10 +392,17 @@ __host__ __device__ inline int stream_warp_bytes(int stages, int own) {
 constexpr int kDeepWarps = 16;
 __host__ __device__ constexpr int stream_warps(int stages) { return stages == kDeepStages ? kDeepWarps : kStreamWarps; }
 
-// A launch's shape for either path: one warp per unit streams, else the relay. units_per_cta: the units a CTA takes
-// (all CTAs take the same share, +-1).
-inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, int units_per_cta, RelayShape &r) {
-    if (wpu == 1 && (cols / 64) % 2 == 0) {
+// A launch's shape: streaming (a warp per unit) when every CTA has kStreamMinUnits units or more, else the fan-in
+// (stages 0; the CTA on one unit at a time, its image img_cols wide). units_per_cta: the units a CTA takes (all CTAs
+// take the same share, +-1).
+constexpr int kStreamMinUnits = 2;
+inline bool plan_gemv(int cols, int img_cols, bool own_images, size_t front, int units_per_cta, RelayShape &r) {
+    const size_t fan = fan_smem_bytes(img_cols);
+    if (units_per_cta < kStreamMinUnits && cols >= 64 && fan <= static_cast<size_t>(kMaxDynSmem)) {
+        r = RelayShape{kFanWarps, 1, cols / 64, fan, 0};
+        return true;
+    }
+    if ((cols / 64) % 2 == 0) {
         const int g = cols / 64;
         const int stages = units_per_cta >= kStreamWarps ? kWideStages : kDeepStages;
         const size_t wb = static_cast<size_t>(stream_warp_bytes(stages, own_images ? g : 0));
@@ -394,9 +414,24 @@ inline bool plan_gemv(int cols, int wpu, bool own_images, size_t front, int unit
             return true;
         }
     }
-    return plan_relay(cols, wpu, own_images, front, r);
+    if (cols >= 64 && fan <= static_cast<size_t>(kMaxDynSmem)) {
+        r = RelayShape{kFanWarps, 1, cols / 64, fan, 0};
+        return true;
+    }
+    return false;
 }
 
+__device__ __forceinline__ uint4 ldg_stream_v4(const uint8_t *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream_u32(const uint8_t *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -444,7 +479,6 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
             s2 = (sc_t ? T.w1 : T.w0) + 512 + 16 * sc_k;
         }
     };
-    unit_src(0);
     auto issue = [&]() {
         if (p_ok) {
             cp_async16(pdst + d_code, s0);
@@ -462,7 +496,9 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
         pdst += kStageBytesR;
         if (pdst == st_end) pdst = ring_s;
     };
+    // (get() may read the previous kernel's output: not before prelude() unless `early`)
     if (!early) prelude();
+    unit_src(0);
     for (int k = 0; k < kStreamStages - 2; ++k) issue();
     if (early) prelude();
     // consumer
@@ -519,6 +555,140 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
         }
     }
     cp_async_wait<0>();   // (no copy in flight when the warp leaves: the stages are released with the CTA)
+}
+
+// ------------------------------------------------------------------------------------------- fan-in ----
+// The path for launches with few units (latency-bound): the whole CTA works on one unit at a time. kFanProducers
+// warps each take one group of a chunk (kFanProducers consecutive groups), multiply it and leave its products in a
+// shared-memory slot; one chain warp then adds the chunk's products in block order (one f32x2 add per product, the
+// only serial work) while the producers fill the other slot. Slots change hands through named barriers (FULL: the
+// producers arrive, the chain warp waits; EMPTY: the reverse), which need no spinning and cannot be left waiting: every
+// warp walks the same units and chunks.
+__device__ __forceinline__ void bar_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void bar_arrive_n(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+struct FanCtx {
+    uint8_t *img;       // the activation image (token stride img_ts)
+    int img_ts;
+    uint8_t *prod;      // two slots of kFanSlotBytes
+    float *e4p;         // kFanProducers x 1 KB
+    int ngroups;        // K / 64
+    uint64_t zero;      // a +0 pair from runtime values (f2_mul_sep)
+};
+
+// get(i, U): the CTA's i-th unit (false past the end); restage(U, me, nthr) by the producers (threads me of nthr)
+// before a unit whose activations differ from the last one's (`changes(U)` true); epi(U, y0, y1, gid, tig) by the
+// chain warp. `early`: the producers' first loads go out before prelude() (which every thread calls once).
+template <typename GetUnit, typename Changes, typename Restage, typename Epi, typename Prelude>
+__device__ void fan_units(const GetUnit &get, const FanCtx &c, const Changes &changes, const Restage &restage,
+                          const Epi &epi, bool early, const Prelude &prelude) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
+    const int G = c.ngroups, nch = (G + kFanProducers - 1) / kFanProducers;
+    if (warp < kFanProducers) {
+        // producer: items (unit i, chunk k), group g = k * kFanProducers + warp; two items' loads ahead in registers
+        int pi = 0, pk = 0;
+        const uint8_t *pw0 = nullptr, *pw1 = nullptr;
+        bool p_ok;
+        auto unit_ptrs = [&](int i) {
+            GemvUnit T;
+            p_ok = get(i, T);
+            pw0 = T.w0;
+            pw1 = T.w1;
+        };
+        uint4 ra[2], rb[2];
+        uint32_t rs[2];
+        auto load = [&](int k) {
+            if (!p_ok) return;
+            const int g = pk * kFanProducers + warp;
+            if (g < G) {
+                const size_t off = static_cast<size_t>(g) * kGroupBytes;
+                ra[k] = ldg_stream_v4(pw0 + off + lane * 16);
+                rb[k] = ldg_stream_v4(pw1 + off + lane * 16);
+                rs[k] = ldg_stream_u32((lane < 16 ? pw0 : pw1) + off + 512 + 4 * (lane & 15));
+            }
+            if (++pk == nch) {
+                pk = 0;
+                unit_ptrs(++pi);
+            }
+        };
+        // (get() may read the previous kernel's output: not before prelude() unless `early`)
+        if (!early) prelude();
+        unit_ptrs(0);
+        load(0);
+        load(1);
+        if (early) prelude();
+        float *e4p = c.e4p + warp * 256;
+        const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
+        const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry;
+        int item = 0;
+        GemvUnit U;
+        for (int i = 0; get(i, U); ++i) {
+            if (changes(U)) {
+                bar_sync_n(kBarProducers, kFanProducers * 32);   // every producer done with the old image
+                restage(U, static_cast<int>(threadIdx.x), kFanProducers * 32);
+                bar_sync_n(kBarProducers, kFanProducers * 32);
+            }
+#pragma unroll 1
+            for (int k = 0; k < nch; ++k, ++item) {
+                const int slot = item & 1;
+                if (item >= 2) bar_sync_n(kBarEmpty + slot, kFanThreads);   // the chain warp read this slot
+                const int g = k * kFanProducers + warp;
+                if (g < G) {
+                    decode_scales(rs[slot], lane, e4p);
+                    __syncwarp();
+                    uint4 *dst = reinterpret_cast<uint4 *>(c.prod + slot * kFanSlotBytes + warp * kFanGroupBytes) + lane;
+                    group_products(ra[slot], rb[slot], e4p, act0 + g * 64, cs0 + g * 4 * kCsEntry, lane, c.zero,
+                                   [&](int j, const uint64_t (&p)[4]) {
+                                       dst[(2 * j) * 32] = make_uint4(static_cast<uint32_t>(p[0]), static_cast<uint32_t>(p[0] >> 32),
+                                                                      static_cast<uint32_t>(p[1]), static_cast<uint32_t>(p[1] >> 32));
+                                       dst[(2 * j + 1) * 32] = make_uint4(static_cast<uint32_t>(p[2]), static_cast<uint32_t>(p[2] >> 32),
+                                                                          static_cast<uint32_t>(p[3]), static_cast<uint32_t>(p[3] >> 32));
+                                   });
+                    __syncwarp();   // (the scale pairs are rewritten by the next group)
+                }
+                bar_arrive_n(kBarFull + slot, kFanThreads);
+                load(slot);
+            }
+        }
+        // the chain warp's last two arrivals on EMPTY, consumed
+        for (int j = item - 2; j < item; ++j)
+            if (j >= 0) bar_sync_n(kBarEmpty + (j & 1), kFanThreads);
+    } else {
+        prelude();
+        int item = 0;
+        GemvUnit U;
+        for (int i = 0; get(i, U); ++i) {
+            uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll 1
+            for (int k = 0; k < nch; ++k, ++item) {
+                const int slot = item & 1;
+                bar_sync_n(kBarFull + slot, kFanThreads);
+                const int ng = min(kFanProducers, G - k * kFanProducers);
+                const uint4 *src = reinterpret_cast<const uint4 *>(c.prod + slot * kFanSlotBytes) + lane;
+#pragma unroll 1
+                for (int gl = 0; gl < ng; ++gl, src += kFanGroupBytes / 16) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint4 a = ld_shared_v4(src + (2 * j) * 32), b = ld_shared_v4(src + (2 * j + 1) * 32);
+                        acc[0] = f2_add(acc[0], pack2(a.x, a.y));
+                        acc[1] = f2_add(acc[1], pack2(a.z, a.w));
+                        acc[2] = f2_add(acc[2], pack2(b.x, b.y));
+                        acc[3] = f2_add(acc[3], pack2(b.z, b.w));
+                    }
+                }
+                bar_arrive_n(kBarEmpty + slot, kFanThreads);
+            }
+            // y = acc * global * 1 (engine/src/kernels.cpp:1320)
+            float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
+            float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                y0[q] = __fmul_rn(y0[q], U.g0);
+                y1[q] = __fmul_rn(y1[q], U.g1);
+            }
+            epi(U, y0, y1, gid, tig);
+        }
+    }
 }
 
 // The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu. smem_warps: the warps'
