@@ -184,13 +184,15 @@ void swiglu_units(std::vector<GemvUnit> &out, const DevTensor &gt, const DevTens
 
 // act_cols: the width of the activation rows the units multiply (0: the buffer's own width); the rows are packed
 // at that width (a narrower writer, e.g. the Gated DeltaNet core, packs them so)
-int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, int act_cols = 0) {
+// swiglu: the units pair gate and up tiles (they cannot be split into one-tile units)
+int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, int act_cols = 0, bool swiglu = false) {
     StaticGemv p{};
     p.units = g->units + u0;
     p.n_units = nu;
     p.act = act.set();
     if (act_cols > 0) p.act = ActSet{act.q, act.scale, act.bsum, act_cols, act.n, act_cols, act_cols / 16};
     p.ncols = n;
+    p.allow_half = swiglu ? 0 : 1;
     p.status = g->d_status;
     return launch_static_gemv(p, g->st, pdl);
 }
@@ -370,7 +372,7 @@ int enqueue_step(gcuda *g, int n) {
         const float *next_norm = l + 1 < s.n_layers ? raw(g->layers[static_cast<size_t>(l) + 1].in_norm) : raw(g->final_norm);
         float *next_hf = l + 1 < s.n_layers ? g->hf : g->hid;
         if (s.dense) {
-            RC_OK(launch_units(g, P.u_mlp, P.n_mlp, g->hq, n, pdl));
+            RC_OK(launch_units(g, P.u_mlp, P.n_mlp, g->hq, n, pdl, 0, true));
             RC_OK(launch_units(g, P.u_dn, P.n_dn, g->shact, n, pdl));
             RC_OK(norm(next_norm, false, next_hf));
         } else {

@@ -122,6 +122,8 @@ struct StaticGemv {
     ActSet act;
     int ncols;          // token columns (<= kMaxTok)
     int wpu, nslots;    // the launch shape (plan_static)
+    int allow_half;     // the units may be split into one-tile units (no swiglu unit)
+    int half;           // (the fan-in path) units of one tile: n_units * 2 of them
     uint32_t *status;
 };
 
@@ -149,10 +151,7 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
     }
     const int slot = warp / wpu;
     const size_t tb = static_cast<size_t>(cols / 64) * kGroupBytes;
-    auto get = [&](int i, GemvUnit &U) -> bool {
-        // CTA-major: unit u on CTA u % grid, so every SM holds the same count (+-1) whatever the slots' share
-        const int u = blockIdx.x + gridDim.x * (slot + nslots * i);
-        if (u >= p.n_units) return false;
+    auto unit_at = [&](int u, GemvUnit &U) {
         if (p.units) {
             U = p.units[u];
             U.tok_mask &= (1 << p.ncols) - 1;
@@ -169,6 +168,21 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         U.tok_mask = (1 << p.ncols) - 1;
         U.act_id = 0;
         for (int t = 0; t < kMaxTok; ++t) U.slot[t] = t;
+        return true;
+    };
+    auto get = [&](int i, GemvUnit &U) -> bool {
+        // CTA-major: unit u on CTA u % grid, so every SM holds the same count (+-1) whatever the slots' share
+        const int u = blockIdx.x + gridDim.x * (slot + nslots * i);
+        if (!p.half) return u < p.n_units && unit_at(u, U);
+        // one-tile units: tile u % 2 of unit u / 2, as tile A
+        if (u >= 2 * p.n_units || !unit_at(u >> 1, U)) return false;
+        if (u & 1) {
+            U.w0 = U.w1;
+            U.g0 = U.g1;
+            U.y0 = U.y1;
+        }
+        U.w1 = U.w0;
+        U.y1 = nullptr;
         return true;
     };
     auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
@@ -190,8 +204,10 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         c.img_ts = act_tstride(cols);
         c.prod = smem + act_smem_bytes(cols);
         c.e4p = reinterpret_cast<float *>(c.prod + 2 * kFanSlotBytes);
+        c.xchg = reinterpret_cast<float4 *>(c.prod + 2 * kFanSlotBytes + kFanProducers * 1024);
         c.ngroups = cols / 64;
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(nslots) >> 31);
+        c.half = p.half != 0;
         fan_units(get, c, [](const GemvUnit &) { return false; }, [](const GemvUnit &, int, int) {}, epi, true, prelude);
     }
 }
@@ -379,8 +395,10 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         c.img_ts = gu ? act_tstride(p.H) : act_tstride(p.ff);
         c.prod = smem + act_smem_bytes(cols);
         c.e4p = reinterpret_cast<float *>(c.prod + 2 * kFanSlotBytes);
+        c.xchg = reinterpret_cast<float4 *>(c.prod + 2 * kFanSlotBytes + kFanProducers * 1024);
         c.ngroups = cols / 64;
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(nslots) >> 31);
+        c.half = false;
         int fan_staged = -2;
         auto changes = [&](const GemvUnit &U) {
             if (gu || U.act_id == fan_staged) return false;

@@ -80,13 +80,16 @@ inline int gemv_opt_in() {
 }
 
 // p.wpu / p.nslots are set here (plan_static); the grid is one CTA per SM at most
+// (p.allow_half: a launch with fewer units than SMs runs one-tile units on the fan-in path, twice the CTAs)
 inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     RelayShape r;
     if (!plan_static(p.act.cols, p.n_units, sm_count(), r)) return GCUDA_E_ARG;
     if (gemv_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
     p.wpu = r.wpu;
     p.nslots = r.nslots;
-    const int grid = std::max(1, std::min(sm_count(), (p.n_units + r.nslots - 1) / r.nslots));
+    p.half = r.stages == 0 && p.allow_half && p.n_units < sm_count();
+    const int units = p.half ? 2 * p.n_units : p.n_units;
+    const int grid = std::max(1, std::min(sm_count(), (units + r.nslots - 1) / r.nslots));
     cudaError_t e;
     if (r.stages == kWideStages)
         e = launch_ex(k_gemv_static<kWideStages>, dim3(grid), dim3(kStreamWarps * 32), r.smem, st, pdl, p);

@@ -49,6 +49,7 @@ int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float g
     p.mode = kStore;
     p.act = ActSet{d_q, d_scale, d_bsum, static_cast<int>(cols), n, static_cast<int>(cols), static_cast<int>(cols / 16)};
     p.ncols = n;
+    p.allow_half = 1;
     p.status = device_status();
     return launch_static_gemv(p, static_cast<cudaStream_t>(stream), false);
 }

@@ -119,15 +119,20 @@ __device__ __forceinline__ void epi_store(const GemvUnit &U, const float (&y0)[4
     for (int h = 0; h < 2; ++h) {
         const int t = 2 * tig + h;
         if (t >= kMaxTok || !((U.tok_mask >> t) & 1)) continue;
-        float *r0 = U.y0 + static_cast<size_t>(U.slot[t]) * U.ystride, *r1 = U.y1 + static_cast<size_t>(U.slot[t]) * U.ystride;
+        float *r0 = U.y0 + static_cast<size_t>(U.slot[t]) * U.ystride;
         if (U.mode == kAccumulate) {
             r0[gid] = __fadd_rn(r0[gid], y0[h]);
             r0[gid + 8] = __fadd_rn(r0[gid + 8], y0[2 + h]);
-            r1[gid] = __fadd_rn(r1[gid], y1[h]);
-            r1[gid + 8] = __fadd_rn(r1[gid + 8], y1[2 + h]);
         } else {
             r0[gid] = y0[h];
             r0[gid + 8] = y0[2 + h];
+        }
+        if (!U.y1) continue;   // (a unit of one tile)
+        float *r1 = U.y1 + static_cast<size_t>(U.slot[t]) * U.ystride;
+        if (U.mode == kAccumulate) {
+            r1[gid] = __fadd_rn(r1[gid], y1[h]);
+            r1[gid + 8] = __fadd_rn(r1[gid + 8], y1[2 + h]);
+        } else {
             r1[gid] = y1[h];
             r1[gid + 8] = y1[2 + h];
         }

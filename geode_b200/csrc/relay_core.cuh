@@ -114,37 +114,39 @@ inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelaySh
 // zeros), token stride ts: act word (t, gl, tig, j) at t * ts + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
 // .. + 3); cs per (gl, tig) kCsEntry bytes at kMaxTok * ts + (gl * 4 + tig) * kCsEntry: for each block j the mma's
 // accumulator quad (cinit(2 tig), cinit(2 tig + 1), cinit(2 tig), cinit(2 tig + 1)), then (ascale(2 tig),
-// ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 15 * bsum. Threads `me` of `nthr` share the work; every thread
-// issues its loads (16 bytes: one block of one token) in batches before it stores.
+// ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 15 * bsum. Threads `me` of `nthr` share the blocks; a thread
+// loads one block of every token (16 bytes each) before it stores any.
 template <typename Src>
 __device__ inline void stage_image(const ActSet &a, const Src &src, int g0, int ng, int ts, uint8_t *img, int me, int nthr) {
-    constexpr int kBatch = 4;
-    const int items = kMaxTok * ng * 4;   // (token, block)
-    for (int base = me; base < items; base += nthr * kBatch) {
-        uint4 v[kBatch];
-        int32_t bs[kBatch];
-        float sc[kBatch];
+    // thread me takes blocks bl = me, me + nthr, ... of every token, four tokens' loads at a time
+    const int nbl = ng * 4;
+    int rows[kMaxTok];
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int i = base + u * nthr;
+    for (int t = 0; t < kMaxTok; ++t) rows[t] = src(t);
+    constexpr int kT = 4;   // tokens whose loads are in flight together
+    for (int bl = me; bl < nbl; bl += nthr)
+#pragma unroll
+    for (int t0 = 0; t0 < kMaxTok; t0 += kT) {
+        const size_t b = static_cast<size_t>(g0) * 4 + bl;
+        uint4 v[kT];
+        int32_t bs[kT];
+        float sc[kT];
+#pragma unroll
+        for (int u = 0; u < kT; ++u) {
             v[u] = make_uint4(0, 0, 0, 0);
             bs[u] = 0;
             sc[u] = 0.0f;
-            if (i < items) {
-                const int t = i / (ng * 4), bl = i % (ng * 4), r = src(t);
-                if (r >= 0) {
-                    const size_t b = static_cast<size_t>(g0) * 4 + bl;
-                    v[u] = *reinterpret_cast<const uint4 *>(a.q + static_cast<size_t>(r) * a.qstride + 16 * b);
-                    bs[u] = a.bsum[static_cast<size_t>(r) * a.sstride + b];
-                    sc[u] = a.scale[static_cast<size_t>(r) * a.sstride + b];
-                }
+            if (rows[t0 + u] >= 0) {
+                const size_t r = static_cast<size_t>(rows[t0 + u]);
+                v[u] = *reinterpret_cast<const uint4 *>(a.q + r * a.qstride + 16 * b);
+                bs[u] = a.bsum[r * a.sstride + b];
+                sc[u] = a.scale[r * a.sstride + b];
             }
         }
+        const int gl = bl >> 2, j = bl & 3;
 #pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            const int i = base + u * nthr;
-            if (i >= items) break;
-            const int t = i / (ng * 4), bl = i % (ng * 4), gl = bl / 4, j = bl % 4;
+        for (int u = 0; u < kT; ++u) {
+            const int t = t0 + u;
             uint8_t *row = img + t * ts + gl * 64 + 4 * j;   // word (t, gl, tig, j) at + tig * 16
             *reinterpret_cast<uint32_t *>(row) = v[u].x;
             *reinterpret_cast<uint32_t *>(row + 16) = v[u].y;
@@ -185,7 +187,8 @@ __device__ __forceinline__ void decode_scales(uint32_t word, int lane, float *e4
 // 2 tig + 1), row gid + 8: the pair), tile B likewise, handed to sink(j, p) in block order.
 // e4p: the group's scales as [tile][block][gid][e(gid), e(gid), e(gid+8), e(gid+8)] floats.
 // wa / wb: the lane's 16 code bytes of tiles A and B.
-template <typename Sink>
+// kOne: tile A only (p[2], p[3] left 0).
+template <bool kOne = false, typename Sink>
 __device__ __forceinline__ void group_products(const uint4 wa, const uint4 wb, const float *e4p, const uint8_t *act,
                                                const uint8_t *cs, int lane, uint64_t zero, const Sink &sink) {
     const int gid = lane >> 2;
@@ -199,20 +202,23 @@ __device__ __forceinline__ void group_products(const uint4 wa, const uint4 wb, c
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         int32_t dA[4], dB[4];
+        (void)dB;
         const uint4 cq = ld_shared_v4(cs + 16 * j);   // the block's accumulator quad
         const int32_t cinit[4] = {static_cast<int32_t>(cq.x), static_cast<int32_t>(cq.y), static_cast<int32_t>(cq.z),
                                   static_cast<int32_t>(cq.w)};
         mma_s8_16816(dA, (wA[j] << 1) & 0x1E1E1E1Eu, (wA[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
-        mma_s8_16816(dB, (wB[j] << 1) & 0x1E1E1E1Eu, (wB[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
         const uint4 eA = ld_shared_v4(e4p + ((0 * 4 + j) * 8 + gid) * 4);
-        const uint4 eB = ld_shared_v4(e4p + ((1 * 4 + j) * 8 + gid) * 4);
         // float(isum) = bits(bias + isum) - bias; p = float(isum) * (e4m3 * ascale)
         const uint64_t FAg = f2_sub(pack2(dA[0], dA[1]), bias2), FAh = f2_sub(pack2(dA[2], dA[3]), bias2);
-        const uint64_t FBg = f2_sub(pack2(dB[0], dB[1]), bias2), FBh = f2_sub(pack2(dB[2], dB[3]), bias2);
-        const uint64_t p[4] = {f2_mul_sep(FAg, f2_mul(pack2(eA.x, eA.y), sp[j]), zero),
-                               f2_mul_sep(FAh, f2_mul(pack2(eA.z, eA.w), sp[j]), zero),
-                               f2_mul_sep(FBg, f2_mul(pack2(eB.x, eB.y), sp[j]), zero),
-                               f2_mul_sep(FBh, f2_mul(pack2(eB.z, eB.w), sp[j]), zero)};
+        uint64_t p[4] = {f2_mul_sep(FAg, f2_mul(pack2(eA.x, eA.y), sp[j]), zero),
+                         f2_mul_sep(FAh, f2_mul(pack2(eA.z, eA.w), sp[j]), zero), 0, 0};
+        if constexpr (!kOne) {
+            mma_s8_16816(dB, (wB[j] << 1) & 0x1E1E1E1Eu, (wB[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
+            const uint4 eB = ld_shared_v4(e4p + ((1 * 4 + j) * 8 + gid) * 4);
+            const uint64_t FBg = f2_sub(pack2(dB[0], dB[1]), bias2), FBh = f2_sub(pack2(dB[2], dB[3]), bias2);
+            p[2] = f2_mul_sep(FBg, f2_mul(pack2(eB.x, eB.y), sp[j]), zero);
+            p[3] = f2_mul_sep(FBh, f2_mul(pack2(eB.z, eB.w), sp[j]), zero);
+        }
         sink(j, p);
     }
 }
@@ -363,15 +369,17 @@ __device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &resta
 
 // the fan-in path's shape (fan_units below)
 constexpr int kFanProducers = 16;
-constexpr int kFanWarps = kFanProducers + 1;
+constexpr int kFanAhead = 4;   // a producer's items in flight
+constexpr int kFanChains = 2;   // chain warps: tile A's sums, tile B's
+constexpr int kFanWarps = kFanProducers + kFanChains;
 constexpr int kFanThreads = kFanWarps * 32;
 constexpr int kFanGroupBytes = 32 * 16 * 8;                      // a group's products: 32 lanes x 16 f32 pairs
 constexpr int kFanSlotBytes = kFanProducers * kFanGroupBytes;
-constexpr int kBarFull = 1, kBarEmpty = 3, kBarProducers = 5;    // (+ slot)
+constexpr int kBarFull = 1, kBarEmpty = 3, kBarProducers = 5, kBarChains = 6;    // (+ slot)
 
-// image (img_cols wide), then two product slots, then a KB of scale pairs per producer
+// image (img_cols wide), then two product slots, then a KB of scale pairs per producer, then the chains' exchange
 __host__ __device__ inline size_t fan_smem_bytes(int img_cols) {
-    return static_cast<size_t>(act_smem_bytes(img_cols)) + 2 * kFanSlotBytes + kFanProducers * 1024;
+    return static_cast<size_t>(act_smem_bytes(img_cols)) + 2 * kFanSlotBytes + kFanProducers * 1024 + 32 * 16;
 }
 
 // ------------------------------------------------------------------------------------------- streaming ----
@@ -572,7 +580,9 @@ struct FanCtx {
     int img_ts;
     uint8_t *prod;      // two slots of kFanSlotBytes
     float *e4p;         // kFanProducers x 1 KB
+    float4 *xchg;       // 32 lanes: tile B's sums, for the tile A chain warp's epilogue
     int ngroups;        // K / 64
+    bool half;          // units of one tile (get() gives it as tile A, y1 = NULL; never a swiglu unit)
     uint64_t zero;      // a +0 pair from runtime values (f2_mul_sep)
 };
 
@@ -585,7 +595,7 @@ __device__ void fan_units(const GetUnit &get, const FanCtx &c, const Changes &ch
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
     const int G = c.ngroups, nch = (G + kFanProducers - 1) / kFanProducers;
     if (warp < kFanProducers) {
-        // producer: items (unit i, chunk k), group g = k * kFanProducers + warp; two items' loads ahead in registers
+        // producer: items (unit i, chunk k), group g = k * kFanProducers + warp; kFanAhead items' loads ahead in registers
         int pi = 0, pk = 0;
         const uint8_t *pw0 = nullptr, *pw1 = nullptr;
         bool p_ok;
@@ -595,15 +605,15 @@ __device__ void fan_units(const GetUnit &get, const FanCtx &c, const Changes &ch
             pw0 = T.w0;
             pw1 = T.w1;
         };
-        uint4 ra[2], rb[2];
-        uint32_t rs[2];
+        uint4 ra[kFanAhead], rb[kFanAhead];
+        uint32_t rs[kFanAhead];
         auto load = [&](int k) {
             if (!p_ok) return;
             const int g = pk * kFanProducers + warp;
             if (g < G) {
                 const size_t off = static_cast<size_t>(g) * kGroupBytes;
                 ra[k] = ldg_stream_v4(pw0 + off + lane * 16);
-                rb[k] = ldg_stream_v4(pw1 + off + lane * 16);
+                if (!c.half) rb[k] = ldg_stream_v4(pw1 + off + lane * 16);
                 rs[k] = ldg_stream_u32((lane < 16 ? pw0 : pw1) + off + 512 + 4 * (lane & 15));
             }
             if (++pk == nch) {
@@ -614,79 +624,123 @@ __device__ void fan_units(const GetUnit &get, const FanCtx &c, const Changes &ch
         // (get() may read the previous kernel's output: not before prelude() unless `early`)
         if (!early) prelude();
         unit_ptrs(0);
-        load(0);
-        load(1);
+#pragma unroll
+        for (int k = 0; k < kFanAhead; ++k) load(k);
         if (early) prelude();
         float *e4p = c.e4p + warp * 256;
         const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
         const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry;
-        int item = 0;
+        // items in turn, kFanAhead per round so that the register buffers are indexed statically
+        int item = 0, ci = 0, ck = 0;
         GemvUnit U;
-        for (int i = 0; get(i, U); ++i) {
-            if (changes(U)) {
-                bar_sync_n(kBarProducers, kFanProducers * 32);   // every producer done with the old image
-                restage(U, static_cast<int>(threadIdx.x), kFanProducers * 32);
-                bar_sync_n(kBarProducers, kFanProducers * 32);
-            }
-#pragma unroll 1
-            for (int k = 0; k < nch; ++k, ++item) {
+        bool c_ok = get(0, U);
+        while (c_ok) {
+#pragma unroll
+            for (int r = 0; r < kFanAhead; ++r) {
+                if (!c_ok) break;
+                if (ck == 0 && changes(U)) {
+                    bar_sync_n(kBarProducers, kFanProducers * 32);   // every producer done with the old image
+                    restage(U, static_cast<int>(threadIdx.x), kFanProducers * 32);
+                    bar_sync_n(kBarProducers, kFanProducers * 32);
+                }
                 const int slot = item & 1;
                 if (item >= 2) bar_sync_n(kBarEmpty + slot, kFanThreads);   // the chain warp read this slot
-                const int g = k * kFanProducers + warp;
+                const int g = ck * kFanProducers + warp;
                 if (g < G) {
-                    decode_scales(rs[slot], lane, e4p);
+                    decode_scales(rs[r], lane, e4p);
                     __syncwarp();
                     uint4 *dst = reinterpret_cast<uint4 *>(c.prod + slot * kFanSlotBytes + warp * kFanGroupBytes) + lane;
-                    group_products(ra[slot], rb[slot], e4p, act0 + g * 64, cs0 + g * 4 * kCsEntry, lane, c.zero,
-                                   [&](int j, const uint64_t (&p)[4]) {
-                                       dst[(2 * j) * 32] = make_uint4(static_cast<uint32_t>(p[0]), static_cast<uint32_t>(p[0] >> 32),
-                                                                      static_cast<uint32_t>(p[1]), static_cast<uint32_t>(p[1] >> 32));
-                                       dst[(2 * j + 1) * 32] = make_uint4(static_cast<uint32_t>(p[2]), static_cast<uint32_t>(p[2] >> 32),
-                                                                          static_cast<uint32_t>(p[3]), static_cast<uint32_t>(p[3] >> 32));
-                                   });
+                    auto put = [&](int j, const uint64_t (&p)[4]) {
+                        dst[(2 * j) * 32] = make_uint4(static_cast<uint32_t>(p[0]), static_cast<uint32_t>(p[0] >> 32),
+                                                       static_cast<uint32_t>(p[1]), static_cast<uint32_t>(p[1] >> 32));
+                        dst[(2 * j + 1) * 32] = make_uint4(static_cast<uint32_t>(p[2]), static_cast<uint32_t>(p[2] >> 32),
+                                                           static_cast<uint32_t>(p[3]), static_cast<uint32_t>(p[3] >> 32));
+                    };
+                    if (c.half)
+                        group_products<true>(ra[r], ra[r], e4p, act0 + g * 64, cs0 + g * 4 * kCsEntry, lane, c.zero, put);
+                    else
+                        group_products<false>(ra[r], rb[r], e4p, act0 + g * 64, cs0 + g * 4 * kCsEntry, lane, c.zero, put);
                     __syncwarp();   // (the scale pairs are rewritten by the next group)
                 }
                 bar_arrive_n(kBarFull + slot, kFanThreads);
-                load(slot);
+                load(r);
+                ++item;
+                if (++ck == nch) {
+                    ck = 0;
+                    c_ok = get(++ci, U);
+                }
             }
         }
         // the chain warp's last two arrivals on EMPTY, consumed
         for (int j = item - 2; j < item; ++j)
             if (j >= 0) bar_sync_n(kBarEmpty + (j & 1), kFanThreads);
     } else {
+        // chain warp h (0: tile A, 1: tile B) adds its tile's products (slot elements 2 j + h); tile B's sums go to
+        // tile A's warp through shared memory, which runs the epilogue
         prelude();
+        const int h = warp - kFanProducers;
         int item = 0;
         GemvUnit U;
         for (int i = 0; get(i, U); ++i) {
-            uint64_t acc[4] = {0, 0, 0, 0};
+            uint64_t acc0 = 0, acc1 = 0;
 #pragma unroll 1
             for (int k = 0; k < nch; ++k, ++item) {
                 const int slot = item & 1;
                 bar_sync_n(kBarFull + slot, kFanThreads);
                 const int ng = min(kFanProducers, G - k * kFanProducers);
-                const uint4 *src = reinterpret_cast<const uint4 *>(c.prod + slot * kFanSlotBytes) + lane;
+                // (half units: both chain warps read tile A's element; warp h adds its rows' half of it)
+                const uint4 *src = reinterpret_cast<const uint4 *>(c.prod + slot * kFanSlotBytes) + (c.half ? 0 : h * 32) + lane;
+                // two groups a round, alternating buffers: a group's four loads go out a round before its adds
+                uint4 va[4], vb[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) va[j] = ld_shared_v4(src + (2 * j) * 32);
+                int gl = 0;
 #pragma unroll 1
-                for (int gl = 0; gl < ng; ++gl, src += kFanGroupBytes / 16) {
+                for (; gl + 2 <= ng; gl += 2) {
+                    const uint4 *s1 = src + (gl + 1) * (kFanGroupBytes / 16);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) vb[j] = ld_shared_v4(s1 + (2 * j) * 32);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const uint4 a = ld_shared_v4(src + (2 * j) * 32), b = ld_shared_v4(src + (2 * j + 1) * 32);
-                        acc[0] = f2_add(acc[0], pack2(a.x, a.y));
-                        acc[1] = f2_add(acc[1], pack2(a.z, a.w));
-                        acc[2] = f2_add(acc[2], pack2(b.x, b.y));
-                        acc[3] = f2_add(acc[3], pack2(b.z, b.w));
+                        acc0 = f2_add(acc0, pack2(va[j].x, va[j].y));
+                        acc1 = f2_add(acc1, pack2(va[j].z, va[j].w));
+                    }
+                    if (gl + 2 < ng) {
+                        const uint4 *s2 = src + (gl + 2) * (kFanGroupBytes / 16);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) va[j] = ld_shared_v4(s2 + (2 * j) * 32);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc0 = f2_add(acc0, pack2(vb[j].x, vb[j].y));
+                        acc1 = f2_add(acc1, pack2(vb[j].z, vb[j].w));
+                    }
+                }
+                if (gl < ng) {   // (an odd count: the last group, already loaded)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        acc0 = f2_add(acc0, pack2(va[j].x, va[j].y));
+                        acc1 = f2_add(acc1, pack2(va[j].z, va[j].w));
                     }
                 }
                 bar_arrive_n(kBarEmpty + slot, kFanThreads);
             }
-            // y = acc * global * 1 (engine/src/kernels.cpp:1320)
-            float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
-            float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
+            // y = acc * global * 1 (engine/src/kernels.cpp:1320). (Half units: warp 0 has all of tile A already; warp 1's
+            // identical sums are not needed.)
+            if (h == 1) c.xchg[lane] = make_float4(lo_f(acc0), hi_f(acc0), lo_f(acc1), hi_f(acc1));
+            bar_sync_n(kBarChains, kFanChains * 32);
+            if (h == 0) {
+                const float4 yb = c.xchg[lane];
+                float y0[4] = {lo_f(acc0), hi_f(acc0), lo_f(acc1), hi_f(acc1)};
+                float y1[4] = {yb.x, yb.y, yb.z, yb.w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                y0[q] = __fmul_rn(y0[q], U.g0);
-                y1[q] = __fmul_rn(y1[q], U.g1);
+                for (int q = 0; q < 4; ++q) {
+                    y0[q] = __fmul_rn(y0[q], U.g0);
+                    y1[q] = __fmul_rn(y1[q], U.g1);
+                }
+                epi(U, y0, y1, gid, tig);
             }
-            epi(U, y0, y1, gid, tig);
+            bar_sync_n(kBarChains, kFanChains * 32);   // (the exchange is free for the next unit)
         }
     }
 }
