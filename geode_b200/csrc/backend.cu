@@ -346,11 +346,11 @@ int enqueue_step(gcuda *g, int n) {
             aa.nchunks = g->nchunks;
             const dim3 grid(g->nchunks, s.n_kv_heads);
             if (s.head_dim == 256) {
-                LAUNCH_OK(launch_ex(k_attn_decode<256>, grid, dim3(128), attn_smem_bytes<256>(), g->st, pdl, aa));
+                LAUNCH_OK(launch_ex(k_attn_decode<256>, grid, dim3(kAttnThreads), attn_smem_bytes<256>(), g->st, pdl, aa));
             } else if (s.head_dim == 128) {
-                LAUNCH_OK(launch_ex(k_attn_decode<128>, grid, dim3(128), attn_smem_bytes<128>(), g->st, pdl, aa));
+                LAUNCH_OK(launch_ex(k_attn_decode<128>, grid, dim3(kAttnThreads), attn_smem_bytes<128>(), g->st, pdl, aa));
             } else {
-                LAUNCH_OK(launch_ex(k_attn_decode<64>, grid, dim3(128), attn_smem_bytes<64>(), g->st, pdl, aa));
+                LAUNCH_OK(launch_ex(k_attn_decode<64>, grid, dim3(kAttnThreads), attn_smem_bytes<64>(), g->st, pdl, aa));
             }
             MergeArgs ma{};
             ma.part = g->part;

@@ -386,13 +386,16 @@ __global__ void k_attn_prep(AttnPrepArgs a) {
 }
 
 // Flash-decoding over the int8 cache (the arithmetic of attend / attend_heads, engine/src/model.cpp:3815-4019,
-// regrouped): one CTA per (KV head, chunk of kChunk positions); its rows are the n tokens x G query heads sharing the
-// KV head (<= 32 rows, two m16 tiles). Per sub-chunk of 64 positions: K and V rows widened to f16 in shared memory
-// (int8 is exact in f16), scores Q.K^T on the tensor cores (mma.sync f16, f32 accumulate) times (1/sqrt(hd) *
-// k_scale[p]), causal mask p <= pos + t, an online softmax, P (times v_scale[p], as the reference folds it into the
-// weights) in f16, O += P.V. Partial (O, max, sum) per (token, head, chunk) for k_attn_merge.
+// regrouped): one CTA (kAttnThreads) per (KV head, chunk of kAttnChunk positions); its rows are the n tokens x G query
+// heads sharing the KV head (<= 32 rows, two m16 tiles). The chunk's raw int8 K and V rows arrive kAttnSub positions at
+// a time by 16-byte cp.async copies into two stages (the next sub-chunk in flight while the current one is used), are
+// widened to f16 in shared memory (int8 is exact in f16: byte | 0x6400 - 1152 with the sign bit flipped), and then:
+// scores Q.K^T on the tensor cores (mma.sync f16, f32 accumulate) times (1/sqrt(hd) * k_scale[p]), causal mask
+// p <= pos + t, an online softmax, P (times v_scale[p], as the reference folds it into the weights) in f16, O += P.V.
+// Partial (O, max, sum) per (token, head, chunk) for k_attn_merge.
 constexpr int kAttnSub = 64;
 constexpr int kAttnChunk = 256;
+constexpr int kAttnThreads = 256;   // 8 warps
 
 struct AttnArgs {
     const float *qn;       // [n][nh][hd]
@@ -414,31 +417,87 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_addr(p)));
 }
 
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_addr(p)));
+}
+
+// four int8 (a word) -> two f16 pairs, exactly: (b ^ 0x80) placed under the f16 exponent of 1024 gives 1024 + b + 128
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t &lo, uint32_t &hi) {
+    const uint32_t x = w ^ 0x80808080u;
+    lo = __byte_perm(x, 0x64646464u, 0x5140);
+    hi = __byte_perm(x, 0x64646464u, 0x7362);
+    const __half2 off = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));   // 1152
+    const __half2 l = __hsub2(*reinterpret_cast<__half2 *>(&lo), off), h = __hsub2(*reinterpret_cast<__half2 *>(&hi), off);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+}
+
 template <int HD>
-__global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
-    constexpr int QS = HD + 8;            // f16 row stride (elements) of Q, K, V tiles
-    constexpr int PS = kAttnSub + 8;
-    constexpr int NT_O = HD / 32;         // O n-tiles (8 dims) per warp
+struct AttnSmem {
+    static constexpr int QS = HD + 8;   // f16 row stride (elements) of Q, K, V tiles
+    static constexpr int PS = kAttnSub + 8;
+    static constexpr size_t q = 0;
+    static constexpr size_t k = q + 32 * QS * 2;
+    static constexpr size_t v = k + kAttnSub * QS * 2;
+    static constexpr size_t pm = v + kAttnSub * QS * 2;
+    static constexpr size_t sc = pm + 32 * PS * 2;                 // scores [32][kAttnSub] f32
+    static constexpr size_t raw = sc + 32 * kAttnSub * 4;          // [2 stages][K, V][kAttnSub][HD] int8
+    static constexpr size_t scl = raw + 2 * 2 * kAttnSub * HD;     // [2 stages][K, V][kAttnSub] f32
+    static constexpr size_t rows = scl + 2 * 2 * kAttnSub * 4;     // row_m, row_l, row_f [32] each
+    static constexpr size_t total = rows + 3 * 32 * 4;
+};
+template <int HD>
+constexpr size_t attn_smem_bytes() { return AttnSmem<HD>::total; }
+
+template <int HD>
+__global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
+    using L = AttnSmem<HD>;
+    constexpr int QS = L::QS, PS = L::PS;
+    constexpr int NT_O = HD / 64;         // O n-tiles (8 dims) per warp: 8 warps x HD/8 dims
     extern __shared__ __align__(16) uint8_t sm[];
-    __half *Qs = reinterpret_cast<__half *>(sm);
-    __half *Ks = Qs + 32 * QS;
-    __half *Vs = Ks + kAttnSub * QS;
-    __half *Ps = Vs + kAttnSub * QS;
-    float *Ss = reinterpret_cast<float *>(Ps + 32 * PS);
-    float *row_m = Ss + 32 * kAttnSub;
+    __half *Qs = reinterpret_cast<__half *>(sm + L::q);
+    __half *Ks = reinterpret_cast<__half *>(sm + L::k);
+    __half *Vs = reinterpret_cast<__half *>(sm + L::v);
+    __half *Ps = reinterpret_cast<__half *>(sm + L::pm);
+    float *Ss = reinterpret_cast<float *>(sm + L::sc);
+    int8_t *raw = reinterpret_cast<int8_t *>(sm + L::raw);
+    float *scl = reinterpret_cast<float *>(sm + L::scl);
+    float *row_m = reinterpret_cast<float *>(sm + L::rows);
     float *row_l = row_m + 32;
     float *row_f = row_l + 32;
-    float *ksc = row_f + 32;
-    float *vsc = ksc + kAttnSub;
-    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
     const int kh = blockIdx.y, chunk = blockIdx.x;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int G = a.nh / a.nkv, rows = a.n * G;
     const int pos = *a.pos, plim = pos + a.n;   // positions < plim exist
     const int c0 = chunk * kAttnChunk;
     if (c0 >= plim) return;
+    const int c1 = min(c0 + kAttnChunk, plim);
+    // sub-chunk s0's raw rows and scales into stage st (positions >= plim: not copied; widened as zeros below)
+    auto fetch = [&](int s0, int st) {
+        constexpr int pieces = HD / 16;   // 16-byte pieces of a row
+        int8_t *rk = raw + (st * 2 + 0) * kAttnSub * HD, *rv = raw + (st * 2 + 1) * kAttnSub * HD;
+        for (int i = tid; i < kAttnSub * pieces; i += kAttnThreads) {
+            const int p = i / pieces, c = i % pieces, gp = s0 + p;
+            if (gp < plim) {
+                const size_t off = (static_cast<size_t>(gp) * a.nkv + kh) * HD + 16 * c;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(rk + p * HD + 16 * c)), "l"(a.kc + off) : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(rv + p * HD + 16 * c)), "l"(a.vc + off) : "memory");
+            }
+        }
+        if (tid < 2 * kAttnSub) {
+            const int which = tid / kAttnSub, p = tid % kAttnSub, gp = s0 + p;
+            if (gp < plim)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(scl + (st * 2 + which) * kAttnSub + p)),
+                             "l"((which ? a.vs : a.ks) + static_cast<size_t>(gp) * a.nkv + kh) : "memory");
+            else
+                scl[(st * 2 + which) * kAttnSub + p] = 0.0f;   // (masked positions: finite scales)
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch(c0, 0);
     // Q rows r = t * G + g -> f16
-    for (int i = tid; i < 32 * HD; i += blockDim.x) {
+    for (int i = tid; i < 32 * HD; i += kAttnThreads) {
         const int r = i / HD, d = i % HD;
         float q = 0.0f;
         if (r < rows) q = a.qn[(static_cast<size_t>(r / G) * a.nh + kh * G + r % G) * HD + d];
@@ -455,69 +514,78 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
         for (int j = 0; j < NT_O; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) o[m][j][e] = 0.0f;
-    for (int s0 = c0; s0 < min(c0 + kAttnChunk, plim); s0 += kAttnSub) {
-        __syncthreads();
-        // K, V rows of the sub-chunk -> f16 (zeros past the end)
-        for (int i = tid; i < kAttnSub * HD / 4; i += blockDim.x) {
-            const int p = i / (HD / 4), d4 = (i % (HD / 4)) * 4, gp = s0 + p;
-            char4 kv = make_char4(0, 0, 0, 0), vv = make_char4(0, 0, 0, 0);
-            if (gp < plim) {
-                kv = *reinterpret_cast<const char4 *>(a.kc + (static_cast<size_t>(gp) * a.nkv + kh) * HD + d4);
-                vv = *reinterpret_cast<const char4 *>(a.vc + (static_cast<size_t>(gp) * a.nkv + kh) * HD + d4);
+    int st = 0;
+    for (int s0 = c0; s0 < c1; s0 += kAttnSub, st ^= 1) {
+        const bool more = s0 + kAttnSub < c1;
+        if (more) fetch(s0 + kAttnSub, st ^ 1);
+        if (more) asm volatile("cp.async.wait_group 1;" ::: "memory");
+        else asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();   // every thread's copies of this sub-chunk landed; the previous sub-chunk's tiles are free
+        {   // widen: 16 int8 of a row per item
+            const int8_t *rk = raw + (st * 2 + 0) * kAttnSub * HD, *rv = raw + (st * 2 + 1) * kAttnSub * HD;
+            for (int i = tid; i < kAttnSub * HD / 16; i += kAttnThreads) {
+                const int p = i / (HD / 16), c = (i % (HD / 16)) * 16;
+                uint4 kw = make_uint4(0, 0, 0, 0), vw = kw;
+                if (s0 + p < plim) {
+                    kw = *reinterpret_cast<const uint4 *>(rk + p * HD + c);
+                    vw = *reinterpret_cast<const uint4 *>(rv + p * HD + c);
+                }
+                uint4 k0, k1, v0, v1;
+                i8x4_to_h2x2(kw.x, k0.x, k0.y);
+                i8x4_to_h2x2(kw.y, k0.z, k0.w);
+                i8x4_to_h2x2(kw.z, k1.x, k1.y);
+                i8x4_to_h2x2(kw.w, k1.z, k1.w);
+                i8x4_to_h2x2(vw.x, v0.x, v0.y);
+                i8x4_to_h2x2(vw.y, v0.z, v0.w);
+                i8x4_to_h2x2(vw.z, v1.x, v1.y);
+                i8x4_to_h2x2(vw.w, v1.z, v1.w);
+                *reinterpret_cast<uint4 *>(Ks + p * QS + c) = k0;
+                *reinterpret_cast<uint4 *>(Ks + p * QS + c + 8) = k1;
+                *reinterpret_cast<uint4 *>(Vs + p * QS + c) = v0;
+                *reinterpret_cast<uint4 *>(Vs + p * QS + c + 8) = v1;
             }
-            __half2 *kd = reinterpret_cast<__half2 *>(Ks + p * QS + d4);
-            __half2 *vd = reinterpret_cast<__half2 *>(Vs + p * QS + d4);
-            kd[0] = __halves2half2(__int2half_rn(kv.x), __int2half_rn(kv.y));
-            kd[1] = __halves2half2(__int2half_rn(kv.z), __int2half_rn(kv.w));
-            vd[0] = __halves2half2(__int2half_rn(vv.x), __int2half_rn(vv.y));
-            vd[1] = __halves2half2(__int2half_rn(vv.z), __int2half_rn(vv.w));
         }
-        if (tid < kAttnSub) {
-            const int gp = s0 + tid;
-            ksc[tid] = gp < plim ? a.ks[static_cast<size_t>(gp) * a.nkv + kh] : 0.0f;
-            vsc[tid] = gp < plim ? a.vs[static_cast<size_t>(gp) * a.nkv + kh] : 0.0f;
-        }
+        const float *ksc = scl + (st * 2 + 0) * kAttnSub, *vsc = scl + (st * 2 + 1) * kAttnSub;
         __syncthreads();
-        // S = Q K^T: warp w -> positions 16 w .. 16 w + 15 (two n8 tiles), both m tiles
+        // S = Q K^T: warp w -> positions 8 w .. 8 w + 7 (one n8 tile), both m tiles
         {
-            float sacc[2][2][4] = {};
+            float sacc[2][4] = {};
 #pragma unroll
-            for (int kk = 0; kk < HD / 16; ++kk) {
+            for (int kk = 0; kk < HD / 32; ++kk) {
+                // B: rows = positions (n), k contiguous: matrices (n 0-7, k 0-7), (n 0-7, k 8-15) for two k-steps
                 uint32_t bq[4];
-                // B: rows = positions (n), k contiguous: matrices (n 0-7,k 0-7), (n 0-7,k 8-15), (n 8-15,k 0-7), (n 8-15,k 8-15)
                 {
                     const int mi = lane >> 3, rr = lane & 7;
-                    const int n = 16 * warp + rr + 8 * (mi >> 1), k = 16 * kk + 8 * (mi & 1);
-                    ldsm_x4(bq, Ks + n * QS + k);
+                    ldsm_x4(bq, Ks + (8 * warp + rr) * QS + 32 * kk + 8 * mi);
                 }
 #pragma unroll
-                for (int m = 0; m < 2; ++m) {
-                    uint32_t aq[4];
-                    const int mi = lane >> 3, rr = lane & 7;
-                    const int r = 16 * m + rr + 8 * (mi & 1), k = 16 * kk + 8 * (mi >> 1);
-                    ldsm_x4(aq, Qs + r * QS + k);
-                    const uint32_t b0[2] = {bq[0], bq[1]}, b1[2] = {bq[2], bq[3]};
-                    mma_f16_16816(sacc[m][0], aq, b0);
-                    mma_f16_16816(sacc[m][1], aq, b1);
-                }
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int m = 0; m < 2; ++m) {
+                        uint32_t aq[4];
+                        const int mi = lane >> 3, rr = lane & 7;
+                        const int r = 16 * m + rr + 8 * (mi & 1), k = 32 * kk + 16 * h + 8 * (mi >> 1);
+                        ldsm_x4(aq, Qs + r * QS + k);
+                        const uint32_t b[2] = {bq[2 * h], bq[2 * h + 1]};
+                        mma_f16_16816(sacc[m], aq, b);
+                    }
             }
 #pragma unroll
             for (int m = 0; m < 2; ++m)
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int r = 16 * m + gid + 8 * (e >> 1), c = 16 * warp + 8 * nt + 2 * tig + (e & 1);
-                        const int gp = s0 + c, t = r / G;
-                        float v = __fmul_rn(sacc[m][nt][e], __fmul_rn(a.scale, ksc[c]));
-                        if (r >= rows || gp > pos + t) v = -INFINITY;
-                        Ss[r * kAttnSub + c] = v;
-                    }
+                for (int e = 0; e < 4; ++e) {
+                    const int r = 16 * m + gid + 8 * (e >> 1), c = 8 * warp + 2 * tig + (e & 1);
+                    const int gp = s0 + c, t = r / G;
+                    float v = __fmul_rn(sacc[m][e], __fmul_rn(a.scale, ksc[c]));
+                    if (r >= rows || gp > pos + t || gp >= plim) v = -INFINITY;
+                    Ss[r * kAttnSub + c] = v;
+                }
         }
         __syncthreads();
-        // online softmax: warp w -> rows 8 w .. 8 w + 7, lanes over 64 columns (2 each)
-        for (int rr = 0; rr < 8; ++rr) {
-            const int r = 8 * warp + rr;
+        // online softmax: warp w -> rows 4 w .. 4 w + 3, lanes over 64 columns (2 each)
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+            const int r = 4 * warp + rr;
             const float s_a = Ss[r * kAttnSub + lane], s_b = Ss[r * kAttnSub + lane + 32];
             const float mx = warp_max(fmaxf(s_a, s_b));
             const float m_old = row_m[r], m_new = fmaxf(m_old, mx);
@@ -528,7 +596,6 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
             const float f = m_old == -INFINITY ? 0.0f : __expf(m_old - m_new);
             Ps[r * PS + lane] = __float2half_rn(__fmul_rn(ea, vsc[lane]));
             Ps[r * PS + lane + 32] = __float2half_rn(__fmul_rn(eb, vsc[lane + 32]));
-            __syncwarp();
             if (lane == 0) {
                 row_l[r] = __fadd_rn(__fmul_rn(row_l[r], f), sum);
                 row_m[r] = m_new;
@@ -536,7 +603,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
             }
         }
         __syncthreads();
-        // O = O * f + P V: warp w -> dims [w * HD/4, (w+1) * HD/4)
+        // O = O * f + P V: warp w -> dims [w * HD/8, (w+1) * HD/8)
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
             const float f0 = row_f[16 * m + gid], f1 = row_f[16 * m + gid + 8];
@@ -557,19 +624,28 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
                 const int r = 16 * m + rr + 8 * (mi & 1), k = 16 * kk + 8 * (mi >> 1);
                 ldsm_x4(ap[m], Ps + r * PS + k);
             }
+            if constexpr (NT_O == 1) {
+                // one n tile per warp: matrices (k 0-7, the tile), (k 8-15, the tile)
+                uint32_t bv[2];
+                const int mi = (lane >> 3) & 1, rr = lane & 7;
+                ldsm_x2_t(bv, Vs + (16 * kk + rr + 8 * mi) * QS + warp * (HD / 8));
 #pragma unroll
-            for (int j = 0; j < NT_O; j += 2) {
-                // V rows = k (positions), dims = n: .trans gives the col-major fragments; matrices (k 0-7, n tile j),
-                // (k 8-15, tile j), (k 0-7, tile j+1), (k 8-15, tile j+1)
-                uint32_t bv[4];
-                const int mi = lane >> 3, rr = lane & 7;
-                const int k = 16 * kk + rr + 8 * (mi & 1), n = warp * (HD / 4) + 8 * (j + (mi >> 1));
-                ldsm_x4_t(bv, Vs + k * QS + n);
-                const uint32_t b0[2] = {bv[0], bv[1]}, b1[2] = {bv[2], bv[3]};
+                for (int m = 0; m < 2; ++m) mma_f16_16816(o[m][0], ap[m], bv);
+            } else {
 #pragma unroll
-                for (int m = 0; m < 2; ++m) {
-                    mma_f16_16816(o[m][j], ap[m], b0);
-                    mma_f16_16816(o[m][j + 1], ap[m], b1);
+                for (int j = 0; j < NT_O; j += 2) {
+                    // V rows = k (positions), dims = n: .trans gives the col-major fragments; matrices (k 0-7, n tile j),
+                    // (k 8-15, tile j), (k 0-7, tile j+1), (k 8-15, tile j+1)
+                    uint32_t bv[4];
+                    const int mi = lane >> 3, rr = lane & 7;
+                    const int k = 16 * kk + rr + 8 * (mi & 1), n = warp * (HD / 8) + 8 * (j + (mi >> 1));
+                    ldsm_x4_t(bv, Vs + k * QS + n);
+                    const uint32_t b0[2] = {bv[0], bv[1]}, b1[2] = {bv[2], bv[3]};
+#pragma unroll
+                    for (int m = 0; m < 2; ++m) {
+                        mma_f16_16816(o[m][j], ap[m], b0);
+                        mma_f16_16816(o[m][j + 1], ap[m], b1);
+                    }
                 }
             }
         }
@@ -585,7 +661,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
             for (int e = 0; e < 4; ++e) {
                 const int r = 16 * m + gid + 8 * (e >> 1);
                 if (r >= rows) continue;
-                const int d = warp * (HD / 4) + 8 * j + 2 * tig + (e & 1);
+                const int d = warp * (HD / 8) + 8 * j + 2 * tig + (e & 1);
                 const int t = r / G, h = kh * G + r % G;
                 a.part[((static_cast<size_t>(t) * a.nh + h) * a.nchunks + chunk) * pstride + d] = o[m][j][e];
             }
@@ -595,11 +671,6 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a) {
         pp[HD] = row_m[tid];
         pp[HD + 1] = row_l[tid];
     }
-}
-
-template <int HD>
-constexpr size_t attn_smem_bytes() {
-    return (32 * (HD + 8) + 2 * kAttnSub * (HD + 8) + 32 * (kAttnSub + 8)) * 2 + (32 * kAttnSub + 3 * 32 + 2 * kAttnSub) * 4;
 }
 
 // The chunks joined (engine/src/model.cpp:3832-3853): M = max m_c, O = sum O_c exp(m_c - M), L = sum l_c exp(m_c - M),
