@@ -107,6 +107,7 @@ __device__ void row_topk(const float *__restrict__ row, int V, int k, float *cv,
 // key (order-preserving value bits, then the complement of the index: the largest value, the lowest index first).
 __global__ void k_argmax_partial(const float *__restrict__ logits, int V, unsigned long long *best) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int r = blockIdx.y;
     const float *row = logits + static_cast<size_t>(r) * V;
     const int per = (V + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(V, lo + per);
@@ -149,6 +150,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_rows(SampleArgs a) {
     __shared__ int misc[4];
     __shared__ double ev[kMaxCand];
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int r = blockIdx.x;
     const float *row = a.logits + static_cast<size_t>(r) * a.V;
     const int tid = threadIdx.x;

@@ -19,6 +19,7 @@ namespace cg = cooperative_groups;
 __global__ void k_embed(const uint8_t *__restrict__ table, int64_t vocab, int H, float global, const int *__restrict__ toks,
                         int n, float *__restrict__ x, uint32_t *status) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const size_t rb = static_cast<size_t>(H / 16) * 9;
     const int t = blockIdx.y;
     if (t >= n) return;
@@ -97,6 +98,7 @@ struct NormArgs {
 
 __global__ void k_norm_quant(NormArgs a) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int t = blockIdx.x;
     if (t >= a.n) return;
     float *xr = a.x + static_cast<size_t>(t) * a.H;
@@ -160,6 +162,7 @@ struct GdnArgs {
 // heads, so the state may change only after every reader has read it.)
 __global__ void k_gdn_conv(GdnArgs a, int conv_dim, float *__restrict__ out) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= conv_dim) return;
     const int K = a.K;
@@ -186,6 +189,7 @@ __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     __shared__ float s_q[kMaxTok][DK], s_k[kMaxTok][DK], s_v[kMaxTok][16], s_o[kMaxTok][16];
     __shared__ float s_beta[kMaxTok], s_decay[kMaxTok], s_ss[kMaxTok], s_red[kMaxTok][4];
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     cg::cluster_group cluster = cg::this_cluster();
     const int S = a.dv / 16;
     const int vh = blockIdx.x / S, s = blockIdx.x % S;
@@ -331,6 +335,7 @@ struct AttnPrepArgs {
 __global__ void k_attn_prep(AttnPrepArgs a) {
     extern __shared__ float sv[];   // per warp hd floats
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     const int per = a.nh + 2 * a.nkv;
     const int p0 = *a.pos;
@@ -468,6 +473,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tig = lane & 3;
     const int kh = blockIdx.y, chunk = blockIdx.x;
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int G = a.nh / a.nkv, rows = a.n * G;
     const int pos = *a.pos, plim = pos + a.n;   // positions < plim exist
     const int c0 = chunk * kAttnChunk;
@@ -692,6 +698,7 @@ __global__ void k_attn_merge(MergeArgs a) {
     extern __shared__ float s_f[];
     __shared__ float s_red[32];
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int pos = *a.pos;
     const int W = a.nh * a.hd;
@@ -768,6 +775,7 @@ __global__ void k_route(const float *__restrict__ logits, int n, int E, int K, R
     extern __shared__ float ps[];   // E floats per warp
     __shared__ int s_ids[kMaxTok * 8], s_first[kMaxTok * 8], s_rank[kMaxTok * 8];
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < n) {
         route_row(logits + static_cast<size_t>(warp) * (E + 1), E, K, ps + warp * E, out->ids + warp * K, out->w + warp * K);
@@ -885,6 +893,7 @@ struct StepState {
 __global__ void k_decide(const int *samples, int *toks, int n, int *pos, StepState *ss) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     int k = 1, nx = samples[n - 1];
     for (int i = 0; i < n; ++i) {
         if (i + 1 < n && samples[i] == toks[i + 1]) {
@@ -905,6 +914,7 @@ __global__ void k_decide(const int *samples, int *toks, int n, int *pos, StepSta
 __global__ void k_rollback(float *conv, const float *conv_bk, size_t conv_n, float *gdn, const float *gdn_bk, size_t gdn_n,
                            int n, const StepState *ss) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int kept = ss->kept;
     if (kept >= n) return;
     const size_t b = static_cast<size_t>(kept - 1);

@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__
         bulk_g2s(ws, w + static_cast<size_t>(r0) * cols, bytes, bar);
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
     const int xs_stride = cols + 8;
     {   // (loads issued in batches before their stores: one round trip per batch, not per load)
         constexpr int kB = 8;
@@ -102,7 +103,6 @@ __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__
         }
     }
     if (!landed) mbar_wait_bounded(bar, 0, nullptr);   // (the copy may still land: not before the CTA ends)
-    asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // route_topk (engine/src/model.cpp:4021-4065) for one token row, by one warp: softmax (max, exp, a float sum in
