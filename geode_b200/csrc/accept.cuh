@@ -214,4 +214,234 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_rows(SampleArgs a) {
     }
 }
 
+// ------------------------------------------------------------------------------------------- rejection sampling ----
+// Speculative sampling (Leviathan et al. 2023, Algorithm 1; Chen et al. 2023) for the draft-model configurations
+// (not in the reference, which only has the greedy/sampled acceptance rule above): draft d_i stands when
+// u_i * q(d_i) < p(d_i); the first rejection resamples from norm(max(0, p - q)); with every draft standing, a bonus
+// token from the last target row. p and q are the rows' filtered distributions (top-k, 1024 when off, by logit with
+// ties to the lower id; weights fast_exp((l - max) * (1/T)) summed in double in logit order; the top-p prefix;
+// probabilities w / kept). Uniforms: Philox4x32-10 (Salmon et al. 2011), key = seed, counter = (sequence, row);
+// words 0-1 the acceptance draw, 2-3 the resample draw, each 53 bits. Resampling walks the support in ascending
+// token id. One CTA (kSampleThreads) per sequence; the sums run on one thread in their fixed order.
+__device__ inline void philox4x32(uint64_t key, uint64_t hi, uint64_t lo, uint32_t (&out)[4]) {
+    uint32_t c0 = static_cast<uint32_t>(lo), c1 = static_cast<uint32_t>(lo >> 32), c2 = static_cast<uint32_t>(hi),
+             c3 = static_cast<uint32_t>(hi >> 32);
+    uint32_t k0 = static_cast<uint32_t>(key), k1 = static_cast<uint32_t>(key >> 32);
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint64_t p0 = 0xD2511F53ull * c0, p1 = 0xCD9E8D57ull * c2;
+        const uint32_t n0 = static_cast<uint32_t>(p1 >> 32) ^ c1 ^ k0, n2 = static_cast<uint32_t>(p0 >> 32) ^ c3 ^ k1;
+        c1 = static_cast<uint32_t>(p1);
+        c3 = static_cast<uint32_t>(p0);
+        c0 = n0;
+        c2 = n2;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    out[0] = c0, out[1] = c1, out[2] = c2, out[3] = c3;
+}
+__device__ __forceinline__ double u53(uint32_t a, uint32_t b) {
+    return static_cast<double>((static_cast<uint64_t>(a) << 21) ^ (static_cast<uint64_t>(b) >> 11)) * (1.0 / 9007199254740992.0);
+}
+
+// (id, value) pairs of n <= kMaxCand by ascending id, in place (bitonic; the padding after n sorts last)
+__device__ void sort_by_id(int *ids, double *vals, int n) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < kMaxCand; i += blockDim.x)
+        if (i >= n) {
+            ids[i] = 0x7fffffff;
+            vals[i] = 0.0;
+        }
+    __syncthreads();
+    for (int size = 2; size <= kMaxCand; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < kMaxCand; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i && ((ids[i] > ids[j]) == ((i & size) == 0))) {
+                    const int ti = ids[i];
+                    ids[i] = ids[j];
+                    ids[j] = ti;
+                    const double tv = vals[i];
+                    vals[i] = vals[j];
+                    vals[j] = tv;
+                }
+            }
+            __syncthreads();
+        }
+}
+
+struct RejectArgs {
+    const float *target;   // [S][k+1][V]
+    const float *draft;    // [S][k][V]
+    const int *drafts;     // [S][k]
+    int k, V;
+    float temperature, top_p;
+    int top_k;
+    uint64_t seed;
+    int *accepted, *next;  // [S]
+};
+
+__global__ void __launch_bounds__(kSampleThreads) k_spec_reject(RejectArgs a) {
+    __shared__ float cv[kMaxCand];
+    __shared__ int ci[kMaxCand];
+    __shared__ uint32_t hist[256];
+    __shared__ int misc[4];
+    __shared__ int pid[kMaxCand], qid[kMaxCand];
+    __shared__ double pp[kMaxCand], qp[kMaxCand];
+    __shared__ int s_np, s_nq, s_acc, s_best;
+    __shared__ double s_pd, s_qd, s_ua, s_ur, s_kept;
+    const int tid = threadIdx.x, seq = blockIdx.x;
+    const int kk = min(a.V, a.top_k > 0 ? a.top_k : kMaxCand);
+    const float it = __fdiv_rn(1.0f, a.temperature);
+    // the filtered distribution of one row into (ids, probs) in logit order; returns the kept count
+    auto filtered = [&](const float *row, int *ids, double *probs) -> int {
+        row_topk(row, a.V, kk, cv, ci, hist, misc);
+        const float mx = cv[0];
+        for (int i = tid; i < kk; i += blockDim.x) probs[i] = static_cast<double>(fast_exp_exact(__fmul_rn(__fsub_rn(cv[i], mx), it)));
+        __syncthreads();
+        if (tid == 0) {
+            double sum = 0.0;
+            for (int i = 0; i < kk; ++i) sum += probs[i];
+            int keep = kk;
+            if (a.top_p < 1.0f) {
+                double acc = 0.0;
+                for (int i = 0; i < kk; ++i) {
+                    acc += probs[i] / sum;
+                    if (acc >= static_cast<double>(a.top_p)) {
+                        keep = i + 1;
+                        break;
+                    }
+                }
+            }
+            double kept = 0.0;
+            for (int i = 0; i < keep; ++i) kept += probs[i];
+            misc[3] = keep;
+            s_kept = kept;
+        }
+        __syncthreads();
+        const int keep = misc[3];
+        const double kept = s_kept;
+        for (int i = tid; i < keep; i += blockDim.x) {
+            ids[i] = ci[i];
+            probs[i] = probs[i] / kept;
+        }
+        __syncthreads();
+        return keep;
+    };
+    // the probability of token tok in a support sorted by id (0 when absent)
+    auto lookup = [&](const int *ids, const double *probs, int n, int tok) -> double {
+        int lo = 0, hi = n - 1;
+        while (lo <= hi) {
+            const int mid = (lo + hi) >> 1;
+            if (ids[mid] == tok) return probs[mid];
+            if (ids[mid] < tok) lo = mid + 1;
+            else hi = mid - 1;
+        }
+        return 0.0;
+    };
+    int accepted = 0, best = -1;
+    for (int i = 0; i <= a.k; ++i) {
+        if (tid == 0) {
+            uint32_t r[4];
+            philox4x32(a.seed, static_cast<uint64_t>(seq), static_cast<uint64_t>(i), r);
+            s_ua = u53(r[0], r[1]);
+            s_ur = u53(r[2], r[3]);
+        }
+        __syncthreads();
+        const double ua = s_ua, ur = s_ur;
+        __syncthreads();
+        const int np = filtered(a.target + (static_cast<size_t>(seq) * (a.k + 1) + i) * a.V, pid, pp);
+        if (i == a.k) {   // every draft stood: the bonus token from the target row
+            if (tid == 0) {
+                double total = 0.0;
+                for (int j = 0; j < np; ++j) total += pp[j];
+                s_qd = total;
+            }
+            sort_by_id(pid, pp, np);
+            if (tid == 0) {
+                const double lim = ur * s_qd;
+                double acc = 0.0;
+                int b = -1;
+                for (int j = 0; j < np; ++j) {
+                    if (pp[j] <= 0.0) continue;
+                    acc += pp[j];
+                    b = pid[j];
+                    if (acc > lim) break;
+                }
+                s_best = b;
+            }
+            __syncthreads();
+            best = s_best;
+            break;
+        }
+        const int nq = filtered(a.draft + (static_cast<size_t>(seq) * a.k + i) * a.V, qid, qp);
+        const int d = a.drafts[static_cast<size_t>(seq) * a.k + i];
+        if (tid == 0) s_pd = s_qd = 0.0;
+        __syncthreads();
+        for (int j = tid; j < np; j += blockDim.x)
+            if (pid[j] == d) s_pd = pp[j];
+        for (int j = tid; j < nq; j += blockDim.x)
+            if (qid[j] == d) s_qd = qp[j];
+        __syncthreads();
+        if (tid == 0) s_acc = s_qd > 0.0 && ua * s_qd < s_pd;
+        __syncthreads();
+        if (s_acc) {
+            ++accepted;
+            continue;
+        }
+        // the residual max(0, p - q) over p's support: its total in p's (logit) order, then the walk by id. pp is
+        // overwritten with rv = p - q (p itself is read again only when the residual is empty)
+        sort_by_id(qid, qp, nq);
+        for (int j = tid; j < np; j += blockDim.x) pp[j] = pp[j] - lookup(qid, qp, nq, pid[j]);
+        __syncthreads();
+        if (tid == 0) {
+            double total = 0.0;
+            for (int j = 0; j < np; ++j)
+                if (pp[j] > 0.0) total += pp[j];
+            s_pd = total;
+        }
+        __syncthreads();
+        const double total = s_pd;
+        sort_by_id(pid, pp, np);   // (rv by ascending id)
+        if (tid == 0) {
+            int b = -1;
+            double acc = 0.0;
+            if (total > 0.0) {
+                const double lim = ur * total;
+                for (int j = 0; j < np; ++j) {
+                    if (pp[j] <= 0.0) continue;
+                    acc += pp[j];
+                    b = pid[j];
+                    if (acc > lim) break;
+                }
+            }
+            s_best = b;
+        }
+        __syncthreads();
+        best = s_best;
+        if (total <= 0.0) {   // p == q on the support: sample from p itself, by id
+            const int np2 = filtered(a.target + (static_cast<size_t>(seq) * (a.k + 1) + i) * a.V, pid, pp);
+            sort_by_id(pid, pp, np2);
+            if (tid == 0) {
+                double acc = 0.0;
+                int b = -1;
+                for (int j = 0; j < np2; ++j) {
+                    if (pp[j] <= 0.0) continue;
+                    acc += pp[j];
+                    b = pid[j];
+                    if (acc > ur) break;
+                }
+                s_best = b;
+            }
+            __syncthreads();
+            best = s_best;
+        }
+        break;
+    }
+    if (tid == 0) {
+        a.accepted[seq] = accepted;
+        a.next[seq] = best;
+    }
+}
+
 }  // namespace gcu

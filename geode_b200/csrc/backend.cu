@@ -97,6 +97,8 @@ struct gcuda {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     float last_ms = 0.0f;
     bool pdl = true;
+    int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
+    size_t rej_cap = 0;
     std::vector<void *> allocs;
 };
 
@@ -526,6 +528,7 @@ void gcuda_close(gcuda *g) {
         if (x.scales) cudaFree(x.scales);
     }
     for (void *p : g->allocs) cudaFree(p);
+    if (g->rej) cudaFree(g->rej);
     if (g->ev0) cudaEventDestroy(g->ev0);
     if (g->ev1) cudaEventDestroy(g->ev1);
     if (g->st) cudaStreamDestroy(g->st);
@@ -816,6 +819,42 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
     RC_OK(gcuda_verify_device(g, g->d_toks, n));
     if (logits) LAUNCH_OK(cudaMemcpyAsync(logits, g->logits, sizeof(float) * n * g->sh.vocab, cudaMemcpyDeviceToHost, g->st));
     if (hidden) LAUNCH_OK(cudaMemcpyAsync(hidden, g->hid, sizeof(float) * n * g->sh.hidden, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    return GCUDA_OK;
+}
+
+int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, const int *drafts, int S, int k, int V,
+                      const gcuda_sampling *sp, uint64_t seed, int *accepted, int *next) {
+    if (!g) return GCUDA_E_ARG;
+    if (!d_target || !d_draft || !drafts || !sp || !accepted || !next || S < 1 || k < 1 || V < 1 || sp->temperature <= 0.0f ||
+        sp->top_k > kMaxCand || !(sp->top_p > 0.0f && sp->top_p <= 1.0f))
+        return fail(g, GCUDA_E_ARG, "spec_reject: bad arguments");
+    cudaSetDevice(g->device);
+    const size_t need = static_cast<size_t>(S) * (k + 2);
+    if (need > g->rej_cap) {
+        if (g->rej) cudaFree(g->rej);
+        g->rej = nullptr;
+        g->rej_cap = 0;
+        if (cudaMalloc(&g->rej, need * sizeof(int)) != cudaSuccess) return fail(g, GCUDA_E_MEMORY, "spec_reject: cudaMalloc");
+        g->rej_cap = need;
+    }
+    int *d_drafts = g->rej, *d_acc = g->rej + static_cast<size_t>(S) * k, *d_next = d_acc + S;
+    LAUNCH_OK(cudaMemcpyAsync(d_drafts, drafts, sizeof(int) * S * k, cudaMemcpyHostToDevice, g->st));
+    RejectArgs a{};
+    a.target = d_target;
+    a.draft = d_draft;
+    a.drafts = d_drafts;
+    a.k = k;
+    a.V = V;
+    a.temperature = sp->temperature;
+    a.top_p = sp->top_p;
+    a.top_k = sp->top_k;
+    a.seed = seed;
+    a.accepted = d_acc;
+    a.next = d_next;
+    LAUNCH_OK(launch_ex(k_spec_reject, dim3(S), dim3(kSampleThreads), 0, g->st, false, a));
+    LAUNCH_OK(cudaMemcpyAsync(accepted, d_acc, sizeof(int) * S, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(next, d_next, sizeof(int) * S, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
     return GCUDA_OK;
 }

@@ -127,6 +127,39 @@ int gcuda_verify_device(gcuda *g, const int *d_toks, int n);
 float gcuda_last_ms(gcuda *g);
 /* Kernels this library launched since the handle opened. */
 uint64_t gcuda_launches(gcuda *g);
+/* The stream the handle enqueues on (a cudaStream_t), for callers that time it with their own events. */
+void *gcuda_stream(gcuda *g);
+/* The embedding table in the pack's own row layout (rows are gathered, not streamed): an id for gcuda_setup's embed. */
+int gcuda_adopt_embedding(gcuda *g, const uint8_t *data, int64_t rows, int64_t cols, float global);
+
+/* ------------------------------------------------------------------------------------ the device-resident loop ----
+ * The speculative step without host round trips (the drafts are the previous batch's own tokens - a measuring loop):
+ * gcuda_begin_device_loop puts the position and the first batch on the device; each gcuda_step_device(n) enqueues the
+ * verify graph, the greedy acceptance of every row, the decision (kept, next, position += kept) and the rollback;
+ * gcuda_sync_step waits and returns the steps taken, the sum of the routed layers' expert-union sizes and the last
+ * kept count. No counterpart in the reference (its loop is host code, engine/src/geode.cpp:318-370). */
+int gcuda_begin_device_loop(gcuda *g, const int *toks, int n);
+int gcuda_step_device(gcuda *g, int n);
+int gcuda_sync_step(gcuda *g, int *steps, int *union_sum, int *last_kept);
+
+/* ----------------------------------------------------------------------------------------- synthetic models ----
+ * Seeded weights made straight in device memory, for measuring runs whose values do not matter (the self-test
+ * weights of engine/src/gpu_check.cpp:51-63: random q4 codes, E4M3 scale bytes in 0x30..0x48). Each returns an id
+ * like its gcuda_adopt_* counterpart. synth_raw: dtype 0 f32, 1 bf16, values N(mean, stdv). gcuda_state_randomize
+ * fills the KV cache up to pos with random int8 rows (scales 0.5) and the conv and recurrent states with small
+ * random values, and sets the position to pos. */
+int gcuda_synth_q4(gcuda *g, int64_t rows, int64_t cols, float global, uint64_t seed);
+int gcuda_synth_raw(gcuda *g, size_t count, int dtype, float mean, float stdv, uint64_t seed);
+int gcuda_synth_embedding(gcuda *g, int64_t rows, int64_t cols, float global, uint64_t seed);
+int gcuda_synth_experts(gcuda *g, int n, int hidden, int ff, float global, uint64_t seed);
+int gcuda_state_randomize(gcuda *g, int pos, uint64_t seed);
+
+/* ------------------------------------------------------------------------------------------------ test hooks ----
+ * gcuda_debug_read: the device copy of one of the last step's intermediate rows (what: 0 x, 1 hf, 2 core_f,
+ * 3 route, 4 hidden, 5 conv output, 6 a|b, 7 z, 8 qkv product); gcuda_debug_step_eager: the step launched kernel by
+ * kernel instead of through the graph (pdl 0/1). */
+int gcuda_debug_read(gcuda *g, int what, void *out, size_t bytes);
+int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl);
 
 /* ------------------------------------------------------------------------------------------- operators ---- */
 /* All on caller-owned device memory, enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).

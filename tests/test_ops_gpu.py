@@ -123,3 +123,38 @@ def test_route_topk_bit_exact(L, O):
         rid, rw = op.oracle_route_topk(O, lg[t], K)
         assert np.array_equal(ids[t].cpu().numpy(), rid)
         assert np.array_equal(w[t].cpu().numpy().view(np.uint32), rw.view(np.uint32))
+
+
+@pytest.mark.parametrize("temperature,top_p,top_k", [(0.7, 0.95, 20), (1.0, 1.0, 0), (0.5, 0.8, 64)])
+def test_spec_reject_bit_exact(L, O, temperature, top_p, top_k):
+    """Rejection sampling (not in the reference; the oracle restates Leviathan et al.'s algorithm): accepted lengths
+    and next tokens equal the oracle's for every sequence, with Philox uniforms keyed by (seed, sequence, row)."""
+    from geode_b200.backend import GSampling, _sig
+    _sig(L)
+    rng = np.random.default_rng(int(temperature * 100) + top_k)
+    S, k, V = 12, 4, 4096
+    target = (rng.standard_normal((S, k + 1, V)) * 3).astype(np.float32)
+    draft = target[:, :k, :] + (rng.standard_normal((S, k, V)) * 0.3).astype(np.float32)   # a close draft model
+    drafts = np.zeros((S, k), np.int32)
+    for s_ in range(S):   # drafts from the draft rows' argmax, some replaced at random
+        drafts[s_] = np.argmax(draft[s_], axis=1)
+        if s_ % 3 == 1:
+            drafts[s_, s_ % k] = rng.integers(0, V)
+    err = C.create_string_buffer(256)
+    g = L.gcuda_open(0, err, 256)
+    assert g, err.value
+    try:
+        d_t, d_d = _dev(target), _dev(np.ascontiguousarray(draft))
+        acc = np.zeros(S, np.int32)
+        nxt = np.zeros(S, np.int32)
+        sp = GSampling(temperature, top_p, top_k)
+        assert L.gcuda_spec_reject(g, _p(d_t), _p(d_d), drafts.ctypes.data, S, k, V, C.byref(sp), 1234,
+                                   acc.ctypes.data, nxt.ctypes.data) == 0
+    finally:
+        L.gcuda_close(g)
+    for s_ in range(S):
+        n = C.c_int(0)
+        ra = O.go_spec_reject(np.ascontiguousarray(target[s_]).ctypes.data, np.ascontiguousarray(draft[s_]).ctypes.data, k, V,
+                              np.ascontiguousarray(drafts[s_]).ctypes.data, temperature, top_p, top_k, 1234, s_, C.byref(n))
+        assert (acc[s_], nxt[s_]) == (ra, n.value), s_
+    assert len(set(acc.tolist())) > 1   # (sequences stop at different drafts)
