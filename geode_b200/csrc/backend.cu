@@ -14,6 +14,7 @@
 #include "launch.hpp"
 #include "ops_impl.cuh"
 #include "accept.cuh"
+#include "noalloc_impl.cuh"
 
 using namespace gcu;
 

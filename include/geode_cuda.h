@@ -183,6 +183,17 @@ int gcuda_op_bf16_gemv(const uint16_t *d_w, int rows, int cols, const float *d_x
 /* route_topk (engine/src/model.cpp:4021-4065) for n rows of E logits: ids [n][K], weights [n][K] */
 int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, float *d_weights, void *stream);
 
+/* gcuda_spec_reject without a handle and without allocating: for callers that must not allocate device memory when
+ * they call it (a serving loop that holds a fixed device-memory budget, or one that cannot take the implicit
+ * synchronisation of cudaMalloc / cudaFree in its step). Same arguments and results as gcuda_spec_reject (d_target
+ * [S][k+1][V] and d_draft [S][k][V] on the device, drafts [S][k] and accepted[S] / next[S] on the host), on `stream`;
+ * it returns after the results are on the host. Its scratch is a fixed device array of the library, so S <= 1024 and
+ * k <= 16 (GCUDA_E_ARG beyond). The first call on a device looks that array up (cudaGetSymbolAddress, with the
+ * device current): make it before any stream capture. Calls that overlap on one device - from several threads or
+ * streams - share the array and race; serialise them. No counterpart in the reference. */
+int gcuda_op_spec_reject_static(const float *d_target, const float *d_draft, const int *drafts, int S, int k, int V,
+                                const gcuda_sampling *s, uint64_t seed, int *accepted, int *next, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
