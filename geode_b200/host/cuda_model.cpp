@@ -1,0 +1,243 @@
+// cuda_model.cpp - see cuda_model.hpp.
+#include "cuda_model.hpp"
+
+#include <dlfcn.h>
+
+#include <cstring>
+
+namespace ghost {
+
+namespace {
+std::string own_dir() {
+    Dl_info info{};
+    if (dladdr(reinterpret_cast<void *>(&own_dir), &info) && info.dli_fname) {
+        std::string p = info.dli_fname;
+        const size_t s = p.rfind('/');
+        if (s != std::string::npos) return p.substr(0, s);
+    }
+    return ".";
+}
+}  // namespace
+
+bool CudaApi::load(const std::string &path, std::string &err) {
+    const std::string p = path.empty() ? own_dir() + "/libgeode_cuda.so" : path;
+    lib = dlopen(p.c_str(), RTLD_NOW | RTLD_LOCAL);
+    if (!lib) {
+        err = std::string("cannot load the CUDA backend (no CPU fallback): ") + dlerror();
+        return false;
+    }
+    bool ok = true;
+    auto sym = [&](auto &fn, const char *name) {
+        fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(lib, name));
+        if (!fn) {
+            err = std::string("the CUDA backend lacks ") + name;
+            ok = false;
+        }
+    };
+    sym(open, "gcuda_open");
+    sym(close, "gcuda_close");
+    sym(last_error, "gcuda_last_error");
+    sym(adopt_q4, "gcuda_adopt_q4");
+    sym(adopt_raw, "gcuda_adopt_raw");
+    sym(adopt_embedding, "gcuda_adopt_embedding");
+    sym(adopt_experts, "gcuda_adopt_experts");
+    sym(setup, "gcuda_setup");
+    sym(verify, "gcuda_verify");
+    sym(keep, "gcuda_keep");
+    sym(position, "gcuda_position");
+    sym(accept, "gcuda_accept");
+    return ok;
+}
+
+CudaApi::~CudaApi() {
+    if (lib) dlclose(lib);
+}
+
+CudaModel::~CudaModel() {
+    if (g_ && api_.close) api_.close(g_);
+}
+
+bool CudaModel::fail(const char *what, std::string &err) {
+    char buf[512] = {0};
+    if (g_) api_.last_error(g_, buf, sizeof buf);
+    err = std::string(what) + ": " + buf;
+    return false;
+}
+
+int CudaModel::position() const { return g_ ? api_.position(g_) : 0; }
+
+bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::string &err) {
+    if (opt.max_tokens < 1 || opt.max_tokens > 8) {
+        err = "max_tokens: 1 .. 8";
+        return false;
+    }
+    if (!api_.load("", err)) return false;
+    if (!pack_.open(dir, err)) return false;
+    char ebuf[512] = {0};
+    g_ = api_.open(opt.device, ebuf, sizeof ebuf);
+    if (!g_) {
+        err = std::string("gcuda_open: ") + ebuf;
+        return false;
+    }
+    const Json &c = pack_.config();
+    const bool dense = pack_.arch() == "qwen35";
+    const int L = static_cast<int>(c["num_hidden_layers"].integer());
+    std::vector<gcuda_layer> layers(static_cast<size_t>(L));
+    // every tensor into device memory, by the names engine/src/model.cpp:94-203 reads
+    auto q4 = [&](const std::string &name, int &id) -> bool {
+        TensorView t;
+        if (!pack_.tensor(name, t, err)) return false;
+        id = api_.adopt_q4(g_, t.data, t.rows(), t.cols(), static_cast<size_t>(t.cols() / 16) * 9, t.global);
+        return id >= 0 || fail(name.c_str(), err);
+    };
+    auto raw = [&](const std::string &name, int &id) -> bool {
+        TensorView t;
+        if (!pack_.tensor(name, t, err)) return false;
+        id = api_.adopt_raw(g_, t.data, t.bytes);
+        return id >= 0 || fail(name.c_str(), err);
+    };
+    const Json &types = c["layer_types"];
+    for (int l = 0; l < L; ++l) {
+        gcuda_layer &x = layers[static_cast<size_t>(l)];
+        std::memset(&x, 0xFF, sizeof x);   // every id -1
+        const std::string p = "layers." + std::to_string(l) + ".";
+        const bool attn = types[static_cast<size_t>(l)].string() == "full_attention";
+        x.attn = attn ? 1 : 0;
+        bool ok = raw(p + "input_layernorm.weight", x.in_norm) && raw(p + "post_attention_layernorm.weight", x.post_norm);
+        if (attn) {
+            ok = ok && q4(p + "self_attn.q_proj.weight", x.q) && q4(p + "self_attn.k_proj.weight", x.k) &&
+                 q4(p + "self_attn.v_proj.weight", x.v) && q4(p + "self_attn.o_proj.weight", x.o) &&
+                 raw(p + "self_attn.q_norm.weight", x.q_norm) && raw(p + "self_attn.k_norm.weight", x.k_norm);
+        } else {
+            ok = ok && q4(p + "linear_attn.in_proj_qkv.weight", x.qkv) && q4(p + "linear_attn.in_proj_z.weight", x.z) &&
+                 q4(p + "linear_attn.out_proj.weight", x.out) && raw(p + "linear_attn.in_proj_a.weight", x.a) &&
+                 raw(p + "linear_attn.in_proj_b.weight", x.b) && raw(p + "linear_attn.A_log", x.A_log) &&
+                 raw(p + "linear_attn.dt_bias", x.dt_bias) && raw(p + "linear_attn.conv1d.weight", x.conv) &&
+                 raw(p + "linear_attn.norm.weight", x.gnorm);
+        }
+        if (dense) {
+            ok = ok && q4(p + "mlp.gate_proj.weight", x.sh_gate) && q4(p + "mlp.up_proj.weight", x.sh_up) &&
+                 q4(p + "mlp.down_proj.weight", x.sh_down);
+        } else {
+            ok = ok && q4(p + "mlp.shared_expert.gate_proj.weight", x.sh_gate) &&
+                 q4(p + "mlp.shared_expert.up_proj.weight", x.sh_up) &&
+                 q4(p + "mlp.shared_expert.down_proj.weight", x.sh_down) && raw(p + "mlp.gate.weight", x.router) &&
+                 raw(p + "mlp.shared_expert_gate.weight", x.shared_gate);
+            if (ok) {
+                ExpertTable e;
+                TensorView sc;
+                ok = pack_.experts(l, e, err) && pack_.tensor(p + "mlp.experts.scales", sc, err);
+                if (ok) {
+                    x.experts = api_.adopt_experts(g_, e.data, static_cast<int>(c["num_experts"].integer()), e.stride,
+                                                   reinterpret_cast<const float *>(sc.data));
+                    ok = x.experts >= 0 || fail("experts", err);
+                }
+            }
+        }
+        if (!ok) return false;
+    }
+    TensorView et;
+    if (!pack_.tensor("embed_tokens.weight", et, err)) return false;
+    const int embed = api_.adopt_embedding(g_, et.data, et.rows(), et.cols(), et.global);
+    if (embed < 0) return fail("embedding", err);
+    int head = -1, norm = -1;
+    if (!q4("lm_head.weight", head) || !raw("norm.weight", norm)) return false;
+    const Json &rope = c["rope_parameters"];
+    gcuda_shape s{};
+    s.hidden = static_cast<int>(c["hidden_size"].integer());
+    s.n_layers = L;
+    s.vocab = static_cast<int>(c["vocab_size"].integer());
+    s.eps = static_cast<float>(c["rms_norm_eps"].number(1e-6));
+    s.n_heads = static_cast<int>(c["num_attention_heads"].integer());
+    s.n_kv_heads = static_cast<int>(c["num_key_value_heads"].integer());
+    s.head_dim = static_cast<int>(c["head_dim"].integer());
+    s.rope_dim = static_cast<int>(static_cast<double>(s.head_dim) * rope["partial_rotary_factor"].number(1.0));
+    s.rope_theta = static_cast<float>(rope["rope_theta"].number(10000.0));
+    s.gdn_k_heads = static_cast<int>(c["linear_num_key_heads"].integer());
+    s.gdn_v_heads = static_cast<int>(c["linear_num_value_heads"].integer());
+    s.gdn_k_dim = static_cast<int>(c["linear_key_head_dim"].integer());
+    s.gdn_v_dim = static_cast<int>(c["linear_value_head_dim"].integer());
+    s.conv_kernel = static_cast<int>(c["linear_conv_kernel_dim"].integer());
+    s.n_experts = static_cast<int>(c["num_experts"].integer());
+    s.top_k = static_cast<int>(c["num_experts_per_tok"].integer());
+    s.moe_ff = static_cast<int>(c["moe_intermediate_size"].integer());
+    s.shared_ff = static_cast<int>(dense ? c["intermediate_size"].integer() : c["shared_expert_intermediate_size"].integer());
+    s.dense = dense ? 1 : 0;
+    s.context = opt.context > 0 ? opt.context : 4096;
+    s.max_tokens = opt.max_tokens;
+    if (api_.setup(g_, &s, layers.data(), embed, head, norm) != 0) return fail("setup", err);
+    max_tokens_ = opt.max_tokens;
+    vocab_ = s.vocab;
+    return true;
+}
+
+bool CudaModel::verify_n(const int *toks, int n, float *logits, std::string &err) {
+    if (!g_) {
+        err = "not open";
+        return false;
+    }
+    if (api_.verify(g_, toks, n, logits, nullptr) != 0) return fail("verify", err);
+    last_n_ = n;
+    return true;
+}
+
+bool CudaModel::verify_keep(int kept, std::string &err) {
+    if (!g_) {
+        err = "not open";
+        return false;
+    }
+    return api_.keep(g_, kept) == 0 || fail("keep", err);
+}
+
+bool CudaModel::accept(const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept, int &next,
+                       std::string &err) {
+    if (!g_ || last_n_ < 1) {
+        err = "accept without a verified batch";
+        return false;
+    }
+    gcuda_sampling sp{p.temperature, p.top_p, p.top_k};
+    double u[8] = {0};
+    const bool sampled = p.temperature > 0.0f;
+    if (sampled) s.peek(last_n_, u);   // row i's draw is the stream's i-th from here
+    int k = 0, nx = 0;
+    if (api_.accept(g_, &sp, sampled ? u : nullptr, stops, n_stops, &k, &nx, nullptr) != 0) return fail("accept", err);
+    if (sampled) s.skip(k);   // the rows sampled: kept of them (the last one gave next)
+    kept = k;
+    next = nx;
+    return true;
+}
+
+bool CudaModel::step(const int *batch, int n, const SamplerParams &p, Sampler &s, const int *stops, int n_stops,
+                     int &kept, int &next, std::string &err) {
+    if (!verify_n(batch, n, nullptr, err) || !accept(p, s, stops, n_stops, kept, next, err)) return false;
+    // (every draft stood: nothing to roll back, as the engine's loop; else the states as after row kept-1)
+    return kept == n || verify_keep(kept, err);
+}
+
+bool pack_summary(const std::string &dir, std::string &out, std::string &err) {
+    Pack p;
+    if (!p.open(dir, err)) return false;
+    const Json &c = p.config();
+    size_t n = 0, q4 = 0, bytes = 0;
+    for (const auto &kv : p.manifest()["tensors"].obj) {
+        TensorView t;
+        if (!p.tensor(kv.first, t, err)) return false;
+        ++n;
+        q4 += t.type == "q4";
+        bytes += t.bytes;
+    }
+    size_t expert_bytes = 0;
+    if (p.manifest()["experts"].has("layers"))
+        for (size_t l = 0; l < p.manifest()["experts"]["layers"].size(); ++l) {
+            ExpertTable e;
+            if (!p.experts(static_cast<int>(l), e, err)) return false;
+            expert_bytes += e.stride * static_cast<size_t>(c["num_experts"].integer());
+        }
+    out = "arch=" + p.arch() + " layers=" + std::to_string(c["num_hidden_layers"].integer()) +
+          " hidden=" + std::to_string(c["hidden_size"].integer()) + " vocab=" + std::to_string(c["vocab_size"].integer()) +
+          " experts=" + std::to_string(c["num_experts"].integer()) + " tensors=" + std::to_string(n) +
+          " q4=" + std::to_string(q4) + " bytes=" + std::to_string(bytes) + " expert_bytes=" + std::to_string(expert_bytes);
+    return true;
+}
+
+}  // namespace ghost

@@ -1,0 +1,103 @@
+// cuda_model.hpp - the host side of the CUDA backend: the engine's Model seam for the speculative verify step
+// (Model::verify_n / verify_keep / can_verify / spec_tokens, engine/src/model.hpp:189-205), its Sampler's uniform
+// stream (engine/src/sampler.hpp) and the acceptance rule of the speculation loop (engine/src/geode.cpp:327-350),
+// over libgeode_cuda.so. The backend library is loaded at run time into a table of its C functions, as the engine
+// loads its NPU backend (dlopen + dlsym, engine/src/model.cpp:2255-2320), so the engine needs no CUDA at build time.
+#pragma once
+
+#include <cstdint>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "../../include/geode_cuda.h"
+#include "pack.hpp"
+
+namespace ghost {
+
+// The C functions of libgeode_cuda.so this host calls.
+struct CudaApi {
+    void *lib = nullptr;
+    decltype(&gcuda_open) open = nullptr;
+    decltype(&gcuda_close) close = nullptr;
+    decltype(&gcuda_last_error) last_error = nullptr;
+    decltype(&gcuda_adopt_q4) adopt_q4 = nullptr;
+    decltype(&gcuda_adopt_raw) adopt_raw = nullptr;
+    decltype(&gcuda_adopt_embedding) adopt_embedding = nullptr;
+    decltype(&gcuda_adopt_experts) adopt_experts = nullptr;
+    decltype(&gcuda_setup) setup = nullptr;
+    decltype(&gcuda_verify) verify = nullptr;
+    decltype(&gcuda_keep) keep = nullptr;
+    decltype(&gcuda_position) position = nullptr;
+    decltype(&gcuda_accept) accept = nullptr;
+    // path: the library file; empty = libgeode_cuda.so beside this library
+    bool load(const std::string &path, std::string &err);
+    ~CudaApi();
+};
+
+struct ModelOptions {
+    int device = 0;
+    int context = 0;      // positions of KV cache; 0 = 4096
+    int max_tokens = 5;   // the largest verify batch (1 accepted + max_tokens - 1 drafts), <= 8
+};
+
+struct SamplerParams {
+    float temperature = 0.0f;   // 0 = greedy
+    float top_p = 1.0f;         // 1 = off
+    int top_k = 0;              // 0 = off (1024 candidates)
+};
+
+// The reference sampler's random stream: std::mt19937_64 seeded once per generate call, one
+// uniform_real_distribution<double>(0, 1) draw (generate_canonical<double, 53>) for each row it samples.
+class Sampler {
+public:
+    void seed(uint64_t s) { rng_.seed(s); }
+    double uniform() { return std::generate_canonical<double, 53>(rng_); }
+    // the next n draws without consuming them
+    void peek(int n, double *out) const {
+        std::mt19937_64 copy = rng_;
+        for (int i = 0; i < n; ++i) out[i] = std::generate_canonical<double, 53>(copy);
+    }
+    void skip(int n) {
+        for (int i = 0; i < n; ++i) uniform();
+    }
+
+private:
+    std::mt19937_64 rng_;
+};
+
+class CudaModel {
+public:
+    CudaModel() = default;
+    CudaModel(const CudaModel &) = delete;
+    CudaModel &operator=(const CudaModel &) = delete;
+    ~CudaModel();
+
+    bool open(const std::string &dir, const ModelOptions &opt, std::string &err);
+    bool can_verify() const { return g_ != nullptr; }
+    int spec_tokens() const { return max_tokens_ - 1; }   // drafts a verify batch can carry
+    int position() const;
+    int vocab() const { return vocab_; }
+
+    // n tokens at positions pos .. pos+n-1 through every layer; logits [n][vocab] (or NULL); position += n
+    bool verify_n(const int *toks, int n, float *logits, std::string &err);
+    // rollback: the states as after the verified batch's row kept-1 (1 <= kept < n); position -= n - kept
+    bool verify_keep(int kept, std::string &err);
+    // the acceptance of the last verified batch (its rows 1.. are the drafts): kept, next (-1: a stop token stood)
+    bool accept(const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept, int &next, std::string &err);
+    // one speculation step: verify_n(batch), accept, verify_keep(kept) unless every draft stood
+    bool step(const int *batch, int n, const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept,
+              int &next, std::string &err);
+
+private:
+    bool fail(const char *what, std::string &err);
+    CudaApi api_;
+    Pack pack_;
+    gcuda *g_ = nullptr;
+    int max_tokens_ = 5, vocab_ = 0, last_n_ = 0;
+};
+
+// The manifest as this host reads it, one line (tests): arch, layers, hidden, vocab, experts, tensor counts, bytes.
+bool pack_summary(const std::string &dir, std::string &out, std::string &err);
+
+}  // namespace ghost
