@@ -206,6 +206,11 @@ def reference_arm(args):
 
 
 # ------------------------------------------------------------------------------------------- the GPU path ----
+# dram__bytes_read.sum + dram__bytes_write.sum of one LM-head launch of k_gemv_static (one ncu capture, the command in
+# profiles/k_gemv_static_lmhead_cfg3.md): 287.9 MB + 20.8 MB
+LMHEAD_TRAFFIC = 308.74e6
+
+
 def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
     """The dominant kernel's roofline, measured live: the q4 GEMV (k_gemv_static, the kernel of every dense product and
     the LM head) on the LM head's shape, 248320 x 2048, 5 token rows; CUDA events on its stream."""
@@ -239,8 +244,8 @@ def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
     alg = rows * cols * 9 // 16 + n * cols + n * (cols // 16) * 8 + n * rows * 4
     ach = alg / (ms * 1e-3) / 1e9
     return {"kernel": "k_gemv_static (q4 GEMV, lm_head 248320x2048, 5 rows)", "bound": "hbm", "achieved": ach,
-            "peak": peak_gbs, "unit": "GB/s", "frac": ach / peak_gbs, "traffic": None, "ms": ms,
-            "algorithmic_bytes": alg}
+            "peak": peak_gbs, "unit": "GB/s", "frac": ach / peak_gbs, "traffic": LMHEAD_TRAFFIC, "ms": ms,
+            "algorithmic_bytes": alg, "traffic_source": "ncu, profiles/k_gemv_static_lmhead_cfg3.md"}
 
 
 def main():
