@@ -184,6 +184,16 @@ def cpu_reference(steps: int = 3, layers: int = 4, threads: int = 0) -> dict:
                       f"{t40 * 1e3:.0f} ms/step"}
 
 
+def max_over_ranks(value: float, dist, device) -> float:
+    """The largest of every rank's value (every rank takes the same collective; a lone process returns its own)."""
+    if dist is None:
+        return value
+    import torch
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -310,10 +320,7 @@ def main():
     ms = e0.elapsed_time(e1)
     steps_done, union_sum, _ = be.sync_step()
     launches_timed = be.launches() - lc0
-    if dist:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, dist, "cuda")
     ms_step = ms / args.steps
     n_moe = 0 if shape.dense else shape.n_layers
     union_layer = union_sum / max(1, steps_done * n_moe) if n_moe else 0.0
@@ -342,10 +349,7 @@ def main():
         toks[0] = nxt
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks(e2e_s, dist, "cuda")
     e2e = world * NTOK * args.e2e_steps / e2e_s
 
     roof = gemv_roofline(cuda_lib(), peak)
