@@ -410,7 +410,7 @@ int enqueue_step(gcuda *g, int n) {
             ea.shout = g->shout;
             ea.status = g->d_status;
             for (int pass : {static_cast<int>(kGateUp), static_cast<int>(kDown)}) {
-                RelayShape r;
+                GemvShape r;
                 if (!plan_experts(pass, H, s.moe_ff, s.shared_ff, s.n_experts, s.top_k, n, sm_count(), r)) return GCUDA_E_ARG;
                 ea.pass = pass;
                 ea.wpu = r.wpu;

@@ -1,19 +1,19 @@
-// relay_core.cuh - the q4 GEMV engine: a unit (two 16-row tiles x all K) is split by K over the WPU warps of a
-// "slot"; warp `part` owns groups [part * SG, (part + 1) * SG) (SG = K / 64 / WPU, a group = 4 blocks of 16 values).
-// Each warp streams its slices of successive units through its own ring of TMA bulk-copy stages, computes its first
-// kPre groups' products p = float(isum) * (e4m3 * ascale) ahead, then takes the running f32 chain from warp part-1
-// (a rendezvous on a named barrier), adds its products in block order, and hands the chain to warp part+1; the last
-// warp writes the result. The additions happen in exactly the reference's order (engine/src/kernels.cpp:1316-1319),
-// so the result is bit for bit matvec_rows_q_ref's, while a 2048-row matrix still spreads over every SM.
+// gemv_core.cuh - the q4 GEMV engine. A unit is two 16-row tiles x all K; its result per (row, token) is the
+// reference's chain acc += float(isum_b) * (e4m3_b * ascale_b) over the blocks b in order (engine/src/kernels.cpp:
+// 1316-1319), bit for bit. Two ways to run a launch:
+//   - streaming (stream_units): a warp per unit, for launches with enough units to fill the SMs; the warp copies its
+//     units' groups into its own shared-memory ring with cp.async and adds every product into the chain as it comes;
+//   - fan-in (fan_units): for launches with few units; the whole CTA works on one unit, producer warps leave each
+//     group's products in a shared slot and chain warps add the slots in block order.
+// Both compute a group's products the same way (group_products): int8 mma.sync block sums whose accumulator starts
+// at 1.5 * 2^23 - 15 * bsum (so float(isum) is one subtraction), then f32x2 products.
 #pragma once
 
 #include "q4_gemv.cuh"
 
 namespace gcu {
 
-constexpr int kRelayStages = 6;   // ring stages per warp, one group of both tiles each
-constexpr int kStageBytesR = 2 * kGroupBytes;
-constexpr int kPre = 2;           // groups computed before the predecessor's hand-off
+constexpr int kStageBytesR = 2 * kGroupBytes;   // a ring stage: one group of both tiles
 
 // f32x2 (sm_100): two IEEE operations per instruction, each lane rounded on its own
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
@@ -52,64 +52,27 @@ __device__ __forceinline__ float e4m3_alu(uint32_t b) {
     return __fmul_rn(__uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20)), 0x1p120f);
 }
 
-// Shared memory per warp: the ring, its barriers, one group's scales as (e, e) float pairs, the relay mailbox
-// (2 parities x 32 lanes x 4 float pairs) and, for launches whose units multiply different activations, the warp's own
-// activation image of its K-slice (else the CTA shares one image of all K).
-// an image's per-(group, tig) entry of accumulator inits and activation scales (kCsEntry bytes, below)
+// Activation images (stage_image below): an image's per-(group, tig) entry of accumulator inits and activation
+// scales is kCsEntry bytes; a warp's own image of sg groups (launches whose units multiply different activations)
+// takes warp_act_bytes(sg), the CTA's shared image of all K act_smem_bytes(K).
 constexpr int kCsEntry = 96;
 __host__ __device__ inline int slice_tstride(int sg) { return sg * 64 + (sg % 2 == 0 ? 64 : 0); }
 __host__ __device__ inline int warp_act_bytes(int sg) { return kMaxTok * slice_tstride(sg) + sg * 4 * kCsEntry; }
-__host__ __device__ inline int warp_base_bytes() {
-    return kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8 + 2 * 32 * 32;
-}
-__host__ __device__ inline int warp_smem_bytes(int sg_own) {   // sg_own: the own image's groups (0: none)
-    const int b = warp_base_bytes() + (sg_own ? warp_act_bytes(sg_own) : 0);
-    return (b + 127) / 128 * 128;
-}
 // the whole-K image the CTA shares (act_tstride: token stride of the full image)
 __host__ __device__ inline int act_tstride(int cols) { return (cols / 64) * 64 + ((cols / 64) % 2 == 0 ? 64 : 0); }
 __host__ __device__ inline int act_smem_bytes(int cols) { return (kMaxTok * act_tstride(cols) + (cols / 64) * 4 * kCsEntry + 127) / 128 * 128; }
-// warps per unit: as many as keep every unit of the launch in flight at once on the GPU's sms x kGemvWarps warps (a
-// launch with more units than warps gets one warp per unit: no relay), at most K/128 (two groups per warp: both
-// computed before the hand-off) and 16; always a divisor of K/64
-__host__ __device__ inline int choose_wpu(int cols, int n_units, int sms) {
-    const int g = cols / 64;
-    int w = n_units > 0 ? (kGemvWarps * sms) / n_units : 16;
-    if (w > g / 2) w = g / 2;
-    if (w > 16) w = 16;
-    if (w < 1) w = 1;
-    while (g % w) --w;
-    return w;
-}
-
 constexpr int kMaxDynSmem = 227 * 1024;
 
 // A launch's shape: wpu warps per unit, nslots units at a time per CTA, the dynamic shared memory. The warps' regions
 // (own: the groups of a per-warp image, 0 for none) follow `front` bytes (the CTA's shared image, or 0). Slots are
 // dropped, then shorter chains taken, until it fits. False if no shape fits.
-struct RelayShape {
+// A launch's shape: wpu = 1 and nslots warps per CTA (streaming, `stages` deep rings), or wpu = kFanWarps and one
+// slot (fan-in, stages 0); sg the groups a unit's warp walks; the dynamic shared memory.
+struct GemvShape {
     int wpu, nslots, sg;
     size_t smem;
-    int stages = 0;   // the streaming path's ring depth (0: the relay)
+    int stages = 0;
 };
-inline bool plan_relay(int cols, int wpu, bool own_images, size_t front, RelayShape &r) {
-    const int g = cols / 64;
-    if (g < 1 || wpu < 1) return false;
-    for (; wpu >= 1; --wpu) {
-        if (g % wpu) continue;
-        const int sg = g / wpu;
-        const size_t wb = static_cast<size_t>(warp_smem_bytes(own_images ? sg : 0));
-        for (int ns = kGemvWarps / wpu; ns >= 1; --ns) {
-            const size_t sm = front + static_cast<size_t>(ns * wpu) * wb;
-            if (sm <= static_cast<size_t>(kMaxDynSmem)) {
-                r = RelayShape{wpu, ns, sg, sm, 0};
-                return true;
-            }
-        }
-    }
-    return false;
-}
-
 // The activation image of groups [g0, g0 + ng) of up to kMaxTok vectors (src(t) = the ActSet row of token column t, -1 =
 // zeros), token stride ts: act word (t, gl, tig, j) at t * ts + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
 // .. + 3); cs per (gl, tig) kCsEntry bytes at kMaxTok * ts + (gl * 4 + tig) * kCsEntry: for each block j the mma's
@@ -223,150 +186,6 @@ __device__ __forceinline__ void group_products(const uint4 wa, const uint4 wb, c
     }
 }
 
-struct RelayCtx {
-    uint8_t *ring;     // kRelayStages stages
-    uint64_t *bar;
-    float *e4p;        // 2 tiles x 16 rows x 4 blocks x (e, e)
-    uint8_t *img;      // the activation image: token t's bytes at t * img_ts, this warp's groups from g_off
-    int img_ts, g_off;
-    uint8_t *own_img;  // the warp's own slice image (launches with per-unit activations), or NULL
-    uint64_t *mail;    // [2][32][4] pairs: this slot's hand-off from the predecessor
-    uint64_t *mail_next;   // the successor's mailbox
-    int part, wpu, sg;
-    int bar_in, bar_out;   // named barrier ids (0: none)
-    uint64_t zero;         // a +0 pair from runtime values (f2_mul_sep)
-};
-
-// The units of one slot: get(i, U) the i-th (false past the end); restage(U) fills ctx.img for U's act_id when it
-// changes (called by every lane); epi(U, y0, y1, gid, tig) by the last warp. `early`: the first weight stages may be
-// requested before prelude() (the units do not depend on the previous kernel); prelude() holds CTA barriers.
-template <typename GetUnit, typename Restage, typename Epi, typename Prelude>
-__device__ bool relay_units(const GetUnit &get, RelayCtx c, const Restage &restage, uint32_t *status, const Epi &epi,
-                            bool early, const Prelude &prelude) {
-    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    const int sg = c.sg;
-    const uint32_t gbytes = kGroupBytes;
-    // producer: items (unit i, group gl) in order
-    int pu = 0, pg = 0, issued = 0;
-    const uint8_t *pw0 = nullptr, *pw1 = nullptr;
-    bool p_ok = false;
-    auto fetch = [&](int i) {
-        GemvUnit T;
-        p_ok = get(i, T);
-        pw0 = T.w0;
-        pw1 = T.w1;
-    };
-    auto issue = [&]() {
-        if (!p_ok) return;
-        const int s = issued % kRelayStages;
-        if (lane == 0) {
-            fence_proxy_async();
-            uint8_t *dst = c.ring + s * kStageBytesR;
-            const size_t off = static_cast<size_t>(c.part * sg + pg) * gbytes;
-            mbar_expect_tx(&c.bar[s], 2 * gbytes);
-            bulk_g2s(dst, pw0 + off, gbytes, &c.bar[s]);
-            bulk_g2s(dst + gbytes, pw1 + off, gbytes, &c.bar[s]);
-        }
-        ++issued;
-        if (++pg == sg) {
-            pg = 0;
-            fetch(++pu);
-        }
-    };
-    if (early) {
-        fetch(0);
-        for (int i = 0; i < kRelayStages - 1; ++i) issue();
-        prelude();
-    } else {
-        prelude();
-        fetch(0);
-        for (int i = 0; i < kRelayStages - 1; ++i) issue();
-    }
-    int consumed = 0;
-    bool ok = true;
-    for (int u = 0;; ++u) {
-        {   // (the unit is read again for the epilogue: nothing of it stays live across the groups)
-            GemvUnit U;
-            if (!get(u, U)) break;
-            restage(U);
-        }
-        const int ts = c.img_ts;
-        const uint8_t *act = c.img + gid * ts + tig * 16 + c.g_off * 64;
-        const uint8_t *cs = c.img + kMaxTok * ts + tig * kCsEntry + c.g_off * 4 * kCsEntry;
-        // one group: wait, the scales to (e, e) pairs, the products into sink(j, p[4])
-        auto group = [&](int gl, const auto &sink) -> bool {
-            if (!ok) return false;   // (after a wait gave up: no more waits; the chain still runs, the status says why)
-            const int s = consumed % kRelayStages;
-            if (!mbar_wait_bounded(&c.bar[s], (consumed / kRelayStages) & 1, status)) return false;
-            const uint8_t *st = c.ring + s * kStageBytesR;
-            // 2 tiles x 64 scale bytes (row w's four blocks in a word): one word per lane, to (e, e) pairs
-            decode_scales(*reinterpret_cast<const uint32_t *>(st + (lane >> 4) * kGroupBytes + 512 + 4 * (lane & 15)), lane,
-                          c.e4p);
-            __syncwarp();
-            group_products(ld_shared_v4(st + lane * 16), ld_shared_v4(st + kGroupBytes + lane * 16), c.e4p, act + gl * 64,
-                           cs + gl * 4 * kCsEntry, lane, c.zero, sink);
-            ++consumed;
-            __syncwarp();   // every lane done with the stage and the scale pairs before they are refilled
-            issue();
-            return true;
-        };
-        // the first kPre groups before the predecessor's hand-off, kept as products
-        uint64_t pre[kPre][4][4];
-        const int npre = sg < kPre ? sg : kPre;
-#pragma unroll
-        for (int gl = 0; gl < kPre; ++gl)
-            if (gl < npre && !group(gl, [&](int j, const uint64_t (&p)[4]) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) pre[gl][j][q] = p[q];
-                }))
-                ok = false;
-        // the chain so far
-        uint64_t acc[4];
-        const int par = u & 1;
-        if (c.part == 0) {
-            acc[0] = acc[1] = acc[2] = acc[3] = 0;
-        } else {
-            asm volatile("bar.sync %0, 64;" ::"r"(c.bar_in) : "memory");
-            const uint64_t *m = c.mail + (par * 32 + lane) * 4;
-            acc[0] = m[0], acc[1] = m[1], acc[2] = m[2], acc[3] = m[3];
-        }
-#pragma unroll
-        for (int gl = 0; gl < kPre; ++gl)
-            if (gl < npre)
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], pre[gl][j][q]);
-        // the rest straight into the chain, block by block
-        auto chain = [&](int, const uint64_t (&p)[4]) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[q]);
-        };
-        for (int gl = npre; gl < sg; ++gl)
-            if (!group(gl, chain)) ok = false;
-        if (c.part + 1 < c.wpu) {
-            uint64_t *m = c.mail_next + (par * 32 + lane) * 4;
-            m[0] = acc[0], m[1] = acc[1], m[2] = acc[2], m[3] = acc[3];
-            asm volatile("bar.sync %0, 64;" ::"r"(c.bar_out) : "memory");
-        } else {
-            // y = acc * global * 1 (engine/src/kernels.cpp:1320); y0: tile A (gid: t 2tig, 2tig+1; gid+8: ...), y1: B
-            GemvUnit U;
-            get(u, U);
-            float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
-            float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                y0[i] = __fmul_rn(y0[i], U.g0);
-                y1[i] = __fmul_rn(y1[i], U.g1);
-            }
-            epi(U, y0, y1, gid, tig);
-        }
-    }
-    // copies still in flight after a failed wait: waited for (bounded) before the shared memory is released
-    for (; !ok && consumed < issued; ++consumed) mbar_wait_bounded(&c.bar[consumed % kRelayStages], (consumed / kRelayStages) & 1, nullptr);
-    return ok;
-}
-
 // the fan-in path's shape (fan_units below)
 constexpr int kFanProducers = 16;
 constexpr int kFanAhead = 4;   // a producer's items in flight
@@ -383,7 +202,7 @@ __host__ __device__ inline size_t fan_smem_bytes(int img_cols) {
 }
 
 // ------------------------------------------------------------------------------------------- streaming ----
-// The path for launches with a warp per unit (wpu = 1, no relay): each warp (up to kStreamWarps) copies its units'
+// The path for launches with a warp per unit (wpu = 1): each warp (up to kStreamWarps) copies its units'
 // groups (both tiles' 576 bytes) into its own ring of shared-memory stages with 16-byte cp.async copies, the
 // stages ahead of the one it multiplies in flight, and adds every product into the chain as it comes. The copies hold
 // no registers (so the CTA runs more warps) and their waits (cp.async.wait_group) always end: the copies land like
@@ -404,10 +223,10 @@ __host__ __device__ constexpr int stream_warps(int stages) { return stages == kD
 // (stages 0; the CTA on one unit at a time, its image img_cols wide). units_per_cta: the units a CTA takes (all CTAs
 // take the same share, +-1).
 constexpr int kStreamMinUnits = 2;
-inline bool plan_gemv(int cols, int img_cols, bool own_images, size_t front, int units_per_cta, RelayShape &r) {
+inline bool plan_gemv(int cols, int img_cols, bool own_images, size_t front, int units_per_cta, GemvShape &r) {
     const size_t fan = fan_smem_bytes(img_cols);
     if (units_per_cta < kStreamMinUnits && cols >= 64 && fan <= static_cast<size_t>(kMaxDynSmem)) {
-        r = RelayShape{kFanWarps, 1, cols / 64, fan, 0};
+        r = GemvShape{kFanWarps, 1, cols / 64, fan, 0};
         return true;
     }
     if ((cols / 64) % 2 == 0) {
@@ -418,12 +237,12 @@ inline bool plan_gemv(int cols, int img_cols, bool own_images, size_t front, int
         if (units_per_cta > 0 && units_per_cta < ns) ns = units_per_cta;
         while (ns >= 1 && front + ns * wb > static_cast<size_t>(kMaxDynSmem)) --ns;
         if (g >= 1 && ns >= 1) {
-            r = RelayShape{1, ns, g, front + ns * wb, stages};
+            r = GemvShape{1, ns, g, front + ns * wb, stages};
             return true;
         }
     }
     if (cols >= 64 && fan <= static_cast<size_t>(kMaxDynSmem)) {
-        r = RelayShape{kFanWarps, 1, cols / 64, fan, 0};
+        r = GemvShape{kFanWarps, 1, cols / 64, fan, 0};
         return true;
     }
     return false;
@@ -743,42 +562,6 @@ __device__ void fan_units(const GetUnit &get, const FanCtx &c, const Changes &ch
             bar_sync_n(kBarChains, kFanChains * 32);   // (the exchange is free for the next unit)
         }
     }
-}
-
-// The per-warp context inside a CTA of kGemvWarps warps: slot = warp / wpu, part = warp % wpu. smem_warps: the warps'
-// regions (warp_smem_bytes(sg_own) each); img / img_ts: the CTA's shared image (or NULL: the warp's own, sg_own groups).
-__device__ inline RelayCtx make_ctx(uint8_t *smem_warps, int wpu, int sg, int sg_own, uint8_t *img, int img_ts) {
-    const int warp = threadIdx.x >> 5;
-    const int wb = warp_smem_bytes(sg_own);
-    uint8_t *base = smem_warps + static_cast<size_t>(warp) * wb;
-    RelayCtx c;
-    c.ring = base;
-    c.bar = reinterpret_cast<uint64_t *>(base + kRelayStages * kStageBytesR);
-    c.e4p = reinterpret_cast<float *>(base + kRelayStages * kStageBytesR + kRelayStages * 8);
-    c.mail = reinterpret_cast<uint64_t *>(base + kRelayStages * kStageBytesR + kRelayStages * 8 + 2 * 16 * 4 * 8);
-    c.own_img = sg_own ? reinterpret_cast<uint8_t *>(c.mail) + 2 * 32 * 32 : nullptr;
-    c.mail_next = reinterpret_cast<uint64_t *>(reinterpret_cast<uint8_t *>(c.mail) + wb);   // the next warp's mailbox
-    c.wpu = wpu;
-    c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);   // (wpu >= 1: always 0)
-    c.part = warp % wpu;
-    c.sg = sg;
-    if (img) {
-        c.img = img;
-        c.img_ts = img_ts;
-        c.g_off = c.part * sg;
-    } else {
-        c.img = c.own_img;
-        c.img_ts = slice_tstride(sg);
-        c.g_off = 0;
-    }
-    const int slot = warp / wpu;
-    c.bar_in = c.part > 0 ? 1 + slot * (wpu - 1) + (c.part - 1) : 0;
-    c.bar_out = c.part + 1 < wpu ? 1 + slot * (wpu - 1) + c.part : 0;
-    if ((threadIdx.x & 31) == 0)
-        for (int s = 0; s < kRelayStages; ++s) mbar_init(&c.bar[s], 1);
-    fence_barrier_init();
-    __syncwarp();
-    return c;
 }
 
 }  // namespace gcu

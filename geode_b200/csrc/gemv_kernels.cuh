@@ -2,7 +2,7 @@
 // activation quantizer.
 #pragma once
 
-#include "relay_core.cuh"
+#include "gemv_core.cuh"
 
 namespace gcu {
 
@@ -127,7 +127,7 @@ struct StaticGemv {
     uint32_t *status;
 };
 
-inline bool plan_static(int cols, int n_units, int sms, RelayShape &r) {
+inline bool plan_static(int cols, int n_units, int sms, GemvShape &r) {
     return plan_gemv(cols, cols, false, static_cast<size_t>(act_smem_bytes(cols)), (n_units + sms - 1) / sms, r);
 }
 
@@ -247,7 +247,7 @@ struct ExpertsArgs {
 
 // gate_up: the CTA's image of h in front of the warps; down: every warp its own image (the units' activations differ).
 // units: the expected count (the union is known on the device only): n*K picks at most, E experts at most.
-inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, RelayShape &r) {
+inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, GemvShape &r) {
     const int picks = n * K < E ? n * K : E;
     if (pass == kGateUp) {
         const int units = picks * (ff / 16) + sff / 16;

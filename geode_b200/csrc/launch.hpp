@@ -63,7 +63,7 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
     return e;
 }
 
-// The GEMV kernels' shared-memory opt-in: the largest any launch shape takes (plan_relay caps it there).
+// The GEMV kernels' shared-memory opt-in: the largest any launch shape takes (plan_gemv caps it there).
 inline int gemv_opt_in() {
     static const int rc = [] {
         const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
@@ -82,7 +82,7 @@ inline int gemv_opt_in() {
 // p.wpu / p.nslots are set here (plan_static); the grid is one CTA per SM at most
 // (p.allow_half: a launch with fewer units than SMs runs one-tile units on the fan-in path, twice the CTAs)
 inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
-    RelayShape r;
+    GemvShape r;
     if (!plan_static(p.act.cols, p.n_units, sm_count(), r)) return GCUDA_E_ARG;
     if (gemv_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
     p.wpu = r.wpu;

@@ -7,11 +7,10 @@
 // 8 token columns per instruction); the accumulator starts at 1.5 * 2^23 - 15 * bsum, so the result reads back as the
 // exact float of isum with one subtraction (the weights enter as the doubled affine codes 2c, level = 2c - 15). The
 // per-(row, token) f32 chain runs in block order with packed f32x2 operations (each lane IEEE, no contraction).
-// K is split across the warps of a "slot" (relay_core.cuh): each warp computes its blocks' products ahead, then
-// continues the one in-order chain its predecessor hands it through a named-barrier rendezvous, so even a
-// 2048-row matrix spreads over the whole GPU without reordering a single addition. Rows are relaid once at load
-// time into 16-row tiles whose bytes a lane reads as its mma fragment; each warp streams its K-slice of two tiles
-// per unit through shared memory with 1-D TMA bulk copies (cp.async.bulk) into a ring of stages.
+// Rows are relaid once at load time into 16-row tiles whose bytes a lane reads as its mma fragment. A launch runs
+// its units (two tiles x all K) either a warp per unit with the weights streamed through per-warp cp.async rings, or -
+// with few units - a CTA per unit whose producer warps compute the products and whose chain warps add them in order
+// (gemv_core.cuh); either way no addition is reordered.
 //
 // Tile layout (per 16-row tile, per group of 4 blocks = 64 columns, 576 bytes):
 //   bytes [0, 512):   lane l = 4 * gid + tig: 16 bytes = 4 words, word j for block 4g + j. Its low nibbles (byte i)
@@ -27,7 +26,6 @@ namespace gcu {
 
 constexpr int kGroupBytes = 576;           // one 16-row tile x 4 blocks
 constexpr int kTileRows = 16;
-constexpr int kGemvWarps = 16;             // warps per CTA
 
 __host__ __device__ inline int tile_bytes(int cols) { return (cols / 64) * kGroupBytes; }
 
