@@ -772,50 +772,63 @@ struct RouteOut {
 };
 
 __global__ void k_route(const float *__restrict__ logits, int n, int E, int K, RouteOut *out, int *union_acc) {
-    extern __shared__ float ps[];   // E floats per warp
-    __shared__ int s_ids[kMaxTok * 8], s_first[kMaxTok * 8], s_rank[kMaxTok * 8];
+    extern __shared__ __align__(16) float ps[];   // E floats per warp
+    __shared__ int s_ids[kMaxTok * 8];
+    __shared__ float s_w[kMaxTok * 8];
+    __shared__ uint32_t s_bits[32];   // the union as a bit set over the experts (E <= 1024)
+    __shared__ int s_base[33];        // per word: the union members before it; [32] the union's size
+    __shared__ int s_mask[kMaxUnion];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) s_bits[threadIdx.x] = 0;
+    if (threadIdx.x < kMaxUnion) s_mask[threadIdx.x] = 0;
     if (warp < n) {
-        route_row(logits + static_cast<size_t>(warp) * (E + 1), E, K, ps + warp * E, out->ids + warp * K, out->w + warp * K);
+        route_row(logits + static_cast<size_t>(warp) * (E + 1), E, K, ps + warp * E, s_ids + warp * K, s_w + warp * K);
         if (lane == 0) out->gs[warp] = sigmoid_cr(logits[static_cast<size_t>(warp) * (E + 1) + E]);
     }
     __syncthreads();
-    // the union, in parallel over the n*K picks (pick p = t*K + k): a pick is its expert's first when no earlier pick
-    // has the expert; its expert's union slot = the number of distinct smaller experts
+    // the union of the n*K picks (pick p = t*K + k) in ascending expert id: a member's slot is the number of members
+    // below it (popcounts of the bit set)
     const int P = n * K, p = threadIdx.x;
-    if (p < P) s_ids[p] = out->ids[p];
-    __syncthreads();
     if (p < P) {
         const int e = s_ids[p];
-        bool first = true;
-        for (int q = 0; q < p; ++q) first &= s_ids[q] != e;
-        s_first[p] = first ? 1 : 0;
+        out->ids[p] = e;
+        out->w[p] = s_w[p];
+        atomicOr(&s_bits[e >> 5], 1u << (e & 31));
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int c = __popc(s_bits[lane]);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        s_base[lane] = incl - c;
+        if (lane == 31) s_base[32] = incl;
+        // the members' ids into their slots
+        uint32_t bits = s_bits[lane];
+        int u = incl - c;
+        while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            out->ex[u++] = 32 * lane + b;
+        }
     }
     __syncthreads();
     if (p < P) {
-        const int e = s_ids[p];
-        int r = 0;
-        for (int q = 0; q < P; ++q) r += s_first[q] && s_ids[q] < e;
-        s_rank[p] = r;
+        const int e = s_ids[p], w = e >> 5;
+        const int u = s_base[w] + __popc(s_bits[w] & ((1u << (e & 31)) - 1u));
+        const int t = p / K;
+        atomicOr(&s_mask[u], 1 << t);
+        out->slot[u][t] = p;
     }
     __syncthreads();
-    if (p < P && s_first[p]) {
-        const int u = s_rank[p], e = s_ids[p];
-        out->ex[u] = e;
-        int m = 0;
-        for (int t = 0; t < kMaxTok; ++t) out->slot[u][t] = 0;
-        for (int q = 0; q < P; ++q)
-            if (s_ids[q] == e) {
-                m |= 1 << (q / K);
-                out->slot[u][q / K] = q;
-            }
-        out->mask[u] = m;
-    }
-    if (p == 0) {
-        int nu = 0;
-        for (int q = 0; q < P; ++q) nu += s_first[q];
+    const int nu = s_base[32];
+    if (threadIdx.x < nu) out->mask[threadIdx.x] = s_mask[threadIdx.x];
+    if (threadIdx.x == 0) {
         out->n_union = nu;
         if (union_acc) atomicAdd(union_acc, nu);
     }

@@ -116,8 +116,21 @@ __device__ inline void route_row(const float *__restrict__ logits, int E, int K,
     for (int e = lane; e < E; e += 32) p[e] = expf_cr(__fsub_rn(logits[e], mx));
     __syncwarp();
     float sum = 0.0f;
-    if (lane == 0)
-        for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+    if (lane == 0) {   // in expert order; the loads four at a time, issued ahead of the adds
+        int e = 0;
+        if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+            const float4 *p4 = reinterpret_cast<const float4 *>(p);
+#pragma unroll 4
+            for (; e + 4 <= E; e += 4) {
+                const float4 v = p4[e >> 2];
+                sum = __fadd_rn(sum, v.x);
+                sum = __fadd_rn(sum, v.y);
+                sum = __fadd_rn(sum, v.z);
+                sum = __fadd_rn(sum, v.w);
+            }
+        }
+        for (; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+    }
     sum = __shfl_sync(0xffffffffu, sum, 0);
     __syncwarp();
     for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
