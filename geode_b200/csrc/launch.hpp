@@ -100,20 +100,22 @@ inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }
 
-// The bf16 GEMV (router, Gated DeltaNet a/b): kBf16Rows rows per CTA. w and x 16-byte aligned, cols and xstride
-// multiples of 8 and 4, n <= kMaxTok.
+// The bf16 GEMV (router, Gated DeltaNet a/b): a CTA per (kBf16Rows rows, group of kBf16Tokens tokens). w and x 16-byte
+// aligned, cols a multiple of 32, xstride of 4, n <= kMaxTok.
 inline int launch_bf16_gemv(const uint16_t *w, int rows, int cols, const float *x, int xstride, int n, float *y,
                             int ystride, uint32_t *status, cudaStream_t st, bool pdl) {
-    if (!w || !x || !y || rows <= 0 || cols <= 0 || cols % 8 || xstride % 4 || n < 1 || n > kMaxTok ||
+    if (!w || !x || !y || rows <= 0 || cols <= 0 || cols % 32 || xstride % 4 || n < 1 || n > kMaxTok ||
         (reinterpret_cast<uintptr_t>(w) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
         return GCUDA_E_ARG;
-    const size_t smem = bf16_gemv_smem(cols, n);
+    const size_t smem = bf16_gemv_smem(cols);
     if (smem > static_cast<size_t>(kMaxDynSmem)) return GCUDA_E_ARG;
     static const bool opted =
         cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) == cudaSuccess;
     if (!opted) return GCUDA_E_CUDA;
-    return launch_ex(k_bf16_gemv, dim3((rows + kBf16Rows - 1) / kBf16Rows), dim3(kBf16Rows * 32), smem, st, pdl, w, rows,
-                     cols, x, xstride, n, y, ystride, status) == cudaSuccess
+    const int groups = (n + kBf16Tokens - 1) / kBf16Tokens;
+    const int rblocks = (rows + kBf16Rows - 1) / kBf16Rows;
+    return launch_ex(k_bf16_gemv, dim3(rblocks * groups), dim3(kBf16Rows * 32), smem, st, pdl, w, rows, cols, x, xstride, n,
+                     y, ystride, status) == cudaSuccess
                ? GCUDA_OK
                : GCUDA_E_CUDA;
 }

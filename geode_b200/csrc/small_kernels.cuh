@@ -24,13 +24,18 @@ __device__ __forceinline__ void bf16_dot8(const uint16_t *__restrict__ w, const 
     out = a;
 }
 
-// kBf16Rows rows per CTA, one warp per row: lane (j = lane & 7, tg = lane >> 3) carries partial sum j of tokens tg and
-// tg + 4. The CTA's rows (contiguous) arrive by one bulk copy issued before the wait for the previous kernel (weights do
-// not depend on it); x is staged after it, token rows padded by 8 floats (the four tg lanes hit different banks).
-// Bits as bf16_dot8's. w 16-byte aligned, cols % 8 == 0. Dynamic smem: bf16_gemv_smem(cols, n).
-constexpr int kBf16Rows = 8;
-__host__ __device__ inline size_t bf16_gemv_smem(int cols, int n) {
-    return 16 + static_cast<size_t>(kBf16Rows) * cols * 2 + static_cast<size_t>(n) * (cols + 8) * 4;
+// A CTA per (kBf16Rows rows, group of kBf16Tokens token columns), a warp per row: lane (j = lane & 7, t = lane >> 3)
+// carries partial sum j of token 4 * group + t, a chain over the columns j, j + 8, ... (cols / 8 long, the reference's
+// order). Small CTAs, so the rows' chains spread over the SMs. The rows (contiguous) arrive by one bulk copy issued
+// before the wait for the previous kernel (weights do not depend on it); the group's activations are staged after it
+// transposed - xs[t][j][i] = x[t][8 i + j], each (t, j) run padded by 4 floats - so a lane reads four of its columns
+// in one load and the 32 lanes' loads hit distinct banks. Bits as bf16_dot8's. w 16-byte aligned, cols % 32 == 0.
+// Dynamic smem: bf16_gemv_smem(cols).
+constexpr int kBf16Rows = 4;     // rows (warps) per CTA
+constexpr int kBf16Tokens = 4;   // token columns per CTA
+__host__ __device__ inline int bf16_run(int cols) { return cols / 8 + 4; }
+__host__ __device__ inline size_t bf16_gemv_smem(int cols) {
+    return 16 + static_cast<size_t>(kBf16Rows) * cols * 2 + static_cast<size_t>(kBf16Tokens) * 8 * bf16_run(cols) * 4;
 }
 
 __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__restrict__ w, int rows, int cols,
@@ -40,7 +45,10 @@ __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__
     uint64_t *bar = reinterpret_cast<uint64_t *>(sm);
     uint16_t *ws = reinterpret_cast<uint16_t *>(sm + 16);
     float *xs = reinterpret_cast<float *>(sm + 16 + static_cast<size_t>(kBf16Rows) * cols * 2);
-    const int r0 = blockIdx.x * kBf16Rows, nr = min(kBf16Rows, rows - r0);
+    const int groups = (n + kBf16Tokens - 1) / kBf16Tokens;
+    const int r0 = (blockIdx.x / groups) * kBf16Rows, t0 = (blockIdx.x % groups) * kBf16Tokens;
+    const int nr = min(kBf16Rows, rows - r0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, t = lane >> 3;
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         fence_barrier_init();
@@ -50,57 +58,58 @@ __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    const int xs_stride = cols + 8;
-    {   // (loads issued in batches before their stores: one round trip per batch, not per load)
+    const int run = bf16_run(cols);
+    {   // the group's tokens, transposed (zeros past n); loads in batches ahead of their stores
         constexpr int kB = 8;
-        const int items = n * (cols / 4);
+        const int items = kBf16Tokens * (cols / 4);
         for (int base = threadIdx.x; base < items; base += blockDim.x * kB) {
             float4 v[kB];
 #pragma unroll
             for (int u = 0; u < kB; ++u) {
                 const int i = base + u * blockDim.x;
-                if (i < items)
-                    v[u] = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(i / (cols / 4)) * xstride + 4 * (i % (cols / 4)));
+                v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (i < items) {
+                    const int tt = i / (cols / 4), c = 4 * (i % (cols / 4));
+                    if (t0 + tt < n) v[u] = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + tt) * xstride + c);
+                }
             }
 #pragma unroll
             for (int u = 0; u < kB; ++u) {
                 const int i = base + u * blockDim.x;
-                if (i < items) *reinterpret_cast<float4 *>(xs + (i / (cols / 4)) * xs_stride + 4 * (i % (cols / 4))) = v[u];
+                if (i < items) {
+                    const int tt = i / (cols / 4), c = 4 * (i % (cols / 4));
+                    float *d = xs + (tt * 8 + (c & 7)) * run + (c >> 3);   // columns c .. c+3: j = c % 8 .. +3, i = c / 8
+                    d[0] = v[u].x;
+                    d[run] = v[u].y;
+                    d[2 * run] = v[u].z;
+                    d[3 * run] = v[u].w;
+                }
             }
         }
     }
     __syncthreads();
     const bool landed = mbar_wait_bounded(bar, 0, status);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, tg = lane >> 3;
     if (landed && warp < nr) {
-        const uint16_t *wr = ws + static_cast<size_t>(warp) * cols;
-        const float *x0 = xs + tg * xs_stride, *x1 = xs + (tg + 4) * xs_stride;
-        float a0 = 0.0f, a1 = 0.0f;
-        if (tg + 4 < n) {
-#pragma unroll 8
-            for (int c = j; c < cols; c += 8) {
-                const float wf = __uint_as_float(static_cast<uint32_t>(wr[c]) << 16);
-                a0 = __fadd_rn(a0, __fmul_rn(wf, x0[c]));
-                a1 = __fadd_rn(a1, __fmul_rn(wf, x1[c]));
-            }
-        } else if (tg < n) {
-#pragma unroll 8
-            for (int c = j; c < cols; c += 8) {
-                const float wf = __uint_as_float(static_cast<uint32_t>(wr[c]) << 16);
-                a0 = __fadd_rn(a0, __fmul_rn(wf, x0[c]));
-            }
+        const float *xr = xs + (t * 8 + j) * run;
+        const uint16_t *wr = ws + static_cast<size_t>(warp) * cols + j;
+        float a = 0.0f;
+#pragma unroll 2
+        for (int i = 0; i < cols / 8; i += 4) {
+            const float4 xv = *reinterpret_cast<const float4 *>(xr + i);
+            const float w0 = __uint_as_float(static_cast<uint32_t>(wr[8 * i]) << 16);
+            const float w1 = __uint_as_float(static_cast<uint32_t>(wr[8 * i + 8]) << 16);
+            const float w2 = __uint_as_float(static_cast<uint32_t>(wr[8 * i + 16]) << 16);
+            const float w3 = __uint_as_float(static_cast<uint32_t>(wr[8 * i + 24]) << 16);
+            a = __fadd_rn(a, __fmul_rn(w0, xv.x));
+            a = __fadd_rn(a, __fmul_rn(w1, xv.y));
+            a = __fadd_rn(a, __fmul_rn(w2, xv.z));
+            a = __fadd_rn(a, __fmul_rn(w3, xv.w));
         }
-        // (a lane group of 8 shares tg: the shuffles below stay inside it)
-        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 4));   // j < 4: a_j + a_{j+4}
-        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));   // (a0+a4)+(a1+a5), (a2+a6)+(a3+a7)
-        a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
-        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 4));
-        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
-        a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
-        if (j == 0) {
-            if (tg < n) y[static_cast<size_t>(tg) * ystride + r0 + warp] = a0;
-            if (tg + 4 < n) y[static_cast<size_t>(tg + 4) * ystride + r0 + warp] = a1;
-        }
+        // (a lane group of 8 shares t: the shuffles below stay inside it)
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));   // j < 4: a_j + a_{j+4}
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));   // (a0+a4)+(a1+a5), (a2+a6)+(a3+a7)
+        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+        if (j == 0 && t0 + t < n) y[static_cast<size_t>(t0 + t) * ystride + r0 + warp] = a;
     }
     if (!landed) mbar_wait_bounded(bar, 0, nullptr);   // (the copy may still land: not before the CTA ends)
 }
