@@ -161,16 +161,26 @@ struct GdnArgs {
 // t < n-1 to backup slot t, the last to the state. (Its own kernel: the q and k channels are read by several value
 // heads, so the state may change only after every reader has read it.)
 __global__ void k_gdn_conv(GdnArgs a, int conv_dim, float *__restrict__ out) {
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    const int K = a.K;
+    // the weights and the state before the wait: written long before the previous kernel (the state by this layer's
+    // last step, which every launch since has waited for)
+    float w[8], st[8];
+    if (ch < conv_dim) {
+        for (int k = 0; k < K; ++k) w[k] = a.convw[static_cast<size_t>(ch) * K + k];
+        for (int k = 0; k < K - 1; ++k) st[k] = a.conv_st[static_cast<size_t>(ch) * (K - 1) + k];
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= conv_dim) return;
-    const int K = a.K;
-    const float *w = a.convw + static_cast<size_t>(ch) * K;
-    float st[8];
-    for (int k = 0; k < K - 1; ++k) st[k] = a.conv_st[static_cast<size_t>(ch) * (K - 1) + k];
-    for (int t = 0; t < a.n; ++t) {
-        const float in = a.proj[static_cast<size_t>(t) * conv_dim + ch];
+    float ins[kMaxTok];
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t)
+        if (t < a.n) ins[t] = a.proj[static_cast<size_t>(t) * conv_dim + ch];
+#pragma unroll
+    for (int t = 0; t < kMaxTok; ++t) {
+        if (t >= a.n) break;
+        const float in = ins[t];
         float acc = 0.0f;
         for (int k = 0; k < K - 1; ++k) acc = __fadd_rn(acc, __fmul_rn(w[k], st[k]));
         acc = __fadd_rn(acc, __fmul_rn(w[K - 1], in));
@@ -186,24 +196,55 @@ __global__ void k_gdn_conv(GdnArgs a, int conv_dim, float *__restrict__ out) {
 template <int DK>
 __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     constexpr int R = DK / 8;
-    __shared__ float s_q[kMaxTok][DK], s_k[kMaxTok][DK], s_v[kMaxTok][16], s_o[kMaxTok][16];
+    __shared__ __align__(16) float s_q[kMaxTok][DK], s_k[kMaxTok][DK], s_v[kMaxTok][16], s_o[kMaxTok][16];
     __shared__ float s_beta[kMaxTok], s_decay[kMaxTok], s_ss[kMaxTok], s_red[kMaxTok][4];
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
     cg::cluster_group cluster = cg::this_cluster();
     const int S = a.dv / 16;
     const int vh = blockIdx.x / S, s = blockIdx.x % S;
     const int rep = a.nv / a.nk, kh = vh / rep;
     const int kd = a.nk * a.dk, vd = a.nv * a.dv;
     const int tid = threadIdx.x, n = a.n;
-    // 1. this CTA's conv outputs (k_gdn_conv, in a.proj): q and k of key head kh, the v columns of the strip
+    // the recurrent state into registers before the wait (written by this layer's last step, which every launch since
+    // has waited for): thread (j, rg) holds column j of the strip, rows rg*R .. rg*R+R-1
+    const int j = tid >> 3, rg = tid & 7;
+    const int col = s * 16 + j;
+    float *Sg = a.state + (static_cast<size_t>(vh) * a.dv + col) * DK + rg * R;
+    float Sr[R];
+#pragma unroll
+    for (int r = 0; r < R; r += 4) {
+        const float4 v4 = *reinterpret_cast<const float4 *>(Sg + r);
+        Sr[r] = v4.x, Sr[r + 1] = v4.y, Sr[r + 2] = v4.z, Sr[r + 3] = v4.w;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    // 1. this CTA's conv outputs (k_gdn_conv, in a.proj): q and k of key head kh, the v columns of the strip, as
+    // float4 pieces (DK / 4 of q, of k, 4 of v per token), every load issued before the stores
     const int cd = 2 * kd + vd;
-    for (int c = tid; c < n * (2 * DK + 16); c += blockDim.x) {
-        const int t = c / (2 * DK + 16), cc = c % (2 * DK + 16);
-        const float *row = a.proj + static_cast<size_t>(t) * cd;
-        if (cc < DK) s_q[t][cc] = row[kh * DK + cc];
-        else if (cc < 2 * DK) s_k[t][cc - DK] = row[kd + kh * DK + (cc - DK)];
-        else s_v[t][cc - 2 * DK] = row[2 * kd + vh * a.dv + s * 16 + (cc - 2 * DK)];
+    {
+        constexpr int P = 2 * (DK / 4) + 4;   // pieces per token
+        constexpr int kB = (kMaxTok * P + 127) / 128;
+        float4 v[kB];
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+            const int c = tid + u * 128;
+            if (c < n * P) {
+                const int t = c / P, cc = c % P;
+                const float *row = a.proj + static_cast<size_t>(t) * cd;
+                const float *src = cc < DK / 4 ? row + kh * DK + 4 * cc
+                                 : cc < DK / 2 ? row + kd + kh * DK + 4 * (cc - DK / 4)
+                                               : row + 2 * kd + vh * a.dv + s * 16 + 4 * (cc - DK / 2);
+                v[u] = *reinterpret_cast<const float4 *>(src);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+            const int c = tid + u * 128;
+            if (c < n * P) {
+                const int t = c / P, cc = c % P;
+                float *dst = cc < DK / 4 ? &s_q[t][4 * cc] : cc < DK / 2 ? &s_k[t][4 * (cc - DK / 4)] : &s_v[t][4 * (cc - DK / 2)];
+                *reinterpret_cast<float4 *>(dst) = v[u];
+            }
+        }
     }
     // gates (engine/src/model.cpp:3604-3611): beta = sigmoid(b), decay = exp(-exp(A_log) * softplus(a + dt_bias))
     if (tid < n) {
@@ -232,12 +273,6 @@ __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     }
     __syncthreads();
     // 3. the delta rule, token by token (engine/src/model.cpp:3501-3524)
-    const int j = tid >> 3, rg = tid & 7;
-    const int col = s * 16 + j;
-    float *Sg = a.state + (static_cast<size_t>(vh) * a.dv + col) * DK + rg * R;
-    float Sr[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) Sr[r] = Sg[r];
     for (int t = 0; t < n; ++t) {
         const float decay = s_decay[t], beta = s_beta[t];
         float mem = 0.0f;
