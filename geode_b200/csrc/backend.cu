@@ -241,7 +241,7 @@ int enqueue_step(gcuda *g, int n) {
             a.wk = g->route->w;
             a.K = s.top_k;
         }
-        LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(512), 0, g->st, pdl, a));
+        LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(kNormThreads), 0, g->st, pdl, a));
         return GCUDA_OK;
     };
     auto raw = [&](int id) -> const float * {
@@ -636,7 +636,8 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
     if (g->ready) return fail(g, GCUDA_E_STATE, "setup: already set up");
     cudaSetDevice(g->device);
     const gcuda_shape &s = *shape;
-    if (s.max_tokens < 1 || s.max_tokens > kMaxTok || s.hidden % 64 || s.n_layers <= 0 || s.context <= 0 ||
+    if (s.max_tokens < 1 || s.max_tokens > kMaxTok || s.hidden % 64 || s.hidden > kNormThreads * kNormPer ||
+        s.n_layers <= 0 || s.context <= 0 ||
         (!s.dense && (s.top_k < 1 || s.top_k > 8 || s.n_experts > 1024 || s.moe_ff % 64 || s.shared_ff % 64)) ||
         (s.dense && s.shared_ff % 64) || s.head_dim % 64 || (s.head_dim != 64 && s.head_dim != 128 && s.head_dim != 256) ||
         s.n_heads % std::max(1, s.n_kv_heads) || s.max_tokens * (s.n_heads / std::max(1, s.n_kv_heads)) > 32)

@@ -41,45 +41,12 @@ __global__ void k_embed(const uint8_t *__restrict__ table, int64_t vocab, int H,
 }
 
 // ------------------------------------------------------------------------------------------- norm + quantize ----
-// Per token (one CTA each, 256 threads): h = x * (1 / sqrt(ss / H + eps)) * (1 + w), ss the sum of squares in double
+// Per token (one CTA each, kNormThreads): h = x * (1 / sqrt(ss / H + eps)) * (1 + w), ss the sum of squares in double
 // (engine/src/kernels.cpp:1520-1529); then h quantized per 16 values (quantize_activation). hf may be NULL.
-// Optionally first x += add0 * gs + sum_k w_k * add_k (the MoE combine, below).
-__device__ inline void block_norm_quant(float *xr, int H, const float *__restrict__ w, float eps, float *hf, int8_t *q,
-                                        float *scale, int32_t *bsum) {
-    __shared__ double red[32];
-    double ss = 0.0;
-    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += static_cast<double>(xr[i]) * xr[i];
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(red[0] / H), eps)));
-    // 16 consecutive values per half-warp: thread i of the CTA handles value i (+ blockDim steps)
-    for (int i0 = 0; i0 < H; i0 += blockDim.x) {
-        const int i = i0 + threadIdx.x;
-        const float h = i < H ? __fmul_rn(__fmul_rn(xr[i], inv), __fadd_rn(1.0f, w[i])) : 0.0f;
-        if (hf && i < H) hf[i] = h;
-        float amax = fabsf(h);
-        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-        const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(h, iv))));
-        int s = qv;
-        for (int o = 8; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (i < H) {
-            q[i] = static_cast<int8_t>(qv);
-            if ((i & 15) == 0) {
-                scale[i / 16] = __fdiv_rn(amax, 127.0f);
-                bsum[i / 16] = s;
-            }
-        }
-    }
-    __syncthreads();
-}
+// Optionally first x += gs * shared + sum_k w_k * y_k (the MoE combine). A thread holds the values
+// tid + k * kNormThreads (k < kNormPer) in registers from load to store; the norm weights are read before the wait
+// for the previous kernel (they do not depend on it). H <= kNormThreads * kNormPer.
+constexpr int kNormThreads = 512, kNormPer = 8;
 
 struct NormArgs {
     float *x;                 // [n][H] residual
@@ -96,37 +63,87 @@ struct NormArgs {
     float *trace_moe;         // [n][H] or NULL: the MoE output (tests)
 };
 
-__global__ void k_norm_quant(NormArgs a) {
+__global__ void __launch_bounds__(kNormThreads) k_norm_quant(NormArgs a) {
+    __shared__ double red[kNormThreads / 32];
+    const int tid = threadIdx.x, H = a.H;
+    float wv[kNormPer];
+#pragma unroll
+    for (int k = 0; k < kNormPer; ++k) {
+        const int i = tid + k * kNormThreads;
+        wv[k] = i < H ? __fadd_rn(1.0f, a.w[i]) : 0.0f;
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int t = blockIdx.x;
     if (t >= a.n) return;
-    float *xr = a.x + static_cast<size_t>(t) * a.H;
+    float *xr = a.x + static_cast<size_t>(t) * H;
+    float xv[kNormPer];
+#pragma unroll
+    for (int k = 0; k < kNormPer; ++k) {
+        const int i = tid + k * kNormThreads;
+        xv[k] = i < H ? xr[i] : 0.0f;
+    }
     if (a.sh) {
         // engine/src/model.cpp:4554-4585 then 5363-5365: out = gs * shared; out += w_k * y_k (k in order, w == 0
-        // skipped); x += out
-        // (every pick's row loaded first, independent loads; then the sum in rank order; K <= 8, checked at set-up)
-        for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
-            float o = __fmul_rn(a.gs[t], a.sh[static_cast<size_t>(t) * a.H + i]);
+        // skipped); x += out. Every pick's value loaded before the sum (K <= 8, checked at set-up).
+        const float gs = a.gs[t];
+        float wk[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) wk[kk] = kk < a.K ? a.wk[t * a.K + kk] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < kNormPer; ++k) {
+            const int i = tid + k * kNormThreads;
+            if (i >= H) break;
             float yk[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-                yk[k] = k < a.K ? a.eout[(static_cast<size_t>(t) * a.K + k) * a.H + i] : 0.0f;
+            for (int kk = 0; kk < 8; ++kk) yk[kk] = kk < a.K ? a.eout[(static_cast<size_t>(t) * a.K + kk) * H + i] : 0.0f;
+            float o = __fmul_rn(gs, a.sh[static_cast<size_t>(t) * H + i]);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                if (k >= a.K) break;
-                const float wv = a.wk[t * a.K + k];
-                if (wv == 0.0f) continue;
-                o = __fadd_rn(o, __fmul_rn(wv, yk[k]));
+            for (int kk = 0; kk < 8; ++kk) {
+                if (kk >= a.K) break;
+                if (wk[kk] == 0.0f) continue;
+                o = __fadd_rn(o, __fmul_rn(wk[kk], yk[kk]));
             }
-            if (a.trace_moe) a.trace_moe[static_cast<size_t>(t) * a.H + i] = o;
-            xr[i] = __fadd_rn(xr[i], o);
+            if (a.trace_moe) a.trace_moe[static_cast<size_t>(t) * H + i] = o;
+            xv[k] = __fadd_rn(xv[k], o);
+            xr[i] = xv[k];
         }
-        __syncthreads();
     }
-    block_norm_quant(xr, a.H, a.w, a.eps, a.hf ? a.hf + static_cast<size_t>(t) * a.H : nullptr,
-                     a.q + static_cast<size_t>(t) * a.H, a.scale + static_cast<size_t>(t) * (a.H / 16),
-                     a.bsum + static_cast<size_t>(t) * (a.H / 16));
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < kNormPer; ++k) ss += static_cast<double>(xv[k]) * xv[k];
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    double tot = 0.0;
+#pragma unroll
+    for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tot / H), a.eps)));
+    float *hf = a.hf ? a.hf + static_cast<size_t>(t) * H : nullptr;
+    int8_t *q = a.q + static_cast<size_t>(t) * H;
+    float *scale = a.scale + static_cast<size_t>(t) * (H / 16);
+    int32_t *bsum = a.bsum + static_cast<size_t>(t) * (H / 16);
+    // 16 consecutive values per half-warp
+#pragma unroll
+    for (int k = 0; k < kNormPer; ++k) {
+        const int i = tid + k * kNormThreads;
+        if (k * kNormThreads >= H) break;   // (uniform)
+        const float h = i < H ? __fmul_rn(__fmul_rn(xv[k], inv), wv[k]) : 0.0f;
+        if (hf && i < H) hf[i] = h;
+        float amax = fabsf(h);
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(h, iv))));
+        int sq = qv;
+        for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (i < H) {
+            q[i] = static_cast<int8_t>(qv);
+            if ((i & 15) == 0) {
+                scale[i / 16] = __fdiv_rn(amax, 127.0f);
+                bsum[i / 16] = sq;
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------------- Gated DeltaNet ----
