@@ -149,10 +149,12 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(NormArgs a) {
 // ------------------------------------------------------------------------------------------- Gated DeltaNet ----
 // Model::gdn (engine/src/model.cpp:3527-3688) after its products, for the n tokens of the batch, as one kernel.
 // Grid: nv value heads x S = dv/16 strips, one cluster (S CTAs) per value head; 128 threads per CTA. Thread
-// (j = tid / 8, rg = tid % 8) holds the recurrent state's column j of the strip, rows rg*R .. rg*R+R-1 (R = dk/8)
-// in registers for the whole batch; the column sums over rows reduce across the 8 rg lanes by shuffles.
-// The state layout: [layer][vh][dv column j][dk row i] (a column contiguous). The gated RMSNorm's sum over the
-// head's dv outputs crosses the cluster through distributed shared memory (fixed order: identical on every CTA).
+// (j = tid / 8, rg = tid % 8) holds column j of the strip's recurrent state, rows 32 m + 4 rg .. 32 m + 4 rg + 3 for
+// m < dk / 32 (four float4 per thread at dk = 128), in registers for the whole batch: the eight rg lanes of a column
+// cover 128 contiguous bytes per m, so every state and backup store is whole lines. The column sums over rows reduce
+// across the rg lanes by shuffles. The state layout: [layer][vh][dv column j][dk row i] (a column contiguous). The
+// gated RMSNorm's sum over the head's dv outputs crosses the cluster: every CTA pushes its partial sums into every
+// peer's shared memory, and all add them in rank order (identical on every CTA).
 // Rollback: after each token t < n-1 the conv and recurrent states are written to backup slot t.
 struct GdnArgs {
     const float *proj;    // [n][conv_dim] (qkv product, before the convolution)
@@ -212,151 +214,184 @@ __global__ void k_gdn_conv(GdnArgs a, int conv_dim, float *__restrict__ out) {
 
 template <int DK>
 __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
-    constexpr int R = DK / 8;
+    constexpr int M = DK / 32;   // float4 row chunks per thread
     __shared__ __align__(16) float s_q[kMaxTok][DK], s_k[kMaxTok][DK], s_v[kMaxTok][16], s_o[kMaxTok][16];
-    __shared__ float s_beta[kMaxTok], s_decay[kMaxTok], s_ss[kMaxTok], s_red[kMaxTok][4];
+    __shared__ float s_beta[kMaxTok], s_decay[kMaxTok];
+    __shared__ float s_ss[8][kMaxTok];   // [source rank][token]: the cluster's partial sums of squares (S <= 8)
     cg::cluster_group cluster = cg::this_cluster();
     const int S = a.dv / 16;
     const int vh = blockIdx.x / S, s = blockIdx.x % S;
     const int rep = a.nv / a.nk, kh = vh / rep;
     const int kd = a.nk * a.dk, vd = a.nv * a.dv;
-    const int tid = threadIdx.x, n = a.n;
-    // the recurrent state into registers before the wait (written by this layer's last step, which every launch since
-    // has waited for): thread (j, rg) holds column j of the strip, rows rg*R .. rg*R+R-1
+    const int tid = threadIdx.x, n = a.n, warp = tid >> 5, lane = tid & 31;
+    // (every CTA of the cluster has started before any writes a peer's shared memory: this arrival, waited for below)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    // before the wait, what the previous kernels cannot change: the recurrent state (written by this layer's last
+    // step, which every launch since has waited for), the gates' and the norm's weights
     const int j = tid >> 3, rg = tid & 7;
     const int col = s * 16 + j;
-    float *Sg = a.state + (static_cast<size_t>(vh) * a.dv + col) * DK + rg * R;
-    float Sr[R];
+    float *Sg = a.state + (static_cast<size_t>(vh) * a.dv + col) * DK + 4 * rg;
+    float4 Sr[M];
 #pragma unroll
-    for (int r = 0; r < R; r += 4) {
-        const float4 v4 = *reinterpret_cast<const float4 *>(Sg + r);
-        Sr[r] = v4.x, Sr[r + 1] = v4.y, Sr[r + 2] = v4.z, Sr[r + 3] = v4.w;
+    for (int m = 0; m < M; ++m) Sr[m] = *reinterpret_cast<const float4 *>(Sg + 32 * m);
+    const int gt = tid - 96;   // warp 3's lanes t < n: token t's gates
+    const bool gate = gt >= 0 && gt < n;
+    float nAe = 0.0f, dtb = 0.0f;
+    if (gate) {
+        nAe = -expf_cr(a.A_log[vh]);
+        dtb = a.dt_bias[vh];
     }
+    const int jj = lane & 15;
+    const float gw = a.gnorm[s * 16 + jj];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    // 1. this CTA's conv outputs (k_gdn_conv, in a.proj): q and k of key head kh, the v columns of the strip, as
-    // float4 pieces (DK / 4 of q, of k, 4 of v per token), every load issued before the stores
+    // 1. every load of the previous kernels' outputs at once: this CTA's conv outputs (q and k of key head kh, the
+    // strip's v columns; k_gdn_conv, in a.proj) as float4 pieces, the gate inputs, z of the tokens this warp outputs
     const int cd = 2 * kd + vd;
-    {
-        constexpr int P = 2 * (DK / 4) + 4;   // pieces per token
-        constexpr int kB = (kMaxTok * P + 127) / 128;
-        float4 v[kB];
+    constexpr int P = 2 * (DK / 4) + 4;   // pieces per token
+    constexpr int kB = (kMaxTok * P + 127) / 128;
+    float4 v[kB];
 #pragma unroll
-        for (int u = 0; u < kB; ++u) {
-            const int c = tid + u * 128;
-            if (c < n * P) {
-                const int t = c / P, cc = c % P;
-                const float *row = a.proj + static_cast<size_t>(t) * cd;
-                const float *src = cc < DK / 4 ? row + kh * DK + 4 * cc
-                                 : cc < DK / 2 ? row + kd + kh * DK + 4 * (cc - DK / 4)
-                                               : row + 2 * kd + vh * a.dv + s * 16 + 4 * (cc - DK / 2);
-                v[u] = *reinterpret_cast<const float4 *>(src);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kB; ++u) {
-            const int c = tid + u * 128;
-            if (c < n * P) {
-                const int t = c / P, cc = c % P;
-                float *dst = cc < DK / 4 ? &s_q[t][4 * cc] : cc < DK / 2 ? &s_k[t][4 * (cc - DK / 4)] : &s_v[t][4 * (cc - DK / 2)];
-                *reinterpret_cast<float4 *>(dst) = v[u];
-            }
+    for (int u = 0; u < kB; ++u) {
+        const int c = tid + u * 128;
+        if (c < n * P) {
+            const int t = c / P, cc = c % P;
+            const float *row = a.proj + static_cast<size_t>(t) * cd;
+            const float *src = cc < DK / 4 ? row + kh * DK + 4 * cc
+                             : cc < DK / 2 ? row + kd + kh * DK + 4 * (cc - DK / 4)
+                                           : row + 2 * kd + vh * a.dv + s * 16 + 4 * (cc - DK / 2);
+            v[u] = *reinterpret_cast<const float4 *>(src);
         }
     }
-    // gates (engine/src/model.cpp:3604-3611): beta = sigmoid(b), decay = exp(-exp(A_log) * softplus(a + dt_bias))
-    if (tid < n) {
-        const float av = a.ab[static_cast<size_t>(tid) * 2 * a.nv + vh], bv = a.ab[static_cast<size_t>(tid) * 2 * a.nv + a.nv + vh];
-        s_beta[tid] = sigmoid_cr(bv);
-        const float x = __fadd_rn(av, a.dt_bias[vh]);
-        const float sp = x > 20.0f ? x : static_cast<float>(log1p(exp(static_cast<double>(x))));
-        s_decay[tid] = expf_cr(__fmul_rn(-expf_cr(a.A_log[vh]), sp));
+    float av = 0.0f, bv = 0.0f;
+    if (gate) {
+        av = a.ab[static_cast<size_t>(gt) * 2 * a.nv + vh];
+        bv = a.ab[static_cast<size_t>(gt) * 2 * a.nv + a.nv + vh];
+    }
+    const int zc = vh * a.dv + s * 16 + jj;
+    float zv[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        if (warp + 4 * i < n) zv[i] = a.z[static_cast<size_t>(warp + 4 * i) * vd + zc];
+#pragma unroll
+    for (int u = 0; u < kB; ++u) {
+        const int c = tid + u * 128;
+        if (c < n * P) {
+            const int t = c / P, cc = c % P;
+            float *dst = cc < DK / 4 ? &s_q[t][4 * cc] : cc < DK / 2 ? &s_k[t][4 * (cc - DK / 4)] : &s_v[t][4 * (cc - DK / 2)];
+            *reinterpret_cast<float4 *>(dst) = v[u];
+        }
     }
     __syncthreads();
-    // 2. q, k L2-normalised over dk (eps 1e-6), q times 1/sqrt(dk): one warp per (token, q|k)
-    {
-        const int warp = tid >> 5, lane = tid & 31;
+    if (warp == 3) {
+        // gates (engine/src/model.cpp:3604-3611): beta = sigmoid(b), decay = exp(-exp(A_log) * softplus(a + dt_bias))
+        if (gate) {
+            s_beta[gt] = sigmoid_cr(bv);
+            const float x = __fadd_rn(av, dtb);
+            const float sp = x > 20.0f ? x : static_cast<float>(log1p(exp(static_cast<double>(x))));
+            s_decay[gt] = expf_cr(__fmul_rn(nAe, sp));
+        }
+    } else {
+        // 2. q, k L2-normalised over dk (eps 1e-6), q times 1/sqrt(dk): warp w < 3 takes tokens w, w + 3 (q and k
+        // together)
         const float qscale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(DK)));
-        for (int item = warp; item < 2 * n; item += 4) {
-            const int t = item >> 1;
-            float *v = (item & 1) ? s_k[t] : s_q[t];
-            float ss = 0.0f;
-            for (int i = lane; i < DK; i += 32) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-            ss = warp_sum(ss);
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ss, 1e-6f)));
-            __syncwarp();
-            for (int i = lane; i < DK; i += 32)
-                v[i] = (item & 1) ? __fmul_rn(v[i], inv) : __fmul_rn(__fmul_rn(v[i], inv), qscale);
+        for (int t = warp; t < n; t += 3) {
+            float sq = 0.0f, sk = 0.0f;
+            for (int i = lane; i < DK; i += 32) {
+                sq = __fadd_rn(sq, __fmul_rn(s_q[t][i], s_q[t][i]));
+                sk = __fadd_rn(sk, __fmul_rn(s_k[t][i], s_k[t][i]));
+            }
+            sq = warp_sum(sq);
+            sk = warp_sum(sk);
+            const float iq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sq, 1e-6f)));
+            const float ik = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sk, 1e-6f)));
+            for (int i = lane; i < DK; i += 32) {
+                s_q[t][i] = __fmul_rn(__fmul_rn(s_q[t][i], iq), qscale);
+                s_k[t][i] = __fmul_rn(s_k[t][i], ik);
+            }
         }
     }
     __syncthreads();
-    // 3. the delta rule, token by token (engine/src/model.cpp:3501-3524)
+    // 3. the delta rule, token by token (engine/src/model.cpp:3501-3524); the row sums as M chains, then the shuffles
     for (int t = 0; t < n; ++t) {
         const float decay = s_decay[t], beta = s_beta[t];
-        float mem = 0.0f;
+        float4 kv[M], qv[M];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            Sr[r] = __fmul_rn(Sr[r], decay);
-            mem = __fmaf_rn(Sr[r], s_k[t][rg * R + r], mem);
+        for (int m = 0; m < M; ++m) {
+            kv[m] = *reinterpret_cast<const float4 *>(&s_k[t][32 * m + 4 * rg]);
+            qv[m] = *reinterpret_cast<const float4 *>(&s_q[t][32 * m + 4 * rg]);
         }
+        float pm[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            Sr[m].x = __fmul_rn(Sr[m].x, decay);
+            Sr[m].y = __fmul_rn(Sr[m].y, decay);
+            Sr[m].z = __fmul_rn(Sr[m].z, decay);
+            Sr[m].w = __fmul_rn(Sr[m].w, decay);
+            pm[m] = __fmaf_rn(Sr[m].w, kv[m].w, __fmaf_rn(Sr[m].z, kv[m].z, __fmaf_rn(Sr[m].y, kv[m].y, __fmul_rn(Sr[m].x, kv[m].x))));
+        }
+        float mem = pm[0];
+#pragma unroll
+        for (int m = 1; m < M; ++m) mem = __fadd_rn(mem, pm[m]);
         mem += __shfl_xor_sync(0xffffffffu, mem, 1);
         mem += __shfl_xor_sync(0xffffffffu, mem, 2);
         mem += __shfl_xor_sync(0xffffffffu, mem, 4);
         const float delta = __fmul_rn(__fsub_rn(s_v[t][j], mem), beta);
-        float o = 0.0f;
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            Sr[r] = __fmaf_rn(s_k[t][rg * R + r], delta, Sr[r]);
-            o = __fmaf_rn(Sr[r], s_q[t][rg * R + r], o);
+        for (int m = 0; m < M; ++m) {
+            Sr[m].x = __fmaf_rn(kv[m].x, delta, Sr[m].x);
+            Sr[m].y = __fmaf_rn(kv[m].y, delta, Sr[m].y);
+            Sr[m].z = __fmaf_rn(kv[m].z, delta, Sr[m].z);
+            Sr[m].w = __fmaf_rn(kv[m].w, delta, Sr[m].w);
+            pm[m] = __fmaf_rn(Sr[m].w, qv[m].w, __fmaf_rn(Sr[m].z, qv[m].z, __fmaf_rn(Sr[m].y, qv[m].y, __fmul_rn(Sr[m].x, qv[m].x))));
         }
+        float o = pm[0];
+#pragma unroll
+        for (int m = 1; m < M; ++m) o = __fadd_rn(o, pm[m]);
         o += __shfl_xor_sync(0xffffffffu, o, 1);
         o += __shfl_xor_sync(0xffffffffu, o, 2);
         o += __shfl_xor_sync(0xffffffffu, o, 4);
         if (rg == 0) s_o[t][j] = o;
         if (t + 1 < n) {
-            float *bk = a.state_bk + t * a.bk_state_stride + (static_cast<size_t>(vh) * a.dv + col) * DK + rg * R;
+            float *bk = a.state_bk + t * a.bk_state_stride + (static_cast<size_t>(vh) * a.dv + col) * DK + 4 * rg;
 #pragma unroll
-            for (int r = 0; r < R; ++r) bk[r] = Sr[r];
+            for (int m = 0; m < M; ++m) *reinterpret_cast<float4 *>(bk + 32 * m) = Sr[m];
         }
     }
 #pragma unroll
-    for (int r = 0; r < R; ++r) Sg[r] = Sr[r];
+    for (int m = 0; m < M; ++m) *reinterpret_cast<float4 *>(Sg + 32 * m) = Sr[m];
     __syncthreads();
-    // 4. gated RMSNorm over the head's dv outputs: o / rms(o) * w * silu_fast(z) (engine/src/model.cpp:3670-3682)
+    // 4. gated RMSNorm over the head's dv outputs: o / rms(o) * w * silu_fast(z) (engine/src/model.cpp:3670-3682).
+    // This CTA's sums of squares into slot s of every peer (the peers have started: the arrival above), then one
+    // cluster barrier (release / acquire) before the sums are read.
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
     if (tid < n) {
         float ss = 0.0f;
-        for (int jj = 0; jj < 16; ++jj) ss = __fmaf_rn(s_o[tid][jj], s_o[tid][jj], ss);
-        s_ss[tid] = ss;
+        for (int c = 0; c < 16; ++c) ss = __fmaf_rn(s_o[tid][c], s_o[tid][c], ss);
+        for (int r = 0; r < S; ++r) cluster.map_shared_rank(&s_ss[0][0], r)[s * kMaxTok + tid] = ss;
     }
-    cluster.sync();
-    if (tid < n) {
-        float tot = 0.0f;
-        for (int r = 0; r < S; ++r) {
-            const float *peer = cluster.map_shared_rank(s_ss, r);
-            tot = __fadd_rn(tot, peer[tid]);
-        }
-        s_red[tid][0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.dv)), a.eps)));
-    }
-    cluster.sync();   // (no CTA leaves while a peer still reads its s_ss)
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     // one warp per token: 16 values = lanes 0..15 (lanes 16..31 idle copies), quantized as one block
-    {
-        const int warp = tid >> 5, lane = tid & 31;
-        for (int t = warp; t < n; t += 4) {
-            const int jj = lane & 15;
-            const int c = vh * a.dv + s * 16 + jj;
-            const float zv = a.z[static_cast<size_t>(t) * vd + c];
-            const float h = __fmul_rn(__fmul_rn(__fmul_rn(s_o[t][jj], s_red[t][0]), a.gnorm[s * 16 + jj]), silu_fast_exact(zv));
-            if (a.core_f && lane < 16) a.core_f[static_cast<size_t>(t) * vd + c] = h;
-            float amax = fabsf(h);
-            for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-            const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(h, iv))));
-            int sm = qv;
-            for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-            if (lane < 16) a.q[static_cast<size_t>(t) * vd + c] = static_cast<int8_t>(qv);
-            if (lane == 0) {
-                a.scale[static_cast<size_t>(t) * (vd / 16) + c / 16] = __fdiv_rn(amax, 127.0f);
-                a.bsum[static_cast<size_t>(t) * (vd / 16) + c / 16] = sm;
-            }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int t = warp + 4 * i;
+        if (t >= n) break;
+        float tot = 0.0f;
+        for (int r = 0; r < S; ++r) tot = __fadd_rn(tot, s_ss[r][t]);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.dv)), a.eps)));
+        const float h = __fmul_rn(__fmul_rn(__fmul_rn(s_o[t][jj], inv), gw), silu_fast_exact(zv[i]));
+        if (a.core_f && lane < 16) a.core_f[static_cast<size_t>(t) * vd + zc] = h;
+        float amax = fabsf(h);
+        for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float iv = amax > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(h, iv))));
+        int sm = qv;
+        for (int o = 8; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        if (lane < 16) a.q[static_cast<size_t>(t) * vd + zc] = static_cast<int8_t>(qv);
+        if (lane == 0) {
+            a.scale[static_cast<size_t>(t) * (vd / 16) + zc / 16] = __fdiv_rn(amax, 127.0f);
+            a.bsum[static_cast<size_t>(t) * (vd / 16) + zc / 16] = sm;
         }
     }
 }
