@@ -35,6 +35,8 @@ def cuda_lib() -> C.CDLL:
         "gcuda_op_q4_dequant": (i32, [vp, i64, f32, vp, i32, vp, vp]),
         "gcuda_op_bf16_gemv": (i32, [vp, i32, i32, vp, i32, vp, vp]),
         "gcuda_op_route_topk": (i32, [vp, i32, i32, i32, vp, vp, vp]),
+        "gcuda_op_route_out_bytes": (sz, []),
+        "gcuda_op_route_union": (i32, [vp, i32, i32, i32, vp, sz, vp]),
     }
     for name, (res, args) in sig.items():
         if hasattr(L, name):

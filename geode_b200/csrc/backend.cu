@@ -382,7 +382,7 @@ int enqueue_step(gcuda *g, int n) {
             const int E = s.n_experts;
             RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.router_w), E + 1, H, g->hf, H, n, g->rlog, E + 1,
                                    g->d_status, g->st, pdl));
-            LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(32 * kMaxTok), kMaxTok * E * sizeof(float), g->st, pdl,
+            LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(kRouteThreads), kMaxTok * E * sizeof(float), g->st, pdl,
                                 static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum));
             const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
             const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),

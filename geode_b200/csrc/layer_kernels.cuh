@@ -846,8 +846,15 @@ __global__ void k_attn_merge(MergeArgs a) {
 // route_topk per token (engine/src/model.cpp:4021-4065), the shared expert's gate sigmoid(w . h)
 // (engine/src/model.cpp:4564-4567; its dot product is the router's last row here), and the union of the picked
 // experts (engine/src/model.cpp:4183-4196): ascending expert ids, each with the tokens that picked it and the
-// pick's slot t * K + k. One CTA, a warp per token.
+// pick's slot t * K + k. One CTA of kRouteWarpsPerTok warps per token slot:
+//   1. every warp of token t finds the row's max (each on its own: no barrier), then exps its quarter of the row;
+//   2. warp (t, 0): the sum in expert order (one lane: the float sum is sequential), p = e / sum, then K rounds of
+//      the warp's max p (redux on the bit patterns: p >= 0) and, among lanes holding it, the lowest expert id - the
+//      reference's selection with its tie rule; only the winning lane rescans its experts; warp (t, 1) the gate;
+//   3. every pick's union slot from popcounts of the union's bit set.
 constexpr int kMaxUnion = 64;
+constexpr int kRouteWarpsPerTok = 4;
+constexpr int kRouteThreads = 32 * kRouteWarpsPerTok * kMaxTok;
 struct RouteOut {
     int n_union;
     int ex[kMaxUnion];
@@ -858,63 +865,136 @@ struct RouteOut {
     float gs[kMaxTok];
 };
 
-__global__ void k_route(const float *__restrict__ logits, int n, int E, int K, RouteOut *out, int *union_acc) {
-    extern __shared__ __align__(16) float ps[];   // E floats per warp
+__global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict__ logits, int n, int E, int K,
+                                                          RouteOut *out, int *union_acc) {
+    extern __shared__ __align__(16) float ps[];   // [kMaxTok][E]
     __shared__ int s_ids[kMaxTok * 8];
-    __shared__ float s_w[kMaxTok * 8];
     __shared__ uint32_t s_bits[32];   // the union as a bit set over the experts (E <= 1024)
-    __shared__ int s_base[33];        // per word: the union members before it; [32] the union's size
     __shared__ int s_mask[kMaxUnion];
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // warp w: token w / 4, quarter (w - t) % 4: a token's four warps on the four SM sub-partitions (w % 4), token t's
+    // lead warp (q = 0) on sub-partition t % 4
+    static_assert(kRouteWarpsPerTok == 4, "one warp per sub-partition");
+    const int t = warp >> 2, q = (warp - t) & 3;
     if (threadIdx.x < 32) s_bits[threadIdx.x] = 0;
     if (threadIdx.x < kMaxUnion) s_mask[threadIdx.x] = 0;
-    if (warp < n) {
-        route_row(logits + static_cast<size_t>(warp) * (E + 1), E, K, ps + warp * E, s_ids + warp * K, s_w + warp * K);
-        if (lane == 0) out->gs[warp] = sigmoid_cr(logits[static_cast<size_t>(warp) * (E + 1) + E]);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const bool live = t < n;
+    const float *row = logits + static_cast<size_t>(t) * (E + 1);
+    float *p = ps + static_cast<size_t>(t) * E;
+    if (live) {
+        float mx = -INFINITY;
+        for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
+        mx = warp_max(mx);
+        for (int e = lane + 32 * q; e < E; e += 32 * kRouteWarpsPerTok) p[e] = expf_cr(__fsub_rn(row[e], mx));
+        if (q == 1 && lane == 0) out->gs[t] = sigmoid_cr(row[E]);
     }
     __syncthreads();
-    // the union of the n*K picks (pick p = t*K + k) in ascending expert id: a member's slot is the number of members
-    // below it (popcounts of the bit set)
-    const int P = n * K, p = threadIdx.x;
-    if (p < P) {
-        const int e = s_ids[p];
-        out->ids[p] = e;
-        out->w[p] = s_w[p];
-        atomicOr(&s_bits[e >> 5], 1u << (e & 31));
-    }
-    __syncthreads();
-    if (warp == 0) {
-        const int c = __popc(s_bits[lane]);
-        int incl = c;
+    if (live && q == 0) {
+        float sum = 0.0f;
+        if (lane == 0) {   // in expert order, 32 values' loads ahead of their adds
+            int e = 0;
+            for (; e + 32 <= E; e += 32) {
+                float v[32];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
+                for (int i = 0; i < 32; ++i) v[i] = p[e + i];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) sum = __fadd_rn(sum, v[i]);
+            }
+            for (; e < E; ++e) sum = __fadd_rn(sum, p[e]);
         }
-        s_base[lane] = incl - c;
-        if (lane == 31) s_base[32] = incl;
-        // the members' ids into their slots
-        uint32_t bits = s_bits[lane];
-        int u = incl - c;
-        while (bits) {
-            const int b = __ffs(bits) - 1;
-            bits &= bits - 1;
-            out->ex[u++] = 32 * lane + b;
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        // K rounds: the warp's largest p (the bit patterns order as the values: p >= 0), the lowest id among the lanes
+        // holding it; only the winning lane recomputes its best untaken expert
+        float top = 0.0f, mine = 0.0f;
+        uint32_t lb = 0;
+        int li = 0x7fffffff;
+        if (E <= 256) {
+            float v[8];   // expert lane + 32 s
+            uint32_t taken = 0;
+#pragma unroll
+            for (int s2 = 0; s2 < 8; ++s2) {
+                const int e = lane + 32 * s2;
+                v[s2] = e < E ? __fdiv_rn(p[e], sum) : 0.0f;
+                if (e >= E) taken |= 1u << s2;
+            }
+            auto local_best = [&]() {
+                lb = 0;
+                li = 0x7fffffff;
+#pragma unroll
+                for (int s2 = 0; s2 < 8; ++s2) {
+                    const uint32_t b2 = __float_as_uint(v[s2]);
+                    if (!((taken >> s2) & 1) && (li == 0x7fffffff || b2 > lb)) lb = b2, li = lane + 32 * s2;
+                }
+            };
+            local_best();
+            for (int k = 0; k < K; ++k) {
+                const uint32_t best = __reduce_max_sync(0xffffffffu, li == 0x7fffffff ? 0u : lb);
+                const int bi = static_cast<int>(
+                    __reduce_min_sync(0xffffffffu, li != 0x7fffffff && lb == best ? static_cast<uint32_t>(li) : 0x7fffffffu));
+                const float bv = __uint_as_float(best);
+                top = __fadd_rn(top, bv);
+                if (lane == k) mine = bv;
+                if (lane == 0) s_ids[t * K + k] = bi;
+                if (bi == li) {
+                    taken |= 1u << (bi >> 5);
+                    local_best();
+                }
+            }
+        } else {   // (wider routers: the probabilities stay in shared memory)
+            for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
+            __syncwarp();
+            uint32_t taken = 0;   // bit s: expert lane + 32 s taken
+            auto local_best = [&]() {
+                lb = 0;
+                li = 0x7fffffff;
+                for (int s2 = 0, e = lane; e < E; ++s2, e += 32) {
+                    const uint32_t b2 = __float_as_uint(p[e]);
+                    if (!((taken >> s2) & 1) && (li == 0x7fffffff || b2 > lb)) lb = b2, li = e;
+                }
+            };
+            local_best();
+            for (int k = 0; k < K; ++k) {
+                const uint32_t best = __reduce_max_sync(0xffffffffu, li == 0x7fffffff ? 0u : lb);
+                const int bi = static_cast<int>(
+                    __reduce_min_sync(0xffffffffu, li != 0x7fffffff && lb == best ? static_cast<uint32_t>(li) : 0x7fffffffu));
+                const float bv = __uint_as_float(best);
+                top = __fadd_rn(top, bv);
+                if (lane == k) mine = bv;
+                if (lane == 0) s_ids[t * K + k] = bi;
+                if (bi == li) {
+                    taken |= 1u << (bi >> 5);
+                    local_best();
+                }
+            }
+        }
+        if (lane < K) {
+            const int pk = t * K + lane;
+            out->w[pk] = __fdiv_rn(mine, top);
+        }
+        __syncwarp();
+        if (lane < K) {
+            const int e = s_ids[t * K + lane];
+            out->ids[t * K + lane] = e;
+            atomicOr(&s_bits[e >> 5], 1u << (e & 31));
         }
     }
     __syncthreads();
-    if (p < P) {
-        const int e = s_ids[p], w = e >> 5;
-        const int u = s_base[w] + __popc(s_bits[w] & ((1u << (e & 31)) - 1u));
-        const int t = p / K;
-        atomicOr(&s_mask[u], 1 << t);
-        out->slot[u][t] = p;
+    // each pick's union slot: the members below its expert (popcounts of the bit set)
+    const int P = n * K, pk = threadIdx.x;
+    if (pk < P) {
+        const int e = s_ids[pk], w = e >> 5, tk = pk / K;
+        int u = __popc(s_bits[w] & ((1u << (e & 31)) - 1u));
+        for (int i = 0; i < w; ++i) u += __popc(s_bits[i]);
+        out->ex[u] = e;   // (every pick of the expert writes the same id)
+        out->slot[u][tk] = pk;
+        atomicOr(&s_mask[u], 1 << tk);
     }
     __syncthreads();
-    const int nu = s_base[32];
-    if (threadIdx.x < nu) out->mask[threadIdx.x] = s_mask[threadIdx.x];
+    int nu = 0;
+    for (int i = 0; i < (E + 31) / 32; ++i) nu += __popc(s_bits[i]);
+    if (static_cast<int>(threadIdx.x) < nu) out->mask[threadIdx.x] = s_mask[threadIdx.x];
     if (threadIdx.x == 0) {
         out->n_union = nu;
         if (union_acc) atomicAdd(union_acc, nu);

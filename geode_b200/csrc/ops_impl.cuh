@@ -79,4 +79,16 @@ int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, 
     return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }
 
+size_t gcuda_op_route_out_bytes(void) { return sizeof(RouteOut); }
+
+int gcuda_op_route_union(const float *d_logits, int n, int E, int K, void *d_out, size_t out_bytes, void *stream) {
+    if (!d_logits || !d_out || n < 1 || n > kMaxTok || E < 1 || E > 1024 || K < 1 || K > 8 || K > E ||
+        out_bytes < sizeof(RouteOut))
+        return GCUDA_E_ARG;
+    k_route<<<1, kRouteThreads, kMaxTok * E * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+        d_logits, n, E, K, static_cast<RouteOut *>(d_out), nullptr);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
 }  // extern "C"

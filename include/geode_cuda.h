@@ -182,6 +182,15 @@ int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, cons
 int gcuda_op_bf16_gemv(const uint16_t *d_w, int rows, int cols, const float *d_x, int n, float *d_y, void *stream);
 /* route_topk (engine/src/model.cpp:4021-4065) for n rows of E logits: ids [n][K], weights [n][K] */
 int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, float *d_weights, void *stream);
+/* The verify step's MoE routing for n <= 8 tokens (one kernel): route_topk per token (engine/src/model.cpp:4021-4065),
+ * the shared expert's gate sigmoid (engine/src/model.cpp:4564-4567) and the union of the picked experts
+ * (engine/src/model.cpp:4183-4196). d_logits: n rows of E + 1 floats (E router logits, then the shared expert's gate
+ * logit); E <= 1024, K <= 8. d_out (out_bytes >= gcuda_op_route_out_bytes()) receives, as 32-bit fields:
+ *   int n_union; int ex[64] (union members, ascending ids); int mask[64] (bit t: token t picked ex[u]);
+ *   int slot[64][8] (slot[u][t] = t * K + k of that pick, where mask bit t is set); int ids[64] ([n][K]);
+ *   float w[64] ([n][K] normalised weights); float gs[8] (the shared expert's gate per token). */
+size_t gcuda_op_route_out_bytes(void);
+int gcuda_op_route_union(const float *d_logits, int n, int E, int K, void *d_out, size_t out_bytes, void *stream);
 
 /* gcuda_spec_reject without a handle and without allocating: for callers that must not allocate device memory when
  * they call it (a serving loop that holds a fixed device-memory budget, or one that cannot take the implicit

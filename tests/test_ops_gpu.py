@@ -125,6 +125,47 @@ def test_route_topk_bit_exact(L, O):
         assert np.array_equal(w[t].cpu().numpy().view(np.uint32), rw.view(np.uint32))
 
 
+@pytest.mark.parametrize("n,E,K", [(5, 256, 8), (8, 128, 8), (1, 64, 4), (3, 1024, 8)])
+def test_route_union_bit_exact(L, O, n, E, K):
+    """The in-step routing kernel: each token's picks and weights bit-exact against route_topk, exact ties going to the
+    lower id; the union ascending with every pick's slot and token mask; the shared expert's gate."""
+    rng = np.random.default_rng(E + n)
+    lg = (rng.standard_normal((n, E + 1)) * 2).astype(np.float32)
+    lg[0, 5] = lg[0, 9] = lg[0, 40] = lg[0, :E].max() + 0.5   # a three-way tie at the top
+    if n > 1:
+        lg[1, :E] = lg[0, :E]                                  # two tokens with the same picks
+    if n > 2:
+        lg[2, 3:E] = -200.0                                    # 3 non-zero probabilities: K - 3 picks tie at 0
+    size = L.gcuda_op_route_out_bytes()
+    out = torch.zeros(size, dtype=torch.uint8, device="cuda")
+    assert L.gcuda_op_route_union(_p(_dev(lg)), n, E, K, _p(out), size, None) == 0
+    torch.cuda.synchronize()
+    raw = out.cpu().numpy().view(np.int32)
+    nu, ex, mask = raw[0], raw[1:65], raw[65:129]
+    slot = raw[129:129 + 512].reshape(64, 8)
+    ids = raw[641:705][:n * K].reshape(n, K)
+    w = raw[705:769].view(np.float32)[:n * K].reshape(n, K)
+    gs = raw[769:777].view(np.float32)[:n]
+    picks = []
+    for t in range(n):
+        rid, rw = op.oracle_route_topk(O, np.ascontiguousarray(lg[t, :E]), K)
+        assert np.array_equal(ids[t], rid), t
+        assert np.array_equal(w[t].view(np.uint32), rw.view(np.uint32)), t
+        picks.append(list(rid))
+        x = np.float32(lg[t, E])
+        ref_gs = np.float32(1.0) / (np.float32(1.0) + np.float32(np.exp(-np.float64(x))))
+        assert gs[t].view(np.uint32) == np.float32(ref_gs).view(np.uint32)
+    union = sorted({int(e) for p in picks for e in p})
+    assert nu == len(union) and list(ex[:nu]) == union
+    for u, e in enumerate(union):
+        m = 0
+        for t in range(n):
+            if e in picks[t]:
+                m |= 1 << t
+                assert slot[u, t] == t * K + picks[t].index(e)
+        assert mask[u] == m
+
+
 @pytest.mark.parametrize("temperature,top_p,top_k", [(0.7, 0.95, 20), (1.0, 1.0, 0), (0.5, 0.8, 64)])
 def test_spec_reject_bit_exact(L, O, temperature, top_p, top_k):
     """Rejection sampling (not in the reference; the oracle restates Leviathan et al.'s algorithm): accepted lengths
