@@ -26,8 +26,12 @@ def _shapes():
     heads = synth.ModelShape("heads-moe", "qwen35moe", 512, 4, 2048, synth.hybrid_types(4), n_heads=4, n_kv_heads=2,
                              head_dim=256, gdn_k_heads=2, gdn_v_heads=4, gdn_k_dim=128, gdn_v_dim=128, n_experts=32,
                              top_k=8, moe_ff=128, shared_ff=128, ctx=1100)
+    # wide enough that the expert GEMVs take their streaming shapes (warp pairs on gate_up, one-tile units on down)
+    wide = synth.ModelShape("wide-moe", "qwen35moe", 1024, 4, 4096, synth.hybrid_types(4), n_heads=4, n_kv_heads=2,
+                            head_dim=256, gdn_k_heads=2, gdn_v_heads=4, gdn_k_dim=128, gdn_v_dim=128, n_experts=64,
+                            top_k=8, moe_ff=256, shared_ff=256, ctx=1100)
     dense = synth.tiny_shape("qwen35", n_layers=4, ctx=640)
-    return {"tiny-moe": tiny, "heads-moe": heads, "tiny-dense": dense}
+    return {"tiny-moe": tiny, "heads-moe": heads, "wide-moe": wide, "tiny-dense": dense}
 
 
 SHAPES = _shapes()
