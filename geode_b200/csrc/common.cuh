@@ -39,6 +39,14 @@ __device__ __forceinline__ void mma_s8_16816(int32_t (&d)[4], uint32_t a0, uint3
         : "r"(a0), "r"(a1), "r"(b), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
 }
 
+// the same with unsigned A (the weight codes as 16 c, 0..240)
+__device__ __forceinline__ void mma_u8s8_16816(int32_t (&d)[4], uint32_t a0, uint32_t a1, uint32_t b, const int32_t (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]));
+}
+
 // D (16x8 f32) = A (16x16 f16, row) * B (16x8 f16, col) + C
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
     asm volatile(

@@ -5,8 +5,8 @@
 //     units' groups into its own shared-memory ring with cp.async and adds every product into the chain as it comes;
 //   - fan-in (fan_units): for launches with few units; the whole CTA works on one unit, producer warps leave each
 //     group's products in a shared slot and chain warps add the slots in block order.
-// Both compute a group's products the same way (group_products): int8 mma.sync block sums whose accumulator starts
-// at 1.5 * 2^23 - 15 * bsum (so float(isum) is one subtraction), then f32x2 products.
+// Both compute a group's products the same way (group_products): int8 mma.sync block sums of the codes as 16 c whose
+// accumulator starts at 1.5 * 2^23 - 120 * bsum (so float(8 isum) is one subtraction), then f32x2 products.
 #pragma once
 
 #include "q4_gemv.cuh"
@@ -44,14 +44,6 @@ __device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return sta
 __device__ __forceinline__ float lo_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v)); }
 __device__ __forceinline__ float hi_f(uint64_t v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
 
-// E4M3 byte -> float, exactly, on the integer and FMA pipes: the low 7 bits placed as an f32 exponent/mantissa
-// (bits 20..26) give 2^(e-127) (1 + m/8) for e >= 1 and the denormal m 2^-129 for e = 0; times 2^120 that is the
-// E4M3 value 2^(e-7) (1 + m/8), resp. m 2^-9 (engine/src/kernels.cpp:39-52). The sign is bit 7. (0x7F / 0xFF, the
-// format's NaN, decode as +-480 here; the quantizer never emits them.)
-__device__ __forceinline__ float e4m3_alu(uint32_t b) {
-    return __fmul_rn(__uint_as_float(((b & 0x80u) << 24) | ((b & 0x7Fu) << 20)), 0x1p120f);
-}
-
 // Activation images (stage_image below): an image's per-(group, tig) entry of accumulator inits and activation
 // scales is kCsEntry bytes; a warp's own image of sg groups (launches whose units multiply different activations)
 // takes warp_act_bytes(sg), the CTA's shared image of all K act_smem_bytes(K).
@@ -77,7 +69,7 @@ struct GemvShape {
 // zeros), token stride ts: act word (t, gl, tig, j) at t * ts + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
 // .. + 3); cs per (gl, tig) kCsEntry bytes at kMaxTok * ts + (gl * 4 + tig) * kCsEntry: for each block j the mma's
 // accumulator quad (cinit(2 tig), cinit(2 tig + 1), cinit(2 tig), cinit(2 tig + 1)), then (ascale(2 tig),
-// ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 15 * bsum. Threads `me` of `nthr` share the blocks; a thread
+// ascale(2 tig + 1)) per block. cinit = 1.5 * 2^23 - 120 * bsum. Threads `me` of `nthr` share the blocks; a thread
 // loads one block of every token (16 bytes each) before it stores any.
 template <typename Src>
 __device__ inline void stage_image(const ActSet &a, const Src &src, int g0, int ng, int ts, uint8_t *img, int me, int nthr) {
@@ -116,7 +108,7 @@ __device__ inline void stage_image(const ActSet &a, const Src &src, int g0, int 
             *reinterpret_cast<uint32_t *>(row + 32) = v[u].z;
             *reinterpret_cast<uint32_t *>(row + 48) = v[u].w;
             int32_t *base_cs = reinterpret_cast<int32_t *>(img + kMaxTok * ts + (gl * 4 + t / 2) * kCsEntry);
-            const int32_t ci = static_cast<int32_t>(kBiasBits) - 15 * bs[u];
+            const int32_t ci = static_cast<int32_t>(kBiasBits) - 120 * bs[u];
             base_cs[4 * j + (t % 2)] = ci;
             base_cs[4 * j + (t % 2) + 2] = ci;
             reinterpret_cast<float *>(base_cs)[16 + 2 * j + (t % 2)] = sc[u];
@@ -139,11 +131,14 @@ __device__ inline void stage_full(const ActSet &a, int ncols, uint8_t *img) {
 // layout group_products reads: [tile][block][gid][e(gid), e(gid), e(gid + 8), e(gid + 8)].
 __device__ __forceinline__ void decode_scales(uint32_t word, int lane, float *e4p) {
     const int tile = lane >> 4, w = lane & 15;
+    // E4M3 pairs through the hardware conversion (exact: every E4M3 value is an f16; 0x7F / 0xFF, the format's NaN,
+    // decode as NaN as in engine/src/kernels.cpp:39-52)
+    const float2 e01 = e4m3x2_to_float2(static_cast<uint16_t>(word & 0xFFFFu));
+    const float2 e23 = e4m3x2_to_float2(static_cast<uint16_t>(word >> 16));
+    const float e[4] = {e01.x, e01.y, e23.x, e23.y};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float e = e4m3_alu((word >> (8 * j)) & 0xFFu);
-        *reinterpret_cast<float2 *>(e4p + ((tile * 4 + j) * 8 + (w & 7)) * 4 + (w >> 3) * 2) = make_float2(e, e);
-    }
+    for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float2 *>(e4p + ((tile * 4 + j) * 8 + (w & 7)) * 4 + (w >> 3) * 2) = make_float2(e[j], e[j]);
 }
 
 // One group of both tiles: for block j = 0..3 the products p[0..3] = tile A (row gid: the token pair (2 tig,
@@ -169,14 +164,15 @@ __device__ __forceinline__ void group_products(const uint4 wa, const uint4 wb, c
         const uint4 cq = ld_shared_v4(cs + 16 * j);   // the block's accumulator quad
         const int32_t cinit[4] = {static_cast<int32_t>(cq.x), static_cast<int32_t>(cq.y), static_cast<int32_t>(cq.z),
                                   static_cast<int32_t>(cq.w)};
-        mma_s8_16816(dA, (wA[j] << 1) & 0x1E1E1E1Eu, (wA[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
+        mma_u8s8_16816(dA, (wA[j] << 4) & 0xF0F0F0F0u, wA[j] & 0xF0F0F0F0u, bv[j], cinit);
         const uint4 eA = ld_shared_v4(e4p + ((0 * 4 + j) * 8 + gid) * 4);
-        // float(isum) = bits(bias + isum) - bias; p = float(isum) * (e4m3 * ascale)
+        // float(8 isum) = bits(bias + 8 isum) - bias; p8 = float(8 isum) * (e4m3 * ascale) = 8 p exactly (a power of two:
+        // the same rounding), and the chain of p8 is 8 times the chain of p; the epilogue multiplies by global / 8
         const uint64_t FAg = f2_sub(pack2(dA[0], dA[1]), bias2), FAh = f2_sub(pack2(dA[2], dA[3]), bias2);
         uint64_t p[4] = {f2_mul_sep(FAg, f2_mul(pack2(eA.x, eA.y), sp[j]), zero),
                          f2_mul_sep(FAh, f2_mul(pack2(eA.z, eA.w), sp[j]), zero), 0, 0};
         if constexpr (!kOne) {
-            mma_s8_16816(dB, (wB[j] << 1) & 0x1E1E1E1Eu, (wB[j] >> 3) & 0x1E1E1E1Eu, bv[j], cinit);
+            mma_u8s8_16816(dB, (wB[j] << 4) & 0xF0F0F0F0u, wB[j] & 0xF0F0F0F0u, bv[j], cinit);
             const uint4 eB = ld_shared_v4(e4p + ((1 * 4 + j) * 8 + gid) * 4);
             const uint64_t FBg = f2_sub(pack2(dB[0], dB[1]), bias2), FBh = f2_sub(pack2(dB[2], dB[3]), bias2);
             p[2] = f2_mul_sep(FBg, f2_mul(pack2(eB.x, eB.y), sp[j]), zero);
@@ -262,6 +258,11 @@ __device__ __forceinline__ uint32_t ldg_stream_u32(const uint8_t *p) {
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
 }
+// (the same with constant offsets on both addresses)
+template <int kDst, int kSrc>
+__device__ __forceinline__ void cp_async16_off(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0+%2], [%1+%3], 16;" ::"r"(dst), "l"(src), "n"(kDst), "n"(kSrc) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -306,27 +307,36 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
             s2 = (sc_t ? T.w1 : T.w0) + 512 + 16 * sc_k;
         }
     };
-    auto issue = [&]() {
+    // two groups (G is even: a pair never straddles two units), one copy group committed for each
+    auto issue2 = [&]() {
         if (p_ok) {
             cp_async16(pdst + d_code, s0);
             cp_async16(pdst + kGroupBytes + d_code, s1);
             if (lane < 8) cp_async16(pdst + d_sc, s2);
-            s0 += kGroupBytes;
-            s1 += kGroupBytes;
-            s2 += kGroupBytes;
-            if (++pg == G) {
+            cp_async_commit();
+            cp_async16_off<kStageBytesR, kGroupBytes>(pdst + d_code, s0);
+            cp_async16_off<kStageBytesR, kGroupBytes>(pdst + kGroupBytes + d_code, s1);
+            if (lane < 8) cp_async16_off<kStageBytesR, kGroupBytes>(pdst + d_sc, s2);
+            cp_async_commit();
+            s0 += 2 * kGroupBytes;
+            s1 += 2 * kGroupBytes;
+            s2 += 2 * kGroupBytes;
+            pg += 2;
+            if (pg == G) {
                 pg = 0;
                 unit_src(++pu);
             }
+        } else {
+            cp_async_commit();
+            cp_async_commit();
         }
-        cp_async_commit();
-        pdst += kStageBytesR;
+        pdst += 2 * kStageBytesR;
         if (pdst == st_end) pdst = ring_s;
     };
     // (get() may read the previous kernel's output: not before prelude() unless `early`)
     if (!early) prelude();
     unit_src(0);
-    for (int k = 0; k < kStreamStages - 2; ++k) issue();
+    for (int k = 0; k < kStreamStages - 2; k += 2) issue2();
     if (early) prelude();
     // consumer
     int cu = 0, cg = 0;
@@ -359,8 +369,7 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
         group_products(ld_shared_v4(st1 + lane * 16), ld_shared_v4(st1 + kGroupBytes + lane * 16), c.e4p + 256,
                        act0 + (cg + 1) * 64, cs0 + (cg + 1) * 4 * kCsEntry, lane, c.zero, chain);
         __syncwarp();   // every lane done with the stages and the scale pairs before they are refilled
-        issue();
-        issue();
+        issue2();
         st = st1 + kStageBytesR == ring_end ? c.ring : st1 + kStageBytesR;
         cg += 2;
         if (cg == G) {
@@ -371,8 +380,8 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
             float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                y0[i] = __fmul_rn(y0[i], U.g0);
-                y1[i] = __fmul_rn(y1[i], U.g1);
+                y0[i] = __fmul_rn(y0[i], __fmul_rn(U.g0, 0.125f));
+                y1[i] = __fmul_rn(y1[i], __fmul_rn(U.g1, 0.125f));
             }
             epi(U, y0, y1, gid, tig);
             acc[0] = acc[1] = acc[2] = acc[3] = 0;
@@ -554,8 +563,8 @@ __device__ void fan_units(const GetUnit &get, const FanCtx &c, const Changes &ch
                 float y1[4] = {yb.x, yb.y, yb.z, yb.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    y0[q] = __fmul_rn(y0[q], U.g0);
-                    y1[q] = __fmul_rn(y1[q], U.g1);
+                    y0[q] = __fmul_rn(y0[q], __fmul_rn(U.g0, 0.125f));
+                    y1[q] = __fmul_rn(y1[q], __fmul_rn(U.g1, 0.125f));
                 }
                 epi(U, y0, y1, gid, tig);
             }

@@ -3,10 +3,13 @@
 //     y[r] = (sum over blocks b, in order, of float(isum_b) * (e4m3(scale_rb) * ascale_b)) * global
 // where isum_b is the integer dot product of block b's 16 weight levels with the token's 16 int8 activations.
 //
-// B200 mapping. The integer block sums run on the tensor cores (mma.sync m16n8k16 s8: 16 rows x one 16-value block x
-// 8 token columns per instruction); the accumulator starts at 1.5 * 2^23 - 15 * bsum, so the result reads back as the
-// exact float of isum with one subtraction (the weights enter as the doubled affine codes 2c, level = 2c - 15). The
-// per-(row, token) f32 chain runs in block order with packed f32x2 operations (each lane IEEE, no contraction).
+// B200 mapping. The integer block sums run on the tensor cores (mma.sync m16n8k16 u8 x s8: 16 rows x one 16-value
+// block x 8 token columns per instruction). The weights enter as 16 c (the affine code in a byte's high nibble, one
+// AND / shift-and-AND per word), so with the accumulator started at 1.5 * 2^23 - 120 * bsum the result reads back as
+// the exact float of 8 isum (level = 2c - 15: 16 c - 120 = 8 level) with one subtraction. Every product and sum of
+// the per-(row, token) f32 chain is then 8 times the reference's, rounded the same way (a power of two, far from
+// the format's limits), and the epilogue's global / 8 (exact) undoes it. The chain runs in block order with packed
+// f32x2 operations (each lane IEEE, no contraction).
 // Rows are relaid once at load time into 16-row tiles whose bytes a lane reads as its mma fragment. A launch runs
 // its units (two tiles x all K) either a warp per unit with the weights streamed through per-warp cp.async rings, or -
 // with few units - a CTA per unit whose producer warps compute the products and whose chain warps add them in order
