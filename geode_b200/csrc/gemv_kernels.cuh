@@ -250,6 +250,16 @@ struct ExpertsArgs {
 inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, GemvShape &r) {
     const int picks = n * K < E ? n * K : E;
     if (pass == kGateUp) {
+        // fewer units than a CTA's warps: warp pairs (stream_pairs), each warp one tile of a unit
+        const int pu = picks * (ff / 16) + sff / 16, per_cta = (pu + sms - 1) / sms;
+        if ((H / 64) % 4 == 0 && per_cta >= kStreamMinUnits && per_cta < kDeepWarps)
+            for (int pairs = kPairWarps / 2; pairs >= 4; --pairs) {
+                const size_t smem = static_cast<size_t>(act_smem_bytes(H)) + pairs * 1024 + 2 * pairs * pair_warp_bytes();
+                if (smem <= static_cast<size_t>(kMaxDynSmem)) {
+                    r = GemvShape{2, pairs, H / 64, smem, kPairStages};
+                    return true;
+                }
+            }
         const int units = picks * (ff / 16) + sff / 16;
         return plan_gemv(H, H, false, static_cast<size_t>(act_smem_bytes(H)), (units + sms - 1) / sms, r);
     }
@@ -373,7 +383,21 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
     auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
         epi_store(U, y0, y1, gid, tig);
     };
-    if constexpr (kStages > 0) {
+    if constexpr (kStages == kPairStages) {
+        // gate_up on warp pairs: the image of h, the pairs' exchange buffers (two of 32 float4), per warp the scale
+        // pairs and the ring
+        const size_t front = static_cast<size_t>(act_smem_bytes(p.H)) + static_cast<size_t>(nslots) * 1024;
+        uint8_t *wbase = smem + front + static_cast<size_t>(warp) * pair_warp_bytes();
+        StreamCtx c;
+        c.e4p = reinterpret_cast<float *>(wbase);
+        c.ring = wbase + 2048;
+        c.img = img;
+        c.img_ts = act_tstride(p.H);
+        c.ngroups = cols / 64;
+        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
+        float4 *xchg = reinterpret_cast<float4 *>(smem + act_smem_bytes(p.H)) + slot * 64;
+        if (gu) stream_pairs(get, c, epi, prelude, warp & 1, xchg, 1 + slot);
+    } else if constexpr (kStages > 0) {
         // per warp: 2 KB of scale pairs, the ring, then (down) the warp's own image of all K
         uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, gu ? 0 : sg);
         uint8_t *own_img = wbase + 2048 + kStages * kStageBytesR;

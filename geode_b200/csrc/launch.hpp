@@ -72,7 +72,8 @@ inline int gemv_opt_in() {
             cudaFuncSetAttribute(k_gemv_static<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_experts<0>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_experts<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) != cudaSuccess)
+            cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_experts<kPairStages>, a, kMaxDynSmem) != cudaSuccess)
             return static_cast<int>(GCUDA_E_CUDA);
         return static_cast<int>(GCUDA_OK);
     }();
