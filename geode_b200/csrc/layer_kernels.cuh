@@ -589,12 +589,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     fetch(c0, 0);
-    // Q rows r = t * G + g -> f16
-    for (int i = tid; i < 32 * HD; i += kAttnThreads) {
-        const int r = i / HD, d = i % HD;
-        float q = 0.0f;
-        if (r < rows) q = a.qn[(static_cast<size_t>(r / G) * a.nh + kh * G + r % G) * HD + d];
-        Qs[r * QS + d] = __float2half_rn(q);
+    // Q rows r = t * G + g -> f16 (rows past n * G zero), walked as (t, g) so that no index divides by G
+    {
+        int t = 0, g = 0;
+        for (int r = 0; r < 32; ++r) {
+            const float *src = r < rows ? a.qn + (static_cast<size_t>(t) * a.nh + kh * G + g) * HD : nullptr;
+            for (int d = tid; d < HD; d += kAttnThreads) Qs[r * QS + d] = __float2half_rn(src ? src[d] : 0.0f);
+            if (++g == G) g = 0, ++t;
+        }
+    }
+    // the token of each score row this lane holds (rows gid + 8 h + 16 m): its causal limit pos + t
+    int lim[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int r = gid + 8 * k;
+        int tt = 0;
+        while ((tt + 1) * G <= r) ++tt;
+        lim[k] = pos + tt;
     }
     if (tid < 32) {
         row_m[tid] = -INFINITY;
@@ -668,9 +679,9 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int r = 16 * m + gid + 8 * (e >> 1), c = 8 * warp + 2 * tig + (e & 1);
-                    const int gp = s0 + c, t = r / G;
+                    const int gp = s0 + c;
                     float v = __fmul_rn(sacc[m][e], __fmul_rn(a.scale, ksc[c]));
-                    if (r >= rows || gp > pos + t || gp >= plim) v = -INFINITY;
+                    if (r >= rows || gp > lim[2 * m + (e >> 1)] || gp >= plim) v = -INFINITY;
                     Ss[r * kAttnSub + c] = v;
                 }
         }

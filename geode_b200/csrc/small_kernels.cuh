@@ -59,32 +59,34 @@ __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
     const int run = bf16_run(cols);
-    {   // the group's tokens, transposed (zeros past n); loads in batches ahead of their stores
-        constexpr int kB = 8;
-        const int items = kBf16Tokens * (cols / 4);
-        for (int base = threadIdx.x; base < items; base += blockDim.x * kB) {
-            float4 v[kB];
+    {   // the group's tokens, transposed (zeros past n): thread i takes float4 column c4 = i, i + blockDim, ... of every
+        // token (no division), every load of a batch issued before its stores
+        const int c4n = cols / 4;
+        for (int c4b = threadIdx.x; c4b < c4n; c4b += blockDim.x * 4) {
+            float4 v[kBf16Tokens][4];
 #pragma unroll
-            for (int u = 0; u < kB; ++u) {
-                const int i = base + u * blockDim.x;
-                v[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                if (i < items) {
-                    const int tt = i / (cols / 4), c = 4 * (i % (cols / 4));
-                    if (t0 + tt < n) v[u] = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + tt) * xstride + c);
-                }
-            }
+            for (int tt = 0; tt < kBf16Tokens; ++tt)
 #pragma unroll
-            for (int u = 0; u < kB; ++u) {
-                const int i = base + u * blockDim.x;
-                if (i < items) {
-                    const int tt = i / (cols / 4), c = 4 * (i % (cols / 4));
-                    float *d = xs + (tt * 8 + (c & 7)) * run + (c >> 3);   // columns c .. c+3: j = c % 8 .. +3, i = c / 8
-                    d[0] = v[u].x;
-                    d[run] = v[u].y;
-                    d[2 * run] = v[u].z;
-                    d[3 * run] = v[u].w;
+                for (int u = 0; u < 4; ++u) {
+                    const int c4 = c4b + u * blockDim.x;
+                    v[tt][u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (c4 < c4n && t0 + tt < n)
+                        v[tt][u] = *reinterpret_cast<const float4 *>(x + static_cast<size_t>(t0 + tt) * xstride + 4 * c4);
                 }
-            }
+#pragma unroll
+            for (int tt = 0; tt < kBf16Tokens; ++tt)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int c4 = c4b + u * blockDim.x;
+                    if (c4 < c4n) {
+                        const int c = 4 * c4;
+                        float *d = xs + (tt * 8 + (c & 7)) * run + (c >> 3);   // columns c .. c+3: j = c % 8 .., i = c / 8
+                        d[0] = v[tt][u].x;
+                        d[run] = v[tt][u].y;
+                        d[2 * run] = v[tt][u].z;
+                        d[3 * run] = v[tt][u].w;
+                    }
+                }
         }
     }
     __syncthreads();
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(kBf16Rows * 32) k_bf16_gemv(const uint16_t *__
         const float *xr = xs + (t * 8 + j) * run;
         const uint16_t *wr = ws + static_cast<size_t>(warp) * cols + j;
         float a = 0.0f;
-#pragma unroll 2
+#pragma unroll 8
         for (int i = 0; i < cols / 8; i += 4) {
             const float4 xv = *reinterpret_cast<const float4 *>(xr + i);
             const float w0 = __uint_as_float(static_cast<uint32_t>(wr[8 * i]) << 16);
