@@ -196,6 +196,7 @@ int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, i
     if (act_cols > 0) p.act = ActSet{act.q, act.scale, act.bsum, act_cols, act.n, act_cols, act_cols / 16};
     p.ncols = n;
     p.allow_half = swiglu ? 0 : 1;
+    p.allow_split = 1;
     p.status = g->d_status;
     return launch_static_gemv(p, g->st, pdl);
 }

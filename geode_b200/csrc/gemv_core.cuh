@@ -211,9 +211,10 @@ constexpr int kWideStages = 6, kDeepStages = 12;
 __host__ __device__ inline int stream_warp_bytes(int stages, int own) {
     return 2048 + stages * kStageBytesR + (own ? (warp_act_bytes(own) + 127) / 128 * 128 : 0);
 }
-// warps per CTA on the streaming path: kStreamWarps (80 registers a thread) for wide launches, kDeepWarps (128) else
+// warps per CTA on the streaming path: kStreamWarps (80 registers a thread) for wide launches, kDeepWarps (128) for
+// the deep rings (kDeepStages, and the K slices' 10)
 constexpr int kDeepWarps = 16;
-__host__ __device__ constexpr int stream_warps(int stages) { return stages == kDeepStages ? kDeepWarps : kStreamWarps; }
+__host__ __device__ constexpr int stream_warps(int stages) { return stages == kDeepStages || stages == 10 ? kDeepWarps : kStreamWarps; }
 
 // A launch's shape: streaming (a warp per unit) when every CTA has kStreamMinUnits units or more, else the fan-in
 // (stages 0; the CTA on one unit at a time, its image img_cols wide). units_per_cta: the units a CTA takes (all CTAs
@@ -267,13 +268,23 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// named barriers (bar.sync / bar.arrive over n threads)
+__device__ __forceinline__ void bar_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+__device__ __forceinline__ void bar_arrive_n(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
 struct StreamCtx {
     float *e4p;           // this warp's 2 KB of (e, e) pairs (two groups)
     uint8_t *ring;        // this warp's ring of stages of kStageBytesR
     const uint8_t *img;   // the activation image (token stride img_ts), groups from 0
     int img_ts;
-    int ngroups;          // K / 64 (even)
+    int ngroups;          // the groups this warp walks per unit (even): K / 64, or its K slice's
     uint64_t zero;        // a +0 pair from runtime values (f2_mul_sep)
+    // K slices (ks > 1): the warps kr = 0 .. ks - 1 of a slice group walk groups [g0, g0 + ngroups) of the same units;
+    // the chains of slices 1.. meet slice 0's at the unit's end through xchg (two buffers of (ks - 1) x 32 lanes x
+    // 32 bytes) at named barrier bar_id (ks warps), added in slice order - f32 accumulation in that order, not the
+    // single chain's. img_g0: the image's group of the slice's first group (g0 for a whole-K image, 0 for a slice's own)
+    int ks = 1, kr = 0, g0 = 0, img_g0 = 0, bar_id = 0;
+    uint4 *xchg = nullptr;
 };
 
 // get(i, U): the warp's i-th unit (false past the end); restage(U) (every lane) before a unit's first group; epi(U, y0,
@@ -298,13 +309,14 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
     uint32_t pdst = ring_s;
     const uint8_t *s0 = nullptr, *s1 = nullptr, *s2 = nullptr;
     bool p_ok;
+    const size_t slice_off = static_cast<size_t>(c.g0) * kGroupBytes;
     auto unit_src = [&](int i) {
         GemvUnit T;
         p_ok = get(i, T);
         if (p_ok) {
-            s0 = T.w0 + lane * 16;
-            s1 = T.w1 + lane * 16;
-            s2 = (sc_t ? T.w1 : T.w0) + 512 + 16 * sc_k;
+            s0 = T.w0 + slice_off + lane * 16;
+            s1 = T.w1 + slice_off + lane * 16;
+            s2 = (sc_t ? T.w1 : T.w0) + slice_off + 512 + 16 * sc_k;
         }
     };
     // two groups (G is even: a pair never straddles two units), one copy group committed for each
@@ -352,9 +364,10 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[q] = f2_add(acc[q], p[q]);
     };
-    const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
-    const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry;
+    const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16 + c.img_g0 * 64;
+    const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry + c.img_g0 * 4 * kCsEntry;
     const uint8_t *ring_end = c.ring + kStreamStages * kStageBytesR;
+    int buf = 0;
     while (c_ok) {
         // items i, i + 1: kStreamStages - 4 groups committed after i + 1's may still fly
         cp_async_wait<kStreamStages - 4>();
@@ -376,14 +389,37 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
             // y = acc * global * 1 (engine/src/kernels.cpp:1320)
             GemvUnit U;
             get(cu, U);
-            float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
-            float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                y0[i] = __fmul_rn(y0[i], __fmul_rn(U.g0, 0.125f));
-                y1[i] = __fmul_rn(y1[i], __fmul_rn(U.g1, 0.125f));
+            bool out = true;
+            if (c.ks > 1) {
+                uint4 *xb = c.xchg + (buf * (c.ks - 1)) * 64 + lane * 2;
+                if (c.kr > 0) {
+                    xb[(c.kr - 1) * 64] = make_uint4(static_cast<uint32_t>(acc[0]), static_cast<uint32_t>(acc[0] >> 32),
+                                                     static_cast<uint32_t>(acc[1]), static_cast<uint32_t>(acc[1] >> 32));
+                    xb[(c.kr - 1) * 64 + 1] = make_uint4(static_cast<uint32_t>(acc[2]), static_cast<uint32_t>(acc[2] >> 32),
+                                                         static_cast<uint32_t>(acc[3]), static_cast<uint32_t>(acc[3] >> 32));
+                    out = false;
+                }
+                bar_sync_n(c.bar_id, 32 * c.ks);
+                if (c.kr == 0)
+                    for (int r = 1; r < c.ks; ++r) {
+                        const uint4 a01 = xb[(r - 1) * 64], a23 = xb[(r - 1) * 64 + 1];
+                        acc[0] = f2_add(acc[0], pack2(a01.x, a01.y));
+                        acc[1] = f2_add(acc[1], pack2(a01.z, a01.w));
+                        acc[2] = f2_add(acc[2], pack2(a23.x, a23.y));
+                        acc[3] = f2_add(acc[3], pack2(a23.z, a23.w));
+                    }
+                buf ^= 1;   // (the next unit's chains go to the other buffer: the barrier above orders its reuse)
             }
-            epi(U, y0, y1, gid, tig);
+            if (out) {
+                float y0[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
+                float y1[4] = {lo_f(acc[2]), hi_f(acc[2]), lo_f(acc[3]), hi_f(acc[3])};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    y0[i] = __fmul_rn(y0[i], __fmul_rn(U.g0, 0.125f));
+                    y1[i] = __fmul_rn(y1[i], __fmul_rn(U.g1, 0.125f));
+                }
+                epi(U, y0, y1, gid, tig);
+            }
             acc[0] = acc[1] = acc[2] = acc[3] = 0;
             cg = 0;
             c_ok = get(++cu, U);
@@ -392,10 +428,6 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
     }
     cp_async_wait<0>();   // (no copy in flight when the warp leaves: the stages are released with the CTA)
 }
-
-// named barriers (bar.sync / bar.arrive over n threads)
-__device__ __forceinline__ void bar_sync_n(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
-__device__ __forceinline__ void bar_arrive_n(int id, int n) { asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 // ------------------------------------------------------------------------------------------- warp pairs ----
 // The streaming path for launches with fewer units than warps: the two warps of a pair each take ONE tile of the

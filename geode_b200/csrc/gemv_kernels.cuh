@@ -124,8 +124,36 @@ struct StaticGemv {
     int wpu, nslots;    // the launch shape (plan_static)
     int allow_half;     // the units may be split into one-tile units (no swiglu unit)
     int half;           // (the fan-in path) units of one tile: n_units * 2 of them
+    int allow_split;    // the units' K may be split over warps (f32 sums in slice order: not the single chain's bits)
     uint32_t *status;
 };
+
+// K slices (stream_units with ks > 1): up to kSplitWarps warps a CTA, ks warps a unit, for launches with too few units
+// to give every warp one (the verify step's projections). The rings (kSplitStages) hold a slice of up to
+// kSplitStages - 2 groups whole, so all of it is requested before the previous kernel ends. ks a power of two, each
+// slice an even number of groups; the xchg buffers after the warps' regions.
+constexpr int kSplitWarps = 16;
+constexpr int kSplitStages = 10;
+__host__ __device__ inline size_t split_xchg_bytes(int slots, int ks) {
+    return static_cast<size_t>(slots) * 2 * (ks - 1) * 1024;
+}
+inline bool plan_split(int cols, int n_units, int sms, GemvShape &r) {
+    const int G = cols / 64;
+    const int slots = (n_units + sms - 1) / sms;
+    if (slots * 2 > kSplitWarps) return false;
+    int ks = 1;
+    while (ks * 2 <= 16 && ks * 2 * slots <= kSplitWarps && G % (4 * ks) == 0) ks *= 2;
+    for (; ks >= 2; ks /= 2) {
+        const int warps = ks * slots;
+        const size_t smem = static_cast<size_t>(act_smem_bytes(cols)) + warps * stream_warp_bytes(kSplitStages, 0) +
+                            split_xchg_bytes(slots, ks);
+        if (smem <= static_cast<size_t>(kMaxDynSmem)) {
+            r = GemvShape{ks, slots, G / ks, smem, kSplitStages};
+            return true;
+        }
+    }
+    return false;
+}
 
 inline bool plan_static(int cols, int n_units, int sms, GemvShape &r) {
     return plan_gemv(cols, cols, false, static_cast<size_t>(act_smem_bytes(cols)), (n_units + sms - 1) / sms, r);
@@ -195,8 +223,17 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         c.ring = wbase + 2048;
         c.img = img;
         c.img_ts = act_tstride(cols);
-        c.ngroups = cols / 64;
+        c.ngroups = (cols / 64) / wpu;
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
+        if (wpu > 1) {   // K slices: warp slot * wpu + kr walks slice kr of its slot's units
+            c.ks = wpu;
+            c.kr = warp % wpu;
+            c.g0 = c.img_g0 = c.kr * c.ngroups;
+            c.bar_id = 1 + slot;
+            c.xchg = reinterpret_cast<uint4 *>(smem + act_smem_bytes(cols) +
+                                               static_cast<size_t>(nslots * wpu) * stream_warp_bytes(kStages, 0) +
+                                               split_xchg_bytes(slot, wpu));
+        }
         stream_units<kStages>(get, c, [](const GemvUnit &) {}, epi, true, prelude);
     } else {
         FanCtx c;

@@ -70,6 +70,7 @@ inline int gemv_opt_in() {
         if (cudaFuncSetAttribute(k_gemv_static<0>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_static<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_static<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemv_static<kSplitStages>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_experts<0>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_experts<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
@@ -84,7 +85,8 @@ inline int gemv_opt_in() {
 // (p.allow_half: a launch with fewer units than SMs runs one-tile units on the fan-in path, twice the CTAs)
 inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     GemvShape r;
-    if (!plan_static(p.act.cols, p.n_units, sm_count(), r)) return GCUDA_E_ARG;
+    const bool split = p.allow_split && plan_split(p.act.cols, p.n_units, sm_count(), r);
+    if (!split && !plan_static(p.act.cols, p.n_units, sm_count(), r)) return GCUDA_E_ARG;
     if (gemv_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
     p.wpu = r.wpu;
     p.nslots = r.nslots;
@@ -92,7 +94,9 @@ inline int launch_static_gemv(StaticGemv p, cudaStream_t st, bool pdl) {
     const int units = p.half ? 2 * p.n_units : p.n_units;
     const int grid = std::max(1, std::min(sm_count(), (units + r.nslots - 1) / r.nslots));
     cudaError_t e;
-    if (r.stages == kWideStages)
+    if (split)
+        e = launch_ex(k_gemv_static<kSplitStages>, dim3(grid), dim3(r.wpu * r.nslots * 32), r.smem, st, pdl, p);
+    else if (r.stages == kWideStages)
         e = launch_ex(k_gemv_static<kWideStages>, dim3(grid), dim3(kStreamWarps * 32), r.smem, st, pdl, p);
     else if (r.stages == kDeepStages)
         e = launch_ex(k_gemv_static<kDeepStages>, dim3(grid), dim3(kDeepWarps * 32), r.smem, st, pdl, p);

@@ -589,14 +589,24 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     fetch(c0, 0);
-    // Q rows r = t * G + g -> f16 (rows past n * G zero), walked as (t, g) so that no index divides by G
+    // Q rows r = t * G + g -> f16 (rows past n * G zero): thread tid takes dim tid % HD of rows tid / HD + kRp * k,
+    // every load issued before the stores; (t, g) stepped along, no index divides by G
     {
-        int t = 0, g = 0;
-        for (int r = 0; r < 32; ++r) {
-            const float *src = r < rows ? a.qn + (static_cast<size_t>(t) * a.nh + kh * G + g) * HD : nullptr;
-            for (int d = tid; d < HD; d += kAttnThreads) Qs[r * QS + d] = __float2half_rn(src ? src[d] : 0.0f);
-            if (++g == G) g = 0, ++t;
+        constexpr int kRp = kAttnThreads / HD;   // rows per pass
+        constexpr int kQ = 32 / kRp;
+        const int d = tid % HD, r0 = tid / HD;
+        int t = 0, g = r0;
+        while (g >= G) g -= G, ++t;
+        float qv[kQ];
+#pragma unroll
+        for (int k = 0; k < kQ; ++k) {
+            const int r = r0 + kRp * k;
+            qv[k] = r < rows ? a.qn[(static_cast<size_t>(t) * a.nh + kh * G + g) * HD + d] : 0.0f;
+            g += kRp;
+            while (g >= G) g -= G, ++t;
         }
+#pragma unroll
+        for (int k = 0; k < kQ; ++k) Qs[(r0 + kRp * k) * QS + d] = __float2half_rn(qv[k]);
     }
     // the token of each score row this lane holds (rows gid + 8 h + 16 m): its causal limit pos + t
     int lim[4];
