@@ -90,19 +90,27 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(NormArgs a) {
         float wk[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) wk[kk] = kk < a.K ? a.wk[t * a.K + kk] : 0.0f;
+        // every value of the thread's columns loaded before any store (x, the output, might alias them for all the
+        // compiler knows: loads after a store would wait a round trip each)
+        float yk[kNormPer][8], shv[kNormPer];
+#pragma unroll
+        for (int k = 0; k < kNormPer; ++k) {
+            const int i = tid + k * kNormThreads;
+            shv[k] = i < H ? a.sh[static_cast<size_t>(t) * H + i] : 0.0f;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+                yk[k][kk] = kk < a.K && i < H ? a.eout[(static_cast<size_t>(t) * a.K + kk) * H + i] : 0.0f;
+        }
 #pragma unroll
         for (int k = 0; k < kNormPer; ++k) {
             const int i = tid + k * kNormThreads;
             if (i >= H) break;
-            float yk[8];
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) yk[kk] = kk < a.K ? a.eout[(static_cast<size_t>(t) * a.K + kk) * H + i] : 0.0f;
-            float o = __fmul_rn(gs, a.sh[static_cast<size_t>(t) * H + i]);
+            float o = __fmul_rn(gs, shv[k]);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
                 if (kk >= a.K) break;
                 if (wk[kk] == 0.0f) continue;
-                o = __fadd_rn(o, __fmul_rn(wk[kk], yk[kk]));
+                o = __fadd_rn(o, __fmul_rn(wk[kk], yk[k][kk]));
             }
             if (a.trace_moe) a.trace_moe[static_cast<size_t>(t) * H + i] = o;
             xv[k] = __fadd_rn(xv[k], o);
@@ -837,14 +845,18 @@ __global__ void k_attn_merge(MergeArgs a) {
     L = 0.0f;
     for (int w = 0; w < nw; ++w) L += s_red[w];
     const int d = tid;
+    // O = sum_c O_c f_c: 16 chunks' loads in flight before their FMAs (two chains)
     float acc0 = 0.0f, acc1 = 0.0f;
-    int c = 0;
-#pragma unroll 4
-    for (; c + 1 < nc; c += 2) {
-        acc0 = fmaf(pp[c * cs + d], s_f[c], acc0);
-        acc1 = fmaf(pp[(c + 1) * cs + d], s_f[c + 1], acc1);
+    for (int c0 = 0; c0 < nc; c0 += 16) {
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = c0 + u < nc ? pp[(c0 + u) * cs + d] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 16; u += 2) {
+            if (c0 + u < nc) acc0 = fmaf(v[u], s_f[c0 + u], acc0);
+            if (c0 + u + 1 < nc) acc1 = fmaf(v[u + 1], s_f[c0 + u + 1], acc1);
+        }
     }
-    if (c < nc) acc0 = fmaf(pp[c * cs + d], s_f[c], acc0);
     const float acc = acc0 + acc1;
     const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
     const float v = __fmul_rn(__fmul_rn(acc, 1.0f / L), sigmoid_cr(gate[d]));
