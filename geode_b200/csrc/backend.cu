@@ -416,10 +416,12 @@ int enqueue_step(gcuda *g, int n) {
                 ea.pass = pass;
                 ea.wpu = r.wpu;
                 ea.nslots = r.nslots;
+                ea.blocked = r.blocked;
                 if (r.stages == kPairStages)
                     LAUNCH_OK(launch_ex(k_gemv_experts<kPairStages>, dim3(sm_count()), dim3(2 * r.nslots * 32), r.smem, g->st, pdl, ea));
                 else if (r.stages == kWideStages)
-                    LAUNCH_OK(launch_ex(k_gemv_experts<kWideStages>, dim3(sm_count()), dim3(kStreamWarps * 32), r.smem, g->st, pdl, ea));
+                    LAUNCH_OK(launch_ex(k_gemv_experts<kWideStages>, dim3(sm_count()),
+                                        dim3((r.blocked ? r.nslots : kStreamWarps) * 32), r.smem, g->st, pdl, ea));
                 else if (r.stages == kDeepStages)
                     LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
                 else

@@ -279,6 +279,7 @@ struct ExpertsArgs {
     ActSet hq, amid, shact;     // amid: [n*K][ff], shact: [n][sff]
     float *eout, *shout;        // [n*K][H], [n][H]
     int wpu, nslots;            // the launch shape (plan_experts)
+    int blocked;                // down: CTA c takes units [c B, (c + 1) B), B = ceil(units / grid), a warp each
     uint32_t *status;
 };
 
@@ -301,6 +302,20 @@ inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, 
         return plan_gemv(H, H, false, static_cast<size_t>(act_smem_bytes(H)), (units + sms - 1) / sms, r);
     }
     const int units = (picks + 1) * (H / 32);
+    // blocked: every CTA's block of consecutive units (at most two experts' worth: B <= H / 32) on one warp each, the
+    // experts' activation images staged once for the CTA - when the worst-case block fits the warps
+    {
+        const int B = (units + sms - 1) / sms, G = ff / 64;
+        const size_t imgs = 2 * static_cast<size_t>(act_smem_bytes(ff));
+        if (G % 2 == 0 && B <= H / 32)
+            for (int w = kStreamWarps; w >= B && w >= 1; --w) {
+                const size_t smem = static_cast<size_t>(w) * stream_warp_bytes(kWideStages, 0) + imgs;
+                if (smem <= static_cast<size_t>(kMaxDynSmem)) {
+                    r = GemvShape{1, w, G, smem, kWideStages, 1};
+                    return true;
+                }
+            }
+    }
     return plan_gemv(ff, ff, true, 0, (units + sms - 1) / sms, r);
 }
 
@@ -337,12 +352,24 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
     const size_t tbH = static_cast<size_t>(tile_bytes(p.H)), tbF = static_cast<size_t>(tile_bytes(p.ff)),
                  tbS = static_cast<size_t>(tile_bytes(p.sff));
     bool ranged = false;
+    const bool blocked = !gu && p.blocked;
+    int ustep = 1, blk0 = 0, blk1 = 0;   // (blocked: the CTA's units [blk0, blk1))
     auto range = [&]() {
         // (read after the dependent-launch wait: the route is the previous kernel's output)
         nu = R.n_union;
         per_ex = gu ? p.ff / 16 : p.H / 32;
         const int sh_units = gu ? p.sff / 16 : p.H / 32;
         total = nu * per_ex + sh_units;
+        if (blocked) {
+            const int B = (total + gridDim.x - 1) / gridDim.x;
+            blk0 = min(total, blockIdx.x * B);
+            blk1 = min(total, blk0 + B);
+            u0 = blk0 + slot;
+            u1 = blk1;
+            ustep = nslots;
+            ranged = true;
+            return;
+        }
         // ranges CTA-major (range r on CTA r % grid): a launch with fewer ranges than slots still spreads over every SM
         const int nslots_all = gridDim.x * nslots, gs = blockIdx.x + gridDim.x * slot;
         const int per = (total + nslots_all - 1) / nslots_all;
@@ -352,7 +379,7 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
     };
     auto get = [&](int i, GemvUnit &U) -> bool {
         if (!ranged) range();
-        const int u = u0 + i;
+        const int u = u0 + i * ustep;
         if (u >= u1) return false;
         const int s = u / per_ex;
         const bool shared = s >= nu;
@@ -435,6 +462,40 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         float4 *xchg = reinterpret_cast<float4 *>(smem + act_smem_bytes(p.H)) + slot * 64;
         if (gu) stream_pairs(get, c, epi, prelude, warp & 1, xchg, 1 + slot);
     } else if constexpr (kStages > 0) {
+      if (blocked) {
+        // down, blocked: per warp 2 KB of scale pairs and the ring; then two images - the block's first expert and the
+        // next (a block spans two at most). The weights' first copies go out before the images are staged.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;");
+        range();
+        const size_t swb = static_cast<size_t>(stream_warp_bytes(kStages, 0));
+        uint8_t *wbase = smem + static_cast<size_t>(warp) * swb;
+        uint8_t *imgs = smem + static_cast<size_t>(nslots) * swb;
+        const int ib = act_smem_bytes(p.ff), its = act_tstride(p.ff);
+        const int s_first = blk0 / max(per_ex, 1);
+        StreamCtx c;
+        c.e4p = reinterpret_cast<float *>(wbase);
+        c.ring = wbase + 2048;
+        c.img = imgs + (u0 < u1 ? (u0 / per_ex - s_first) : 0) * ib;
+        c.img_ts = its;
+        c.ngroups = cols / 64;
+        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
+        auto stage_block = [&]() {
+            // half the threads stage the first expert's image, half the second's (if the block reaches it)
+            const int half = blockDim.x / 2, k = threadIdx.x >= half ? 1 : 0;
+            const int s = s_first + k;
+            if (blk0 < blk1 && s * per_ex < blk1) {
+                const bool shared = s >= nu;
+                const int mask = shared ? (1 << p.n) - 1 : R.mask[s];
+                int rows[kMaxTok];
+                for (int t = 0; t < kMaxTok; ++t) rows[t] = t < p.n && ((mask >> t) & 1) ? (shared ? t : R.slot[s][t]) : -1;
+                stage_image(shared ? p.shact : p.amid, [&](int t) { return rows[t]; }, 0, cols / 64, its, imgs + k * ib,
+                            threadIdx.x - k * half, half);
+            }
+            __syncthreads();
+        };
+        stream_units<kStages>(get, c, [](const GemvUnit &) {}, epi, true, stage_block);
+      } else {
         // per warp: 2 KB of scale pairs, the ring, then (down) the warp's own image of all K
         uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, gu ? 0 : sg);
         uint8_t *own_img = wbase + 2048 + kStages * kStageBytesR;
@@ -447,6 +508,7 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
         own = gu ? nullptr : own_img;
         stream_units<kStages>(get, c, restage, epi, false, prelude);
+      }
     } else {
         // one image for the CTA: h (gate_up, staged in the prelude), or the unit's picks' rows (down, restaged by the
         // producers when the expert changes)
