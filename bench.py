@@ -267,6 +267,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=40, help="(smaller cases for profiling)")
+    ap.add_argument("--ep", action="store_true",
+                    help="N > 1: one sequence over all GPUs, the routed experts striped over them (gcuda_set_ep; strong "
+                         "scaling); without it each GPU verifies its own sequence (replicas, weak scaling)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -281,8 +284,13 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     from geode_b200 import synth
-    from geode_b200.backend import synthetic
+    from geode_b200.backend import synthetic, ep_unique_id
     from geode_b200 import cuda_lib
+    ep = None
+    if args.ep and world > 1:
+        obj = [ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ep = (rank, world, obj[0])
 
     peak, peak_kind = measured_peaks()
     shape = synth.baseline_shape(3)
@@ -291,10 +299,12 @@ def main():
         shape.layer_types = synth.hybrid_types(args.layers)
     context = CTX + args.warmup + args.steps + args.e2e_steps + 64
     t_build = time.perf_counter()
-    be = synthetic(shape, context=context, max_tokens=NTOK, device=local, seed=rank)
-    be.randomize_state(CTX, seed=7 + rank)
+    # (expert parallel: every rank the same model, state and tokens - one sequence)
+    seed = 0 if ep else rank
+    be = synthetic(shape, context=context, max_tokens=NTOK, device=local, seed=seed, ep=ep)
+    be.randomize_state(CTX, seed=7 + seed)
     t_build = time.perf_counter() - t_build
-    rng = np.random.default_rng(rank)
+    rng = np.random.default_rng(seed)
     toks = rng.integers(0, shape.vocab, NTOK).astype(np.int32)
     launches0 = be.launches()
 
@@ -326,7 +336,8 @@ def main():
     union_layer = union_sum / max(1, steps_done * n_moe) if n_moe else 0.0
     mean_ctx = (pos0 + be.pos) / 2
     b = step_bytes(shape, union_layer, mean_ctx)
-    value = world * NTOK * args.steps / (ms * 1e-3)
+    seqs = 1 if ep else world   # sequences the job verifies at once
+    value = seqs * NTOK * args.steps / (ms * 1e-3)
 
     # ---- e2e: the C ABI with host buffers, every step synchronous (tokens in, logits out, accept, keep)
     pinned = torch.empty((NTOK, shape.vocab), dtype=torch.float32, pin_memory=True).numpy()
@@ -350,7 +361,7 @@ def main():
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     e2e_s = max_over_ranks(e2e_s, dist, "cuda")
-    e2e = world * NTOK * args.e2e_steps / e2e_s
+    e2e = seqs * NTOK * args.e2e_steps / e2e_s
 
     roof = gemv_roofline(cuda_lib(), peak)
     cb = None
@@ -362,11 +373,12 @@ def main():
     step_ach = b["total"] / (ms_step * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong" if ep else "weak", "vs_baseline": None,
         "dtype": "q4xint8->f32", "data": "synthetic (random q4 codes / E4M3 scales made on the device; random 8192-position KV)",
         "config": {"workload": "cfg3: MoE 35B-A3B shape verify (40 layers, 256 experts top-8 + shared, vocab 248320), "
                                "1 accepted + 4 drafts, ctx 8192, greedy acceptance + GDN rollback",
-                   "global_batch": NTOK * world, "seq_len": CTX, "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+                   "global_batch": NTOK * seqs, "seq_len": CTX,
+                   "parallelism": f"ep{world}" if ep else f"replicas x{world}" if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2 (20 GB of weights per GPU; no flush)", "layers": shape.n_layers},
         "roofline": roof,
         "step_roofline": {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,

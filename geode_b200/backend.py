@@ -58,6 +58,8 @@ def _sig(L):
         "gcuda_debug_read": (i32, [vp, i32, vp, sz]),
         "gcuda_debug_step_eager": (i32, [vp, vp, i32, i32]),
         "gcuda_synth_q4": (i32, [vp, i64, i64, f32, C.c_uint64]),
+        "gcuda_ep_unique_id": (i32, [vp]),
+        "gcuda_set_ep": (i32, [vp, i32, i32, vp]),
         "gcuda_synth_raw": (i32, [vp, sz, i32, f32, f32, C.c_uint64]),
         "gcuda_synth_embedding": (i32, [vp, i64, i64, f32, C.c_uint64]),
         "gcuda_synth_experts": (i32, [vp, i32, i32, i32, f32, C.c_uint64]),
@@ -85,13 +87,24 @@ class GcudaError(RuntimeError):
 class Backend:
     """One gcuda handle over a geode-pack directory (or, with pack_dir None, a synthetic model: see synthetic())."""
 
-    def __init__(self, pack_dir: Optional[str], context: int, max_tokens: int = 5, device: int = 0):
+    def __init__(self, pack_dir: Optional[str], context: int, max_tokens: int = 5, device: int = 0,
+                 ep: Optional[tuple] = None):
+        """ep: (rank, world, id) - this handle's rank in an expert-parallel group (gcuda_set_ep; id from ep_unique_id()
+        on one rank, the same bytes on every rank)."""
         self.L = L = cuda_lib()
         _sig(L)
         err = C.create_string_buffer(512)
         self.g = L.gcuda_open(device, err, 512)
         if not self.g:
             raise GcudaError("gcuda_open: " + err.value.decode())
+        if ep is not None:
+            rank, world, uid = ep
+            buf = C.create_string_buffer(bytes(uid), len(uid))
+            if L.gcuda_set_ep(self.g, rank, world, buf) != 0:
+                msg = self.error()
+                L.gcuda_close(self.g)
+                self.g = None
+                raise GcudaError("set_ep: " + msg)
         if pack_dir is None:
             return
         with open(os.path.join(pack_dir, "geode.json")) as f:
@@ -262,11 +275,22 @@ class Backend:
         return int(self.L.gcuda_launches(self.g))
 
 
-def synthetic(shape, context: int, max_tokens: int = 5, device: int = 0, seed: int = 0) -> Backend:
+def ep_unique_id() -> bytes:
+    """NCCL's 128-byte id for a new expert-parallel group (made on one rank, handed to all)."""
+    L = cuda_lib()
+    _sig(L)
+    buf = C.create_string_buffer(128)
+    if L.gcuda_ep_unique_id(buf) != 0:
+        raise GcudaError("ep_unique_id: NCCL unavailable")
+    return buf.raw
+
+
+def synthetic(shape, context: int, max_tokens: int = 5, device: int = 0, seed: int = 0,
+              ep: Optional[tuple] = None) -> Backend:
     """A backend over a model of `shape` (geode_b200.synth.ModelShape) whose q4 weights are random bytes made on the
     device (gcuda_synth_*: random codes, E4M3 scales 0x30..0x48) - the same bytes a pack of that shape streams, for
     measuring at full size without writing ~20 GB of pack first."""
-    be = Backend(None, context, max_tokens, device)
+    be = Backend(None, context, max_tokens, device, ep=ep)
     L, g = be.L, be.g
     k = [seed]
 

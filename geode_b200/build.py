@@ -47,7 +47,7 @@ def build_cuda(force: bool = False) -> str:
     for cmd, p in procs:
         if p.wait() != 0:
             raise RuntimeError("nvcc failed: " + " ".join(cmd))
-    subprocess.check_call([NVCC, *ARCH, "-shared", "-o", CUDA_SO, *objs, "-lcudart", "-lcuda"])
+    subprocess.check_call([NVCC, *ARCH, "-shared", "-o", CUDA_SO, *objs, "-lcudart", "-lcuda", "-ldl"])
     return CUDA_SO
 
 

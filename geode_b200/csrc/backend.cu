@@ -2,6 +2,8 @@
 // state, and the verify step (Model::verify_n's Adreno branch, engine/src/model.cpp:1529-1592, redone for sm_100a)
 // recorded once per batch size as a CUDA graph of dependent launches.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstdio>
@@ -58,6 +60,36 @@ struct LayerPlan {
 
 }  // namespace
 
+namespace {
+// NCCL, loaded on first use (single-GPU users need no NCCL): the few functions the expert-parallel step calls
+struct NcclApi {
+    bool tried = false, ok = false;
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+    decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclCommDestroy) comm_destroy = nullptr;
+    decltype(&ncclGetErrorString) error_string = nullptr;
+};
+NcclApi &nccl() {
+    static NcclApi a;
+    if (!a.tried) {
+        a.tried = true;
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (h) {
+            a.get_unique_id = reinterpret_cast<decltype(&ncclGetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+            a.comm_init_rank = reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
+            a.all_reduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(h, "ncclAllReduce"));
+            a.comm_destroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
+            a.error_string = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
+            a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+        }
+    }
+    return a;
+}
+
+}  // namespace
+
 struct gcuda {
     int device = 0;
     cudaStream_t st = nullptr;
@@ -101,6 +133,10 @@ struct gcuda {
     int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
     size_t rej_cap = 0;
     std::vector<void *> allocs;
+    // expert parallelism (gcuda_set_ep): this rank's experts are e % ep_world == ep_rank; the expert outputs meet
+    // through one all-reduce per MoE layer on the handle's stream
+    int ep_rank = 0, ep_world = 1;
+    ncclComm_t comm = nullptr;
 };
 
 namespace {
@@ -384,7 +420,10 @@ int enqueue_step(gcuda *g, int n) {
             RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.router_w), E + 1, H, g->hf, H, n, g->rlog, E + 1,
                                    g->d_status, g->st, pdl));
             LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(kRouteThreads), kMaxTok * E * sizeof(float), g->st, pdl,
-                                static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum));
+                                static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum,
+                                g->ep_rank, g->ep_world));
+            if (g->ep_world > 1)   // (rows of picks other ranks compute stay zero for the all-reduce)
+                LAUNCH_OK(cudaMemsetAsync(g->eout, 0, static_cast<size_t>(n) * s.top_k * H * sizeof(float), g->st));
             const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
             const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
                             *sd = tensor(g, L.sh_down, kQ4Tiled);
@@ -426,6 +465,13 @@ int enqueue_step(gcuda *g, int n) {
                     LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
                 else
                     LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kFanThreads), r.smem, g->st, pdl, ea));
+            }
+            if (g->ep_world > 1) {
+                // every pick's row from the rank that owns its expert (the others hold zeros there: the sum is that row
+                // exactly), so the combine below runs on every rank in rank order as on one GPU
+                const ncclResult_t nr = nccl().all_reduce(g->eout, g->eout, static_cast<size_t>(n) * s.top_k * H, ncclFloat,
+                                                          ncclSum, g->comm, g->st);
+                if (nr != ncclSuccess) return fail(g, GCUDA_E_CUDA, std::string("ncclAllReduce: ") + nccl().error_string(nr));
             }
             RC_OK(norm(next_norm, true, next_hf));
         }
@@ -539,8 +585,37 @@ void gcuda_close(gcuda *g) {
     if (g->rej) cudaFree(g->rej);
     if (g->ev0) cudaEventDestroy(g->ev0);
     if (g->ev1) cudaEventDestroy(g->ev1);
+    if (g->comm) nccl().comm_destroy(g->comm);
     if (g->st) cudaStreamDestroy(g->st);
     delete g;
+}
+
+int gcuda_ep_unique_id(void *id_out) {
+    if (!id_out) return GCUDA_E_ARG;
+    if (!nccl().ok) return GCUDA_E_CUDA;
+    ncclUniqueId id;
+    if (nccl().get_unique_id(&id) != ncclSuccess) return GCUDA_E_CUDA;
+    std::memcpy(id_out, &id, sizeof id);
+    return GCUDA_OK;
+}
+
+int gcuda_set_ep(gcuda *g, int rank, int world, const void *id) {
+    if (!g || world < 1 || rank < 0 || rank >= world || (world > 1 && !id)) return GCUDA_E_ARG;
+    if (g->ready) return fail(g, GCUDA_E_STATE, "set_ep: before gcuda_setup");
+    if (g->comm) return fail(g, GCUDA_E_STATE, "set_ep: already set");
+    g->ep_rank = rank;
+    g->ep_world = world;
+    if (world == 1) return GCUDA_OK;
+    if (!nccl().ok) return fail(g, GCUDA_E_CUDA, "set_ep: libnccl.so.2 not found");
+    cudaSetDevice(g->device);
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof uid);
+    const ncclResult_t r = nccl().comm_init_rank(&g->comm, world, uid, rank);
+    if (r != ncclSuccess) {
+        g->comm = nullptr;
+        return fail(g, GCUDA_E_CUDA, std::string("ncclCommInitRank: ") + nccl().error_string(r));
+    }
+    return GCUDA_OK;
 }
 
 int gcuda_last_error(gcuda *g, char *buf, int len) {

@@ -356,7 +356,7 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
     int ustep = 1, blk0 = 0, blk1 = 0;   // (blocked: the CTA's units [blk0, blk1))
     auto range = [&]() {
         // (read after the dependent-launch wait: the route is the previous kernel's output)
-        nu = R.n_union;
+        nu = R.n_own;   // (this rank's members of the union: all of it on one GPU)
         per_ex = gu ? p.ff / 16 : p.H / 32;
         const int sh_units = gu ? p.sff / 16 : p.H / 32;
         total = nu * per_ex + sh_units;
@@ -384,9 +384,10 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
         const int s = u / per_ex;
         const bool shared = s >= nu;
         const int j = shared ? u - nu * per_ex : u % per_ex;
-        const int e = shared ? 0 : R.ex[s];
-        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = shared ? t : R.slot[s][t];
-        U.tok_mask = shared ? all : R.mask[s];
+        const int su = shared ? 0 : R.own[s];   // the member's index in the union
+        const int e = shared ? 0 : R.ex[su];
+        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = shared ? t : R.slot[su][t];
+        U.tok_mask = shared ? all : R.mask[su];
         U.act_id = shared ? -1 : s;
         if (gu) {
             if (shared) {
@@ -486,9 +487,10 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
             const int s = s_first + k;
             if (blk0 < blk1 && s * per_ex < blk1) {
                 const bool shared = s >= nu;
-                const int mask = shared ? (1 << p.n) - 1 : R.mask[s];
+                const int su = shared ? 0 : R.own[s];
+                const int mask = shared ? (1 << p.n) - 1 : R.mask[su];
                 int rows[kMaxTok];
-                for (int t = 0; t < kMaxTok; ++t) rows[t] = t < p.n && ((mask >> t) & 1) ? (shared ? t : R.slot[s][t]) : -1;
+                for (int t = 0; t < kMaxTok; ++t) rows[t] = t < p.n && ((mask >> t) & 1) ? (shared ? t : R.slot[su][t]) : -1;
                 stage_image(shared ? p.shact : p.amid, [&](int t) { return rows[t]; }, 0, cols / 64, its, imgs + k * ib,
                             threadIdx.x - k * half, half);
             }

@@ -896,14 +896,19 @@ struct RouteOut {
     int ids[kMaxTok * 8];
     float w[kMaxTok * 8];
     float gs[kMaxTok];
+    // expert parallelism: the union members this rank computes (expert e on rank e % world), as union indices in
+    // ascending order; n_own == n_union and own[u] == u on one GPU
+    int n_own;
+    int own[kMaxUnion];
 };
 
 __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict__ logits, int n, int E, int K,
-                                                          RouteOut *out, int *union_acc) {
+                                                          RouteOut *out, int *union_acc, int ep_rank, int ep_world) {
     extern __shared__ __align__(16) float ps[];   // [kMaxTok][E]
     __shared__ int s_ids[kMaxTok * 8];
     __shared__ uint32_t s_bits[32];   // the union as a bit set over the experts (E <= 1024)
     __shared__ int s_mask[kMaxUnion];
+    __shared__ int s_ex[kMaxUnion];   // the union's expert ids (for the expert-parallel ownership below)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // warp w: token w / 4, quarter (w - t) % 4: a token's four warps on the four SM sub-partitions (w % 4), token t's
     // lead warp (q = 0) on sub-partition t % 4
@@ -1021,6 +1026,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict
         int u = __popc(s_bits[w] & ((1u << (e & 31)) - 1u));
         for (int i = 0; i < w; ++i) u += __popc(s_bits[i]);
         out->ex[u] = e;   // (every pick of the expert writes the same id)
+        s_ex[u] = e;
         out->slot[u][tk] = pk;
         atomicOr(&s_mask[u], 1 << tk);
     }
@@ -1031,6 +1037,19 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict
     if (threadIdx.x == 0) {
         out->n_union = nu;
         if (union_acc) atomicAdd(union_acc, nu);
+    }
+    // this rank's members of the union (expert e on rank e % world), ascending, by ballots over the union in 32s
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        int base = 0;
+        for (int u0 = 0; u0 < nu; u0 += 32) {
+            const int u = u0 + lane;
+            const bool mine = u < nu && s_ex[u] % ep_world == ep_rank;
+            const uint32_t bal = __ballot_sync(0xffffffffu, mine);
+            if (mine) out->own[base + __popc(bal & ((1u << lane) - 1u))] = u;
+            base += __popc(bal);
+        }
+        if (lane == 0) out->n_own = base;
     }
 }
 

@@ -86,7 +86,7 @@ int gcuda_op_route_union(const float *d_logits, int n, int E, int K, void *d_out
         out_bytes < sizeof(RouteOut))
         return GCUDA_E_ARG;
     k_route<<<1, kRouteThreads, kMaxTok * E * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
-        d_logits, n, E, K, static_cast<RouteOut *>(d_out), nullptr);
+        d_logits, n, E, K, static_cast<RouteOut *>(d_out), nullptr, 0, 1);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }

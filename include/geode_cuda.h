@@ -82,6 +82,16 @@ int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, c
  * (context positions) and the scratch, and records the verify step as CUDA graphs. */
 int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, int embed, int lm_head, int final_norm);
 
+/* Expert parallelism (no counterpart in the reference, which runs on one device): the MoE layers' routed experts
+ * striped over `world` handles, one per GPU (expert e on rank e % world); everything else computed on every rank. The
+ * expert outputs meet through one NCCL all-reduce per MoE layer on the handle's stream (each pick's row is non-zero on
+ * its owner only, so the sum is that row exactly), and every rank combines in rank order: the logits equal the
+ * one-GPU step's bit for bit. gcuda_ep_unique_id fills NCCL's 128-byte id on one rank, which the caller hands to
+ * every rank; gcuda_set_ep (before gcuda_setup, same id, ranks 0..world-1, each its own device) joins the group.
+ * libnccl.so.2 is loaded on first use; world 1 needs none. */
+int gcuda_ep_unique_id(void *id_out);
+int gcuda_set_ep(gcuda *g, int rank, int world, const void *id);
+
 /* Model::verify_n (engine/src/model.cpp:1483): n tokens (toks[0] the last accepted token, then the drafts) at the
  * next positions through every layer; logits [n][vocab] (host; NULL: left on the device) and hidden [n][hidden]
  * (the rows after the final norm, the MTP layer's input; NULL: not wanted). The position moves on by n. */
