@@ -128,6 +128,10 @@ struct gcuda {
     int *d_samples = nullptr;
     unsigned long long *d_best = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    // a second stream for work beside the main chain (the Gated DeltaNet's a|b product beside its input product),
+    // forked and joined by events - also inside the step's captured graphs
+    cudaStream_t st2 = nullptr;
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     float last_ms = 0.0f;
     bool pdl = true;
     int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
@@ -290,9 +294,13 @@ int enqueue_step(gcuda *g, int n) {
         const gcuda_layer &L = g->layers[static_cast<size_t>(l)];
         const LayerPlan &P = g->plan[static_cast<size_t>(l)];
         if (!L.attn) {
-            RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
+            // the a|b product (the recurrence's gates) on the side stream, beside the input product and the conv
+            LAUNCH_OK(cudaEventRecord(g->fork_ev, g->st));
+            LAUNCH_OK(cudaStreamWaitEvent(g->st2, g->fork_ev, 0));
             RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H, g->hf, H, n, g->ab,
-                                   2 * s.gdn_v_heads, g->d_status, g->st, pdl));
+                                   2 * s.gdn_v_heads, g->d_status, g->st2, false));
+            LAUNCH_OK(cudaEventRecord(g->join_ev, g->st2));
+            RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
             GdnArgs a{};
             a.proj = g->big;
             a.z = g->zb;
@@ -338,6 +346,7 @@ int enqueue_step(gcuda *g, int n) {
             cfg.attrs = attr;
             cfg.numAttrs = pdl ? 2 : 1;
             cudaError_t e;
+            LAUNCH_OK(cudaStreamWaitEvent(g->st, g->join_ev, 0));   // (the gates)
             if (s.gdn_k_dim == 128) e = cudaLaunchKernelEx(&cfg, k_gdn<128>, a);
             else if (s.gdn_k_dim == 64) e = cudaLaunchKernelEx(&cfg, k_gdn<64>, a);
             else e = cudaLaunchKernelEx(&cfg, k_gdn<32>, a);
@@ -561,6 +570,13 @@ gcuda *gcuda_open(int device, char *err, int err_len) {
     }
     cudaEventCreate(&g->ev0);
     cudaEventCreate(&g->ev1);
+    if (cudaStreamCreateWithFlags(&g->st2, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&g->fork_ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&g->join_ev, cudaEventDisableTiming) != cudaSuccess) {
+        put("side stream / events");
+        gcuda_close(g);
+        return nullptr;
+    }
     if (!dalloc(g, &g->d_status, 1)) {
         put(g->err);
         gcuda_close(g);
@@ -586,6 +602,9 @@ void gcuda_close(gcuda *g) {
     if (g->ev0) cudaEventDestroy(g->ev0);
     if (g->ev1) cudaEventDestroy(g->ev1);
     if (g->comm) nccl().comm_destroy(g->comm);
+    if (g->fork_ev) cudaEventDestroy(g->fork_ev);
+    if (g->join_ev) cudaEventDestroy(g->join_ev);
+    if (g->st2) cudaStreamDestroy(g->st2);
     if (g->st) cudaStreamDestroy(g->st);
     delete g;
 }
