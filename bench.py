@@ -218,7 +218,7 @@ def reference_arm(args):
 # ------------------------------------------------------------------------------------------- the GPU path ----
 # dram__bytes_read.sum + dram__bytes_write.sum of one LM-head launch of k_gemv_static (one ncu capture, the command in
 # profiles/k_gemv_static_lmhead_cfg3.md): 287.9 MB + 20.8 MB
-LMHEAD_TRAFFIC = 310.98e6
+LMHEAD_TRAFFIC = 307.97e6
 
 
 def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
