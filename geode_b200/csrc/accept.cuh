@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_spec_reject(RejectArgs a) {
     __shared__ int misc[4];
     __shared__ int pid[kMaxCand], qid[kMaxCand];
     __shared__ double pp[kMaxCand], qp[kMaxCand];
-    __shared__ int s_np, s_nq, s_acc, s_best;
+    __shared__ int s_acc, s_best;
     __shared__ double s_pd, s_qd, s_ua, s_ur, s_kept;
     const int tid = threadIdx.x, seq = blockIdx.x;
     const int kk = min(a.V, a.top_k > 0 ? a.top_k : kMaxCand);

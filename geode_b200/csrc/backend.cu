@@ -1255,15 +1255,7 @@ int gcuda_step_device(gcuda *g, int n) {
     cudaSetDevice(g->device);
     LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
     count_launch(g->graph_kernels[n]);
-    SampleArgs a{};
-    a.logits = g->logits;
-    a.V = g->sh.vocab;
-    a.n = n;
-    a.temperature = 0.0f;
-    a.top_p = 1.0f;
-    a.u = g->d_u;
-    a.out = g->d_samples;
-    (void)a;
+    // greedy: every row's argmax (the reference's Sampler at temperature 0)
     LAUNCH_OK(launch_ex(k_argmax_partial, dim3(64, n), dim3(256), 0, g->st, false, static_cast<const float *>(g->logits),
                         g->sh.vocab, g->d_best));
     LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, g->pdl, g->d_best, n, g->d_samples));

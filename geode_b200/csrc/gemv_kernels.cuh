@@ -164,7 +164,7 @@ template <int kStages>
 __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) * 32, 1) k_gemv_static(StaticGemv p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5;
-    const int cols = p.act.cols, wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
+    const int cols = p.act.cols, wpu = p.wpu, nslots = p.nslots;
     uint8_t *img = smem;
     auto prelude = [&]() {
         // (the weights do not depend on the previous kernel: their first stages are already requested)
