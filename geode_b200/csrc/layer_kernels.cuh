@@ -808,56 +808,49 @@ struct MergeArgs {
     float *core_f;       // [n][nh * hd] or NULL
 };
 
-// One CTA per (token, head), one thread per dim (blockDim = hd, a multiple of 32): the chunks' factors in shared
-// memory, then every dim's sum over the chunks with independent loads. Dynamic smem: nchunks floats.
+// One CTA per (token, head), one thread per dim (blockDim = hd, a multiple of 32).
 __global__ void k_attn_merge(MergeArgs a) {
-    extern __shared__ float s_f[];
-    __shared__ float s_red[32];
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
     const int pos = *a.pos;
     const int W = a.nh * a.hd;
     const size_t cs = a.hd + 2;
     const int t = blockIdx.x / a.nh, h = blockIdx.x % a.nh;
     const int nc = min(a.nchunks, (pos + t) / kAttnChunk + 1);
     const float *pp = a.part + (static_cast<size_t>(t) * a.nh + h) * a.nchunks * cs;
-    // M = max m_c
-    float M = -INFINITY;
-    for (int c = tid; c < nc; c += blockDim.x) M = fmaxf(M, pp[c * cs + a.hd]);
-    M = warp_max(M);
-    if (lane == 0) s_red[warp] = M;
-    __syncthreads();
-    M = s_red[0];
-    for (int w = 1; w < nw; ++w) M = fmaxf(M, s_red[w]);
-    __syncthreads();
-    // f_c = exp(m_c - M), L = sum l_c f_c
-    float L = 0.0f;
-    for (int c = tid; c < nc; c += blockDim.x) {
-        const float mc = pp[c * cs + a.hd];
-        const float f = mc == -INFINITY ? 0.0f : __expf(mc - M);
-        s_f[c] = f;
-        L += pp[c * cs + a.hd + 1] * f;
-    }
-    L = warp_sum(L);
-    if (lane == 0) s_red[warp] = L;
-    __syncthreads();
-    L = 0.0f;
-    for (int w = 0; w < nw; ++w) L += s_red[w];
+    // every thread on its own (no reductions, no barriers): the chunks' (m, l) - the same addresses for the whole CTA -
+    // and its dim's partials, kMergeBatch chunks' loads in flight at once, folded in with the online rescaling
+    // (M the running max, L and acc rescaled by exp(M_old - M_new) when it grows)
+    constexpr int kMergeBatch = 40;
     const int d = tid;
-    // O = sum_c O_c f_c: 16 chunks' loads in flight before their FMAs (two chains)
-    float acc0 = 0.0f, acc1 = 0.0f;
-    for (int c0 = 0; c0 < nc; c0 += 16) {
-        float v[16];
+    float M = -INFINITY, L = 0.0f, acc = 0.0f;
+    for (int c0 = 0; c0 < nc; c0 += kMergeBatch) {
+        float mv[kMergeBatch], lv[kMergeBatch], vv[kMergeBatch];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) v[u] = c0 + u < nc ? pp[(c0 + u) * cs + d] : 0.0f;
+        for (int u = 0; u < kMergeBatch; ++u) {
+            const bool in = c0 + u < nc;
+            const float *q = pp + static_cast<size_t>(c0 + u) * cs;
+            mv[u] = in ? q[a.hd] : -INFINITY;
+            lv[u] = in ? q[a.hd + 1] : 0.0f;
+            vv[u] = in ? q[d] : 0.0f;
+        }
+        float mb = M;
 #pragma unroll
-        for (int u = 0; u < 16; u += 2) {
-            if (c0 + u < nc) acc0 = fmaf(v[u], s_f[c0 + u], acc0);
-            if (c0 + u + 1 < nc) acc1 = fmaf(v[u + 1], s_f[c0 + u + 1], acc1);
+        for (int u = 0; u < kMergeBatch; ++u) mb = fmaxf(mb, mv[u]);
+        if (mb > M) {
+            const float r = M == -INFINITY ? 0.0f : __expf(M - mb);
+            L *= r;
+            acc *= r;
+            M = mb;
+        }
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) {
+            const float f = mv[u] == -INFINITY ? 0.0f : __expf(mv[u] - M);
+            L = fmaf(lv[u], f, L);
+            acc = fmaf(vv[u], f, acc);
         }
     }
-    const float acc = acc0 + acc1;
     const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
     const float v = __fmul_rn(__fmul_rn(acc, 1.0f / L), sigmoid_cr(gate[d]));
     const int col = h * a.hd + d;
