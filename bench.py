@@ -258,6 +258,84 @@ def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
             "algorithmic_bytes": alg, "traffic_source": "ncu, profiles/k_gemv_static_lmhead_cfg3.md"}
 
 
+def accept_bench(args) -> int:
+    """The acceptance microbench (BASELINE cfg 5): 256 sequences x 8 drafts, vocab 248320, target and draft logits
+    N(0, 3) fp32 resident on the device (4.3 GB, larger than L2), drafts = the draft rows' argmax. Times, with CUDA
+    events on the launching stream, the greedy acceptance of all sequences in one call (gcuda_op_greedy_verify: every
+    target row's first maximum, then the rule) and rejection sampling at temperature 0.7, top-k 20, top-p 0.95,
+    Philox seed 1234 (gcuda_op_spec_reject_static, whose results reach the host inside the timed call)."""
+    import ctypes as C
+    import torch
+    from geode_b200 import cuda_lib
+    from geode_b200.backend import GSampling, _sig
+    S, K, V = 256, 8, 248320
+    L = cuda_lib()
+    _sig(L)
+    L.gcuda_op_spec_reject_static.restype = C.c_int
+    L.gcuda_op_spec_reject_static.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                              C.c_uint64, C.c_void_p, C.c_void_p, C.c_void_p]
+    peak, peak_kind = measured_peaks()
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    target = torch.randn((S, K + 1, V), generator=gen, device="cuda") * 3
+    draft = torch.randn((S, K, V), generator=gen, device="cuda") * 3
+    drafts = draft.argmax(dim=2).to(torch.int32).contiguous()
+    h_drafts = drafts.cpu().numpy()
+    scratch = torch.empty(S * (K + 1), dtype=torch.int64, device="cuda")
+    acc = torch.empty(S, dtype=torch.int32, device="cuda")
+    nxt = torch.empty(S, dtype=torch.int32, device="cuda")
+    h_acc, h_nxt = np.zeros(S, np.int32), np.zeros(S, np.int32)
+    st = torch.cuda.current_stream()
+    sp = GSampling(0.7, 0.95, 20)
+
+    def greedy():
+        assert L.gcuda_op_greedy_verify(target.data_ptr(), drafts.data_ptr(), S, K, V, scratch.data_ptr(), acc.data_ptr(),
+                                        nxt.data_ptr(), st.cuda_stream) == 0
+
+    def reject():
+        assert L.gcuda_op_spec_reject_static(target.data_ptr(), draft.data_ptr(), h_drafts.ctypes.data, S, K, V,
+                                             C.byref(sp), 1234, h_acc.ctypes.data, h_nxt.ctypes.data, st.cuda_stream) == 0
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    steps = max(3, min(args.steps, 50))
+    with Clocks(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        ms_g = timed(greedy, steps)
+        ms_r = timed(reject, steps)
+    a = h_acc.copy()
+    rows = S * (K + 1)
+    bytes_g = rows * V * 4 + S * K * 4 + S * 8
+    # rejection sampling reads, per sequence, the target rows 0..accepted and the draft rows 0..min(accepted, K-1)
+    rows_r = int(np.sum(np.minimum(a + 1, K + 1) + np.minimum(a + 1, K)))
+    bytes_r = rows_r * V * 4
+    ach = bytes_g / (ms_g * 1e-3) / 1e9
+    line = {
+        "metric": "acceptance rows/s (cfg5: 256 sequences x (8+1) rows, vocab 248320)", "value": rows / (ms_g * 1e-3),
+        "unit": "verified rows/s (greedy)", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
+        "ms_per_step": ms_g, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (logits N(0, 3) made on the device, seed 5; drafts = the draft rows' argmax)",
+        "config": {"workload": "cfg5: acceptance microbench, 256 x 8 drafts, V 248320, T 0.7, top-k 20, top-p 0.95, "
+                               "Philox(1234)", "l2": "inputs larger than L2 (4.3 GB of logits; no flush)"},
+        "roofline": {"kernel": "k_argmax_rows (+ k_greedy_decide)", "bound": "hbm", "achieved": ach, "peak": peak,
+                     "unit": "GB/s", "frac": ach / peak, "traffic": None, "algorithmic_bytes": bytes_g},
+        "rejection": {"ms_per_call": ms_r, "sequences_per_s": S / (ms_r * 1e-3), "rows_read": rows_r,
+                      "achieved_gbs": bytes_r / (ms_r * 1e-3) / 1e9, "mean_accepted": float(a.mean()),
+                      "accepted_hist": np.bincount(a, minlength=K + 1).tolist()},
+        "cpu_baseline": None, "e2e": None, "clocks": clk.summary(), "peak_kind": peak_kind,
+    }
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -270,9 +348,15 @@ def main():
     ap.add_argument("--ep", action="store_true",
                     help="N > 1: one sequence over all GPUs, the routed experts striped over them (gcuda_set_ep; strong "
                          "scaling); without it each GPU verifies its own sequence (replicas, weak scaling)")
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg5"],
+                    help="cfg3: the verify step (the headline); cfg5: the acceptance microbench (one GPU)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "cfg5":
+        import torch
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        return accept_bench(args)
 
     import torch
     rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))

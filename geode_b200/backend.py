@@ -65,6 +65,7 @@ def _sig(L):
         "gcuda_synth_experts": (i32, [vp, i32, i32, i32, f32, C.c_uint64]),
         "gcuda_state_randomize": (i32, [vp, i32, C.c_uint64]),
         "gcuda_step_device": (i32, [vp, i32]),
+        "gcuda_step_device_reject": (i32, [vp, i32, vp, vp, C.c_uint64]),
         "gcuda_begin_device_loop": (i32, [vp, vp, i32]),
         "gcuda_sync_step": (i32, [vp, vp, vp, vp]),
         "gcuda_stream": (vp, [vp]),
@@ -259,6 +260,13 @@ class Backend:
 
     def step_device(self, n: int):
         self._rc(self.L.gcuda_step_device(self.g, n), "step_device")
+
+    def step_device_reject(self, n: int, d_draft: int, temperature: float, top_p: float = 1.0, top_k: int = 0,
+                           seed: int = 1234):
+        """gcuda_step_device with rejection sampling against the draft rows at d_draft ([n-1][vocab] f32, device)."""
+        sp = GSampling(temperature, top_p, top_k)
+        self._rc(self.L.gcuda_step_device_reject(self.g, n, C.c_void_p(d_draft), C.byref(sp), C.c_uint64(seed)),
+                 "step_device_reject")
 
     def sync_step(self):
         steps, usum, kept = C.c_int(0), C.c_int(0), C.c_int(0)

@@ -3,6 +3,8 @@
 // speculative (rejection) sampling rule for draft models (not in the reference; Leviathan et al. 2023).
 #pragma once
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace gcu {
@@ -103,29 +105,90 @@ __device__ void row_topk(const float *__restrict__ row, int V, int k, float *cv,
         }
 }
 
-// Greedy rows split over many CTAs: each reduces its slice to the first maximum and merges it into best[r], a 64-bit
-// key (order-preserving value bits, then the complement of the index: the largest value, the lowest index first).
-__global__ void k_argmax_partial(const float *__restrict__ logits, int V, unsigned long long *best) {
+// The first maximum as std::max_element finds it (`if (*largest < *it) largest = it`), with whole float4 loads, four
+// in flight per thread, and one merge per CTA: the CTA's key reduced through shared memory, then a single 64-bit
+// atomicMax into best[r] (a row split over gridDim.x CTAs). Under < , -0.0 and +0.0 are equal (the first one stays:
+// -0.0 is taken as +0.0), a NaN after the first element never replaces the maximum, and a NaN first element is never
+// replaced (index 0: the all-ones key, above every value's). Rows of any
+// length; the vector loop when V is a multiple of 4 and the rows' base is 16-byte aligned (every row then is).
+constexpr int kArgmaxThreads = 256;
+__global__ void __launch_bounds__(kArgmaxThreads) k_argmax_rows(const float *__restrict__ logits, int V,
+                                                                unsigned long long *best) {
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;");
-    const int r = blockIdx.y;
+    __shared__ unsigned long long s_k[kArgmaxThreads / 32];
+    const int r = blockIdx.y, tid = threadIdx.x;
     const float *row = logits + static_cast<size_t>(r) * V;
-    const int per = (V + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(V, lo + per);
     unsigned long long k = 0;
-    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        const float v = row[i];
-        if (v != v) continue;   // (NaN: never the maximum)
+    auto take = [&](float v, int i) {
+        v = __fadd_rn(v, 0.0f);   // (-0 -> +0)
+        if (v != v) return;
         const unsigned long long key = (static_cast<unsigned long long>(fkey(v)) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(i));
         k = key > k ? key : k;
+    };
+    if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+        const int nv = V >> 2, per = (nv + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(nv, lo + per);
+        const float4 *row4 = reinterpret_cast<const float4 *>(row);
+        int i = lo + tid;
+        for (; i + 3 * kArgmaxThreads < hi; i += 4 * kArgmaxThreads) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldg(row4 + i + u * kArgmaxThreads);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int e = 4 * (i + u * kArgmaxThreads);
+                take(v[u].x, e), take(v[u].y, e + 1), take(v[u].z, e + 2), take(v[u].w, e + 3);
+            }
+        }
+        for (; i < hi; i += kArgmaxThreads) {
+            const float4 v = __ldg(row4 + i);
+            take(v.x, 4 * i), take(v.y, 4 * i + 1), take(v.z, 4 * i + 2), take(v.w, 4 * i + 3);
+        }
+    } else {
+        const int per = (V + gridDim.x - 1) / gridDim.x, lo = blockIdx.x * per, hi = min(V, lo + per);
+        for (int i = lo + tid; i < hi; i += kArgmaxThreads) take(__ldg(row + i), i);
     }
+    if (blockIdx.x == 0 && tid == 0 && row[0] != row[0]) k = ~0ull;
     for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long ok = __shfl_xor_sync(0xffffffffu, k, o);
         k = ok > k ? ok : k;
     }
-    if ((threadIdx.x & 31) == 0 && k) atomicMax(&best[r], k);
+    if ((tid & 31) == 0) s_k[tid >> 5] = k;
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < kArgmaxThreads / 32; ++w) k = s_k[w] > k ? s_k[w] : k;
+        if (k) atomicMax(&best[r], k);
+    }
 }
+// CTAs per row for k_argmax_rows: about two waves of the GPU over all rows, at most 64 a row
+inline int argmax_slices(int rows, int sms) { return rows >= 2 * sms * 8 ? 1 : std::min(64, std::max(1, 2 * sms * 8 / rows)); }
+
+// Greedy speculative acceptance of S sequences from their rows' first maxima (best: [S][k+1] keys of k_argmax_rows):
+// draft i stands while row i's argmax equals it (geode_generate's rule at temperature 0, engine/src/geode.cpp:327-350,
+// without stop tokens); next = the argmax of the first row whose draft fell, or of row k when all stood. One thread
+// a sequence; the keys are reset to zero for the next use.
+__global__ void k_greedy_decide(unsigned long long *best, const int *__restrict__ drafts, int S, int k, int *accepted,
+                                int *next) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    unsigned long long *b = best + static_cast<size_t>(s) * (k + 1);
+    auto arg = [&](int i) {
+        const unsigned long long key = b[i];
+        return key ? static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFu)) : 0;
+    };
+    int a = 0;
+    while (a < k && arg(a) == drafts[static_cast<size_t>(s) * k + a]) ++a;
+    accepted[s] = a;
+    next[s] = arg(a);
+    for (int i = 0; i <= k; ++i) b[i] = 0;
+}
+
 // best -> the rows' samples; best reset for the next use
 __global__ void k_argmax_finish(unsigned long long *best, int n, int *out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // (the partial maxima are complete and visible)
+    asm volatile("griddepcontrol.launch_dependents;");
     const int r = threadIdx.x;
     if (r >= n) return;
     const unsigned long long k = best[r];

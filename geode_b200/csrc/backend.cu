@@ -136,6 +136,8 @@ struct gcuda {
     bool pdl = true;
     int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
     size_t rej_cap = 0;
+    int *d_rej_step = nullptr;      // gcuda_step_device_reject's result: accepted, next
+    uint64_t reject_steps = 0;      // (its Philox sequence index: one per step)
     std::vector<void *> allocs;
     // expert parallelism (gcuda_set_ep): this rank's experts are e % ep_world == ep_rank; the expert outputs meet
     // through one all-reduce per MoE layer on the handle's stream
@@ -805,6 +807,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         !dalloc(g, &g->logits, static_cast<size_t>(T) * s.vocab) || !dalloc(g, &g->core_f, static_cast<size_t>(T) * g->corew) ||
         !dalloc(g, &g->inv_freq, std::max(1, s.rope_dim / 2)) || !dalloc(g, &g->route, 1) ||
         !dalloc(g, &g->d_u, kMaxTok) || !dalloc(g, &g->d_samples, kMaxTok) || !dalloc(g, &g->step, 1) || !dalloc(g, &g->d_best, kMaxTok) ||
+        !dalloc(g, &g->d_rej_step, 2) ||
         !act_alloc(g, g->hq, T, H) || !act_alloc(g, g->core, T, g->corew) ||
         !act_alloc(g, g->amid, T * K, ffw) || !act_alloc(g, g->shact, T, s.shared_ff))
         return GCUDA_E_MEMORY;
@@ -983,8 +986,8 @@ int gcuda_accept(gcuda *g, const gcuda_sampling *sp, const double *uniforms, con
     a.u = g->d_u;
     a.out = g->d_samples;
     if (greedy) {
-        LAUNCH_OK(launch_ex(k_argmax_partial, dim3(64, n), dim3(256), 0, g->st, false, static_cast<const float *>(g->logits),
-                            g->sh.vocab, g->d_best));
+        LAUNCH_OK(launch_ex(k_argmax_rows, dim3(argmax_slices(n, sm_count()), n), dim3(kArgmaxThreads), 0, g->st, false,
+                            static_cast<const float *>(g->logits), g->sh.vocab, g->d_best));
         LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, false, g->d_best, n, g->d_samples));
     } else {
         LAUNCH_OK(launch_ex(k_sample_rows, dim3(n), dim3(kSampleThreads), 0, g->st, false, a));
@@ -1247,20 +1250,52 @@ int gcuda_state_randomize(gcuda *g, int pos, uint64_t seed) {
 }
 
 // The device-resident speculative step, enqueued without waiting: the verify graph for n tokens at the device
-// position, the greedy acceptance of every row (k_sample_rows), the decision (k_decide: kept, next, position += kept,
-// toks[0] = next) and the rollback of the Gated DeltaNet states (k_rollback). The drafts toks[1..n-1] are the
-// caller's (gcuda_set_drafts); gcuda_sync_step reads the decision and the position back.
+// position, the greedy acceptance of every row (k_argmax_rows, k_argmax_finish), the decision (k_decide: kept, next,
+// position += kept, toks[0] = next) and the rollback of the Gated DeltaNet states (k_rollback). The drafts
+// toks[1..n-1] stay those of the first batch (gcuda_begin_device_loop); gcuda_sync_step reads the decision and the
+// position back.
 int gcuda_step_device(gcuda *g, int n) {
     if (!g || !g->ready || n < 2 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "step_device: 2 .. max_tokens");
     cudaSetDevice(g->device);
     LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
     count_launch(g->graph_kernels[n]);
     // greedy: every row's argmax (the reference's Sampler at temperature 0)
-    LAUNCH_OK(launch_ex(k_argmax_partial, dim3(64, n), dim3(256), 0, g->st, false, static_cast<const float *>(g->logits),
-                        g->sh.vocab, g->d_best));
+    LAUNCH_OK(launch_ex(k_argmax_rows, dim3(argmax_slices(n, sm_count()), n), dim3(kArgmaxThreads), 0, g->st, false,
+                        static_cast<const float *>(g->logits), g->sh.vocab, g->d_best));
     LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, g->pdl, g->d_best, n, g->d_samples));
     LAUNCH_OK(launch_ex(k_decide, dim3(1), dim3(32), 0, g->st, g->pdl, static_cast<const int *>(g->d_samples), g->d_toks, n,
                         g->d_pos, g->step));
+    LAUNCH_OK(launch_ex(k_rollback, dim3(sm_count() * 4), dim3(256), 0, g->st, g->pdl, g->conv,
+                        static_cast<const float *>(g->conv_bk), g->conv_n, g->gdn, static_cast<const float *>(g->gdn_bk),
+                        g->gdn_n, n, static_cast<const StepState *>(g->step)));
+    return GCUDA_OK;
+}
+
+// The same step with speculative (rejection) sampling in place of the greedy rule: k_spec_reject on the verified rows
+// against the draft model's rows d_draft [n-1][V] (on the device), the drafts toks[1..n-1]; Philox key = seed plus
+// the handle's count of these steps times a constant (fresh uniforms every step); then the decision and the rollback.
+int gcuda_step_device_reject(gcuda *g, int n, const float *d_draft, const gcuda_sampling *sp, uint64_t seed) {
+    if (!g || !g->ready || n < 2 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "step_device_reject: 2 .. max_tokens");
+    if (!d_draft || !sp || sp->temperature <= 0.0f || sp->top_k > kMaxCand || !(sp->top_p > 0.0f && sp->top_p <= 1.0f))
+        return fail(g, GCUDA_E_ARG, "step_device_reject: bad arguments");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
+    count_launch(g->graph_kernels[n]);
+    RejectArgs a{};
+    a.target = g->logits;
+    a.draft = d_draft;
+    a.drafts = g->d_toks + 1;
+    a.k = n - 1;
+    a.V = g->sh.vocab;
+    a.temperature = sp->temperature;
+    a.top_p = sp->top_p;
+    a.top_k = sp->top_k;
+    a.seed = seed + 0x9E3779B97F4A7C15ull * g->reject_steps++;
+    a.accepted = g->d_rej_step;
+    a.next = g->d_rej_step + 1;
+    LAUNCH_OK(launch_ex(k_spec_reject, dim3(1), dim3(kSampleThreads), 0, g->st, false, a));
+    LAUNCH_OK(launch_ex(k_decide_reject, dim3(1), dim3(32), 0, g->st, g->pdl, static_cast<const int *>(g->d_rej_step),
+                        static_cast<const int *>(g->d_rej_step + 1), g->d_toks, g->d_pos, g->step));
     LAUNCH_OK(launch_ex(k_rollback, dim3(sm_count() * 4), dim3(256), 0, g->st, g->pdl, g->conv,
                         static_cast<const float *>(g->conv_bk), g->conv_n, g->gdn, static_cast<const float *>(g->gdn_bk),
                         g->gdn_n, n, static_cast<const StepState *>(g->step)));

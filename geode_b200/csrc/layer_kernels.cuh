@@ -1135,6 +1135,19 @@ __global__ void k_decide(const int *samples, int *toks, int n, int *pos, StepSta
     toks[0] = nx;
 }
 
+// The same decision from a rejection-sampling result (k_spec_reject on one sequence: accepted drafts, next token)
+__global__ void k_decide_reject(const int *accepted, const int *next, int *toks, int *pos, StepState *ss) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    const int k = accepted[0] + 1, nx = next[0];
+    ss->kept = k;
+    ss->next = nx;
+    ss->steps += 1;
+    *pos += k;
+    toks[0] = nx;
+}
+
 // state = backup[kept - 1] when kept < n (a grid-stride copy of the conv and recurrent states)
 __global__ void k_rollback(float *conv, const float *conv_bk, size_t conv_n, float *gdn, const float *gdn_bk, size_t gdn_n,
                            int n, const StepState *ss) {

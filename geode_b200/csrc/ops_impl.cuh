@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/geode_cuda.h"
+#include "accept.cuh"
 #include "gemv_kernels.cuh"
 #include "small_kernels.cuh"
 #include "launch.hpp"
@@ -89,6 +90,23 @@ int gcuda_op_route_union(const float *d_logits, int n, int E, int K, void *d_out
         d_logits, n, E, K, static_cast<RouteOut *>(d_out), nullptr, 0, 1);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_greedy_verify(const float *d_target, const int *d_drafts, int S, int k, int V, uint64_t *d_scratch,
+                           int *d_accepted, int *d_next, void *stream) {
+    if (!d_target || !d_drafts || !d_scratch || !d_accepted || !d_next || S < 1 || k < 1 || V < 1 || S > 65535 ||
+        static_cast<int64_t>(S) * (k + 1) > 65535)
+        return GCUDA_E_ARG;   // (rows on the grid's y dimension)
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int rows = S * (k + 1);
+    auto *best = reinterpret_cast<unsigned long long *>(d_scratch);
+    if (cudaMemsetAsync(best, 0, sizeof(unsigned long long) * rows, st) != cudaSuccess) return GCUDA_E_CUDA;
+    if (launch_ex(k_argmax_rows, dim3(argmax_slices(rows, sm_count()), rows), dim3(kArgmaxThreads), 0, st, false, d_target, V,
+                  best) != cudaSuccess ||
+        launch_ex(k_greedy_decide, dim3((S + 127) / 128), dim3(128), 0, st, false, best, d_drafts, S, k, d_accepted,
+                  d_next) != cudaSuccess)
+        return GCUDA_E_CUDA;
+    return GCUDA_OK;
 }
 
 }  // extern "C"

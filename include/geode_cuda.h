@@ -151,6 +151,11 @@ int gcuda_adopt_embedding(gcuda *g, const uint8_t *data, int64_t rows, int64_t c
 int gcuda_begin_device_loop(gcuda *g, const int *toks, int n);
 int gcuda_step_device(gcuda *g, int n);
 int gcuda_sync_step(gcuda *g, int *steps, int *union_sum, int *last_kept);
+/* gcuda_step_device with speculative (rejection) sampling in place of the greedy acceptance (the draft-model
+ * configurations): the verified rows against the draft model's rows d_draft [n-1][vocab] on the device, the drafts
+ * toks[1..n-1]; Philox4x32-10 key = seed plus the handle's count of these steps times a constant. As
+ * gcuda_spec_reject for one sequence, chained on the device with the decision and the rollback. */
+int gcuda_step_device_reject(gcuda *g, int n, const float *d_draft, const gcuda_sampling *s, uint64_t seed);
 
 /* ----------------------------------------------------------------------------------------- synthetic models ----
  * Seeded weights made straight in device memory, for measuring runs whose values do not matter (the self-test
@@ -201,6 +206,14 @@ int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, 
  *   float w[64] ([n][K] normalised weights); float gs[8] (the shared expert's gate per token). */
 size_t gcuda_op_route_out_bytes(void);
 int gcuda_op_route_union(const float *d_logits, int n, int E, int K, void *d_out, size_t out_bytes, void *stream);
+/* Greedy speculative acceptance of S sequences at once (geode_generate's rule at temperature 0,
+ * engine/src/geode.cpp:327-350, no stop tokens): row i's sample is its first maximum (Sampler::sample at temperature
+ * 0, std::max_element, engine/src/sampler.cpp:16-22; NaN never the maximum, a row of NaN only gives 0); draft i
+ * stands while row i's sample equals it. d_target [S][k+1][V], d_drafts [S][k]; d_accepted[S] = drafts that stood,
+ * d_next[S] = the sample of the first row whose draft fell (row k's when all stood). d_scratch: S*(k+1) 64-bit words
+ * the call zeroes first. No counterpart in the reference as one call (its rule runs per sequence on the host). */
+int gcuda_op_greedy_verify(const float *d_target, const int *d_drafts, int S, int k, int V, uint64_t *d_scratch,
+                           int *d_accepted, int *d_next, void *stream);
 
 /* gcuda_spec_reject without a handle and without allocating: for callers that must not allocate device memory when
  * they call it (a serving loop that holds a fixed device-memory budget, or one that cannot take the implicit

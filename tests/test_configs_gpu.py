@@ -1,0 +1,163 @@
+"""Parity at two of the benchmark configurations' own model shapes (the third, the MoE 35B-A3B shape, is the one the
+benchmark runs; its structure is covered by the smaller MoE shapes of test_model_gpu.py):
+
+- cfg 1: one full-attention layer (16 q / 4 kv heads, head_dim 128), hidden 2048, SwiGLU FFN 6144, vocab 32768, a
+  KV cache of 1024 random positions; greedy acceptance;
+- cfg 2: the dense 2B hybrid - 24 layers, 3 Gated DeltaNet : 1 attention (16 heads dk = dv = 128; attention 16 / 4
+  heads, head_dim 256), FFN 6144, vocab 248320, 4096 random positions of KV and random recurrent / conv states;
+  rejection sampling at temperature 0.7 (Philox uniforms) against a draft model close to the target.
+
+The packs hold random q4 bytes (the quantizer's output for N(0, 0.02) weights takes minutes to write at these sizes;
+the kernels read the same format either way). Checked, as in test_model_gpu.py: the verified rows' logits within
+max|d| <= 1e-2 x (max - min) of the oracle's; the acceptance bit-exact on the GPU's own logits (go_accept,
+go_spec_reject); after the rollback the next batch's logits again within the tolerance. The first drafts of each
+batch are planted (the GPU's own greedy continuation) so that drafts can stand and the rollback move partway.
+
+The tolerance and the model's own conditioning: 24 layers of random weights with the activations requantized to int8
+before every product amplify rounding-level differences - the oracle's own logits move by about 1.8% of their range
+when its recurrent and conv states and KV scales are scaled by (1 + 1e-6 N(0, 1)). A row that misses 1e-2 x range is
+therefore held to max(1e-2 x range, DRIFT_FACTOR x the oracle's own movement under that perturbation), measured on
+the same batch; a wrong kernel moves logits by a good part of their range, far above either bound.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from geode_b200 import synth  # noqa: E402
+import oracle_py as op  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+DRIFT_FACTOR = 2.0
+DRIFT_EPS = 1e-6
+
+
+def _close(got, ref):
+    rng_ = ref.max(axis=-1) - ref.min(axis=-1)
+    err = np.abs(got - ref).max(axis=-1)
+    return err, rng_, bool(np.all(err <= TOL * rng_))
+
+
+def _check(ora, st_before, toks, got, ref, what):
+    """got within TOL x range of ref; failing that, within DRIFT_FACTOR x the oracle's own movement when its state
+    (recurrent, conv, KV scales) is scaled by (1 + DRIFT_EPS N(0, 1)) before the same batch."""
+    err, rr, ok = _close(got, ref)
+    if ok:
+        return
+    s2 = st_before.copy()
+    p = np.random.default_rng(9)
+    for a in (s2.gdn, s2.conv, s2.kvs):
+        a[:] = a * (1 + DRIFT_EPS * p.standard_normal(a.shape)).astype(np.float32)
+    drift = np.abs(ora.forward(s2, toks, logits=True)["logits"] - ref).max(axis=-1)
+    bound = np.maximum(TOL * rr, DRIFT_FACTOR * drift)
+    assert np.all(err <= bound), f"{what}: max|d| {err} vs range {rr}, the oracle's own drift {drift}"
+
+
+def _compact_kv(ora, st):
+    c = ora.cfg
+    A = max(1, ora.n_attn)
+    row = c.n_kv_heads * c.head_dim
+    kv = st.kv.reshape(A, 2, st.ctx, row)[:, :, :st.pos].copy()
+    kvs = st.kvs.reshape(A, 2, st.ctx, c.n_kv_heads)[:, :, :st.pos].copy()
+    return kv, kvs
+
+
+def _random_state(ora, st, positions, rng):
+    """positions of random int8 KV rows (scales U(0.005, 0.02)), random conv and recurrent states."""
+    c = ora.cfg
+    A = max(1, ora.n_attn)
+    row = c.n_kv_heads * c.head_dim
+    kv = st.kv.reshape(A, 2, st.ctx, row)
+    kvs = st.kvs.reshape(A, 2, st.ctx, c.n_kv_heads)
+    if ora.n_attn:
+        kv[:, :, :positions] = rng.integers(-127, 128, kv[:, :, :positions].shape, dtype=np.int8)
+        kvs[:, :, :positions] = rng.uniform(0.005, 0.02, kvs[:, :, :positions].shape).astype(np.float32)
+    if ora.n_gdn:
+        st.conv[:] = (rng.standard_normal(st.conv.shape) * 0.3).astype(np.float32)
+        st.gdn[:] = (rng.standard_normal(st.gdn.shape) * 0.02).astype(np.float32)
+    st.pos = positions
+
+
+@pytest.fixture(scope="module", params=[1, 2])
+def config(request, tmp_path_factory):
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from geode_b200.backend import Backend
+    cfg = request.param
+    shape = synth.baseline_shape(cfg)
+    d = str(tmp_path_factory.mktemp(f"cfg{cfg}"))
+    synth.write_pack(d, shape, seed=20 + cfg, fill="random")
+    ora = op.Oracle(d)
+    ctx = shape.ctx + 16   # (room for the two batches after the config's 1024 / 4096 positions)
+    st = ora.new_state(ctx)
+    rng = np.random.default_rng(30 + cfg)
+    _random_state(ora, st, shape.ctx - 8, rng)
+    be = Backend(d, context=ctx, max_tokens=5)
+    kv, kvs = _compact_kv(ora, st)
+    be.state_put(st.conv, st.gdn, kv, kvs, st.pos)
+    yield cfg, shape, ora, be, st, rng
+    be.close()
+
+
+def _planted(be, ora, st, rng, vocab, j):
+    """t0, then j drafts = the GPU's own greedy continuation (each found by a verify from the saved state, which is
+    then put back), then random ones."""
+    kv, kvs = _compact_kv(ora, st)
+    snap = (st.conv.copy(), st.gdn.copy(), np.zeros_like(kv), np.zeros_like(kvs))
+    be.state_get(*snap, st.pos)
+    toks = [int(rng.integers(0, vocab))]
+    for i in range(4):
+        if i < j:
+            got, _ = be.verify(np.array(toks, np.int32), logits=True)
+            be.state_put(*snap, st.pos)
+            toks.append(int(np.argmax(got[-1])))
+        else:
+            toks.append(int(rng.integers(0, vocab)))
+    return np.array(toks, dtype=np.int32)
+
+
+def test_config_verify_accept_rollback(config):
+    from geode_b200.backend import GSampling
+    cfg, shape, ora, be, st, rng = config
+    O = op.oracle_lib()
+    V = shape.vocab
+    j = 2
+    toks = _planted(be, ora, st, rng, V, j)
+    before = st.copy()
+    ref = ora.forward(st, toks, logits=True)
+    got, _ = be.verify(toks, logits=True)
+    _check(ora, before, toks, got, ref["logits"], f"cfg {cfg}")
+    if cfg == 1:   # greedy acceptance (engine/src/geode.cpp:327-350)
+        kept, nxt, samples = be.accept(0.0)
+        ref_next = C.c_int(0)
+        ref_samples = np.zeros(5, np.int32)
+        ref_kept = O.go_accept(got.ctypes.data, 5, V, toks.ctypes.data, 0.0, 1.0, 0, C.c_uint64(0), None, 0,
+                               C.byref(ref_next), ref_samples.ctypes.data)
+        assert (kept, nxt) == (ref_kept, ref_next.value) and np.array_equal(samples, ref_samples)
+    else:          # rejection sampling at T 0.7 against a draft model close to the target
+        draft = np.ascontiguousarray(got[:4] + (rng.standard_normal((4, V)) * 0.3).astype(np.float32))
+        d_draft = torch.from_numpy(draft).cuda()
+        acc, nx = np.zeros(1, np.int32), np.zeros(1, np.int32)
+        sp = GSampling(0.7, 1.0, 0)
+        d_logits = be.L.gcuda_device_logits(be.g)
+        assert be.L.gcuda_spec_reject(be.g, d_logits, d_draft.data_ptr(), np.ascontiguousarray(toks[1:]).ctypes.data, 1,
+                                      4, V, C.byref(sp), 77, acc.ctypes.data, nx.ctypes.data) == 0
+        ref_next = C.c_int(0)
+        ra = O.go_spec_reject(got.ctypes.data, draft.ctypes.data, 4, V, np.ascontiguousarray(toks[1:]).ctypes.data, 0.7,
+                              1.0, 0, C.c_uint64(77), 0, C.byref(ref_next))
+        assert (int(acc[0]), int(nx[0])) == (ra, ref_next.value)
+        kept = ra + 1
+    if kept < 5:
+        be.keep(kept)
+    st.__dict__.update(before.copy().__dict__)
+    ora.forward(st, toks[:kept], logits=False)
+    assert be.pos == st.pos
+    toks2 = rng.integers(0, V, 5).astype(np.int32)
+    before2 = st.copy()
+    ref2 = ora.forward(st, toks2, logits=True)
+    got2, _ = be.verify(toks2, logits=True)
+    _check(ora, before2, toks2, got2, ref2["logits"], f"cfg {cfg} after the rollback")

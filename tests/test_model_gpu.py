@@ -147,3 +147,51 @@ def test_accept_bit_exact(setup, temperature, top_p, top_k):
         st.__dict__.update(before.copy().__dict__)
         ora.forward(st, toks[:kept], logits=False)
         assert be.pos == st.pos
+
+
+@pytest.mark.parametrize("mode", ["greedy", "reject"])
+def test_device_loop_step(setup, mode):
+    """The device-resident step (gcuda_step_device: graph, greedy acceptance, decision, rollback on the device; and
+    gcuda_step_device_reject with rejection sampling): its kept count equals the oracle's rule on the logits the same
+    batch gives from the same state (gcuda_verify, then the state put back), and after its rollback the next batch's
+    logits still match the oracle's."""
+    shape, ora, be, st, rng = setup
+    O = op.oracle_lib()
+    V = shape.vocab
+    for rep in range(3):
+        j = int(rng.integers(0, 5))
+        toks = _planted(ora, st, rng.integers(0, V), j, rng, V)
+        before = st.copy()
+        pos0 = be.pos
+        conv, gdn = np.zeros_like(st.conv), np.zeros_like(st.gdn)
+        kv, kvs = _compact_kv(ora, st)
+        kv, kvs = np.zeros_like(kv), np.zeros_like(kvs)
+        be.state_get(conv, gdn, kv, kvs, pos0)
+        got, _ = be.verify(toks, logits=True)
+        be.state_put(conv, gdn, kv, kvs, pos0)
+        be.begin_device_loop(toks)
+        if mode == "greedy":
+            be.step_device(5)
+            nxt = op.C.c_int(0)
+            ref_kept = O.go_accept(got.ctypes.data, 5, V, toks.ctypes.data, 0.0, 1.0, 0, op.C.c_uint64(0), None, 0,
+                                   op.C.byref(nxt), np.zeros(5, np.int32).ctypes.data)
+        else:
+            draft = np.ascontiguousarray(got[:4] + (rng.standard_normal((4, V)) * 0.3).astype(np.float32))
+            d_draft = torch.from_numpy(draft).cuda()
+            seed = 4242
+            be.step_device_reject(5, d_draft.data_ptr(), 0.7, 0.95, 20, seed=seed)
+            key = (seed + 0x9E3779B97F4A7C15 * rep) & (2 ** 64 - 1)   # (the handle's rep-th such step)
+            nxt = op.C.c_int(0)
+            acc = O.go_spec_reject(got.ctypes.data, draft.ctypes.data, 4, V, np.ascontiguousarray(toks[1:]).ctypes.data,
+                                   0.7, 0.95, 20, op.C.c_uint64(key), 0, op.C.byref(nxt))
+            ref_kept = acc + 1
+        steps, _, kept = be.sync_step()
+        assert steps == 1 and kept == ref_kept, (mode, rep, kept, ref_kept)
+        assert be.pos == pos0 + kept
+        st.__dict__.update(before.copy().__dict__)
+        ora.forward(st, toks[:kept], logits=False)
+    toks = rng.integers(0, V, 5)
+    ref = ora.forward(st, toks, logits=True)
+    got, _ = be.verify(toks, logits=True)
+    err, rr, ok = _close(got, ref["logits"])
+    assert ok, f"after the device steps: max|d| {err} vs range {rr}"

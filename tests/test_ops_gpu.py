@@ -199,3 +199,55 @@ def test_spec_reject_bit_exact(L, O, temperature, top_p, top_k):
                               np.ascontiguousarray(drafts[s_]).ctypes.data, temperature, top_p, top_k, 1234, s_, C.byref(n))
         assert (acc[s_], nxt[s_]) == (ra, n.value), s_
     assert len(set(acc.tolist())) > 1   # (sequences stop at different drafts)
+
+
+@pytest.mark.parametrize("V,offset", [(4096, 0), (1001, 0), (4096, 1)])
+def test_greedy_verify_bit_exact(L, O, V, offset):
+    """gcuda_op_greedy_verify (k_argmax_rows + k_greedy_decide) for many sequences at once: accepted counts and next
+    tokens equal the oracle's acceptance rule at temperature 0 (go_accept: std::max_element per row, draft i+1 stands
+    while row i's sample is that draft) on every sequence - with rows of tied maxima, -0.0 before +0.0, NaN first or
+    inside a row, rows of NaN only; rows whose length is not a multiple of 4 and rows not on a 16-byte boundary take
+    the scalar loads."""
+    rng = np.random.default_rng(V + offset)
+    S, k = 61, 4
+    target = (rng.standard_normal((S, k + 1, V)) * 3).astype(np.float32)
+    drafts = np.zeros((S, k), np.int32)
+    for s_ in range(S):
+        am = np.argmax(target[s_], axis=1)
+        j = s_ % (k + 1)                    # the first j drafts are the rows' argmax
+        drafts[s_, :j] = am[:j]
+        drafts[s_, j:] = rng.integers(0, V, k - j)
+    # edge rows (each on the row whose draft decides)
+    target[1, 0, 7] = target[1, 0, 900] = target[1, 0].max() + 1.0           # a tie: the lower index
+    drafts[1, 0] = 7
+    target[2, 0, :] = 0.0
+    target[2, 0, 3] = -0.0                                                 # all equal: index 0
+    drafts[2, 0] = 0
+    target[3, 0, 0] = np.nan                                               # NaN first: index 0
+    drafts[3, 0] = 0
+    target[4, 0, 5] = np.nan                                               # NaN inside: skipped
+    drafts[4, 0] = int(np.nanargmax(target[4, 0]))
+    target[5, 0, :] = np.nan                                               # NaN only: 0
+    drafts[5, 0] = 0
+    target[6, 1, :] = -np.inf                                              # -inf only: the first
+    drafts[6, :2] = [int(np.argmax(target[6, 0])), 0]
+    flat = np.zeros(S * (k + 1) * V + offset, np.float32)
+    flat[offset:] = target.reshape(-1)
+    d_flat = _dev(flat)
+    d_drafts = _dev(drafts)
+    scratch = torch.zeros(S * (k + 1), dtype=torch.int64, device="cuda")
+    acc = torch.full((S,), -1, dtype=torch.int32, device="cuda")
+    nxt = torch.full((S,), -1, dtype=torch.int32, device="cuda")
+    assert L.gcuda_op_greedy_verify(_p(d_flat) + 4 * offset, _p(d_drafts), S, k, V, _p(scratch), _p(acc), _p(nxt),
+                                    None) == 0
+    torch.cuda.synchronize()
+    acc, nxt = acc.cpu().numpy(), nxt.cpu().numpy()
+    assert int(scratch.abs().sum()) == 0   # (left zeroed)
+    for s_ in range(S):
+        batch = np.concatenate([[0], drafts[s_]]).astype(np.int32)
+        n = C.c_int(0)
+        kept = O.go_accept(np.ascontiguousarray(target[s_]).ctypes.data, k + 1, V, batch.ctypes.data, 0.0, 1.0, 0,
+                           C.c_uint64(0), None, 0, C.byref(n), np.zeros(k + 1, np.int32).ctypes.data)
+        assert (acc[s_], nxt[s_]) == (kept - 1, n.value), s_
+    assert len(set(acc.tolist())) == k + 1   # (every accepted length occurs)
+    assert L.gcuda_op_greedy_verify(_p(d_flat), _p(d_drafts), 0, k, V, _p(scratch), _p(d_drafts), _p(d_drafts), None) != 0
