@@ -18,63 +18,191 @@ __device__ __forceinline__ uint32_t fkey(float f) {
 constexpr int kSampleThreads = 1024;
 constexpr int kMaxCand = 1024;
 
-// The k largest (value desc, index asc) of a row into cv/ci (k <= kMaxCand), sorted. Block-wide (1024 threads).
-__device__ void row_topk(const float *__restrict__ row, int V, int k, float *cv, int *ci, uint32_t *hist, int *misc) {
-    const int tid = threadIdx.x;
-    uint32_t prefix = 0, mask = 0;
-    int need = k;
-    for (int pass = 0; pass < 4; ++pass) {
-        const int shift = 24 - 8 * pass;
-        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-        __syncthreads();
-        for (int i = tid; i < V; i += blockDim.x) {
-            const uint32_t key = fkey(row[i]);
-            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1u);
+constexpr int kFastTopK = 256;   // the candidate pass serves k up to this
+constexpr int kFastCap = 1024;   // candidates it holds (more qualify: the radix path)
+
+__device__ __forceinline__ float key_float(uint32_t key) {   // (fkey's inverse)
+    return __uint_as_float((key & 0x80000000u) ? (key & 0x7FFFFFFFu) : ~key);
+}
+
+// The k largest keys of a row by two reads of it (k <= kFastTopK, blockDim.x == kSampleThreads): every thread's
+// largest key, then tau = the k-th largest of those - k distinct elements reach it, so every one of the row's k
+// largest does too - then every element with key >= tau into cand (one ballot per warp and element position, one
+// shared atomic per warp that has any), sorted by (key desc, index asc); its first k into cv/ci. Returns false, with
+// nothing written to cv/ci, when more than kFastCap elements reach tau (ties or a flat row): the radix path then.
+__device__ bool row_topk_fast(const float *__restrict__ row, int V, int k, float *cv, int *ci, uint32_t *tk,
+                              unsigned long long *cand, int *misc) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    constexpr int nt = kSampleThreads;
+    const bool vec = (V & 3) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+    const float4 *r4 = reinterpret_cast<const float4 *>(row);
+    const int nv = V >> 2;
+    uint32_t m = 0;
+    auto mx4 = [](uint32_t a, const float4 &v) {
+        return max(max(a, max(fkey(v.x), fkey(v.y))), max(fkey(v.z), fkey(v.w)));
+    };
+    if (vec) {
+        int i = tid;
+        for (; i + 3 * nt < nv; i += 4 * nt) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldg(r4 + i + u * nt);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) m = mx4(m, v[u]);
         }
-        __syncthreads();
-        if (tid == 0) {
-            int acc = 0, d = 255;
-            for (; d > 0; --d) {
-                if (acc + static_cast<int>(hist[d]) >= need) break;
-                acc += hist[d];
-            }
-            misc[0] = d;
-            misc[1] = need - acc;
-        }
-        __syncthreads();
-        prefix |= static_cast<uint32_t>(misc[0]) << shift;
-        mask |= 255u << shift;
-        need = misc[1];
-        __syncthreads();
+        for (; i < nv; i += nt) m = mx4(m, __ldg(r4 + i));
+    } else {
+        for (int i = tid; i < V; i += nt) m = max(m, fkey(__ldg(row + i)));
     }
-    // prefix = the k-th largest key; `need` of the elements equal to it are taken, the lowest indices first
-    const uint32_t tau = prefix;
-    const int per = (V + blockDim.x - 1) / blockDim.x, lo = tid * per, hi = min(V, lo + per);
-    int eq = 0;
-    for (int i = lo; i < hi; ++i) eq += fkey(row[i]) == tau;
-    // exclusive scan of eq over threads (in index order)
-    __shared__ int scan[kSampleThreads];
-    scan[tid] = eq;
-    __syncthreads();
-    for (int off = 1; off < blockDim.x; off <<= 1) {
-        const int v = tid >= off ? scan[tid - off] : 0;
-        __syncthreads();
-        scan[tid] += v;
-        __syncthreads();
-    }
-    int rank = scan[tid] - eq;
+    tk[tid] = m;   // (0 for a thread without elements: below every key but the all-ones NaN's, which then takes all)
     if (tid == 0) misc[2] = 0;
     __syncthreads();
-    for (int i = lo; i < hi; ++i) {
-        const uint32_t key = fkey(row[i]);
-        if (key > tau || (key == tau && rank++ < need)) {
-            const int at = atomicAdd(&misc[2], 1);
-            if (at < kMaxCand) {
-                cv[at] = row[i];
-                ci[at] = i;
+    for (int size = 2; size <= nt; size <<= 1)   // bitonic, descending
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const int j = tid ^ stride;
+            if (j > tid) {
+                const bool desc = (tid & size) == 0;
+                const uint32_t a = tk[tid], b = tk[j];
+                if ((a < b) == desc) {
+                    tk[tid] = b;
+                    tk[j] = a;
+                }
+            }
+            __syncthreads();
+        }
+    const uint32_t tau = tk[k - 1];
+    auto put = [&](bool p, uint32_t key, int idx) {   // (called by whole warps: every trip count is block-uniform)
+        const unsigned bal = __ballot_sync(0xffffffffu, p);
+        if (!bal) return;
+        const int lead = __ffs(bal) - 1;
+        int base = 0;
+        if (lane == lead) base = atomicAdd(&misc[2], __popc(bal));
+        base = __shfl_sync(0xffffffffu, base, lead);
+        const int at = base + __popc(bal & ((1u << lane) - 1u));
+        if (p && at < kFastCap)
+            cand[at] = (static_cast<unsigned long long>(key) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(idx));
+    };
+    if (vec) {
+        for (int i0 = 0; i0 < nv; i0 += 4 * nt) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * nt + tid;
+                v[u] = i < nv ? __ldg(r4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * nt + tid;
+                const bool in = i < nv;
+                const uint32_t kx = fkey(v[u].x), ky = fkey(v[u].y), kz = fkey(v[u].z), kw = fkey(v[u].w);
+                put(in && kx >= tau, kx, 4 * i);
+                put(in && ky >= tau, ky, 4 * i + 1);
+                put(in && kz >= tau, kz, 4 * i + 2);
+                put(in && kw >= tau, kw, 4 * i + 3);
             }
         }
+    } else {
+        for (int i0 = 0; i0 < V; i0 += nt) {
+            const int i = i0 + tid;
+            const uint32_t kx = i < V ? fkey(__ldg(row + i)) : 0u;
+            put(i < V && kx >= tau, kx, i);
+        }
     }
+    __syncthreads();
+    const int n = misc[2];
+    if (n > kFastCap) return false;   // (block-uniform)
+    int P = 1;
+    while (P < n) P <<= 1;
+    for (int i = n + tid; i < P; i += nt) cand[i] = 0ull;   // (below every candidate: they sort last)
+    __syncthreads();
+    for (int size = 2; size <= P; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < P; i += nt) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned long long a = cand[i], b = cand[j];
+                    if ((a < b) == desc) {
+                        cand[i] = b;
+                        cand[j] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    for (int i = tid; i < k; i += nt) {
+        const unsigned long long c = cand[i];
+        cv[i] = key_float(static_cast<uint32_t>(c >> 32));
+        ci[i] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(c & 0xFFFFFFFFu));
+    }
+    return true;
+}
+
+// The k largest (value desc, index asc) of a row into cv/ci (k <= kMaxCand), sorted. Block-wide (1024 threads).
+// Selection by key (fkey, then the lower index) - the candidate pass when k is small, else a radix select - and the
+// selected k ordered by (value desc, index asc) in one bitonic network, so both selections give the same arrays.
+__device__ void row_topk(const float *__restrict__ row, int V, int k, float *cv, int *ci, uint32_t *hist, int *misc) {
+    const int tid = threadIdx.x;
+    __shared__ int scan[kSampleThreads];
+    __shared__ unsigned long long cand[kFastCap];
+    const bool fast = k <= kFastTopK && blockDim.x == kSampleThreads &&
+                      row_topk_fast(row, V, k, cv, ci, reinterpret_cast<uint32_t *>(scan), cand, misc);
+    if (!fast) {
+        __syncthreads();   // (the candidate pass's last reads of scan and misc)
+        uint32_t prefix = 0, mask = 0;
+        int need = k;
+        for (int pass = 0; pass < 4; ++pass) {
+            const int shift = 24 - 8 * pass;
+            for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+            __syncthreads();
+            for (int i = tid; i < V; i += blockDim.x) {
+                const uint32_t key = fkey(row[i]);
+                if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255], 1u);
+            }
+            __syncthreads();
+            if (tid == 0) {
+                int acc = 0, d = 255;
+                for (; d > 0; --d) {
+                    if (acc + static_cast<int>(hist[d]) >= need) break;
+                    acc += hist[d];
+                }
+                misc[0] = d;
+                misc[1] = need - acc;
+            }
+            __syncthreads();
+            prefix |= static_cast<uint32_t>(misc[0]) << shift;
+            mask |= 255u << shift;
+            need = misc[1];
+            __syncthreads();
+        }
+        // prefix = the k-th largest key; `need` of the elements equal to it are taken, the lowest indices first
+        const uint32_t tau = prefix;
+        const int per = (V + blockDim.x - 1) / blockDim.x, lo = tid * per, hi = min(V, lo + per);
+        int eq = 0;
+        for (int i = lo; i < hi; ++i) eq += fkey(row[i]) == tau;
+        // exclusive scan of eq over threads (in index order)
+        scan[tid] = eq;
+        __syncthreads();
+        for (int off = 1; off < blockDim.x; off <<= 1) {
+            const int v = tid >= off ? scan[tid - off] : 0;
+            __syncthreads();
+            scan[tid] += v;
+            __syncthreads();
+        }
+        int rank = scan[tid] - eq;
+        if (tid == 0) misc[2] = 0;
+        __syncthreads();
+        for (int i = lo; i < hi; ++i) {
+            const uint32_t key = fkey(row[i]);
+            if (key > tau || (key == tau && rank++ < need)) {
+                const int at = atomicAdd(&misc[2], 1);
+                if (at < kMaxCand) {
+                    cv[at] = row[i];
+                    ci[at] = i;
+                }
+            }
+        }
+    }   // (the radix path)
     __syncthreads();
     // bitonic sort of kMaxCand slots by (value desc, index asc); empty slots last
     for (int i = tid; i < kMaxCand; i += blockDim.x)
