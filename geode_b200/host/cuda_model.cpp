@@ -3,6 +3,7 @@
 
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <cstring>
 
 namespace ghost {
@@ -46,6 +47,9 @@ bool CudaApi::load(const std::string &path, std::string &err) {
     sym(keep, "gcuda_keep");
     sym(position, "gcuda_position");
     sym(accept, "gcuda_accept");
+    sym(state_get, "gcuda_state_get");
+    sym(state_put, "gcuda_state_put");
+    sym(reset, "gcuda_reset");
     return ok;
 }
 
@@ -168,6 +172,91 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
     if (api_.setup(g_, &s, layers.data(), embed, head, norm) != 0) return fail("setup", err);
     max_tokens_ = opt.max_tokens;
     vocab_ = s.vocab;
+    context_ = s.context;
+    dir_ = dir;
+    // what a state of this model holds (engine/src/model.cpp:351-358: the attention layers' KV, the Gated DeltaNet
+    // layers' conv and recurrent states)
+    int n_attn = 0, n_gdn = 0;
+    for (int l = 0; l < L; ++l) (types[static_cast<size_t>(l)].string() == "full_attention" ? n_attn : n_gdn)++;
+    const uint64_t conv_dim = 2ull * s.gdn_k_heads * s.gdn_k_dim + static_cast<uint64_t>(s.gdn_v_heads) * s.gdn_v_dim;
+    shapes_.n_attn = static_cast<uint32_t>(n_attn);
+    shapes_.kv_heads = static_cast<uint32_t>(s.n_kv_heads);
+    shapes_.kv_row = static_cast<uint32_t>(s.n_kv_heads * s.head_dim);
+    shapes_.hidden = static_cast<uint32_t>(s.hidden);
+    shapes_.n_layers = static_cast<uint32_t>(L);
+    shapes_.conv_n = static_cast<uint64_t>(n_gdn) * conv_dim * static_cast<uint64_t>(std::max(0, s.conv_kernel - 1));
+    shapes_.gdn_n = static_cast<uint64_t>(n_gdn) * s.gdn_v_heads * s.gdn_k_dim * s.gdn_v_dim;
+    text_only_ = !pack_.has("mtp.fc.weight");
+    for (const auto &kv : pack_.manifest()["tensors"].obj)
+        if (kv.first.rfind("vision.", 0) == 0) text_only_ = false;   // (engine/src/vision.cpp's tensors)
+    conv_id_ = new_conversation_id(this);
+    return true;
+}
+
+uint64_t CudaModel::state_fingerprint() const { return ghost::state_fingerprint(pack_print(dir_), shapes_); }
+
+bool CudaModel::save_state(const std::string &path, bool append, int extra, int &code, std::string &err) {
+    code = 1;   // (GHOST_E_ARG)
+    if (!g_) {
+        err = "not open";
+        return false;
+    }
+    if (!text_only_) {
+        err = "a pack with an MTP layer or a vision encoder: its state holds what this backend does not keep";
+        return false;
+    }
+    const int pos = position();
+    const StateShapes &s = shapes_;
+    std::vector<float> conv(std::max<uint64_t>(1, s.conv_n)), gdn(std::max<uint64_t>(1, s.gdn_n));
+    std::vector<int8_t> kv(std::max<size_t>(1, static_cast<size_t>(s.n_attn) * 2 * pos * s.kv_row));
+    std::vector<float> ks(std::max<size_t>(1, static_cast<size_t>(s.n_attn) * 2 * pos * s.kv_heads));
+    code = 7;   // (GHOST_E_BACKEND)
+    if (api_.state_get(g_, conv.data(), gdn.data(), kv.data(), ks.data(), pos) != 0) return fail("state_get", err);
+    StateMeta m;
+    m.position = pos;
+    m.extra = extra;
+    m.conv_id = conv_id_;
+    code = 2;   // (GHOST_E_IO)
+    if (!write_state(path, state_fingerprint(), s, m, conv.data(), gdn.data(), kv.data(), ks.data(), append, err))
+        return false;
+    code = 0;
+    return true;
+}
+
+bool CudaModel::load_state(const std::string &path, int &extra, int &code, std::string &err) {
+    code = 1;
+    if (!g_) {
+        err = "not open";
+        return false;
+    }
+    auto refuse = [&](int c) {   // the conversation empty after any failure, as the engine's
+        api_.reset(g_);
+        conv_id_ = new_conversation_id(this);
+        last_n_ = 0;
+        code = c;
+        return false;
+    };
+    if (!text_only_) {
+        err = "a pack with an MTP layer or a vision encoder: its state holds what this backend does not keep";
+        return refuse(3);
+    }
+    StateMeta m;
+    std::vector<float> conv, gdn, ks;
+    std::vector<int8_t> kv;
+    const StateError e = read_state(path, state_fingerprint(), shapes_, context_, m, conv, gdn, kv, ks, err);
+    if (e != StateError::none) return refuse(e == StateError::format ? 3 : e == StateError::context ? 1 : 2);
+    conv.resize(std::max<size_t>(1, conv.size()));
+    gdn.resize(std::max<size_t>(1, gdn.size()));
+    kv.resize(std::max<size_t>(1, kv.size()));
+    ks.resize(std::max<size_t>(1, ks.size()));
+    if (api_.state_put(g_, conv.data(), gdn.data(), kv.data(), ks.data(), m.position) != 0) {
+        fail("state_put", err);
+        return refuse(7);
+    }
+    conv_id_ = m.conv_id;
+    extra = m.extra;
+    last_n_ = 0;
+    code = 0;
     return true;
 }
 

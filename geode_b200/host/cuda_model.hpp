@@ -12,6 +12,7 @@
 
 #include "../../include/geode_cuda.h"
 #include "pack.hpp"
+#include "state_file.hpp"
 
 namespace ghost {
 
@@ -30,6 +31,9 @@ struct CudaApi {
     decltype(&gcuda_keep) keep = nullptr;
     decltype(&gcuda_position) position = nullptr;
     decltype(&gcuda_accept) accept = nullptr;
+    decltype(&gcuda_state_get) state_get = nullptr;
+    decltype(&gcuda_state_put) state_put = nullptr;
+    decltype(&gcuda_reset) reset = nullptr;
     // path: the library file; empty = libgeode_cuda.so beside this library
     bool load(const std::string &path, std::string &err);
     ~CudaApi();
@@ -89,12 +93,28 @@ public:
     bool step(const int *batch, int n, const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept,
               int &next, std::string &err);
 
+    // Model::save_state / load_state (engine/src/state.cpp:241-465) in the engine's state file: the device's KV rows
+    // and recurrent states through the host (gcuda_state_get / gcuda_state_put), so a state saved by the reference
+    // engine (CPU or GPU path) continues here and back. extra: the caller's token passed on but not computed yet.
+    // A failed load leaves the conversation empty (position 0), as the engine's. Packs with an MTP layer or a vision
+    // encoder are refused (their states hold that layer's KV rows and the images' positions, which this backend does
+    // not keep). code: 0, or GHOST_E_IO / GHOST_E_FORMAT / GHOST_E_ARG as include/geode_host.h lists them.
+    bool save_state(const std::string &path, bool append, int extra, int &code, std::string &err);
+    bool load_state(const std::string &path, int &extra, int &code, std::string &err);
+    // the shapes the state file records and the fingerprint it carries for this pack
+    const StateShapes &state_shapes() const { return shapes_; }
+    uint64_t state_fingerprint() const;
+
 private:
     bool fail(const char *what, std::string &err);
     CudaApi api_;
     Pack pack_;
     gcuda *g_ = nullptr;
-    int max_tokens_ = 5, vocab_ = 0, last_n_ = 0;
+    int max_tokens_ = 5, vocab_ = 0, last_n_ = 0, context_ = 0;
+    std::string dir_;
+    StateShapes shapes_;
+    bool text_only_ = true;    // no MTP layer, no vision encoder in the pack
+    uint64_t conv_id_ = 0;     // the conversation (new at open and after a failed load; a loaded state's)
 };
 
 // The manifest as this host reads it, one line (tests): arch, layers, hidden, vocab, experts, tensor counts, bytes.

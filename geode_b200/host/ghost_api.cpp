@@ -1,6 +1,7 @@
 // ghost_api.cpp - the C ABI of include/geode_host.h over CudaModel.
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "../../include/geode_host.h"
 #include "cuda_model.hpp"
@@ -9,6 +10,7 @@ struct ghost_model {
     ghost::CudaModel model;
     ghost::SamplerParams params;
     ghost::Sampler sampler;
+    int32_t pending = -1;   // the token passed on but not computed yet (geode.cpp's `pending`)
 };
 
 namespace {
@@ -89,6 +91,7 @@ int ghost_step(ghost_model *m, const int32_t *batch, int32_t n, const int32_t *s
     }
     *kept = k;
     *next = nx;
+    m->pending = nx;
     return GHOST_OK;
 }
 
@@ -100,6 +103,118 @@ int ghost_pack_summary(const char *dir, char *out, size_t out_len, char *err, si
         return GHOST_E_IO;
     }
     put(s, out, out_len);
+    return GHOST_OK;
+}
+
+int ghost_state_save(ghost_model *m, const char *path, int32_t append, int32_t *out_position, char *err,
+                     size_t err_len) {
+    if (!m || !path || !*path) {
+        put("ghost_state_save: bad arguments", err, err_len);
+        return GHOST_E_ARG;
+    }
+    std::string e;
+    int code = 0;
+    if (!m->model.save_state(path, append != 0, m->pending, code, e)) {
+        put(e, err, err_len);
+        return code;
+    }
+    if (out_position) *out_position = m->model.position();
+    return GHOST_OK;
+}
+
+int ghost_state_load(ghost_model *m, const char *path, int32_t *out_position, char *err, size_t err_len) {
+    if (!m || !path || !*path) {
+        put("ghost_state_load: bad arguments", err, err_len);
+        return GHOST_E_ARG;
+    }
+    std::string e;
+    int code = 0, extra = -1;
+    const bool ok = m->model.load_state(path, extra, code, e);
+    m->pending = ok ? extra : -1;
+    if (out_position) *out_position = m->model.position();
+    if (!ok) {
+        put(e, err, err_len);
+        return code;
+    }
+    return GHOST_OK;
+}
+
+int32_t ghost_pending(ghost_model *m) { return m ? m->pending : -1; }
+
+namespace {
+ghost::StateShapes shapes_of(const ghost_state_shapes *s) {
+    ghost::StateShapes o;
+    o.n_attn = s->n_attn;
+    o.kv_heads = s->kv_heads;
+    o.kv_row = s->kv_row;
+    o.hidden = s->hidden;
+    o.n_layers = s->n_layers;
+    o.conv_n = s->conv_n;
+    o.gdn_n = s->gdn_n;
+    return o;
+}
+int state_code(ghost::StateError e) {
+    return e == ghost::StateError::none     ? GHOST_OK
+           : e == ghost::StateError::format ? GHOST_E_FORMAT
+           : e == ghost::StateError::context ? GHOST_E_ARG
+                                             : GHOST_E_IO;
+}
+}  // namespace
+
+uint64_t ghost_state_fingerprint(const char *pack_dir, const ghost_state_shapes *s) {
+    if (!pack_dir || !s) return 0;
+    return ghost::state_fingerprint(ghost::pack_print(pack_dir), shapes_of(s));
+}
+
+int ghost_state_write(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t position,
+                      int32_t extra, uint64_t conv_id, const float *conv, const float *gdn, const int8_t *kv,
+                      const float *kv_scale, int32_t append, char *err, size_t err_len) {
+    if (!path || !s) return GHOST_E_ARG;
+    ghost::StateMeta m;
+    m.position = position;
+    m.extra = extra;
+    m.conv_id = conv_id;
+    std::string e;
+    if (!ghost::write_state(path, fingerprint, shapes_of(s), m, conv, gdn, kv, kv_scale, append != 0, e)) {
+        put(e, err, err_len);
+        return e.rfind("write_state: bad", 0) == 0 ? GHOST_E_ARG : GHOST_E_IO;
+    }
+    return GHOST_OK;
+}
+
+int ghost_state_peek(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context,
+                     int32_t *position, int32_t *extra, uint64_t *conv_id, char *err, size_t err_len) {
+    if (!path || !s) return GHOST_E_ARG;
+    ghost::StateMeta m;
+    std::string e;
+    const ghost::StateError r = ghost::peek_state(path, fingerprint, shapes_of(s), context, m, e);
+    if (r != ghost::StateError::none) {
+        put(e, err, err_len);
+        return state_code(r);
+    }
+    if (position) *position = m.position;
+    if (extra) *extra = m.extra;
+    if (conv_id) *conv_id = m.conv_id;
+    return GHOST_OK;
+}
+
+int ghost_state_read(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context, float *conv,
+                     float *gdn, int8_t *kv, float *kv_scale, char *err, size_t err_len) {
+    if (!path || !s) return GHOST_E_ARG;
+    ghost::StateMeta m;
+    std::vector<float> c, g, ks;
+    std::vector<int8_t> k;
+    std::string e;
+    const ghost::StateError r = ghost::read_state(path, fingerprint, shapes_of(s), context, m, c, g, k, ks, e);
+    if (r != ghost::StateError::none) {
+        put(e, err, err_len);
+        return state_code(r);
+    }
+    if ((!c.empty() && !conv) || (!g.empty() && !gdn) || (!k.empty() && (!kv || !kv_scale))) return GHOST_E_ARG;
+    if (!c.empty()) std::memcpy(conv, c.data(), c.size() * sizeof(float));
+    if (!g.empty()) std::memcpy(gdn, g.data(), g.size() * sizeof(float));
+    if (!k.empty()) std::memcpy(kv, k.data(), k.size());
+    if (!ks.empty()) std::memcpy(kv_scale, ks.data(), ks.size() * sizeof(float));
     return GHOST_OK;
 }
 

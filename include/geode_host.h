@@ -22,7 +22,8 @@ extern "C" {
 enum {
     GHOST_OK = 0,
     GHOST_E_ARG = 1,      /* a bad argument (as GEODE_E_ARG) */
-    GHOST_E_IO = 2,       /* the pack is missing or unreadable (as GEODE_E_IO) */
+    GHOST_E_IO = 2,       /* a file is missing, unreadable or the wrong size (as GEODE_E_IO) */
+    GHOST_E_FORMAT = 3,   /* another model's, format's or version's file, or a damaged one (as GEODE_E_FORMAT) */
     GHOST_E_BACKEND = 7,  /* the CUDA backend failed or is absent (no CPU fallback) */
 };
 
@@ -56,6 +57,43 @@ int ghost_step(ghost_model *m, const int32_t *batch, int32_t n, const int32_t *s
 /* The pack's manifest as this host reads it, one line (arch, layers, hidden, vocab, experts, tensors, bytes); no GPU
  * needed. */
 int ghost_pack_summary(const char *dir, char *out, size_t out_len, char *err, size_t err_len);
+
+/* ------------------------------------------------------------------------------------ the conversation on disk ----
+ * geode_state_save / geode_state_load (engine/include/geode/geode.h:171-191) for this host, in the engine's own state
+ * file (engine/src/state.cpp): a state saved by the reference engine - its CPU or its GPU path - continues here, and
+ * one saved here continues there. Between steps only. The file holds the KV rows of every attention layer, the Gated
+ * DeltaNet conv and recurrent states and the token passed on but not computed yet (ghost_pending).
+ * ghost_state_save: append = the file holds an earlier state of this conversation - only what changed is written, its
+ * header last; otherwise it is written whole to path.tmp, then renamed over path. ghost_state_load: the saved
+ * conversation replaces this one; GHOST_E_FORMAT for another model's / format's / version's or a damaged file,
+ * GHOST_E_ARG when it is longer than this model's context, GHOST_E_IO when unreadable or cut short; on failure the
+ * conversation is empty. Packs with an MTP layer or a vision encoder: GHOST_E_ARG (save) / GHOST_E_FORMAT (load).
+ * out_position (may be NULL): the conversation's length in tokens. */
+int ghost_state_save(ghost_model *m, const char *path, int32_t append, int32_t *out_position, char *err,
+                     size_t err_len);
+int ghost_state_load(ghost_model *m, const char *path, int32_t *out_position, char *err, size_t err_len);
+/* The token passed on but not computed yet: the last ghost_step's next, or a loaded state's (-1: none). */
+int32_t ghost_pending(ghost_model *m);
+
+/* The state file alone, with host buffers (no GPU): what ghost_state_save / ghost_state_load write and read. Shapes:
+ * n_attn attention layers, kv_heads, kv_row = kv_heads x head_dim, hidden, n_layers, conv_n and gdn_n floats of the
+ * Gated DeltaNet conv and recurrent states. Buffers in the layouts of gcuda_state_get / gcuda_state_put: conv, gdn
+ * the engine's own; kv [n_attn][2][position][kv_row] int8, kv_scale [n_attn][2][position][kv_heads] f32. */
+typedef struct {
+    uint32_t n_attn, kv_heads, kv_row, hidden, n_layers;
+    uint64_t conv_n, gdn_n;
+} ghost_state_shapes;
+/* The fingerprint a state of this pack (geode.json in pack_dir) and these shapes carries (Model::fingerprint). */
+uint64_t ghost_state_fingerprint(const char *pack_dir, const ghost_state_shapes *s);
+int ghost_state_write(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t position,
+                      int32_t extra, uint64_t conv_id, const float *conv, const float *gdn, const int8_t *kv,
+                      const float *kv_scale, int32_t append, char *err, size_t err_len);
+/* The header, checked against the fingerprint, the shapes and context (position < context): position, extra and
+ * conversation id out, to size the buffers of ghost_state_read. */
+int ghost_state_peek(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context,
+                     int32_t *position, int32_t *extra, uint64_t *conv_id, char *err, size_t err_len);
+int ghost_state_read(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context, float *conv,
+                     float *gdn, int8_t *kv, float *kv_scale, char *err, size_t err_len);
 
 #ifdef __cplusplus
 }

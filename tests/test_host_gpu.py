@@ -77,3 +77,74 @@ def test_host_verify_and_steps(env):
             assert H.ghost_position(m) == be.pos
     finally:
         be.close()
+
+
+def test_host_state_file(env, tmp_path):
+    """ghost_state_save / ghost_state_load through the device, in the engine's own state file: a state the reference
+    engine saved (oracle/_ref, where it is built; else one written from the oracle's state by ghost_state_write) loads
+    into the GPU, whose next batch then matches the oracle's continuation within the parity tolerance; the GPU's state
+    saved back reads as the same buffers (ghost_state_read) and loads again; a file of another model is refused and
+    leaves the conversation empty."""
+    H, m, d, shape = env
+    from test_state_file import Shapes, _state
+    H.ghost_state_save.argtypes = [C.c_void_p, C.c_char_p, C.c_int32, C.POINTER(C.c_int32), C.c_char_p, C.c_size_t]
+    H.ghost_state_load.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_int32), C.c_char_p, C.c_size_t]
+    H.ghost_pending.argtypes = [C.c_void_p]
+    H.ghost_state_fingerprint.restype = C.c_uint64
+    H.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
+    H.ghost_state_write.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.c_int32, C.c_uint64,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t]
+    ora = op.Oracle(d)
+    c = ora.cfg
+    conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+    s = Shapes(ora.n_attn, c.n_kv_heads, c.n_kv_heads * c.head_dim, c.hidden, c.n_layers,
+               ora.n_gdn * conv_dim * (c.conv_kernel - 1), ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim)
+    fp = H.ghost_state_fingerprint(d.encode(), C.byref(s))
+    rng = np.random.default_rng(8)
+    prompt = rng.integers(0, shape.vocab, 260).astype(np.int32)
+    err = C.create_string_buffer(512)
+    a = str(tmp_path / "a.state")
+    if op.have_reference():
+        ref = op.Reference(d, ctx=shape.ctx)
+        ref.forward(prompt, all_logits=False)
+        ref.save_state(a)
+        ref.close()
+    else:
+        st0, kv0, kvs0 = _state(ora, prompt, shape.ctx)
+        assert H.ghost_state_write(a.encode(), fp, C.byref(s), st0.pos, 0, 9, st0.conv.ctypes.data, st0.gdn.ctypes.data,
+                                   kv0.ctypes.data, kvs0.ctypes.data, 0, err, 512) == 0, err.value
+    pos = C.c_int32(0)
+    assert H.ghost_state_load(m, a.encode(), C.byref(pos), err, 512) == 0, err.value
+    assert pos.value == 260 and H.ghost_position(m) == 260 and H.ghost_pending(m) == 0
+    st, _, _ = _state(ora, prompt, shape.ctx)
+    toks = rng.integers(0, shape.vocab, 5).astype(np.int32)
+    lg = np.zeros((5, shape.vocab), np.float32)
+    assert H.ghost_verify(m, toks.ctypes.data_as(C.c_void_p), 5, lg.ctypes.data_as(C.c_void_p), err, 512) == 0, err.value
+    want = ora.forward(st, toks)["logits"]
+    span = want.max(1) - want.min(1)
+    assert np.all(np.abs(lg - want).max(1) <= 1e-2 * span)
+    # the GPU's state (265 positions) saved, read back on the host, loaded again
+    b = str(tmp_path / "b.state")
+    assert H.ghost_state_save(m, b.encode(), 0, C.byref(pos), err, 512) == 0, err.value
+    assert pos.value == 265
+    from test_state_file import _read
+    rc, e, got = _read(H, b, fp, s, shape.ctx)
+    assert rc == 0, e
+    P, extra, cid, conv, gdn, kv, kvs = got
+    assert P == 265
+    assert np.allclose(gdn[:st.gdn.size], st.gdn, rtol=5e-2, atol=5e-3)
+    assert np.abs(kv.astype(np.int32) - _state(ora, np.concatenate([prompt, toks]), shape.ctx)[1].astype(np.int32)).max() <= 2
+    assert H.ghost_state_load(m, b.encode(), C.byref(pos), err, 512) == 0, err.value
+    assert H.ghost_position(m) == 265
+    lg2 = np.zeros((5, shape.vocab), np.float32)
+    toks2 = rng.integers(0, shape.vocab, 5).astype(np.int32)
+    assert H.ghost_verify(m, toks2.ctypes.data_as(C.c_void_p), 5, lg2.ctypes.data_as(C.c_void_p), err, 512) == 0
+    want2 = ora.forward(st, toks2)["logits"]
+    span2 = want2.max(1) - want2.min(1)
+    assert np.all(np.abs(lg2 - want2).max(1) <= 1e-2 * span2)
+    # another model's file: refused, the conversation empty
+    bad = bytearray(open(b, "rb").read())
+    bad[16] ^= 1   # (the fingerprint; the checksum no longer matches either)
+    open(str(tmp_path / "bad.state"), "wb").write(bad)
+    assert H.ghost_state_load(m, str(tmp_path / "bad.state").encode(), C.byref(pos), err, 512) == 3
+    assert H.ghost_position(m) == 0 and H.ghost_pending(m) == -1

@@ -1,0 +1,190 @@
+"""The engine's state file through the host library, without a GPU (libgeode_host.so: ghost_state_write / peek /
+read, the format behind ghost_state_save / ghost_state_load).
+
+- pinned to the reference engine (oracle/_ref, its own Model::save_state / load_state): the file the reference saves
+  after a prompt reads back as the oracle's state after the same prompt (bit for bit - the oracle is itself pinned to
+  the reference), and the file written here from those buffers equals the reference's byte for byte; a file written
+  here loads into the reference, which then continues exactly as the oracle from that state;
+- round trip, append (in place: the same buffers back, gen 2, the earlier KV blocks kept), and the refusals: a
+  damaged header, another model's fingerprint, a file cut short, an interrupted save, a state longer than the
+  context.
+"""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from geode_b200 import synth
+import oracle_py as op
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HOST_SO = os.path.join(ROOT, "geode_b200", "libgeode_host.so")
+ref_only = pytest.mark.skipif(not op.have_reference(), reason="the reference build oracle/_ref is not here")
+
+OK, E_ARG, E_IO, E_FORMAT = 0, 1, 2, 3
+
+
+class Shapes(C.Structure):
+    _fields_ = [("n_attn", C.c_uint32), ("kv_heads", C.c_uint32), ("kv_row", C.c_uint32), ("hidden", C.c_uint32),
+                ("n_layers", C.c_uint32), ("conv_n", C.c_uint64), ("gdn_n", C.c_uint64)]
+
+
+@pytest.fixture(scope="module")
+def H():
+    if not os.path.exists(HOST_SO):
+        pytest.fail(f"{HOST_SO} is not built (python -m geode_b200.build)")
+    L = C.CDLL(HOST_SO)
+    vp, i32, u64, sz = C.c_void_p, C.c_int32, C.c_uint64, C.c_size_t
+    L.ghost_state_fingerprint.restype = u64
+    L.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
+    L.ghost_state_write.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, i32, u64, vp, vp, vp, vp, i32, C.c_char_p, sz]
+    L.ghost_state_peek.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, C.POINTER(i32), C.POINTER(i32),
+                                   C.POINTER(u64), C.c_char_p, sz]
+    L.ghost_state_read.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, vp, vp, vp, vp, C.c_char_p, sz]
+    return L
+
+
+@pytest.fixture(scope="module")
+def model(tmp_path_factory):
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d = str(tmp_path_factory.mktemp("statepack"))
+    synth.write_pack(d, shape, seed=3)
+    ora = op.Oracle(d)
+    c = ora.cfg
+    conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+    s = Shapes(ora.n_attn, c.n_kv_heads, c.n_kv_heads * c.head_dim, c.hidden, c.n_layers,
+               ora.n_gdn * conv_dim * (c.conv_kernel - 1), ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim)
+    toks = np.random.default_rng(4).integers(0, shape.vocab, 400).astype(np.int32)
+    return d, shape, ora, s, toks
+
+
+def _state(ora, toks, ctx):
+    st = ora.new_state(ctx)
+    ora.forward(st, toks, logits=False)
+    c = ora.cfg
+    A, row = ora.n_attn, c.n_kv_heads * c.head_dim
+    kv = np.ascontiguousarray(st.kv.reshape(A, 2, ctx, row)[:, :, :st.pos])
+    kvs = np.ascontiguousarray(st.kvs.reshape(A, 2, ctx, c.n_kv_heads)[:, :, :st.pos])
+    return st, kv, kvs
+
+
+def _p(a):
+    return a.ctypes.data
+
+
+def _write(H, path, fp, s, st, kv, kvs, conv_id=77, extra=-1, append=0):
+    err = C.create_string_buffer(256)
+    rc = H.ghost_state_write(path.encode(), fp, C.byref(s), st.pos, extra, conv_id, _p(st.conv), _p(st.gdn), _p(kv),
+                             _p(kvs), append, err, 256)
+    assert rc == OK, err.value
+    return rc
+
+
+def _read(H, path, fp, s, context):
+    err = C.create_string_buffer(256)
+    pos, extra, cid = C.c_int32(0), C.c_int32(0), C.c_uint64(0)
+    rc = H.ghost_state_peek(path.encode(), fp, C.byref(s), context, C.byref(pos), C.byref(extra), C.byref(cid), err, 256)
+    if rc != OK:
+        return rc, err.value.decode(), None
+    P = pos.value
+    conv = np.zeros(max(1, s.conv_n), np.float32)
+    gdn = np.zeros(max(1, s.gdn_n), np.float32)
+    kv = np.zeros((s.n_attn, 2, P, s.kv_row), np.int8)
+    kvs = np.zeros((s.n_attn, 2, P, s.kv_heads), np.float32)
+    rc = H.ghost_state_read(path.encode(), fp, C.byref(s), context, _p(conv), _p(gdn), _p(kv), _p(kvs), err, 256)
+    return rc, err.value.decode(), (P, extra.value, cid.value, conv, gdn, kv, kvs)
+
+
+def test_roundtrip_append_and_refusals(H, model, tmp_path):
+    d, shape, ora, s, toks = model
+    fp = H.ghost_state_fingerprint(d.encode(), C.byref(s))
+    st1, kv1, kvs1 = _state(ora, toks[:100], shape.ctx)
+    st2, kv2, kvs2 = _state(ora, toks[:400], shape.ctx)
+    path = str(tmp_path / "a.state")
+    _write(H, path, fp, s, st1, kv1, kvs1, extra=123)
+    rc, e, got = _read(H, path, fp, s, shape.ctx)
+    assert rc == OK, e
+    P, extra, cid, conv, gdn, kv, kvs = got
+    assert (P, extra, cid) == (100, 123, 77)
+    assert np.array_equal(conv[:st1.conv.size], st1.conv) and np.array_equal(gdn[:st1.gdn.size], st1.gdn)
+    assert np.array_equal(kv, kv1) and np.array_equal(kvs, kvs1)
+    # append: the same conversation grown - written in place, gen 2, and it reads back as the later state
+    _write(H, path, fp, s, st2, kv2, kvs2, extra=5, append=1)
+    assert not os.path.exists(path + ".tmp")
+    raw = open(path, "rb").read()
+    assert int.from_bytes(raw[32:40], "little") == 2   # (gen)
+    rc, e, got = _read(H, path, fp, s, shape.ctx)
+    assert rc == OK, e
+    P, extra, cid, conv, gdn, kv, kvs = got
+    assert (P, extra, cid) == (400, 5, 77)
+    assert np.array_equal(kv, kv2) and np.array_equal(kvs, kvs2) and np.array_equal(gdn[:st2.gdn.size], st2.gdn)
+    # the same as a whole write of the later state, but for gen and the header's checksum
+    whole = str(tmp_path / "w.state")
+    _write(H, whole, fp, s, st2, kv2, kvs2, extra=5)
+    raw_w = open(whole, "rb").read()
+    assert len(raw) == len(raw_w)
+    a, w = np.frombuffer(raw, np.uint8), np.frombuffer(raw_w, np.uint8)
+    diff = np.nonzero(a != w)[0]
+    assert len(diff) and all(32 <= i < 40 or 136 <= i < 144 or 4096 <= i < 4104 or _in_trail(raw, i) for i in diff)
+    # another conversation: not an append (written whole, gen 1)
+    _write(H, path, fp, s, st2, kv2, kvs2, conv_id=78, append=1)
+    assert int.from_bytes(open(path, "rb").read()[32:40], "little") == 1
+    # refusals
+    assert _read(H, path, fp + 1, s, shape.ctx)[0] == E_FORMAT            # another model
+    assert _read(H, path, fp, s, 400)[0] == E_ARG                          # longer than the context
+    bad = bytearray(open(path, "rb").read())
+    bad[44] ^= 1                                                           # (extra, under the checksum)
+    open(str(tmp_path / "d.state"), "wb").write(bad)
+    assert _read(H, str(tmp_path / "d.state"), fp, s, shape.ctx)[0] == E_FORMAT
+    good = open(path, "rb").read()
+    open(str(tmp_path / "t.state"), "wb").write(good[:len(good) - 1000])
+    assert _read(H, str(tmp_path / "t.state"), fp, s, shape.ctx)[0] == E_IO   # cut short
+    torn = bytearray(good)
+    torn[4096] ^= 1                                                        # (the fixed part's leading gen)
+    open(str(tmp_path / "g.state"), "wb").write(torn)
+    assert _read(H, str(tmp_path / "g.state"), fp, s, shape.ctx)[0] == E_IO   # an interrupted save
+    assert _read(H, str(tmp_path / "missing.state"), fp, s, shape.ctx)[0] == E_IO
+
+
+def _in_trail(raw, i):
+    """i lies in the fixed part's trailing gen (its offset from the header's layout)."""
+    fixed_offset = int.from_bytes(raw[104:112], "little")
+    fixed_bytes = int.from_bytes(raw[112:120], "little")
+    trail = fixed_offset + fixed_bytes - 8
+    return trail <= i < trail + 8
+
+
+@ref_only
+def test_pinned_to_the_reference(H, model, tmp_path):
+    d, shape, ora, s, toks = model
+    fp = H.ghost_state_fingerprint(d.encode(), C.byref(s))
+    ref = op.Reference(d, ctx=shape.ctx)
+    try:
+        ref.forward(toks[:300], all_logits=False)
+        a = str(tmp_path / "ref.state")
+        ref.save_state(a)
+        # the reference's file reads here as the oracle's state after the same prompt
+        rc, e, got = _read(H, a, fp, s, shape.ctx)
+        assert rc == OK, e
+        P, extra, cid, conv, gdn, kv, kvs = got
+        st, kv_o, kvs_o = _state(ora, toks[:300], shape.ctx)
+        assert P == 300 and extra == 0
+        assert np.array_equal(conv[:st.conv.size], st.conv) and np.array_equal(gdn[:st.gdn.size], st.gdn)
+        assert np.array_equal(kv, kv_o) and np.array_equal(kvs, kvs_o)
+        # written here from those buffers (the reference's conversation id and extra): the same bytes
+        b = str(tmp_path / "ours.state")
+        _write(H, b, fp, s, st, kv_o, kvs_o, conv_id=cid, extra=0)
+        assert open(a, "rb").read() == open(b, "rb").read()
+        # a state written here (another length) loads into the reference, which continues as the oracle does
+        st2, kv2, kvs2 = _state(ora, toks[:137], shape.ctx)
+        c = str(tmp_path / "ours2.state")
+        _write(H, c, fp, s, st2, kv2, kvs2, conv_id=5, extra=0)
+        ref.load_state(c)
+        assert ref.pos == 137
+        nxt = toks[137:142]
+        got_l = ref.forward(nxt, all_logits=True)["logits"]
+        want = ora.forward(st2, nxt, logits=True)["logits"]
+        assert np.array_equal(got_l, want)
+    finally:
+        ref.close()
