@@ -94,6 +94,10 @@ def test_host_state_file(env, tmp_path):
     H.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
     H.ghost_state_write.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.c_int32, C.c_uint64,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t]
+    H.ghost_state_peek.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.POINTER(C.c_int32),
+                                   C.POINTER(C.c_int32), C.POINTER(C.c_uint64), C.c_char_p, C.c_size_t]
+    H.ghost_state_read.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
     ora = op.Oracle(d)
     c = ora.cfg
     conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
