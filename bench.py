@@ -184,6 +184,51 @@ def cpu_reference(steps: int = 3, layers: int = 4, threads: int = 0) -> dict:
                       f"{t40 * 1e3:.0f} ms/step"}
 
 
+ACCEPT_METRIC = "acceptance rows/s (cfg5: 256 sequences x (8+1) rows, vocab 248320)"
+ACCEPT_UNIT = "verified rows/s (greedy)"
+
+
+def cpu_accept_reference(seqs: int = 24, seed: int = 5) -> dict:
+    """The acceptance microbench's CPU side on a bounded sample (`seqs` of its 256 sequences, the same shapes: 8+1
+    target rows and 8 draft rows of N(0, 3) logits over vocab 248320, drafts = the draft rows' argmax): greedy with the
+    reference engine's own rule (oracle/_ref: geode_generate's acceptance around geode::Sampler at temperature 0, one
+    sequence after another on one thread), and rejection sampling (T 0.7, top-k 20, top-p 0.95, Philox 1234) with
+    the oracle's port - the reference has none. value = the greedy rate in the GPU line's unit: the 9 rows of a
+    sequence per sequence (the rule reads only up to the first failed draft, as the GPU call's rows are counted)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes as C
+    import oracle_py as op  # (the baseline leg only: the reference's code timed on the host)
+    S, K, V = seqs, 8, 248320
+    rng = np.random.default_rng(seed)
+    target = (rng.standard_normal((S, K + 1, V), dtype=np.float32) * 3).astype(np.float32)
+    draft = (rng.standard_normal((S, K, V), dtype=np.float32) * 3).astype(np.float32)
+    drafts = np.ascontiguousarray(np.argmax(draft, axis=2).astype(np.int32))
+    kind = "reference" if op.have_reference() else "port"
+    lib = op.reference_lib() if kind == "reference" else op.oracle_lib()
+    accept = lib.ref_accept if kind == "reference" else lib.go_accept
+    samples = np.zeros(K + 1, np.int32)
+    nxt = C.c_int(0)
+    t0 = time.perf_counter()
+    for s_ in range(S):
+        batch = np.ascontiguousarray(np.concatenate([[0], drafts[s_]]).astype(np.int32))
+        accept(np.ascontiguousarray(target[s_]).ctypes.data, K + 1, V, batch.ctypes.data, 0.0, 1.0, 0, C.c_uint64(0), None,
+               0, C.byref(nxt), samples.ctypes.data)
+    t_greedy = time.perf_counter() - t0
+    O = op.oracle_lib()
+    n_rej = max(1, S // 3)
+    t0 = time.perf_counter()
+    for s_ in range(n_rej):
+        O.go_spec_reject(np.ascontiguousarray(target[s_]).ctypes.data, np.ascontiguousarray(draft[s_]).ctypes.data, K, V,
+                         np.ascontiguousarray(drafts[s_]).ctypes.data, 0.7, 0.95, 20, C.c_uint64(1234), s_, C.byref(nxt))
+    t_rej = time.perf_counter() - t0
+    return {"kind": kind, "value": S * (K + 1) / t_greedy, "unit": ACCEPT_UNIT, "cores": 1,
+            "sample": f"{S} of the 256 sequences (seeded N(0, 3) logits, drafts = the draft rows' argmax): greedy by the "
+                      f"{'reference engine' if kind == 'reference' else 'oracle port'}'s rule {t_greedy * 1e3:.1f} ms; "
+                      f"rejection sampling by the oracle port (no reference code) on {n_rej} sequences "
+                      f"{t_rej * 1e3:.0f} ms",
+            "rejection_port_sequences_per_s": n_rej / t_rej}
+
+
 def max_over_ranks(value: float, dist, device) -> float:
     """The largest of every rank's value (every rank takes the same collective; a lone process returns its own)."""
     if dist is None:
@@ -199,6 +244,18 @@ def reference_arm(args):
     if rank != 0:
         return 0
     t0 = time.perf_counter()
+    if args.workload == "cfg5":
+        cb = cpu_accept_reference()
+        v = cb["value"]
+        print(json.dumps({"impl": "reference", "metric": ACCEPT_METRIC, "value": v, "unit": ACCEPT_UNIT,
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": 256 * 9 / v * 1e3, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": "cfg5: acceptance microbench, 256 x 8 drafts, V 248320, greedy"},
+                          "cpu_baseline": cb,
+                          "e2e": {"value": v, "unit": ACCEPT_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                          "wall_s": time.perf_counter() - t0}))
+        return 0
     cb = cpu_reference(steps=max(1, min(args.steps, 3)))
     if cb.get("value") is None:
         print(json.dumps({"impl": "reference", "unavailable": cb["sample"]}))
@@ -319,8 +376,7 @@ def accept_bench(args) -> int:
     bytes_r = rows_r * V * 4
     ach = bytes_g / (ms_g * 1e-3) / 1e9
     line = {
-        "metric": "acceptance rows/s (cfg5: 256 sequences x (8+1) rows, vocab 248320)", "value": rows / (ms_g * 1e-3),
-        "unit": "verified rows/s (greedy)", "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
+        "metric": ACCEPT_METRIC, "value": rows / (ms_g * 1e-3), "unit": ACCEPT_UNIT, "n_gpus": 1, "steps": steps, "warmup": max(3, args.warmup),
         "ms_per_step": ms_g, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (logits N(0, 3) made on the device, seed 5; drafts = the draft rows' argmax)",
         "config": {"workload": "cfg5: acceptance microbench, 256 x 8 drafts, V 248320, T 0.7, top-k 20, top-p 0.95, "
@@ -330,7 +386,8 @@ def accept_bench(args) -> int:
         "rejection": {"ms_per_call": ms_r, "sequences_per_s": S / (ms_r * 1e-3), "rows_read": rows_r,
                       "achieved_gbs": bytes_r / (ms_r * 1e-3) / 1e9, "mean_accepted": float(a.mean()),
                       "accepted_hist": np.bincount(a, minlength=K + 1).tolist()},
-        "cpu_baseline": None, "e2e": None, "clocks": clk.summary(), "peak_kind": peak_kind,
+        "cpu_baseline": None if args.no_cpu_baseline else cpu_accept_reference(), "e2e": None,
+        "clocks": clk.summary(), "peak_kind": peak_kind,
     }
     print(json.dumps(line))
     return 0

@@ -50,3 +50,13 @@ def test_max_over_ranks_single():
     sys.path.insert(0, ROOT)
     import bench
     assert bench.max_over_ranks(3.5, None, "cpu") == 3.5
+
+
+def test_cpu_accept_reference_leg():
+    """The acceptance microbench's CPU leg (bench.py --workload cfg5: its cpu_baseline and its --impl reference arm):
+    the reference engine's greedy rule and the rejection-sampling port over a small sample give positive rates in the
+    GPU line's unit."""
+    import bench
+    cb = bench.cpu_accept_reference(seqs=3)
+    assert cb["unit"] == bench.ACCEPT_UNIT and cb["value"] > 0 and cb["rejection_port_sequences_per_s"] > 0
+    assert cb["kind"] in ("reference", "port") and cb["cores"] == 1
