@@ -8,7 +8,11 @@ restatement, so tests/test_oracle.py pins the restatement to the reference where
   the sampler's uniform stream (std::mt19937_64 + generate_canonical, engine/src/sampler.cpp:45);
 - accept.npz: the acceptance rule (engine/src/geode.cpp:327-350) around geode::Sampler, greedy and sampled;
 - model_moe.npz / model_dense.npz: Model::forward_batch over a prompt and a 5-token verify batch on a tiny synthetic
-  pack (written by geode_b200/synth.py with the seed stored), every logit and the per-layer trace.
+  pack (written by geode_b200/synth.py with the seed stored), every logit and the per-layer trace;
+- state_file.npz: Model::save_state's file (engine/src/state.cpp) after a 20-token prompt on a tiny synthetic pack,
+  with that pack's geode.json (the state's fingerprint hashes it) and the shapes the state records.
+
+Run with names (kernels, accept, model, state) to regenerate only those fixtures.
 """
 import ctypes as C
 import os
@@ -119,12 +123,40 @@ def model(arch, name, seed=21, attn_block=64):
     np.savez_compressed(os.path.join(OUT, name + ".npz"), **out)
 
 
+def state_file(seed=31):
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_pack(d, shape, seed=seed)
+        ref = op.Reference(d, threads=1, ctx=shape.ctx)
+        prompt = np.random.default_rng(seed + 1).integers(0, shape.vocab, 20).astype(np.int32)
+        ref.forward(prompt, all_logits=False)
+        path = os.path.join(d, "s.state")
+        ref.save_state(path)
+        ref.close()
+        ora = op.Oracle(d)
+        c = ora.cfg
+        conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+        shapes = np.array([ora.n_attn, c.n_kv_heads, c.n_kv_heads * c.head_dim, c.hidden, c.n_layers,
+                           ora.n_gdn * conv_dim * (c.conv_kernel - 1),
+                           ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim], np.uint64)
+        manifest = np.frombuffer(open(os.path.join(d, "geode.json"), "rb").read(), np.uint8)
+        state = np.frombuffer(open(path, "rb").read(), np.uint8)
+    np.savez_compressed(os.path.join(OUT, "state_file.npz"), seed=seed, prompt=prompt, shapes=shapes,
+                        manifest=manifest, state=state)
+
+
 if __name__ == "__main__":
     if not op.have_reference():
         sys.exit("build the reference first: make -C oracle ref")
     R = op.reference_lib()
-    kernels(R)
-    accept(R)
-    model("qwen35moe", "model_moe")
-    model("qwen35", "model_dense")
+    which = set(sys.argv[1:]) or {"kernels", "accept", "model", "state"}
+    if "kernels" in which:
+        kernels(R)
+    if "accept" in which:
+        accept(R)
+    if "model" in which:
+        model("qwen35moe", "model_moe")
+        model("qwen35", "model_dense")
+    if "state" in which:
+        state_file()
     print("written to", OUT)

@@ -5,6 +5,8 @@ read, the format behind ghost_state_save / ghost_state_load).
   after a prompt reads back as the oracle's state after the same prompt (bit for bit - the oracle is itself pinned to
   the reference), and the file written here from those buffers equals the reference's byte for byte; a file written
   here loads into the reference, which then continues exactly as the oracle from that state;
+- the same pin without the reference build, from tests/golden/state_file.npz (a file the reference saved, with its
+  pack's manifest; made by tests/golden/make_golden.py);
 - round trip, append (in place: the same buffers back, gen 2, the earlier KV blocks kept), and the refusals: a
   damaged header, another model's fingerprint, a file cut short, an interrupted save, a state longer than the
   context.
@@ -188,3 +190,38 @@ def test_pinned_to_the_reference(H, model, tmp_path):
         assert np.array_equal(got_l, want)
     finally:
         ref.close()
+
+
+def test_golden_state_file(H, tmp_path):
+    """Without the reference build: tests/golden/state_file.npz holds the file the reference engine's save_state wrote
+    after a 20-token prompt on a tiny pack, and that pack's geode.json. The fingerprint computed here from the manifest
+    equals the file's; the file reads here as the oracle's state after the same prompt (the pack written again from
+    its seed gives the same manifest); written again here from what was read, it is the same bytes."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "state_file.npz"))
+    state = g["state"].tobytes()
+    d = tmp_path / "pack"
+    d.mkdir()
+    (d / "geode.json").write_bytes(g["manifest"].tobytes())
+    sh = [int(x) for x in g["shapes"]]
+    s = Shapes(*sh)
+    fp = H.ghost_state_fingerprint(str(d).encode(), C.byref(s))
+    assert fp == int.from_bytes(state[16:24], "little")
+    path = str(tmp_path / "golden.state")
+    open(path, "wb").write(state)
+    rc, e, got = _read(H, path, fp, s, 640)
+    assert rc == OK, e
+    P, extra, cid, conv, gdn, kv, kvs = got
+    assert (P, extra) == (20, 0)
+    # the oracle's state after the same prompt on the same pack
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d2 = str(tmp_path / "again")
+    synth.write_pack(d2, shape, seed=int(g["seed"]))
+    assert open(os.path.join(d2, "geode.json"), "rb").read() == g["manifest"].tobytes()
+    st, kv_o, kvs_o = _state(op.Oracle(d2), g["prompt"], shape.ctx)
+    assert np.array_equal(conv[:st.conv.size], st.conv) and np.array_equal(gdn[:st.gdn.size], st.gdn)
+    assert np.array_equal(kv, kv_o) and np.array_equal(kvs, kvs_o)
+    out = str(tmp_path / "again.state")
+    err = C.create_string_buffer(256)
+    assert H.ghost_state_write(out.encode(), fp, C.byref(s), P, extra, cid, _p(conv), _p(gdn), _p(kv), _p(kvs), 0, err,
+                               256) == OK, err.value
+    assert open(out, "rb").read() == state
