@@ -154,7 +154,8 @@ int gcuda_sync_step(gcuda *g, int *steps, int *union_sum, int *last_kept);
 /* gcuda_step_device with speculative (rejection) sampling in place of the greedy acceptance (the draft-model
  * configurations): the verified rows against the draft model's rows d_draft [n-1][vocab] on the device, the drafts
  * toks[1..n-1]; Philox4x32-10 key = seed plus the handle's count of these steps times a constant. As
- * gcuda_spec_reject for one sequence, chained on the device with the decision and the rollback. */
+ * gcuda_spec_reject for one sequence, chained on the device with the decision and the rollback. No counterpart in
+ * the reference (it has no rejection sampling, and its loop is host code). */
 int gcuda_step_device_reject(gcuda *g, int n, const float *d_draft, const gcuda_sampling *s, uint64_t seed);
 
 /* ----------------------------------------------------------------------------------------- synthetic models ----

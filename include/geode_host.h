@@ -72,7 +72,8 @@ int ghost_pack_summary(const char *dir, char *out, size_t out_len, char *err, si
 int ghost_state_save(ghost_model *m, const char *path, int32_t append, int32_t *out_position, char *err,
                      size_t err_len);
 int ghost_state_load(ghost_model *m, const char *path, int32_t *out_position, char *err, size_t err_len);
-/* The token passed on but not computed yet: the last ghost_step's next, or a loaded state's (-1: none). */
+/* The token passed on but not computed yet: the last ghost_step's next, or a loaded state's (-1: none) - the
+ * engine's `pending` (engine/src/geode.cpp:490-519, the `extra` its state file carries). */
 int32_t ghost_pending(ghost_model *m);
 
 /* The state file alone, with host buffers (no GPU): what ghost_state_save / ghost_state_load write and read. Shapes:
