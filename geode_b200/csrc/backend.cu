@@ -920,6 +920,11 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
     if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "verify before setup");
     if (!toks || n < 1 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "a verified batch of " + std::to_string(n) + " tokens");
     if (g->pos + n > g->sh.context) return fail(g, GCUDA_E_ARG, "the context is full");
+    // every token's embedding row exists before anything runs (engine/src/model.cpp:1551-1555): a bad id is an error
+    // that leaves the conversation as it was
+    for (int t = 0; t < n; ++t)
+        if (toks[t] < 0 || toks[t] >= g->sh.vocab)
+            return fail(g, GCUDA_E_ARG, "cannot read the embedding of token " + std::to_string(toks[t]));
     cudaSetDevice(g->device);
     LAUNCH_OK(cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
     RC_OK(gcuda_verify_device(g, g->d_toks, n));

@@ -94,7 +94,8 @@ int gcuda_set_ep(gcuda *g, int rank, int world, const void *id);
 
 /* Model::verify_n (engine/src/model.cpp:1483): n tokens (toks[0] the last accepted token, then the drafts) at the
  * next positions through every layer; logits [n][vocab] (host; NULL: left on the device) and hidden [n][hidden]
- * (the rows after the final norm, the MTP layer's input; NULL: not wanted). The position moves on by n. */
+ * (the rows after the final norm, the MTP layer's input; NULL: not wanted). The position moves on by n. A token id
+ * outside [0, vocab): GCUDA_E_ARG before anything runs, the conversation as it was (engine/src/model.cpp:1551-1555). */
 int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden);
 /* Model::verify_keep (engine/src/model.cpp:1594): keep the first `kept` (1 .. n-1) of the last verified batch - the
  * Gated DeltaNet states as after token kept-1, the position back by n - kept. */
@@ -131,7 +132,9 @@ int gcuda_state_put(gcuda *g, const float *conv, const float *gdn, const int8_t 
 /* Device pointers of the last batch's results (the verify step's outputs stay resident): logits [max_tokens][vocab]. */
 const float *gcuda_device_logits(gcuda *g);
 /* The verify step with the tokens already on the device (d_toks: n int32) and the results left there - the resident
- * form of gcuda_verify for callers that keep their batches on the GPU. */
+ * form of gcuda_verify for callers that keep their batches on the GPU. Token ids are checked on the device only: one
+ * out of range gives GCUDA_E_DEVICE after the step has run on a zero row in its place, the position unmoved but the
+ * recurrent states advanced - reset or load the conversation after it. */
 int gcuda_verify_device(gcuda *g, const int *d_toks, int n);
 /* Milliseconds of the last gcuda_verify / gcuda_verify_device on the device (CUDA events on the handle's stream). */
 float gcuda_last_ms(gcuda *g);
