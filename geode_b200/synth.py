@@ -223,9 +223,13 @@ class _Writer:
 
 
 def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quantized",
-               router_std: float = 0.05, weight_std: float = 0.02) -> Dict:
+               router_std: float = 0.05, weight_std: float = 0.02, mtp: bool = False) -> Dict:
     """Writes a geode-pack for ``shape`` into out_dir; returns the manifest. fill: "quantized" (N(0, weight_std)
-    weights through the reference quantizer) or "random" (random q4 bytes)."""
+    weights through the reference quantizer) or "random" (random q4 bytes). mtp: also the MTP drafting layer, as the
+    engine reads it (engine/src/model.cpp:175-191, engine/src/pack.cpp:300-305): mtp.fc.weight [hidden, 2 hidden],
+    the norms mtp.norm / mtp.pre_fc_norm_embedding / mtp.pre_fc_norm_hidden, a full-attention decoder layer under
+    mtp.layers.0. with its MLP (routed experts after the last layer's, manifest "mtp": {"experts": ...}). Its tensors
+    come after every other, so the rest of the pack is the same bytes with or without it."""
     os.makedirs(out_dir, exist_ok=True)
     rng = np.random.default_rng(seed)
     s = shape
@@ -255,11 +259,13 @@ def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quan
     ex_path = os.path.join(out_dir, "experts.bin")
     experts = _Writer(ex_path) if not s.dense else None
     row_b = lambda cols: cols // KBLOCK * 9
-    for l in range(s.n_layers):
-        p = f"layers.{l}."
+
+    def decoder_layer(p, attn):
+        """A decoder layer's tensors under prefix p; its routed experts' table entry (None: dense)."""
+        entry = None
         f32(p + "input_layernorm.weight", rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))
         f32(p + "post_attention_layernorm.weight", rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))
-        if s.layer_types[l] == "full_attention":
+        if attn:
             q4(p + "self_attn.q_proj.weight", s.n_heads * s.head_dim * 2, H)
             q4(p + "self_attn.k_proj.weight", s.n_kv_heads * s.head_dim, H)
             q4(p + "self_attn.v_proj.weight", s.n_kv_heads * s.head_dim, H)
@@ -308,9 +314,22 @@ def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quan
                     experts.off += blk.size
                 scales[e] = (g0, g1)
             f32(p + "mlp.experts.scales", scales)
-            expert_layers.append({"file": "experts.bin", "offset": first, "stride": stride, "format": "q4"})
+            entry = {"file": "experts.bin", "offset": first, "stride": stride, "format": "q4"}
+        return entry
+
+    for l in range(s.n_layers):
+        entry = decoder_layer(f"layers.{l}.", s.layer_types[l] == "full_attention")
+        if entry is not None:
+            expert_layers.append(entry)
+
     f32("norm.weight", rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))
     q4("lm_head.weight", s.vocab, H)
+    mtp_entry = None
+    if mtp:
+        q4("mtp.fc.weight", H, 2 * H)
+        for n_ in ("mtp.norm.weight", "mtp.pre_fc_norm_embedding.weight", "mtp.pre_fc_norm_hidden.weight"):
+            f32(n_, rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))
+        mtp_entry = decoder_layer("mtp.layers.0.", True)
     dense.close()
     files = [{"name": "dense.bin", "size": os.path.getsize(os.path.join(out_dir, "dense.bin"))}]
     if experts is not None:
@@ -331,6 +350,8 @@ def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quan
                     "shared_expert_intermediate_size": s.shared_ff})
     manifest = {"format": "geode-pack", "version": 1, "arch": s.arch, "files": files, "config": cfg,
                 "tensors": tensors, "experts": {"layers": expert_layers}, "formats": {"q4": {"layout": "rows"}}}
+    if mtp:
+        manifest["mtp"] = {"experts": mtp_entry} if mtp_entry is not None else {}
     with open(os.path.join(out_dir, "geode.json"), "w") as f:
         json.dump(manifest, f, indent=1)
     return manifest

@@ -686,6 +686,56 @@ int go_forward(const go_model *m, go_state *s, const int *toks, int n, float *lo
     return 0;
 }
 
+/* Model::forward_mtp (engine/src/model.cpp:4965-5039) on the CPU path: the fc input per position, the layer's
+ * attention over its own KV slot (the main layers' attention, at positions pos..), its MLP (expert layer n_layers),
+ * the logits of the last position after mtp.norm */
+int go_forward_mtp(const go_model *m, const go_mtp *mtp, int8_t *kv, float *kvs, int ctx, const int *next,
+                   const float *hidden, int n, int pos, float *logits, float *out_hidden) {
+    const go_config *c = &m->cfg;
+    const int H = c->hidden;
+    if (n <= 0 || pos < 0 || pos + n > ctx || !mtp || !kv || !kvs) return -1;
+    for (int t = 0; t < n; ++t)
+        if (next[t] < 0 || next[t] >= m->embed.rows) return -1;
+    float *in = (float *)malloc(sizeof(float) * (size_t)n * 2 * H);
+    float *e = (float *)malloc(sizeof(float) * (size_t)H);
+    float *x = (float *)malloc(sizeof(float) * (size_t)n * H);
+    float *h = (float *)malloc(sizeof(float) * (size_t)n * H);
+    float *mix = (float *)malloc(sizeof(float) * (size_t)n * H);
+    float *moe = (float *)malloc(sizeof(float) * (size_t)n * H);
+    /* [norm_e(embedding) | norm_h(hidden)] per position, then fc (5008-5024) */
+    for (int t = 0; t < n; ++t) {
+        float *row = in + (size_t)t * 2 * H;
+        go_dequant_row(&m->embed, next[t], e);
+        go_rmsnorm(e, mtp->pre_e, row, H, c->eps, 1);
+        go_rmsnorm(hidden + (size_t)t * H, mtp->pre_h, row + H, H, c->eps, 1);
+    }
+    matmul(&mtp->fc, n, in, x);
+    const go_layer *L = &mtp->layer;
+    for (int t = 0; t < n; ++t) go_rmsnorm(x + (size_t)t * H, L->in_norm, h + (size_t)t * H, H, c->eps, 1);
+    /* the attention at the MTP layer's positions pos.. over its own KV (apos_ = pos, 5029-5032) */
+    go_state v = {pos, ctx, NULL, NULL, kv, kvs};
+    attn_layer(m, L, 0, &v, n, h, mix);
+    for (int t = 0; t < n; ++t) {
+        float *xr = x + (size_t)t * H;
+        for (int i = 0; i < H; ++i) xr[i] += mix[(size_t)t * H + i];
+        go_rmsnorm(xr, L->post_norm, h + (size_t)t * H, H, c->eps, 1);
+    }
+    mlp_layer(m, L, c->n_layers, n, h, moe, NULL);
+    for (size_t i = 0; i < (size_t)n * H; ++i) x[i] += moe[i];
+    if (logits || out_hidden) {
+        go_rmsnorm(x + (size_t)(n - 1) * H, mtp->norm, h, H, c->eps, 1);
+        if (out_hidden) memcpy(out_hidden, h, sizeof(float) * (size_t)H);
+        if (logits) matmul(&m->lm_head, 1, h, logits);
+    }
+    free(in);
+    free(e);
+    free(x);
+    free(h);
+    free(mix);
+    free(moe);
+    return 0;
+}
+
 /* ---------------------------------------------------------------- sampling ---- */
 
 /* MT19937-64 (Matsumoto & Nishimura 2000; the std::mt19937_64 of the C++ standard, [rand.predef]) */

@@ -84,6 +84,23 @@ typedef struct {
 int go_forward(const go_model *m, go_state *s, const int *toks, int n, float *logits, float *hidden,
                const go_trace *tr);
 
+/* The MTP drafting layer (a pack with one: engine/src/model.cpp:175-191): fc [hidden][2 hidden] over
+ * [norm(embedding of the next token) | norm(hidden state)], then a full-attention decoder layer (mtp.layers.0.) whose
+ * MLP takes the routed experts after the main layers', then mtp.norm. */
+typedef struct {
+    go_layer layer;
+    go_q4 fc;
+    const float *norm, *pre_e, *pre_h;
+} go_mtp;
+
+/* Model::forward_mtp (engine/src/model.cpp:4965-5039): n positions from pos, position t taking hidden row t (the main
+ * model's, after its final norm) and the embedding of next[t]; each attends to the MTP layer's own positions up to it,
+ * whose KV (kv [2][ctx][nkv*hd] int8 K then V, kvs [2][ctx][nkv] f32 scales) it writes. logits [vocab] of the last
+ * position (NULL: none) from lm_head; out_hidden [hidden] (NULL: not wanted): that position's output after mtp.norm.
+ * Returns 0, or -1 on a bad argument. */
+int go_forward_mtp(const go_model *m, const go_mtp *mtp, int8_t *kv, float *kvs, int ctx, const int *next,
+                   const float *hidden, int n, int pos, float *logits, float *out_hidden);
+
 /* ---- the kernels, exposed for kernel-level tests ---- */
 float go_e4m3_value(uint8_t b);
 void go_dequant_row(const go_q4 *w, int64_t r, float *out);

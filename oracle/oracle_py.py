@@ -64,6 +64,10 @@ class GoState(C.Structure):
                 ("kvs", C.c_void_p)]
 
 
+class GoMtp(C.Structure):
+    _fields_ = [("layer", GoLayer), ("fc", GoQ4), ("norm", C.c_void_p), ("pre_e", C.c_void_p), ("pre_h", C.c_void_p)]
+
+
 class GoTrace(C.Structure):
     _fields_ = [(n, C.c_void_p) for n in ("x", "mixer", "moe", "out", "ids", "weights", "gate")]
 
@@ -122,11 +126,15 @@ class OracleState:
         self.gdn = np.zeros(max(1, n_gdn * nv * dk * dv), np.float32)
         self.kv = np.zeros(max(1, n_attn * 2 * ctx * kv_row), np.int8)
         self.kvs = np.zeros(max(1, n_attn * 2 * ctx * c.n_kv_heads), np.float32)
+        # the MTP layer's own KV slot (after the main attention layers' in the engine's cache)
+        self.mtp_kv = np.zeros(2 * ctx * kv_row if ora.has_mtp else 1, np.int8)
+        self.mtp_kvs = np.zeros(2 * ctx * c.n_kv_heads if ora.has_mtp else 1, np.float32)
 
     def copy(self) -> "OracleState":
         s = object.__new__(OracleState)
         s.ctx, s.pos = self.ctx, self.pos
         s.conv, s.gdn, s.kv, s.kvs = self.conv.copy(), self.gdn.copy(), self.kv.copy(), self.kvs.copy()
+        s.mtp_kv, s.mtp_kvs = self.mtp_kv.copy(), self.mtp_kvs.copy()
         return s
 
     def struct(self) -> GoState:
@@ -168,12 +176,11 @@ class Oracle:
             return _ptr(a)
 
         ex = self.pack.manifest["experts"]["layers"]
-        for l in range(p.n_layers):
-            pre = f"layers.{l}."
-            x = L[l]
-            x.attn = 1 if p.attn[l] else 0
+
+        def fill(x, pre, attn, e):
+            x.attn = 1 if attn else 0
             x.in_norm, x.post_norm = arr(pre + "input_layernorm.weight"), arr(pre + "post_attention_layernorm.weight")
-            if p.attn[l]:
+            if attn:
                 x.q, x.k, x.v, x.o = (q4(pre + "self_attn." + n + "_proj.weight") for n in "qkvo")
                 x.q_norm, x.k_norm = arr(pre + "self_attn.q_norm.weight"), arr(pre + "self_attn.k_norm.weight")
             else:
@@ -189,11 +196,25 @@ class Oracle:
                 x.sh_gate, x.sh_up, x.sh_down = (q4(pre + f"mlp.shared_expert.{n}_proj.weight")
                                                  for n in ("gate", "up", "down"))
                 x.router, x.shared_gate = arr(pre + "mlp.gate.weight"), arr(pre + "mlp.shared_expert_gate.weight")
-                e = ex[l]
                 buf = p.files[e["file"]]
                 x.experts = _ptr(buf) + e["offset"]
                 x.expert_stride = e["stride"]
                 x.expert_scales = arr(pre + "mlp.experts.scales")
+
+        for l in range(p.n_layers):
+            fill(L[l], f"layers.{l}.", p.attn[l], ex[l] if l < len(ex) else None)
+        # the MTP drafting layer, when the pack has one (engine/src/model.cpp:175-191, engine/src/pack.cpp:300-305)
+        self.has_mtp = "mtp" in p.manifest
+        self.mtp = None
+        if self.has_mtp:
+            self.mtp = GoMtp()
+            fill(self.mtp.layer, "mtp.layers.0.", True, p.manifest["mtp"].get("experts"))
+            self.mtp.fc = q4("mtp.fc.weight")
+            self.mtp.norm, self.mtp.pre_e = arr("mtp.norm.weight"), arr("mtp.pre_fc_norm_embedding.weight")
+            self.mtp.pre_h = arr("mtp.pre_fc_norm_hidden.weight")
+            self.lib.go_forward_mtp.restype = C.c_int
+            self.lib.go_forward_mtp.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                                C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         self._keep = keep
         self._layers = L
         self.model = GoModel(cfg, C.addressof(L), q4("embed_tokens.weight"), q4("lm_head.weight"), arr("norm.weight"))
@@ -202,6 +223,23 @@ class Oracle:
 
     def new_state(self, ctx: int) -> OracleState:
         return OracleState(self, ctx)
+
+    def forward_mtp(self, state: OracleState, next_toks, hidden, pos: int, logits: bool = True):
+        """go_forward_mtp over the state's MTP KV slot (state.mtp_kv / mtp_kvs): position i from pos takes hidden[i]
+        and the embedding of next_toks[i]; the last position's logits and its output after mtp.norm (or None)."""
+        if not self.has_mtp:
+            raise RuntimeError("the pack has no MTP layer")
+        next_toks = np.ascontiguousarray(np.asarray(next_toks, dtype=np.int32))
+        hidden = np.ascontiguousarray(hidden, dtype=np.float32)
+        n = len(next_toks)
+        lg = np.zeros(self.pack.vocab, np.float32) if logits else None
+        mh = np.zeros(self.pack.hidden, np.float32) if logits else None
+        rc = self.lib.go_forward_mtp(C.addressof(self.model), C.addressof(self.mtp), _ptr(state.mtp_kv),
+                                     _ptr(state.mtp_kvs), state.ctx, _ptr(next_toks), _ptr(hidden), n, pos,
+                                     _ptr(lg) if logits else None, _ptr(mh) if logits else None)
+        if rc != 0:
+            raise RuntimeError("oracle forward_mtp failed")
+        return lg, mh
 
     def forward(self, state: OracleState, toks, logits: bool = True, hidden: bool = False, trace: bool = False):
         toks = np.ascontiguousarray(np.asarray(toks, dtype=np.int32))
@@ -309,14 +347,18 @@ def oracle_route_topk(lib, logits: np.ndarray, K: int):
 class Reference:
     """The reference engine's geode::Model over a pack (oracle/_ref/libgeode_ref.so)."""
 
-    def __init__(self, pack_dir: str, threads: int = 1, ctx: int = 8192, attn_block: Optional[int] = None):
+    def __init__(self, pack_dir: str, threads: int = 1, ctx: int = 8192, attn_block: Optional[int] = None,
+                 draft: bool = False):
         if not have_reference():
             raise RuntimeError("the reference build oracle/_ref/libgeode_ref.so is missing")
         if attn_block is not None:
             os.environ["GEODE_ATTN_BLOCK"] = str(attn_block)
         self.lib = lib = C.CDLL(REF_SO)
-        lib.ref_open.restype = C.c_void_p
-        lib.ref_open.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        lib.ref_open2.restype = C.c_void_p
+        lib.ref_open2.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int]
+        lib.ref_hidden.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        lib.ref_mtp.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                C.c_char_p, C.c_int]
         lib.ref_close.argtypes = [C.c_void_p]
         lib.ref_forward.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_char_p, C.c_int]
         lib.ref_position.argtypes = [C.c_void_p]
@@ -325,7 +367,7 @@ class Reference:
         lib.ref_trace.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int]
         lib.ref_trace_get.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
         err = C.create_string_buffer(512)
-        self.h = lib.ref_open(pack_dir.encode(), threads, ctx, err, 512)
+        self.h = lib.ref_open2(pack_dir.encode(), threads, ctx, 1 if draft else 0, err, 512)
         if attn_block is not None:
             del os.environ["GEODE_ATTN_BLOCK"]
         if not self.h:
@@ -385,6 +427,28 @@ class Reference:
         self.lib.ref_profile.argtypes = [C.c_void_p, C.c_char_p, C.c_int]
         self.lib.ref_profile(self.h, buf, 8192)
         return buf.value.decode()
+
+    def hidden_rows(self, n: int) -> np.ndarray:
+        """Model::hidden(t) for the last forward_batch's first n tokens (after the final norm; MTP packs only)."""
+        out = np.zeros((n, self.hidden), np.float32)
+        for t in range(n):
+            if self.lib.ref_hidden(self.h, t, out[t].ctypes.data) != 0:
+                raise RuntimeError("the reference keeps no hidden rows (no MTP layer bound)")
+        return out
+
+    def mtp(self, next_toks, hidden, pos: int, logits: bool = True):
+        """Model::forward_mtp: position i from pos takes hidden[i] and the embedding of next_toks[i]; the last
+        position's logits and its normed output (Model::mtp_hidden), or (None, None)."""
+        next_toks = np.ascontiguousarray(np.asarray(next_toks, dtype=np.int32))
+        hidden = np.ascontiguousarray(hidden, dtype=np.float32)
+        n = len(next_toks)
+        lg = np.zeros(self.vocab, np.float32) if logits else None
+        mh = np.zeros(self.hidden, np.float32) if logits else None
+        err = C.create_string_buffer(512)
+        if self.lib.ref_mtp(self.h, next_toks.ctypes.data, hidden.ctypes.data, n, pos,
+                            lg.ctypes.data if logits else None, mh.ctypes.data if logits else None, err, 512) != 0:
+            raise RuntimeError("reference forward_mtp: " + err.value.decode())
+        return lg, mh
 
     def save_state(self, path: str):
         err = C.create_string_buffer(512)

@@ -2,6 +2,7 @@
 // reference checkout by oracle/Makefile into oracle/_ref/), so the Python tests can call it with ctypes:
 //   - the whole verify pass:  geode::Model::open / forward_batch(all_logits) / save_state / load_state
 //     (engine/src/model.hpp:161,166,239-240), with the per-layer trace hook (engine/src/model.hpp:92-105,341);
+//   - the MTP drafting layer: Model::forward_mtp and the hidden rows it takes (engine/src/model.hpp:168-183);
 //   - the kernels the pass is made of (engine/src/kernels.hpp): quantize_activation, matvec_rows_q_ref,
 //     dequant_row, matvec_rows_bf16_multi, rmsnorm, fast_exp; route_topk (engine/src/model.hpp:30);
 //   - the sampler (engine/src/sampler.hpp) and the acceptance rule of the speculation loop, restated around it
@@ -41,7 +42,9 @@ void put_err(const std::string &e, char *err, int len) {
 
 extern "C" {
 
-void *ref_open(const char *dir, int threads, int ctx, char *err, int errlen) {
+// draft: 1 = bind the pack's MTP layer (ModelOptions::no_draft false: forward_mtp works, the state holds the
+// layer's KV), 0 = leave it unread as the verify tests do
+void *ref_open2(const char *dir, int threads, int ctx, int draft, char *err, int errlen) {
     auto *r = new Ref;
     geode::ModelOptions o;
     o.compute_threads = threads;
@@ -49,7 +52,7 @@ void *ref_open(const char *dir, int threads, int ctx, char *err, int errlen) {
     o.memory_budget = 0;
     o.npu = 0;
     o.mode = 1;   // RunMode::Cpu
-    o.no_draft = true, o.no_vision = true, o.no_audio = true;
+    o.no_draft = draft == 0, o.no_vision = true, o.no_audio = true;
     std::string e;
     if (!r->model.open(dir, o, e)) {
         put_err(e, err, errlen);
@@ -61,7 +64,37 @@ void *ref_open(const char *dir, int threads, int ctx, char *err, int errlen) {
     return r;
 }
 
+void *ref_open(const char *dir, int threads, int ctx, char *err, int errlen) {
+    return ref_open2(dir, threads, ctx, 0, err, errlen);
+}
+
 void ref_close(void *h) { delete static_cast<Ref *>(h); }
+
+// Model::hidden(t) (engine/src/model.hpp:181): token t of the last forward_batch after the final norm (kept when the
+// model has an MTP layer), hidden floats into out; -1 when the model keeps none
+int ref_hidden(void *h, int t, float *out) {
+    Ref *r = static_cast<Ref *>(h);
+    if (!r->model.has_mtp()) return -1;
+    std::memcpy(out, r->model.hidden(t), static_cast<size_t>(r->hidden) * 4);
+    return 0;
+}
+
+// Model::forward_mtp (engine/src/model.cpp:4965-5039): n positions from pos, position i taking hidden row i
+// (hidden: n x hidden floats) and the embedding of next[i]; logits: the last position's [vocab] (NULL: none);
+// mtp_hidden (NULL: not wanted): that position's output after the layer's final norm (Model::mtp_hidden)
+int ref_mtp(void *h, const int *next, const float *hidden, int n, int pos, float *logits, float *mtp_hidden, char *err,
+            int errlen) {
+    Ref *r = static_cast<Ref *>(h);
+    std::vector<const float *> rows(static_cast<size_t>(n));
+    for (int t = 0; t < n; ++t) rows[static_cast<size_t>(t)] = hidden + static_cast<size_t>(t) * r->hidden;
+    std::string e;
+    if (!r->model.forward_mtp(next, rows.data(), n, pos, logits, e)) {
+        put_err(e, err, errlen);
+        return -1;
+    }
+    if (logits && mtp_hidden) std::memcpy(mtp_hidden, r->model.mtp_hidden(), static_cast<size_t>(r->hidden) * 4);
+    return 0;
+}
 
 int ref_position(void *h) { return static_cast<Ref *>(h)->model.position(); }
 

@@ -10,9 +10,12 @@ restatement, so tests/test_oracle.py pins the restatement to the reference where
 - model_moe.npz / model_dense.npz: Model::forward_batch over a prompt and a 5-token verify batch on a tiny synthetic
   pack (written by geode_b200/synth.py with the seed stored), every logit and the per-layer trace;
 - state_file.npz: Model::save_state's file (engine/src/state.cpp) after a 20-token prompt on a tiny synthetic pack,
-  with that pack's geode.json (the state's fingerprint hashes it) and the shapes the state records.
+  with that pack's geode.json (the state's fingerprint hashes it) and the shapes the state records;
+- mtp_moe.npz / mtp_dense.npz: the MTP drafting layer (Model::forward_mtp, engine/src/model.cpp:4965-5039) on a tiny
+  pack with one: the main model's hidden rows after a prompt, the MTP pass over the prompt's positions (logits and
+  normed output of the last), then one chained position fed its own draft.
 
-Run with names (kernels, accept, model, state) to regenerate only those fixtures.
+Run with names (kernels, accept, model, state, mtp) to regenerate only those fixtures.
 """
 import ctypes as C
 import os
@@ -145,11 +148,27 @@ def state_file(seed=31):
                         manifest=manifest, state=state)
 
 
+def mtp(arch, name, seed=41):
+    shape = synth.tiny_shape(arch, n_layers=4, ctx=640)
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_pack(d, shape, seed=seed, mtp=True)
+        ref = op.Reference(d, threads=1, ctx=shape.ctx, draft=True)
+        prompt = np.random.default_rng(seed + 1).integers(0, shape.vocab, 40).astype(np.int32)
+        ref.forward(prompt, all_logits=False)
+        hid = ref.hidden_rows(len(prompt))
+        lg1, h1 = ref.mtp(prompt[1:], hid[:-1], 0)
+        draft = int(np.argmax(lg1))
+        lg2, h2 = ref.mtp([draft], h1[None], len(prompt) - 1)
+        ref.close()
+    np.savez_compressed(os.path.join(OUT, name + ".npz"), seed=seed, prompt=prompt, hidden=hid, logits1=lg1,
+                        mtp_hidden1=h1, draft=draft, logits2=lg2, mtp_hidden2=h2)
+
+
 if __name__ == "__main__":
     if not op.have_reference():
         sys.exit("build the reference first: make -C oracle ref")
     R = op.reference_lib()
-    which = set(sys.argv[1:]) or {"kernels", "accept", "model", "state"}
+    which = set(sys.argv[1:]) or {"kernels", "accept", "model", "state", "mtp"}
     if "kernels" in which:
         kernels(R)
     if "accept" in which:
@@ -159,4 +178,7 @@ if __name__ == "__main__":
         model("qwen35", "model_dense")
     if "state" in which:
         state_file()
+    if "mtp" in which:
+        mtp("qwen35moe", "mtp_moe")
+        mtp("qwen35", "mtp_dense")
     print("written to", OUT)
