@@ -270,6 +270,23 @@ bool CudaModel::verify_n(const int *toks, int n, float *logits, std::string &err
     return true;
 }
 
+bool CudaModel::prefill(const int *toks, int n, std::string &err) {
+    if (!g_) {
+        err = "not open";
+        return false;
+    }
+    if (!toks || n < 1) {
+        err = "prefill: no tokens";
+        return false;
+    }
+    for (int i = 0; i < n; i += max_tokens_) {
+        const int k = std::min(max_tokens_, n - i);
+        if (api_.verify(g_, toks + i, k, nullptr, nullptr) != 0) return fail("prefill", err);
+    }
+    last_n_ = 0;   // (nothing to accept or keep: the prompt is all kept)
+    return true;
+}
+
 bool CudaModel::verify_keep(int kept, std::string &err) {
     if (!g_) {
         err = "not open";

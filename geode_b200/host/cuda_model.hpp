@@ -85,6 +85,10 @@ public:
 
     // n tokens at positions pos .. pos+n-1 through every layer; logits [n][vocab] (or NULL); position += n
     bool verify_n(const int *toks, int n, float *logits, std::string &err);
+    // geode_prefill (engine/include/geode/geode.h:166-169): n prompt tokens appended to the conversation, no logits -
+    // through the verify graphs, max_tokens positions a launch (not a tensor-core prefill: the GEMVs' weight stream
+    // is read once per max_tokens tokens)
+    bool prefill(const int *toks, int n, std::string &err);
     // rollback: the states as after the verified batch's row kept-1 (1 <= kept < n); position -= n - kept
     bool verify_keep(int kept, std::string &err);
     // the acceptance of the last verified batch (its rows 1.. are the drafts): kept, next (-1: a stop token stood)

@@ -152,3 +152,32 @@ def test_host_state_file(env, tmp_path):
     open(str(tmp_path / "bad.state"), "wb").write(bad)
     assert H.ghost_state_load(m, str(tmp_path / "bad.state").encode(), C.byref(pos), err, 512) == 3
     assert H.ghost_position(m) == 0 and H.ghost_pending(m) == -1
+
+
+def test_host_prefill(env):
+    """ghost_prefill (geode_prefill's counterpart): a 23-token prompt in through the verify step, then a batch whose
+    logits match the oracle's after the same prompt within the parity tolerance; a token out of range is refused."""
+    H, m, d, shape = env
+    H.ghost_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t]
+    H.ghost_pending.argtypes = [C.c_void_p]
+    err = C.create_string_buffer(512)
+    ora = op.Oracle(d)
+    st = ora.new_state(shape.ctx)
+    rng = np.random.default_rng(21)
+    p0 = H.ghost_position(m)
+    if p0:   # (the conversation the earlier tests left: the oracle replays from empty, so start from empty too)
+        pytest.skip("the shared handle holds a conversation")
+    prompt = rng.integers(0, shape.vocab, 23).astype(np.int32)
+    assert H.ghost_prefill(m, prompt.ctypes.data_as(C.c_void_p), 23, err, 512) == 0, err.value
+    assert H.ghost_position(m) == 23 and H.ghost_pending(m) == -1
+    ora.forward(st, prompt, logits=False)
+    toks = rng.integers(0, shape.vocab, 5).astype(np.int32)
+    lg = np.zeros((5, shape.vocab), np.float32)
+    assert H.ghost_verify(m, toks.ctypes.data_as(C.c_void_p), 5, lg.ctypes.data_as(C.c_void_p), err, 512) == 0, err.value
+    want = ora.forward(st, toks)["logits"]
+    span = want.max(1) - want.min(1)
+    assert np.all(np.abs(lg - want).max(1) <= 1e-2 * span)
+    bad = prompt[:3].copy()
+    bad[1] = shape.vocab
+    assert H.ghost_prefill(m, bad.ctypes.data_as(C.c_void_p), 3, err, 512) == 1
+    assert H.ghost_position(m) == 28
