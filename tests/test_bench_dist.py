@@ -75,7 +75,7 @@ def test_step_bytes_match_the_hand_computed_figures():
     assert q4(2 * s3.moe_ff, s3.hidden) + q4(s3.hidden, s3.moe_ff) == 1769472
     assert q4(s3.vocab, s3.hidden) == 286064640
     b3 = bench.step_bytes(s3, 37.6, 8192)
-    assert abs(b3["experts"] - 37.6 * 40 * 1769472) < 2
+    assert abs(b3["experts"] - 37.6 * 40 * 1769472) <= 40   # (rounded to a byte per layer)
     assert abs(b3["total"] / 3.82e9 - 1) < 0.005 and abs(b3["dense"] / 925e6 - 1) < 0.002
     assert abs(b3["kv"] / 170e6 - 1) < 0.01 and abs(b3["state"] / 67e6 - 1) < 0.01
     b2 = bench.step_bytes(synth.baseline_shape(2), 0, 4096)
