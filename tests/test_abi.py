@@ -44,3 +44,27 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(geode_b200, "_cuda", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         geode_b200.cuda_lib()
+
+
+def test_no_gpu_fails_loudly(tmp_path):
+    """Where there is no GPU, the backend and the host side refuse with an error and a message - no CPU fallback:
+    gcuda_open returns NULL with the CUDA error, ghost_open GHOST_E_BACKEND (7) with it and no model."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is here")
+    from geode_b200 import synth
+    L = C.CDLL(LIBS["geode_cuda.h"])
+    L.gcuda_open.restype = C.c_void_p
+    L.gcuda_open.argtypes = [C.c_int, C.c_char_p, C.c_int]
+    err = C.create_string_buffer(512)
+    assert not L.gcuda_open(0, err, 512)
+    assert err.value
+    H = C.CDLL(LIBS["geode_host.h"])
+    H.ghost_open.argtypes = [C.c_char_p, C.c_int32, C.c_int32, C.c_int32, C.POINTER(C.c_void_p), C.c_char_p,
+                             C.c_size_t]
+    d = str(tmp_path / "pack")
+    synth.write_pack(d, synth.tiny_shape("qwen35moe", n_layers=2, ctx=64), seed=1)
+    m = C.c_void_p(1)
+    err = C.create_string_buffer(512)
+    assert H.ghost_open(d.encode(), 0, 64, 5, C.byref(m), err, 512) == 7
+    assert not m.value and b"gcuda_open" in err.value
