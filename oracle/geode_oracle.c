@@ -13,6 +13,7 @@
 #include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #define KBLOCK 16
 
@@ -311,13 +312,59 @@ static void qact_free(qact a) {
     free(a.s);
 }
 
+/* Large products split by rows over threads (GEODE_ORACLE_THREADS, default the host's cores, at most 32): every row's
+ * arithmetic is the same whichever thread runs it, so the results are the single-threaded ones bit for bit. */
+typedef struct {
+    const go_q4 *w;
+    const int8_t *q;
+    const float *s;
+    float *y;
+    int64_t r0, r1;
+} mv_job;
+
+static void *mv_run(void *p) {
+    const mv_job *j = (const mv_job *)p;
+    go_matvec_q(j->w, j->q, j->s, j->y, j->r0, j->r1);
+    return NULL;
+}
+
+static int g_threads;
+static pthread_once_t g_threads_once = PTHREAD_ONCE_INIT;
+static void threads_init(void) {
+    const char *e = getenv("GEODE_ORACLE_THREADS");
+    long c = e ? atol(e) : sysconf(_SC_NPROCESSORS_ONLN);
+    g_threads = c < 1 ? 1 : c > 32 ? 32 : (int)c;
+}
+
+static void matvec_rows(const go_q4 *w, const int8_t *q, const float *s, float *y) {
+    pthread_once(&g_e4_once, e4m3_init);
+    pthread_once(&g_threads_once, threads_init);
+    const int T = g_threads;
+    if (T <= 1 || w->rows * w->cols < ((int64_t)1 << 22)) {
+        go_matvec_q(w, q, s, y, 0, w->rows);
+        return;
+    }
+    pthread_t th[32];
+    mv_job jb[32];
+    int started[32] = {0};
+    const int64_t chunk = (w->rows + T - 1) / T;
+    for (int i = 0; i < T; ++i) {
+        const int64_t r0 = (int64_t)i * chunk, r1 = r0 + chunk < w->rows ? r0 + chunk : w->rows;
+        jb[i] = (mv_job){w, q, s, y, r0 < w->rows ? r0 : w->rows, r1};
+        started[i] = jb[i].r0 < jb[i].r1 && pthread_create(&th[i], NULL, mv_run, &jb[i]) == 0;
+        if (!started[i] && jb[i].r0 < jb[i].r1) mv_run(&jb[i]);   /* (no thread: this one does the rows) */
+    }
+    for (int i = 0; i < T; ++i)
+        if (started[i]) pthread_join(th[i], NULL);
+}
+
 /* Model::matmul's int8 path (engine/src/model.cpp:3388-3397, 3422-3424): each token's activation quantized, then
  * matvec_rows_q over every row. xs [n][cols], ys [n][rows] */
 static void matmul(const go_q4 *w, int n, const float *xs, float *ys) {
     qact a = qact_new(w->cols);
     for (int t = 0; t < n; ++t) {
         go_quantize_activation(xs + (size_t)t * w->cols, w->cols, a.q, a.s, NULL);
-        go_matvec_q(w, a.q, a.s, ys + (size_t)t * w->rows, 0, w->rows);
+        matvec_rows(w, a.q, a.s, ys + (size_t)t * w->rows);
     }
     qact_free(a);
 }
