@@ -1,0 +1,55 @@
+"""The oracle against the reference engine at two benchmark configurations' own model shapes (where the reference build
+is here): cfg 1 (one attention layer, hidden 2048, FFN 6144, vocab 32768, 1024 random KV positions) and cfg 2 (the
+24-layer dense hybrid, vocab 248320, 4096 random KV positions and random recurrent / conv states). The starting state
+goes into the reference through its own state file (written here by ghost_state_write, which the state-file tests pin
+to the reference's save_state) and into the oracle directly; then 5 tokens through both: every logit equal."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from geode_b200 import synth
+import oracle_py as op
+from test_configs_gpu import _compact_kv, _random_state
+from test_state_file import HOST_SO, Shapes
+
+pytestmark = pytest.mark.skipif(not op.have_reference(), reason="the reference build oracle/_ref is not here")
+
+
+@pytest.mark.parametrize("cfg", [1, 2])
+def test_oracle_equals_reference_at_config_shape(cfg, tmp_path):
+    shape = synth.baseline_shape(cfg)
+    d = str(tmp_path / "pack")
+    synth.write_pack(d, shape, seed=60 + cfg, fill="random")
+    ora = op.Oracle(d)
+    ctx = shape.ctx + 16
+    st = ora.new_state(ctx)
+    rng = np.random.default_rng(70 + cfg)
+    _random_state(ora, st, shape.ctx - 8, rng)
+    c = ora.cfg
+    conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+    s = Shapes(ora.n_attn, c.n_kv_heads, c.n_kv_heads * c.head_dim, c.hidden, c.n_layers,
+               ora.n_gdn * conv_dim * max(0, c.conv_kernel - 1), ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim)
+    H = C.CDLL(HOST_SO)
+    H.ghost_state_fingerprint.restype = C.c_uint64
+    H.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
+    H.ghost_state_write.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.c_int32, C.c_uint64,
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t]
+    kv, kvs = _compact_kv(ora, st)
+    kv, kvs = np.ascontiguousarray(kv), np.ascontiguousarray(kvs)
+    path = str(tmp_path / "start.state")
+    err = C.create_string_buffer(256)
+    fp = H.ghost_state_fingerprint(d.encode(), C.byref(s))
+    assert H.ghost_state_write(path.encode(), fp, C.byref(s), st.pos, 0, 1, st.conv.ctypes.data, st.gdn.ctypes.data,
+                               kv.ctypes.data, kvs.ctypes.data, 0, err, 256) == 0, err.value
+    toks = rng.integers(0, shape.vocab, 5).astype(np.int32)
+    ref = op.Reference(d, threads=os.cpu_count() or 1, ctx=ctx)
+    try:
+        ref.load_state(path)
+        assert ref.pos == shape.ctx - 8
+        want = ref.forward(toks, all_logits=True)["logits"]
+    finally:
+        ref.close()
+    got = ora.forward(st, toks, logits=True)["logits"]
+    assert np.array_equal(got, want)
