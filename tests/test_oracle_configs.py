@@ -1,6 +1,8 @@
-"""The oracle against the reference engine at two benchmark configurations' own model shapes (where the reference build
-is here): cfg 1 (one attention layer, hidden 2048, FFN 6144, vocab 32768, 1024 random KV positions) and cfg 2 (the
-24-layer dense hybrid, vocab 248320, 4096 random KV positions and random recurrent / conv states). The starting state
+"""The oracle against the reference engine at the benchmark configurations' own model shapes (where the reference build
+is here): cfg 1 (one attention layer, hidden 2048, FFN 6144, vocab 32768, 1024 random KV positions), cfg 2 (the
+24-layer dense hybrid, vocab 248320, 4096 random KV positions and random recurrent / conv states) and cfg 3 at full
+width on 4 of its 40 layers (3 Gated DeltaNet : 1 attention, 256 experts top-8 with ff 512 and the shared expert,
+vocab 248320, 8192 random KV positions - the whole model's pack is 20 GB). The starting state
 goes into the reference through its own state file (written here by ghost_state_write, which the state-file tests pin
 to the reference's save_state) and into the oracle directly; then 5 tokens through both: every logit equal."""
 import ctypes as C
@@ -17,9 +19,12 @@ from test_state_file import HOST_SO, Shapes
 pytestmark = pytest.mark.skipif(not op.have_reference(), reason="the reference build oracle/_ref is not here")
 
 
-@pytest.mark.parametrize("cfg", [1, 2])
+@pytest.mark.parametrize("cfg", [1, 2, 3])
 def test_oracle_equals_reference_at_config_shape(cfg, tmp_path):
     shape = synth.baseline_shape(cfg)
+    if cfg == 3:
+        shape.n_layers = 4
+        shape.layer_types = synth.hybrid_types(4)
     d = str(tmp_path / "pack")
     synth.write_pack(d, shape, seed=60 + cfg, fill="random")
     ora = op.Oracle(d)
