@@ -28,6 +28,7 @@ torch = pytest.importorskip("torch")
 
 from geode_b200 import synth  # noqa: E402
 import oracle_py as op  # noqa: E402
+from state_helpers import compact_kv as _compact_kv, random_state as _random_state  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -55,31 +56,6 @@ def _check(ora, st_before, toks, got, ref, what):
     drift = np.abs(ora.forward(s2, toks, logits=True)["logits"] - ref).max(axis=-1)
     bound = np.maximum(TOL * rr, DRIFT_FACTOR * drift)
     assert np.all(err <= bound), f"{what}: max|d| {err} vs range {rr}, the oracle's own drift {drift}"
-
-
-def _compact_kv(ora, st):
-    c = ora.cfg
-    A = max(1, ora.n_attn)
-    row = c.n_kv_heads * c.head_dim
-    kv = st.kv.reshape(A, 2, st.ctx, row)[:, :, :st.pos].copy()
-    kvs = st.kvs.reshape(A, 2, st.ctx, c.n_kv_heads)[:, :, :st.pos].copy()
-    return kv, kvs
-
-
-def _random_state(ora, st, positions, rng):
-    """positions of random int8 KV rows (scales U(0.005, 0.02)), random conv and recurrent states."""
-    c = ora.cfg
-    A = max(1, ora.n_attn)
-    row = c.n_kv_heads * c.head_dim
-    kv = st.kv.reshape(A, 2, st.ctx, row)
-    kvs = st.kvs.reshape(A, 2, st.ctx, c.n_kv_heads)
-    if ora.n_attn:
-        kv[:, :, :positions] = rng.integers(-127, 128, kv[:, :, :positions].shape, dtype=np.int8)
-        kvs[:, :, :positions] = rng.uniform(0.005, 0.02, kvs[:, :, :positions].shape).astype(np.float32)
-    if ora.n_gdn:
-        st.conv[:] = (rng.standard_normal(st.conv.shape) * 0.3).astype(np.float32)
-        st.gdn[:] = (rng.standard_normal(st.gdn.shape) * 0.02).astype(np.float32)
-    st.pos = positions
 
 
 @pytest.fixture(scope="module", params=[1, 2])

@@ -15,6 +15,7 @@ torch = pytest.importorskip("torch")
 
 from geode_b200 import synth  # noqa: E402
 import oracle_py as op  # noqa: E402
+from state_helpers import compact_kv as _compact_kv  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -55,18 +56,6 @@ def setup(request, tmp_path_factory):
     be.state_put(st.conv, st.gdn, kv, kvs, st.pos)
     yield shape, ora, be, st, rng
     be.close()
-
-
-def _compact_kv(ora, st):
-    """The oracle's KV arrays ([layer][K|V][ctx][row]) cut to the positions held, as the state bridge takes them."""
-    c = ora.cfg
-    A = max(1, ora.n_attn)
-    row = c.n_kv_heads * c.head_dim
-    if ora.n_attn == 0:
-        return np.zeros((1, 2, st.pos, row), np.int8), np.zeros((1, 2, st.pos, c.n_kv_heads), np.float32)
-    kv = st.kv.reshape(A, 2, st.ctx, row)[:, :, :st.pos].copy()
-    kvs = st.kvs.reshape(A, 2, st.ctx, c.n_kv_heads)[:, :, :st.pos].copy()
-    return kv, kvs
 
 
 def _close(got, ref):

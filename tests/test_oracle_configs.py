@@ -13,7 +13,7 @@ import pytest
 
 from geode_b200 import synth
 import oracle_py as op
-from test_configs_gpu import _compact_kv, _random_state
+from state_helpers import compact_kv as _compact_kv, random_state as _random_state
 from test_state_file import HOST_SO, Shapes
 
 pytestmark = pytest.mark.skipif(not op.have_reference(), reason="the reference build oracle/_ref is not here")
