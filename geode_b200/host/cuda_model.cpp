@@ -270,6 +270,17 @@ bool CudaModel::verify_n(const int *toks, int n, float *logits, std::string &err
     return true;
 }
 
+bool CudaModel::reset(std::string &err) {
+    if (!g_) {
+        err = "not open";
+        return false;
+    }
+    if (api_.reset(g_) != 0) return fail("reset", err);
+    conv_id_ = new_conversation_id(this);
+    last_n_ = 0;
+    return true;
+}
+
 bool CudaModel::prefill(const int *toks, int n, std::string &err) {
     if (!g_) {
         err = "not open";

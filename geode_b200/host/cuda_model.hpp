@@ -85,6 +85,8 @@ public:
 
     // n tokens at positions pos .. pos+n-1 through every layer; logits [n][vocab] (or NULL); position += n
     bool verify_n(const int *toks, int n, float *logits, std::string &err);
+    // Model::reset / geode_reset: the conversation empty (position 0, zero states), a new conversation id
+    bool reset(std::string &err);
     // geode_prefill (engine/include/geode/geode.h:166-169): n prompt tokens appended to the conversation, no logits -
     // through the verify graphs, max_tokens positions a launch (not a tensor-core prefill: the GEMVs' weight stream
     // is read once per max_tokens tokens)

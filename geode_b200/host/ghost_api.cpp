@@ -61,6 +61,17 @@ int ghost_verify(ghost_model *m, const int32_t *toks, int32_t n, float *logits, 
     return GHOST_OK;
 }
 
+int ghost_reset(ghost_model *m, char *err, size_t err_len) {
+    if (!m) return GHOST_E_ARG;
+    std::string e;
+    if (!m->model.reset(e)) {
+        put(e, err, err_len);
+        return GHOST_E_BACKEND;
+    }
+    m->pending = -1;
+    return GHOST_OK;
+}
+
 int ghost_prefill(ghost_model *m, const int32_t *prompt, int32_t n, char *err, size_t err_len) {
     if (!m || !prompt || n < 1) {
         put("ghost_prefill: bad arguments", err, err_len);

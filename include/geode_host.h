@@ -46,6 +46,9 @@ int32_t ghost_spec_tokens(ghost_model *m);
 int32_t ghost_position(ghost_model *m);
 /* Model::verify_n: n tokens through every layer at the next positions; logits [n][vocab] (NULL: not wanted) */
 int ghost_verify(ghost_model *m, const int32_t *toks, int32_t n, float *logits, char *err, size_t err_len);
+/* geode_reset (engine/include/geode/geode.h:216): the conversation empty - position 0, zero states, no pending token, a
+ * new conversation (an append of a later save goes to a new file). */
+int ghost_reset(ghost_model *m, char *err, size_t err_len);
 /* geode_prefill (engine/include/geode/geode.h:166-169): the prompt's n tokens appended to the conversation, nothing
  * generated. It runs through the verify step, max_tokens positions a launch (correct at any length; not a tensor-core
  * prefill). A token id out of range or a prompt past the context: GHOST_E_ARG, the conversation then holds the

@@ -181,3 +181,10 @@ def test_host_prefill(env):
     bad[1] = shape.vocab
     assert H.ghost_prefill(m, bad.ctypes.data_as(C.c_void_p), 3, err, 512) == 1
     assert H.ghost_position(m) == 28
+    # ghost_reset: the conversation empty; the same prompt again gives the same next batch
+    H.ghost_reset.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+    assert H.ghost_reset(m, err, 512) == 0 and H.ghost_position(m) == 0 and H.ghost_pending(m) == -1
+    assert H.ghost_prefill(m, prompt.ctypes.data_as(C.c_void_p), 23, err, 512) == 0, err.value
+    lg2 = np.zeros_like(lg)
+    assert H.ghost_verify(m, toks.ctypes.data_as(C.c_void_p), 5, lg2.ctypes.data_as(C.c_void_p), err, 512) == 0
+    assert np.array_equal(lg2, lg)
