@@ -4,7 +4,8 @@ is here): cfg 1 (one attention layer, hidden 2048, FFN 6144, vocab 32768, 1024 r
 width on 4 of its 40 layers (3 Gated DeltaNet : 1 attention, 256 experts top-8 with ff 512 and the shared expert,
 vocab 248320, 8192 random KV positions - the whole model's pack is 20 GB). The starting state
 goes into the reference through its own state file (written here by ghost_state_write, which the state-file tests pin
-to the reference's save_state) and into the oracle directly; then 5 tokens through both: every logit equal."""
+to the reference's save_state) and into the oracle directly; then 5 tokens through both: every logit equal. And the
+acceptance rule at the full vocabulary, greedy and sampled."""
 import ctypes as C
 import os
 
@@ -58,3 +59,29 @@ def test_oracle_equals_reference_at_config_shape(cfg, tmp_path):
         ref.close()
     got = ora.forward(st, toks, logits=True)["logits"]
     assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("temperature,top_p,top_k", [(0.0, 1.0, 0), (0.7, 0.95, 20), (1.0, 1.0, 0)])
+def test_accept_rule_full_vocab(temperature, top_p, top_k):
+    """The acceptance rule (engine/src/geode.cpp:327-350 around geode::Sampler) at the full vocabulary, 248320: the
+    oracle's kept count, next token and every row's sample equal the reference's, greedy and sampled, on rows of
+    N(0, 3) logits whose drafts are planted (each row's greedy sample, then a wrong one) so that drafts stand and fall."""
+    V = 248320
+    rng = np.random.default_rng(int(temperature * 10) + top_k)
+    R, O = op.reference_lib(), op.oracle_lib()
+    for case in range(4):
+        rows = (rng.standard_normal((5, V), dtype=np.float32) * 3).astype(np.float32)
+        batch = np.zeros(5, np.int32)
+        batch[0] = rng.integers(0, V)
+        stand = case % 5
+        for i in range(4):
+            batch[i + 1] = int(np.argmax(rows[i])) if i < stand else int(rng.integers(0, V))
+        seed = int(rng.integers(0, 2 ** 31))
+        out = []
+        for lib, fn in ((R, "ref_accept"), (O, "go_accept")):
+            nxt = C.c_int(0)
+            samples = np.zeros(5, np.int32)
+            kept = getattr(lib, fn)(rows.ctypes.data, 5, V, batch.ctypes.data, temperature, top_p, top_k,
+                                    C.c_uint64(seed), None, 0, C.byref(nxt), samples.ctypes.data)
+            out.append((kept, nxt.value, samples.tolist()))
+        assert out[0] == out[1], (case, out)
