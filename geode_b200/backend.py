@@ -29,7 +29,7 @@ class GLayer(C.Structure):
 
 
 class GSampling(C.Structure):
-    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int)]
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int), ("presence_penalty", C.c_float)]
 
 
 def _sig(L):
@@ -48,7 +48,8 @@ def _sig(L):
         "gcuda_keep": (i32, [vp, i32]),
         "gcuda_position": (i32, [vp]),
         "gcuda_reset": (i32, [vp]),
-        "gcuda_accept": (i32, [vp, vp, vp, vp, i32, vp, vp, vp]),  # g, sampling, uniforms, stops, n_stops, kept, next, samples
+        # g, sampling, uniforms, stops, n_stops, seen, n_seen, kept, next, samples
+        "gcuda_accept": (i32, [vp, vp, vp, vp, i32, vp, i32, vp, vp, vp]),
         "gcuda_spec_reject": (i32, [vp, vp, vp, vp, i32, i32, i32, vp, C.c_uint64, vp, vp]),
         "gcuda_state_get": (i32, [vp, vp, vp, vp, vp, i32]),
         "gcuda_state_put": (i32, [vp, vp, vp, vp, vp, i32]),
@@ -239,16 +240,19 @@ class Backend:
     def state_get(self, conv, gdn, kv, kvs, positions: int):
         self._rc(self.L.gcuda_state_get(self.g, _ptr(conv), _ptr(gdn), _ptr(kv), _ptr(kvs), positions), "state_get")
 
-    def accept(self, temperature=0.0, top_p=1.0, top_k=0, uniforms=None, stops=()):
-        """The acceptance of the last verified batch (its own tokens are the drafts): (kept, next, samples)."""
+    def accept(self, temperature=0.0, top_p=1.0, top_k=0, uniforms=None, stops=(), presence_penalty=0.0, seen=()):
+        """The acceptance of the last verified batch (its own tokens are the drafts): (kept, next, samples). With a
+        presence penalty, seen lists the answer's sampled tokens so far (distinct); the device logits are penalised in
+        place."""
         n = self._last_n
         u = np.ascontiguousarray(np.zeros(n) if uniforms is None else np.asarray(uniforms, dtype=np.float64))
         st = np.ascontiguousarray(np.asarray(list(stops) or [0], dtype=np.int32))
+        sn = np.ascontiguousarray(np.asarray(list(seen) or [0], dtype=np.int32))
         kept, nxt = C.c_int(0), C.c_int(0)
         samples = np.zeros(n, np.int32)
-        sp = GSampling(temperature, top_p, top_k)
-        self._rc(self.L.gcuda_accept(self.g, C.addressof(sp), _ptr(u), _ptr(st), len(stops), C.byref(kept),
-                                     C.byref(nxt), _ptr(samples)), "accept")
+        sp = GSampling(temperature, top_p, top_k, presence_penalty)
+        self._rc(self.L.gcuda_accept(self.g, C.addressof(sp), _ptr(u), _ptr(st), len(stops), _ptr(sn), len(seen),
+                                     C.byref(kept), C.byref(nxt), _ptr(samples)), "accept")
         return kept.value, nxt.value, samples
 
     def randomize_state(self, pos: int, seed: int = 1):

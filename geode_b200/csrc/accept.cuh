@@ -324,6 +324,32 @@ __global__ void k_argmax_finish(unsigned long long *best, int n, int *out) {
     best[r] = 0;
 }
 
+// The presence penalty of geode_generate (engine/src/geode.cpp:234-255) on the rows of one verified batch, in place:
+// row i loses `penalty` (one f32 subtraction, as the engine's lg[t] -= penalty) at every token the answer sampled
+// before row i - the caller's list (distinct ids) and, for i >= 1, the drafts toks[1..i] that are new to it (bit j of
+// fresh: toks[j] is neither in the list nor an earlier draft). Those drafts are rows 0..i-1's samples whenever row
+// i's sample is used (each of those rows' draft stood), so every row is penalised independently and in parallel.
+// Each id is written by one thread. Grid: (slices of the list, rows).
+struct PresenceArgs {
+    float *logits;   // [n][V]
+    int V, n;
+    float penalty;
+    const int *seen;   // [n_seen] distinct ids in [0, V)
+    int n_seen;
+    int toks[kMaxTok];
+    unsigned fresh;
+};
+__global__ void k_presence(PresenceArgs a) {
+    float *row = a.logits + static_cast<size_t>(blockIdx.y) * a.V;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n_seen; i += gridDim.x * blockDim.x) {
+        const int t = a.seen[i];
+        row[t] = __fsub_rn(row[t], a.penalty);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+        for (int j = 1; j <= static_cast<int>(blockIdx.y); ++j)
+            if ((a.fresh >> j) & 1u) row[a.toks[j]] = __fsub_rn(row[a.toks[j]], a.penalty);
+}
+
 struct SampleArgs {
     const float *logits;   // [n][V]
     int V, n;

@@ -137,6 +137,9 @@ struct gcuda {
     int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
     size_t rej_cap = 0;
     int *d_rej_step = nullptr;      // gcuda_step_device_reject's result: accepted, next
+    int *d_seen = nullptr;          // gcuda_accept's presence-penalty list on the device (grown on demand)
+    size_t seen_cap = 0;
+    std::vector<uint8_t> seen_mark; // (a host bitmap over the vocabulary, all zero between calls)
     uint64_t reject_steps = 0;      // (its Philox sequence index: one per step)
     std::vector<void *> allocs;
     // expert parallelism (gcuda_set_ep): this rank's experts are e % ep_world == ep_rank; the expert outputs meet
@@ -601,6 +604,7 @@ void gcuda_close(gcuda *g) {
     }
     for (void *p : g->allocs) cudaFree(p);
     if (g->rej) cudaFree(g->rej);
+    if (g->d_seen) cudaFree(g->d_seen);
     if (g->ev0) cudaEventDestroy(g->ev0);
     if (g->ev1) cudaEventDestroy(g->ev1);
     if (g->comm) nccl().comm_destroy(g->comm);
@@ -944,6 +948,7 @@ int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, con
     const size_t need = static_cast<size_t>(S) * (k + 2);
     if (need > g->rej_cap) {
         if (g->rej) cudaFree(g->rej);
+    if (g->d_seen) cudaFree(g->d_seen);
         g->rej = nullptr;
         g->rej_cap = 0;
         if (cudaMalloc(&g->rej, need * sizeof(int)) != cudaSuccess) return fail(g, GCUDA_E_MEMORY, "spec_reject: cudaMalloc");
@@ -970,17 +975,59 @@ int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, con
     return GCUDA_OK;
 }
 
-int gcuda_accept(gcuda *g, const gcuda_sampling *sp, const double *uniforms, const int *stops, int n_stops, int *kept,
-                 int *next, int *samples) {
+int gcuda_accept(gcuda *g, const gcuda_sampling *sp, const double *uniforms, const int *stops, int n_stops,
+                 const int *seen, int n_seen, int *kept, int *next, int *samples) {
     if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "accept before setup");
     if (!sp || !kept || !next || g->last_batch < 1) return fail(g, GCUDA_E_STATE, "accept without a verified batch");
     cudaSetDevice(g->device);
     const int n = g->last_batch;
     const bool greedy = sp->temperature <= 0.0f;
-    if (!greedy) {
-        if (!uniforms) return fail(g, GCUDA_E_ARG, "accept: sampling needs the uniforms");
-        LAUNCH_OK(cudaMemcpyAsync(g->d_u, uniforms, sizeof(double) * n, cudaMemcpyHostToDevice, g->st));
+    if (!greedy && !uniforms) return fail(g, GCUDA_E_ARG, "accept: sampling needs the uniforms");
+    if (sp->presence_penalty != 0.0f) {
+        // engine/src/geode.cpp:234-255: the list holds each sampled id once; the drafts new to it are marked fresh
+        const int V = g->sh.vocab;
+        if (n_seen < 0 || (n_seen > 0 && !seen)) return fail(g, GCUDA_E_ARG, "accept: a bad seen list");
+        g->seen_mark.resize(static_cast<size_t>(V), 0);
+        PresenceArgs pa{};
+        bool ok = true;
+        for (int i = 0; i < n_seen && ok; ++i) {
+            const int t = seen[i];
+            ok = t >= 0 && t < V && !g->seen_mark[static_cast<size_t>(t)];
+            if (ok) g->seen_mark[static_cast<size_t>(t)] = 1;
+        }
+        for (int j = 1; j < n && ok; ++j) {
+            const int t = g->last_toks[j];
+            pa.toks[j] = t;
+            if (!g->seen_mark[static_cast<size_t>(t)]) {
+                g->seen_mark[static_cast<size_t>(t)] = 1;
+                pa.fresh |= 1u << j;
+            }
+        }
+        for (int i = 0; i < n_seen; ++i)   // (the marks back to zero, as far as they were set)
+            if (seen[i] >= 0 && seen[i] < V) g->seen_mark[static_cast<size_t>(seen[i])] = 0;
+        for (int j = 1; j < n; ++j) g->seen_mark[static_cast<size_t>(g->last_toks[j])] = 0;
+        if (!ok) return fail(g, GCUDA_E_ARG, "accept: the seen list holds an id twice or one outside the vocabulary");
+        if (static_cast<size_t>(n_seen) > g->seen_cap) {
+            LAUNCH_OK(cudaStreamSynchronize(g->st));
+            if (g->d_seen) cudaFree(g->d_seen);
+            g->d_seen = nullptr;
+            g->seen_cap = 0;
+            const size_t cap = std::max<size_t>(1024, static_cast<size_t>(n_seen));
+            if (cudaMalloc(&g->d_seen, cap * sizeof(int)) != cudaSuccess) return fail(g, GCUDA_E_MEMORY, "accept: cudaMalloc");
+            g->seen_cap = cap;
+        }
+        if (n_seen > 0)
+            LAUNCH_OK(cudaMemcpyAsync(g->d_seen, seen, sizeof(int) * n_seen, cudaMemcpyHostToDevice, g->st));
+        pa.logits = g->logits;
+        pa.V = V;
+        pa.n = n;
+        pa.penalty = sp->presence_penalty;
+        pa.seen = g->d_seen;
+        pa.n_seen = n_seen;
+        const int slices = std::max(1, std::min(64, (n_seen + 255) / 256));
+        LAUNCH_OK(launch_ex(k_presence, dim3(slices, n), dim3(256), 0, g->st, false, pa));
     }
+    if (!greedy) LAUNCH_OK(cudaMemcpyAsync(g->d_u, uniforms, sizeof(double) * n, cudaMemcpyHostToDevice, g->st));
     SampleArgs a{};
     a.logits = g->logits;
     a.V = g->sh.vocab;
@@ -1046,6 +1093,7 @@ int gcuda_reset(gcuda *g) {
     LAUNCH_OK(cudaStreamSynchronize(g->st));
     g->pos = 0;
     g->last_batch = 0;
+    g->reject_steps = 0;   // the device-side rejection sampler's Philox sequence starts over with the conversation
     return GCUDA_OK;
 }
 

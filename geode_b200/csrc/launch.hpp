@@ -1,5 +1,8 @@
 // launch.hpp - host-side launch helpers: the static GEMV's launch (shared-memory opt-in, grid sized to the SMs,
 // optionally as a programmatic dependent launch), a process-wide launch counter and the operators' status word.
+// What depends on the GPU (its SM count, the kernels' shared-memory opt-in, the status word) is kept per device and
+// set up the first time a launch on that device (the current one) needs it, so handles on several GPUs of one
+// process each get their own.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -7,6 +10,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/geode_cuda.h"
 #include "gemv_kernels.cuh"
@@ -19,25 +23,55 @@ inline std::atomic<uint64_t> &launch_counter() {
 }
 inline void count_launch(uint64_t k = 1) { launch_counter().fetch_add(k, std::memory_order_relaxed); }
 
-inline int sm_count() {
-    static int n = [] {
-        int dev = 0, c = 148;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev);
-        return c;
-    }();
-    return n;
+// Per-device set-up state, filled lazily under one mutex. gemv_rc / bf16_rc: 0 = not tried yet, else the outcome
+// (GCUDA_OK or GCUDA_E_CUDA) of the shared-memory opt-in on that device.
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    std::mutex mu;
+    int sms[kMaxDevices] = {};
+    int gemv_rc[kMaxDevices] = {};
+    int bf16_rc[kMaxDevices] = {};
+    uint32_t *status[kMaxDevices] = {};
+};
+inline DeviceState &device_state() {
+    static DeviceState d;
+    return d;
+}
+inline int current_device() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    return dev;
 }
 
-// The operators' status word (device memory, zeroed once): kernels OR error flags into it.
+inline int sm_count() {
+    const int dev = current_device();
+    if (dev < 0) return 148;
+    DeviceState &d = device_state();
+    std::lock_guard<std::mutex> lock(d.mu);
+    if (!d.sms[dev]) {
+        int c = 0;
+        if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+        d.sms[dev] = c;
+    }
+    return d.sms[dev];
+}
+
+// The operators' status word on the current device (device memory, zeroed once): kernels OR error flags into it.
 inline uint32_t *device_status() {
-    static uint32_t *p = [] {
+    const int dev = current_device();
+    if (dev < 0) return nullptr;
+    DeviceState &d = device_state();
+    std::lock_guard<std::mutex> lock(d.mu);
+    if (!d.status[dev]) {
         void *q = nullptr;
-        if (cudaMalloc(&q, 4) != cudaSuccess) return static_cast<uint32_t *>(nullptr);
-        cudaMemset(q, 0, 4);
-        return static_cast<uint32_t *>(q);
-    }();
-    return p;
+        if (cudaMalloc(&q, 4) != cudaSuccess) return nullptr;
+        if (cudaMemset(q, 0, 4) != cudaSuccess) {
+            cudaFree(q);
+            return nullptr;
+        }
+        d.status[dev] = static_cast<uint32_t *>(q);
+    }
+    return d.status[dev];
 }
 
 // Launch with the programmatic-stream-serialization attribute when pdl: the kernel may begin (its prologue, the
@@ -64,21 +98,38 @@ inline cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cuda
 }
 
 // The GEMV kernels' shared-memory opt-in: the largest any launch shape takes (plan_gemv caps it there).
+// (cudaFuncSetAttribute acts on the current device's context, so each device opts in once.)
 inline int gemv_opt_in() {
-    static const int rc = [] {
+    const int dev = current_device();
+    if (dev < 0) return GCUDA_E_CUDA;
+    DeviceState &d = device_state();
+    std::lock_guard<std::mutex> lock(d.mu);
+    if (!d.gemv_rc[dev]) {
         const cudaFuncAttribute a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-        if (cudaFuncSetAttribute(k_gemv_static<0>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_static<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_static<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_static<kSplitStages>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<0>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<kWideStages>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemv_experts<kPairStages>, a, kMaxDynSmem) != cudaSuccess)
-            return static_cast<int>(GCUDA_E_CUDA);
-        return static_cast<int>(GCUDA_OK);
-    }();
-    return rc;
+        const bool ok = cudaFuncSetAttribute(k_gemv_static<0>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_static<kWideStages>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_static<kDeepStages>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_static<kSplitStages>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_experts<0>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_experts<kWideStages>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_gemv_experts<kPairStages>, a, kMaxDynSmem) == cudaSuccess;
+        d.gemv_rc[dev] = ok ? static_cast<int>(GCUDA_OK) : static_cast<int>(GCUDA_E_CUDA);
+    }
+    return d.gemv_rc[dev];
+}
+
+inline int bf16_opt_in() {
+    const int dev = current_device();
+    if (dev < 0) return GCUDA_E_CUDA;
+    DeviceState &d = device_state();
+    std::lock_guard<std::mutex> lock(d.mu);
+    if (!d.bf16_rc[dev])
+        d.bf16_rc[dev] = cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) ==
+                                 cudaSuccess
+                             ? static_cast<int>(GCUDA_OK)
+                             : static_cast<int>(GCUDA_E_CUDA);
+    return d.bf16_rc[dev];
 }
 
 // p.wpu / p.nslots are set here (plan_static); the grid is one CTA per SM at most
@@ -114,9 +165,7 @@ inline int launch_bf16_gemv(const uint16_t *w, int rows, int cols, const float *
         return GCUDA_E_ARG;
     const size_t smem = bf16_gemv_smem(cols);
     if (smem > static_cast<size_t>(kMaxDynSmem)) return GCUDA_E_ARG;
-    static const bool opted =
-        cudaFuncSetAttribute(k_bf16_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem) == cudaSuccess;
-    if (!opted) return GCUDA_E_CUDA;
+    if (bf16_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
     const int groups = (n + kBf16Tokens - 1) / kBf16Tokens;
     const int rblocks = (rows + kBf16Rows - 1) / kBf16Rows;
     return launch_ex(k_bf16_gemv, dim3(rblocks * groups), dim3(kBf16Rows * 32), smem, st, pdl, w, rows, cols, x, xstride, n,

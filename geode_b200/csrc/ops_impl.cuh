@@ -52,6 +52,7 @@ int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float g
     p.ncols = n;
     p.allow_half = 1;
     p.status = device_status();
+    if (!p.status) return GCUDA_E_CUDA;
     return launch_static_gemv(p, static_cast<cudaStream_t>(stream), false);
 }
 
@@ -67,8 +68,9 @@ int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, cons
 }
 
 int gcuda_op_bf16_gemv(const uint16_t *d_w, int rows, int cols, const float *d_x, int n, float *d_y, void *stream) {
-    return launch_bf16_gemv(d_w, rows, cols, d_x, cols, n, d_y, rows, device_status(), static_cast<cudaStream_t>(stream),
-                            false);
+    uint32_t *status = device_status();
+    if (!status) return GCUDA_E_CUDA;
+    return launch_bf16_gemv(d_w, rows, cols, d_x, cols, n, d_y, rows, status, static_cast<cudaStream_t>(stream), false);
 }
 
 int gcuda_op_route_topk(const float *d_logits, int n, int E, int K, int *d_ids, float *d_weights, void *stream) {

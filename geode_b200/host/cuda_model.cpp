@@ -83,7 +83,7 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
         err = std::string("gcuda_open: ") + ebuf;
         return false;
     }
-    const Json &c = pack_.config();
+    const JsonRef c = pack_.config();
     const bool dense = pack_.arch() == "qwen35";
     const int L = static_cast<int>(c["num_hidden_layers"].integer());
     std::vector<gcuda_layer> layers(static_cast<size_t>(L));
@@ -100,12 +100,12 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
         id = api_.adopt_raw(g_, t.data, t.bytes);
         return id >= 0 || fail(name.c_str(), err);
     };
-    const Json &types = c["layer_types"];
+    const JsonRef types = c["layer_types"];
     for (int l = 0; l < L; ++l) {
         gcuda_layer &x = layers[static_cast<size_t>(l)];
         std::memset(&x, 0xFF, sizeof x);   // every id -1
         const std::string p = "layers." + std::to_string(l) + ".";
-        const bool attn = types[static_cast<size_t>(l)].string() == "full_attention";
+        const bool attn = types[static_cast<size_t>(l)].text() == "full_attention";
         x.attn = attn ? 1 : 0;
         bool ok = raw(p + "input_layernorm.weight", x.in_norm) && raw(p + "post_attention_layernorm.weight", x.post_norm);
         if (attn) {
@@ -146,7 +146,7 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
     if (embed < 0) return fail("embedding", err);
     int head = -1, norm = -1;
     if (!q4("lm_head.weight", head) || !raw("norm.weight", norm)) return false;
-    const Json &rope = c["rope_parameters"];
+    const JsonRef rope = c["rope_parameters"];
     gcuda_shape s{};
     s.hidden = static_cast<int>(c["hidden_size"].integer());
     s.n_layers = L;
@@ -177,7 +177,7 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
     // what a state of this model holds (engine/src/model.cpp:351-358: the attention layers' KV, the Gated DeltaNet
     // layers' conv and recurrent states)
     int n_attn = 0, n_gdn = 0;
-    for (int l = 0; l < L; ++l) (types[static_cast<size_t>(l)].string() == "full_attention" ? n_attn : n_gdn)++;
+    for (int l = 0; l < L; ++l) (types[static_cast<size_t>(l)].text() == "full_attention" ? n_attn : n_gdn)++;
     const uint64_t conv_dim = 2ull * s.gdn_k_heads * s.gdn_k_dim + static_cast<uint64_t>(s.gdn_v_heads) * s.gdn_v_dim;
     shapes_.n_attn = static_cast<uint32_t>(n_attn);
     shapes_.kv_heads = static_cast<uint32_t>(s.n_kv_heads);
@@ -187,8 +187,9 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
     shapes_.conv_n = static_cast<uint64_t>(n_gdn) * conv_dim * static_cast<uint64_t>(std::max(0, s.conv_kernel - 1));
     shapes_.gdn_n = static_cast<uint64_t>(n_gdn) * s.gdn_v_heads * s.gdn_k_dim * s.gdn_v_dim;
     text_only_ = !pack_.has("mtp.fc.weight");
-    for (const auto &kv : pack_.manifest()["tensors"].obj)
-        if (kv.first.rfind("vision.", 0) == 0) text_only_ = false;   // (engine/src/vision.cpp's tensors)
+    const JsonRef tensors = pack_.manifest()["tensors"];
+    for (size_t i = 0; i < tensors.size(); ++i)
+        if (tensors.key_at(i).substr(0, 7) == "vision.") text_only_ = false;   // (engine/src/vision.cpp's tensors)
     conv_id_ = new_conversation_id(this);
     return true;
 }
@@ -306,27 +307,34 @@ bool CudaModel::verify_keep(int kept, std::string &err) {
     return api_.keep(g_, kept) == 0 || fail("keep", err);
 }
 
-bool CudaModel::accept(const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept, int &next,
-                       std::string &err) {
+bool CudaModel::accept(const SamplerParams &p, Sampler &s, SeenTokens &seen, const int *stops, int n_stops, int &kept,
+                       int &next, std::string &err) {
     if (!g_ || last_n_ < 1) {
         err = "accept without a verified batch";
         return false;
     }
-    gcuda_sampling sp{p.temperature, p.top_p, p.top_k};
+    gcuda_sampling sp{p.temperature, p.top_p, p.top_k, p.presence_penalty};
     double u[8] = {0};
+    int samples[8] = {0};
     const bool sampled = p.temperature > 0.0f;
     if (sampled) s.peek(last_n_, u);   // row i's draw is the stream's i-th from here
     int k = 0, nx = 0;
-    if (api_.accept(g_, &sp, sampled ? u : nullptr, stops, n_stops, &k, &nx, nullptr) != 0) return fail("accept", err);
+    const std::vector<int> &sl = seen.list();
+    if (api_.accept(g_, &sp, sampled ? u : nullptr, stops, n_stops, sl.data(), static_cast<int>(sl.size()), &k, &nx,
+                    samples) != 0)
+        return fail("accept", err);
     if (sampled) s.skip(k);   // the rows sampled: kept of them (the last one gave next)
+    if (p.presence_penalty != 0.0f)
+        for (int i = 0; i < k; ++i) seen.add(samples[i], vocab_);   // (every sampled row, as the engine's sample())
     kept = k;
     next = nx;
     return true;
 }
 
-bool CudaModel::step(const int *batch, int n, const SamplerParams &p, Sampler &s, const int *stops, int n_stops,
-                     int &kept, int &next, std::string &err) {
-    if (!verify_n(batch, n, nullptr, err) || !accept(p, s, stops, n_stops, kept, next, err)) return false;
+bool CudaModel::step(const int *batch, int n, const SamplerParams &p, Sampler &s, SeenTokens &seen, const int *stops,
+                     int n_stops, int &kept, int &next, std::string &err) {
+    if (p.presence_penalty != 0.0f && n > 0) seen.add(batch[0], vocab_);
+    if (!verify_n(batch, n, nullptr, err) || !accept(p, s, seen, stops, n_stops, kept, next, err)) return false;
     // (every draft stood: nothing to roll back, as the engine's loop; else the states as after row kept-1)
     return kept == n || verify_keep(kept, err);
 }
@@ -334,17 +342,18 @@ bool CudaModel::step(const int *batch, int n, const SamplerParams &p, Sampler &s
 bool pack_summary(const std::string &dir, std::string &out, std::string &err) {
     Pack p;
     if (!p.open(dir, err)) return false;
-    const Json &c = p.config();
+    const JsonRef c = p.config();
     size_t n = 0, q4 = 0, bytes = 0;
-    for (const auto &kv : p.manifest()["tensors"].obj) {
+    const JsonRef tensors = p.manifest()["tensors"];
+    for (size_t i = 0; i < tensors.size(); ++i) {
         TensorView t;
-        if (!p.tensor(kv.first, t, err)) return false;
+        if (!p.tensor(std::string(tensors.key_at(i)), t, err)) return false;
         ++n;
         q4 += t.type == "q4";
         bytes += t.bytes;
     }
     size_t expert_bytes = 0;
-    if (p.manifest()["experts"].has("layers"))
+    if (p.manifest()["experts"]["layers"].present())
         for (size_t l = 0; l < p.manifest()["experts"]["layers"].size(); ++l) {
             ExpertTable e;
             if (!p.experts(static_cast<int>(l), e, err)) return false;

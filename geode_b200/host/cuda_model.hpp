@@ -46,9 +46,32 @@ struct ModelOptions {
 };
 
 struct SamplerParams {
-    float temperature = 0.0f;   // 0 = greedy
-    float top_p = 1.0f;         // 1 = off
-    int top_k = 0;              // 0 = off (1024 candidates)
+    float temperature = 0.0f;        // 0 = greedy
+    float top_p = 1.0f;              // 1 = off
+    int top_k = 0;                   // 0 = off (1024 candidates)
+    float presence_penalty = 0.0f;   // 0 = off (geode_sampling's, engine/src/geode.cpp:234-255)
+};
+
+// The answer's sampled tokens for the presence penalty (geode_generate's seen / is_seen, engine/src/geode.cpp:
+// 234-255): each id once, in the order first sampled; cleared when a generation starts.
+class SeenTokens {
+public:
+    void clear() {
+        list_.clear();
+        mark_.clear();
+    }
+    void add(int tok, int vocab) {
+        if (tok < 0 || tok >= vocab) return;
+        if (mark_.size() < static_cast<size_t>(vocab)) mark_.resize(static_cast<size_t>(vocab), 0);
+        if (mark_[static_cast<size_t>(tok)]) return;
+        mark_[static_cast<size_t>(tok)] = 1;
+        list_.push_back(tok);
+    }
+    const std::vector<int> &list() const { return list_; }
+
+private:
+    std::vector<int> list_;
+    std::vector<uint8_t> mark_;
 };
 
 // The reference sampler's random stream: std::mt19937_64 seeded once per generate call, one
@@ -93,11 +116,15 @@ public:
     bool prefill(const int *toks, int n, std::string &err);
     // rollback: the states as after the verified batch's row kept-1 (1 <= kept < n); position -= n - kept
     bool verify_keep(int kept, std::string &err);
-    // the acceptance of the last verified batch (its rows 1.. are the drafts): kept, next (-1: a stop token stood)
-    bool accept(const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept, int &next, std::string &err);
-    // one speculation step: verify_n(batch), accept, verify_keep(kept) unless every draft stood
-    bool step(const int *batch, int n, const SamplerParams &p, Sampler &s, const int *stops, int n_stops, int &kept,
-              int &next, std::string &err);
+    // the acceptance of the last verified batch (its rows 1.. are the drafts): kept, next (-1: a stop token stood);
+    // with a presence penalty the rows are penalised for `seen`, and the rows' samples are added to it
+    bool accept(const SamplerParams &p, Sampler &s, SeenTokens &seen, const int *stops, int n_stops, int &kept,
+                int &next, std::string &err);
+    // one speculation step: verify_n(batch), accept, verify_keep(kept) unless every draft stood. batch[0] is the
+    // answer's last sampled token: with a presence penalty it joins `seen` first (a no-op after the first step,
+    // whose batch[0] is the previous step's next)
+    bool step(const int *batch, int n, const SamplerParams &p, Sampler &s, SeenTokens &seen, const int *stops,
+              int n_stops, int &kept, int &next, std::string &err);
 
     // Model::save_state / load_state (engine/src/state.cpp:241-465) in the engine's state file: the device's KV rows
     // and recurrent states through the host (gcuda_state_get / gcuda_state_put), so a state saved by the reference

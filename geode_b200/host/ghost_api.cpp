@@ -10,6 +10,7 @@ struct ghost_model {
     ghost::CudaModel model;
     ghost::SamplerParams params;
     ghost::Sampler sampler;
+    ghost::SeenTokens seen;   // the answer's tokens for the presence penalty (from ghost_set_sampling on)
     int32_t pending = -1;   // the token passed on but not computed yet (geode.cpp's `pending`)
 };
 
@@ -103,7 +104,9 @@ int ghost_set_sampling(ghost_model *m, const ghost_sampling *s) {
     m->params.temperature = s->temperature;
     m->params.top_p = s->top_p;
     m->params.top_k = s->top_k;
+    m->params.presence_penalty = s->presence_penalty;
     m->sampler.seed(s->seed);
+    m->seen.clear();
     return GHOST_OK;
 }
 
@@ -112,7 +115,7 @@ int ghost_step(ghost_model *m, const int32_t *batch, int32_t n, const int32_t *s
     if (!m || !batch || n < 1 || !kept || !next) return GHOST_E_ARG;
     std::string e;
     int k = 0, nx = 0;
-    if (!m->model.step(batch, n, m->params, m->sampler, stops, n_stops, k, nx, e)) {
+    if (!m->model.step(batch, n, m->params, m->sampler, m->seen, stops, n_stops, k, nx, e)) {
         put(e, err, err_len);
         return GHOST_E_BACKEND;
     }

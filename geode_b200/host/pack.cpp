@@ -25,17 +25,17 @@ bool Pack::open(const std::string &dir, std::string &err) {
     std::stringstream ss;
     ss << in.rdbuf();
     std::string jerr;
-    if (!parse_json(ss.str(), m_, jerr)) {
+    if (!m_.load(ss.str(), jerr)) {
         err = "geode.json: " + jerr;
         return false;
     }
-    const Json &files = m_["files"];
-    if (files.kind != Json::Array) {
+    const JsonRef files = manifest()["files"];
+    if (!files.is_list()) {
         err = "geode.json: no file list";
         return false;
     }
-    for (const Json &f : files.arr) {
-        const std::string name = f["name"].string();
+    for (const JsonRef f : files) {
+        const std::string name = f["name"].text();
         const std::string path = dir + "/" + name;
         const int fd = ::open(path.c_str(), O_RDONLY);
         if (fd < 0) {
@@ -66,19 +66,19 @@ bool Pack::open(const std::string &dir, std::string &err) {
 }
 
 bool Pack::tensor(const std::string &name, TensorView &out, std::string &err) const {
-    const Json &t = m_["tensors"][name];
-    if (t.kind != Json::Object) {
+    const JsonRef t = manifest()["tensors"][name];
+    if (!t.is_map()) {
         err = "tensor " + name + " is not in the pack";
         return false;
     }
-    const auto f = files_.find(t["file"].string());
+    const auto f = files_.find(t["file"].text());
     if (f == files_.end()) {
-        err = "tensor " + name + ": unknown file " + t["file"].string();
+        err = "tensor " + name + ": unknown file " + t["file"].text();
         return false;
     }
     out = TensorView();
-    out.type = t["type"].string();
-    for (const Json &d : t["shape"].arr) out.shape.push_back(d.integer());
+    out.type = t["type"].text();
+    for (const JsonRef d : t["shape"]) out.shape.push_back(d.integer());
     out.global = static_cast<float>(t["global"].number(1.0));
     int64_t n = 1;
     for (int64_t d : out.shape) n *= d;
@@ -99,13 +99,13 @@ bool Pack::tensor(const std::string &name, TensorView &out, std::string &err) co
 }
 
 bool Pack::experts(int layer, ExpertTable &out, std::string &err) const {
-    const Json &ls = m_["experts"]["layers"];
-    if (ls.kind != Json::Array || layer < 0 || static_cast<size_t>(layer) >= ls.size()) {
+    const JsonRef ls = manifest()["experts"]["layers"];
+    if (!ls.is_list() || layer < 0 || static_cast<size_t>(layer) >= ls.size()) {
         err = "no expert table for layer " + std::to_string(layer);
         return false;
     }
-    const Json &e = ls[static_cast<size_t>(layer)];
-    const auto f = files_.find(e["file"].string());
+    const JsonRef e = ls[static_cast<size_t>(layer)];
+    const auto f = files_.find(e["file"].text());
     if (f == files_.end()) {
         err = "experts of layer " + std::to_string(layer) + ": unknown file";
         return false;

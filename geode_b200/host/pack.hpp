@@ -39,10 +39,10 @@ public:
     ~Pack();
 
     bool open(const std::string &dir, std::string &err);
-    const Json &manifest() const { return m_; }
-    const Json &config() const { return m_["config"]; }
-    const std::string &arch() const { return m_["arch"].string(); }
-    bool has(const std::string &name) const { return m_["tensors"].has(name); }
+    JsonRef manifest() const { return m_.root(); }
+    JsonRef config() const { return m_.root()["config"]; }
+    std::string arch() const { return m_.root()["arch"].text(); }
+    bool has(const std::string &name) const { return m_.root()["tensors"][name].present(); }
     // false (and err) when the tensor is missing or its bytes run past its file
     bool tensor(const std::string &name, TensorView &out, std::string &err) const;
     bool experts(int layer, ExpertTable &out, std::string &err) const;
@@ -52,7 +52,7 @@ private:
         const uint8_t *data = nullptr;
         size_t size = 0;
     };
-    Json m_;
+    JsonDoc m_;
     std::map<std::string, Mapped> files_;
 };
 

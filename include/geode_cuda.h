@@ -101,22 +101,30 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
  * Gated DeltaNet states as after token kept-1, the position back by n - kept. */
 int gcuda_keep(gcuda *g, int kept);
 int gcuda_position(gcuda *g);
-/* The conversation from the start (position 0, zero states). */
+/* The conversation from the start (position 0, zero states; the device-side rejection sampler's random sequence
+ * restarts too, so a repeated conversation with the same seed draws the same uniforms). */
 int gcuda_reset(gcuda *g);
 
-/* Sampling parameters (engine/src/sampler.hpp:11-15). */
+/* Sampling parameters (engine/src/sampler.hpp:11-15, and geode_sampling's presence_penalty,
+ * engine/include/geode/geode.h). */
 typedef struct {
-    float temperature; /* 0 = greedy */
-    float top_p;       /* 1 = off */
-    int top_k;         /* 0 = off (then 1024 candidates, engine/src/sampler.cpp:11) */
+    float temperature;      /* 0 = greedy */
+    float top_p;            /* 1 = off */
+    int top_k;              /* 0 = off (then 1024 candidates, engine/src/sampler.cpp:11) */
+    float presence_penalty; /* 0 = off; used by gcuda_accept only (the rejection samplers take none and ignore it) */
 } gcuda_sampling;
 
 /* The acceptance of geode_generate (engine/src/geode.cpp:327-350) on the last verified batch's logits (on the
  * device): row i sampled with uniforms[i] (the draw Sampler::sample makes for row i, in [0,1); ignored when
  * greedy); draft i+1 stands while row i's sample equals toks[i+1] and is not in stops. Returns kept (1 .. n) in
- * *kept, the first sample that is no draft in *next, and every row's sample in samples[n] (NULL: not wanted). */
-int gcuda_accept(gcuda *g, const gcuda_sampling *s, const double *uniforms, const int *stops, int n_stops, int *kept,
-                 int *next, int *samples);
+ * *kept, the first sample that is no draft in *next, and every row's sample in samples[n] (NULL: not wanted).
+ * With a presence penalty (engine/src/geode.cpp:234-255), seen[n_seen] lists the tokens the answer has sampled so
+ * far, each once (ids in [0, vocab); GCUDA_E_ARG otherwise): before row i is sampled, the penalty is subtracted from
+ * its logit of every listed token and of every draft toks[1..i] not listed (the samples of rows 0..i-1 when their
+ * drafts stood), once per token - in place, in the device logits. The caller then adds the samples of rows
+ * 0..kept-1 that are new to its list. seen is ignored when the penalty is 0. */
+int gcuda_accept(gcuda *g, const gcuda_sampling *s, const double *uniforms, const int *stops, int n_stops,
+                 const int *seen, int n_seen, int *kept, int *next, int *samples);
 /* Speculative (rejection) sampling (Leviathan et al. 2023) over S sequences x (k+1) target rows and k draft rows of V
  * logits already on the device (target [S][k+1][V], draft [S][k][V]), Philox4x32-10 uniforms (key seed, counter
  * (sequence, row)); accepted[S] and next[S] on the host. Not in the reference: no counterpart there. */
@@ -223,10 +231,13 @@ int gcuda_op_greedy_verify(const float *d_target, const int *d_drafts, int S, in
  * they call it (a serving loop that holds a fixed device-memory budget, or one that cannot take the implicit
  * synchronisation of cudaMalloc / cudaFree in its step). Same arguments and results as gcuda_spec_reject (d_target
  * [S][k+1][V] and d_draft [S][k][V] on the device, drafts [S][k] and accepted[S] / next[S] on the host), on `stream`;
- * it returns after the results are on the host. Its scratch is a fixed device array of the library, so S <= 1024 and
- * k <= 16 (GCUDA_E_ARG beyond). The first call on a device looks that array up (cudaGetSymbolAddress, with the
- * device current): make it before any stream capture. Calls that overlap on one device - from several threads or
- * streams - share the array and race; serialise them. No counterpart in the reference. */
+ * every call copies the drafts from host memory and synchronises `stream`, so it blocks the calling thread until the
+ * results are on the host. Its scratch is a fixed device array of the library, so S <= 1024 and k <= 16 (GCUDA_E_ARG
+ * beyond). The first call on a device looks that array up (cudaGetSymbolAddress, with the device current) and keeps
+ * the address for the life of the process: make that first call before any stream capture, and do not call
+ * cudaDeviceReset on a device between calls (the kept address would no longer be valid). Calls that overlap on one
+ * device - from several threads or streams - share the array and race; serialise them. No counterpart in the
+ * reference. */
 int gcuda_op_spec_reject_static(const float *d_target, const float *d_draft, const int *drafts, int S, int k, int V,
                                 const gcuda_sampling *s, uint64_t seed, int *accepted, int *next, void *stream);
 

@@ -30,10 +30,12 @@ enum {
 typedef struct ghost_model ghost_model;
 
 typedef struct {
-    float temperature;   /* 0 = greedy */
-    float top_p;         /* 1 = off */
-    int32_t top_k;       /* 0 = off */
-    uint64_t seed;       /* the sampler's mt19937_64 seed (set once per generation, as geode_generate) */
+    float temperature;        /* 0 = greedy */
+    float top_p;              /* 1 = off */
+    int32_t top_k;            /* 0 = off */
+    uint64_t seed;            /* the sampler's mt19937_64 seed (set once per generation, as geode_generate) */
+    float presence_penalty;   /* 0 = off: subtracted from the logits of the answer's tokens so far before each row is
+                                 sampled (engine/src/geode.cpp:234-255) */
 } ghost_sampling;
 
 /* Opens the pack in dir on CUDA device `device` with `context` positions of KV cache (0 = 4096) and verify batches
@@ -56,10 +58,12 @@ int ghost_reset(ghost_model *m, char *err, size_t err_len);
 int ghost_prefill(ghost_model *m, const int32_t *prompt, int32_t n, char *err, size_t err_len);
 /* Model::verify_keep: keep the first `kept` rows of the last batch (1 <= kept < n; with every row kept, no call) */
 int ghost_keep(ghost_model *m, int32_t kept, char *err, size_t err_len);
-/* The sampling of the steps that follow; seeds the sampler's stream */
+/* The sampling of the steps that follow - a new answer, as a geode_generate call: seeds the sampler's stream and
+ * empties the answer's tokens for the presence penalty */
 int ghost_set_sampling(ghost_model *m, const ghost_sampling *s);
 /* One speculation step: verify batch[0..n) (the accepted token, then n - 1 drafts), accept (kept = 1 + the drafts
- * that stood; next = the first sample that is no draft, -1 when a stop token stood), roll back to kept rows. */
+ * that stood; next = the first sample that is no draft, -1 when a stop token stood), roll back to kept rows. With a
+ * presence penalty, batch[0] (the answer's last sampled token) and every row sampled join the answer's tokens. */
 int ghost_step(ghost_model *m, const int32_t *batch, int32_t n, const int32_t *stops, int32_t n_stops, int32_t *kept,
                int32_t *next, char *err, size_t err_len);
 /* The pack's manifest as this host reads it, one line (arch, layers, hidden, vocab, experts, tensors, bytes); no GPU

@@ -885,18 +885,44 @@ int go_sample(const float *logits, int n, float temperature, float top_p, int to
 }
 
 /* engine/src/geode.cpp:327-350: rows sampled in order (one draw per sampled row when not greedy); draft i+1 stands
- * while row i's sample is that draft and no stop token */
-int go_accept(const float *rows, int n, int V, const int *batch, float temperature, float top_p, int top_k,
-              uint64_t seed, const int *stops, int n_stops, int *next, int *samples) {
+ * while row i's sample is that draft and no stop token. Each row goes through geode_generate's sample()
+ * (engine/src/geode.cpp:246-255): with a presence penalty, the penalty is first subtracted from the row's logit of
+ * every token in seen (in/out: the answer's tokens so far, each once, in the order first sampled; room for n more),
+ * and the sample joins seen when it is new (only while the penalty is on, as the engine's is_seen). The rows are not
+ * modified (each is sampled from a copy). */
+int go_accept_seen(const float *rows, int n, int V, const int *batch, float temperature, float top_p, int top_k,
+                   uint64_t seed, const int *stops, int n_stops, float penalty, int *seen, int *n_seen, int *next,
+                   int *samples) {
     go_mt64 g;
     go_mt64_seed(&g, seed);
     for (int i = 0; i < n; ++i) samples[i] = -1;
     int kept = 1;
     *next = -1;
+    const int on = penalty != 0.0f;
+    float *row = on ? (float *)malloc(sizeof(float) * (size_t)V) : NULL;
+    unsigned char *is_seen = on ? (unsigned char *)calloc((size_t)V, 1) : NULL;
+    if (on && (!row || !is_seen)) {
+        free(row);
+        free(is_seen);
+        return -1;
+    }
+    if (on)
+        for (int j = 0; j < *n_seen; ++j)
+            if (seen[j] >= 0 && seen[j] < V) is_seen[seen[j]] = 1;
     for (int i = 0; i < n; ++i) {
+        const float *lg = rows + (size_t)i * V;
+        if (on) {
+            memcpy(row, lg, sizeof(float) * (size_t)V);
+            for (int j = 0; j < *n_seen; ++j) row[seen[j]] -= penalty;
+            lg = row;
+        }
         const double u = temperature > 0.0f ? go_canonical(&g) : 0.0;
-        const int y = go_sample(rows + (size_t)i * V, V, temperature, top_p, top_k, u);
+        const int y = go_sample(lg, V, temperature, top_p, top_k, u);
         samples[i] = y;
+        if (on && y >= 0 && y < V && !is_seen[y]) {
+            is_seen[y] = 1;
+            seen[(*n_seen)++] = y;
+        }
         int stop = 0;
         for (int s = 0; s < n_stops; ++s) stop |= stops[s] == y;
         if (i + 1 < n && y == batch[i + 1] && !stop) {
@@ -906,7 +932,16 @@ int go_accept(const float *rows, int n, int V, const int *batch, float temperatu
         *next = y;
         break;
     }
+    free(row);
+    free(is_seen);
     return kept;
+}
+
+int go_accept(const float *rows, int n, int V, const int *batch, float temperature, float top_p, int top_k,
+              uint64_t seed, const int *stops, int n_stops, int *next, int *samples) {
+    int none = 0;
+    return go_accept_seen(rows, n, V, batch, temperature, top_p, top_k, seed, stops, n_stops, 0.0f, NULL, &none, next,
+                          samples);
 }
 
 /* ---------------------------------------------------------------- rejection sampling (not in the reference) ---- */

@@ -127,6 +127,10 @@ int go_sample(const float *logits, int n, float temperature, float top_p, int to
 /* engine/src/geode.cpp:327-350: returns kept; *next the first non-draft sample (-1 if none); samples[n] */
 int go_accept(const float *rows, int n, int V, const int *batch, float temperature, float top_p, int top_k,
               uint64_t seed, const int *stops, int n_stops, int *next, int *samples);
+/* go_accept with geode_generate's presence penalty (engine/src/geode.cpp:234-255): seen in/out, room for n more */
+int go_accept_seen(const float *rows, int n, int V, const int *batch, float temperature, float top_p, int top_k,
+                   uint64_t seed, const int *stops, int n_stops, float penalty, int *seen, int *n_seen, int *next,
+                   int *samples);
 
 /* Standard speculative (rejection) sampling (Leviathan et al. 2023; Chen et al. 2023), with Philox4x32-10
  * uniforms. NOT in the reference: parity unpinned. target [n_drafts+1][V], draft [n_drafts][V] logits; the

@@ -284,6 +284,10 @@ def oracle_lib():
     lib.go_accept.restype = C.c_int
     lib.go_accept.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float, C.c_int, C.c_uint64,
                               C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+    lib.go_accept_seen.restype = C.c_int
+    lib.go_accept_seen.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float, C.c_int,
+                                   C.c_uint64, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p]
     lib.go_spec_reject.restype = C.c_int
     lib.go_spec_reject.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float,
                                    C.c_int, C.c_uint64, C.c_uint64, C.c_void_p]
@@ -477,6 +481,10 @@ def reference_lib():
     lib.ref_accept.restype = C.c_int
     lib.ref_accept.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float, C.c_int, C.c_uint64,
                                C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]
+    lib.ref_accept_seen.restype = C.c_int
+    lib.ref_accept_seen.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float, C.c_int,
+                                    C.c_uint64, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    C.c_void_p]
     lib.ref_uniforms.argtypes = [C.c_uint64, C.c_int, C.c_void_p]
     return lib
 
@@ -520,3 +528,38 @@ def write_long_state(template: str, out: str, position: int, seed: int = 0):
             sc = (np.abs(rng.standard_normal(2 * n_attn * B * heads)) * 0.5 / 127 + 1e-4).astype(np.float32)
             f.write(kv.tobytes())
             f.write(sc.tobytes())
+
+
+def accept_seen(lib, rows, batch, temperature, top_p, top_k, seed, penalty, seen, stops=(), fn="go_accept_seen"):
+    """The acceptance with the presence penalty through lib.<fn> (go_accept_seen of the oracle, ref_accept_seen of the
+    reference build): (kept, next, samples, the seen list after it)."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    n, V = rows.shape
+    batch = np.ascontiguousarray(batch, dtype=np.int32)
+    buf = np.zeros(len(seen) + n + 1, np.int32)
+    buf[:len(seen)] = np.asarray(seen, dtype=np.int32)
+    ns = C.c_int(len(seen))
+    st = np.ascontiguousarray(np.asarray(list(stops) or [0], dtype=np.int32))
+    nxt = C.c_int(0)
+    samples = np.zeros(n, np.int32)
+    kept = getattr(lib, fn)(rows.ctypes.data, n, V, batch.ctypes.data, temperature, top_p, top_k, C.c_uint64(seed),
+                            st.ctypes.data, len(stops), penalty, buf.ctypes.data, C.byref(ns), C.byref(nxt),
+                            samples.ctypes.data)
+    return kept, nxt.value, samples, buf[:ns.value].copy()
+
+
+def plant_penalized_drafts(rows, batch, seen, penalty, stand):
+    """Sets batch[1..stand] to the greedy samples of rows 0..stand-1 under the presence penalty (each row's logits
+    less the penalty at the tokens of seen and at the drafts planted before it, once each - the f32 subtraction the
+    engine makes), so that those drafts stand under the penalty. Returns batch."""
+    pen = np.float32(penalty)
+    known = set(int(t) for t in seen)
+    for i in range(stand):
+        r = np.array(rows[i], dtype=np.float32, copy=True)
+        idx = np.array(sorted(known), dtype=np.int64)
+        if idx.size:
+            r[idx] = r[idx] - pen
+        y = int(np.argmax(r))
+        batch[i + 1] = y
+        known.add(y)
+    return batch

@@ -280,6 +280,56 @@ int ref_accept(const float *rows, int n, int V, const int *batch, float temperat
     return kept;
 }
 
+// ref_accept with geode_generate's presence penalty, its sample() lambda restated (engine/src/geode.cpp:234-255):
+// before a row is sampled every token of seen loses the penalty; a new sample joins seen (the is_seen bitmap is
+// only kept while the penalty is on). seen in/out (room for n more), *n_seen its length.
+int ref_accept_seen(const float *rows, int n, int V, const int *batch, float temperature, float top_p, int top_k,
+                    uint64_t seed, const int *stops, int n_stops, float penalty, int *seen, int *n_seen, int *next,
+                    int *samples) {
+    geode::Sampler s;
+    s.seed(seed);
+    geode::SamplerParams sp;
+    sp.temperature = temperature;
+    sp.top_p = top_p;
+    sp.top_k = top_k;
+    std::vector<int32_t> seen_list(seen, seen + *n_seen);
+    std::vector<uint8_t> is_seen(penalty != 0.0f ? static_cast<size_t>(V) : 0, 0);
+    for (int32_t t : seen_list)
+        if (!is_seen.empty()) is_seen[static_cast<size_t>(t)] = 1;
+    std::vector<float> row(static_cast<size_t>(V));
+    const auto sample = [&](float *lg) {
+        for (int32_t t : seen_list) lg[static_cast<size_t>(t)] -= penalty;
+        const int32_t tok = s.sample(lg, V, sp);
+        if (!is_seen.empty() && tok >= 0 && static_cast<size_t>(tok) < is_seen.size() && !is_seen[static_cast<size_t>(tok)]) {
+            is_seen[static_cast<size_t>(tok)] = 1;
+            seen_list.push_back(tok);
+        }
+        return tok;
+    };
+    auto is_stop = [&](int t) {
+        for (int i = 0; i < n_stops; ++i)
+            if (stops[i] == t) return true;
+        return false;
+    };
+    for (int i = 0; i < n; ++i) samples[i] = -1;
+    int kept = 1;
+    *next = -1;
+    for (int i = 0; i < n; ++i) {
+        std::memcpy(row.data(), rows + static_cast<size_t>(i) * V, static_cast<size_t>(V) * 4);
+        const int y = sample(row.data());
+        samples[i] = y;
+        if (i + 1 < n && y == batch[i + 1] && !is_stop(y)) {
+            ++kept;
+            continue;
+        }
+        *next = y;
+        break;
+    }
+    for (size_t j = 0; j < seen_list.size(); ++j) seen[j] = seen_list[j];
+    *n_seen = static_cast<int>(seen_list.size());
+    return kept;
+}
+
 // the sampler's uniform stream: the first n draws uniform_real_distribution<double>(0, 1) makes from
 // mt19937_64(seed) (engine/src/sampler.cpp:45 draws (0, kept); the distribution is a + (b - a) * canonical)
 void ref_uniforms(uint64_t seed, int n, double *out) {

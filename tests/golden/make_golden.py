@@ -7,6 +7,7 @@ restatement, so tests/test_oracle.py pins the restatement to the reference where
   fast_exp (engine/src/kernels.cpp, engine/src/model.cpp:4021), the q4 block quantizer (engine/src/yue2_q4.cpp:88) and
   the sampler's uniform stream (std::mt19937_64 + generate_canonical, engine/src/sampler.cpp:45);
 - accept.npz: the acceptance rule (engine/src/geode.cpp:327-350) around geode::Sampler, greedy and sampled;
+- accept_seen.npz: the same with geode_generate's presence penalty (engine/src/geode.cpp:234-255);
 - model_moe.npz / model_dense.npz: Model::forward_batch over a prompt and a 5-token verify batch on a tiny synthetic
   pack (written by geode_b200/synth.py with the seed stored), every logit and the per-layer trace;
 - state_file.npz: Model::save_state's file (engine/src/state.cpp) after a 20-token prompt on a tiny synthetic pack,
@@ -15,7 +16,7 @@ restatement, so tests/test_oracle.py pins the restatement to the reference where
   pack with one: the main model's hidden rows after a prompt, the MTP pass over the prompt's positions (logits and
   normed output of the last), then one chained position fed its own draft.
 
-Run with names (kernels, accept, model, state, mtp) to regenerate only those fixtures.
+Run with names (kernels, accept, accept_seen, model, state, mtp) to regenerate only those fixtures.
 """
 import ctypes as C
 import os
@@ -108,6 +109,42 @@ def accept(R):
                         kept=np.array(kept), next=np.array(nxt), samples=np.array(samples))
 
 
+def accept_seen(R):
+    """The acceptance with geode_generate's presence penalty (engine/src/geode.cpp:234-255): seen lists that hold
+    some rows' greedy maxima, drafts planted as the penalised greedy samples (they stand only under the penalty), a
+    draft repeated and one already seen."""
+    rng = np.random.default_rng(91)
+    V = 4096
+    cases = [(0.0, 1.0, 0, 2.5), (0.7, 0.95, 20, 1.5), (0.0, 1.0, 0, -0.75), (1.1, 0.9, 40, 3.0), (0.0, 1.0, 0, 0.0),
+             (0.7, 1.0, 0, 0.5)]
+    rows = (rng.standard_normal((len(cases), 5, V)) * 3).astype(np.float32)
+    batch = rng.integers(0, V, (len(cases), 5)).astype(np.int32)
+    params, seen_in, n_in, kept, nxt, samples, seen_out, n_out = [], [], [], [], [], [], [], []
+    for c, (T, P, K, pen) in enumerate(cases):
+        seen = list(rng.choice(V, 12, replace=False))
+        seen[0] = int(np.argmax(rows[c, 0]))   # row 0's maximum is penalised
+        seen[1] = int(np.argmax(rows[c, 2]))
+        op.plant_penalized_drafts(rows[c], batch[c], seen, pen, 1 + c % 4)
+        if c == 2:
+            batch[c, 4] = batch[c, 3]   # a draft repeated (it joins seen once)
+        if c == 3:
+            batch[c, 1] = seen[5]       # a draft already seen
+        seed = int(rng.integers(0, 2 ** 40))
+        k, n, s, so = op.accept_seen(R, rows[c], batch[c], T, P, K, seed, pen, seen, fn="ref_accept_seen")
+        params.append((T, P, K, seed, pen))
+        seen_in.append(np.pad(np.array(seen, np.int32), (0, 8)))
+        n_in.append(len(seen))
+        kept.append(k)
+        nxt.append(n)
+        samples.append(s)
+        seen_out.append(np.pad(so, (0, 20 - len(so))))
+        n_out.append(len(so))
+    np.savez_compressed(os.path.join(OUT, "accept_seen.npz"), rows=rows, batch=batch,
+                        params=np.array(params, np.float64), seen=np.array(seen_in), n_seen=np.array(n_in),
+                        kept=np.array(kept), next=np.array(nxt), samples=np.array(samples),
+                        seen_out=np.array(seen_out), n_seen_out=np.array(n_out))
+
+
 def model(arch, name, seed=21, attn_block=64):
     shape = synth.tiny_shape(arch, n_layers=4, ctx=640)
     with tempfile.TemporaryDirectory() as d:
@@ -168,11 +205,13 @@ if __name__ == "__main__":
     if not op.have_reference():
         sys.exit("build the reference first: make -C oracle ref")
     R = op.reference_lib()
-    which = set(sys.argv[1:]) or {"kernels", "accept", "model", "state", "mtp"}
+    which = set(sys.argv[1:]) or {"kernels", "accept", "accept_seen", "model", "state", "mtp"}
     if "kernels" in which:
         kernels(R)
     if "accept" in which:
         accept(R)
+    if "accept_seen" in which:
+        accept_seen(R)
     if "model" in which:
         model("qwen35moe", "model_moe")
         model("qwen35", "model_dense")

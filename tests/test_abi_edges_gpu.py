@@ -34,7 +34,7 @@ def test_bad_calls_leave_the_conversation(tmp_path):
         out = np.zeros((5, V), np.float32)
         sp = GSampling(0.0, 1.0, 0)
         kept, nxt = C.c_int(0), C.c_int(0)
-        assert L.gcuda_accept(a.g, C.byref(sp), None, None, 0, C.byref(kept), C.byref(nxt), None) == E_STATE
+        assert L.gcuda_accept(a.g, C.byref(sp), None, None, 0, None, 0, C.byref(kept), C.byref(nxt), None) == E_STATE
         assert L.gcuda_verify(a.g, toks.ctypes.data, 0, out.ctypes.data, None) == E_ARG
         assert L.gcuda_verify(a.g, toks.ctypes.data, 6, out.ctypes.data, None) == E_ARG
         for bad in (V, -1):

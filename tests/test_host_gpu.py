@@ -17,7 +17,8 @@ pytestmark = pytest.mark.gpu
 
 
 class GSamp(C.Structure):
-    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int32), ("seed", C.c_uint64)]
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int32), ("seed", C.c_uint64),
+                ("presence_penalty", C.c_float)]
 
 
 @pytest.fixture(scope="module")
@@ -77,6 +78,80 @@ def test_host_verify_and_steps(env):
             assert H.ghost_position(m) == be.pos
     finally:
         be.close()
+
+
+def test_host_presence_steps(env):
+    """ghost_step with geode_generate's presence penalty over consecutive steps of one answer: the host keeps the
+    answer's tokens (batch[0], then every row it samples) from ghost_set_sampling on; each step's kept and next equal
+    the oracle's rule (go_accept_seen) on the same logits with the oracle's own list carried along, greedy and
+    sampled."""
+    H, m, d, shape = env
+    from geode_b200.backend import Backend
+    be = Backend(d, context=shape.ctx, max_tokens=5)
+    O = op.oracle_lib()
+    rng = np.random.default_rng(12)
+    err = C.create_string_buffer(512)
+    H.ghost_reset.argtypes = [C.c_void_p, C.c_char_p, C.c_size_t]
+    H.ghost_prefill.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t]
+    try:
+        # both handles at the same conversation: the host's position, reached by a prefill on the Python handle
+        assert H.ghost_reset(m, err, 512) == 0, err.value
+        prompt = rng.integers(0, shape.vocab, 7).astype(np.int32)
+        assert H.ghost_prefill(m, prompt.ctypes.data_as(C.c_void_p), 7, err, 512) == 0, err.value
+        be.reset()
+        be.verify(prompt[:5])
+        be.verify(prompt[5:])
+        for temp, seed, pen in [(0.0, 0, 2.0), (0.8, 91, 1.25)]:
+            sp = GSamp(temp, 0.95 if temp else 1.0, 40 if temp else 0, seed, pen)
+            assert H.ghost_set_sampling(m, C.byref(sp)) == 0
+            seen = []
+            mt_seed = seed   # the host's sampler stream: one draw per sampled row, from the seed on
+            draws = 0
+            tok = int(rng.integers(0, shape.vocab))
+            for step in range(4):
+                batch = np.array([tok] + [int(t) for t in rng.integers(0, shape.vocab, 4)], np.int32)
+                rows, _ = be.verify(batch)
+                if tok not in seen:
+                    seen.append(tok)
+                u_all = op.oracle_uniforms(O, mt_seed, draws + 5)
+                kept_r, next_r, samples_r, seen_after = _accept_with_stream(O, rows, batch, temp, sp, u_all[draws:],
+                                                                            pen, seen)
+                kept, nxt = C.c_int32(0), C.c_int32(0)
+                assert H.ghost_step(m, batch.ctypes.data_as(C.c_void_p), 5, None, 0, C.byref(kept), C.byref(nxt), err,
+                                    512) == 0, err.value
+                assert (kept.value, nxt.value) == (kept_r, next_r), (temp, step, kept.value, nxt.value, kept_r, next_r)
+                seen = seen_after
+                draws += kept_r if temp > 0 else 0
+                if kept.value < 5:
+                    be.keep(kept.value)
+                assert H.ghost_position(m) == be.pos
+                tok = nxt.value
+    finally:
+        be.close()
+        H.ghost_reset(m, err, 512)   # (the conversation empty again for the tests after this one)
+
+
+def _accept_with_stream(O, rows, batch, temp, sp, u, pen, seen):
+    """go_accept_seen's rule with the given uniforms in place of a seeded stream: row by row, go_sample on the
+    penalised row (the oracle's own go_sample, pinned to the reference's Sampler)."""
+    rows = np.ascontiguousarray(rows, dtype=np.float32)
+    V = rows.shape[1]
+    seen = list(seen)
+    kept, samples = 1, []
+    for i in range(5):
+        r = rows[i].copy()
+        idx = np.array(seen, np.int64)
+        if pen != 0.0 and idx.size:
+            r[idx] = r[idx] - np.float32(pen)
+        y = O.go_sample(r.ctypes.data, V, sp.temperature, sp.top_p, sp.top_k, float(u[i]) if temp > 0 else 0.0)
+        samples.append(y)
+        if pen != 0.0 and y not in seen:
+            seen.append(y)
+        if i + 1 < 5 and y == batch[i + 1]:
+            kept += 1
+            continue
+        return kept, y, samples, seen
+    return kept, -1, samples, seen
 
 
 def test_host_state_file(env, tmp_path):

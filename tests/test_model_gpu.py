@@ -138,6 +138,45 @@ def test_accept_bit_exact(setup, temperature, top_p, top_k):
         assert be.pos == st.pos
 
 
+@pytest.mark.parametrize("temperature,top_p,top_k,penalty", [(0.0, 1.0, 0, 2.0), (0.0, 1.0, 0, -1.0),
+                                                              (0.7, 0.95, 20, 1.5), (1.0, 1.0, 0, 0.75)])
+def test_accept_presence_penalty(setup, temperature, top_p, top_k, penalty):
+    """gcuda_accept with geode_generate's presence penalty (engine/src/geode.cpp:234-255): the seen list holds the
+    oracle's greedy maxima of the batch's rows and random ids, the drafts are the oracle's penalised greedy samples;
+    the GPU's kept, next and samples equal the oracle's rule (go_accept_seen, pinned to the reference) on the GPU's own
+    logits bit for bit, and the penalty is seen to move a greedy sample."""
+    shape, ora, be, st, rng = setup
+    O = op.oracle_lib()
+    V = shape.vocab
+    moved = False
+    for rep in range(3):
+        t0 = int(rng.integers(0, V))
+        lg = ora.forward(st.copy(), [t0] + [int(t) for t in rng.integers(0, V, 4)], logits=True)["logits"]
+        seen = list(dict.fromkeys([int(np.argmax(lg[i])) for i in range(2)] +
+                                  [int(t) for t in rng.choice(V, 30, replace=False)]))
+        toks = np.array([t0, 0, 0, 0, 0], np.int32)
+        toks[1:] = rng.integers(0, V, 4)
+        op.plant_penalized_drafts(lg, toks, seen, penalty, int(rng.integers(0, 5)))
+        before = st.copy()
+        got, _ = be.verify(toks, logits=True)
+        seed = int(rng.integers(0, 2 ** 31))
+        u = op.oracle_uniforms(O, seed, 5)
+        kept, nxt, samples = be.accept(temperature, top_p, top_k, uniforms=u, presence_penalty=penalty, seen=seen)
+        ref_kept, ref_next, ref_samples, _ = op.accept_seen(O, got, toks, temperature, top_p, top_k, seed, penalty,
+                                                            seen)
+        assert kept == ref_kept and nxt == ref_next and np.array_equal(samples, ref_samples), \
+            (kept, ref_kept, nxt, ref_next, samples, ref_samples)
+        if temperature == 0.0:
+            moved |= any(samples[i] != int(np.argmax(got[i])) for i in range(kept))
+        if kept < 5:
+            be.keep(kept)
+        st.__dict__.update(before.copy().__dict__)
+        ora.forward(st, toks[:kept], logits=False)
+        assert be.pos == st.pos
+    if temperature == 0.0 and penalty > 0:
+        assert moved, "the penalty never changed a greedy sample: the test does not exercise it"
+
+
 @pytest.mark.parametrize("mode", ["greedy", "reject"])
 def test_device_loop_step(setup, mode):
     """The device-resident step (gcuda_step_device: graph, greedy acceptance, decision, rollback on the device; and

@@ -87,6 +87,20 @@ def test_golden_accept(O):
         assert kept == g["kept"][case] and nxt.value == g["next"][case] and np.array_equal(samples, g["samples"][case])
 
 
+def test_golden_accept_seen(O):
+    """The acceptance with geode_generate's presence penalty (engine/src/geode.cpp:234-255) against the reference's
+    outcomes: kept, next, every row's sample and the answer's seen list after the step, bit for bit."""
+    g = _golden("accept_seen.npz")
+    for case in range(g["params"].shape[0]):
+        T, P, K, seed, pen = g["params"][case]
+        seen = g["seen"][case][: g["n_seen"][case]]
+        kept, nxt, samples, after = op.accept_seen(O, g["rows"][case], g["batch"][case], float(T), float(P), int(K),
+                                                   int(seed), float(pen), seen)
+        assert kept == g["kept"][case] and nxt == g["next"][case], case
+        assert np.array_equal(samples, g["samples"][case]), case
+        assert np.array_equal(after, g["seen_out"][case][: g["n_seen_out"][case]]), case
+
+
 @pytest.mark.parametrize("name", ["model_moe", "model_dense"])
 def test_golden_model(name):
     """The whole verify pass (forward_batch over a prompt, then 5 rows with every logit) on the committed tiny pack
@@ -198,6 +212,28 @@ def test_ref_accept(R, O):
         k2 = O.go_accept(rows.ctypes.data, 5, V, batch.ctypes.data, T, P, K, C.c_uint64(seed), None, 0, C.byref(n2),
                          s2.ctypes.data)
         assert (k1, n1.value) == (k2, n2.value) and np.array_equal(s1, s2), case
+
+
+@ref_only
+def test_ref_accept_seen(R, O):
+    """The presence penalty's acceptance, oracle against the live reference build: greedy and sampled, positive and
+    negative penalties, seen lists holding rows' maxima, drafts planted as the penalised greedy samples."""
+    rng = np.random.default_rng(16)
+    V = 5000
+    for case in range(16):
+        rows = (rng.standard_normal((5, V)) * 3).astype(np.float32)
+        batch = rng.integers(0, V, 5).astype(np.int32)
+        seen = list(rng.choice(V, int(rng.integers(0, 40)), replace=False))
+        for i in range(min(len(seen), 4)):
+            seen[i] = int(np.argmax(rows[i]))
+        seen = list(dict.fromkeys(int(t) for t in seen))
+        pen = [2.0, -1.0, 0.5, 4.0][case % 4]
+        op.plant_penalized_drafts(rows, batch, seen, pen, case % 5)
+        T, P, K = [(0.0, 1.0, 0), (0.7, 0.95, 20), (0.0, 1.0, 0), (1.3, 0.8, 40)][case % 4]
+        seed = int(rng.integers(0, 2 ** 40))
+        a = op.accept_seen(R, rows, batch, T, P, K, seed, pen, seen, fn="ref_accept_seen")
+        b = op.accept_seen(O, rows, batch, T, P, K, seed, pen, seen)
+        assert a[:2] == b[:2] and np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3]), case
 
 
 @ref_only

@@ -69,11 +69,11 @@ def test_accept_rule_full_vocab(temperature, top_p, top_k):
     V = 248320
     rng = np.random.default_rng(int(temperature * 10) + top_k)
     R, O = op.reference_lib(), op.oracle_lib()
-    for case in range(4):
+    for case in range(5):
         rows = (rng.standard_normal((5, V), dtype=np.float32) * 3).astype(np.float32)
         batch = np.zeros(5, np.int32)
         batch[0] = rng.integers(0, V)
-        stand = case % 5
+        stand = case   # 0..4 greedy drafts planted (4: every draft stands, the bonus token is row 4's sample)
         for i in range(4):
             batch[i + 1] = int(np.argmax(rows[i])) if i < stand else int(rng.integers(0, V))
         seed = int(rng.integers(0, 2 ** 31))
@@ -85,3 +85,23 @@ def test_accept_rule_full_vocab(temperature, top_p, top_k):
                                     C.c_uint64(seed), None, 0, C.byref(nxt), samples.ctypes.data)
             out.append((kept, nxt.value, samples.tolist()))
         assert out[0] == out[1], (case, out)
+
+
+@pytest.mark.parametrize("temperature,top_p,top_k", [(0.0, 1.0, 0), (0.7, 0.95, 20)])
+def test_accept_presence_full_vocab(temperature, top_p, top_k):
+    """geode_generate's presence penalty (engine/src/geode.cpp:234-255) at the full vocabulary, 248320: the oracle's
+    kept count, next token, samples and seen list after the step equal the reference's. The seen lists hold rows'
+    maxima and 200 other ids; the drafts are the penalised greedy samples (every count 0..4 of them)."""
+    V = 248320
+    rng = np.random.default_rng(33 + top_k)
+    R, O = op.reference_lib(), op.oracle_lib()
+    for case in range(5):
+        rows = (rng.standard_normal((5, V), dtype=np.float32) * 3).astype(np.float32)
+        batch = rng.integers(0, V, 5).astype(np.int32)
+        seen = [int(np.argmax(rows[i])) for i in range(4)] + [int(t) for t in rng.choice(V, 200, replace=False)]
+        seen = list(dict.fromkeys(seen))
+        op.plant_penalized_drafts(rows, batch, seen, 1.5, case)
+        seed = int(rng.integers(0, 2 ** 31))
+        a = op.accept_seen(R, rows, batch, temperature, top_p, top_k, seed, 1.5, seen, fn="ref_accept_seen")
+        b = op.accept_seen(O, rows, batch, temperature, top_p, top_k, seed, 1.5, seen)
+        assert a[:2] == b[:2] and np.array_equal(a[2], b[2]) and np.array_equal(a[3], b[3]), (case, a, b)
