@@ -38,6 +38,8 @@ def cuda_lib() -> C.CDLL:
         "gcuda_op_route_out_bytes": (sz, []),
         "gcuda_op_route_union": (i32, [vp, i32, i32, i32, vp, sz, vp]),
         "gcuda_op_greedy_verify": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, vp]),
+        "gcuda_op_norm_quant": (i32, [vp, i32, i32, vp, f32, vp, vp, vp, vp, vp]),
+        "gcuda_debug_expf_table": (i32, [C.c_uint32, i64, vp, vp]),
     }
     for name, (res, args) in sig.items():
         if hasattr(L, name):

@@ -58,6 +58,8 @@ def _sig(L):
         "gcuda_launches": (C.c_uint64, [vp]),
         "gcuda_debug_read": (i32, [vp, i32, vp, sz]),
         "gcuda_debug_step_eager": (i32, [vp, vp, i32, i32]),
+        "gcuda_debug_trace": (i32, [vp, vp, i32, vp, vp, vp, vp, vp, vp]),
+        "gcuda_debug_expf_table": (i32, [C.c_uint32, i64, vp, vp]),
         "gcuda_synth_q4": (i32, [vp, i64, i64, f32, C.c_uint64]),
         "gcuda_ep_unique_id": (i32, [vp]),
         "gcuda_set_ep": (i32, [vp, i32, i32, vp]),
@@ -254,6 +256,25 @@ class Backend:
         self._rc(self.L.gcuda_accept(self.g, C.addressof(sp), _ptr(u), _ptr(st), len(stops), _ptr(sn), len(seen),
                                      C.byref(kept), C.byref(nxt), _ptr(samples)), "accept")
         return kept.value, nxt.value, samples
+
+    def trace(self, toks):
+        """One step with the per-layer trace (gcuda_debug_trace): x [L+1][n][H]; for MoE models router_logits
+        [L][n][E+1], ids / weights [L][n][K], gate [L][n], n_union [L]. The logits stay on the device."""
+        toks = np.ascontiguousarray(np.asarray(toks, dtype=np.int32))
+        sh = self.shape
+        n, L_, H = len(toks), sh.n_layers, sh.hidden
+        out = {"x": np.zeros((L_ + 1, n, H), np.float32)}
+        moe = sh.n_experts > 0 and not sh.dense
+        if moe:
+            E, K = sh.n_experts, sh.top_k
+            out.update(router_logits=np.zeros((L_, n, E + 1), np.float32), ids=np.zeros((L_, n, K), np.int32),
+                       weights=np.zeros((L_, n, K), np.float32), gate=np.zeros((L_, n), np.float32),
+                       n_union=np.zeros(L_, np.int32))
+        p = (lambda k: _ptr(out[k]) if moe else None)
+        self._rc(self.L.gcuda_debug_trace(self.g, _ptr(toks), n, _ptr(out["x"]), p("router_logits"), p("ids"),
+                                          p("weights"), p("gate"), p("n_union")), "debug_trace")
+        self._last_n = n
+        return out
 
     def randomize_state(self, pos: int, seed: int = 1):
         self._rc(self.L.gcuda_state_randomize(self.g, pos, C.c_uint64(seed)), "state_randomize")

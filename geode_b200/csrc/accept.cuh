@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample_rows(SampleArgs a) {
     const int k = min(a.V, a.top_k > 0 ? a.top_k : kMaxCand);
     row_topk(row, a.V, k, cv, ci, hist, misc);
     const float mx = cv[0];
-    for (int i = tid; i < k; i += blockDim.x) ev[i] = static_cast<double>(expf_cr(__fdiv_rn(__fsub_rn(cv[i], mx), a.temperature)));
+    for (int i = tid; i < k; i += blockDim.x) ev[i] = static_cast<double>(expf_ref(__fdiv_rn(__fsub_rn(cv[i], mx), a.temperature)));
     __syncthreads();
     if (tid == 0) {
         double sum = 0.0;

@@ -137,6 +137,10 @@ struct gcuda {
     int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
     size_t rej_cap = 0;
     int *d_rej_step = nullptr;      // gcuda_step_device_reject's result: accepted, next
+    // gcuda_debug_trace: per-layer copies enqueued inside one eager step (null outside it)
+    float *tr_x = nullptr;          // [n_layers + 1][n][H]: each layer's input x, then the last layer's output
+    float *tr_rlog = nullptr;       // [n_layers][n][E + 1]: the router's logits (and the shared expert's gate logit)
+    RouteOut *tr_route = nullptr;   // [n_layers]
     int *d_seen = nullptr;          // gcuda_accept's presence-penalty list on the device (grown on demand)
     size_t seen_cap = 0;
     std::vector<uint8_t> seen_mark; // (a host bitmap over the vocabulary, all zero between calls)
@@ -295,9 +299,13 @@ int enqueue_step(gcuda *g, int n) {
         return t ? static_cast<const float *>(t->d) : nullptr;
     };
     RC_OK(norm(raw(g->layers[0].in_norm), false, g->hf));
+    const size_t xrows = static_cast<size_t>(n) * H;
     for (int l = 0; l < s.n_layers; ++l) {
         const gcuda_layer &L = g->layers[static_cast<size_t>(l)];
         const LayerPlan &P = g->plan[static_cast<size_t>(l)];
+        if (g->tr_x)
+            LAUNCH_OK(cudaMemcpyAsync(g->tr_x + static_cast<size_t>(l) * xrows, g->x, xrows * sizeof(float),
+                                      cudaMemcpyDeviceToDevice, g->st));
         if (!L.attn) {
             // the a|b product (the recurrence's gates) on the side stream, beside the input product and the conv
             LAUNCH_OK(cudaEventRecord(g->fork_ev, g->st));
@@ -436,6 +444,12 @@ int enqueue_step(gcuda *g, int n) {
             LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(kRouteThreads), kMaxTok * E * sizeof(float), g->st, pdl,
                                 static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum,
                                 g->ep_rank, g->ep_world));
+            if (g->tr_route) {
+                LAUNCH_OK(cudaMemcpyAsync(g->tr_route + l, g->route, sizeof(RouteOut), cudaMemcpyDeviceToDevice, g->st));
+                LAUNCH_OK(cudaMemcpyAsync(g->tr_rlog + static_cast<size_t>(l) * n * (E + 1), g->rlog,
+                                          static_cast<size_t>(n) * (E + 1) * sizeof(float), cudaMemcpyDeviceToDevice,
+                                          g->st));
+            }
             if (g->ep_world > 1)   // (rows of picks other ranks compute stay zero for the all-reduce)
                 LAUNCH_OK(cudaMemsetAsync(g->eout, 0, static_cast<size_t>(n) * s.top_k * H * sizeof(float), g->st));
             const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
@@ -490,6 +504,9 @@ int enqueue_step(gcuda *g, int n) {
             RC_OK(norm(next_norm, true, next_hf));
         }
     }
+    if (g->tr_x)
+        LAUNCH_OK(cudaMemcpyAsync(g->tr_x + static_cast<size_t>(s.n_layers) * xrows, g->x, xrows * sizeof(float),
+                                  cudaMemcpyDeviceToDevice, g->st));
     // the logits of every row (engine/src/model.cpp:5397-5410): hq holds rmsnorm(x, final_norm) quantized
     RC_OK(launch_units(g, g->lm_u, static_cast<int>((s.vocab + 31) / 32), g->hq, n, pdl));
     return GCUDA_OK;
@@ -1196,6 +1213,64 @@ int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl) {
     g->pdl = keep;
     if (rc != GCUDA_OK) return rc;
     RC_OK(check_status(g));
+    g->pos += n;
+    g->last_batch = n;
+    return GCUDA_OK;
+}
+
+// Tests: one eager step with per-layer copies (the reference's LayerTrace, engine/src/model.hpp:92-105): x, the
+// router's logits and its routing per layer; the step otherwise as gcuda_verify's (position and batch advance).
+int gcuda_debug_trace(gcuda *g, const int *toks, int n, float *x, float *router_logits, int *ids, float *weights,
+                      float *gate, int *n_union) {
+    if (!g || !g->ready || !toks || !x || n < 1 || n > g->sh.max_tokens) return GCUDA_E_ARG;
+    const gcuda_shape &s = g->sh;
+    if (g->pos + n > s.context) return fail(g, GCUDA_E_ARG, "trace: past the context");
+    for (int i = 0; i < n; ++i)
+        if (toks[i] < 0 || toks[i] >= s.vocab) return fail(g, GCUDA_E_ARG, "trace: a token id out of range");
+    cudaSetDevice(g->device);
+    const bool moe = !s.dense && s.n_experts > 0;
+    const size_t L = static_cast<size_t>(s.n_layers), H = static_cast<size_t>(s.hidden), E1 = static_cast<size_t>(s.n_experts) + 1;
+    const size_t xbytes = (L + 1) * n * H * sizeof(float), rbytes = L * n * E1 * sizeof(float);
+    void *bx = nullptr, *br = nullptr, *bt = nullptr;
+    if (cudaMalloc(&bx, xbytes) != cudaSuccess ||
+        (moe && (cudaMalloc(&br, rbytes) != cudaSuccess || cudaMalloc(&bt, L * sizeof(RouteOut)) != cudaSuccess))) {
+        cudaFree(bx);
+        cudaFree(br);
+        return fail(g, GCUDA_E_MEMORY, "trace: cudaMalloc");
+    }
+    g->tr_x = static_cast<float *>(bx);
+    g->tr_rlog = static_cast<float *>(br);
+    g->tr_route = static_cast<RouteOut *>(bt);
+    int rc = GCUDA_OK;
+    if (cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st) != cudaSuccess ||
+        cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st) != cudaSuccess)
+        rc = GCUDA_E_CUDA;
+    if (rc == GCUDA_OK) rc = enqueue_step(g, n);
+    if (rc == GCUDA_OK) rc = check_status(g);
+    std::vector<RouteOut> ro(moe ? L : 0);
+    if (rc == GCUDA_OK && (cudaMemcpy(x, bx, xbytes, cudaMemcpyDeviceToHost) != cudaSuccess ||
+                           (moe && cudaMemcpy(ro.data(), bt, L * sizeof(RouteOut), cudaMemcpyDeviceToHost) != cudaSuccess) ||
+                           (moe && router_logits && cudaMemcpy(router_logits, br, rbytes, cudaMemcpyDeviceToHost) != cudaSuccess)))
+        rc = GCUDA_E_CUDA;
+    g->tr_x = nullptr;
+    g->tr_rlog = nullptr;
+    g->tr_route = nullptr;
+    cudaFree(bx);
+    cudaFree(br);
+    cudaFree(bt);
+    if (rc != GCUDA_OK) return rc;
+    const int K = s.top_k;
+    for (size_t l = 0; l < ro.size(); ++l) {
+        for (int t = 0; t < n; ++t) {
+            for (int k = 0; k < K; ++k) {
+                if (ids) ids[(l * n + t) * K + k] = ro[l].ids[t * K + k];
+                if (weights) weights[(l * n + t) * K + k] = ro[l].w[t * K + k];
+            }
+            if (gate) gate[l * n + t] = ro[l].gs[t];
+        }
+        if (n_union) n_union[l] = ro[l].n_union;
+    }
+    std::memcpy(g->last_toks, toks, sizeof(int) * n);
     g->pos += n;
     g->last_batch = n;
     return GCUDA_OK;

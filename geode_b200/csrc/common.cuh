@@ -135,10 +135,47 @@ __device__ __forceinline__ float fast_exp_exact(float x) {
     return __uint_as_float(bits);
 }
 __device__ __forceinline__ float silu_fast_exact(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, fast_exp_exact(-x))); }
-// expf rounded once from a double exp: the correctly rounded value in all but vanishingly rare cases (glibc's expf
-// is too)
-__device__ __forceinline__ float expf_cr(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
-__device__ __forceinline__ float sigmoid_cr(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cr(-x))); }
-__device__ __forceinline__ float silu_cr(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x))); }
+// The reference's float exp is glibc's expf (std::exp on a float, in route_topk's softmax, the Sampler's weights, the
+// Gated DeltaNet's gates, silu and sigmoid). glibc's expf is not correctly rounded: a double exp rounded to float
+// differs from it on 170 648 of the 2^32 inputs. expf_ref restates glibc's algorithm instead (the ARM
+// optimized-routines expf by Szabolcs Nagy, in glibc since 2.27): x * 32/ln2 = k + r with k the nearest integer,
+// 2^(k/32) from a 32-entry table of 2^(i/32) (each entry the double nearest 2^(i/32), its exponent field less i << 47,
+// computed to 80 digits for this file), 2^(r/32) by a cubic in double precision, the product rounded once to float;
+// the multiply-adds fused, as in glibc's FMA build. It equals glibc's expf on all 2^32 inputs (checked on the host and
+// on the device against the host's glibc by the tests).
+__constant__ uint64_t kExp2Table[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+__device__ __forceinline__ float expf_ref(float x) {
+    const uint32_t ux = __float_as_uint(x);
+    if (((ux >> 20) & 0x7ffu) >= 0x42bu) {   // |x| >= 88: the ends of the range
+        if (ux == 0xff800000u) return 0.0f;                  // -inf
+        if (((ux >> 20) & 0x7ffu) >= 0x7f8u) return __fadd_rn(x, x);   // +inf, NaN
+        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);       // overflows
+        if (x < -0x1.9fe368p6f) return 0.0f;                             // underflows to zero
+    }
+    constexpr double kInvLn2x32 = 0x1.71547652b82fep+0 * 32.0;
+    constexpr double kShift = 0x1.8p+52;   // (adding it rounds to an integer in the low mantissa bits)
+    constexpr double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0, c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0,
+                     c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double xd = static_cast<double>(x);
+    double kd = __fma_rn(kInvLn2x32, xd, kShift);
+    const uint64_t ki = static_cast<uint64_t>(__double_as_longlong(kd));
+    kd = __dsub_rn(kd, kShift);
+    const double r = __fma_rn(kInvLn2x32, xd, -kd);
+    const double s = __longlong_as_double(static_cast<long long>(kExp2Table[ki & 31u] + (ki << 47)));
+    const double z = __fma_rn(c0, r, c1);
+    const double r2 = __dmul_rn(r, r);
+    const double y = __fma_rn(z, r2, __fma_rn(c2, r, 1.0));
+    return __double2float_rn(__dmul_rn(y, s));
+}
+__device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_ref(-x))); }
+__device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))); }
 
 }  // namespace gcu

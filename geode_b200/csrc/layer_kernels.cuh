@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     const bool gate = gt >= 0 && gt < n;
     float nAe = 0.0f, dtb = 0.0f;
     if (gate) {
-        nAe = -expf_cr(a.A_log[vh]);
+        nAe = -expf_ref(a.A_log[vh]);
         dtb = a.dt_bias[vh];
     }
     const int jj = lane & 15;
@@ -294,10 +294,10 @@ __global__ void __launch_bounds__(128) k_gdn(GdnArgs a) {
     if (warp == 3) {
         // gates (engine/src/model.cpp:3604-3611): beta = sigmoid(b), decay = exp(-exp(A_log) * softplus(a + dt_bias))
         if (gate) {
-            s_beta[gt] = sigmoid_cr(bv);
+            s_beta[gt] = sigmoid_ref(bv);
             const float x = __fadd_rn(av, dtb);
-            const float sp = x > 20.0f ? x : static_cast<float>(log1p(exp(static_cast<double>(x))));
-            s_decay[gt] = expf_cr(__fmul_rn(nAe, sp));
+            const float sp = x > 20.0f ? x : static_cast<float>(log1p(static_cast<double>(expf_ref(x))));
+            s_decay[gt] = expf_ref(__fmul_rn(nAe, sp));
         }
     } else {
         // 2. q, k L2-normalised over dk (eps 1e-6), q times 1/sqrt(dk): warp w < 3 takes tokens w, w + 3 (q and k
@@ -852,7 +852,7 @@ __global__ void k_attn_merge(MergeArgs a) {
         }
     }
     const float *gate = a.qg + (static_cast<size_t>(t) * a.nh + h) * 2 * a.hd + a.hd;
-    const float v = __fmul_rn(__fmul_rn(acc, 1.0f / L), sigmoid_cr(gate[d]));
+    const float v = __fmul_rn(__fmul_rn(acc, 1.0f / L), sigmoid_ref(gate[d]));
     const int col = h * a.hd + d;
     if (a.core_f) a.core_f[static_cast<size_t>(t) * W + col] = v;
     float amax = fabsf(v);
@@ -918,8 +918,8 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict
         float mx = -INFINITY;
         for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
         mx = warp_max(mx);
-        for (int e = lane + 32 * q; e < E; e += 32 * kRouteWarpsPerTok) p[e] = expf_cr(__fsub_rn(row[e], mx));
-        if (q == 1 && lane == 0) out->gs[t] = sigmoid_cr(row[E]);
+        for (int e = lane + 32 * q; e < E; e += 32 * kRouteWarpsPerTok) p[e] = expf_ref(__fsub_rn(row[e], mx));
+        if (q == 1 && lane == 0) out->gs[t] = sigmoid_ref(row[E]);
     }
     __syncthreads();
     if (live && q == 0) {

@@ -11,6 +11,15 @@
 
 using namespace gcu;
 
+namespace gcu {
+// out[i] = expf_ref of the float whose bits are first + i (the test hook gcuda_debug_expf_table)
+__global__ void k_expf_table(uint32_t first, int64_t count, float *out) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        out[i] = expf_ref(__uint_as_float(first + static_cast<uint32_t>(i)));
+}
+}  // namespace gcu
+
 extern "C" {
 
 size_t gcuda_op_q4_tiled_bytes(int64_t rows, int64_t cols) {
@@ -90,6 +99,34 @@ int gcuda_op_route_union(const float *d_logits, int n, int E, int K, void *d_out
         return GCUDA_E_ARG;
     k_route<<<1, kRouteThreads, kMaxTok * E * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
         d_logits, n, E, K, static_cast<RouteOut *>(d_out), nullptr, 0, 1);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_norm_quant(const float *d_x, int n, int H, const float *d_w, float eps, float *d_hf, int8_t *d_q,
+                        float *d_scale, int32_t *d_bsum, void *stream) {
+    if (!d_x || !d_w || !d_q || !d_scale || !d_bsum || n < 1 || H < 16 || H % 16 || H > kNormThreads * kNormPer)
+        return GCUDA_E_ARG;
+    NormArgs a{};
+    a.x = const_cast<float *>(d_x);   // (read only: the combine, which writes x, is off)
+    a.w = d_w;
+    a.eps = eps;
+    a.H = H;
+    a.n = n;
+    a.hf = d_hf;
+    a.q = d_q;
+    a.scale = d_scale;
+    a.bsum = d_bsum;
+    return launch_ex(k_norm_quant, dim3(n), dim3(kNormThreads), 0, static_cast<cudaStream_t>(stream), false, a) ==
+                   cudaSuccess
+               ? GCUDA_OK
+               : GCUDA_E_CUDA;
+}
+
+int gcuda_debug_expf_table(uint32_t first, int64_t count, float *d_out, void *stream) {
+    if (!d_out || count < 1 || static_cast<uint64_t>(first) + static_cast<uint64_t>(count) > (1ull << 32))
+        return GCUDA_E_ARG;
+    k_expf_table<<<148 * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(first, count, d_out);
     count_launch();
     return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }

@@ -101,8 +101,8 @@ __device__ __forceinline__ void epi_store(const GemvUnit &U, const float (&y0)[4
         for (int h = 0; h < 2; ++h) {
             const int t = 2 * tig + h;
             const bool on = ((U.tok_mask >> t) & 1) != 0;
-            const float a0 = __fmul_rn(silu_cr(y0[h]), y1[h]);
-            const float a1 = __fmul_rn(silu_cr(y0[2 + h]), y1[2 + h]);
+            const float a0 = __fmul_rn(silu_ref(y0[h]), y1[h]);
+            const float a1 = __fmul_rn(silu_ref(y0[2 + h]), y1[2 + h]);
             const Quant16 r = quant16_lanes(on ? a0 : 0.0f, on ? a1 : 0.0f);
             if (!on) continue;
             const size_t slot = static_cast<size_t>(U.slot[t]);

@@ -124,7 +124,7 @@ __device__ inline void route_row(const float *__restrict__ logits, int E, int K,
     float mx = -INFINITY;
     for (int e = lane; e < E; e += 32) mx = fmaxf(mx, logits[e]);
     mx = warp_max(mx);
-    for (int e = lane; e < E; e += 32) p[e] = expf_cr(__fsub_rn(logits[e], mx));
+    for (int e = lane; e < E; e += 32) p[e] = expf_ref(__fsub_rn(logits[e], mx));
     __syncwarp();
     float sum = 0.0f;
     if (lane == 0) {   // in expert order; the loads four at a time, issued ahead of the adds

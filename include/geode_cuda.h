@@ -186,7 +186,18 @@ int gcuda_state_randomize(gcuda *g, int pos, uint64_t seed);
  * 3 route, 4 hidden, 5 conv output, 6 a|b, 7 z, 8 qkv product); gcuda_debug_step_eager: the step launched kernel by
  * kernel instead of through the graph (pdl 0/1). */
 int gcuda_debug_read(gcuda *g, int what, void *out, size_t bytes);
+/* The kernels' float exp (the reference's: glibc's expf, restated) of the floats whose bit patterns are first ..
+ * first + count - 1, into d_out [count] on `stream`: for checking it against the host's expf. */
+int gcuda_debug_expf_table(uint32_t first, int64_t count, float *d_out, void *stream);
 int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl);
+/* One step as gcuda_verify (position and batch advance; logits left on the device) launched kernel by kernel with a
+ * per-layer trace, the reference's LayerTrace (engine/src/model.hpp:92-105): x [n_layers + 1][n][hidden] (each layer's
+ * input, then the last layer's output); for MoE models (else untouched; each may be NULL) router_logits
+ * [n_layers][n][n_experts + 1] (the router's logits, then the shared expert's gate logit), ids and weights
+ * [n_layers][n][top_k] (route_topk's picks), gate [n_layers][n] (the shared expert's sigmoid gate) and n_union
+ * [n_layers] (distinct experts picked). */
+int gcuda_debug_trace(gcuda *g, const int *toks, int n, float *x, float *router_logits, int *ids, float *weights,
+                      float *gate, int *n_union);
 
 /* ------------------------------------------------------------------------------------------- operators ---- */
 /* All on caller-owned device memory, enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
@@ -198,6 +209,12 @@ int gcuda_op_q4_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint
 /* quantize_activation for n rows of cols floats (engine/src/kernels.cpp:1254-1295): q [n][cols], scale and bsum
  * [n][cols/16] */
 int gcuda_op_quantize(const float *d_x, int n, int cols, int8_t *d_q, float *d_scale, int32_t *d_bsum, void *stream);
+/* The step's norm-and-quantize kernel for n rows of H floats: hf = rmsnorm(x, w) with the zero-centred weight (1 + w)
+ * and the sum of squares in double (engine/src/kernels.cpp:1520-1529), then quantize_activation of hf
+ * (engine/src/kernels.cpp:1254-1295): hf [n][H] (NULL: not written), q [n][H], scale and bsum [n][H/16]. H a multiple
+ * of 16, at most 4096. */
+int gcuda_op_norm_quant(const float *d_x, int n, int H, const float *d_w, float eps, float *d_hf, int8_t *d_q,
+                        float *d_scale, int32_t *d_bsum, void *stream);
 /* y[t][r] = matvec_rows_q_ref (engine/src/kernels.cpp:1304-1322) of the tiled matrix with n (<= 8) quantized rows;
  * bit for bit the reference's int8 product. y [n][rows]. */
 int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float global, const int8_t *d_q,

@@ -1091,3 +1091,115 @@ int go_spec_reject(const float *target, const float *draft, int n_drafts, int V,
     free(qp);
     return accepted;
 }
+
+/* ------------------------------------------------------------------ the exp premise (test infrastructure) ---- */
+
+/* The kernels stand in (float)exp((double)x) for the reference's float exp (std::exp on a float calls glibc's
+ * expf): in route_topk's softmax (engine/src/model.cpp:4021-4065), the Sampler's weights (engine/src/sampler.cpp:
+ * 16-50), the Gated DeltaNet's decay and the SwiGLU / sigmoid gates. These count, over float bit patterns, where that
+ * stand-in differs from glibc's expf - computed here on the host (go_expf_mismatch) or read from a table the device
+ * computed (go_expf_check_table). Two NaNs count as equal; every other pair is compared bit for bit. The first `cap`
+ * differing patterns go to first[]. */
+/* glibc's expf restated (the ARM optimized-routines expf by Szabolcs Nagy, in glibc since 2.27; the multiply-adds
+ * fused as in glibc's FMA build): x * 32/ln2 = k + r, 2^(k/32) from a table of 2^(i/32) (the double nearest each,
+ * its exponent field less i << 47), 2^(r/32) by a cubic in double, one rounding to float. The kernels' expf_ref is
+ * the same sequence. */
+static const uint64_t go_exp2_table[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull};
+
+float go_expf_restated(float x) {
+    uint32_t ux;
+    memcpy(&ux, &x, 4);
+    const uint32_t top = (ux >> 20) & 0x7ffu;
+    if (top >= 0x42bu) {
+        if (ux == 0xff800000u) return 0.0f;
+        if (top >= 0x7f8u) return x + x;
+        if (x > 0x1.62e42ep6f) return INFINITY;
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    const double inv_ln2_32 = 0x1.71547652b82fep+0 * 32.0, shift = 0x1.8p+52;
+    const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0, c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0,
+                 c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double xd = (double)x;
+    double kd = fma(inv_ln2_32, xd, shift);
+    uint64_t ki;
+    memcpy(&ki, &kd, 8);
+    kd -= shift;
+    const double r = fma(inv_ln2_32, xd, -kd);
+    const uint64_t t = go_exp2_table[ki & 31u] + (ki << 47);
+    double s;
+    memcpy(&s, &t, 8);
+    const double z = fma(c0, r, c1);
+    const double y = fma(z, r * r, fma(c2, r, 1.0));
+    return (float)(y * s);
+}
+
+typedef struct {
+    uint64_t lo, hi;
+    const float *vals;   /* NULL: computed here (restated: go_expf_restated, else (float)exp((double)x)) */
+    int restated;
+    uint64_t count;
+    uint32_t first[16];
+    int nfirst;
+} expf_job;
+
+static void *expf_run(void *p) {
+    expf_job *j = (expf_job *)p;
+    for (uint64_t b = j->lo; b < j->hi; ++b) {
+        const uint32_t bits = (uint32_t)b;
+        float x;
+        memcpy(&x, &bits, 4);
+        const float want = expf(x);
+        const float got = j->vals ? j->vals[b - j->lo] : j->restated ? go_expf_restated(x) : (float)exp((double)x);
+        uint32_t wb, gb;
+        memcpy(&wb, &want, 4);
+        memcpy(&gb, &got, 4);
+        if (wb != gb && !(want != want && got != got)) {
+            if (j->nfirst < 16) j->first[j->nfirst++] = bits;
+            ++j->count;
+        }
+    }
+    return NULL;
+}
+
+static uint64_t expf_sweep(uint64_t lo, uint64_t n, const float *vals, int restated, int threads, uint32_t *first,
+                           int cap) {
+    if (threads < 1) threads = 1;
+    if (threads > 64) threads = 64;
+    expf_job jobs[64];
+    pthread_t th[64];
+    int started[64];
+    for (int t = 0; t < threads; ++t) {
+        jobs[t].lo = lo + n * (uint64_t)t / (uint64_t)threads;
+        jobs[t].hi = lo + n * (uint64_t)(t + 1) / (uint64_t)threads;
+        jobs[t].vals = vals ? vals + (jobs[t].lo - lo) : NULL;
+        jobs[t].restated = restated;
+        jobs[t].count = 0;
+        jobs[t].nfirst = 0;
+        started[t] = pthread_create(&th[t], NULL, expf_run, &jobs[t]) == 0;
+        if (!started[t]) expf_run(&jobs[t]);
+    }
+    uint64_t total = 0;
+    int k = 0;
+    for (int t = 0; t < threads; ++t) {
+        if (started[t]) pthread_join(th[t], NULL);
+        total += jobs[t].count;
+        for (int i = 0; i < jobs[t].nfirst && k < cap; ++i) first[k++] = jobs[t].first[i];
+    }
+    return total;
+}
+
+uint64_t go_expf_mismatch(uint64_t lo, uint64_t hi, int restated, int threads, uint32_t *first, int cap) {
+    return hi > lo ? expf_sweep(lo, hi - lo, NULL, restated, threads, first, cap) : 0;
+}
+
+uint64_t go_expf_check_table(uint64_t lo, uint64_t n, const float *vals, int threads, uint32_t *first, int cap) {
+    return expf_sweep(lo, n, vals, 0, threads, first, cap);
+}

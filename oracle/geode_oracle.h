@@ -139,6 +139,14 @@ int go_spec_reject(const float *target, const float *draft, int n_drafts, int V,
                    float temperature, float top_p, int top_k, uint64_t seed, uint64_t seq, int *next);
 void go_philox4x32(uint64_t key, uint64_t counter_hi, uint64_t counter_lo, uint32_t out[4]);
 
+/* The exp premise (test infrastructure): float bit patterns in [lo, hi) where glibc's expf(x) differs from
+ * go_expf_restated(x) (restated = 1) or from (float)exp((double)x) (restated = 0) (go_expf_mismatch), or from a
+ * device-computed table vals[n] for patterns lo.. (go_expf_check_table); NaNs equal; the first cap differing
+ * patterns in first[]. */
+float go_expf_restated(float x);
+uint64_t go_expf_mismatch(uint64_t lo, uint64_t hi, int restated, int threads, uint32_t *first, int cap);
+uint64_t go_expf_check_table(uint64_t lo, uint64_t n, const float *vals, int threads, uint32_t *first, int cap);
+
 #ifdef __cplusplus
 }
 #endif

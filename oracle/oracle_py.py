@@ -288,6 +288,12 @@ def oracle_lib():
     lib.go_accept_seen.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float, C.c_int,
                                    C.c_uint64, C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_void_p]
+    lib.go_expf_restated.restype = C.c_float
+    lib.go_expf_restated.argtypes = [C.c_float]
+    lib.go_expf_mismatch.restype = C.c_uint64
+    lib.go_expf_mismatch.argtypes = [C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_void_p, C.c_int]
+    lib.go_expf_check_table.restype = C.c_uint64
+    lib.go_expf_check_table.argtypes = [C.c_uint64, C.c_uint64, C.c_void_p, C.c_int, C.c_void_p, C.c_int]
     lib.go_spec_reject.restype = C.c_int
     lib.go_spec_reject.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float,
                                    C.c_int, C.c_uint64, C.c_uint64, C.c_void_p]

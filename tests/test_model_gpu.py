@@ -91,9 +91,19 @@ def test_state_roundtrip(setup):
     kv, kvs = np.zeros_like(kv_ref), np.zeros_like(kvs_ref)
     be.state_get(conv, gdn, kv, kvs, st.pos)
     assert np.allclose(conv, st.conv, rtol=1e-2, atol=1e-3)
-    assert np.allclose(gdn, st.gdn, rtol=5e-2, atol=5e-3)
-    # the int8 rows: equal, or one code apart where the GPU's float differs in the last bit before rounding
-    assert np.abs(kv.astype(np.int32) - kv_ref.astype(np.int32)).max() <= 2
+    # the recurrent states per (layer, value head), normwise: a wrong index in one head moves that head's state by
+    # about its own size; rounding-level differences carried through a few batches stay far below 1e-2
+    c = ora.cfg
+    if ora.n_gdn:
+        a = gdn.reshape(ora.n_gdn, c.gdn_v_heads, -1).astype(np.float64)
+        b = st.gdn.reshape(ora.n_gdn, c.gdn_v_heads, -1).astype(np.float64)
+        rel = np.linalg.norm(a - b, axis=-1) / np.maximum(np.linalg.norm(b, axis=-1), 1e-30)
+        assert rel.max() <= 1e-2, f"recurrent state per head: worst relative difference {rel.max():.2e}"
+    # the int8 rows: equal, or one code apart where the GPU's float differs in the last bits before rounding - and
+    # those rare
+    d = np.abs(kv.astype(np.int32) - kv_ref.astype(np.int32))
+    assert d.max() <= 1, f"KV codes {d.max()} apart"
+    assert np.count_nonzero(d) <= 1e-2 * d.size, f"{np.count_nonzero(d)} of {d.size} KV codes differ"
     assert np.allclose(kvs, kvs_ref, rtol=1e-2, atol=1e-6)
 
 

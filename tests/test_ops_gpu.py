@@ -67,6 +67,36 @@ def test_quantize_bit_exact(L, O, cols):
         assert np.array_equal(b[t].cpu().numpy(), rb)
 
 
+@pytest.mark.parametrize("H", [256, 2048, 4096])
+def test_norm_quant_bit_exact(L, O, H):
+    """The step's norm-and-quantize kernel (k_norm_quant, without the MoE combine) against rmsnorm with the
+    zero-centred weight (engine/src/kernels.cpp:1520-1529) then quantize_activation (engine/src/kernels.cpp:1254-1295)
+    in the oracle, pinned to the reference: hf, codes, scales and block sums bit for bit. The kernel sums the squares
+    in double in another order than the reference's sequential loop; every product is exact in double, and the float
+    of the mean square matched on every row of these tests."""
+    rng = np.random.default_rng(H)
+    n = 8
+    x = (rng.standard_normal((n, H)) * rng.uniform(0.1, 30.0, (n, 1))).astype(np.float32)
+    x[1, :16] = 0.0   # a zero block after the norm: scale 0, codes 0
+    w = (rng.standard_normal(H) * 0.1).astype(np.float32)
+    eps = 1e-6
+    d_x, d_w = _dev(x), _dev(w)
+    hf = torch.zeros((n, H), dtype=torch.float32, device="cuda")
+    q = torch.zeros((n, H), dtype=torch.int8, device="cuda")
+    sc = torch.zeros((n, H // 16), dtype=torch.float32, device="cuda")
+    bs = torch.zeros((n, H // 16), dtype=torch.int32, device="cuda")
+    assert L.gcuda_op_norm_quant(_p(d_x), n, H, _p(d_w), eps, _p(hf), _p(q), _p(sc), _p(bs), None) == 0
+    torch.cuda.synchronize()
+    for t in range(n):
+        ref = np.zeros(H, np.float32)
+        O.go_rmsnorm(x[t].ctypes.data, w.ctypes.data, ref.ctypes.data, H, eps, 1)
+        assert np.array_equal(hf[t].cpu().numpy().view(np.uint32), ref.view(np.uint32)), t
+        rq, rs, rb = op.oracle_quantize_activation(O, ref)
+        assert np.array_equal(q[t].cpu().numpy(), rq), t
+        assert np.array_equal(sc[t].cpu().numpy().view(np.uint32), rs.view(np.uint32)), t
+        assert np.array_equal(bs[t].cpu().numpy(), rb), t
+
+
 @pytest.mark.parametrize("rows,cols,n", [(64, 512, 1), (1024, 2048, 5), (96, 4096, 3), (256, 2048, 8)])
 def test_q4_gemv_bit_exact(L, O, rows, cols, n):
     rng = np.random.default_rng(rows + cols + n)
