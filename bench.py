@@ -126,23 +126,22 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------- the CPU path ----
-def cpu_reference(steps: int = 3, layers: int = 4, threads: int = 0) -> dict:
+def cpu_reference(steps: int = 5, warmup: int = 1, distinct: int = 4, threads: int = 0) -> dict:
     """The reference engine's own CPU verify path (oracle/_ref: Model::forward_batch with every row's logits, then the
-    acceptance rule around geode::Sampler) on a bounded sample of the cfg-3 workload: the same shapes (hidden 2048,
-    256 experts top-8, vocab 248320, the 8192-position int8 KV cache), `layers` of the 40 layers (3 GDN : 1 attention
-    as in the model). The per-step time is scaled to 40 layers from the reference's own stage timer: lm_head once,
-    the rest x 40 / layers."""
+    acceptance rule around geode::Sampler) on the cfg-3 workload at its full depth: the same shapes (hidden 2048,
+    40 layers, 256 experts top-8, vocab 248320, the 8192-position int8 KV cache). The pack holds `distinct` layers'
+    bytes (3 GDN : 1 attention) that the 40 layers name in turn (synth.write_pack's distinct_layers), so every layer
+    reads as many bytes as a distinct one (the 2.4 GB pack is far larger than the host's caches) while the pack is
+    written in seconds. `warmup` untimed steps (they read the routed experts in), then the median of `steps`."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle_py as op  # (the baseline leg only: the reference's code timed on the host)
     from geode_b200 import synth
 
     kind = "reference" if op.have_reference() else "port"
     shape = synth.baseline_shape(3)
-    shape.n_layers = layers
-    shape.layer_types = synth.hybrid_types(layers)
     threads = threads or os.cpu_count() or 1
     with tempfile.TemporaryDirectory() as d:
-        synth.write_pack(d, shape, seed=1, fill="random")
+        synth.write_pack(d, shape, seed=1, fill="random", distinct_layers=distinct)
         if kind != "reference":
             return {"kind": "port", "value": None, "unit": UNIT, "cores": 1,
                     "sample": "the reference build is missing: no CPU number"}
@@ -152,18 +151,12 @@ def cpu_reference(steps: int = 3, layers: int = 4, threads: int = 0) -> dict:
         op.write_long_state(os.path.join(d, "t.state"), os.path.join(d, "l.state"), CTX)
         lib = op.reference_lib()
         rng = np.random.default_rng(3)
-        times, heads = [], []
+        times = []
         import ctypes as C
 
-        def head_ms():
-            p = ref.profile()
-            i = p.index("lm_head ") + len("lm_head ")
-            return float(p[i:].split(" ")[0])
-
-        for it in range(steps + 1):
+        for it in range(warmup + steps):
             ref.load_state(os.path.join(d, "l.state"))
             toks = rng.integers(0, shape.vocab, NTOK).astype(np.int32)
-            h0 = head_ms()
             t0 = time.perf_counter()
             out = ref.forward(toks, all_logits=True)
             nxt = C.c_int(0)
@@ -171,17 +164,15 @@ def cpu_reference(steps: int = 3, layers: int = 4, threads: int = 0) -> dict:
             lib.ref_accept(out["logits"].ctypes.data, NTOK, shape.vocab, toks.ctypes.data, 0.0, 1.0, 0, C.c_uint64(1),
                            None, 0, C.byref(nxt), samples.ctypes.data)
             t1 = time.perf_counter()
-            if it > 0:   # (the first is the warm-up: it reads every routed expert into the cache)
+            if it >= warmup:
                 times.append(t1 - t0)
-                heads.append(head_ms() - h0)
         ref.close()
     t = statistics.median(times)
-    th = statistics.median(heads) / 1e3
-    t40 = th + (t - th) * 40 / layers
-    return {"kind": kind, "value": NTOK / t40, "unit": UNIT, "cores": threads,
-            "sample": f"{layers} of 40 layers (3 GDN : 1 attention) + lm_head, ctx {CTX}, greedy acceptance; median of "
-                      f"{steps} steps after 1 warm-up = {t * 1e3:.0f} ms (lm_head {th * 1e3:.0f} ms), scaled to 40 layers = "
-                      f"{t40 * 1e3:.0f} ms/step"}
+    return {"kind": kind, "value": NTOK / t, "unit": UNIT, "cores": threads, "steps": steps, "warmup": warmup,
+            "layers": shape.n_layers,
+            "sample": f"all 40 layers (3 GDN : 1 attention; {distinct} layers' bytes named in turn) + lm_head, ctx {CTX}, "
+                      f"5 rows, greedy acceptance; median of {steps} steps after {warmup} warm-up = {t * 1e3:.0f} ms/step "
+                      f"(state reloaded before each step)"}
 
 
 ACCEPT_METRIC = "acceptance rows/s (cfg5: 256 sequences x (8+1) rows, vocab 248320)"
@@ -256,16 +247,20 @@ def reference_arm(args):
                           "e2e": {"value": v, "unit": ACCEPT_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
                           "wall_s": time.perf_counter() - t0}))
         return 0
-    cb = cpu_reference(steps=max(1, min(args.steps, 3)))
+    # (each step about a second on 16 cores: at most 5 timed steps after 1 warm-up, so the run stays within minutes)
+    steps, warmup = max(1, min(args.steps, 5)), 1
+    cb = cpu_reference(steps=steps, warmup=warmup)
     if cb.get("value") is None:
         print(json.dumps({"impl": "reference", "unavailable": cb["sample"]}))
         return 0
     v = cb["value"]
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": NTOK / v * 1e3, "higher_is_better": True, "scaling": "weak",
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+            "warmup": warmup, "ms_per_step": NTOK / v * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q4xint8->f32", "data": "synthetic",
-            "config": {"workload": "cfg3: MoE 35B-A3B shape verify, 1+4 tokens, ctx 8192, greedy", "global_batch": NTOK,
-                       "seq_len": CTX, "parallelism": "cpu"},
+            "config": {"workload": "cfg3: MoE 35B-A3B shape verify (40 layers, 256 experts top-8 + shared, vocab "
+                                   "248320), 1 accepted + 4 drafts, ctx 8192, greedy acceptance", "global_batch": NTOK,
+                       "seq_len": CTX, "parallelism": "cpu", "layers": 40,
+                       "requested": {"steps": args.steps, "warmup": args.warmup}},
             "cpu_baseline": cb, "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": time.perf_counter() - t0}
     print(json.dumps(line))
@@ -313,6 +308,63 @@ def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
     return {"kernel": "k_gemv_static (q4 GEMV, lm_head 248320x2048, 5 rows)", "bound": "hbm", "achieved": ach,
             "peak": peak_gbs, "unit": "GB/s", "frac": ach / peak_gbs, "traffic": LMHEAD_TRAFFIC, "ms": ms,
             "algorithmic_bytes": alg, "traffic_source": "ncu, profiles/k_gemv_static_lmhead_cfg3.md"}
+
+
+KT_NAMES = ["gate_up", "down", "lm_head", "dense"]
+# ncu figures of the dominant kernel, per launch (the capture's command and numbers: this file)
+GATEUP_PROFILE = os.path.join(ROOT, "profiles", "k_gemv_experts_gateup_cfg3.md")
+
+
+def profiled_traffic(path: str):
+    """dram bytes read + written per launch from a committed ncu summary's `traffic_per_launch_bytes:` line."""
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_per_launch_bytes:"):
+                    return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+def kernel_rooflines(be, shape, toks, peak_gbs, reps: int = 5) -> dict:
+    """Per kind of launch inside the step (gcuda_debug_kernel_times: eager steps, no programmatic overlap, CUDA events
+    around each launch): device ms per step, launches, algorithmic bytes per launch and GB/s. The expert products'
+    algorithmic bytes: the q4 weights of the routed experts the layer's union names plus the shared expert's (9/16
+    byte per value); the activations and outputs (< 0.2%) are left out."""
+    import ctypes as C
+    L = be.L
+    L.gcuda_debug_kernel_times.restype = C.c_int
+    L.gcuda_debug_kernel_times.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                           C.c_void_p, C.c_void_p]
+    ms = np.zeros(4, np.float32)
+    nl = np.zeros(4, np.int32)
+    step_ms = C.c_float(0)
+    usum = C.c_int(0)
+    t = np.ascontiguousarray(toks, dtype=np.int32)
+    be._rc(L.gcuda_debug_kernel_times(be.g, t.ctypes.data, len(t), reps, ms.ctypes.data, nl.ctypes.data,
+                                      C.byref(step_ms), C.byref(usum)), "kernel_times")
+    H, q4 = shape.hidden, (lambda r, c: r * c * 9 // 16)
+    n_moe = 0 if shape.dense else shape.n_layers
+    union = usum.value / max(1, n_moe)
+    per = {
+        "gate_up": (union * q4(2 * shape.moe_ff, H) + q4(2 * shape.shared_ff, H)) if n_moe else 0,
+        "down": (union * q4(H, shape.moe_ff) + q4(H, shape.shared_ff)) if n_moe else 0,
+        "lm_head": q4(shape.vocab, H),
+        "dense": None,
+    }
+    out = {"timing": "eager steps, kernel by kernel (no programmatic overlap), CUDA events around each launch; "
+                     f"mean of {reps} steps", "eager_step_ms": step_ms.value, "union_per_layer": union}
+    for k, name in enumerate(KT_NAMES):
+        d = {"ms_per_step": float(ms[k]), "launches_per_step": int(nl[k]),
+             "share_of_eager_step": float(ms[k]) / step_ms.value if step_ms.value else None}
+        if per[name] and nl[k]:
+            ms_launch = float(ms[k]) / nl[k]
+            ach = per[name] / (ms_launch * 1e-3) / 1e9
+            d.update(ms_per_launch=ms_launch, algorithmic_bytes_per_launch=int(per[name]), achieved_gbs=ach,
+                     frac=ach / peak_gbs)
+        out[name] = d
+    return out
 
 
 def accept_bench(args) -> int:
@@ -504,7 +556,15 @@ def main():
     e2e_s = max_over_ranks(e2e_s, dist, "cuda")
     e2e = seqs * NTOK * args.e2e_steps / e2e_s
 
-    roof = gemv_roofline(cuda_lib(), peak)
+    lm_op = gemv_roofline(cuda_lib(), peak)
+    kr = kernel_rooflines(be, shape, toks, peak)
+    gu = kr["gate_up"]
+    roof = {"kernel": "k_gemv_experts gate_up (the union's routed experts + the shared expert, SwiGLU + quantize "
+                      "epilogue): the step's largest kernel by device time", "bound": "hbm",
+            "achieved": gu.get("achieved_gbs"), "peak": peak, "unit": "GB/s", "frac": gu.get("frac"),
+            "traffic": profiled_traffic(GATEUP_PROFILE), "ms": gu.get("ms_per_launch"),
+            "algorithmic_bytes": gu.get("algorithmic_bytes_per_launch"), "launches_per_step": gu["launches_per_step"],
+            "timing": kr["timing"], "traffic_source": "ncu, " + os.path.relpath(GATEUP_PROFILE, ROOT)}
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -522,6 +582,8 @@ def main():
                    "parallelism": f"ep{world}" if ep else f"replicas x{world}" if world > 1 else "1 GPU",
                    "l2": "inputs larger than L2 (20 GB of weights per GPU; no flush)", "layers": shape.n_layers},
         "roofline": roof,
+        "kernels": kr,
+        "lm_head_operator": lm_op,
         "step_roofline": {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,
                           "peak_kind": peak_kind, "algorithmic_bytes_per_step": b, "experts_per_layer": union_layer,
                           "mean_context": mean_ctx},

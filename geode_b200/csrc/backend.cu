@@ -137,6 +137,13 @@ struct gcuda {
     int *rej = nullptr;   // gcuda_spec_reject's device buffers: drafts, accepted, next
     size_t rej_cap = 0;
     int *d_rej_step = nullptr;      // gcuda_step_device_reject's result: accepted, next
+    // gcuda_debug_kernel_times: events around each launch of the timed kinds inside eager steps (off: null)
+    struct KernelMarks {
+        std::vector<cudaEvent_t> pool;          // created on demand, kept for the handle's life
+        std::vector<std::pair<int, int>> marks; // (kind, first of the two pool events)
+        size_t used = 0;
+    };
+    KernelMarks *kt = nullptr;
     // gcuda_debug_trace: per-layer copies enqueued inside one eager step (null outside it)
     float *tr_x = nullptr;          // [n_layers + 1][n][H]: each layer's input x, then the last layer's output
     float *tr_rlog = nullptr;       // [n_layers][n][E + 1]: the router's logits (and the shared expert's gate logit)
@@ -237,6 +244,24 @@ void swiglu_units(std::vector<GemvUnit> &out, const DevTensor &gt, const DevTens
 // act_cols: the width of the activation rows the units multiply (0: the buffer's own width); the rows are packed
 // at that width (a narrower writer, e.g. the Gated DeltaNet core, packs them so)
 // swiglu: the units pair gate and up tiles (they cannot be split into one-tile units)
+// The launches gcuda_debug_kernel_times tells apart (kind ids of include/geode_cuda.h's GCUDA_KT_*).
+enum { kKtGateUp = 0, kKtDown = 1, kKtLmHead = 2, kKtDense = 3, kKtKinds = 4 };
+
+// Records an event on the handle's stream before (begin) or after (end) a launch of `kind` while kernel timing is
+// on; nothing otherwise (and never inside a graph capture: the timing runs eager steps only).
+bool kt_mark(gcuda *g, int kind, bool begin) {
+    if (!g->kt) return true;
+    gcuda::KernelMarks &m = *g->kt;
+    if (m.used >= m.pool.size()) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreate(&e) != cudaSuccess) return false;
+        m.pool.push_back(e);
+    }
+    const int id = static_cast<int>(m.used++);
+    if (begin) m.marks.emplace_back(kind, id);
+    return cudaEventRecord(m.pool[static_cast<size_t>(id)], g->st) == cudaSuccess;
+}
+
 int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, int act_cols = 0, bool swiglu = false) {
     StaticGemv p{};
     p.units = g->units + u0;
@@ -247,7 +272,11 @@ int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, i
     p.allow_half = swiglu ? 0 : 1;
     p.allow_split = 1;
     p.status = g->d_status;
-    return launch_static_gemv(p, g->st, pdl);
+    const bool head = u0 == g->lm_u;
+    if (!kt_mark(g, head ? kKtLmHead : kKtDense, true)) return GCUDA_E_CUDA;
+    const int rc = launch_static_gemv(p, g->st, pdl);
+    if (!kt_mark(g, head ? kKtLmHead : kKtDense, false)) return GCUDA_E_CUDA;
+    return rc;
 }
 
 #define LAUNCH_OK(call)                                                        \
@@ -484,6 +513,8 @@ int enqueue_step(gcuda *g, int n) {
                 ea.wpu = r.wpu;
                 ea.nslots = r.nslots;
                 ea.blocked = r.blocked;
+                const int kind = pass == static_cast<int>(kGateUp) ? kKtGateUp : kKtDown;
+                if (!kt_mark(g, kind, true)) return GCUDA_E_CUDA;
                 if (r.stages == kPairStages)
                     LAUNCH_OK(launch_ex(k_gemv_experts<kPairStages>, dim3(sm_count()), dim3(2 * r.nslots * 32), r.smem, g->st, pdl, ea));
                 else if (r.stages == kWideStages)
@@ -493,6 +524,7 @@ int enqueue_step(gcuda *g, int n) {
                     LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
                 else
                     LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kFanThreads), r.smem, g->st, pdl, ea));
+                if (!kt_mark(g, kind, false)) return GCUDA_E_CUDA;
             }
             if (g->ep_world > 1) {
                 // every pick's row from the rank that owns its expert (the others hold zeros there: the sum is that row
@@ -1273,6 +1305,62 @@ int gcuda_debug_trace(gcuda *g, const int *toks, int n, float *x, float *router_
     std::memcpy(g->last_toks, toks, sizeof(int) * n);
     g->pos += n;
     g->last_batch = n;
+    return GCUDA_OK;
+}
+
+// Tests / measuring: `reps` eager steps of the same n tokens at the same position (no PDL, so an event pair brackets
+// each launch), the device time of each timed kind summed over the steps.
+int gcuda_debug_kernel_times(gcuda *g, const int *toks, int n, int reps, float *ms, int *launches, float *step_ms,
+                             int *union_sum) {
+    if (!g || !g->ready || !toks || !ms || !launches || n < 1 || n > g->sh.max_tokens || reps < 1) return GCUDA_E_ARG;
+    if (g->pos + n > g->sh.context) return fail(g, GCUDA_E_ARG, "kernel_times: past the context");
+    cudaSetDevice(g->device);
+    gcuda::KernelMarks marks;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    LAUNCH_OK(cudaEventCreate(&e0));
+    LAUNCH_OK(cudaEventCreate(&e1));
+    for (int k = 0; k < kKtKinds; ++k) ms[k] = 0.0f, launches[k] = 0;
+    float total = 0.0f;
+    int u0 = 0, u1 = 0;
+    LAUNCH_OK(cudaMemcpy(&u0, &g->step->n_union_sum, sizeof(int), cudaMemcpyDeviceToHost));
+    const bool keep_pdl = g->pdl;
+    g->pdl = false;
+    int rc = GCUDA_OK;
+    for (int r = 0; r < reps && rc == GCUDA_OK; ++r) {
+        marks.marks.clear();
+        marks.used = 0;
+        g->kt = &marks;
+        if (cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st) != cudaSuccess ||
+            cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st) != cudaSuccess ||
+            cudaEventRecord(e0, g->st) != cudaSuccess)
+            rc = GCUDA_E_CUDA;
+        if (rc == GCUDA_OK) rc = enqueue_step(g, n);
+        g->kt = nullptr;
+        if (rc == GCUDA_OK && (cudaEventRecord(e1, g->st) != cudaSuccess || cudaStreamSynchronize(g->st) != cudaSuccess))
+            rc = GCUDA_E_CUDA;
+        if (rc != GCUDA_OK) break;
+        float t = 0.0f;
+        cudaEventElapsedTime(&t, e0, e1);
+        total += t;
+        for (const auto &m : marks.marks) {
+            float d = 0.0f;
+            cudaEventElapsedTime(&d, marks.pool[static_cast<size_t>(m.second)], marks.pool[static_cast<size_t>(m.second) + 1]);
+            ms[m.first] += d;
+            ++launches[m.first];
+        }
+    }
+    g->pdl = keep_pdl;
+    if (rc == GCUDA_OK) rc = check_status(g);
+    if (rc == GCUDA_OK && cudaMemcpy(&u1, &g->step->n_union_sum, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = GCUDA_E_CUDA;
+    for (cudaEvent_t e : marks.pool) cudaEventDestroy(e);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc != GCUDA_OK) return rc;
+    for (int k = 0; k < kKtKinds; ++k) ms[k] /= static_cast<float>(reps), launches[k] /= reps;
+    if (step_ms) *step_ms = total / static_cast<float>(reps);
+    if (union_sum) *union_sum = (u1 - u0) / reps;
+    g->last_batch = 0;   // (the steps ran at the same position: nothing to accept or keep)
     return GCUDA_OK;
 }
 

@@ -143,7 +143,9 @@ __device__ __forceinline__ float silu_fast_exact(float x) { return __fdiv_rn(x, 
 // computed to 80 digits for this file), 2^(r/32) by a cubic in double precision, the product rounded once to float;
 // the multiply-adds fused, as in glibc's FMA build. It equals glibc's expf on all 2^32 inputs (checked on the host and
 // on the device against the host's glibc by the tests).
-__constant__ uint64_t kExp2Table[32] = {
+// (global memory read through L1, not __constant__: the lanes of a warp index it with different k, which the constant
+// cache would serve one address at a time)
+__device__ const uint64_t kExp2Table[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
     0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
@@ -169,7 +171,7 @@ __device__ __forceinline__ float expf_ref(float x) {
     const uint64_t ki = static_cast<uint64_t>(__double_as_longlong(kd));
     kd = __dsub_rn(kd, kShift);
     const double r = __fma_rn(kInvLn2x32, xd, -kd);
-    const double s = __longlong_as_double(static_cast<long long>(kExp2Table[ki & 31u] + (ki << 47)));
+    const double s = __longlong_as_double(static_cast<long long>(__ldg(&kExp2Table[ki & 31u]) + (ki << 47)));
     const double z = __fma_rn(c0, r, c1);
     const double r2 = __dmul_rn(r, r);
     const double y = __fma_rn(z, r2, __fma_rn(c2, r, 1.0));

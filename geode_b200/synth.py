@@ -223,13 +223,16 @@ class _Writer:
 
 
 def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quantized",
-               router_std: float = 0.05, weight_std: float = 0.02, mtp: bool = False) -> Dict:
+               router_std: float = 0.05, weight_std: float = 0.02, mtp: bool = False, distinct_layers: int = 0) -> Dict:
     """Writes a geode-pack for ``shape`` into out_dir; returns the manifest. fill: "quantized" (N(0, weight_std)
     weights through the reference quantizer) or "random" (random q4 bytes). mtp: also the MTP drafting layer, as the
     engine reads it (engine/src/model.cpp:175-191, engine/src/pack.cpp:300-305): mtp.fc.weight [hidden, 2 hidden],
     the norms mtp.norm / mtp.pre_fc_norm_embedding / mtp.pre_fc_norm_hidden, a full-attention decoder layer under
     mtp.layers.0. with its MLP (routed experts after the last layer's, manifest "mtp": {"experts": ...}). Its tensors
-    come after every other, so the rest of the pack is the same bytes with or without it."""
+    come after every other, so the rest of the pack is the same bytes with or without it. distinct_layers = k > 0:
+    only layers 0..k-1 get bytes of their own; layer l >= k names layer l % k's bytes in the manifest (its tensors and
+    its expert table entry at the same offsets; the layer kinds must repeat with period k) - a full-depth model whose
+    every layer reads as many bytes as a distinct one would, on a pack of k layers' size."""
     os.makedirs(out_dir, exist_ok=True)
     rng = np.random.default_rng(seed)
     s = shape
@@ -317,10 +320,21 @@ def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quan
             entry = {"file": "experts.bin", "offset": first, "stride": stride, "format": "q4"}
         return entry
 
+    k = distinct_layers if 0 < distinct_layers < s.n_layers else s.n_layers
     for l in range(s.n_layers):
-        entry = decoder_layer(f"layers.{l}.", s.layer_types[l] == "full_attention")
-        if entry is not None:
-            expert_layers.append(entry)
+        if l < k:
+            entry = decoder_layer(f"layers.{l}.", s.layer_types[l] == "full_attention")
+            if entry is not None:
+                expert_layers.append(entry)
+            continue
+        src = l % k
+        if s.layer_types[l] != s.layer_types[src]:
+            raise ValueError(f"layer {l} is not of layer {src}'s kind: the kinds must repeat every {k} layers")
+        pre = f"layers.{src}."
+        for name in [n_ for n_ in tensors if n_.startswith(pre)]:
+            tensors[f"layers.{l}." + name[len(pre):]] = dict(tensors[name])
+        if not s.dense:
+            expert_layers.append(dict(expert_layers[src]))
 
     f32("norm.weight", rng.standard_normal(H, dtype=np.float32) * np.float32(0.1))
     q4("lm_head.weight", s.vocab, H)

@@ -198,6 +198,18 @@ int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl);
  * [n_layers] (distinct experts picked). */
 int gcuda_debug_trace(gcuda *g, const int *toks, int n, float *x, float *router_logits, int *ids, float *weights,
                       float *gate, int *n_union);
+/* Device time per kind of launch: `reps` steps of the n tokens at the current position (the position does not move),
+ * launched kernel by kernel without programmatic overlap so that CUDA events bracket each launch. ms[4] and
+ * launches[4] per step for GCUDA_KT_GATE_UP (the routed and shared experts' gate|up product with SwiGLU), GCUDA_KT_DOWN
+ * (their down product), GCUDA_KT_LM_HEAD and GCUDA_KT_DENSE (the layers' other q4 products); *step_ms the whole step
+ * (NULL: not wanted), *union_sum the routed experts the step's MoE layers read (summed over layers; NULL: not
+ * wanted). */
+#define GCUDA_KT_GATE_UP 0
+#define GCUDA_KT_DOWN 1
+#define GCUDA_KT_LM_HEAD 2
+#define GCUDA_KT_DENSE 3
+int gcuda_debug_kernel_times(gcuda *g, const int *toks, int n, int reps, float *ms, int *launches, float *step_ms,
+                             int *union_sum);
 
 /* ------------------------------------------------------------------------------------------- operators ---- */
 /* All on caller-owned device memory, enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
