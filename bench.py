@@ -315,16 +315,22 @@ KT_NAMES = ["gate_up", "down", "lm_head", "dense"]
 GATEUP_PROFILE = os.path.join(ROOT, "profiles", "k_gemv_experts_gateup_cfg3.md")
 
 
-def profiled_traffic(path: str):
-    """dram bytes read + written per launch from a committed ncu summary's `traffic_per_launch_bytes:` line."""
+def profiled_traffic(path: str, blocks: float):
+    """dram bytes read + written of one launch, from a committed ncu summary's `traffic_per_launch_bytes:` and
+    `expert_blocks_in_launch:` lines, scaled to a launch that reads `blocks` expert blocks (the traffic grows in
+    proportion to the blocks read)."""
+    got = {}
     try:
         with open(path) as f:
             for line in f:
-                if line.strip().startswith("traffic_per_launch_bytes:"):
-                    return float(line.split(":", 1)[1].split()[0])
+                k, _, v = line.strip().partition(":")
+                if k in ("traffic_per_launch_bytes", "expert_blocks_in_launch"):
+                    got[k] = float(v.split()[0])
     except OSError:
-        pass
-    return None
+        return None
+    if len(got) != 2 or not blocks:
+        return None
+    return got["traffic_per_launch_bytes"] * blocks / got["expert_blocks_in_launch"]
 
 
 def kernel_rooflines(be, shape, toks, peak_gbs, reps: int = 5) -> dict:
@@ -562,9 +568,10 @@ def main():
     roof = {"kernel": "k_gemv_experts gate_up (the union's routed experts + the shared expert, SwiGLU + quantize "
                       "epilogue): the step's largest kernel by device time", "bound": "hbm",
             "achieved": gu.get("achieved_gbs"), "peak": peak, "unit": "GB/s", "frac": gu.get("frac"),
-            "traffic": profiled_traffic(GATEUP_PROFILE), "ms": gu.get("ms_per_launch"),
+            "traffic": profiled_traffic(GATEUP_PROFILE, kr["union_per_layer"] + 1), "ms": gu.get("ms_per_launch"),
             "algorithmic_bytes": gu.get("algorithmic_bytes_per_launch"), "launches_per_step": gu["launches_per_step"],
-            "timing": kr["timing"], "traffic_source": "ncu, " + os.path.relpath(GATEUP_PROFILE, ROOT)}
+            "timing": kr["timing"], "traffic_source": "ncu, " + os.path.relpath(GATEUP_PROFILE, ROOT) +
+            " (a 41-block launch, scaled to this run's mean union + the shared expert)"}
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
