@@ -31,6 +31,7 @@ struct DeviceState {
     int sms[kMaxDevices] = {};
     int gemv_rc[kMaxDevices] = {};
     int bf16_rc[kMaxDevices] = {};
+    int umma_rc[kMaxDevices] = {};
     uint32_t *status[kMaxDevices] = {};
 };
 inline DeviceState &device_state() {

@@ -8,6 +8,7 @@
 #include "gemv_kernels.cuh"
 #include "small_kernels.cuh"
 #include "launch.hpp"
+#include "umma_gemm.cuh"
 
 using namespace gcu;
 
@@ -18,9 +19,87 @@ __global__ void k_expf_table(uint32_t first, int64_t count, float *out) {
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
         out[i] = expf_ref(__uint_as_float(first + static_cast<uint32_t>(i)));
 }
+// Dynamic shared memory of the tensor-core product's launches: its rings, padded to more than half an SM's shared
+// memory so that one CTA holds an SM (each allocates all 512 tensor-memory columns).
+constexpr int kUmmaSmemFloor = 120 * 1024;
+template <int NT>
+constexpr int umma_launch_smem() {
+    return static_cast<int>(umma_smem_bytes<NT>()) > kUmmaSmemFloor ? static_cast<int>(umma_smem_bytes<NT>()) : kUmmaSmemFloor;
+}
+inline int umma_opt_in() {
+    const int dev = current_device();
+    if (dev < 0) return GCUDA_E_CUDA;
+    DeviceState &d = device_state();
+    std::lock_guard<std::mutex> lock(d.mu);
+    if (!d.umma_rc[dev]) {
+        const cudaFuncAttribute at = cudaFuncAttributeMaxDynamicSharedMemorySize;
+        const bool ok = cudaFuncSetAttribute(k_umma_gemm<4>, at, umma_launch_smem<4>()) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_umma_gemm<8>, at, umma_launch_smem<8>()) == cudaSuccess &&
+                        cudaFuncSetAttribute(k_umma_gemm<32>, at, umma_launch_smem<32>()) == cudaSuccess;
+        d.umma_rc[dev] = ok ? static_cast<int>(GCUDA_OK) : static_cast<int>(GCUDA_E_CUDA);
+    }
+    return d.umma_rc[dev];
+}
+
+// The tensor-core q4 product on a U-layout matrix for n token rows of act (the token block NT chosen from n); one
+// persistent CTA an SM at most.
+inline int launch_umma_gemm(UmmaGemmArgs a, cudaStream_t st) {
+    if (umma_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
+    const int nt = a.act.n <= 4 ? 4 : a.act.n <= 8 ? 8 : 32;
+    const int units = (a.rows / kUmmaRows) * ((a.act.n + nt - 1) / nt);
+    const dim3 grid(std::max(1, std::min(units, sm_count())));
+    cudaError_t e;
+    if (nt == 4) e = launch_ex(k_umma_gemm<4>, grid, dim3(kUmmaThreads), umma_launch_smem<4>(), st, false, a);
+    else if (nt == 8) e = launch_ex(k_umma_gemm<8>, grid, dim3(kUmmaThreads), umma_launch_smem<8>(), st, false, a);
+    else e = launch_ex(k_umma_gemm<32>, grid, dim3(kUmmaThreads), umma_launch_smem<32>(), st, false, a);
+    return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
 }  // namespace gcu
 
 extern "C" {
+
+int gcuda_op_status(int clear) {
+    uint32_t *st = device_status();
+    if (!st) return GCUDA_E_CUDA;
+    uint32_t v = 0;
+    if (cudaMemcpy(&v, st, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return GCUDA_E_CUDA;
+    if (clear && v && cudaMemset(st, 0, 4) != cudaSuccess) return GCUDA_E_CUDA;
+    return static_cast<int>(v & 0x7FFFFFFFu);
+}
+
+size_t gcuda_op_q4_umma_bytes(int64_t rows, int64_t cols) {
+    if (rows <= 0 || rows % kUmmaRows || cols <= 0 || cols % 256) return 0;
+    return static_cast<size_t>(rows) * static_cast<size_t>(cols) / 16 * 9;
+}
+
+int gcuda_op_q4_umma_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint8_t *d_u, void *stream) {
+    if (!d_pack || !d_u || gcuda_op_q4_umma_bytes(rows, cols) == 0 || (reinterpret_cast<uintptr_t>(d_u) & 15))
+        return GCUDA_E_ARG;
+    k_umma_relayout<<<148 * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(d_pack, rows, cols, d_u);
+    count_launch();
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_q4_gemm_umma(const uint8_t *d_u, int64_t rows, int64_t cols, float global, const int8_t *d_q,
+                          const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream) {
+    if (!d_u || !d_q || !d_scale || !d_bsum || !d_y || gcuda_op_q4_umma_bytes(rows, cols) == 0 || n < 1 ||
+        rows > (1 << 24) || cols > (1 << 16) || (reinterpret_cast<uintptr_t>(d_u) & 15) ||
+        (reinterpret_cast<uintptr_t>(d_q) & 15))
+        return GCUDA_E_ARG;
+    UmmaGemmArgs a{};
+    a.w = d_u;
+    a.rows = static_cast<int>(rows);
+    a.cols = static_cast<int>(cols);
+    a.global = global;
+    a.act = ActSet{d_q, d_scale, d_bsum, static_cast<int>(cols), n, static_cast<int>(cols), static_cast<int>(cols / 16)};
+    a.y = d_y;
+    a.ystride = static_cast<int>(rows);
+    a.status = device_status();
+    if (!a.status) return GCUDA_E_CUDA;
+    return launch_umma_gemm(a, static_cast<cudaStream_t>(stream));
+}
+
 
 size_t gcuda_op_q4_tiled_bytes(int64_t rows, int64_t cols) {
     const int64_t rows_pad = (rows + 31) / 32 * 32;

@@ -1,0 +1,314 @@
+// umma_gemm.cuh - the q4 product on the tcgen05 tensor core, bit for bit the reference's matvec_rows_q_ref
+// (engine/src/kernels.cpp:1304-1322) for any number of token rows:
+//   y[t][r] = (sum over blocks b in order of float(isum_b) * (e4m3[r][b] * ascale[t][b])) * global.
+//
+// The integer block sums come from int8 MMAs of K = 32 (two 16-value blocks): A = the weight codes as u8 (c' in
+// 0..15, level = 2 c' - 15) for 128 rows, B = 2 NT "columns" per K-step, column 2t holding token t's 16 activations
+// of the first block and zeros for the second, column 2t + 1 the reverse - so one MMA leaves each block's own sum
+// sum_i c'_i q_i of every token in its own TMEM column, and isum = 2 D - 15 bsum (bsum: the activation block's sum).
+// No accumulation in the tensor core: the float chain over the blocks, in block order, runs in the epilogue threads
+// (one thread a row) with the reference's own operations, so the result is exact.
+//
+// Weights in the "U" layout (gcuda_op_q4_umma_relayout), the same 9/16 byte per value as the pack:
+//   codes: for 128-row tile T and K-step ks (32 columns) 128 rows x 16 bytes at ((T * KS + ks) * 128 + r) * 16,
+//          byte j = c'(column 32 ks + j) | c'(column 32 ks + 16 + j) << 4 - a row's K-step unpacks with two masks
+//          into the two 16-byte halves the canonical K-major layout wants;
+//   scales: after rows * cols / 2 code bytes, per tile, 64-column group g and row a 32-bit word of the four blocks'
+//          E4M3 bytes at ((T * (cols / 64) + g) * 128 + r) * 4.
+//
+// A CTA (persistent over units = (tile, block of NT tokens)) runs four roles on its own rings:
+//   warp 8 lane 0: 16 KB bulk copies of 8 K-steps' packed codes (cp.async.bulk, mbarrier complete_tx);
+//   warps 4-7: per K-step each thread unpacks its row into the A stage (8 rows x 16 B core matrices, the two K halves
+//              128 B apart, row groups 256 B apart) and the first 2N threads write B's 16-byte pieces;
+//   warp 9 lane 0: one MMA per K-step into the TMEM buffer of the current chunk (two buffers of 256 columns), a commit
+//              that frees the A stage, a commit per chunk that hands the buffer to the epilogue;
+//   warps 0-3: per chunk, each thread loads its row's columns (tcgen05.ld) and adds the blocks into its tokens'
+//              chains; at the end of a unit, y = chain * global.
+// Every wait is bounded: one that gives up sets kErrWaitTimeout in the status word and the CTA stops its units.
+#pragma once
+
+#include "common.cuh"
+#include "q4_gemv.cuh"
+#include "umma.cuh"
+
+namespace gcu {
+
+constexpr int kUmmaRows = 128;
+constexpr int kUmmaStepBytes = kUmmaRows * 16;   // one tile's packed codes of one K-step
+constexpr int kUmmaPackSteps = 8;                // K-steps per bulk copy
+constexpr int kUmmaPackStages = 4;
+constexpr int kUmmaABStages = 8;
+constexpr int kUmmaThreads = 320;
+constexpr uint32_t kUmmaWaitLimit = 1u << 22;    // polls before a wait gives up (seconds at most)
+
+__host__ __device__ inline size_t umma_code_bytes(int64_t rows, int64_t cols) {
+    return static_cast<size_t>(rows) * static_cast<size_t>(cols) / 2;
+}
+
+template <int NT>
+struct UmmaSmem {
+    static constexpr int N = 2 * NT;                  // MMA columns
+    static constexpr int kABBytes = 4096 + N * 32;    // A (128 x 32) then B (N x 32)
+    alignas(128) uint8_t packed[kUmmaPackStages][kUmmaPackSteps * kUmmaStepBytes];
+    alignas(128) uint8_t ab[kUmmaABStages][kABBytes];
+    uint64_t packed_full[kUmmaPackStages], packed_empty[kUmmaPackStages];
+    uint64_t ab_full[kUmmaABStages], ab_empty[kUmmaABStages];
+    uint64_t tm_full[2], tm_empty[2];
+    uint32_t tmem_base;
+    int abort;
+};
+
+struct UmmaGemmArgs {
+    const uint8_t *w;   // U layout
+    int rows, cols;
+    float global;
+    ActSet act;         // token t: q at t * qstride, scale / bsum at t * sstride
+    float *y;
+    int ystride;        // y[t * ystride + row]
+    uint32_t *status;
+};
+
+template <int NT>
+__host__ __device__ constexpr size_t umma_smem_bytes() { return sizeof(UmmaSmem<NT>) + 128; }
+
+#if defined(__CUDA_ARCH__)
+__device__ __forceinline__ bool umma_give_up(volatile int *abort, uint32_t *status) {
+    *abort = 1;
+    if (status) atomicOr(status, kErrWaitTimeout);
+    return false;
+}
+// a bounded wait that also stops when another role of the CTA gave up
+__device__ __forceinline__ bool umma_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    for (uint32_t i = 0; i < kUmmaWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && *abort) return false;
+    }
+    return false;
+}
+#endif
+
+template <int NT>
+__global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
+#if defined(__CUDA_ARCH__)
+    extern __shared__ uint8_t smem_raw[];
+    UmmaSmem<NT> &S = *reinterpret_cast<UmmaSmem<NT> *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    constexpr int N = 2 * NT;
+    constexpr int KT = 256 / N;   // K-steps per TMEM buffer (256 columns)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KS = a.cols / 32, G = a.cols / 64;
+    const int tiles = a.rows / kUmmaRows, tblocks = (a.act.n + NT - 1) / NT, units = tiles * tblocks;
+    volatile int *abort = &S.abort;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kUmmaPackStages; ++i) mbar_init(&S.packed_full[i], 1), mbar_init(&S.packed_empty[i], 128);
+        for (int i = 0; i < kUmmaABStages; ++i) mbar_init(&S.ab_full[i], 128), mbar_init(&S.ab_empty[i], 1);
+        for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], 128);
+        S.abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 9) {
+        tmem_alloc(&S.tmem_base, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = S.tmem_base;
+
+    if (warp == 8) {
+        // ---- the copies of the packed codes
+        if (lane == 0) {
+            uint32_t s = 0, ph = 0;
+            int last_ph[kUmmaPackStages];
+            for (int i = 0; i < kUmmaPackStages; ++i) last_ph[i] = -1;
+            for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+                const int T = u / tblocks;
+                for (int pc = 0; pc < KS / kUmmaPackSteps && !*abort; ++pc) {
+                    if (!umma_wait(&S.packed_empty[s], ph ^ 1, abort)) {
+                        umma_give_up(abort, a.status);
+                        break;
+                    }
+                    mbar_expect_tx(&S.packed_full[s], kUmmaPackSteps * kUmmaStepBytes);
+                    bulk_g2s(S.packed[s], a.w + (static_cast<size_t>(T) * KS + static_cast<size_t>(pc) * kUmmaPackSteps) * kUmmaStepBytes,
+                             kUmmaPackSteps * kUmmaStepBytes, &S.packed_full[s]);
+                    last_ph[s] = static_cast<int>(ph);
+                    if (++s == kUmmaPackStages) s = 0, ph ^= 1;
+                }
+            }
+            // no copy may still be writing this CTA's shared memory when it leaves (after a give-up the unpackers
+            // stop consuming): wait for each stage's last fill, bounded
+            for (int i = 0; i < kUmmaPackStages; ++i)
+                if (last_ph[i] >= 0 && !mbar_wait(&S.packed_full[i], static_cast<uint32_t>(last_ph[i]), kUmmaWaitLimit))
+                    umma_give_up(abort, a.status);
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ---- unpack A, write B
+        const int t = threadIdx.x - 128;   // the row this thread unpacks
+        uint32_t ps = 0, pph = 0, as = 0, aph = 0;
+        const int g = t >> 3, ri = t & 7;
+        for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+            const int tb = u % tblocks;
+            const int nt = min(NT, a.act.n - tb * NT);
+            for (int ks = 0; ks < KS; ++ks) {
+                if ((ks % kUmmaPackSteps) == 0 && !umma_wait(&S.packed_full[ps], pph, abort)) {
+                    umma_give_up(abort, a.status);
+                    break;
+                }
+                if (!umma_wait(&S.ab_empty[as], aph ^ 1, abort)) {
+                    umma_give_up(abort, a.status);
+                    break;
+                }
+                const uint4 x = *reinterpret_cast<const uint4 *>(S.packed[ps] + ((ks % kUmmaPackSteps) * kUmmaRows + t) * 16);
+                constexpr uint32_t M4 = 0x0F0F0F0Fu;
+                const uint4 lo = make_uint4(x.x & M4, x.y & M4, x.z & M4, x.w & M4);
+                const uint4 hi = make_uint4((x.x >> 4) & M4, (x.y >> 4) & M4, (x.z >> 4) & M4, (x.w >> 4) & M4);
+                uint8_t *A = S.ab[as];
+                *reinterpret_cast<uint4 *>(A + g * 256 + ri * 16) = lo;
+                *reinterpret_cast<uint4 *>(A + g * 256 + 128 + ri * 16) = hi;
+                if (t < 2 * N) {
+                    const int n_ = t >> 1, c = t & 1, tok = n_ >> 1, h = n_ & 1;
+                    uint4 v = make_uint4(0, 0, 0, 0);
+                    if (c == h && tok < nt)
+                        v = __ldg(reinterpret_cast<const uint4 *>(a.act.q + static_cast<size_t>(tb * NT + tok) * a.act.qstride +
+                                                                  static_cast<size_t>(ks) * 32 + 16 * c));
+                    *reinterpret_cast<uint4 *>(A + 4096 + (n_ >> 3) * 256 + c * 128 + (n_ & 7) * 16) = v;
+                }
+                fence_async_smem();
+                mbar_arrive(&S.ab_full[as]);
+                if ((ks % kUmmaPackSteps) == kUmmaPackSteps - 1) {
+                    mbar_arrive(&S.packed_empty[ps]);
+                    if (++ps == kUmmaPackStages) ps = 0, pph ^= 1;
+                }
+                if (++as == kUmmaABStages) as = 0, aph ^= 1;
+            }
+        }
+    } else if (warp == 9) {
+        // ---- the MMAs
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_i8(kUmmaRows, N, false, true);
+            uint32_t as = 0, aph = 0, tb_ = 0, tph = 0;
+            int last_as = -1;   // the stage of the last MMA issued, and the phase its commit completes
+            uint32_t last_aph = 0;
+            for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+                for (int ks = 0; ks < KS; ++ks) {
+                    const int kk = ks % KT;
+                    if (kk == 0 && !umma_wait(&S.tm_empty[tb_], tph ^ 1, abort)) {
+                        umma_give_up(abort, a.status);
+                        break;
+                    }
+                    if (!umma_wait(&S.ab_full[as], aph, abort)) {
+                        umma_give_up(abort, a.status);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ab = smem_u32(S.ab[as]);
+                    umma_i8(tbase + tb_ * 256 + static_cast<uint32_t>(kk * N), umma_smem_desc(ab, 128, 256),
+                            umma_smem_desc(ab + 4096, 128, 256), idesc, false);
+                    umma_commit(&S.ab_empty[as]);
+                    last_as = static_cast<int>(as);
+                    last_aph = aph;
+                    if (++as == kUmmaABStages) as = 0, aph ^= 1;
+                    if (kk == KT - 1 || ks == KS - 1) {
+                        umma_commit(&S.tm_full[tb_]);
+                        if (++tb_ == 2) tb_ = 0, tph ^= 1;
+                    }
+                }
+            }
+            // every MMA this thread issued has finished before the tensor memory is freed (its last commit covers
+            // all earlier ones) - after a give-up too
+            if (last_as >= 0 && !mbar_wait(&S.ab_empty[last_as], last_aph, kUmmaWaitLimit)) umma_give_up(abort, a.status);
+        }
+    } else {
+        // ---- the epilogue: warp w < 4 reads TMEM lanes 32 w .. 32 w + 31 (its rows)
+        const int r = warp * 32 + lane;
+        uint32_t tb_ = 0, tph = 0;
+        for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+            const int T = u / tblocks, tb = u % tblocks;
+            const int nt = min(NT, a.act.n - tb * NT);
+            const int row = T * kUmmaRows + r;
+            const uint8_t *sc = a.w + umma_code_bytes(a.rows, a.cols) + (static_cast<size_t>(T) * G * kUmmaRows + r) * 4;
+            float acc[NT];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+            bool ok = true;
+            for (int c0 = 0; c0 < KS && ok; c0 += KT) {
+                if (!umma_wait(&S.tm_full[tb_], tph, abort)) {
+                    ok = umma_give_up(abort, a.status);
+                    break;
+                }
+                tc_fence_after();
+                const int kn = min(KT, KS - c0);
+                for (int kk = 0; kk < kn; ++kk) {
+                    const int ks = c0 + kk;
+                    uint32_t d[N];
+#pragma unroll
+                    for (int j = 0; j < N / 8; ++j) {
+                        uint32_t v[8];
+                        tmem_ld8(tbase + (static_cast<uint32_t>(warp * 32) << 16) + tb_ * 256 + static_cast<uint32_t>(kk * N + 8 * j), v);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) d[8 * j + i] = v[i];
+                    }
+                    tmem_wait_ld();
+                    const uint32_t sw = __ldg(reinterpret_cast<const uint32_t *>(sc + static_cast<size_t>(ks >> 1) * kUmmaRows * 4));
+                    const float2 e = e4m3x2_to_float2((sw >> (16 * (ks & 1))) & 0xFFFFu);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int b = 2 * ks + h;
+                        const float eb = h ? e.y : e.x;
+#pragma unroll
+                        for (int t = 0; t < NT; ++t) {
+                            if (t >= nt) break;
+                            const size_t so = static_cast<size_t>(tb * NT + t) * a.act.sstride + b;
+                            const int32_t isum = 2 * static_cast<int32_t>(d[2 * t + h]) - 15 * __ldg(a.act.bsum + so);
+                            acc[t] = __fadd_rn(acc[t], __fmul_rn(static_cast<float>(isum), __fmul_rn(eb, __ldg(a.act.scale + so))));
+                        }
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&S.tm_empty[tb_]);
+                if (++tb_ == 2) tb_ = 0, tph ^= 1;
+            }
+            if (!ok) break;
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                if (t < nt) a.y[static_cast<size_t>(tb * NT + t) * a.ystride + row] = __fmul_rn(acc[t], a.global);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 9) {
+        __syncwarp();
+        tmem_dealloc(tbase, 512);
+    }
+#endif
+}
+
+// pack rows (C/2 code bytes, value 2j in the low nibble, then C/16 E4M3 bytes) -> the U layout; a thread per 16
+// output bytes of codes or per scale word
+__global__ void k_umma_relayout(const uint8_t *__restrict__ pack, int64_t rows, int64_t cols, uint8_t *__restrict__ u) {
+    const int64_t KS = cols / 32, G = cols / 64, rb = cols / 2 + cols / 16;
+    const int64_t n_code = rows * KS, n_sc = rows * G;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n_code + n_sc;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        if (i < n_code) {
+            const int64_t r = i % kUmmaRows, rest = i / kUmmaRows, ks = rest % KS, T = rest / KS;
+            const uint8_t *src = pack + (T * kUmmaRows + r) * rb + ks * 16;   // values 32 ks .. 32 ks + 31
+            auto code = [&](int v) {   // the pack's code of value v of this K-step, remapped so level = 2 c' - 15
+                const int c = (src[v >> 1] >> ((v & 1) * 4)) & 15;
+                return c < 8 ? c + 8 : 15 - c;
+            };
+            uint8_t out[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) out[j] = static_cast<uint8_t>(code(j) | (code(16 + j) << 4));
+            *reinterpret_cast<uint4 *>(u + i * 16) = *reinterpret_cast<const uint4 *>(out);
+        } else {
+            const int64_t k = i - n_code;
+            const int64_t r = k % kUmmaRows, rest = k / kUmmaRows, g = rest % G, T = rest / G;
+            const uint8_t *s = pack + (T * kUmmaRows + r) * rb + cols / 2 + g * 4;
+            const uint32_t w = s[0] | (s[1] << 8) | (s[2] << 16) | (static_cast<uint32_t>(s[3]) << 24);
+            *reinterpret_cast<uint32_t *>(u + umma_code_bytes(rows, cols) + k * 4) = w;
+        }
+    }
+}
+
+}  // namespace gcu

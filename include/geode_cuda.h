@@ -214,6 +214,9 @@ int gcuda_debug_kernel_times(gcuda *g, const int *toks, int n, int reps, float *
 /* ------------------------------------------------------------------------------------------- operators ---- */
 /* All on caller-owned device memory, enqueued on `stream` (a cudaStream_t; NULL = the legacy default stream).
  * They return once enqueued. */
+/* The operators' status word on the current device, after the work enqueued so far (synchronous): 0, or the flags
+ * kernels raised (1: a bounded wait gave up, 2: a shape out of range, 4: a bad token id); clear != 0 zeroes it. */
+int gcuda_op_status(int clear);
 
 /* tiles: the bytes gcuda_op_q4_tiled_bytes gives; the pack's rows -> the GEMV's tile layout */
 size_t gcuda_op_q4_tiled_bytes(int64_t rows, int64_t cols);
@@ -231,6 +234,16 @@ int gcuda_op_norm_quant(const float *d_x, int n, int H, const float *d_w, float 
  * bit for bit the reference's int8 product. y [n][rows]. */
 int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float global, const int8_t *d_q,
                      const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream);
+/* The tensor-core (tcgen05) q4 product for any number of token rows. The matrix first goes to its "U" layout
+ * (gcuda_op_q4_umma_bytes: 9/16 byte per value, as the pack; rows a multiple of 128, cols of 256; 0 otherwise) from
+ * the pack's rows (C/2 code bytes then C/16 E4M3 bytes). y [n][rows] = matvec_rows_q_ref (engine/src/kernels.cpp:
+ * 1304-1322) of each of the n quantized rows (q [n][cols], scale and bsum [n][cols/16]), bit for bit: int8 MMAs give
+ * each 16-value block's own integer sum, the float chain over the blocks runs in block order. A wait inside the
+ * kernel that gives up sets the operators' status word (gcuda_op_status). */
+size_t gcuda_op_q4_umma_bytes(int64_t rows, int64_t cols);
+int gcuda_op_q4_umma_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint8_t *d_u, void *stream);
+int gcuda_op_q4_gemm_umma(const uint8_t *d_u, int64_t rows, int64_t cols, float global, const int8_t *d_q,
+                          const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream);
 /* dequant_row (engine/src/kernels.cpp:1214-1228) of nrows rows (d_rows int64) of a tiled matrix: out [nrows][cols] */
 int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, const int64_t *d_rows, int nrows,
                         float *d_out, void *stream);
