@@ -84,7 +84,7 @@ int gcuda_op_q4_umma_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols,
 int gcuda_op_q4_gemm_umma(const uint8_t *d_u, int64_t rows, int64_t cols, float global, const int8_t *d_q,
                           const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream) {
     if (!d_u || !d_q || !d_scale || !d_bsum || !d_y || gcuda_op_q4_umma_bytes(rows, cols) == 0 || n < 1 ||
-        rows > (1 << 24) || cols > (1 << 16) || (reinterpret_cast<uintptr_t>(d_u) & 15) ||
+        rows > (1 << 24) || cols > kUmmaMaxCols || (reinterpret_cast<uintptr_t>(d_u) & 15) ||
         (reinterpret_cast<uintptr_t>(d_q) & 15))
         return GCUDA_E_ARG;
     UmmaGemmArgs a{};

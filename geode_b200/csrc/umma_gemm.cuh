@@ -17,13 +17,15 @@
 //          E4M3 bytes at ((T * (cols / 64) + g) * 128 + r) * 4.
 //
 // A CTA (persistent over units = (tile, block of NT tokens)) runs four roles on its own rings:
-//   warp 8 lane 0: 16 KB bulk copies of 8 K-steps' packed codes (cp.async.bulk, mbarrier complete_tx);
-//   warps 4-7: per K-step each thread unpacks its row into the A stage (8 rows x 16 B core matrices, the two K halves
+//   warp 12 lane 0: per chunk of 8 K-steps, bulk copies (cp.async.bulk, mbarrier complete_tx) of the tile's packed
+//              codes (16 KB) and of each token's 256 activations;
+//   warps 8-11: per K-step each thread unpacks its row into the A stage (8 rows x 16 B core matrices, the two K halves
 //              128 B apart, row groups 256 B apart) and the first 2N threads write B's 16-byte pieces;
-//   warp 9 lane 0: one MMA per K-step into the TMEM buffer of the current chunk (two buffers of 256 columns), a commit
-//              that frees the A stage, a commit per chunk that hands the buffer to the epilogue;
-//   warps 0-3: per chunk, each thread loads its row's columns (tcgen05.ld) and adds the blocks into its tokens'
-//              chains; at the end of a unit, y = chain * global.
+//   warp 13 lane 0: one MMA per K-step into the TMEM buffer of the current chunk (two buffers of 256 columns), a
+//              commit that frees the A stage, a commit per chunk that hands the buffer to the epilogue;
+//   warps 0-7: two warps per TMEM lane quarter (the rows), each with half of the unit's tokens: per chunk its rows'
+//              scale words, then its columns (tcgen05.ld, several K-steps before one wait) into its tokens' chains,
+//              with the unit's per-token block sums and scales staged in shared memory; y = chain * global.
 // Every wait is bounded: one that gives up sets kErrWaitTimeout in the status word and the CTA stops its units.
 #pragma once
 
@@ -35,10 +37,12 @@ namespace gcu {
 
 constexpr int kUmmaRows = 128;
 constexpr int kUmmaStepBytes = kUmmaRows * 16;   // one tile's packed codes of one K-step
-constexpr int kUmmaPackSteps = 8;                // K-steps per bulk copy
+constexpr int kUmmaPackSteps = 8;                // K-steps per chunk of bulk copies
 constexpr int kUmmaPackStages = 4;
 constexpr int kUmmaABStages = 8;
-constexpr int kUmmaThreads = 320;
+constexpr int kUmmaEpiWarps = 8;                 // two per TMEM lane quarter, each half of the token columns
+constexpr int kUmmaThreads = 32 * (kUmmaEpiWarps + 4 + 2);
+constexpr int kUmmaMaxCols = 4096;
 constexpr uint32_t kUmmaWaitLimit = 1u << 22;    // polls before a wait gives up (seconds at most)
 
 __host__ __device__ inline size_t umma_code_bytes(int64_t rows, int64_t cols) {
@@ -47,15 +51,20 @@ __host__ __device__ inline size_t umma_code_bytes(int64_t rows, int64_t cols) {
 
 template <int NT>
 struct UmmaSmem {
-    static constexpr int N = 2 * NT;                  // MMA columns
-    static constexpr int kABBytes = 4096 + N * 32;    // A (128 x 32) then B (N x 32)
-    alignas(128) uint8_t packed[kUmmaPackStages][kUmmaPackSteps * kUmmaStepBytes];
+    static constexpr int N = 2 * NT;                              // MMA columns
+    static constexpr int kABBytes = 4096 + N * 32;                // A (128 x 32) then B (N x 32)
+    static constexpr int kActBytes = NT * kUmmaPackSteps * 32;    // the chunk's activations: NT tokens x 256 bytes
+    static constexpr int kPackBytes = kUmmaPackSteps * kUmmaStepBytes + kActBytes;
+    alignas(128) uint8_t packed[kUmmaPackStages][kPackBytes];
     alignas(128) uint8_t ab[kUmmaABStages][kABBytes];
+    // per token and K-step: the two blocks' activation sums, then their scales' bits (the epilogue's unit data)
+    alignas(16) int4 tokdata[NT * (kUmmaMaxCols / 32)];
     uint64_t packed_full[kUmmaPackStages], packed_empty[kUmmaPackStages];
     uint64_t ab_full[kUmmaABStages], ab_empty[kUmmaABStages];
     uint64_t tm_full[2], tm_empty[2];
     uint32_t tmem_base;
     int abort;
+    int epi_stop;   // the epilogue warps' common decision to stop after a unit
 };
 
 struct UmmaGemmArgs {
@@ -85,6 +94,7 @@ __device__ __forceinline__ bool umma_wait(uint64_t *bar, uint32_t parity, volati
     }
     return false;
 }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(32 * kUmmaEpiWarps) : "memory"); }
 #endif
 
 template <int NT>
@@ -93,7 +103,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     UmmaSmem<NT> &S = *reinterpret_cast<UmmaSmem<NT> *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     constexpr int N = 2 * NT;
-    constexpr int KT = 256 / N;   // K-steps per TMEM buffer (256 columns)
+    constexpr int KT = 256 / N;         // K-steps per TMEM buffer (256 columns)
+    constexpr int HT = NT / 2;          // tokens per epilogue warp
+    constexpr int KB = NT >= 16 ? 1 : NT == 8 ? 2 : 4;   // K-steps whose TMEM loads go out together
+    constexpr int kCodeBytes = kUmmaPackSteps * kUmmaStepBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KS = a.cols / 32, G = a.cols / 64;
     const int tiles = a.rows / kUmmaRows, tblocks = (a.act.n + NT - 1) / NT, units = tiles * tblocks;
@@ -101,11 +114,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < kUmmaPackStages; ++i) mbar_init(&S.packed_full[i], 1), mbar_init(&S.packed_empty[i], 128);
         for (int i = 0; i < kUmmaABStages; ++i) mbar_init(&S.ab_full[i], 128), mbar_init(&S.ab_empty[i], 1);
-        for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], 128);
+        for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], 32 * kUmmaEpiWarps);
         S.abort = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_barrier_init();
     }
-    if (warp == 9) {
+    if (warp == kUmmaEpiWarps + 5) {
         tmem_alloc(&S.tmem_base, 512);
         tmem_relinquish();
     }
@@ -114,22 +127,27 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     tc_fence_after();
     const uint32_t tbase = S.tmem_base;
 
-    if (warp == 8) {
-        // ---- the copies of the packed codes
+    if (warp == kUmmaEpiWarps + 4) {
+        // ---- bulk copies: per chunk of 8 K-steps the tile's packed codes (16 KB) and each token's 256 activations
         if (lane == 0) {
             uint32_t s = 0, ph = 0;
             int last_ph[kUmmaPackStages];
             for (int i = 0; i < kUmmaPackStages; ++i) last_ph[i] = -1;
             for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
-                const int T = u / tblocks;
+                const int T = u / tblocks, tb = u % tblocks;
+                const int nt = min(NT, a.act.n - tb * NT);
                 for (int pc = 0; pc < KS / kUmmaPackSteps && !*abort; ++pc) {
                     if (!umma_wait(&S.packed_empty[s], ph ^ 1, abort)) {
                         umma_give_up(abort, a.status);
                         break;
                     }
-                    mbar_expect_tx(&S.packed_full[s], kUmmaPackSteps * kUmmaStepBytes);
+                    mbar_expect_tx(&S.packed_full[s], kCodeBytes + nt * kUmmaPackSteps * 32);
                     bulk_g2s(S.packed[s], a.w + (static_cast<size_t>(T) * KS + static_cast<size_t>(pc) * kUmmaPackSteps) * kUmmaStepBytes,
-                             kUmmaPackSteps * kUmmaStepBytes, &S.packed_full[s]);
+                             kCodeBytes, &S.packed_full[s]);
+                    for (int tok = 0; tok < nt; ++tok)
+                        bulk_g2s(S.packed[s] + kCodeBytes + tok * kUmmaPackSteps * 32,
+                                 a.act.q + static_cast<size_t>(tb * NT + tok) * a.act.qstride + static_cast<size_t>(pc) * kUmmaPackSteps * 32,
+                                 kUmmaPackSteps * 32, &S.packed_full[s]);
                     last_ph[s] = static_cast<int>(ph);
                     if (++s == kUmmaPackStages) s = 0, ph ^= 1;
                 }
@@ -140,11 +158,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 if (last_ph[i] >= 0 && !mbar_wait(&S.packed_full[i], static_cast<uint32_t>(last_ph[i]), kUmmaWaitLimit))
                     umma_give_up(abort, a.status);
         }
-    } else if (warp >= 4 && warp < 8) {
-        // ---- unpack A, write B
-        const int t = threadIdx.x - 128;   // the row this thread unpacks
+    } else if (warp >= kUmmaEpiWarps && warp < kUmmaEpiWarps + 4) {
+        // ---- unpack A (a thread a row), write B's 16-byte pieces from the staged activations
+        const int t = threadIdx.x - 32 * kUmmaEpiWarps;
         uint32_t ps = 0, pph = 0, as = 0, aph = 0;
         const int g = t >> 3, ri = t & 7;
+        const int n_ = t >> 1, c = t & 1, tok = n_ >> 1, h = n_ & 1;   // (this thread's B piece, t < 2N)
         for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
             const int tb = u % tblocks;
             const int nt = min(NT, a.act.n - tb * NT);
@@ -165,14 +184,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 *reinterpret_cast<uint4 *>(A + g * 256 + ri * 16) = lo;
                 *reinterpret_cast<uint4 *>(A + g * 256 + 128 + ri * 16) = hi;
                 if (t < 2 * N) {
-                    const int n_ = t >> 1, c = t & 1, tok = n_ >> 1, h = n_ & 1;
                     uint4 v = make_uint4(0, 0, 0, 0);
                     if (c == h && tok < nt)
-                        v = __ldg(reinterpret_cast<const uint4 *>(a.act.q + static_cast<size_t>(tb * NT + tok) * a.act.qstride +
-                                                                  static_cast<size_t>(ks) * 32 + 16 * c));
+                        v = *reinterpret_cast<const uint4 *>(S.packed[ps] + kCodeBytes + tok * kUmmaPackSteps * 32 +
+                                                             (ks % kUmmaPackSteps) * 32 + 16 * c);
                     *reinterpret_cast<uint4 *>(A + 4096 + (n_ >> 3) * 256 + c * 128 + (n_ & 7) * 16) = v;
                 }
-                fence_async_smem();
+                fence_proxy_async();
                 mbar_arrive(&S.ab_full[as]);
                 if ((ks % kUmmaPackSteps) == kUmmaPackSteps - 1) {
                     mbar_arrive(&S.packed_empty[ps]);
@@ -181,7 +199,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 if (++as == kUmmaABStages) as = 0, aph ^= 1;
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == kUmmaEpiWarps + 5) {
         // ---- the MMAs
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_i8(kUmmaRows, N, false, true);
@@ -218,48 +236,69 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
             if (last_as >= 0 && !mbar_wait(&S.ab_empty[last_as], last_aph, kUmmaWaitLimit)) umma_give_up(abort, a.status);
         }
     } else {
-        // ---- the epilogue: warp w < 4 reads TMEM lanes 32 w .. 32 w + 31 (its rows)
-        const int r = warp * 32 + lane;
+        // ---- the epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows) and the columns of tokens
+        // HT (w / 4) .. + HT - 1 of the unit's block
+        const int quarter = warp & 3, half = warp >> 2;
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
         uint32_t tb_ = 0, tph = 0;
-        for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
+        // (every epilogue warp runs the same units: the named barriers below must see all of them, so whether to go
+        // on after a unit is decided once, by thread 0, and read by all after the barrier)
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
             const int T = u / tblocks, tb = u % tblocks;
             const int nt = min(NT, a.act.n - tb * NT);
+            // the unit's per-token block data: (bsum, bsum, scale, scale) of blocks 2 ks, 2 ks + 1
+            for (int i = threadIdx.x; i < NT * KS; i += 32 * kUmmaEpiWarps) {
+                const int tk = i / KS, ks = i - tk * KS;
+                int4 v = make_int4(0, 0, 0, 0);
+                if (tk < nt) {
+                    const size_t so = static_cast<size_t>(tb * NT + tk) * a.act.sstride + 2 * ks;
+                    const int2 bs = __ldg(reinterpret_cast<const int2 *>(a.act.bsum + so));
+                    const float2 sc = __ldg(reinterpret_cast<const float2 *>(a.act.scale + so));
+                    v = make_int4(bs.x, bs.y, __float_as_int(sc.x), __float_as_int(sc.y));
+                }
+                S.tokdata[tk * KS + ks] = v;
+            }
+            epi_sync();
             const int row = T * kUmmaRows + r;
-            const uint8_t *sc = a.w + umma_code_bytes(a.rows, a.cols) + (static_cast<size_t>(T) * G * kUmmaRows + r) * 4;
-            float acc[NT];
+            const uint32_t *sc = reinterpret_cast<const uint32_t *>(a.w + umma_code_bytes(a.rows, a.cols)) +
+                                 static_cast<size_t>(T) * G * kUmmaRows + r;
+            float acc[HT];
 #pragma unroll
-            for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+            for (int j = 0; j < HT; ++j) acc[j] = 0.0f;
             bool ok = true;
             for (int c0 = 0; c0 < KS && ok; c0 += KT) {
+                const int kn = min(KT, KS - c0);
+                uint32_t sw[(KT + 1) / 2];   // the row's scale words of the chunk's K-steps (two K-steps a word)
+#pragma unroll
+                for (int j = 0; j < (KT + 1) / 2; ++j)
+                    sw[j] = 2 * j < kn ? __ldg(sc + static_cast<size_t>((c0 >> 1) + j) * kUmmaRows) : 0u;
                 if (!umma_wait(&S.tm_full[tb_], tph, abort)) {
                     ok = umma_give_up(abort, a.status);
                     break;
                 }
                 tc_fence_after();
-                const int kn = min(KT, KS - c0);
-                for (int kk = 0; kk < kn; ++kk) {
-                    const int ks = c0 + kk;
-                    uint32_t d[N];
+                for (int k0 = 0; k0 < kn; k0 += KB) {
+                    uint32_t d[KB][NT];
 #pragma unroll
-                    for (int j = 0; j < N / 8; ++j) {
-                        uint32_t v[8];
-                        tmem_ld8(tbase + (static_cast<uint32_t>(warp * 32) << 16) + tb_ * 256 + static_cast<uint32_t>(kk * N + 8 * j), v);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) d[8 * j + i] = v[i];
-                    }
+                    for (int j = 0; j < KB; ++j)
+                        if (k0 + j < kn)
+                            tmem_ld<NT>(tbase + lane_off + tb_ * 256 + static_cast<uint32_t>((k0 + j) * N + half * NT), d[j]);
                     tmem_wait_ld();
-                    const uint32_t sw = __ldg(reinterpret_cast<const uint32_t *>(sc + static_cast<size_t>(ks >> 1) * kUmmaRows * 4));
-                    const float2 e = e4m3x2_to_float2((sw >> (16 * (ks & 1))) & 0xFFFFu);
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int b = 2 * ks + h;
-                        const float eb = h ? e.y : e.x;
+                    for (int j = 0; j < KB; ++j) {
+                        if (k0 + j >= kn) break;
+                        const int kk = k0 + j, ks = c0 + kk;
+                        const float2 e = e4m3x2_to_float2((sw[kk >> 1] >> (16 * (kk & 1))) & 0xFFFFu);
 #pragma unroll
-                        for (int t = 0; t < NT; ++t) {
-                            if (t >= nt) break;
-                            const size_t so = static_cast<size_t>(tb * NT + t) * a.act.sstride + b;
-                            const int32_t isum = 2 * static_cast<int32_t>(d[2 * t + h]) - 15 * __ldg(a.act.bsum + so);
-                            acc[t] = __fadd_rn(acc[t], __fmul_rn(static_cast<float>(isum), __fmul_rn(eb, __ldg(a.act.scale + so))));
+                        for (int tl = 0; tl < HT; ++tl) {
+                            const int tk = half * HT + tl;
+                            if (tk >= nt) break;
+                            const int4 td = S.tokdata[tk * KS + ks];
+                            const int32_t s0 = 2 * static_cast<int32_t>(d[j][2 * tl]) - 15 * td.x;
+                            acc[tl] = __fadd_rn(acc[tl], __fmul_rn(static_cast<float>(s0), __fmul_rn(e.x, __int_as_float(td.z))));
+                            const int32_t s1 = 2 * static_cast<int32_t>(d[j][2 * tl + 1]) - 15 * td.y;
+                            acc[tl] = __fadd_rn(acc[tl], __fmul_rn(static_cast<float>(s1), __fmul_rn(e.y, __int_as_float(td.w))));
                         }
                     }
                 }
@@ -267,16 +306,22 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 mbar_arrive(&S.tm_empty[tb_]);
                 if (++tb_ == 2) tb_ = 0, tph ^= 1;
             }
-            if (!ok) break;
+            if (ok) {
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-                if (t < nt) a.y[static_cast<size_t>(tb * NT + t) * a.ystride + row] = __fmul_rn(acc[t], a.global);
+                for (int tl = 0; tl < HT; ++tl) {
+                    const int tk = half * HT + tl;
+                    if (tk < nt) a.y[static_cast<size_t>(tb * NT + tk) * a.ystride + row] = __fmul_rn(acc[tl], a.global);
+                }
+            }
+            if (threadIdx.x == 0) S.epi_stop = (!ok || *abort) ? 1 : 0;
+            epi_sync();   // (every epilogue thread done with the unit's data before the next unit's goes in)
+            if (S.epi_stop) break;
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 9) {
+    if (warp == kUmmaEpiWarps + 5) {
         __syncwarp();
         tmem_dealloc(tbase, 512);
     }

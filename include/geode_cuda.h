@@ -235,7 +235,8 @@ int gcuda_op_norm_quant(const float *d_x, int n, int H, const float *d_w, float 
 int gcuda_op_q4_gemv(const uint8_t *d_tiles, int64_t rows, int64_t cols, float global, const int8_t *d_q,
                      const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream);
 /* The tensor-core (tcgen05) q4 product for any number of token rows. The matrix first goes to its "U" layout
- * (gcuda_op_q4_umma_bytes: 9/16 byte per value, as the pack; rows a multiple of 128, cols of 256; 0 otherwise) from
+ * (gcuda_op_q4_umma_bytes: 9/16 byte per value, as the pack; rows a multiple of 128, cols of 256; 0 otherwise; the
+ * product takes cols up to 4096) from
  * the pack's rows (C/2 code bytes then C/16 E4M3 bytes). y [n][rows] = matvec_rows_q_ref (engine/src/kernels.cpp:
  * 1304-1322) of each of the n quantized rows (q [n][cols], scale and bsum [n][cols/16]), bit for bit: int8 MMAs give
  * each 16-value block's own integer sum, the float chain over the blocks runs in block order. A wait inside the
