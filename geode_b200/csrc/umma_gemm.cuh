@@ -30,6 +30,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "q4_gemv.cuh"
 #include "umma.cuh"
 
@@ -39,7 +40,7 @@ constexpr int kUmmaRows = 128;
 constexpr int kUmmaStepBytes = kUmmaRows * 16;   // one tile's packed codes of one K-step
 constexpr int kUmmaPackSteps = 8;                // K-steps per chunk of bulk copies
 constexpr int kUmmaPackStages = 4;
-constexpr int kUmmaABStages = 8;
+constexpr int kUmmaUnpackBatch = 4;              // K-steps an unpacker thread writes before one proxy fence
 constexpr int kUmmaEpiWarps = 8;                 // two per TMEM lane quarter, each half of the token columns
 constexpr int kUmmaThreads = 32 * (kUmmaEpiWarps + 4 + 2);
 constexpr int kUmmaMaxCols = 4096;
@@ -51,16 +52,18 @@ __host__ __device__ inline size_t umma_code_bytes(int64_t rows, int64_t cols) {
 
 template <int NT>
 struct UmmaSmem {
+    // A/B stages: as many as the shared memory holds next to the rest (a multiple of the unpack batch)
+    static constexpr int kABStages = NT >= 32 ? 8 : NT >= 8 ? 16 : 24;
     static constexpr int N = 2 * NT;                              // MMA columns
     static constexpr int kABBytes = 4096 + N * 32;                // A (128 x 32) then B (N x 32)
     static constexpr int kActBytes = NT * kUmmaPackSteps * 32;    // the chunk's activations: NT tokens x 256 bytes
     static constexpr int kPackBytes = kUmmaPackSteps * kUmmaStepBytes + kActBytes;
     alignas(128) uint8_t packed[kUmmaPackStages][kPackBytes];
-    alignas(128) uint8_t ab[kUmmaABStages][kABBytes];
+    alignas(128) uint8_t ab[kABStages][kABBytes];
     // per token and K-step: the two blocks' activation sums, then their scales' bits (the epilogue's unit data)
     alignas(16) int4 tokdata[NT * (kUmmaMaxCols / 32)];
     uint64_t packed_full[kUmmaPackStages], packed_empty[kUmmaPackStages];
-    uint64_t ab_full[kUmmaABStages], ab_empty[kUmmaABStages];
+    uint64_t ab_full[kABStages], ab_empty[kABStages];
     uint64_t tm_full[2], tm_empty[2];
     uint32_t tmem_base;
     int abort;
@@ -105,7 +108,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     constexpr int N = 2 * NT;
     constexpr int KT = 256 / N;         // K-steps per TMEM buffer (256 columns)
     constexpr int HT = NT / 2;          // tokens per epilogue warp
-    constexpr int KB = NT >= 16 ? 1 : NT == 8 ? 2 : 4;   // K-steps whose TMEM loads go out together
+    constexpr int KB = NT >= 32 ? 1 : 4;   // K-steps whose TMEM loads go out together
     constexpr int kCodeBytes = kUmmaPackSteps * kUmmaStepBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KS = a.cols / 32, G = a.cols / 64;
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     volatile int *abort = &S.abort;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kUmmaPackStages; ++i) mbar_init(&S.packed_full[i], 1), mbar_init(&S.packed_empty[i], 128);
-        for (int i = 0; i < kUmmaABStages; ++i) mbar_init(&S.ab_full[i], 128), mbar_init(&S.ab_empty[i], 1);
+        for (int i = 0; i < UmmaSmem<NT>::kABStages; ++i) mbar_init(&S.ab_full[i], 128), mbar_init(&S.ab_empty[i], 1);
         for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], 32 * kUmmaEpiWarps);
         S.abort = 0;
         fence_barrier_init();
@@ -164,39 +167,49 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
         uint32_t ps = 0, pph = 0, as = 0, aph = 0;
         const int g = t >> 3, ri = t & 7;
         const int n_ = t >> 1, c = t & 1, tok = n_ >> 1, h = n_ & 1;   // (this thread's B piece, t < 2N)
+        constexpr int KU = kUmmaUnpackBatch, AB = UmmaSmem<NT>::kABStages;
         for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
             const int tb = u % tblocks;
             const int nt = min(NT, a.act.n - tb * NT);
-            for (int ks = 0; ks < KS; ++ks) {
-                if ((ks % kUmmaPackSteps) == 0 && !umma_wait(&S.packed_full[ps], pph, abort)) {
+            bool ok = true;
+            for (int k0 = 0; k0 < KS && ok; k0 += KU) {
+                // KU K-steps at once (KS, the chunk and the ring are multiples of KU): their stages free, their packed
+                // rows and activation pieces loaded, written, one fence, then their arrivals
+                if ((k0 % kUmmaPackSteps) == 0 && !umma_wait(&S.packed_full[ps], pph, abort)) ok = false;
+                for (int j = 0; j < KU && ok; ++j)
+                    if (!umma_wait(&S.ab_empty[as + j], aph ^ 1, abort)) ok = false;
+                if (!ok) {
                     umma_give_up(abort, a.status);
                     break;
                 }
-                if (!umma_wait(&S.ab_empty[as], aph ^ 1, abort)) {
-                    umma_give_up(abort, a.status);
-                    break;
+                uint4 x[KU], v[KU];
+#pragma unroll
+                for (int j = 0; j < KU; ++j) {
+                    const int kp = (k0 + j) % kUmmaPackSteps;
+                    x[j] = *reinterpret_cast<const uint4 *>(S.packed[ps] + (kp * kUmmaRows + t) * 16);
+                    v[j] = make_uint4(0, 0, 0, 0);
+                    if (t < 2 * N && c == h && tok < nt)
+                        v[j] = *reinterpret_cast<const uint4 *>(S.packed[ps] + kCodeBytes + tok * kUmmaPackSteps * 32 + kp * 32 + 16 * c);
                 }
-                const uint4 x = *reinterpret_cast<const uint4 *>(S.packed[ps] + ((ks % kUmmaPackSteps) * kUmmaRows + t) * 16);
-                constexpr uint32_t M4 = 0x0F0F0F0Fu;
-                const uint4 lo = make_uint4(x.x & M4, x.y & M4, x.z & M4, x.w & M4);
-                const uint4 hi = make_uint4((x.x >> 4) & M4, (x.y >> 4) & M4, (x.z >> 4) & M4, (x.w >> 4) & M4);
-                uint8_t *A = S.ab[as];
-                *reinterpret_cast<uint4 *>(A + g * 256 + ri * 16) = lo;
-                *reinterpret_cast<uint4 *>(A + g * 256 + 128 + ri * 16) = hi;
-                if (t < 2 * N) {
-                    uint4 v = make_uint4(0, 0, 0, 0);
-                    if (c == h && tok < nt)
-                        v = *reinterpret_cast<const uint4 *>(S.packed[ps] + kCodeBytes + tok * kUmmaPackSteps * 32 +
-                                                             (ks % kUmmaPackSteps) * 32 + 16 * c);
-                    *reinterpret_cast<uint4 *>(A + 4096 + (n_ >> 3) * 256 + c * 128 + (n_ & 7) * 16) = v;
+#pragma unroll
+                for (int j = 0; j < KU; ++j) {
+                    constexpr uint32_t M4 = 0x0F0F0F0Fu;
+                    uint8_t *A = S.ab[as + j];
+                    *reinterpret_cast<uint4 *>(A + g * 256 + ri * 16) =
+                        make_uint4(x[j].x & M4, x[j].y & M4, x[j].z & M4, x[j].w & M4);
+                    *reinterpret_cast<uint4 *>(A + g * 256 + 128 + ri * 16) =
+                        make_uint4((x[j].x >> 4) & M4, (x[j].y >> 4) & M4, (x[j].z >> 4) & M4, (x[j].w >> 4) & M4);
+                    if (t < 2 * N) *reinterpret_cast<uint4 *>(A + 4096 + (n_ >> 3) * 256 + c * 128 + (n_ & 7) * 16) = v[j];
                 }
                 fence_proxy_async();
-                mbar_arrive(&S.ab_full[as]);
-                if ((ks % kUmmaPackSteps) == kUmmaPackSteps - 1) {
+#pragma unroll
+                for (int j = 0; j < KU; ++j) mbar_arrive(&S.ab_full[as + j]);
+                if (((k0 + KU) % kUmmaPackSteps) == 0) {
                     mbar_arrive(&S.packed_empty[ps]);
                     if (++ps == kUmmaPackStages) ps = 0, pph ^= 1;
                 }
-                if (++as == kUmmaABStages) as = 0, aph ^= 1;
+                as += KU;
+                if (as == AB) as = 0, aph ^= 1;
             }
         }
     } else if (warp == kUmmaEpiWarps + 5) {
@@ -224,7 +237,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                     umma_commit(&S.ab_empty[as]);
                     last_as = static_cast<int>(as);
                     last_aph = aph;
-                    if (++as == kUmmaABStages) as = 0, aph ^= 1;
+                    if (++as == UmmaSmem<NT>::kABStages) as = 0, aph ^= 1;
                     if (kk == KT - 1 || ks == KS - 1) {
                         umma_commit(&S.tm_full[tb_]);
                         if (++tb_ == 2) tb_ = 0, tph ^= 1;
@@ -263,9 +276,10 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
             const int row = T * kUmmaRows + r;
             const uint32_t *sc = reinterpret_cast<const uint32_t *>(a.w + umma_code_bytes(a.rows, a.cols)) +
                                  static_cast<size_t>(T) * G * kUmmaRows + r;
-            float acc[HT];
+            uint64_t acc[HT / 2];   // token pairs (2 tp, 2 tp + 1) of this warp's half, as f32x2
 #pragma unroll
-            for (int j = 0; j < HT; ++j) acc[j] = 0.0f;
+            for (int j = 0; j < HT / 2; ++j) acc[j] = 0;
+            const uint64_t zero = static_cast<uint64_t>(static_cast<uint32_t>(a.rows) >> 31);   // +0 pair, runtime
             bool ok = true;
             for (int c0 = 0; c0 < KS && ok; c0 += KT) {
                 const int kn = min(KT, KS - c0);
@@ -290,15 +304,24 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                         if (k0 + j >= kn) break;
                         const int kk = k0 + j, ks = c0 + kk;
                         const float2 e = e4m3x2_to_float2((sw[kk >> 1] >> (16 * (kk & 1))) & 0xFFFFu);
+                        const uint64_t e0 = pack2(__float_as_uint(e.x), __float_as_uint(e.x));
+                        const uint64_t e1 = pack2(__float_as_uint(e.y), __float_as_uint(e.y));
+                        // two tokens at a time in f32x2 lanes (each lane rounded on its own, the product kept apart
+                        // from the add); a token past the block's end has zero sums and scales and is not stored
 #pragma unroll
-                        for (int tl = 0; tl < HT; ++tl) {
-                            const int tk = half * HT + tl;
-                            if (tk >= nt) break;
-                            const int4 td = S.tokdata[tk * KS + ks];
-                            const int32_t s0 = 2 * static_cast<int32_t>(d[j][2 * tl]) - 15 * td.x;
-                            acc[tl] = __fadd_rn(acc[tl], __fmul_rn(static_cast<float>(s0), __fmul_rn(e.x, __int_as_float(td.z))));
-                            const int32_t s1 = 2 * static_cast<int32_t>(d[j][2 * tl + 1]) - 15 * td.y;
-                            acc[tl] = __fadd_rn(acc[tl], __fmul_rn(static_cast<float>(s1), __fmul_rn(e.y, __int_as_float(td.w))));
+                        for (int tp = 0; tp < HT / 2; ++tp) {
+                            const int tk = half * HT + 2 * tp;
+                            const int4 ta = S.tokdata[tk * KS + ks], tbd = S.tokdata[(tk + 1) * KS + ks];
+                            const float fa0 = static_cast<float>(2 * static_cast<int32_t>(d[j][4 * tp]) - 15 * ta.x);
+                            const float fb0 = static_cast<float>(2 * static_cast<int32_t>(d[j][4 * tp + 2]) - 15 * tbd.x);
+                            const float fa1 = static_cast<float>(2 * static_cast<int32_t>(d[j][4 * tp + 1]) - 15 * ta.y);
+                            const float fb1 = static_cast<float>(2 * static_cast<int32_t>(d[j][4 * tp + 3]) - 15 * tbd.y);
+                            const uint64_t p0 = f2_mul_sep(pack2(__float_as_uint(fa0), __float_as_uint(fb0)),
+                                                           f2_mul(e0, pack2(static_cast<uint32_t>(ta.z), static_cast<uint32_t>(tbd.z))), zero);
+                            acc[tp] = f2_add(acc[tp], p0);
+                            const uint64_t p1 = f2_mul_sep(pack2(__float_as_uint(fa1), __float_as_uint(fb1)),
+                                                           f2_mul(e1, pack2(static_cast<uint32_t>(ta.w), static_cast<uint32_t>(tbd.w))), zero);
+                            acc[tp] = f2_add(acc[tp], p1);
                         }
                     }
                 }
@@ -310,7 +333,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
 #pragma unroll
                 for (int tl = 0; tl < HT; ++tl) {
                     const int tk = half * HT + tl;
-                    if (tk < nt) a.y[static_cast<size_t>(tb * NT + tk) * a.ystride + row] = __fmul_rn(acc[tl], a.global);
+                    const float v = (tl & 1) ? hi_f(acc[tl >> 1]) : lo_f(acc[tl >> 1]);
+                    if (tk < nt) a.y[static_cast<size_t>(tb * NT + tk) * a.ystride + row] = __fmul_rn(v, a.global);
                 }
             }
             if (threadIdx.x == 0) S.epi_stop = (!ok || *abort) ? 1 : 0;
