@@ -35,7 +35,7 @@ inline int umma_opt_in() {
         const cudaFuncAttribute at = cudaFuncAttributeMaxDynamicSharedMemorySize;
         const bool ok = cudaFuncSetAttribute(k_umma_gemm<4>, at, umma_launch_smem<4>()) == cudaSuccess &&
                         cudaFuncSetAttribute(k_umma_gemm<8>, at, umma_launch_smem<8>()) == cudaSuccess &&
-                        cudaFuncSetAttribute(k_umma_gemm<32>, at, umma_launch_smem<32>()) == cudaSuccess;
+                        cudaFuncSetAttribute(k_umma_gemm<16>, at, umma_launch_smem<16>()) == cudaSuccess;
         d.umma_rc[dev] = ok ? static_cast<int>(GCUDA_OK) : static_cast<int>(GCUDA_E_CUDA);
     }
     return d.umma_rc[dev];
@@ -45,13 +45,13 @@ inline int umma_opt_in() {
 // persistent CTA an SM at most.
 inline int launch_umma_gemm(UmmaGemmArgs a, cudaStream_t st) {
     if (umma_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
-    const int nt = a.act.n <= 4 ? 4 : a.act.n <= 8 ? 8 : 32;
+    const int nt = a.act.n <= 4 ? 4 : a.act.n <= 8 ? 8 : 16;
     const int units = (a.rows / kUmmaRows) * ((a.act.n + nt - 1) / nt);
     const dim3 grid(std::max(1, std::min(units, sm_count())));
     cudaError_t e;
     if (nt == 4) e = launch_ex(k_umma_gemm<4>, grid, dim3(kUmmaThreads), umma_launch_smem<4>(), st, false, a);
     else if (nt == 8) e = launch_ex(k_umma_gemm<8>, grid, dim3(kUmmaThreads), umma_launch_smem<8>(), st, false, a);
-    else e = launch_ex(k_umma_gemm<32>, grid, dim3(kUmmaThreads), umma_launch_smem<32>(), st, false, a);
+    else e = launch_ex(k_umma_gemm<16>, grid, dim3(kUmmaThreads), umma_launch_smem<16>(), st, false, a);
     return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }
 

@@ -39,8 +39,7 @@ namespace gcu {
 constexpr int kUmmaRows = 128;
 constexpr int kUmmaStepBytes = kUmmaRows * 16;   // one tile's packed codes of one K-step
 constexpr int kUmmaPackSteps = 8;                // K-steps per chunk of bulk copies
-constexpr int kUmmaPackStages = 4;
-constexpr int kUmmaUnpackBatch = 4;              // K-steps an unpacker thread writes before one proxy fence
+constexpr int kUmmaUnpackBatch = kUmmaPackSteps; // K-steps an unpacker thread writes before one proxy fence
 constexpr int kUmmaEpiWarps = 8;                 // two per TMEM lane quarter, each half of the token columns
 constexpr int kUmmaThreads = 32 * (kUmmaEpiWarps + 4 + 2);
 constexpr int kUmmaMaxCols = 4096;
@@ -53,17 +52,19 @@ __host__ __device__ inline size_t umma_code_bytes(int64_t rows, int64_t cols) {
 template <int NT>
 struct UmmaSmem {
     // A/B stages: as many as the shared memory holds next to the rest (a multiple of the unpack batch)
-    static constexpr int kABStages = NT >= 32 ? 8 : NT >= 8 ? 16 : 24;
+    static constexpr int kABStages = NT >= 8 ? 16 : 24;
+    static constexpr int kPackStages = NT >= 32 ? 2 : 4;
     static constexpr int N = 2 * NT;                              // MMA columns
     static constexpr int kABBytes = 4096 + N * 32;                // A (128 x 32) then B (N x 32)
     static constexpr int kActBytes = NT * kUmmaPackSteps * 32;    // the chunk's activations: NT tokens x 256 bytes
     static constexpr int kPackBytes = kUmmaPackSteps * kUmmaStepBytes + kActBytes;
-    alignas(128) uint8_t packed[kUmmaPackStages][kPackBytes];
+    alignas(128) uint8_t packed[kPackStages][kPackBytes];
     alignas(128) uint8_t ab[kABStages][kABBytes];
     // per token and K-step: the two blocks' activation sums, then their scales' bits (the epilogue's unit data)
     alignas(16) int4 tokdata[NT * (kUmmaMaxCols / 32)];
-    uint64_t packed_full[kUmmaPackStages], packed_empty[kUmmaPackStages];
-    uint64_t ab_full[kABStages], ab_empty[kABStages];
+    uint64_t packed_full[kPackStages], packed_empty[kPackStages];
+    // the A/B ring moves in batches of kUmmaUnpackBatch stages: one full / one empty barrier per batch
+    uint64_t ab_full[kABStages / kUmmaUnpackBatch], ab_empty[kABStages / kUmmaUnpackBatch];
     uint64_t tm_full[2], tm_empty[2];
     uint32_t tmem_base;
     int abort;
@@ -108,16 +109,19 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     constexpr int N = 2 * NT;
     constexpr int KT = 256 / N;         // K-steps per TMEM buffer (256 columns)
     constexpr int HT = NT / 2;          // tokens per epilogue warp
-    constexpr int KB = NT >= 32 ? 1 : 4;   // K-steps whose TMEM loads go out together
+    constexpr int KB = NT >= 16 ? 1 : 4;   // K-steps whose TMEM loads go out together (a group)
     constexpr int kCodeBytes = kUmmaPackSteps * kUmmaStepBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KS = a.cols / 32, G = a.cols / 64;
     const int tiles = a.rows / kUmmaRows, tblocks = (a.act.n + NT - 1) / NT, units = tiles * tblocks;
     volatile int *abort = &S.abort;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kUmmaPackStages; ++i) mbar_init(&S.packed_full[i], 1), mbar_init(&S.packed_empty[i], 128);
-        for (int i = 0; i < UmmaSmem<NT>::kABStages; ++i) mbar_init(&S.ab_full[i], 128), mbar_init(&S.ab_empty[i], 1);
-        for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], 32 * kUmmaEpiWarps);
+        // (consumer barriers count warps: each warp's lanes finish, sync, then one lane arrives - 128 arrivals on one
+        // barrier would serialise on its shared-memory word)
+        for (int i = 0; i < UmmaSmem<NT>::kPackStages; ++i) mbar_init(&S.packed_full[i], 1), mbar_init(&S.packed_empty[i], 4);
+        for (int i = 0; i < UmmaSmem<NT>::kABStages / kUmmaUnpackBatch; ++i)
+            mbar_init(&S.ab_full[i], 4), mbar_init(&S.ab_empty[i], 1);
+        for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], kUmmaEpiWarps);
         S.abort = 0;
         fence_barrier_init();
     }
@@ -134,8 +138,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
         // ---- bulk copies: per chunk of 8 K-steps the tile's packed codes (16 KB) and each token's 256 activations
         if (lane == 0) {
             uint32_t s = 0, ph = 0;
-            int last_ph[kUmmaPackStages];
-            for (int i = 0; i < kUmmaPackStages; ++i) last_ph[i] = -1;
+            int last_ph[UmmaSmem<NT>::kPackStages];
+            for (int i = 0; i < UmmaSmem<NT>::kPackStages; ++i) last_ph[i] = -1;
             for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
                 const int T = u / tblocks, tb = u % tblocks;
                 const int nt = min(NT, a.act.n - tb * NT);
@@ -152,12 +156,12 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                                  a.act.q + static_cast<size_t>(tb * NT + tok) * a.act.qstride + static_cast<size_t>(pc) * kUmmaPackSteps * 32,
                                  kUmmaPackSteps * 32, &S.packed_full[s]);
                     last_ph[s] = static_cast<int>(ph);
-                    if (++s == kUmmaPackStages) s = 0, ph ^= 1;
+                    if (++s == UmmaSmem<NT>::kPackStages) s = 0, ph ^= 1;
                 }
             }
             // no copy may still be writing this CTA's shared memory when it leaves (after a give-up the unpackers
             // stop consuming): wait for each stage's last fill, bounded
-            for (int i = 0; i < kUmmaPackStages; ++i)
+            for (int i = 0; i < UmmaSmem<NT>::kPackStages; ++i)
                 if (last_ph[i] >= 0 && !mbar_wait(&S.packed_full[i], static_cast<uint32_t>(last_ph[i]), kUmmaWaitLimit))
                     umma_give_up(abort, a.status);
         }
@@ -176,8 +180,8 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 // KU K-steps at once (KS, the chunk and the ring are multiples of KU): their stages free, their packed
                 // rows and activation pieces loaded, written, one fence, then their arrivals
                 if ((k0 % kUmmaPackSteps) == 0 && !umma_wait(&S.packed_full[ps], pph, abort)) ok = false;
-                for (int j = 0; j < KU && ok; ++j)
-                    if (!umma_wait(&S.ab_empty[as + j], aph ^ 1, abort)) ok = false;
+                if (ok && !umma_wait(&S.ab_empty[as / KU], aph ^ 1, abort)) ok = false;
+                ok = __all_sync(0xffffffffu, ok);   // (the warp syncs below: its lanes go on, or stop, together)
                 if (!ok) {
                     umma_give_up(abort, a.status);
                     break;
@@ -202,11 +206,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                     if (t < 2 * N) *reinterpret_cast<uint4 *>(A + 4096 + (n_ >> 3) * 256 + c * 128 + (n_ & 7) * 16) = v[j];
                 }
                 fence_proxy_async();
-#pragma unroll
-                for (int j = 0; j < KU; ++j) mbar_arrive(&S.ab_full[as + j]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.ab_full[as / KU]);
                 if (((k0 + KU) % kUmmaPackSteps) == 0) {
-                    mbar_arrive(&S.packed_empty[ps]);
-                    if (++ps == kUmmaPackStages) ps = 0, pph ^= 1;
+                    if (lane == 0) mbar_arrive(&S.packed_empty[ps]);
+                    if (++ps == UmmaSmem<NT>::kPackStages) ps = 0, pph ^= 1;
                 }
                 as += KU;
                 if (as == AB) as = 0, aph ^= 1;
@@ -219,29 +223,40 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
             uint32_t as = 0, aph = 0, tb_ = 0, tph = 0;
             int last_as = -1;   // the stage of the last MMA issued, and the phase its commit completes
             uint32_t last_aph = 0;
+            constexpr int KU = kUmmaUnpackBatch, AB = UmmaSmem<NT>::kABStages;
             for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
-                for (int ks = 0; ks < KS; ++ks) {
-                    const int kk = ks % KT;
-                    if (kk == 0 && !umma_wait(&S.tm_empty[tb_], tph ^ 1, abort)) {
-                        umma_give_up(abort, a.status);
-                        break;
-                    }
-                    if (!umma_wait(&S.ab_full[as], aph, abort)) {
-                        umma_give_up(abort, a.status);
+                bool ok = true;
+                for (int k0 = 0; k0 < KS && ok; k0 += KU) {
+                    // one batch: its KU MMAs (a TMEM buffer handed over at each chunk's end, which may fall inside the
+                    // batch), then one commit that frees the batch's stages
+                    if (!umma_wait(&S.ab_full[as / KU], aph, abort)) {
+                        ok = umma_give_up(abort, a.status);
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t ab = smem_u32(S.ab[as]);
-                    umma_i8(tbase + tb_ * 256 + static_cast<uint32_t>(kk * N), umma_smem_desc(ab, 128, 256),
-                            umma_smem_desc(ab + 4096, 128, 256), idesc, false);
-                    umma_commit(&S.ab_empty[as]);
-                    last_as = static_cast<int>(as);
-                    last_aph = aph;
-                    if (++as == UmmaSmem<NT>::kABStages) as = 0, aph ^= 1;
-                    if (kk == KT - 1 || ks == KS - 1) {
-                        umma_commit(&S.tm_full[tb_]);
-                        if (++tb_ == 2) tb_ = 0, tph ^= 1;
+                    for (int j = 0; j < KU && ok; ++j) {
+                        const int ks = k0 + j, kk = ks % KT;
+                        if (kk == 0) {
+                            if (!umma_wait(&S.tm_empty[tb_], tph ^ 1, abort)) {
+                                ok = umma_give_up(abort, a.status);
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        const uint32_t ab = smem_u32(S.ab[as + j]);
+                        umma_i8(tbase + tb_ * 256 + static_cast<uint32_t>(kk * N), umma_smem_desc(ab, 128, 256),
+                                umma_smem_desc(ab + 4096, 128, 256), idesc, false);
+                        if (kk == KT - 1 || ks == KS - 1) {
+                            umma_commit(&S.tm_full[tb_]);
+                            if (++tb_ == 2) tb_ = 0, tph ^= 1;
+                        }
                     }
+                    // (also after a give-up inside the batch: the commit then covers the MMAs it did issue)
+                    umma_commit(&S.ab_empty[as / KU]);
+                    last_as = static_cast<int>(as / KU);
+                    last_aph = aph;
+                    as += KU;
+                    if (as == AB) as = 0, aph ^= 1;
                 }
             }
             // every MMA this thread issued has finished before the tensor memory is freed (its last commit covers
@@ -287,18 +302,21 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
 #pragma unroll
                 for (int j = 0; j < (KT + 1) / 2; ++j)
                     sw[j] = 2 * j < kn ? __ldg(sc + static_cast<size_t>((c0 >> 1) + j) * kUmmaRows) : 0u;
-                if (!umma_wait(&S.tm_full[tb_], tph, abort)) {
+                if (!__all_sync(0xffffffffu, umma_wait(&S.tm_full[tb_], tph, abort))) {   // (warp-uniform: syncs below)
                     ok = umma_give_up(abort, a.status);
                     break;
                 }
                 tc_fence_after();
-                for (int k0 = 0; k0 < kn; k0 += KB) {
-                    uint32_t d[KB][NT];
+                // groups of KB K-steps, two register buffers: the next group's TMEM loads are in flight while this
+                // group's chains run (tcgen05.wait::ld waits for every load issued, so one group is waited at a time)
+                uint32_t dA[KB][NT], dB[KB][NT];
+                auto load_group = [&](int k0, uint32_t (&d)[KB][NT]) {
 #pragma unroll
                     for (int j = 0; j < KB; ++j)
                         if (k0 + j < kn)
                             tmem_ld<NT>(tbase + lane_off + tb_ * 256 + static_cast<uint32_t>((k0 + j) * N + half * NT), d[j]);
-                    tmem_wait_ld();
+                };
+                auto chain_group = [&](int k0, const uint32_t (&d)[KB][NT]) {
 #pragma unroll
                     for (int j = 0; j < KB; ++j) {
                         if (k0 + j >= kn) break;
@@ -324,9 +342,22 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                             acc[tp] = f2_add(acc[tp], p1);
                         }
                     }
+                };
+                load_group(0, dA);
+                tmem_wait_ld();
+                for (int k0 = 0; k0 < kn; k0 += 2 * KB) {
+                    if (k0 + KB < kn) load_group(k0 + KB, dB);
+                    chain_group(k0, dA);
+                    tmem_wait_ld();
+                    if (k0 + KB < kn) {
+                        if (k0 + 2 * KB < kn) load_group(k0 + 2 * KB, dA);
+                        chain_group(k0 + KB, dB);
+                        tmem_wait_ld();
+                    }
                 }
                 tc_fence_before();
-                mbar_arrive(&S.tm_empty[tb_]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.tm_empty[tb_]);
                 if (++tb_ == 2) tb_ = 0, tph ^= 1;
             }
             if (ok) {
