@@ -25,6 +25,13 @@ __host__ __device__ constexpr uint64_t umma_smem_desc(uint32_t smem_addr, uint32
            (static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32) | (static_cast<uint64_t>(1) << 46);
 }
 
+// The same for the K-major layout with the 128-byte swizzle (layout type 2): an atom of 8 rows x 128 bytes, the 16-byte
+// chunk c of row r stored at chunk c ^ (r % 8); atoms along M (or N) `sbo` bytes apart; the leading byte offset is
+// fixed at 16 bytes (one K-atom per operand here). A K step inside the atom advances the start address by its bytes.
+__host__ __device__ constexpr uint64_t umma_smem_desc_sw128(uint32_t smem_addr, uint32_t sbo_bytes) {
+    return umma_smem_desc(smem_addr, 16, sbo_bytes) | (static_cast<uint64_t>(2) << 61);
+}
+
 // int8 x int8 -> s32, both operands K-major; a_signed / b_signed: s8 (else u8)
 __host__ __device__ constexpr uint32_t umma_idesc_i8(int M, int N, bool a_signed, bool b_signed) {
     return (2u << 4) | ((a_signed ? 1u : 0u) << 7) | ((b_signed ? 1u : 0u) << 10) |

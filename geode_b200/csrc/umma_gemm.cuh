@@ -19,10 +19,13 @@
 // A CTA (persistent over units = (tile, block of NT tokens)) runs four roles on its own rings:
 //   warp 12 lane 0: per chunk of 8 K-steps, bulk copies (cp.async.bulk, mbarrier complete_tx) of the tile's packed
 //              codes (16 KB) and of each token's 256 activations;
-//   warps 8-11: per K-step each thread unpacks its row into the A stage (8 rows x 16 B core matrices, the two K halves
-//              128 B apart, row groups 256 B apart) and the first 2N threads write B's 16-byte pieces;
-//   warp 13 lane 0: one MMA per K-step into the TMEM buffer of the current chunk (two buffers of 256 columns), a
-//              commit that frees the A stage, a commit per chunk that hands the buffer to the epilogue;
+//   warps 8-11: per batch of 8 K-steps each thread unpacks its row into the batch's A (the K-major layout with the
+//              128-byte swizzle: K-atoms of 8 rows x 128 bytes, four K-steps each; the tensor core reads it at full
+//              shared-memory width, where the unswizzled layout made each MMA take about 200 ns) and the first 2N
+//              threads write B's 16-byte pieces; one proxy fence a batch;
+//   warp 13 lane 0: per batch, its 8 MMAs (descriptors 32 bytes further into the K-atom per step) into the TMEM
+//              buffer of the current chunk (two buffers of 256 columns), a commit that frees the batch, a commit per
+//              chunk that hands the buffer to the epilogue;
 //   warps 0-7: two warps per TMEM lane quarter (the rows), each with half of the unit's tokens: per chunk its rows'
 //              scale words, then its columns (tcgen05.ld, several K-steps before one wait) into its tokens' chains,
 //              with the unit's per-token block sums and scales staged in shared memory; y = chain * global.
@@ -51,20 +54,23 @@ __host__ __device__ inline size_t umma_code_bytes(int64_t rows, int64_t cols) {
 
 template <int NT>
 struct UmmaSmem {
-    // A/B stages: as many as the shared memory holds next to the rest (a multiple of the unpack batch)
-    static constexpr int kABStages = NT >= 8 ? 16 : 24;
-    static constexpr int kPackStages = NT >= 32 ? 2 : 4;
+    // A/B batches (8 K-steps each): as many as the shared memory holds next to the rest
+    static constexpr int kABBatches = NT >= 8 ? 2 : 3;
+    static constexpr int kPackStages = 4;
     static constexpr int N = 2 * NT;                              // MMA columns
-    static constexpr int kABBytes = 4096 + N * 32;                // A (128 x 32) then B (N x 32)
+    // a batch: two K-atoms of A (128 rows x 128 bytes = four K-steps each, 128-byte swizzle), then B's two K-atoms
+    // (N rows x 128 bytes each); every atom 1024-byte aligned (the swizzle repeats every 8 rows of 128 bytes)
+    static constexpr int kAAtomBytes = kUmmaRows * 128;
+    static constexpr int kBAtomBytes = N * 128;
+    static constexpr int kABBatchBytes = 2 * kAAtomBytes + 2 * kBAtomBytes;
     static constexpr int kActBytes = NT * kUmmaPackSteps * 32;    // the chunk's activations: NT tokens x 256 bytes
     static constexpr int kPackBytes = kUmmaPackSteps * kUmmaStepBytes + kActBytes;
+    alignas(1024) uint8_t ab[kABBatches][kABBatchBytes];
     alignas(128) uint8_t packed[kPackStages][kPackBytes];
-    alignas(128) uint8_t ab[kABStages][kABBytes];
     // per token and K-step: the two blocks' activation sums, then their scales' bits (the epilogue's unit data)
     alignas(16) int4 tokdata[NT * (kUmmaMaxCols / 32)];
     uint64_t packed_full[kPackStages], packed_empty[kPackStages];
-    // the A/B ring moves in batches of kUmmaUnpackBatch stages: one full / one empty barrier per batch
-    uint64_t ab_full[kABStages / kUmmaUnpackBatch], ab_empty[kABStages / kUmmaUnpackBatch];
+    uint64_t ab_full[kABBatches], ab_empty[kABBatches];
     uint64_t tm_full[2], tm_empty[2];
     uint32_t tmem_base;
     int abort;
@@ -82,7 +88,7 @@ struct UmmaGemmArgs {
 };
 
 template <int NT>
-__host__ __device__ constexpr size_t umma_smem_bytes() { return sizeof(UmmaSmem<NT>) + 128; }
+__host__ __device__ constexpr size_t umma_smem_bytes() { return sizeof(UmmaSmem<NT>) + 1024; }
 
 #if defined(__CUDA_ARCH__)
 __device__ __forceinline__ bool umma_give_up(volatile int *abort, uint32_t *status) {
@@ -105,7 +111,7 @@ template <int NT>
 __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
 #if defined(__CUDA_ARCH__)
     extern __shared__ uint8_t smem_raw[];
-    UmmaSmem<NT> &S = *reinterpret_cast<UmmaSmem<NT> *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    UmmaSmem<NT> &S = *reinterpret_cast<UmmaSmem<NT> *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     constexpr int N = 2 * NT;
     constexpr int KT = 256 / N;         // K-steps per TMEM buffer (256 columns)
     constexpr int HT = NT / 2;          // tokens per epilogue warp
@@ -119,8 +125,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
         // (consumer barriers count warps: each warp's lanes finish, sync, then one lane arrives - 128 arrivals on one
         // barrier would serialise on its shared-memory word)
         for (int i = 0; i < UmmaSmem<NT>::kPackStages; ++i) mbar_init(&S.packed_full[i], 1), mbar_init(&S.packed_empty[i], 4);
-        for (int i = 0; i < UmmaSmem<NT>::kABStages / kUmmaUnpackBatch; ++i)
-            mbar_init(&S.ab_full[i], 4), mbar_init(&S.ab_empty[i], 1);
+        for (int i = 0; i < UmmaSmem<NT>::kABBatches; ++i) mbar_init(&S.ab_full[i], 4), mbar_init(&S.ab_empty[i], 1);
         for (int i = 0; i < 2; ++i) mbar_init(&S.tm_full[i], 1), mbar_init(&S.tm_empty[i], kUmmaEpiWarps);
         S.abort = 0;
         fence_barrier_init();
@@ -169,9 +174,11 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
         // ---- unpack A (a thread a row), write B's 16-byte pieces from the staged activations
         const int t = threadIdx.x - 32 * kUmmaEpiWarps;
         uint32_t ps = 0, pph = 0, as = 0, aph = 0;
-        const int g = t >> 3, ri = t & 7;
+        const int ri = t & 7;
         const int n_ = t >> 1, c = t & 1, tok = n_ >> 1, h = n_ & 1;   // (this thread's B piece, t < 2N)
-        constexpr int KU = kUmmaUnpackBatch, AB = UmmaSmem<NT>::kABStages;
+        constexpr int KU = kUmmaUnpackBatch, NB = UmmaSmem<NT>::kABBatches;
+        // this thread's row in an A atom and its B row (128-byte swizzle: chunk q of the row at chunk q ^ (row % 8))
+        const int a_row = (t >> 3) * 1024 + ri * 128, b_row = (n_ >> 3) * 1024 + (n_ & 7) * 128;
         for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
             const int tb = u % tblocks;
             const int nt = min(NT, a.act.n - tb * NT);
@@ -180,7 +187,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 // KU K-steps at once (KS, the chunk and the ring are multiples of KU): their stages free, their packed
                 // rows and activation pieces loaded, written, one fence, then their arrivals
                 if ((k0 % kUmmaPackSteps) == 0 && !umma_wait(&S.packed_full[ps], pph, abort)) ok = false;
-                if (ok && !umma_wait(&S.ab_empty[as / KU], aph ^ 1, abort)) ok = false;
+                if (ok && !umma_wait(&S.ab_empty[as], aph ^ 1, abort)) ok = false;
                 ok = __all_sync(0xffffffffu, ok);   // (the warp syncs below: its lanes go on, or stop, together)
                 if (!ok) {
                     umma_give_up(abort, a.status);
@@ -198,22 +205,24 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
 #pragma unroll
                 for (int j = 0; j < KU; ++j) {
                     constexpr uint32_t M4 = 0x0F0F0F0Fu;
-                    uint8_t *A = S.ab[as + j];
-                    *reinterpret_cast<uint4 *>(A + g * 256 + ri * 16) =
+                    const int ka = j >> 2, kq = j & 3;   // K-atom of the batch, K-step inside it (32 bytes)
+                    uint8_t *A = S.ab[as] + ka * UmmaSmem<NT>::kAAtomBytes + a_row;
+                    *reinterpret_cast<uint4 *>(A + (((2 * kq) ^ ri) << 4)) =
                         make_uint4(x[j].x & M4, x[j].y & M4, x[j].z & M4, x[j].w & M4);
-                    *reinterpret_cast<uint4 *>(A + g * 256 + 128 + ri * 16) =
+                    *reinterpret_cast<uint4 *>(A + (((2 * kq + 1) ^ ri) << 4)) =
                         make_uint4((x[j].x >> 4) & M4, (x[j].y >> 4) & M4, (x[j].z >> 4) & M4, (x[j].w >> 4) & M4);
-                    if (t < 2 * N) *reinterpret_cast<uint4 *>(A + 4096 + (n_ >> 3) * 256 + c * 128 + (n_ & 7) * 16) = v[j];
+                    if (t < 2 * N)
+                        *reinterpret_cast<uint4 *>(S.ab[as] + 2 * UmmaSmem<NT>::kAAtomBytes + ka * UmmaSmem<NT>::kBAtomBytes +
+                                                   b_row + (((2 * kq + c) ^ (n_ & 7)) << 4)) = v[j];
                 }
                 fence_proxy_async();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&S.ab_full[as / KU]);
+                if (lane == 0) mbar_arrive(&S.ab_full[as]);
                 if (((k0 + KU) % kUmmaPackSteps) == 0) {
                     if (lane == 0) mbar_arrive(&S.packed_empty[ps]);
                     if (++ps == UmmaSmem<NT>::kPackStages) ps = 0, pph ^= 1;
                 }
-                as += KU;
-                if (as == AB) as = 0, aph ^= 1;
+                if (++as == NB) as = 0, aph ^= 1;
             }
         }
     } else if (warp == kUmmaEpiWarps + 5) {
@@ -223,13 +232,13 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
             uint32_t as = 0, aph = 0, tb_ = 0, tph = 0;
             int last_as = -1;   // the stage of the last MMA issued, and the phase its commit completes
             uint32_t last_aph = 0;
-            constexpr int KU = kUmmaUnpackBatch, AB = UmmaSmem<NT>::kABStages;
+            constexpr int KU = kUmmaUnpackBatch, NB = UmmaSmem<NT>::kABBatches;
             for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
                 bool ok = true;
                 for (int k0 = 0; k0 < KS && ok; k0 += KU) {
                     // one batch: its KU MMAs (a TMEM buffer handed over at each chunk's end, which may fall inside the
                     // batch), then one commit that frees the batch's stages
-                    if (!umma_wait(&S.ab_full[as / KU], aph, abort)) {
+                    if (!umma_wait(&S.ab_full[as], aph, abort)) {
                         ok = umma_give_up(abort, a.status);
                         break;
                     }
@@ -243,20 +252,22 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                             }
                             tc_fence_after();
                         }
-                        const uint32_t ab = smem_u32(S.ab[as + j]);
-                        umma_i8(tbase + tb_ * 256 + static_cast<uint32_t>(kk * N), umma_smem_desc(ab, 128, 256),
-                                umma_smem_desc(ab + 4096, 128, 256), idesc, false);
+                        // K-step j: K-atom j / 4, 32 bytes further into it per step
+                        const uint32_t ab = smem_u32(S.ab[as]) + static_cast<uint32_t>((j & 3) * 32);
+                        const uint32_t a_at = ab + static_cast<uint32_t>((j >> 2) * UmmaSmem<NT>::kAAtomBytes);
+                        const uint32_t b_at = ab + static_cast<uint32_t>(2 * UmmaSmem<NT>::kAAtomBytes + (j >> 2) * UmmaSmem<NT>::kBAtomBytes);
+                        umma_i8(tbase + tb_ * 256 + static_cast<uint32_t>(kk * N), umma_smem_desc_sw128(a_at, 1024),
+                                umma_smem_desc_sw128(b_at, 1024), idesc, false);
                         if (kk == KT - 1 || ks == KS - 1) {
                             umma_commit(&S.tm_full[tb_]);
                             if (++tb_ == 2) tb_ = 0, tph ^= 1;
                         }
                     }
                     // (also after a give-up inside the batch: the commit then covers the MMAs it did issue)
-                    umma_commit(&S.ab_empty[as / KU]);
-                    last_as = static_cast<int>(as / KU);
+                    umma_commit(&S.ab_empty[as]);
+                    last_as = static_cast<int>(as);
                     last_aph = aph;
-                    as += KU;
-                    if (as == AB) as = 0, aph ^= 1;
+                    if (++as == NB) as = 0, aph ^= 1;
                 }
             }
             // every MMA this thread issued has finished before the tensor memory is freed (its last commit covers

@@ -24,6 +24,18 @@ int check_smem() {
     return want != got;
 }
 
+// int8, K-major, 128-byte swizzle (CuTe's Layout_K_SW128_Atom tiled to Rows x 128): an atom of 8 rows x 128 bytes (four
+// K = 32 steps), row groups 1024 bytes apart
+template <int Rows>
+int check_smem_sw128() {
+    auto layout = tile_to_shape(UMMA::Layout_K_SW128_Atom<uint8_t>{}, make_shape(Int<Rows>{}, Int<128>{}));
+    auto t = make_tensor(make_smem_ptr(reinterpret_cast<uint8_t *>(0)), layout);
+    const uint64_t want = static_cast<uint64_t>(UMMA::make_umma_desc<UMMA::Major::K>(t));
+    const uint64_t got = gcu::umma_smem_desc_sw128(0, 1024);
+    std::printf("smem sw128 rows %d: cute %016llx ours %016llx\n", Rows, (unsigned long long)want, (unsigned long long)got);
+    return want != got;
+}
+
 template <int M, int N, class A, class B>
 int check_idesc() {
     const uint32_t want = static_cast<uint32_t>(
@@ -39,6 +51,8 @@ int main() {
     bad += check_smem<8, 128, 0>();   // (one group of 8 rows: the stride between groups is unused, CuTe writes 0)
     bad += check_smem<64, 128, 256>();
     bad += check_smem<128, 2048, 16>();
+    bad += check_smem_sw128<128>();
+    bad += check_smem_sw128<64>();
     bad += check_idesc<128, 8, uint8_t, int8_t>();
     bad += check_idesc<128, 16, uint8_t, int8_t>();
     bad += check_idesc<128, 64, uint8_t, int8_t>();
