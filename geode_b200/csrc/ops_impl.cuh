@@ -9,8 +9,15 @@
 #include "small_kernels.cuh"
 #include "launch.hpp"
 #include "umma_gemm.cuh"
+#include "moe_umma.cuh"
 
 using namespace gcu;
+
+#define RC_GRID(call)                       \
+    do {                                    \
+        const int r_ = (call);              \
+        if (r_ != GCUDA_OK) return r_;      \
+    } while (0)
 
 namespace gcu {
 // out[i] = expf_ref of the float whose bits are first + i (the test hook gcuda_debug_expf_table)
@@ -55,6 +62,15 @@ inline int launch_umma_gemm(UmmaGemmArgs a, cudaStream_t st) {
     return e == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
 }
 
+// the grouped form: the unit count lives on the device, so every SM gets a CTA (up to the table's capacity)
+inline int launch_umma_grouped(UmmaGemmArgs a, int cap, cudaStream_t st) {
+    if (umma_opt_in() != GCUDA_OK) return GCUDA_E_CUDA;
+    const dim3 grid(std::max(1, std::min(cap, sm_count())));
+    return launch_ex(k_umma_gemm<kMoeNT>, grid, dim3(kUmmaThreads), umma_launch_smem<kMoeNT>(), st, false, a) == cudaSuccess
+               ? GCUDA_OK
+               : GCUDA_E_CUDA;
+}
+
 }  // namespace gcu
 
 extern "C" {
@@ -71,6 +87,88 @@ int gcuda_op_status(int clear) {
 size_t gcuda_op_q4_umma_bytes(int64_t rows, int64_t cols) {
     if (rows <= 0 || rows % kUmmaRows || cols <= 0 || cols % 256) return 0;
     return static_cast<size_t>(rows) * static_cast<size_t>(cols) / 16 * 9;
+}
+
+size_t gcuda_op_moe_umma_expert_bytes(int H, int ff) {
+    const size_t gu = gcuda_op_q4_umma_bytes(2 * static_cast<int64_t>(ff), H), dn = gcuda_op_q4_umma_bytes(H, ff);
+    return gu && dn ? gu + dn : 0;
+}
+
+size_t gcuda_op_moe_umma_work_bytes(int n, int K, int E, int H, int ff) {
+    if (n < 1 || K < 1 || E < 1 || E > kMoeMaxExperts || gcuda_op_moe_umma_expert_bytes(H, ff) == 0) return 0;
+    return moe_work_layout(n, K, E, H, ff, nullptr, nullptr);
+}
+
+int gcuda_op_moe_umma_relayout(const uint8_t *d_pack, size_t pack_stride, int E, int H, int ff, uint8_t *d_u,
+                               void *stream) {
+    const size_t eb = gcuda_op_moe_umma_expert_bytes(H, ff);
+    const size_t gu = gcuda_op_q4_umma_bytes(2 * static_cast<int64_t>(ff), H);
+    if (!d_pack || !d_u || eb == 0 || E < 1 || pack_stride < eb || (reinterpret_cast<uintptr_t>(d_u) & 15)) return GCUDA_E_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int e = 0; e < E; ++e) {   // (each expert's pack block: gate_up rows, then down rows - the same bytes, relaid)
+        const uint8_t *src = d_pack + static_cast<size_t>(e) * pack_stride;
+        uint8_t *dst = d_u + static_cast<size_t>(e) * eb;
+        k_umma_relayout<<<148 * 4, 256, 0, st>>>(src, 2 * static_cast<int64_t>(ff), H, dst);
+        k_umma_relayout<<<148 * 4, 256, 0, st>>>(src + gu, H, ff, dst + gu);
+        count_launch(2);
+    }
+    return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+int gcuda_op_moe_umma(const uint8_t *d_u, const float *d_globals, int E, int H, int ff, const int8_t *d_q,
+                      const float *d_scale, const int32_t *d_bsum, int n, const int *d_ids, int K, float *d_out,
+                      void *d_work, size_t work_bytes, void *stream) {
+    const size_t need = gcuda_op_moe_umma_work_bytes(n, K, E, H, ff);
+    if (!d_u || !d_globals || !d_q || !d_scale || !d_bsum || !d_ids || !d_out || !d_work || need == 0 ||
+        work_bytes < need || H > kUmmaMaxCols || ff > kUmmaMaxCols || (reinterpret_cast<uintptr_t>(d_work) & 255) ||
+        (reinterpret_cast<uintptr_t>(d_u) & 15) || (reinterpret_cast<uintptr_t>(d_q) & 15) ||
+        static_cast<int64_t>(n) * K > (1 << 24))
+        return GCUDA_E_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t *status = device_status();
+    if (!status) return GCUDA_E_CUDA;
+    MoeWork w{};
+    moe_work_layout(n, K, E, H, ff, static_cast<uint8_t *>(d_work), &w);
+    const int P = n * K;
+    MoePlanArgs pa{};
+    pa.ids = d_ids;
+    pa.P = P;
+    pa.E = E;
+    pa.experts = d_u;
+    pa.stride = gcuda_op_moe_umma_expert_bytes(H, ff);
+    pa.gu_bytes = gcuda_op_q4_umma_bytes(2 * static_cast<int64_t>(ff), H);
+    pa.globals = d_globals;
+    pa.tiles_gu = 2 * ff / kUmmaRows;
+    pa.tiles_dn = H / kUmmaRows;
+    pa.w = w;
+    pa.status = status;
+    if (launch_ex(k_moe_plan, dim3(1), dim3(kMoePlanThreads), 0, st, false, pa) != cudaSuccess) return GCUDA_E_CUDA;
+    UmmaGemmArgs a{};
+    a.rows = 2 * ff;
+    a.cols = H;
+    a.act = ActSet{d_q, d_scale, d_bsum, H, n, H, H / 16};
+    a.y = w.gu;
+    a.ystride = 2 * ff;
+    a.status = status;
+    a.units = w.units_gu;
+    a.n_units = w.counts;
+    a.toklist = w.toklist;
+    a.act_div = K;
+    RC_GRID(launch_umma_grouped(a, w.cap_gu, st));
+    const int64_t work = static_cast<int64_t>(P) * ff;
+    if (launch_ex(k_swiglu_quant, dim3(static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 16))), dim3(256), 0, st,
+                  false, static_cast<const float *>(w.gu), P, ff, w.aq, w.as, w.ab) != cudaSuccess)
+        return GCUDA_E_CUDA;
+    a.rows = H;
+    a.cols = ff;
+    a.act = ActSet{w.aq, w.as, w.ab, ff, P, ff, ff / 16};
+    a.y = d_out;
+    a.ystride = H;
+    a.units = w.units_dn;
+    a.n_units = w.counts + 1;
+    a.act_div = 1;
+    RC_GRID(launch_umma_grouped(a, w.cap_dn, st));
+    return GCUDA_OK;
 }
 
 int gcuda_op_q4_umma_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint8_t *d_u, void *stream) {

@@ -77,20 +77,53 @@ struct UmmaSmem {
     int epi_stop;   // the epilogue warps' common decision to stop after a unit
 };
 
-struct UmmaGemmArgs {
-    const uint8_t *w;   // U layout
-    int rows, cols;
+// A unit of the grouped form: one 128-row tile of one matrix (U layout) against up to NT token entries
+// toklist[tok0 ..tok0 + nt) (activation row entry / act_div, output row entry).
+struct UmmaUnit {
+    const uint8_t *w;
     float global;
-    ActSet act;         // token t: q at t * qstride, scale / bsum at t * sstride
+    int tile, nt, tok0;
+};
+
+struct UmmaGemmArgs {
+    const uint8_t *w;   // U layout (the dense form: one matrix, every tile x every block of NT tokens)
+    int rows, cols;     // every unit's matrix shape
+    float global;
+    ActSet act;         // activation row r: q at r * qstride, scale / bsum at r * sstride
     float *y;
-    int ystride;        // y[t * ystride + row]
+    int ystride;        // y[output row * ystride + matrix row]
     uint32_t *status;
+    // the grouped form (units != NULL): the unit table, its length (on the device), the token entries
+    const UmmaUnit *units;
+    const int *n_units;
+    const int *toklist;
+    int act_div;
+};
+
+// what a role needs of unit u: the matrix, its global, the tile, the token count and the first entry
+struct UmmaUnitView {
+    const uint8_t *w;
+    float global;
+    int tile, nt, tok0;
 };
 
 template <int NT>
 __host__ __device__ constexpr size_t umma_smem_bytes() { return sizeof(UmmaSmem<NT>) + 1024; }
 
 #if defined(__CUDA_ARCH__)
+template <int NT>
+__device__ __forceinline__ UmmaUnitView umma_unit(const UmmaGemmArgs &a, int u, int tblocks) {
+    if (a.units) {
+        const UmmaUnit U = a.units[u];
+        return UmmaUnitView{U.w, U.global, U.tile, U.nt, U.tok0};
+    }
+    const int tb = u % tblocks;
+    return UmmaUnitView{a.w, a.global, u / tblocks, min(NT, a.act.n - tb * NT), tb * NT};
+}
+// token entry i of a unit: its activation row and its output row
+__device__ __forceinline__ int umma_entry(const UmmaGemmArgs &a, const UmmaUnitView &v, int i) {
+    return a.units ? __ldg(a.toklist + v.tok0 + i) : v.tok0 + i;
+}
 __device__ __forceinline__ bool umma_give_up(volatile int *abort, uint32_t *status) {
     *abort = 1;
     if (status) atomicOr(status, kErrWaitTimeout);
@@ -119,7 +152,9 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
     constexpr int kCodeBytes = kUmmaPackSteps * kUmmaStepBytes;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int KS = a.cols / 32, G = a.cols / 64;
-    const int tiles = a.rows / kUmmaRows, tblocks = (a.act.n + NT - 1) / NT, units = tiles * tblocks;
+    const int tiles = a.rows / kUmmaRows, tblocks = (a.act.n + NT - 1) / NT;
+    const int units = a.units ? *a.n_units : tiles * tblocks;
+    const int act_div = a.units ? a.act_div : 1;
     volatile int *abort = &S.abort;
     if (threadIdx.x == 0) {
         // (consumer barriers count warps: each warp's lanes finish, sync, then one lane arrives - 128 arrivals on one
@@ -146,19 +181,20 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
             int last_ph[UmmaSmem<NT>::kPackStages];
             for (int i = 0; i < UmmaSmem<NT>::kPackStages; ++i) last_ph[i] = -1;
             for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
-                const int T = u / tblocks, tb = u % tblocks;
-                const int nt = min(NT, a.act.n - tb * NT);
+                const UmmaUnitView U = umma_unit<NT>(a, u, tblocks);
+                const int nt = U.nt;
                 for (int pc = 0; pc < KS / kUmmaPackSteps && !*abort; ++pc) {
                     if (!umma_wait(&S.packed_empty[s], ph ^ 1, abort)) {
                         umma_give_up(abort, a.status);
                         break;
                     }
                     mbar_expect_tx(&S.packed_full[s], kCodeBytes + nt * kUmmaPackSteps * 32);
-                    bulk_g2s(S.packed[s], a.w + (static_cast<size_t>(T) * KS + static_cast<size_t>(pc) * kUmmaPackSteps) * kUmmaStepBytes,
+                    bulk_g2s(S.packed[s], U.w + (static_cast<size_t>(U.tile) * KS + static_cast<size_t>(pc) * kUmmaPackSteps) * kUmmaStepBytes,
                              kCodeBytes, &S.packed_full[s]);
                     for (int tok = 0; tok < nt; ++tok)
                         bulk_g2s(S.packed[s] + kCodeBytes + tok * kUmmaPackSteps * 32,
-                                 a.act.q + static_cast<size_t>(tb * NT + tok) * a.act.qstride + static_cast<size_t>(pc) * kUmmaPackSteps * 32,
+                                 a.act.q + static_cast<size_t>(umma_entry(a, U, tok) / act_div) * a.act.qstride +
+                                     static_cast<size_t>(pc) * kUmmaPackSteps * 32,
                                  kUmmaPackSteps * 32, &S.packed_full[s]);
                     last_ph[s] = static_cast<int>(ph);
                     if (++s == UmmaSmem<NT>::kPackStages) s = 0, ph ^= 1;
@@ -180,8 +216,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
         // this thread's row in an A atom and its B row (128-byte swizzle: chunk q of the row at chunk q ^ (row % 8))
         const int a_row = (t >> 3) * 1024 + ri * 128, b_row = (n_ >> 3) * 1024 + (n_ & 7) * 128;
         for (int u = blockIdx.x; u < units && !*abort; u += gridDim.x) {
-            const int tb = u % tblocks;
-            const int nt = min(NT, a.act.n - tb * NT);
+            const int nt = umma_unit<NT>(a, u, tblocks).nt;
             bool ok = true;
             for (int k0 = 0; k0 < KS && ok; k0 += KU) {
                 // KU K-steps at once (KS, the chunk and the ring are multiples of KU): their stages free, their packed
@@ -284,14 +319,14 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
         // (every epilogue warp runs the same units: the named barriers below must see all of them, so whether to go
         // on after a unit is decided once, by thread 0, and read by all after the barrier)
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
-            const int T = u / tblocks, tb = u % tblocks;
-            const int nt = min(NT, a.act.n - tb * NT);
+            const UmmaUnitView U = umma_unit<NT>(a, u, tblocks);
+            const int T = U.tile, nt = U.nt;
             // the unit's per-token block data: (bsum, bsum, scale, scale) of blocks 2 ks, 2 ks + 1
             for (int i = threadIdx.x; i < NT * KS; i += 32 * kUmmaEpiWarps) {
                 const int tk = i / KS, ks = i - tk * KS;
                 int4 v = make_int4(0, 0, 0, 0);
                 if (tk < nt) {
-                    const size_t so = static_cast<size_t>(tb * NT + tk) * a.act.sstride + 2 * ks;
+                    const size_t so = static_cast<size_t>(umma_entry(a, U, tk) / act_div) * a.act.sstride + 2 * ks;
                     const int2 bs = __ldg(reinterpret_cast<const int2 *>(a.act.bsum + so));
                     const float2 sc = __ldg(reinterpret_cast<const float2 *>(a.act.scale + so));
                     v = make_int4(bs.x, bs.y, __float_as_int(sc.x), __float_as_int(sc.y));
@@ -300,7 +335,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
             }
             epi_sync();
             const int row = T * kUmmaRows + r;
-            const uint32_t *sc = reinterpret_cast<const uint32_t *>(a.w + umma_code_bytes(a.rows, a.cols)) +
+            const uint32_t *sc = reinterpret_cast<const uint32_t *>(U.w + umma_code_bytes(a.rows, a.cols)) +
                                  static_cast<size_t>(T) * G * kUmmaRows + r;
             uint64_t acc[HT / 2];   // token pairs (2 tp, 2 tp + 1) of this warp's half, as f32x2
 #pragma unroll
@@ -376,7 +411,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
                 for (int tl = 0; tl < HT; ++tl) {
                     const int tk = half * HT + tl;
                     const float v = (tl & 1) ? hi_f(acc[tl >> 1]) : lo_f(acc[tl >> 1]);
-                    if (tk < nt) a.y[static_cast<size_t>(tb * NT + tk) * a.ystride + row] = __fmul_rn(v, a.global);
+                    if (tk < nt) a.y[static_cast<size_t>(umma_entry(a, U, tk)) * a.ystride + row] = __fmul_rn(v, U.global);
                 }
             }
             if (threadIdx.x == 0) S.epi_stop = (!ok || *abort) ? 1 : 0;

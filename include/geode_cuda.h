@@ -245,6 +245,22 @@ size_t gcuda_op_q4_umma_bytes(int64_t rows, int64_t cols);
 int gcuda_op_q4_umma_relayout(const uint8_t *d_pack, int64_t rows, int64_t cols, uint8_t *d_u, void *stream);
 int gcuda_op_q4_gemm_umma(const uint8_t *d_u, int64_t rows, int64_t cols, float global, const int8_t *d_q,
                           const float *d_scale, const int32_t *d_bsum, int n, float *d_y, void *stream);
+/* The routed experts of many token rows at once on the tensor core (the batched configuration), bit for bit the
+ * reference's per-pick products (Model::moe, engine/src/model.cpp:4496-4543): out [n*K][H] row p = t * K + k =
+ * down(quant(silu(gate) * up)) of expert ids[p] on token t's quantized h (q [n][H], scale and bsum [n][H/16]), where
+ * gate | up = gate_up . h. The experts in the U layout, expert e's block (gate_up 2 ff x H, then down H x ff) at
+ * d_u + e * gcuda_op_moe_umma_expert_bytes(H, ff), made from the pack's blocks by gcuda_op_moe_umma_relayout;
+ * d_globals [E][2] their per-matrix scales. H and ff multiples of 256, at most 4096; E <= 1024. d_work: the caller's
+ * scratch of gcuda_op_moe_umma_work_bytes (256-byte aligned): the picks grouped by expert and the units of the two
+ * grouped products are planned on the device. The combine (weights, shared expert) is the caller's. An expert id out
+ * of range: its pick is left out and the status word (gcuda_op_status) raised. */
+size_t gcuda_op_moe_umma_expert_bytes(int H, int ff);
+size_t gcuda_op_moe_umma_work_bytes(int n, int K, int E, int H, int ff);
+int gcuda_op_moe_umma_relayout(const uint8_t *d_pack, size_t pack_stride, int E, int H, int ff, uint8_t *d_u,
+                               void *stream);
+int gcuda_op_moe_umma(const uint8_t *d_u, const float *d_globals, int E, int H, int ff, const int8_t *d_q,
+                      const float *d_scale, const int32_t *d_bsum, int n, const int *d_ids, int K, float *d_out,
+                      void *d_work, size_t work_bytes, void *stream);
 /* dequant_row (engine/src/kernels.cpp:1214-1228) of nrows rows (d_rows int64) of a tiled matrix: out [nrows][cols] */
 int gcuda_op_q4_dequant(const uint8_t *d_tiles, int64_t cols, float global, const int64_t *d_rows, int nrows,
                         float *d_out, void *stream);

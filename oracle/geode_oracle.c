@@ -686,6 +686,18 @@ static void mlp_layer(const go_model *m, const go_layer *L, int l, int n, const 
     free(gu);
 }
 
+/* One routed pick of Model::moe (engine/src/model.cpp:4496-4543) by itself: the expert block (gate_up [2 ff][H] q4
+ * rows, then down [H][ff]) on one token's h: gate_up on the quantized h, silu(gate) * up, quantized again, down. */
+void go_expert_pair(const uint8_t *blk, float g_gu, float g_dn, int H, int ff, const float *h, float *y) {
+    float *gu = (float *)malloc(sizeof(float) * 2 * (size_t)ff);
+    go_q4 gw = {blk, 2 * ff, H, g_gu};
+    go_q4 dw = {blk + (size_t)(2 * ff) * q4_row_bytes(H), H, ff, g_dn};
+    matmul(&gw, 1, h, gu);
+    for (int i = 0; i < ff; ++i) gu[i] = silu(gu[i]) * gu[ff + i];
+    matmul(&dw, 1, gu, y);
+    free(gu);
+}
+
 /* Model::forward_batch (engine/src/model.cpp:5235-5413) without images, for the verify pass */
 int go_forward(const go_model *m, go_state *s, const int *toks, int n, float *logits, float *hidden, const go_trace *tr) {
     const go_config *c = &m->cfg;

@@ -147,6 +147,9 @@ float go_expf_restated(float x);
 uint64_t go_expf_mismatch(uint64_t lo, uint64_t hi, int restated, int threads, uint32_t *first, int cap);
 uint64_t go_expf_check_table(uint64_t lo, uint64_t n, const float *vals, int threads, uint32_t *first, int cap);
 
+/* one routed pick of Model::moe (engine/src/model.cpp:4496-4543): y [H] from h [H] and the expert block */
+void go_expert_pair(const uint8_t *blk, float g_gu, float g_dn, int H, int ff, const float *h, float *y);
+
 #ifdef __cplusplus
 }
 #endif

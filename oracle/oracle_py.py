@@ -294,6 +294,7 @@ def oracle_lib():
     lib.go_expf_mismatch.argtypes = [C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_void_p, C.c_int]
     lib.go_expf_check_table.restype = C.c_uint64
     lib.go_expf_check_table.argtypes = [C.c_uint64, C.c_uint64, C.c_void_p, C.c_int, C.c_void_p, C.c_int]
+    lib.go_expert_pair.argtypes = [C.c_void_p, C.c_float, C.c_float, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
     lib.go_spec_reject.restype = C.c_int
     lib.go_spec_reject.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_float, C.c_float,
                                    C.c_int, C.c_uint64, C.c_uint64, C.c_void_p]

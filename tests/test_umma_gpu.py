@@ -64,3 +64,56 @@ def test_umma_shapes_refused(L):
     d = torch.zeros(1024, dtype=torch.uint8, device="cuda")
     assert L.gcuda_op_q4_gemm_umma(d.data_ptr(), 100, 256, 1.0, d.data_ptr(), d.data_ptr(), d.data_ptr(), 1,
                                    d.data_ptr(), None) != 0
+
+
+@pytest.mark.parametrize("n,K,E,H,ff", [(20, 4, 16, 512, 256), (64, 8, 64, 2048, 512)])
+def test_moe_umma_bit_exact(L, O, n, K, E, H, ff):
+    """The routed experts of many rows on the tensor core (gcuda_op_moe_umma: the picks grouped by expert on the device,
+    the grouped gate_up, SwiGLU + quantize, the grouped down) against the oracle's per-pick expert products
+    (go_expert_pair, the reference's Model::moe pick, engine/src/model.cpp:4496-4543): every output row bit for bit.
+    The picks lean on a few experts (Zipf-like), so units of several token blocks and single picks both occur."""
+    import ctypes as C
+    rng = np.random.default_rng(n + E)
+    gu_rows = 2 * ff
+    blocks, globs = [], []
+    for e in range(E):
+        gu, g0 = synth.q4_random(rng, gu_rows, H)
+        dn, g1 = synth.q4_random(rng, H, ff)
+        blocks.append(np.concatenate([gu.reshape(-1), dn.reshape(-1)]))
+        globs.append((g0, g1))
+    pack = np.ascontiguousarray(np.stack(blocks))
+    stride = pack.shape[1]
+    globs = np.array(globs, np.float32)
+    p_e = 1.0 / np.arange(1, E + 1)
+    p_e /= p_e.sum()
+    ids = np.stack([rng.choice(E, K, replace=False, p=p_e) for _ in range(n)]).astype(np.int32)
+    h = (rng.standard_normal((n, H)) * rng.uniform(0.5, 2.0, (n, 1))).astype(np.float32)
+    eb = L.gcuda_op_moe_umma_expert_bytes(H, ff)
+    assert eb == stride
+    d_pack = torch.from_numpy(pack).cuda()
+    d_u = torch.zeros(E * eb, dtype=torch.uint8, device="cuda")
+    assert L.gcuda_op_moe_umma_relayout(d_pack.data_ptr(), stride, E, H, ff, d_u.data_ptr(), None) == 0
+    d_h = torch.from_numpy(h).cuda()
+    q = torch.zeros((n, H), dtype=torch.int8, device="cuda")
+    s = torch.zeros((n, H // 16), dtype=torch.float32, device="cuda")
+    b = torch.zeros((n, H // 16), dtype=torch.int32, device="cuda")
+    assert L.gcuda_op_quantize(d_h.data_ptr(), n, H, q.data_ptr(), s.data_ptr(), b.data_ptr(), None) == 0
+    wb = L.gcuda_op_moe_umma_work_bytes(n, K, E, H, ff)
+    work = torch.zeros(wb, dtype=torch.uint8, device="cuda")
+    out = torch.full((n * K, H), float("nan"), dtype=torch.float32, device="cuda")
+    d_ids = torch.from_numpy(ids).cuda()
+    d_g = torch.from_numpy(globs).cuda()
+    for rep in range(2):   # (twice: the work buffer's plan from the first call is overwritten cleanly)
+        assert L.gcuda_op_moe_umma(d_u.data_ptr(), d_g.data_ptr(), E, H, ff, q.data_ptr(), s.data_ptr(), b.data_ptr(), n,
+                                   d_ids.data_ptr(), K, out.data_ptr(), work.data_ptr(), wb, None) == 0
+        torch.cuda.synchronize()
+        assert L.gcuda_op_status(1) == 0
+    got = out.cpu().numpy()
+    for t in range(n):
+        for k in range(K):
+            e = int(ids[t, k])
+            ref = np.zeros(H, np.float32)
+            O.go_expert_pair(pack[e].ctypes.data, float(globs[e, 0]), float(globs[e, 1]), H, ff, h[t].ctypes.data,
+                             ref.ctypes.data)
+            row = got[t * K + k]
+            assert np.array_equal(row.view(np.uint32), ref.view(np.uint32)), (t, k, e, np.abs(row - ref).max())
