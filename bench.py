@@ -451,6 +451,130 @@ def accept_bench(args) -> int:
     return 0
 
 
+CFG4_METRIC = "MoE expert stage of the batched verify (cfg4: 64 sequences x 5 rows, 256 experts top-8, Zipf picks)"
+CFG4_UNIT = "verified rows/s through the 40 layers' routed experts"
+
+
+def zipf_picks(rng, n: int, E: int, K: int, s: float = 1.0) -> np.ndarray:
+    """n rows of K distinct experts each, expert popularity Zipf(s) over a random ranking of the E experts (the
+    router-logit bias BASELINE cfg 4 describes, drawn directly)."""
+    rank = rng.permutation(E)
+    p = 1.0 / (np.arange(1, E + 1, dtype=np.float64) ** s)
+    p = p[np.argsort(rank)]
+    p /= p.sum()
+    return np.stack([rng.choice(E, K, replace=False, p=p) for _ in range(n)]).astype(np.int32)
+
+
+def cfg4_bench(args) -> int:
+    """The batched configuration's routed experts on the tensor core (gcuda_op_moe_umma): 320 token rows (64
+    sequences x 5), top-8 of 256 experts with Zipf(1.0) picks, hidden 2048, expert ff 512, 40 layers - each layer's
+    picks grouped by expert on the device, the grouped gate_up, SwiGLU + quantize and the grouped down, exact per pick.
+    A step = the 40 layers' expert stages one after another (the attention / Gated DeltaNet of 64 sequences and the
+    combine are not built for this configuration). Weights: random U-layout bytes made on the device (18 GB, far
+    above L2; no flush), activations random."""
+    import ctypes as C
+    import torch
+    from geode_b200 import cuda_lib
+    L = cuda_lib()
+    peak, peak_kind = measured_peaks()
+    n_seq, rows_per, E, K, H, ff = 64, NTOK, 256, 8, 2048, 512
+    layers = max(1, min(args.layers, 40))   # (fewer only for profiling)
+    n = n_seq * rows_per
+    rng = np.random.default_rng(4)
+    eb = L.gcuda_op_moe_umma_expert_bytes(H, ff)
+    gu_code = 2 * ff * H // 2
+    gu_bytes = 2 * ff * H * 9 // 16
+    dn_code = H * ff // 2
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    experts = []
+    for _ in range(layers):   # random codes, scale bytes in 0x30..0x48 (sane E4M3 values)
+        u = torch.randint(0, 256, (E, eb), dtype=torch.uint8, device="cuda", generator=gen)
+        u[:, gu_code:gu_bytes] = torch.randint(0x30, 0x49, (E, gu_bytes - gu_code), dtype=torch.uint8, device="cuda", generator=gen)
+        u[:, gu_bytes + dn_code:] = torch.randint(0x30, 0x49, (E, eb - gu_bytes - dn_code), dtype=torch.uint8, device="cuda", generator=gen)
+        experts.append(u)
+    globs = torch.full((E, 2), 1e-3, dtype=torch.float32, device="cuda")
+    ids = [torch.from_numpy(zipf_picks(rng, n, E, K)).cuda() for _ in range(layers)]
+    union = [int(torch.unique(i).numel()) for i in ids]
+    x = torch.randn(n, H, device="cuda", generator=gen)
+    q = torch.empty(n, H, dtype=torch.int8, device="cuda")
+    sc = torch.empty(n, H // 16, device="cuda")
+    bs = torch.empty(n, H // 16, dtype=torch.int32, device="cuda")
+    L.gcuda_op_quantize(x.data_ptr(), n, H, q.data_ptr(), sc.data_ptr(), bs.data_ptr(), None)
+    wb = L.gcuda_op_moe_umma_work_bytes(n, K, E, H, ff)
+    work = torch.empty(wb, dtype=torch.uint8, device="cuda")
+    out = torch.empty(n * K, H, device="cuda")
+    st = torch.cuda.current_stream()
+
+    def step():
+        for l in range(layers):
+            rc = L.gcuda_op_moe_umma(experts[l].data_ptr(), globs.data_ptr(), E, H, ff, q.data_ptr(), sc.data_ptr(),
+                                     bs.data_ptr(), n, ids[l].data_ptr(), K, out.data_ptr(), work.data_ptr(), wb,
+                                     st.cuda_stream)
+            assert rc == 0, rc
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    assert L.gcuda_op_status(1) == 0
+    steps = max(3, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        e0.record(st)
+        for _ in range(steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    wbytes = sum(union) * eb           # the routed experts' weights each step reads once
+    ach = wbytes / (ms * 1e-3) / 1e9
+    macs = n * K * (2 * ff * H + H * ff) * layers   # the picks' products (useful multiply-adds)
+    cb = None
+    if not args.no_cpu_baseline:
+        cb = cpu_moe_port(layers)
+    line = {
+        "metric": CFG4_METRIC, "value": n * 1e3 / ms, "unit": CFG4_UNIT, "n_gpus": 1, "steps": steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4xint8->f32 (tcgen05 kind::i8, exact per pick)",
+        "data": "synthetic (random U-layout q4 bytes and activations made on the device; Zipf(1.0) picks)",
+        "config": {"workload": "cfg4: routed-expert stage only (gcuda_op_moe_umma per layer), 320 rows, 40 layers",
+                   "global_batch": n, "seq_len": None, "parallelism": "1 GPU",
+                   "l2": "inputs larger than L2 (18 GB of expert weights; no flush)", "layers": layers},
+        "roofline": {"kernel": "k_umma_gemm (grouped, tcgen05 int8 MMAs + exact float chain) with the plan and SwiGLU "
+                               "kernels", "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                     "frac": ach / peak, "traffic": None, "algorithmic_bytes_per_step": wbytes,
+                     "experts_per_layer": sum(union) / layers},
+        "tensor": {"useful_tops": 2 * macs / (ms * 1e-3) / 1e12, "note": "2 x the picks' multiply-adds / time; the MMAs "
+                   "do twice that (each K = 32 step holds two blocks' zero-padded columns)"},
+        "cpu_baseline": cb, "e2e": None, "gpu_launches": 4 * layers, "clocks": clk.summary(), "peak_kind": peak_kind,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def cpu_moe_port(layers: int, picks: int = 48) -> dict:
+    """The CPU side of the cfg4 line: the oracle's port of the reference's per-pick expert product (go_expert_pair,
+    engine/src/model.cpp:4496-4543; one thread) on a sample of `picks` picks, scaled to the step's 320 x 8 x 40."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle_py as op
+    from geode_b200 import synth
+    O = op.oracle_lib()
+    rng = np.random.default_rng(5)
+    H, ff = 2048, 512
+    gu, g0 = synth.q4_random(rng, 2 * ff, H)
+    dn, g1 = synth.q4_random(rng, H, ff)
+    blk = np.ascontiguousarray(np.concatenate([gu.reshape(-1), dn.reshape(-1)]))
+    h = rng.standard_normal(H).astype(np.float32)
+    y = np.zeros(H, np.float32)
+    t0 = time.perf_counter()
+    for _ in range(picks):
+        O.go_expert_pair(blk.ctypes.data, g0, g1, H, ff, h.ctypes.data, y.ctypes.data)
+    t = (time.perf_counter() - t0) / picks
+    step = t * 320 * 8 * layers
+    return {"kind": "port", "value": 320 / step, "unit": CFG4_UNIT, "cores": 1,
+            "sample": f"{picks} picks of the oracle's port of the per-pick expert product, {t * 1e3:.2f} ms each, "
+                      f"scaled to 320 rows x 8 picks x {layers} layers = {step:.1f} s a step"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -463,15 +587,16 @@ def main():
     ap.add_argument("--ep", action="store_true",
                     help="N > 1: one sequence over all GPUs, the routed experts striped over them (gcuda_set_ep; strong "
                          "scaling); without it each GPU verifies its own sequence (replicas, weak scaling)")
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg5"],
-                    help="cfg3: the verify step (the headline); cfg5: the acceptance microbench (one GPU)")
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg4", "cfg5"],
+                    help="cfg3: the verify step (the headline); cfg4: the batched configuration's routed experts on the "
+                         "tensor core (one GPU); cfg5: the acceptance microbench (one GPU)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
-    if args.workload == "cfg5":
+    if args.workload in ("cfg4", "cfg5"):
         import torch
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        return accept_bench(args)
+        return accept_bench(args) if args.workload == "cfg5" else cfg4_bench(args)
 
     import torch
     rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
