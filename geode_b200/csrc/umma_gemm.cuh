@@ -375,6 +375,7 @@ __global__ void __launch_bounds__(kUmmaThreads, 1) k_umma_gemm(UmmaGemmArgs a) {
 #pragma unroll
                         for (int tp = 0; tp < HT / 2; ++tp) {
                             const int tk = half * HT + 2 * tp;
+                            if (tk >= nt) break;   // (the unit's last pair may hold one token; none after it)
                             const int4 ta = S.tokdata[tk * KS + ks], tbd = S.tokdata[(tk + 1) * KS + ks];
                             const float fa0 = static_cast<float>(2 * static_cast<int32_t>(d[j][4 * tp]) - 15 * ta.x);
                             const float fb0 = static_cast<float>(2 * static_cast<int32_t>(d[j][4 * tp + 2]) - 15 * tbd.x);
