@@ -584,9 +584,10 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=40, help="(smaller cases for profiling)")
-    ap.add_argument("--ep", action="store_true",
-                    help="N > 1: one sequence over all GPUs, the routed experts striped over them (gcuda_set_ep; strong "
-                         "scaling); without it each GPU verifies its own sequence (replicas, weak scaling)")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: each GPU verifies its own sequence (replicas, weak scaling); without it (the default) "
+                         "one sequence runs over all GPUs with the routed experts striped over them (expert "
+                         "parallelism, gcuda_set_ep; strong scaling)")
     ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg4", "cfg5"],
                     help="cfg3: the verify step (the headline); cfg4: the batched configuration's routed experts on the "
                          "tensor core (one GPU); cfg5: the acceptance microbench (one GPU)")
@@ -611,7 +612,7 @@ def main():
     from geode_b200.backend import synthetic, ep_unique_id
     from geode_b200 import cuda_lib
     ep = None
-    if args.ep and world > 1:
+    if not args.replicas and world > 1:
         obj = [ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         ep = (rank, world, obj[0])

@@ -17,6 +17,7 @@
 #include "ops_impl.cuh"
 #include "accept.cuh"
 #include "noalloc_impl.cuh"
+#include "ep_exchange.cuh"
 
 using namespace gcu;
 
@@ -67,6 +68,7 @@ struct NcclApi {
     decltype(&ncclGetUniqueId) get_unique_id = nullptr;
     decltype(&ncclCommInitRank) comm_init_rank = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclCommDestroy) comm_destroy = nullptr;
     decltype(&ncclGetErrorString) error_string = nullptr;
 };
@@ -80,9 +82,10 @@ NcclApi &nccl() {
             a.get_unique_id = reinterpret_cast<decltype(&ncclGetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
             a.comm_init_rank = reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
             a.all_reduce = reinterpret_cast<decltype(&ncclAllReduce)>(dlsym(h, "ncclAllReduce"));
+            a.all_gather = reinterpret_cast<decltype(&ncclAllGather)>(dlsym(h, "ncclAllGather"));
             a.comm_destroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
             a.error_string = reinterpret_cast<decltype(&ncclGetErrorString)>(dlsym(h, "ncclGetErrorString"));
-            a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.comm_destroy && a.error_string;
+            a.ok = a.get_unique_id && a.comm_init_rank && a.all_reduce && a.all_gather && a.comm_destroy && a.error_string;
         }
     }
     return a;
@@ -154,9 +157,16 @@ struct gcuda {
     uint64_t reject_steps = 0;      // (its Philox sequence index: one per step)
     std::vector<void *> allocs;
     // expert parallelism (gcuda_set_ep): this rank's experts are e % ep_world == ep_rank; the expert outputs meet
-    // through one all-reduce per MoE layer on the handle's stream
+    // through k_ep_exchange (peer stores over NVLink and per-layer flags); NCCL only carries the set-up's handles
     int ep_rank = 0, ep_world = 1;
     ncclComm_t comm = nullptr;
+    void *xbuf = nullptr;               // this rank's exchange buffer: flags [n_layers][world] (padded), then eout
+    uint32_t *xflags = nullptr;
+    int *ep_epoch = nullptr;            // (device) the step's epoch, one per step
+    unsigned int *xcount = nullptr;     // (device) the exchange kernel's arrival counter
+    void *peer_base[kMaxEpWorld] = {};  // the peers' exchange buffers, mapped here
+    float *peer_eout[kMaxEpWorld] = {};
+    uint32_t *peer_flags[kMaxEpWorld] = {};
 };
 
 namespace {
@@ -296,6 +306,11 @@ int enqueue_step(gcuda *g, int n) {
     const int H = s.hidden;
     const bool pdl = g->pdl;
     const DevTensor *emb = tensor(g, g->embed, kRaw);
+    if (g->ep_world > 1) {   // (the step's epoch: every rank runs the same steps, so the epochs agree)
+        k_ep_tick<<<1, 32, 0, g->st>>>(g->ep_epoch);
+        count_launch();
+        LAUNCH_OK(cudaGetLastError());
+    }
     {
         const dim3 grid((H + 255) / 256, n);
         LAUNCH_OK(launch_ex(k_embed, grid, dim3(256), 0, g->st, false, static_cast<const uint8_t *>(emb->d),
@@ -479,8 +494,6 @@ int enqueue_step(gcuda *g, int n) {
                                           static_cast<size_t>(n) * (E + 1) * sizeof(float), cudaMemcpyDeviceToDevice,
                                           g->st));
             }
-            if (g->ep_world > 1)   // (rows of picks other ranks compute stay zero for the all-reduce)
-                LAUNCH_OK(cudaMemsetAsync(g->eout, 0, static_cast<size_t>(n) * s.top_k * H * sizeof(float), g->st));
             const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
             const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
                             *sd = tensor(g, L.sh_down, kQ4Tiled);
@@ -527,11 +540,23 @@ int enqueue_step(gcuda *g, int n) {
                 if (!kt_mark(g, kind, false)) return GCUDA_E_CUDA;
             }
             if (g->ep_world > 1) {
-                // every pick's row from the rank that owns its expert (the others hold zeros there: the sum is that row
-                // exactly), so the combine below runs on every rank in rank order as on one GPU
-                const ncclResult_t nr = nccl().all_reduce(g->eout, g->eout, static_cast<size_t>(n) * s.top_k * H, ncclFloat,
-                                                          ncclSum, g->comm, g->st);
-                if (nr != ncclSuccess) return fail(g, GCUDA_E_CUDA, std::string("ncclAllReduce: ") + nccl().error_string(nr));
+                // every pick's row from the rank that owns its expert, stored here by that rank over NVLink, so the
+                // combine below runs on every rank in rank order as on one GPU
+                ExchangeArgs xa{};
+                xa.eout = g->eout;
+                for (int r = 0; r < kMaxEpWorld; ++r) xa.peer_eout[r] = g->peer_eout[r], xa.peer_flags[r] = g->peer_flags[r];
+                xa.flags = g->xflags;
+                xa.route = g->route;
+                xa.epoch = g->ep_epoch;
+                xa.count = g->xcount;
+                xa.status = g->d_status;
+                xa.n = n;
+                xa.K = s.top_k;
+                xa.H = H;
+                xa.rank = g->ep_rank;
+                xa.world = g->ep_world;
+                xa.layer = l;
+                LAUNCH_OK(launch_ex(k_ep_exchange, dim3(kExchangeCtas), dim3(kExchangeThreads), 0, g->st, false, xa));
             }
             RC_OK(norm(next_norm, true, next_hf));
         }
@@ -656,6 +681,9 @@ void gcuda_close(gcuda *g) {
     if (g->d_seen) cudaFree(g->d_seen);
     if (g->ev0) cudaEventDestroy(g->ev0);
     if (g->ev1) cudaEventDestroy(g->ev1);
+    for (int r = 0; r < kMaxEpWorld; ++r)
+        if (g->peer_base[r]) cudaIpcCloseMemHandle(g->peer_base[r]);
+    if (g->xbuf) cudaFree(g->xbuf);
     if (g->comm) nccl().comm_destroy(g->comm);
     if (g->fork_ev) cudaEventDestroy(g->fork_ev);
     if (g->join_ev) cudaEventDestroy(g->join_ev);
@@ -674,7 +702,7 @@ int gcuda_ep_unique_id(void *id_out) {
 }
 
 int gcuda_set_ep(gcuda *g, int rank, int world, const void *id) {
-    if (!g || world < 1 || rank < 0 || rank >= world || (world > 1 && !id)) return GCUDA_E_ARG;
+    if (!g || world < 1 || world > kMaxEpWorld || rank < 0 || rank >= world || (world > 1 && !id)) return GCUDA_E_ARG;
     if (g->ready) return fail(g, GCUDA_E_STATE, "set_ep: before gcuda_setup");
     if (g->comm) return fail(g, GCUDA_E_STATE, "set_ep: already set");
     g->ep_rank = rank;
@@ -787,6 +815,48 @@ int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, c
     return static_cast<int>(g->experts.size()) - 1;
 }
 
+// The exchange buffer of expert parallelism: this rank's [flags | eout] in one allocation (so one IPC handle maps it),
+// the handles of every rank gathered through NCCL, the peers' buffers opened here.
+int ep_exchange_setup(gcuda *g, size_t eout_floats) {
+    const int W = g->ep_world;
+    const size_t fbytes = (static_cast<size_t>(g->sh.n_layers) * W * sizeof(uint32_t) + 255) / 256 * 256;
+    const size_t bytes = fbytes + eout_floats * sizeof(float);
+    if (cudaMalloc(&g->xbuf, bytes) != cudaSuccess) {
+        g->xbuf = nullptr;
+        return fail(g, GCUDA_E_MEMORY, "ep exchange buffer: cudaMalloc");
+    }
+    LAUNCH_OK(cudaMemset(g->xbuf, 0, bytes));
+    g->xflags = static_cast<uint32_t *>(g->xbuf);
+    g->eout = reinterpret_cast<float *>(static_cast<uint8_t *>(g->xbuf) + fbytes);
+    if (!dalloc(g, &g->ep_epoch, 1) || !dalloc(g, &g->xcount, 1)) return GCUDA_E_MEMORY;
+    LAUNCH_OK(cudaMemset(g->ep_epoch, 0, sizeof(int)));
+    LAUNCH_OK(cudaMemset(g->xcount, 0, sizeof(unsigned int)));
+    cudaIpcMemHandle_t mine;
+    LAUNCH_OK(cudaIpcGetMemHandle(&mine, g->xbuf));
+    void *d_h = nullptr;
+    if (cudaMalloc(&d_h, sizeof(cudaIpcMemHandle_t) * (W + 1)) != cudaSuccess) return fail(g, GCUDA_E_MEMORY, "cudaMalloc");
+    std::vector<cudaIpcMemHandle_t> all(static_cast<size_t>(W));
+    uint8_t *d_mine = static_cast<uint8_t *>(d_h) + sizeof(cudaIpcMemHandle_t) * W;
+    cudaError_t e = cudaMemcpy(d_mine, &mine, sizeof mine, cudaMemcpyHostToDevice);
+    ncclResult_t nr = ncclSuccess;
+    if (e == cudaSuccess) nr = nccl().all_gather(d_mine, d_h, sizeof mine, ncclUint8, g->comm, g->st);
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaStreamSynchronize(g->st);
+    if (e == cudaSuccess && nr == ncclSuccess) e = cudaMemcpy(all.data(), d_h, sizeof(cudaIpcMemHandle_t) * W, cudaMemcpyDeviceToHost);
+    cudaFree(d_h);
+    if (nr != ncclSuccess) return fail(g, GCUDA_E_CUDA, std::string("ncclAllGather: ") + nccl().error_string(nr));
+    LAUNCH_OK(e);
+    for (int r = 0; r < W; ++r) {
+        if (r == g->ep_rank) continue;
+        void *p = nullptr;
+        const cudaError_t eo = cudaIpcOpenMemHandle(&p, all[static_cast<size_t>(r)], cudaIpcMemLazyEnablePeerAccess);
+        if (eo != cudaSuccess) return cuda_fail(g, eo, "cudaIpcOpenMemHandle (a peer's exchange buffer)");
+        g->peer_base[r] = p;
+        g->peer_flags[r] = static_cast<uint32_t *>(p);
+        g->peer_eout[r] = reinterpret_cast<float *>(static_cast<uint8_t *>(p) + fbytes);
+    }
+    return GCUDA_OK;
+}
+
 int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, int embed, int lm_head, int final_norm) {
     if (!g || !shape || !layers) return fail(g, GCUDA_E_ARG, "setup: no shape");
     if (g->ready) return fail(g, GCUDA_E_STATE, "setup: already set up");
@@ -854,7 +924,8 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         !dalloc(g, &g->ab, static_cast<size_t>(T) * std::max(1, 2 * s.gdn_v_heads)) ||
         !dalloc(g, &g->kb, static_cast<size_t>(T) * g->kvrow) || !dalloc(g, &g->vb, static_cast<size_t>(T) * g->kvrow) ||
         !dalloc(g, &g->qn, static_cast<size_t>(T) * s.n_heads * s.head_dim) ||
-        !dalloc(g, &g->rlog, static_cast<size_t>(T) * (E + 1)) || !dalloc(g, &g->eout, static_cast<size_t>(T) * K * H) ||
+        !dalloc(g, &g->rlog, static_cast<size_t>(T) * (E + 1)) ||
+        (g->ep_world == 1 && !dalloc(g, &g->eout, static_cast<size_t>(T) * K * H)) ||
         !dalloc(g, &g->shout, static_cast<size_t>(T) * H) ||
         !dalloc(g, &g->part, static_cast<size_t>(T) * s.n_heads * g->nchunks * (s.head_dim + 2)) ||
         !dalloc(g, &g->logits, static_cast<size_t>(T) * s.vocab) || !dalloc(g, &g->core_f, static_cast<size_t>(T) * g->corew) ||
@@ -864,6 +935,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         !act_alloc(g, g->hq, T, H) || !act_alloc(g, g->core, T, g->corew) ||
         !act_alloc(g, g->amid, T * K, ffw) || !act_alloc(g, g->shact, T, s.shared_ff))
         return GCUDA_E_MEMORY;
+    if (g->ep_world > 1) RC_OK(ep_exchange_setup(g, static_cast<size_t>(T) * K * H));
     // inv_freq as the reference computes it (engine/src/model.cpp:737-740), host powf
     {
         std::vector<float> inv(static_cast<size_t>(std::max(1, s.rope_dim / 2)));

@@ -1,6 +1,8 @@
 """Expert parallelism over two GPUs (gcuda_set_ep, include/geode_cuda.h): each rank computes the routed experts it
-owns (expert e on rank e % 2), the expert outputs meet through one NCCL all-reduce per MoE layer, and every rank
-combines in rank order - so the logits of a verify batch equal the one-GPU step's bit for bit, on both ranks.
+owns (expert e on rank e % 2), stores those picks' rows into the other rank's expert-output buffer over NVLink and
+waits for the other's (k_ep_exchange: peer memory mapped through CUDA IPC, per-layer flags with bounded waits), and
+every rank combines in rank order - so the logits of a verify batch equal the one-GPU step's bit for bit, on both
+ranks.
 Skipped with fewer than two GPUs. The ranks are child processes; a host barrier before the first collective keeps a
 rank whose set-up failed from leaving the other inside one."""
 import multiprocessing as mp
