@@ -719,6 +719,8 @@ def main():
         "lm_head_operator": lm_op,
         "step_roofline": {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,
                           "peak_kind": peak_kind, "algorithmic_bytes_per_step": b, "experts_per_layer": union_layer,
+                          "per_gpu": "bytes and experts of one GPU (under expert parallelism each reads its own experts "
+                                     "and every dense weight)",
                           "mean_context": mean_ctx},
         "cpu_baseline": cb,
         "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": NTOK * 4,

@@ -1027,10 +1027,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict
     int nu = 0;
     for (int i = 0; i < (E + 31) / 32; ++i) nu += __popc(s_bits[i]);
     if (static_cast<int>(threadIdx.x) < nu) out->mask[threadIdx.x] = s_mask[threadIdx.x];
-    if (threadIdx.x == 0) {
-        out->n_union = nu;
-        if (union_acc) atomicAdd(union_acc, nu);
-    }
+    if (threadIdx.x == 0) out->n_union = nu;
     // this rank's members of the union (expert e on rank e % world), ascending, by ballots over the union in 32s
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
@@ -1042,7 +1039,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict
             if (mine) out->own[base + __popc(bal & ((1u << lane) - 1u))] = u;
             base += __popc(bal);
         }
-        if (lane == 0) out->n_own = base;
+        if (lane == 0) {
+            out->n_own = base;
+            if (union_acc) atomicAdd(union_acc, base);   // (the experts this rank reads: the whole union on one GPU)
+        }
     }
 }
 

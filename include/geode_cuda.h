@@ -157,8 +157,8 @@ int gcuda_adopt_embedding(gcuda *g, const uint8_t *data, int64_t rows, int64_t c
  * The speculative step without host round trips (the drafts are the previous batch's own tokens - a measuring loop):
  * gcuda_begin_device_loop puts the position and the first batch on the device; each gcuda_step_device(n) enqueues the
  * verify graph, the greedy acceptance of every row, the decision (kept, next, position += kept) and the rollback;
- * gcuda_sync_step waits and returns the steps taken, the sum of the routed layers' expert-union sizes and the last
- * kept count. No counterpart in the reference (its loop is host code, engine/src/geode.cpp:318-370). */
+ * gcuda_sync_step waits and returns the steps taken, the sum over the routed layers of the experts this rank read
+ * (the union of the picks; under expert parallelism this rank's members of it) and the last kept count. No counterpart in the reference (its loop is host code, engine/src/geode.cpp:318-370). */
 int gcuda_begin_device_loop(gcuda *g, const int *toks, int n);
 int gcuda_step_device(gcuda *g, int n);
 int gcuda_sync_step(gcuda *g, int *steps, int *union_sum, int *last_kept);
@@ -202,8 +202,8 @@ int gcuda_debug_trace(gcuda *g, const int *toks, int n, float *x, float *router_
  * launched kernel by kernel without programmatic overlap so that CUDA events bracket each launch. ms[4] and
  * launches[4] per step for GCUDA_KT_GATE_UP (the routed and shared experts' gate|up product with SwiGLU), GCUDA_KT_DOWN
  * (their down product), GCUDA_KT_LM_HEAD and GCUDA_KT_DENSE (the layers' other q4 products); *step_ms the whole step
- * (NULL: not wanted), *union_sum the routed experts the step's MoE layers read (summed over layers; NULL: not
- * wanted). */
+ * (NULL: not wanted), *union_sum the routed experts the step's MoE layers read on this rank (summed over layers;
+ * NULL: not wanted). */
 #define GCUDA_KT_GATE_UP 0
 #define GCUDA_KT_DOWN 1
 #define GCUDA_KT_LM_HEAD 2
