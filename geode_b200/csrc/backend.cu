@@ -162,6 +162,7 @@ struct gcuda {
     ncclComm_t comm = nullptr;
     void *xbuf = nullptr;               // this rank's exchange buffer: flags [n_layers][world] (padded), then eout
     uint32_t *xflags = nullptr;
+    size_t eout_stride = 0;             // expert parallelism: floats of one layer's slot of eout (a slot per layer)
     int *ep_epoch = nullptr;            // (device) the step's epoch, one per step
     unsigned int *xcount = nullptr;     // (device) the exchange kernel's arrival counter
     void *peer_base[kMaxEpWorld] = {};  // the peers' exchange buffers, mapped here
@@ -300,6 +301,10 @@ int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, i
         if (r_ != GCUDA_OK) return g->err.empty() ? fail(g, r_, #call) : r_;   \
     } while (0)
 
+// The expert outputs of layer l: one buffer on one GPU; under expert parallelism a slot per layer, so that a peer
+// storing layer l + 1's rows never meets this rank still combining layer l's.
+float *eout_of(gcuda *g, int l) { return g->eout + (g->ep_world > 1 ? static_cast<size_t>(l) * g->eout_stride : 0); }
+
 // The verify step for n tokens on g->st (toks in g->d_toks, the position in g->d_pos).
 int enqueue_step(gcuda *g, int n) {
     const gcuda_shape &s = g->sh;
@@ -307,7 +312,15 @@ int enqueue_step(gcuda *g, int n) {
     const bool pdl = g->pdl;
     const DevTensor *emb = tensor(g, g->embed, kRaw);
     if (g->ep_world > 1) {   // (the step's epoch: every rank runs the same steps, so the epochs agree)
-        k_ep_tick<<<1, 32, 0, g->st>>>(g->ep_epoch);
+        TickArgs ta{};
+        ta.epoch = g->ep_epoch;
+        ta.flags = g->xflags;
+        for (int r = 0; r < kMaxEpWorld; ++r) ta.peer_flags[r] = g->peer_flags[r];
+        ta.status = g->d_status;
+        ta.rank = g->ep_rank;
+        ta.world = g->ep_world;
+        ta.row = s.n_layers;
+        k_ep_tick<<<1, 32, 0, g->st>>>(ta);
         count_launch();
         LAUNCH_OK(cudaGetLastError());
     }
@@ -317,7 +330,7 @@ int enqueue_step(gcuda *g, int n) {
                             static_cast<int64_t>(s.vocab), H, emb->global, static_cast<const int *>(g->d_toks), n, g->x,
                             g->d_status));
     }
-    auto norm = [&](const float *w, bool combine, float *hf_out) -> int {
+    auto norm = [&](const float *w, bool combine, float *hf_out, int moe_layer = 0) -> int {
         NormArgs a{};
         a.x = g->x;
         a.w = w;
@@ -331,7 +344,7 @@ int enqueue_step(gcuda *g, int n) {
         if (combine) {
             a.sh = g->shout;
             a.gs = g->route->gs;
-            a.eout = g->eout;
+            a.eout = eout_of(g, moe_layer);
             a.wk = g->route->w;
             a.K = s.top_k;
         }
@@ -516,7 +529,7 @@ int enqueue_step(gcuda *g, int n) {
             ea.hq = g->hq.set();
             ea.amid = g->amid.set();
             ea.shact = g->shact.set();
-            ea.eout = g->eout;
+            ea.eout = eout_of(g, l);
             ea.shout = g->shout;
             ea.status = g->d_status;
             for (int pass : {static_cast<int>(kGateUp), static_cast<int>(kDown)}) {
@@ -543,8 +556,11 @@ int enqueue_step(gcuda *g, int n) {
                 // every pick's row from the rank that owns its expert, stored here by that rank over NVLink, so the
                 // combine below runs on every rank in rank order as on one GPU
                 ExchangeArgs xa{};
-                xa.eout = g->eout;
-                for (int r = 0; r < kMaxEpWorld; ++r) xa.peer_eout[r] = g->peer_eout[r], xa.peer_flags[r] = g->peer_flags[r];
+                xa.eout = eout_of(g, l);
+                for (int r = 0; r < kMaxEpWorld; ++r) {
+                    xa.peer_eout[r] = g->peer_eout[r] ? g->peer_eout[r] + static_cast<size_t>(l) * g->eout_stride : nullptr;
+                    xa.peer_flags[r] = g->peer_flags[r];
+                }
                 xa.flags = g->xflags;
                 xa.route = g->route;
                 xa.epoch = g->ep_epoch;
@@ -558,7 +574,7 @@ int enqueue_step(gcuda *g, int n) {
                 xa.layer = l;
                 LAUNCH_OK(launch_ex(k_ep_exchange, dim3(kExchangeCtas), dim3(kExchangeThreads), 0, g->st, false, xa));
             }
-            RC_OK(norm(next_norm, true, next_hf));
+            RC_OK(norm(next_norm, true, next_hf, l));
         }
     }
     if (g->tr_x)
@@ -816,11 +832,13 @@ int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, c
 }
 
 // The exchange buffer of expert parallelism: this rank's [flags | eout] in one allocation (so one IPC handle maps it),
-// the handles of every rank gathered through NCCL, the peers' buffers opened here.
-int ep_exchange_setup(gcuda *g, size_t eout_floats) {
+// the handles of every rank gathered through NCCL, the peers' buffers opened here. Flags [n_layers + 1][world]: a row
+// per layer's exchange and the step-start row; eout a slot of `slot_floats` per layer.
+int ep_exchange_setup(gcuda *g, size_t slot_floats) {
     const int W = g->ep_world;
-    const size_t fbytes = (static_cast<size_t>(g->sh.n_layers) * W * sizeof(uint32_t) + 255) / 256 * 256;
-    const size_t bytes = fbytes + eout_floats * sizeof(float);
+    const size_t fbytes = (static_cast<size_t>(g->sh.n_layers + 1) * W * sizeof(uint32_t) + 255) / 256 * 256;
+    const size_t bytes = fbytes + static_cast<size_t>(g->sh.n_layers) * slot_floats * sizeof(float);
+    g->eout_stride = slot_floats;
     if (cudaMalloc(&g->xbuf, bytes) != cudaSuccess) {
         g->xbuf = nullptr;
         return fail(g, GCUDA_E_MEMORY, "ep exchange buffer: cudaMalloc");

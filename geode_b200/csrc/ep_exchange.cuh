@@ -1,6 +1,6 @@
 // ep_exchange.cuh - expert parallelism's exchange of the routed experts' outputs over NVLink, without a collective
 // library in the step: every rank's MoE layer computes the picks whose experts it owns (expert e on rank e % world),
-// then k_ep_exchange stores those rows straight into every peer's expert-output buffer (peer memory mapped through
+// then k_ep_exchange stores those rows straight into every peer's slot for the layer (peer memory mapped through
 // CUDA IPC at set-up), raises this layer's flag in every peer (the step's epoch, a release store at system scope)
 // and waits, bounded, until every peer's flag for the layer holds the same epoch. The combine that follows reads
 // all the picks' rows from local memory in rank order, as on one GPU, so the step's results equal the one-GPU
@@ -20,9 +20,9 @@ constexpr int kExchangeCtas = 32;
 constexpr uint32_t kExchangeWaitLimit = 1u << 24;   // polls of a peer's flag before the wait gives up
 
 struct ExchangeArgs {
-    float *eout;                          // this rank's rows [n * K][H] (its own picks computed, the rest to come)
-    float *peer_eout[kMaxEpWorld];        // the peers' buffers (this rank's slot: unused)
-    uint32_t *peer_flags[kMaxEpWorld];    // the peers' flags [n_layers][world]
+    float *eout;                          // this layer's rows [n * K][H] (its own picks computed, the rest to come)
+    float *peer_eout[kMaxEpWorld];        // the peers' slots for this layer (this rank's entry: unused)
+    uint32_t *peer_flags[kMaxEpWorld];    // the peers' flags [n_layers + 1][world]
     uint32_t *flags;                      // this rank's flags, written by the peers
     const RouteOut *route;
     const int *epoch;
@@ -40,8 +40,34 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
     return v;
 }
 
-__global__ void k_ep_tick(int *epoch) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) *epoch += 1;
+struct TickArgs {
+    int *epoch;
+    uint32_t *flags;                      // this rank's flags; row `row` is the step-start row
+    uint32_t *peer_flags[kMaxEpWorld];
+    uint32_t *status;
+    int rank, world, row;
+};
+
+// The step's start under expert parallelism: the epoch advanced, then a handshake with every peer (the epoch stored
+// into the peer's step-start flag, a bounded wait for the peer's). A peer that has started this step has finished
+// the last one (its stream's order), so no rank stores a layer's rows into a peer still combining that layer's rows
+// of the step before, nor raises a layer's flag there before the peer has read the previous step's - whatever the
+// number of MoE layers.
+__global__ void k_ep_tick(TickArgs a) {
+    __shared__ uint32_t ep;
+    if (threadIdx.x == 0) {
+        ep = static_cast<uint32_t>(*a.epoch + 1);
+        *a.epoch = static_cast<int>(ep);
+    }
+    __syncthreads();
+    const int s = threadIdx.x;
+    if (s < a.world && s != a.rank) {
+        st_release_sys(a.peer_flags[s] + a.row * a.world + a.rank, ep);
+        const uint32_t *f = a.flags + a.row * a.world + s;
+        bool ok = false;
+        for (uint32_t it = 0; it < kExchangeWaitLimit && !ok; ++it) ok = ld_acquire_sys(f) == ep;
+        if (!ok && a.status) atomicOr(a.status, kErrWaitTimeout);
+    }
 }
 
 __global__ void __launch_bounds__(kExchangeThreads) k_ep_exchange(ExchangeArgs a) {
