@@ -1,5 +1,5 @@
-"""Parity at two of the benchmark configurations' own model shapes (the third, the MoE 35B-A3B shape, is the one the
-benchmark runs; its structure is covered by the smaller MoE shapes of test_model_gpu.py):
+"""Parity at two of the benchmark configurations' own model shapes (the third, the MoE 35B-A3B shape the benchmark
+runs, has its own test, test_cfg3_gpu.py):
 
 - cfg 1: one full-attention layer (16 q / 4 kv heads, head_dim 128), hidden 2048, SwiGLU FFN 6144, vocab 32768, a
   KV cache of 1024 random positions; greedy acceptance;
