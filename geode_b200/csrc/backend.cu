@@ -1087,7 +1087,6 @@ int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, con
     const size_t need = static_cast<size_t>(S) * (k + 2);
     if (need > g->rej_cap) {
         if (g->rej) cudaFree(g->rej);
-    if (g->d_seen) cudaFree(g->d_seen);
         g->rej = nullptr;
         g->rej_cap = 0;
         if (cudaMalloc(&g->rej, need * sizeof(int)) != cudaSuccess) return fail(g, GCUDA_E_MEMORY, "spec_reject: cudaMalloc");

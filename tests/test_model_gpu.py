@@ -154,7 +154,8 @@ def test_accept_presence_penalty(setup, temperature, top_p, top_k, penalty):
     """gcuda_accept with geode_generate's presence penalty (engine/src/geode.cpp:234-255): the seen list holds the
     oracle's greedy maxima of the batch's rows and random ids, the drafts are the oracle's penalised greedy samples;
     the GPU's kept, next and samples equal the oracle's rule (go_accept_seen, pinned to the reference) on the GPU's own
-    logits bit for bit, and the penalty is seen to move a greedy sample."""
+    logits bit for bit, and the penalty is seen to move a greedy sample. Between the reps the handle's rejection
+    sampler reallocates its scratch, which must leave the accept's device copy of the seen list alone."""
     shape, ora, be, st, rng = setup
     O = op.oracle_lib()
     V = shape.vocab
@@ -176,6 +177,16 @@ def test_accept_presence_penalty(setup, temperature, top_p, top_k, penalty):
                                                             seen)
         assert kept == ref_kept and nxt == ref_next and np.array_equal(samples, ref_samples), \
             (kept, ref_kept, nxt, ref_next, samples, ref_samples)
+        # the handle's rejection sampler grows its own scratch here (S rises every rep); the accept's seen list on the
+        # device must outlive that - the next rep's list is no longer, so its buffer is reused
+        from geode_b200.backend import GSampling
+        S = 2 + 3 * rep
+        tgt = torch.from_numpy(np.ascontiguousarray(np.tile(got[None], (S, 1, 1)))).cuda()
+        dft = torch.from_numpy(np.ascontiguousarray(np.tile(got[None, :4], (S, 1, 1)))).cuda()
+        dd = np.ascontiguousarray(np.tile(toks[1:], S).astype(np.int32))
+        acc, nx = np.zeros(S, np.int32), np.zeros(S, np.int32)
+        assert be.L.gcuda_spec_reject(be.g, tgt.data_ptr(), dft.data_ptr(), dd.ctypes.data, S, 4, V,
+                                      op.C.byref(GSampling(0.7, 1.0, 0)), 5, acc.ctypes.data, nx.ctypes.data) == 0
         if temperature == 0.0:
             moved |= any(samples[i] != int(np.argmax(got[i])) for i in range(kept))
         if kept < 5:
