@@ -72,6 +72,9 @@ def _sig(L):
         "gcuda_begin_device_loop": (i32, [vp, vp, i32]),
         "gcuda_sync_step": (i32, [vp, vp, vp, vp]),
         "gcuda_stream": (vp, [vp]),
+        "gcuda_set_mtp": (i32, [vp, i32, i32, i32, i32, vp]),
+        "gcuda_draft": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
+        "gcuda_draft_next": (i32, [vp, i32, i32, vp, vp, vp]),
     }
     for name, (res, args) in sigs.items():
         if hasattr(L, name):
@@ -146,15 +149,14 @@ class Backend:
             return check(L.gcuda_adopt_raw(self.g, _ptr(b), b.nbytes), name)
 
         attn = [t == "full_attention" for t in c["layer_types"]]
-        layers = (GLayer * c["num_hidden_layers"])()
-        for l in range(c["num_hidden_layers"]):
-            p = f"layers.{l}."
-            x = layers[l]
+
+        def layer(x, p, is_attn, experts):
+            """one decoder layer's tensors under prefix p (layers.{l}. or mtp.layers.0.)"""
             for f_ in GLayer._fields_:
                 setattr(x, f_[0], -1)
-            x.attn = 1 if attn[l] else 0
+            x.attn = 1 if is_attn else 0
             x.in_norm, x.post_norm = raw(p + "input_layernorm.weight"), raw(p + "post_attention_layernorm.weight")
-            if attn[l]:
+            if is_attn:
                 x.q, x.k, x.v, x.o = (q4(p + f"self_attn.{n}_proj.weight") for n in "qkvo")
                 x.q_norm, x.k_norm = raw(p + "self_attn.q_norm.weight"), raw(p + "self_attn.k_norm.weight")
             else:
@@ -169,12 +171,24 @@ class Backend:
             else:
                 x.sh_gate, x.sh_up, x.sh_down = (q4(p + f"mlp.shared_expert.{n}_proj.weight") for n in ("gate", "up", "down"))
                 x.router, x.shared_gate = raw(p + "mlp.gate.weight"), raw(p + "mlp.shared_expert_gate.weight")
-                e = m["experts"]["layers"][l]
-                buf = files[e["file"]]
+                buf = files[experts["file"]]
                 E = c["num_experts"]
-                blocks = np.ascontiguousarray(buf[e["offset"]: e["offset"] + E * e["stride"]])
+                blocks = np.ascontiguousarray(buf[experts["offset"]: experts["offset"] + E * experts["stride"]])
                 sc, _ = tensor_bytes(p + "mlp.experts.scales")
-                x.experts = check(L.gcuda_adopt_experts(self.g, _ptr(blocks), E, e["stride"], _ptr(sc)), p + "experts")
+                x.experts = check(L.gcuda_adopt_experts(self.g, _ptr(blocks), E, experts["stride"], _ptr(sc)),
+                                  p + "experts")
+
+        layers = (GLayer * c["num_hidden_layers"])()
+        for l in range(c["num_hidden_layers"]):
+            layer(layers[l], f"layers.{l}.", attn[l], None if dense else m["experts"]["layers"][l])
+        self.has_mtp = "mtp" in m
+        if self.has_mtp:
+            # the MTP drafting layer (engine/src/model.cpp:175-191): fc, its norms, one attention decoder layer
+            mt = GLayer()
+            layer(mt, "mtp.layers.0.", True, None if dense else m["mtp"]["experts"])
+            check(L.gcuda_set_mtp(self.g, q4("mtp.fc.weight"), raw("mtp.pre_fc_norm_embedding.weight"),
+                                  raw("mtp.pre_fc_norm_hidden.weight"), raw("mtp.norm.weight"), C.addressof(mt)),
+                  "set_mtp")
         eb, et = tensor_bytes("embed_tokens.weight")
         embed = check(L.gcuda_adopt_embedding(self.g, _ptr(eb), et["shape"][0], et["shape"][1], et.get("global", 1.0)), "embed")
         head = q4("lm_head.weight")
@@ -232,6 +246,25 @@ class Backend:
 
     def keep(self, kept: int):
         self._rc(self.L.gcuda_keep(self.g, kept), "keep")
+
+    def draft(self, toks, pos: int, hidden=None, logits: bool = False):
+        """gcuda_draft: the MTP pass over positions pos.. (toks: the next tokens; hidden: their rows, or None for the
+        last verified batch's); (draft, prob, the last position's logits or None)."""
+        toks = np.ascontiguousarray(np.asarray(toks, dtype=np.int32))
+        hd = None if hidden is None else np.ascontiguousarray(hidden, dtype=np.float32)
+        d, pr = C.c_int(0), C.c_float(0.0)
+        lg = np.zeros(self.vocab, np.float32) if logits else None
+        self._rc(self.L.gcuda_draft(self.g, _ptr(toks), len(toks), pos, _ptr(hd) if hd is not None else None,
+                                    C.byref(d), C.byref(pr), _ptr(lg) if lg is not None else None), "draft")
+        return d.value, pr.value, lg
+
+    def draft_next(self, tok: int, pos: int, logits: bool = False):
+        """gcuda_draft_next: one chained MTP position; (draft, prob, logits or None)."""
+        d, pr = C.c_int(0), C.c_float(0.0)
+        lg = np.zeros(self.vocab, np.float32) if logits else None
+        self._rc(self.L.gcuda_draft_next(self.g, int(tok), pos, C.byref(d), C.byref(pr),
+                                         _ptr(lg) if lg is not None else None), "draft_next")
+        return d.value, pr.value, lg
 
     def reset(self):
         self._rc(self.L.gcuda_reset(self.g), "reset")

@@ -291,6 +291,42 @@ __global__ void __launch_bounds__(kArgmaxThreads) k_argmax_rows(const float *__r
 // CTAs per row for k_argmax_rows: about two waves of the GPU over all rows, at most 64 a row
 inline int argmax_slices(int rows, int sms) { return rows >= 2 * sms * 8 ? 1 : std::min(64, std::max(1, 2 * sms * 8 / rows)); }
 
+// softmax_at (engine/src/model.cpp:1287-1292): the probability of the row's entry `*best` under the softmax, the float
+// of 1 / sum_i exp(double(lg[i] - lg[best])) - the difference in float, the exp and the sum in double. Each CTA sums
+// a strided slice, the last CTA to arrive adds the slices in CTA order: the double sum is grouped unlike the
+// reference's one loop, so its last bits may differ; rounded to float the result is the same but where it falls on a
+// rounding boundary of the float.
+constexpr int kSoftmaxCtas = 64, kSoftmaxThreads = 256;
+__global__ void __launch_bounds__(kSoftmaxThreads) k_softmax_at(const float *__restrict__ lg, int V,
+                                                                 const int *__restrict__ best, double *part,
+                                                                 unsigned int *count, float *prob) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
+    __shared__ double red[kSoftmaxThreads / 32];
+    __shared__ bool last;
+    const float m = lg[*best];
+    double acc = 0.0;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x)
+        acc += exp(static_cast<double>(__fsub_rn(lg[i], m)));
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int w = 0; w < kSoftmaxThreads / 32; ++w) t += red[w];
+        part[blockIdx.x] = t;
+        __threadfence();
+        last = atomicAdd(count, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    double sum = 0.0;
+    for (int b = 0; b < static_cast<int>(gridDim.x); ++b) sum += *reinterpret_cast<volatile double *>(part + b);
+    *prob = static_cast<float>(1.0 / sum);
+    *count = 0;
+}
+
 // Greedy speculative acceptance of S sequences from their rows' first maxima (best: [S][k+1] keys of k_argmax_rows):
 // draft i stands while row i's argmax equals it (geode_generate's rule at temperature 0, engine/src/geode.cpp:327-350,
 // without stop tokens); next = the argmax of the first row whose draft fell, or of row k when all stood. One thread

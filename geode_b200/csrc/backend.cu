@@ -168,6 +168,25 @@ struct gcuda {
     void *peer_base[kMaxEpWorld] = {};  // the peers' exchange buffers, mapped here
     float *peer_eout[kMaxEpWorld] = {};
     uint32_t *peer_flags[kMaxEpWorld] = {};
+    // the MTP drafting layer (gcuda_set_mtp): an attention layer with the model's MLP on its own KV slot (attention
+    // slot n_attn), its fc and norms; one pass per draft, captured per row count
+    bool has_mtp = false;
+    int mtp_fc = -1, mtp_pre_e = -1, mtp_pre_h = -1, mtp_norm = -1;
+    gcuda_layer mtp_layer{};
+    LayerPlan mtp_plan;
+    int mtp_fc_u = 0, mtp_lm_u = 0;
+    ActBuf mtp_in;                      // [T][2H]: the fc's input rows, quantized
+    float *mtp_hin = nullptr;           // [T][H]: the hidden rows the pass takes
+    float *mtp_hf = nullptr;            // [T][H]: its rows after mtp.norm (a chained draft's hidden row)
+    float *mtp_logits = nullptr;        // [V]: the last row's logits
+    float *mtp_prob = nullptr;
+    double *mtp_part = nullptr;         // k_softmax_at's partial sums
+    unsigned int *mtp_count = nullptr;
+    int *d_mtp_toks = nullptr, *d_mtp_pos = nullptr, *d_mtp_draft = nullptr;
+    unsigned long long *d_mtp_best = nullptr;
+    cudaGraphExec_t mtp_graph[kMaxTok + 1] = {};
+    uint64_t mtp_graph_kernels[kMaxTok + 1] = {};
+    int mtp_rows = 0;                   // the last pass's rows (a chained draft goes on from row mtp_rows - 1)
 };
 
 namespace {
@@ -301,287 +320,352 @@ int launch_units(gcuda *g, int u0, int nu, const ActBuf &act, int n, bool pdl, i
         if (r_ != GCUDA_OK) return g->err.empty() ? fail(g, r_, #call) : r_;   \
     } while (0)
 
-// The expert outputs of layer l: one buffer on one GPU; under expert parallelism a slot per layer, so that a peer
-// storing layer l + 1's rows never meets this rank still combining layer l's.
+// The expert outputs of layer l: one buffer on one GPU; under expert parallelism a slot per layer (the MTP layer's
+// after the model's), so that a peer storing layer l + 1's rows never meets this rank still combining layer l's.
 float *eout_of(gcuda *g, int l) { return g->eout + (g->ep_world > 1 ? static_cast<size_t>(l) * g->eout_stride : 0); }
+
+const float *raw_of(gcuda *g, int id) {
+    const DevTensor *t = tensor(g, id, kRaw);
+    return t ? static_cast<const float *>(t->d) : nullptr;
+}
+
+// rmsnorm (+ quantize) of the n rows of x into `out` from column col0 (out's rows may be wider than H: the two halves
+// of the MTP layer's input); with combine, the MoE combine of layer moe_layer into x first.
+int enqueue_norm(gcuda *g, int n, float *x, const float *w, bool combine, float *hf_out, int moe_layer,
+                 const ActBuf &out, int col0 = 0) {
+    const gcuda_shape &s = g->sh;
+    NormArgs a{};
+    a.x = x;
+    a.w = w;
+    a.eps = s.eps;
+    a.H = s.hidden;
+    a.n = n;
+    a.hf = hf_out;
+    a.q = out.q + col0;
+    a.scale = out.scale + col0 / 16;
+    a.bsum = out.bsum + col0 / 16;
+    a.ostride = out.cols;
+    if (combine) {
+        a.sh = g->shout;
+        a.gs = g->route->gs;
+        a.eout = eout_of(g, moe_layer);
+        a.wk = g->route->w;
+        a.K = s.top_k;
+    }
+    LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(kNormThreads), 0, g->st, g->pdl, a));
+    return GCUDA_OK;
+}
+
+// Expert parallelism's step start: the epoch advanced and every peer met (k_ep_tick).
+int enqueue_tick(gcuda *g) {
+    TickArgs ta{};
+    ta.epoch = g->ep_epoch;
+    ta.flags = g->xflags;
+    for (int r = 0; r < kMaxEpWorld; ++r) ta.peer_flags[r] = g->peer_flags[r];
+    ta.status = g->d_status;
+    ta.rank = g->ep_rank;
+    ta.world = g->ep_world;
+    ta.row = g->sh.n_layers + 1;
+    k_ep_tick<<<1, 32, 0, g->st>>>(ta);
+    count_launch();
+    LAUNCH_OK(cudaGetLastError());
+    return GCUDA_OK;
+}
+
+// One decoder layer over the n rows of g->x, whose rmsnorm(x, in_norm) is in g->hf / g->hq already: the mixer at
+// the positions d_pos.. (attention over KV slot P.ai), the MLP, then the next norm (next_norm into next_hf and g->hq,
+// with the MoE combine). l: the layer's index (the MTP layer: n_layers).
+int enqueue_layer(gcuda *g, int n, int l, const gcuda_layer &L, const LayerPlan &P, const int *d_pos,
+                  const float *next_norm, float *next_hf) {
+    const gcuda_shape &s = g->sh;
+    const int H = s.hidden;
+    const bool pdl = g->pdl;
+    auto norm = [&](const float *w, bool combine, float *hf_out, int moe_layer = 0) -> int {
+        return enqueue_norm(g, n, g->x, w, combine, hf_out, moe_layer, g->hq);
+    };
+    auto raw = [&](int id) { return raw_of(g, id); };
+    if (!L.attn) {
+        // the a|b product (the recurrence's gates) on the side stream, beside the input product and the conv
+        LAUNCH_OK(cudaEventRecord(g->fork_ev, g->st));
+        LAUNCH_OK(cudaStreamWaitEvent(g->st2, g->fork_ev, 0));
+        RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H, g->hf, H, n, g->ab,
+                               2 * s.gdn_v_heads, g->d_status, g->st2, false));
+        LAUNCH_OK(cudaEventRecord(g->join_ev, g->st2));
+        RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
+        GdnArgs a{};
+        a.proj = g->big;
+        a.z = g->zb;
+        a.ab = g->ab;
+        a.convw = raw(L.conv);
+        a.A_log = raw(L.A_log);
+        a.dt_bias = raw(L.dt_bias);
+        a.gnorm = raw(L.gnorm);
+        const size_t conv_l = static_cast<size_t>(g->conv_dim) * (s.conv_kernel - 1);
+        const size_t st_l = static_cast<size_t>(s.gdn_v_heads) * s.gdn_v_dim * s.gdn_k_dim;
+        a.conv_st = g->conv + P.gi * conv_l;
+        a.state = g->gdn + P.gi * st_l;
+        a.conv_bk = g->conv_bk + P.gi * conv_l;
+        a.state_bk = g->gdn_bk + P.gi * st_l;
+        a.bk_conv_stride = g->conv_n;
+        a.bk_state_stride = g->gdn_n;
+        a.n = n;
+        a.nk = s.gdn_k_heads;
+        a.nv = s.gdn_v_heads;
+        a.dk = s.gdn_k_dim;
+        a.dv = s.gdn_v_dim;
+        a.K = s.conv_kernel;
+        a.eps = s.eps;
+        a.q = g->core.q;
+        a.scale = g->core.scale;
+        a.bsum = g->core.bsum;
+        a.core_f = g->core_f;
+        LAUNCH_OK(launch_ex(k_gdn_conv, dim3((g->conv_dim + 127) / 128), dim3(128), 0, g->st, pdl, a, g->conv_dim,
+                            g->convd));
+        a.proj = g->convd;
+        cudaLaunchConfig_t cfg{};
+        const int S = s.gdn_v_dim / 16;
+        cfg.gridDim = dim3(s.gdn_v_heads * S);
+        cfg.blockDim = dim3(128);
+        cfg.stream = g->st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = S;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = pdl ? 2 : 1;
+        cudaError_t e;
+        LAUNCH_OK(cudaStreamWaitEvent(g->st, g->join_ev, 0));   // (the gates)
+        if (s.gdn_k_dim == 128) e = cudaLaunchKernelEx(&cfg, k_gdn<128>, a);
+        else if (s.gdn_k_dim == 64) e = cudaLaunchKernelEx(&cfg, k_gdn<64>, a);
+        else e = cudaLaunchKernelEx(&cfg, k_gdn<32>, a);
+        count_launch();
+        LAUNCH_OK(e);
+        RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, g->vd));
+    } else {
+        RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
+        AttnPrepArgs pa{};
+        pa.qg = g->big;
+        pa.kb = g->kb;
+        pa.vb = g->vb;
+        pa.q_norm = raw(L.q_norm);
+        pa.k_norm = raw(L.k_norm);
+        pa.inv_freq = g->inv_freq;
+        pa.pos = d_pos;
+        pa.n = n;
+        pa.nh = s.n_heads;
+        pa.nkv = s.n_kv_heads;
+        pa.hd = s.head_dim;
+        pa.half = s.rope_dim / 2;
+        pa.eps = s.eps;
+        pa.qn = g->qn;
+        const size_t kvl = static_cast<size_t>(s.context) * g->kvrow;
+        pa.kc = g->kc + P.ai * kvl;
+        pa.vc = g->vc + P.ai * kvl;
+        pa.ks = g->ks + P.ai * static_cast<size_t>(s.context) * s.n_kv_heads;
+        pa.vs = g->vs + P.ai * static_cast<size_t>(s.context) * s.n_kv_heads;
+        pa.ctx = s.context;
+        pa.status = g->d_status;
+        const int items = n * (s.n_heads + 2 * s.n_kv_heads);
+        LAUNCH_OK(launch_ex(k_attn_prep, dim3((items + 3) / 4), dim3(128), 4 * s.head_dim * sizeof(float), g->st, pdl, pa));
+        AttnArgs aa{};
+        aa.qn = g->qn;
+        aa.kc = pa.kc;
+        aa.vc = pa.vc;
+        aa.ks = pa.ks;
+        aa.vs = pa.vs;
+        aa.pos = d_pos;
+        aa.n = n;
+        aa.nh = s.n_heads;
+        aa.nkv = s.n_kv_heads;
+        aa.ctx = s.context;
+        aa.scale = 1.0f / std::sqrt(static_cast<float>(s.head_dim));
+        aa.part = g->part;
+        aa.nchunks = g->nchunks;
+        const dim3 grid(g->nchunks, s.n_kv_heads);
+        if (s.head_dim == 256) {
+            LAUNCH_OK(launch_ex(k_attn_decode<256>, grid, dim3(kAttnThreads), attn_smem_bytes<256>(), g->st, pdl, aa));
+        } else if (s.head_dim == 128) {
+            LAUNCH_OK(launch_ex(k_attn_decode<128>, grid, dim3(kAttnThreads), attn_smem_bytes<128>(), g->st, pdl, aa));
+        } else {
+            LAUNCH_OK(launch_ex(k_attn_decode<64>, grid, dim3(kAttnThreads), attn_smem_bytes<64>(), g->st, pdl, aa));
+        }
+        MergeArgs ma{};
+        ma.part = g->part;
+        ma.qg = g->big;
+        ma.pos = d_pos;
+        ma.n = n;
+        ma.nh = s.n_heads;
+        ma.hd = s.head_dim;
+        ma.nchunks = g->nchunks;
+        ma.q = g->core.q;
+        ma.scale = g->core.scale;
+        ma.bsum = g->core.bsum;
+        ma.core_f = g->core_f;
+        LAUNCH_OK(launch_ex(k_attn_merge, dim3(n * s.n_heads), dim3(s.head_dim), sizeof(float) * g->nchunks, g->st, pdl, ma));
+        RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, s.n_heads * s.head_dim));
+    }
+    // x += mix happened in the output product's epilogue; h = rmsnorm(x, post_norm)
+    RC_OK(norm(raw(L.post_norm), false, g->hf));
+    if (s.dense) {
+        RC_OK(launch_units(g, P.u_mlp, P.n_mlp, g->hq, n, pdl, 0, true));
+        RC_OK(launch_units(g, P.u_dn, P.n_dn, g->shact, n, pdl));
+        RC_OK(norm(next_norm, false, next_hf));
+    } else {
+        const int E = s.n_experts;
+        RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.router_w), E + 1, H, g->hf, H, n, g->rlog, E + 1,
+                               g->d_status, g->st, pdl));
+        LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(kRouteThreads), kMaxTok * E * sizeof(float), g->st, pdl,
+                            static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, l < s.n_layers ? &g->step->n_union_sum : nullptr,
+                            g->ep_rank, g->ep_world));
+        if (g->tr_route && l < s.n_layers) {
+            LAUNCH_OK(cudaMemcpyAsync(g->tr_route + l, g->route, sizeof(RouteOut), cudaMemcpyDeviceToDevice, g->st));
+            LAUNCH_OK(cudaMemcpyAsync(g->tr_rlog + static_cast<size_t>(l) * n * (E + 1), g->rlog,
+                                      static_cast<size_t>(n) * (E + 1) * sizeof(float), cudaMemcpyDeviceToDevice,
+                                      g->st));
+        }
+        const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
+        const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
+                        *sd = tensor(g, L.sh_down, kQ4Tiled);
+        ExpertsArgs ea{};
+        ea.route = g->route;
+        ea.experts = X.d;
+        ea.stride = X.stride;
+        ea.scales = X.scales;
+        ea.sh_gate = static_cast<const uint8_t *>(sg->d);
+        ea.sh_up = static_cast<const uint8_t *>(su->d);
+        ea.sh_down = static_cast<const uint8_t *>(sd->d);
+        ea.sh_g0 = sg->global;
+        ea.sh_g1 = su->global;
+        ea.sh_g2 = sd->global;
+        ea.H = H;
+        ea.ff = s.moe_ff;
+        ea.sff = s.shared_ff;
+        ea.K = s.top_k;
+        ea.n = n;
+        ea.hq = g->hq.set();
+        ea.amid = g->amid.set();
+        ea.shact = g->shact.set();
+        ea.eout = eout_of(g, l);
+        ea.shout = g->shout;
+        ea.status = g->d_status;
+        for (int pass : {static_cast<int>(kGateUp), static_cast<int>(kDown)}) {
+            GemvShape r;
+            if (!plan_experts(pass, H, s.moe_ff, s.shared_ff, s.n_experts, s.top_k, n, sm_count(), r)) return GCUDA_E_ARG;
+            ea.pass = pass;
+            ea.wpu = r.wpu;
+            ea.nslots = r.nslots;
+            ea.blocked = r.blocked;
+            const int kind = pass == static_cast<int>(kGateUp) ? kKtGateUp : kKtDown;
+            if (!kt_mark(g, kind, true)) return GCUDA_E_CUDA;
+            if (r.stages == kPairStages)
+                LAUNCH_OK(launch_ex(k_gemv_experts<kPairStages>, dim3(sm_count()), dim3(2 * r.nslots * 32), r.smem, g->st, pdl, ea));
+            else if (r.stages == kWideStages)
+                LAUNCH_OK(launch_ex(k_gemv_experts<kWideStages>, dim3(sm_count()),
+                                    dim3((r.blocked ? r.nslots : kStreamWarps) * 32), r.smem, g->st, pdl, ea));
+            else if (r.stages == kDeepStages)
+                LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
+            else
+                LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kFanThreads), r.smem, g->st, pdl, ea));
+            if (!kt_mark(g, kind, false)) return GCUDA_E_CUDA;
+        }
+        if (g->ep_world > 1) {
+            // every pick's row from the rank that owns its expert, stored here by that rank over NVLink, so the
+            // combine below runs on every rank in rank order as on one GPU
+            ExchangeArgs xa{};
+            xa.eout = eout_of(g, l);
+            for (int r = 0; r < kMaxEpWorld; ++r) {
+                xa.peer_eout[r] = g->peer_eout[r] ? g->peer_eout[r] + static_cast<size_t>(l) * g->eout_stride : nullptr;
+                xa.peer_flags[r] = g->peer_flags[r];
+            }
+            xa.flags = g->xflags;
+            xa.route = g->route;
+            xa.epoch = g->ep_epoch;
+            xa.count = g->xcount;
+            xa.status = g->d_status;
+            xa.n = n;
+            xa.K = s.top_k;
+            xa.H = H;
+            xa.rank = g->ep_rank;
+            xa.world = g->ep_world;
+            xa.layer = l;
+            LAUNCH_OK(launch_ex(k_ep_exchange, dim3(kExchangeCtas), dim3(kExchangeThreads), 0, g->st, false, xa));
+        }
+        RC_OK(norm(next_norm, true, next_hf, l));
+    }
+    return GCUDA_OK;
+}
 
 // The verify step for n tokens on g->st (toks in g->d_toks, the position in g->d_pos).
 int enqueue_step(gcuda *g, int n) {
     const gcuda_shape &s = g->sh;
     const int H = s.hidden;
-    const bool pdl = g->pdl;
     const DevTensor *emb = tensor(g, g->embed, kRaw);
-    if (g->ep_world > 1) {   // (the step's epoch: every rank runs the same steps, so the epochs agree)
-        TickArgs ta{};
-        ta.epoch = g->ep_epoch;
-        ta.flags = g->xflags;
-        for (int r = 0; r < kMaxEpWorld; ++r) ta.peer_flags[r] = g->peer_flags[r];
-        ta.status = g->d_status;
-        ta.rank = g->ep_rank;
-        ta.world = g->ep_world;
-        ta.row = s.n_layers;
-        k_ep_tick<<<1, 32, 0, g->st>>>(ta);
-        count_launch();
-        LAUNCH_OK(cudaGetLastError());
-    }
+    if (g->ep_world > 1) RC_OK(enqueue_tick(g));   // (the step's epoch: every rank runs the same steps)
     {
         const dim3 grid((H + 255) / 256, n);
         LAUNCH_OK(launch_ex(k_embed, grid, dim3(256), 0, g->st, false, static_cast<const uint8_t *>(emb->d),
                             static_cast<int64_t>(s.vocab), H, emb->global, static_cast<const int *>(g->d_toks), n, g->x,
                             g->d_status));
     }
-    auto norm = [&](const float *w, bool combine, float *hf_out, int moe_layer = 0) -> int {
-        NormArgs a{};
-        a.x = g->x;
-        a.w = w;
-        a.eps = s.eps;
-        a.H = H;
-        a.n = n;
-        a.hf = hf_out;
-        a.q = g->hq.q;
-        a.scale = g->hq.scale;
-        a.bsum = g->hq.bsum;
-        if (combine) {
-            a.sh = g->shout;
-            a.gs = g->route->gs;
-            a.eout = eout_of(g, moe_layer);
-            a.wk = g->route->w;
-            a.K = s.top_k;
-        }
-        LAUNCH_OK(launch_ex(k_norm_quant, dim3(n), dim3(kNormThreads), 0, g->st, pdl, a));
-        return GCUDA_OK;
-    };
-    auto raw = [&](int id) -> const float * {
-        const DevTensor *t = tensor(g, id, kRaw);
-        return t ? static_cast<const float *>(t->d) : nullptr;
-    };
-    RC_OK(norm(raw(g->layers[0].in_norm), false, g->hf));
+    RC_OK(enqueue_norm(g, n, g->x, raw_of(g, g->layers[0].in_norm), false, g->hf, 0, g->hq));
     const size_t xrows = static_cast<size_t>(n) * H;
     for (int l = 0; l < s.n_layers; ++l) {
-        const gcuda_layer &L = g->layers[static_cast<size_t>(l)];
-        const LayerPlan &P = g->plan[static_cast<size_t>(l)];
         if (g->tr_x)
             LAUNCH_OK(cudaMemcpyAsync(g->tr_x + static_cast<size_t>(l) * xrows, g->x, xrows * sizeof(float),
                                       cudaMemcpyDeviceToDevice, g->st));
-        if (!L.attn) {
-            // the a|b product (the recurrence's gates) on the side stream, beside the input product and the conv
-            LAUNCH_OK(cudaEventRecord(g->fork_ev, g->st));
-            LAUNCH_OK(cudaStreamWaitEvent(g->st2, g->fork_ev, 0));
-            RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.ab_w), 2 * s.gdn_v_heads, H, g->hf, H, n, g->ab,
-                                   2 * s.gdn_v_heads, g->d_status, g->st2, false));
-            LAUNCH_OK(cudaEventRecord(g->join_ev, g->st2));
-            RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
-            GdnArgs a{};
-            a.proj = g->big;
-            a.z = g->zb;
-            a.ab = g->ab;
-            a.convw = raw(L.conv);
-            a.A_log = raw(L.A_log);
-            a.dt_bias = raw(L.dt_bias);
-            a.gnorm = raw(L.gnorm);
-            const size_t conv_l = static_cast<size_t>(g->conv_dim) * (s.conv_kernel - 1);
-            const size_t st_l = static_cast<size_t>(s.gdn_v_heads) * s.gdn_v_dim * s.gdn_k_dim;
-            a.conv_st = g->conv + P.gi * conv_l;
-            a.state = g->gdn + P.gi * st_l;
-            a.conv_bk = g->conv_bk + P.gi * conv_l;
-            a.state_bk = g->gdn_bk + P.gi * st_l;
-            a.bk_conv_stride = g->conv_n;
-            a.bk_state_stride = g->gdn_n;
-            a.n = n;
-            a.nk = s.gdn_k_heads;
-            a.nv = s.gdn_v_heads;
-            a.dk = s.gdn_k_dim;
-            a.dv = s.gdn_v_dim;
-            a.K = s.conv_kernel;
-            a.eps = s.eps;
-            a.q = g->core.q;
-            a.scale = g->core.scale;
-            a.bsum = g->core.bsum;
-            a.core_f = g->core_f;
-            LAUNCH_OK(launch_ex(k_gdn_conv, dim3((g->conv_dim + 127) / 128), dim3(128), 0, g->st, pdl, a, g->conv_dim,
-                                g->convd));
-            a.proj = g->convd;
-            cudaLaunchConfig_t cfg{};
-            const int S = s.gdn_v_dim / 16;
-            cfg.gridDim = dim3(s.gdn_v_heads * S);
-            cfg.blockDim = dim3(128);
-            cfg.stream = g->st;
-            cudaLaunchAttribute attr[2];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = S;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-            attr[1].val.programmaticStreamSerializationAllowed = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = pdl ? 2 : 1;
-            cudaError_t e;
-            LAUNCH_OK(cudaStreamWaitEvent(g->st, g->join_ev, 0));   // (the gates)
-            if (s.gdn_k_dim == 128) e = cudaLaunchKernelEx(&cfg, k_gdn<128>, a);
-            else if (s.gdn_k_dim == 64) e = cudaLaunchKernelEx(&cfg, k_gdn<64>, a);
-            else e = cudaLaunchKernelEx(&cfg, k_gdn<32>, a);
-            count_launch();
-            LAUNCH_OK(e);
-            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, g->vd));
-        } else {
-            RC_OK(launch_units(g, P.u_in, P.n_in, g->hq, n, pdl));
-            AttnPrepArgs pa{};
-            pa.qg = g->big;
-            pa.kb = g->kb;
-            pa.vb = g->vb;
-            pa.q_norm = raw(L.q_norm);
-            pa.k_norm = raw(L.k_norm);
-            pa.inv_freq = g->inv_freq;
-            pa.pos = g->d_pos;
-            pa.n = n;
-            pa.nh = s.n_heads;
-            pa.nkv = s.n_kv_heads;
-            pa.hd = s.head_dim;
-            pa.half = s.rope_dim / 2;
-            pa.eps = s.eps;
-            pa.qn = g->qn;
-            const size_t kvl = static_cast<size_t>(s.context) * g->kvrow;
-            pa.kc = g->kc + P.ai * kvl;
-            pa.vc = g->vc + P.ai * kvl;
-            pa.ks = g->ks + P.ai * static_cast<size_t>(s.context) * s.n_kv_heads;
-            pa.vs = g->vs + P.ai * static_cast<size_t>(s.context) * s.n_kv_heads;
-            pa.ctx = s.context;
-            pa.status = g->d_status;
-            const int items = n * (s.n_heads + 2 * s.n_kv_heads);
-            LAUNCH_OK(launch_ex(k_attn_prep, dim3((items + 3) / 4), dim3(128), 4 * s.head_dim * sizeof(float), g->st, pdl, pa));
-            AttnArgs aa{};
-            aa.qn = g->qn;
-            aa.kc = pa.kc;
-            aa.vc = pa.vc;
-            aa.ks = pa.ks;
-            aa.vs = pa.vs;
-            aa.pos = g->d_pos;
-            aa.n = n;
-            aa.nh = s.n_heads;
-            aa.nkv = s.n_kv_heads;
-            aa.ctx = s.context;
-            aa.scale = 1.0f / std::sqrt(static_cast<float>(s.head_dim));
-            aa.part = g->part;
-            aa.nchunks = g->nchunks;
-            const dim3 grid(g->nchunks, s.n_kv_heads);
-            if (s.head_dim == 256) {
-                LAUNCH_OK(launch_ex(k_attn_decode<256>, grid, dim3(kAttnThreads), attn_smem_bytes<256>(), g->st, pdl, aa));
-            } else if (s.head_dim == 128) {
-                LAUNCH_OK(launch_ex(k_attn_decode<128>, grid, dim3(kAttnThreads), attn_smem_bytes<128>(), g->st, pdl, aa));
-            } else {
-                LAUNCH_OK(launch_ex(k_attn_decode<64>, grid, dim3(kAttnThreads), attn_smem_bytes<64>(), g->st, pdl, aa));
-            }
-            MergeArgs ma{};
-            ma.part = g->part;
-            ma.qg = g->big;
-            ma.pos = g->d_pos;
-            ma.n = n;
-            ma.nh = s.n_heads;
-            ma.hd = s.head_dim;
-            ma.nchunks = g->nchunks;
-            ma.q = g->core.q;
-            ma.scale = g->core.scale;
-            ma.bsum = g->core.bsum;
-            ma.core_f = g->core_f;
-            LAUNCH_OK(launch_ex(k_attn_merge, dim3(n * s.n_heads), dim3(s.head_dim), sizeof(float) * g->nchunks, g->st, pdl, ma));
-            RC_OK(launch_units(g, P.u_out, P.n_out, g->core, n, pdl, s.n_heads * s.head_dim));
-        }
-        // x += mix happened in the output product's epilogue; h = rmsnorm(x, post_norm)
-        RC_OK(norm(raw(L.post_norm), false, g->hf));
-        const float *next_norm = l + 1 < s.n_layers ? raw(g->layers[static_cast<size_t>(l) + 1].in_norm) : raw(g->final_norm);
+        const float *next_norm = l + 1 < s.n_layers ? raw_of(g, g->layers[static_cast<size_t>(l) + 1].in_norm)
+                                                    : raw_of(g, g->final_norm);
         float *next_hf = l + 1 < s.n_layers ? g->hf : g->hid;
-        if (s.dense) {
-            RC_OK(launch_units(g, P.u_mlp, P.n_mlp, g->hq, n, pdl, 0, true));
-            RC_OK(launch_units(g, P.u_dn, P.n_dn, g->shact, n, pdl));
-            RC_OK(norm(next_norm, false, next_hf));
-        } else {
-            const int E = s.n_experts;
-            RC_OK(launch_bf16_gemv(static_cast<const uint16_t *>(P.router_w), E + 1, H, g->hf, H, n, g->rlog, E + 1,
-                                   g->d_status, g->st, pdl));
-            LAUNCH_OK(launch_ex(k_route, dim3(1), dim3(kRouteThreads), kMaxTok * E * sizeof(float), g->st, pdl,
-                                static_cast<const float *>(g->rlog), n, E, s.top_k, g->route, &g->step->n_union_sum,
-                                g->ep_rank, g->ep_world));
-            if (g->tr_route) {
-                LAUNCH_OK(cudaMemcpyAsync(g->tr_route + l, g->route, sizeof(RouteOut), cudaMemcpyDeviceToDevice, g->st));
-                LAUNCH_OK(cudaMemcpyAsync(g->tr_rlog + static_cast<size_t>(l) * n * (E + 1), g->rlog,
-                                          static_cast<size_t>(n) * (E + 1) * sizeof(float), cudaMemcpyDeviceToDevice,
-                                          g->st));
-            }
-            const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
-            const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
-                            *sd = tensor(g, L.sh_down, kQ4Tiled);
-            ExpertsArgs ea{};
-            ea.route = g->route;
-            ea.experts = X.d;
-            ea.stride = X.stride;
-            ea.scales = X.scales;
-            ea.sh_gate = static_cast<const uint8_t *>(sg->d);
-            ea.sh_up = static_cast<const uint8_t *>(su->d);
-            ea.sh_down = static_cast<const uint8_t *>(sd->d);
-            ea.sh_g0 = sg->global;
-            ea.sh_g1 = su->global;
-            ea.sh_g2 = sd->global;
-            ea.H = H;
-            ea.ff = s.moe_ff;
-            ea.sff = s.shared_ff;
-            ea.K = s.top_k;
-            ea.n = n;
-            ea.hq = g->hq.set();
-            ea.amid = g->amid.set();
-            ea.shact = g->shact.set();
-            ea.eout = eout_of(g, l);
-            ea.shout = g->shout;
-            ea.status = g->d_status;
-            for (int pass : {static_cast<int>(kGateUp), static_cast<int>(kDown)}) {
-                GemvShape r;
-                if (!plan_experts(pass, H, s.moe_ff, s.shared_ff, s.n_experts, s.top_k, n, sm_count(), r)) return GCUDA_E_ARG;
-                ea.pass = pass;
-                ea.wpu = r.wpu;
-                ea.nslots = r.nslots;
-                ea.blocked = r.blocked;
-                const int kind = pass == static_cast<int>(kGateUp) ? kKtGateUp : kKtDown;
-                if (!kt_mark(g, kind, true)) return GCUDA_E_CUDA;
-                if (r.stages == kPairStages)
-                    LAUNCH_OK(launch_ex(k_gemv_experts<kPairStages>, dim3(sm_count()), dim3(2 * r.nslots * 32), r.smem, g->st, pdl, ea));
-                else if (r.stages == kWideStages)
-                    LAUNCH_OK(launch_ex(k_gemv_experts<kWideStages>, dim3(sm_count()),
-                                        dim3((r.blocked ? r.nslots : kStreamWarps) * 32), r.smem, g->st, pdl, ea));
-                else if (r.stages == kDeepStages)
-                    LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
-                else
-                    LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kFanThreads), r.smem, g->st, pdl, ea));
-                if (!kt_mark(g, kind, false)) return GCUDA_E_CUDA;
-            }
-            if (g->ep_world > 1) {
-                // every pick's row from the rank that owns its expert, stored here by that rank over NVLink, so the
-                // combine below runs on every rank in rank order as on one GPU
-                ExchangeArgs xa{};
-                xa.eout = eout_of(g, l);
-                for (int r = 0; r < kMaxEpWorld; ++r) {
-                    xa.peer_eout[r] = g->peer_eout[r] ? g->peer_eout[r] + static_cast<size_t>(l) * g->eout_stride : nullptr;
-                    xa.peer_flags[r] = g->peer_flags[r];
-                }
-                xa.flags = g->xflags;
-                xa.route = g->route;
-                xa.epoch = g->ep_epoch;
-                xa.count = g->xcount;
-                xa.status = g->d_status;
-                xa.n = n;
-                xa.K = s.top_k;
-                xa.H = H;
-                xa.rank = g->ep_rank;
-                xa.world = g->ep_world;
-                xa.layer = l;
-                LAUNCH_OK(launch_ex(k_ep_exchange, dim3(kExchangeCtas), dim3(kExchangeThreads), 0, g->st, false, xa));
-            }
-            RC_OK(norm(next_norm, true, next_hf, l));
-        }
+        RC_OK(enqueue_layer(g, n, l, g->layers[static_cast<size_t>(l)], g->plan[static_cast<size_t>(l)], g->d_pos,
+                            next_norm, next_hf));
     }
     if (g->tr_x)
         LAUNCH_OK(cudaMemcpyAsync(g->tr_x + static_cast<size_t>(s.n_layers) * xrows, g->x, xrows * sizeof(float),
                                   cudaMemcpyDeviceToDevice, g->st));
     // the logits of every row (engine/src/model.cpp:5397-5410): hq holds rmsnorm(x, final_norm) quantized
-    RC_OK(launch_units(g, g->lm_u, static_cast<int>((s.vocab + 31) / 32), g->hq, n, pdl));
+    RC_OK(launch_units(g, g->lm_u, static_cast<int>((s.vocab + 31) / 32), g->hq, n, g->pdl));
+    return GCUDA_OK;
+}
+
+// The MTP pass (Model::forward_mtp, engine/src/model.cpp:4965-5039, as its GPU branch runs it for Model::draft,
+// engine/src/model.cpp:1368-1446) over n positions from *d_mtp_pos: the embeddings of the n next tokens
+// (d_mtp_toks) and the n hidden rows (mtp_hin) each through its norm into one 2H-wide row, the fc product, the
+// decoder layer over the MTP's own KV slot, mtp.norm (into mtp_hf), the last row's logits, their first maximum (the
+// greedy draft) and softmax_at's probability of it.
+int enqueue_mtp(gcuda *g, int n) {
+    const gcuda_shape &s = g->sh;
+    const int H = s.hidden;
+    const DevTensor *emb = tensor(g, g->embed, kRaw);
+    if (g->ep_world > 1) RC_OK(enqueue_tick(g));
+    {
+        const dim3 grid((H + 255) / 256, n);
+        LAUNCH_OK(launch_ex(k_embed, grid, dim3(256), 0, g->st, false, static_cast<const uint8_t *>(emb->d),
+                            static_cast<int64_t>(s.vocab), H, emb->global, static_cast<const int *>(g->d_mtp_toks), n,
+                            g->x, g->d_status));
+    }
+    // [rmsnorm(e, pre_e) | rmsnorm(hidden, pre_h)] quantized as one 2H row (its 16-value blocks never straddle the
+    // halves, so the two norms quantize their halves alone), then x = fc . that row
+    RC_OK(enqueue_norm(g, n, g->x, raw_of(g, g->mtp_pre_e), false, nullptr, 0, g->mtp_in, 0));
+    RC_OK(enqueue_norm(g, n, g->mtp_hin, raw_of(g, g->mtp_pre_h), false, nullptr, 0, g->mtp_in, H));
+    RC_OK(launch_units(g, g->mtp_fc_u, (H + 31) / 32, g->mtp_in, n, g->pdl));
+    RC_OK(enqueue_norm(g, n, g->x, raw_of(g, g->mtp_layer.in_norm), false, g->hf, 0, g->hq));
+    RC_OK(enqueue_layer(g, n, s.n_layers, g->mtp_layer, g->mtp_plan, g->d_mtp_pos, raw_of(g, g->mtp_norm), g->mtp_hf));
+    // the last row's logits: hq's row n - 1 holds rmsnorm(x, mtp.norm) quantized
+    ActBuf last = g->hq;
+    last.q += static_cast<size_t>(n - 1) * H;
+    last.scale += static_cast<size_t>(n - 1) * (H / 16);
+    last.bsum += static_cast<size_t>(n - 1) * (H / 16);
+    last.n = 1;
+    RC_OK(launch_units(g, g->mtp_lm_u, static_cast<int>((s.vocab + 31) / 32), last, 1, g->pdl));
+    LAUNCH_OK(launch_ex(k_argmax_rows, dim3(argmax_slices(1, sm_count()), 1), dim3(kArgmaxThreads), 0, g->st, false,
+                        static_cast<const float *>(g->mtp_logits), s.vocab, g->d_mtp_best));
+    LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, false, g->d_mtp_best, 1, g->d_mtp_draft));
+    LAUNCH_OK(launch_ex(k_softmax_at, dim3(kSoftmaxCtas), dim3(kSoftmaxThreads), 0, g->st, false,
+                        static_cast<const float *>(g->mtp_logits), s.vocab, static_cast<const int *>(g->d_mtp_draft),
+                        g->mtp_part, g->mtp_count, g->mtp_prob));
     return GCUDA_OK;
 }
 
@@ -612,6 +696,23 @@ int record_graphs(gcuda *g) {
         }
         if (e != cudaSuccess) return cuda_fail(g, e, "cudaStreamEndCapture");
         const cudaError_t ei = cudaGraphInstantiate(&g->graph[n], graph, 0);
+        cudaGraphDestroy(graph);
+        if (ei != cudaSuccess) return cuda_fail(g, ei, "cudaGraphInstantiate");
+    }
+    for (int n = 1; g->has_mtp && n <= g->sh.max_tokens; ++n) {
+        cudaGraph_t graph = nullptr;
+        LAUNCH_OK(cudaStreamBeginCapture(g->st, cudaStreamCaptureModeThreadLocal));
+        const uint64_t k0 = launch_counter().load();
+        const int rc = enqueue_mtp(g, n);
+        g->mtp_graph_kernels[n] = launch_counter().load() - k0;
+        launch_counter().fetch_sub(g->mtp_graph_kernels[n]);
+        const cudaError_t e = cudaStreamEndCapture(g->st, &graph);
+        if (rc != GCUDA_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e != cudaSuccess) return cuda_fail(g, e, "cudaStreamEndCapture");
+        const cudaError_t ei = cudaGraphInstantiate(&g->mtp_graph[n], graph, 0);
         cudaGraphDestroy(graph);
         if (ei != cudaSuccess) return cuda_fail(g, ei, "cudaGraphInstantiate");
     }
@@ -685,6 +786,8 @@ void gcuda_close(gcuda *g) {
     cudaSetDevice(g->device);
     if (g->st) cudaStreamSynchronize(g->st);
     for (auto &ge : g->graph)
+        if (ge) cudaGraphExecDestroy(ge);
+    for (auto &ge : g->mtp_graph)
         if (ge) cudaGraphExecDestroy(ge);
     for (auto &t : g->tensors)
         if (t.d) cudaFree(t.d);
@@ -832,12 +935,13 @@ int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, c
 }
 
 // The exchange buffer of expert parallelism: this rank's [flags | eout] in one allocation (so one IPC handle maps it),
-// the handles of every rank gathered through NCCL, the peers' buffers opened here. Flags [n_layers + 1][world]: a row
-// per layer's exchange and the step-start row; eout a slot of `slot_floats` per layer.
+// the handles of every rank gathered through NCCL, the peers' buffers opened here. Flags [n_layers + 2][world]: a row
+// per layer's exchange (the MTP layer's after the model's) and the step-start row; eout a slot of `slot_floats` per
+// layer.
 int ep_exchange_setup(gcuda *g, size_t slot_floats) {
     const int W = g->ep_world;
-    const size_t fbytes = (static_cast<size_t>(g->sh.n_layers + 1) * W * sizeof(uint32_t) + 255) / 256 * 256;
-    const size_t bytes = fbytes + static_cast<size_t>(g->sh.n_layers) * slot_floats * sizeof(float);
+    const size_t fbytes = (static_cast<size_t>(g->sh.n_layers + 2) * W * sizeof(uint32_t) + 255) / 256 * 256;
+    const size_t bytes = fbytes + static_cast<size_t>(g->sh.n_layers + 1) * slot_floats * sizeof(float);
     g->eout_stride = slot_floats;
     if (cudaMalloc(&g->xbuf, bytes) != cudaSuccess) {
         g->xbuf = nullptr;
@@ -926,8 +1030,9 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
     // state
     g->conv_n = static_cast<size_t>(g->n_gdn) * g->conv_dim * std::max(0, s.conv_kernel - 1);
     g->gdn_n = static_cast<size_t>(g->n_gdn) * s.gdn_v_heads * s.gdn_v_dim * s.gdn_k_dim;
-    const size_t kv = static_cast<size_t>(g->n_attn) * s.context * g->kvrow;
-    const size_t kvs = static_cast<size_t>(g->n_attn) * s.context * s.n_kv_heads;
+    const int kv_slots = g->n_attn + (g->has_mtp ? 1 : 0);   // (the MTP layer's slot after the model's)
+    const size_t kv = static_cast<size_t>(kv_slots) * s.context * g->kvrow;
+    const size_t kvs = static_cast<size_t>(kv_slots) * s.context * s.n_kv_heads;
     g->nchunks = (s.context + kAttnChunk - 1) / kAttnChunk;
     const int E = s.dense ? 0 : s.n_experts, K = s.dense ? 1 : s.top_k;
     const int ffw = s.dense ? 64 : s.moe_ff;
@@ -954,6 +1059,13 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         !act_alloc(g, g->amid, T * K, ffw) || !act_alloc(g, g->shact, T, s.shared_ff))
         return GCUDA_E_MEMORY;
     if (g->ep_world > 1) RC_OK(ep_exchange_setup(g, static_cast<size_t>(T) * K * H));
+    if (g->has_mtp &&
+        (!act_alloc(g, g->mtp_in, T, 2 * H) || !dalloc(g, &g->mtp_hin, static_cast<size_t>(T) * H) ||
+         !dalloc(g, &g->mtp_hf, static_cast<size_t>(T) * H) || !dalloc(g, &g->mtp_logits, s.vocab) ||
+         !dalloc(g, &g->mtp_prob, 1) || !dalloc(g, &g->mtp_part, kSoftmaxCtas) || !dalloc(g, &g->mtp_count, 1) ||
+         !dalloc(g, &g->d_mtp_toks, kMaxTok) || !dalloc(g, &g->d_mtp_pos, 1) || !dalloc(g, &g->d_mtp_draft, 1) ||
+         !dalloc(g, &g->d_mtp_best, 1)))
+        return GCUDA_E_MEMORY;
     // inv_freq as the reference computes it (engine/src/model.cpp:737-740), host powf
     {
         std::vector<float> inv(static_cast<size_t>(std::max(1, s.rope_dim / 2)));
@@ -966,11 +1078,9 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
     g->plan.assign(static_cast<size_t>(s.n_layers), LayerPlan{});
     int gi = 0, ai = 0;
     auto q4 = [&](int id) { return tensor(g, id, kQ4Tiled); };
-    for (int l = 0; l < s.n_layers; ++l) {
-        const gcuda_layer &L = g->layers[static_cast<size_t>(l)];
-        LayerPlan &P = g->plan[static_cast<size_t>(l)];
+    auto build = [&](const gcuda_layer &L, LayerPlan &P, const std::string &name) -> int {
         if (!tensor(g, L.in_norm, kRaw) || !tensor(g, L.post_norm, kRaw))
-            return fail(g, GCUDA_E_ARG, "setup: layer " + std::to_string(l) + " lacks its norms");
+            return fail(g, GCUDA_E_ARG, "setup: layer " + name + " lacks its norms");
         if (!L.attn) {
             P.gi = gi++;
             const DevTensor *qkv = q4(L.qkv), *z = q4(L.z), *out = q4(L.out);
@@ -978,7 +1088,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
             if (!qkv || !z || !out || !a || !b || !tensor(g, L.conv, kRaw) || !tensor(g, L.A_log, kRaw) ||
                 !tensor(g, L.dt_bias, kRaw) || !tensor(g, L.gnorm, kRaw) || qkv->rows != g->conv_dim || z->rows != g->vd ||
                 out->rows != H || out->cols != g->vd)
-                return fail(g, GCUDA_E_ARG, "setup: GDN layer " + std::to_string(l) + " tensors");
+                return fail(g, GCUDA_E_ARG, "setup: GDN layer " + name + " tensors");
             P.u_in = static_cast<int>(U.size());
             plain_units(U, *qkv, g->big, g->conv_dim, kStore);
             plain_units(U, *z, g->zb, g->vd, kStore);
@@ -994,7 +1104,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
             const DevTensor *q = q4(L.q), *k = q4(L.k), *v = q4(L.v), *o = q4(L.o);
             if (!q || !k || !v || !o || !tensor(g, L.q_norm, kRaw) || !tensor(g, L.k_norm, kRaw) || q->rows != g->qw ||
                 k->rows != g->kvrow || v->rows != g->kvrow || o->rows != H || o->cols != s.n_heads * s.head_dim)
-                return fail(g, GCUDA_E_ARG, "setup: attention layer " + std::to_string(l) + " tensors");
+                return fail(g, GCUDA_E_ARG, "setup: attention layer " + name + " tensors");
             P.u_in = static_cast<int>(U.size());
             plain_units(U, *q, g->big, g->qw, kStore);
             plain_units(U, *k, g->kb, g->kvrow, kStore);
@@ -1006,7 +1116,7 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         }
         const DevTensor *sg = q4(L.sh_gate), *su = q4(L.sh_up), *sd = q4(L.sh_down);
         if (!sg || !su || !sd || sg->rows != s.shared_ff || su->rows != s.shared_ff || sd->rows != H)
-            return fail(g, GCUDA_E_ARG, "setup: layer " + std::to_string(l) + " MLP tensors");
+            return fail(g, GCUDA_E_ARG, "setup: layer " + name + " MLP tensors");
         if (s.dense) {
             P.u_mlp = static_cast<int>(U.size());
             swiglu_units(U, *sg, *su, g->shact);
@@ -1018,17 +1128,35 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
             const DevTensor *r = tensor(g, L.router, kRaw), *gt = tensor(g, L.shared_gate, kRaw);
             if (!r || !gt || L.experts < 0 || L.experts >= static_cast<int>(g->experts.size()) ||
                 g->experts[static_cast<size_t>(L.experts)].n != s.n_experts)
-                return fail(g, GCUDA_E_ARG, "setup: MoE layer " + std::to_string(l) + " tensors");
+                return fail(g, GCUDA_E_ARG, "setup: MoE layer " + name + " tensors");
             if (!dalloc(g, &P.router_w, static_cast<size_t>(s.n_experts + 1) * H)) return GCUDA_E_MEMORY;
             cudaMemcpy(P.router_w, r->d, r->bytes, cudaMemcpyDeviceToDevice);
             cudaMemcpy(P.router_w + static_cast<size_t>(s.n_experts) * H, gt->d, gt->bytes, cudaMemcpyDeviceToDevice);
         }
+        return GCUDA_OK;
+    };
+    for (int l = 0; l < s.n_layers; ++l)
+        RC_OK(build(g->layers[static_cast<size_t>(l)], g->plan[static_cast<size_t>(l)], std::to_string(l)));
+    if (g->has_mtp) {
+        // the MTP layer: attention slot n_attn (its KV after the model's), the fc [H][2H], its norms
+        if (!g->mtp_layer.attn) return fail(g, GCUDA_E_ARG, "setup: the MTP layer is no attention layer");
+        RC_OK(build(g->mtp_layer, g->mtp_plan, "mtp"));
+        const DevTensor *fc = q4(g->mtp_fc);
+        if (!fc || fc->rows != H || fc->cols != 2 * H || !tensor(g, g->mtp_pre_e, kRaw) || !tensor(g, g->mtp_pre_h, kRaw) ||
+            !tensor(g, g->mtp_norm, kRaw))
+            return fail(g, GCUDA_E_ARG, "setup: the MTP layer's fc / norms");
+        g->mtp_fc_u = static_cast<int>(U.size());
+        plain_units(U, *fc, g->x, H, kStore);
     }
     const DevTensor *head = q4(lm_head);
     if (!head || head->rows != s.vocab || !tensor(g, final_norm, kRaw) || !tensor(g, embed, kRaw))
         return fail(g, GCUDA_E_ARG, "setup: lm_head / norm / embedding");
     g->lm_u = static_cast<int>(U.size());
     plain_units(U, *head, g->logits, s.vocab, kStore);
+    if (g->has_mtp) {
+        g->mtp_lm_u = static_cast<int>(U.size());
+        plain_units(U, *head, g->mtp_logits, s.vocab, kStore);
+    }
     g->n_units = static_cast<int>(U.size());
     if (!dalloc(g, &g->units, U.size())) return GCUDA_E_MEMORY;
     cudaMemcpy(g->units, U.data(), U.size() * sizeof(GemvUnit), cudaMemcpyHostToDevice);
@@ -1075,6 +1203,71 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
     if (hidden) LAUNCH_OK(cudaMemcpyAsync(hidden, g->hid, sizeof(float) * n * g->sh.hidden, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
     return GCUDA_OK;
+}
+
+int gcuda_set_mtp(gcuda *g, int fc, int pre_e, int pre_h, int norm, const gcuda_layer *layer) {
+    if (!g || !layer) return fail(g, GCUDA_E_ARG, "set_mtp: no layer");
+    if (g->ready) return fail(g, GCUDA_E_STATE, "set_mtp: after setup");
+    if (!layer->attn) return fail(g, GCUDA_E_ARG, "set_mtp: the MTP layer is an attention layer");
+    g->has_mtp = true;
+    g->mtp_fc = fc;
+    g->mtp_pre_e = pre_e;
+    g->mtp_pre_h = pre_h;
+    g->mtp_norm = norm;
+    g->mtp_layer = *layer;
+    return GCUDA_OK;
+}
+
+namespace {
+// one MTP pass of n rows (its inputs in place): the captured pass, then the draft, its probability and the logits
+int run_mtp(gcuda *g, int n, int *draft, float *prob, float *logits) {
+    LAUNCH_OK(cudaGraphLaunch(g->mtp_graph[n], g->st));
+    count_launch(g->mtp_graph_kernels[n]);
+    RC_OK(check_status(g));
+    g->mtp_rows = n;
+    LAUNCH_OK(cudaMemcpyAsync(draft, g->d_mtp_draft, sizeof(int), cudaMemcpyDeviceToHost, g->st));
+    if (prob) LAUNCH_OK(cudaMemcpyAsync(prob, g->mtp_prob, sizeof(float), cudaMemcpyDeviceToHost, g->st));
+    if (logits)
+        LAUNCH_OK(cudaMemcpyAsync(logits, g->mtp_logits, sizeof(float) * g->sh.vocab, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    return GCUDA_OK;
+}
+
+int mtp_checks(gcuda *g, const int *toks, int n, int pos, int *draft) {
+    if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "draft before setup");
+    if (!g->has_mtp) return fail(g, GCUDA_E_STATE, "draft: no MTP layer (gcuda_set_mtp before gcuda_setup)");
+    if (!toks || !draft || n < 1 || n > g->sh.max_tokens || pos < 0 || pos + n > g->sh.context)
+        return fail(g, GCUDA_E_ARG, "bad draft");
+    for (int t = 0; t < n; ++t)
+        if (toks[t] < 0 || toks[t] >= g->sh.vocab)
+            return fail(g, GCUDA_E_ARG, "cannot read the embedding of token " + std::to_string(toks[t]));
+    return GCUDA_OK;
+}
+}  // namespace
+
+int gcuda_draft(gcuda *g, const int *toks, int n, int pos, const float *hidden, int *draft, float *prob, float *logits) {
+    RC_OK(mtp_checks(g, toks, n, pos, draft));
+    if (!hidden && n > g->last_batch)
+        return fail(g, GCUDA_E_STATE, "draft: the last verified batch has fewer than " + std::to_string(n) + " rows");
+    cudaSetDevice(g->device);
+    const size_t rows = static_cast<size_t>(n) * g->sh.hidden * sizeof(float);
+    LAUNCH_OK(cudaMemcpyAsync(g->d_mtp_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->d_mtp_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    if (hidden) LAUNCH_OK(cudaMemcpyAsync(g->mtp_hin, hidden, rows, cudaMemcpyHostToDevice, g->st));
+    else LAUNCH_OK(cudaMemcpyAsync(g->mtp_hin, g->hid, rows, cudaMemcpyDeviceToDevice, g->st));
+    return run_mtp(g, n, draft, prob, logits);
+}
+
+int gcuda_draft_next(gcuda *g, int tok, int pos, int *draft, float *prob, float *logits) {
+    RC_OK(mtp_checks(g, &tok, 1, pos, draft));
+    if (g->mtp_rows < 1) return fail(g, GCUDA_E_STATE, "draft_next without a draft before it");
+    cudaSetDevice(g->device);
+    const size_t H = static_cast<size_t>(g->sh.hidden);
+    LAUNCH_OK(cudaMemcpyAsync(g->d_mtp_toks, &tok, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->d_mtp_pos, &pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->mtp_hin, g->mtp_hf + (g->mtp_rows - 1) * H, H * sizeof(float), cudaMemcpyDeviceToDevice,
+                              g->st));
+    return run_mtp(g, 1, draft, prob, logits);
 }
 
 int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, const int *drafts, int S, int k, int V,
@@ -1232,6 +1425,7 @@ int gcuda_reset(gcuda *g) {
     g->pos = 0;
     g->last_batch = 0;
     g->reject_steps = 0;   // the device-side rejection sampler's Philox sequence starts over with the conversation
+    g->mtp_rows = 0;
     return GCUDA_OK;
 }
 

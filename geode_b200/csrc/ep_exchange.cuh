@@ -22,7 +22,7 @@ constexpr uint32_t kExchangeWaitLimit = 1u << 24;   // polls of a peer's flag be
 struct ExchangeArgs {
     float *eout;                          // this layer's rows [n * K][H] (its own picks computed, the rest to come)
     float *peer_eout[kMaxEpWorld];        // the peers' slots for this layer (this rank's entry: unused)
-    uint32_t *peer_flags[kMaxEpWorld];    // the peers' flags [n_layers + 1][world]
+    uint32_t *peer_flags[kMaxEpWorld];    // the peers' flags [n_layers + 2][world]
     uint32_t *flags;                      // this rank's flags, written by the peers
     const RouteOut *route;
     const int *epoch;

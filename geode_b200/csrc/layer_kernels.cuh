@@ -54,9 +54,10 @@ struct NormArgs {
     float eps;
     int H, n;
     float *hf;                // [n][H] or NULL
-    int8_t *q;                // [n][H]
-    float *scale;             // [n][H/16]
+    int8_t *q;                // [n][ostride]: row t's H values at q + t * ostride
+    float *scale;             // [n][ostride / 16]
     int32_t *bsum;
+    int ostride;              // the output rows' width (H, or wider: one part of a wider row); 0 = H
     // the MoE combine, when sh != NULL: x += gs[t] * sh[t] + sum_k w[t][k] * eout[t*K + k] (rank order)
     const float *sh, *gs, *eout, *wk;
     int K;
@@ -128,9 +129,10 @@ __global__ void __launch_bounds__(kNormThreads) k_norm_quant(NormArgs a) {
     for (int w = 0; w < kNormThreads / 32; ++w) tot += red[w];
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(tot / H), a.eps)));
     float *hf = a.hf ? a.hf + static_cast<size_t>(t) * H : nullptr;
-    int8_t *q = a.q + static_cast<size_t>(t) * H;
-    float *scale = a.scale + static_cast<size_t>(t) * (H / 16);
-    int32_t *bsum = a.bsum + static_cast<size_t>(t) * (H / 16);
+    const int os = a.ostride ? a.ostride : H;
+    int8_t *q = a.q + static_cast<size_t>(t) * os;
+    float *scale = a.scale + static_cast<size_t>(t) * (os / 16);
+    int32_t *bsum = a.bsum + static_cast<size_t>(t) * (os / 16);
     // 16 consecutive values per half-warp
 #pragma unroll
     for (int k = 0; k < kNormPer; ++k) {

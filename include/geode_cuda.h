@@ -83,11 +83,13 @@ int gcuda_adopt_experts(gcuda *g, const uint8_t *blocks, int n, size_t stride, c
 int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, int embed, int lm_head, int final_norm);
 
 /* Expert parallelism (no counterpart in the reference, which runs on one device): the MoE layers' routed experts
- * striped over `world` handles, one per GPU (expert e on rank e % world); everything else computed on every rank. The
- * expert outputs meet through one NCCL all-reduce per MoE layer on the handle's stream (each pick's row is non-zero on
- * its owner only, so the sum is that row exactly), and every rank combines in rank order: the logits equal the
+ * striped over `world` (<= 8) handles, one per GPU of one node (expert e on rank e % world); everything else computed
+ * on every rank. In each MoE layer every rank stores the rows of the picks it owns into every peer's buffer over
+ * NVLink (peer memory mapped through CUDA IPC at gcuda_setup; per-layer flags with bounded waits - a peer that never
+ * arrives makes the step fail with GCUDA_E_DEVICE), and every rank combines in rank order: the logits equal the
  * one-GPU step's bit for bit. gcuda_ep_unique_id fills NCCL's 128-byte id on one rank, which the caller hands to
- * every rank; gcuda_set_ep (before gcuda_setup, same id, ranks 0..world-1, each its own device) joins the group.
+ * every rank; gcuda_set_ep (before gcuda_setup, same id, ranks 0..world-1, each its own device) joins the group, and
+ * every rank must then reach gcuda_setup (it gathers the buffers' handles through NCCL) and run the same calls.
  * libnccl.so.2 is loaded on first use; world 1 needs none. */
 int gcuda_ep_unique_id(void *id_out);
 int gcuda_set_ep(gcuda *g, int rank, int world, const void *id);
@@ -101,6 +103,21 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
  * Gated DeltaNet states as after token kept-1, the position back by n - kept. */
 int gcuda_keep(gcuda *g, int kept);
 int gcuda_position(gcuda *g);
+
+/* The MTP drafting layer (Model::forward_mtp, engine/src/model.cpp:4965-5039; the pack's mtp.* tensors,
+ * engine/src/model.cpp:175-191): its fc [hidden][2 hidden] (q4), the norms mtp.pre_fc_norm_embedding / _hidden and
+ * mtp.norm (f32), and its decoder layer (an attention layer with the model's MLP; routed experts by
+ * gcuda_adopt_experts). Before gcuda_setup, which gives the layer its own KV cache of `context` positions. */
+int gcuda_set_mtp(gcuda *g, int fc, int pre_e, int pre_h, int norm, const gcuda_layer *layer);
+/* Model::draft (engine/src/model.cpp:1295-1446, its GPU branch): the MTP pass over the positions pos .. pos+n-1 of
+ * its KV (n <= max_tokens), position i taking the embedding of toks[i] and hidden row i - hidden [n][hidden] on the
+ * host, or NULL for the last verified batch's rows (gcuda_verify's `hidden`; n at most that batch's size) - then
+ * draft = the first maximum of the last position's logits and prob (NULL: not wanted) its softmax probability
+ * (softmax_at, engine/src/model.cpp:1287-1292); logits (NULL: not wanted) gets those vocab logits. */
+int gcuda_draft(gcuda *g, const int *toks, int n, int pos, const float *hidden, int *draft, float *prob, float *logits);
+/* Model::draft_next (engine/src/model.cpp:1448-1480): one chained MTP position `pos` from the last pass's output row
+ * after mtp.norm and the embedding of tok (the draft just made). */
+int gcuda_draft_next(gcuda *g, int tok, int pos, int *draft, float *prob, float *logits);
 /* The conversation from the start (position 0, zero states; the device-side rejection sampler's random sequence
  * restarts too, so a repeated conversation with the same seed draws the same uniforms). */
 int gcuda_reset(gcuda *g);
