@@ -50,6 +50,9 @@ bool CudaApi::load(const std::string &path, std::string &err) {
     sym(state_get, "gcuda_state_get");
     sym(state_put, "gcuda_state_put");
     sym(reset, "gcuda_reset");
+    sym(set_mtp, "gcuda_set_mtp");
+    sym(draft, "gcuda_draft");
+    sym(draft_next, "gcuda_draft_next");
     return ok;
 }
 
@@ -101,11 +104,9 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
         return id >= 0 || fail(name.c_str(), err);
     };
     const JsonRef types = c["layer_types"];
-    for (int l = 0; l < L; ++l) {
-        gcuda_layer &x = layers[static_cast<size_t>(l)];
+    // one decoder layer's tensors under prefix p; l: its index for the expert table (-1: the MTP layer's)
+    auto load_layer = [&](gcuda_layer &x, const std::string &p, bool attn, int l) -> bool {
         std::memset(&x, 0xFF, sizeof x);   // every id -1
-        const std::string p = "layers." + std::to_string(l) + ".";
-        const bool attn = types[static_cast<size_t>(l)].text() == "full_attention";
         x.attn = attn ? 1 : 0;
         bool ok = raw(p + "input_layernorm.weight", x.in_norm) && raw(p + "post_attention_layernorm.weight", x.post_norm);
         if (attn) {
@@ -138,7 +139,22 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
                 }
             }
         }
-        if (!ok) return false;
+        return ok;
+    };
+    for (int l = 0; l < L; ++l)
+        if (!load_layer(layers[static_cast<size_t>(l)], "layers." + std::to_string(l) + ".",
+                        types[static_cast<size_t>(l)].text() == "full_attention", l))
+            return false;
+    // the MTP drafting layer (engine/src/model.cpp:175-191), when the pack has one: on the device beside the model
+    if (pack_.has("mtp.fc.weight")) {
+        gcuda_layer mt;
+        int fc = -1, pre_e = -1, pre_h = -1, mnorm = -1;
+        if (!load_layer(mt, "mtp.layers.0.", true, -1) || !q4("mtp.fc.weight", fc) ||
+            !raw("mtp.pre_fc_norm_embedding.weight", pre_e) || !raw("mtp.pre_fc_norm_hidden.weight", pre_h) ||
+            !raw("mtp.norm.weight", mnorm))
+            return false;
+        if (api_.set_mtp(g_, fc, pre_e, pre_h, mnorm, &mt) != 0) return fail("set_mtp", err);
+        has_mtp_ = true;
     }
     TensorView et;
     if (!pack_.tensor("embed_tokens.weight", et, err)) return false;
@@ -192,6 +208,22 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
         if (tensors.key_at(i).substr(0, 7) == "vision.") text_only_ = false;   // (engine/src/vision.cpp's tensors)
     conv_id_ = new_conversation_id(this);
     return true;
+}
+
+bool CudaModel::draft(const int *toks, int n, int pos, const float *hidden, int &draft, float *prob, std::string &err) {
+    if (!g_ || !has_mtp_) {
+        err = "no drafting: the pack has no MTP layer";
+        return false;
+    }
+    return api_.draft(g_, toks, n, pos, hidden, &draft, prob, nullptr) == 0 || fail("draft", err);
+}
+
+bool CudaModel::draft_next(int tok, int pos, int &draft, float *prob, std::string &err) {
+    if (!g_ || !has_mtp_) {
+        err = "no drafting: the pack has no MTP layer";
+        return false;
+    }
+    return api_.draft_next(g_, tok, pos, &draft, prob, nullptr) == 0 || fail("draft_next", err);
 }
 
 uint64_t CudaModel::state_fingerprint() const { return ghost::state_fingerprint(pack_print(dir_), shapes_); }

@@ -34,6 +34,9 @@ struct CudaApi {
     decltype(&gcuda_state_get) state_get = nullptr;
     decltype(&gcuda_state_put) state_put = nullptr;
     decltype(&gcuda_reset) reset = nullptr;
+    decltype(&gcuda_set_mtp) set_mtp = nullptr;
+    decltype(&gcuda_draft) draft = nullptr;
+    decltype(&gcuda_draft_next) draft_next = nullptr;
     // path: the library file; empty = libgeode_cuda.so beside this library
     bool load(const std::string &path, std::string &err);
     ~CudaApi();
@@ -126,6 +129,14 @@ public:
     bool step(const int *batch, int n, const SamplerParams &p, Sampler &s, SeenTokens &seen, const int *stops,
               int n_stops, int &kept, int &next, std::string &err);
 
+    // Model::draft / draft_next (engine/src/model.cpp:1295-1480) on the device's MTP layer: the MTP pass over the
+    // positions pos .. pos+n-1 (toks: the tokens after them; hidden: n rows, or NULL for the last verified batch's),
+    // the greedy draft from the last position and its softmax probability (prob may be NULL); draft_next: one chained
+    // position from the last pass's own output row. False when the pack has no MTP layer.
+    bool has_mtp() const { return has_mtp_; }
+    bool draft(const int *toks, int n, int pos, const float *hidden, int &draft, float *prob, std::string &err);
+    bool draft_next(int tok, int pos, int &draft, float *prob, std::string &err);
+
     // Model::save_state / load_state (engine/src/state.cpp:241-465) in the engine's state file: the device's KV rows
     // and recurrent states through the host (gcuda_state_get / gcuda_state_put), so a state saved by the reference
     // engine (CPU or GPU path) continues here and back. extra: the caller's token passed on but not computed yet.
@@ -147,6 +158,7 @@ private:
     std::string dir_;
     StateShapes shapes_;
     bool text_only_ = true;    // no MTP layer, no vision encoder in the pack
+    bool has_mtp_ = false;     // the MTP layer is on the device (gcuda_set_mtp)
     uint64_t conv_id_ = 0;     // the conversation (new at open and after a failed load; a loaded state's)
 };
 

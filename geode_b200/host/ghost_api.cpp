@@ -62,6 +62,31 @@ int ghost_verify(ghost_model *m, const int32_t *toks, int32_t n, float *logits, 
     return GHOST_OK;
 }
 
+int ghost_draft(ghost_model *m, const int32_t *toks, int32_t n, int32_t pos, const float *hidden, int32_t *draft,
+                float *prob, char *err, size_t err_len) {
+    if (!m || !toks || !draft || n < 1) return GHOST_E_ARG;
+    std::string e;
+    int d = -1;
+    if (!m->model.draft(toks, n, pos, hidden, d, prob, e)) {
+        put(e, err, err_len);
+        return GHOST_E_BACKEND;
+    }
+    *draft = d;
+    return GHOST_OK;
+}
+
+int ghost_draft_next(ghost_model *m, int32_t tok, int32_t pos, int32_t *draft, float *prob, char *err, size_t err_len) {
+    if (!m || !draft) return GHOST_E_ARG;
+    std::string e;
+    int d = -1;
+    if (!m->model.draft_next(tok, pos, d, prob, e)) {
+        put(e, err, err_len);
+        return GHOST_E_BACKEND;
+    }
+    *draft = d;
+    return GHOST_OK;
+}
+
 int ghost_reset(ghost_model *m, char *err, size_t err_len) {
     if (!m) return GHOST_E_ARG;
     std::string e;

@@ -100,21 +100,25 @@ bool Pack::tensor(const std::string &name, TensorView &out, std::string &err) co
 
 bool Pack::experts(int layer, ExpertTable &out, std::string &err) const {
     const JsonRef ls = manifest()["experts"]["layers"];
-    if (!ls.is_list() || layer < 0 || static_cast<size_t>(layer) >= ls.size()) {
-        err = "no expert table for layer " + std::to_string(layer);
+    const std::string what = layer < 0 ? std::string("the MTP layer") : "layer " + std::to_string(layer);
+    // layer -1: the MTP layer's table, the manifest's "mtp": {"experts": ...} (engine/src/pack.cpp:300-305)
+    const JsonRef e = layer < 0 ? manifest()["mtp"]["experts"]
+                                : (ls.is_list() && static_cast<size_t>(layer) < ls.size() ? ls[static_cast<size_t>(layer)]
+                                                                                          : JsonRef());
+    if (!e.is_map()) {
+        err = "no expert table for " + what;
         return false;
     }
-    const JsonRef e = ls[static_cast<size_t>(layer)];
     const auto f = files_.find(e["file"].text());
     if (f == files_.end()) {
-        err = "experts of layer " + std::to_string(layer) + ": unknown file";
+        err = "experts of " + what + ": unknown file";
         return false;
     }
     out.stride = static_cast<size_t>(e["stride"].integer());
     const size_t off = static_cast<size_t>(e["offset"].integer());
     const size_t n = static_cast<size_t>(config()["num_experts"].integer());
     if (off + n * out.stride > f->second.size) {
-        err = "experts of layer " + std::to_string(layer) + " run past their file";
+        err = "experts of " + what + " run past their file";
         return false;
     }
     out.data = f->second.data + off;

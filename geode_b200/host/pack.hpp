@@ -45,6 +45,7 @@ public:
     bool has(const std::string &name) const { return m_.root()["tensors"][name].present(); }
     // false (and err) when the tensor is missing or its bytes run past its file
     bool tensor(const std::string &name, TensorView &out, std::string &err) const;
+    // a MoE layer's routed experts (layer -1: the MTP layer's)
     bool experts(int layer, ExpertTable &out, std::string &err) const;
 
 private:

@@ -48,6 +48,15 @@ int32_t ghost_spec_tokens(ghost_model *m);
 int32_t ghost_position(ghost_model *m);
 /* Model::verify_n: n tokens through every layer at the next positions; logits [n][vocab] (NULL: not wanted) */
 int ghost_verify(ghost_model *m, const int32_t *toks, int32_t n, float *logits, char *err, size_t err_len);
+/* Model::draft / draft_next (engine/src/model.cpp:1295-1480) on the device's MTP layer (packs with mtp.*; else
+ * GHOST_E_BACKEND): the MTP pass over positions pos .. pos+n-1 - toks the tokens after them, hidden n rows of hidden
+ * floats or NULL for the last verified batch's rows - the greedy draft from the last position, prob (NULL: not wanted)
+ * its softmax probability; ghost_draft_next: one chained position pos from the last pass's own output row and tok. The
+ * engine's loop: after a step that kept k rows of a batch at P, ghost_draft(the k tokens after P .. P+k-1, k, P, NULL)
+ * drafts the next batch's first draft, ghost_draft_next chains the rest while the probability stays high. */
+int ghost_draft(ghost_model *m, const int32_t *toks, int32_t n, int32_t pos, const float *hidden, int32_t *draft,
+                float *prob, char *err, size_t err_len);
+int ghost_draft_next(ghost_model *m, int32_t tok, int32_t pos, int32_t *draft, float *prob, char *err, size_t err_len);
 /* geode_reset (engine/include/geode/geode.h:216): the conversation empty - position 0, zero states, no pending token, a
  * new conversation (an append of a later save goes to a new file). */
 int ghost_reset(ghost_model *m, char *err, size_t err_len);

@@ -263,3 +263,62 @@ def test_host_prefill(env):
     lg2 = np.zeros_like(lg)
     assert H.ghost_verify(m, toks.ctypes.data_as(C.c_void_p), 5, lg2.ctypes.data_as(C.c_void_p), err, 512) == 0
     assert np.array_equal(lg2, lg)
+
+
+def test_host_drafts(tmp_path):
+    """ghost_draft / ghost_draft_next through the host (a pack with the MTP layer: CudaModel adopts mtp.* and the
+    MTP layer's experts, gcuda_set_mtp) equal the Python binding's gcuda_draft / gcuda_draft_next after the same
+    batches - the same kernels on the same bytes, so the same drafts and probabilities bit for bit; the pass's
+    numerics against the oracle are tests/test_mtp_gpu.py's. A pack without the layer refuses to draft."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from geode_b200.backend import Backend
+    H = C.CDLL(HOST_SO)
+    vp, i32 = C.c_void_p, C.c_int32
+    H.ghost_open.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp), C.c_char_p, C.c_size_t]
+    H.ghost_close.argtypes = [vp]
+    H.ghost_verify.argtypes = [vp, vp, i32, vp, C.c_char_p, C.c_size_t]
+    H.ghost_draft.argtypes = [vp, vp, i32, i32, vp, C.POINTER(i32), C.POINTER(C.c_float), C.c_char_p, C.c_size_t]
+    H.ghost_draft_next.argtypes = [vp, i32, i32, C.POINTER(i32), C.POINTER(C.c_float), C.c_char_p, C.c_size_t]
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d = str(tmp_path / "mtp")
+    synth.write_pack(d, shape, seed=71, mtp=True)
+    err = C.create_string_buffer(512)
+    m = C.c_void_p()
+    assert H.ghost_open(d.encode(), 0, shape.ctx, 5, C.byref(m), err, 512) == 0, err.value
+    be = Backend(d, context=shape.ctx, max_tokens=5)
+    rng = np.random.default_rng(72)
+    try:
+        pos = 0
+        tok = int(rng.integers(0, shape.vocab))
+        for rep in range(3):
+            batch = np.array([tok] + [int(t) for t in rng.integers(0, shape.vocab, 4)], np.int32)
+            assert H.ghost_verify(m, batch.ctypes.data_as(vp), 5, None, err, 512) == 0, err.value
+            be.verify(batch, logits=False)
+            nxt = np.array(list(batch[1:]) + [int(rng.integers(0, shape.vocab))], np.int32)
+            dh, ph = i32(0), C.c_float(0.0)
+            assert H.ghost_draft(m, nxt.ctypes.data_as(vp), 5, pos, None, C.byref(dh), C.byref(ph), err, 512) == 0, \
+                err.value
+            dp, pp, _ = be.draft(nxt, pos)
+            assert (dh.value, np.float32(ph.value)) == (dp, np.float32(pp)), (rep, dh.value, dp, ph.value, pp)
+            q = pos + 5
+            assert H.ghost_draft_next(m, dh.value, q, C.byref(dh), C.byref(ph), err, 512) == 0, err.value
+            dp, pp, _ = be.draft_next(dp, q)
+            assert (dh.value, np.float32(ph.value)) == (dp, np.float32(pp))
+            pos += 5
+            tok = dh.value
+    finally:
+        H.ghost_close(m)
+        be.close()
+    plain = str(tmp_path / "plain")
+    synth.write_pack(plain, shape, seed=71)
+    assert H.ghost_open(plain.encode(), 0, shape.ctx, 5, C.byref(m), err, 512) == 0, err.value
+    try:
+        toks = np.array([1, 2], np.int32)
+        dh, ph = i32(0), C.c_float(0.0)
+        hid = np.zeros((2, shape.hidden), np.float32)
+        assert H.ghost_draft(m, toks.ctypes.data_as(vp), 2, 0, hid.ctypes.data_as(vp), C.byref(dh), C.byref(ph), err,
+                             512) != 0
+        assert b"MTP" in err.value
+    finally:
+        H.ghost_close(m)
