@@ -18,6 +18,7 @@
 #include "accept.cuh"
 #include "noalloc_impl.cuh"
 #include "ep_exchange.cuh"
+#include "experts_lane.cuh"
 
 using namespace gcu;
 
@@ -36,6 +37,7 @@ struct DevTensor {
 struct DevExperts {
     uint8_t *d = nullptr;
     bool tiled = false;   // already in the GEMV's tile layout (synthesized on the device)
+    bool r16 = false;     // in the expert kernels' R16 layout (experts_lane.cuh)
     int n = 0;
     size_t stride = 0;
     float *scales = nullptr;   // device [n][2]
@@ -163,6 +165,7 @@ struct gcuda {
     void *xbuf = nullptr;               // this rank's exchange buffer: flags [n_layers][world] (padded), then eout
     uint32_t *xflags = nullptr;
     size_t eout_stride = 0;             // expert parallelism: floats of one layer's slot of eout (a slot per layer)
+    size_t lane_avail = 0;              // the expert kernels' dynamic shared memory (set_attrs)
     int *ep_epoch = nullptr;            // (device) the step's epoch, one per step
     unsigned int *xcount = nullptr;     // (device) the exchange kernel's arrival counter
     void *peer_base[kMaxEpWorld] = {};  // the peers' exchange buffers, mapped here
@@ -529,48 +532,46 @@ int enqueue_layer(gcuda *g, int n, int l, const gcuda_layer &L, const LayerPlan 
         const DevExperts &X = g->experts[static_cast<size_t>(L.experts)];
         const DevTensor *sg = tensor(g, L.sh_gate, kQ4Tiled), *su = tensor(g, L.sh_up, kQ4Tiled),
                         *sd = tensor(g, L.sh_down, kQ4Tiled);
-        ExpertsArgs ea{};
-        ea.route = g->route;
-        ea.experts = X.d;
-        ea.stride = X.stride;
-        ea.scales = X.scales;
-        ea.sh_gate = static_cast<const uint8_t *>(sg->d);
-        ea.sh_up = static_cast<const uint8_t *>(su->d);
-        ea.sh_down = static_cast<const uint8_t *>(sd->d);
-        ea.sh_g0 = sg->global;
-        ea.sh_g1 = su->global;
-        ea.sh_g2 = sd->global;
-        ea.H = H;
-        ea.ff = s.moe_ff;
-        ea.sff = s.shared_ff;
-        ea.K = s.top_k;
-        ea.n = n;
-        ea.hq = g->hq.set();
-        ea.amid = g->amid.set();
-        ea.shact = g->shact.set();
-        ea.eout = eout_of(g, l);
-        ea.shout = g->shout;
-        ea.status = g->d_status;
-        for (int pass : {static_cast<int>(kGateUp), static_cast<int>(kDown)}) {
-            GemvShape r;
-            if (!plan_experts(pass, H, s.moe_ff, s.shared_ff, s.n_experts, s.top_k, n, sm_count(), r)) return GCUDA_E_ARG;
-            ea.pass = pass;
-            ea.wpu = r.wpu;
-            ea.nslots = r.nslots;
-            ea.blocked = r.blocked;
-            const int kind = pass == static_cast<int>(kGateUp) ? kKtGateUp : kKtDown;
-            if (!kt_mark(g, kind, true)) return GCUDA_E_CUDA;
-            if (r.stages == kPairStages)
-                LAUNCH_OK(launch_ex(k_gemv_experts<kPairStages>, dim3(sm_count()), dim3(2 * r.nslots * 32), r.smem, g->st, pdl, ea));
-            else if (r.stages == kWideStages)
-                LAUNCH_OK(launch_ex(k_gemv_experts<kWideStages>, dim3(sm_count()),
-                                    dim3((r.blocked ? r.nslots : kStreamWarps) * 32), r.smem, g->st, pdl, ea));
-            else if (r.stages == kDeepStages)
-                LAUNCH_OK(launch_ex(k_gemv_experts<kDeepStages>, dim3(sm_count()), dim3(kDeepWarps * 32), r.smem, g->st, pdl, ea));
-            else
-                LAUNCH_OK(launch_ex(k_gemv_experts<0>, dim3(sm_count()), dim3(kFanThreads), r.smem, g->st, pdl, ea));
-            if (!kt_mark(g, kind, false)) return GCUDA_E_CUDA;
-        }
+        // the union's routed experts and the shared expert, a lane a weight row (experts_lane.cuh)
+        LaneArgs la{};
+        la.route = g->route;
+        la.experts = X.d;
+        la.stride = X.stride;
+        la.down_off = static_cast<size_t>(2 * s.moe_ff / 16) * (H / 64) * kLaneTileGroup;
+        la.globals = X.scales;
+        la.sh_gate = static_cast<const uint8_t *>(sg->d);
+        la.sh_up = static_cast<const uint8_t *>(su->d);
+        la.sh_down = static_cast<const uint8_t *>(sd->d);
+        la.sh_g0 = sg->global;
+        la.sh_g1 = su->global;
+        la.sh_g2 = sd->global;
+        la.H = H;
+        la.ff = s.moe_ff;
+        la.K = s.top_k;
+        la.n = n;
+        la.hq = g->hq.set();
+        la.amid = g->amid.set();
+        la.shact = g->shact.set();
+        la.eout = eout_of(g, l);
+        la.shout = g->shout;
+        la.status = g->d_status;
+        const dim3 lgrid(sm_count()), lblock(kLaneWarps * 32);
+        const int su_ = lane_stages(true, n, s.top_k, H, g->lane_avail), sd_ = lane_stages(false, n, s.top_k, s.moe_ff, g->lane_avail);
+        if (su_ < 2 || sd_ < 2) return fail(g, GCUDA_E_ARG, "the expert kernels' activation rows leave no room for their rings");
+        if (!kt_mark(g, kKtGateUp, true)) return GCUDA_E_CUDA;
+        la.stages = su_;
+        const size_t smu = lane_smem_bytes(true, n, s.top_k, H, su_), smd = lane_smem_bytes(false, n, s.top_k, s.moe_ff, sd_);
+        if ((H / 64) % kLaneStageGroups == 0)
+            LAUNCH_OK(launch_ex(k_experts_lane<true, kLaneStageGroups>, lgrid, lblock, smu, g->st, pdl, la));
+        else
+            LAUNCH_OK(launch_ex(k_experts_lane<true, 1>, lgrid, lblock, smu, g->st, pdl, la));
+        if (!kt_mark(g, kKtGateUp, false) || !kt_mark(g, kKtDown, true)) return GCUDA_E_CUDA;
+        la.stages = sd_;
+        if ((s.moe_ff / 64) % kLaneStageGroups == 0)
+            LAUNCH_OK(launch_ex(k_experts_lane<false, kLaneStageGroups>, lgrid, lblock, smd, g->st, pdl, la));
+        else
+            LAUNCH_OK(launch_ex(k_experts_lane<false, 1>, lgrid, lblock, smd, g->st, pdl, la));
+        if (!kt_mark(g, kKtDown, false)) return GCUDA_E_CUDA;
         if (g->ep_world > 1) {
             // every pick's row from the rank that owns its expert, stored here by that rank over NVLink, so the
             // combine below runs on every rank in rank order as on one GPU
@@ -675,6 +676,17 @@ int set_attrs(gcuda *g) {
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<256>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<128>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<64>())));
+    // (the expert kernels hold the route in static shared memory: the rest of the CTA's limit is dynamic)
+    for (const void *fn : {reinterpret_cast<const void *>(k_experts_lane<true, kLaneStageGroups>),
+                           reinterpret_cast<const void *>(k_experts_lane<false, kLaneStageGroups>),
+                           reinterpret_cast<const void *>(k_experts_lane<true, 1>),
+                           reinterpret_cast<const void *>(k_experts_lane<false, 1>)}) {
+        cudaFuncAttributes fa{};
+        LAUNCH_OK(cudaFuncGetAttributes(&fa, fn));
+        const int avail = kMaxDynSmem - static_cast<int>(fa.sharedSizeBytes);
+        LAUNCH_OK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, avail));
+        g->lane_avail = static_cast<size_t>(avail);
+    }
     // (k_route: kMaxTok * E floats, 32 KB at E = 1024, within the default limit; its limit is left as it is, so that
     // no model lowers it under another caller's needs - attributes last for the process)
     (void)s;
@@ -1011,20 +1023,59 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
         const size_t want = static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9 + static_cast<size_t>(H) * (s.moe_ff / 16) * 9;
         for (auto &X : g->experts) {
             if (X.stride != want) return fail(g, GCUDA_E_ARG, "setup: an expert block of unexpected size");
-            if (X.tiled) continue;
+            if (X.r16) continue;
             uint8_t *tmp = nullptr;
             cudaError_t e = cudaMalloc(&tmp, X.stride);
             if (e != cudaSuccess) return cuda_fail(g, e, "setup cudaMalloc");
             const size_t gu_tiled = gcuda_op_q4_tiled_bytes(2 * s.moe_ff, H);
             for (int i = 0; i < X.n; ++i) {
                 uint8_t *blk = X.d + static_cast<size_t>(i) * X.stride;
+                if (!X.tiled) {   // the pack's rows -> tiles
+                    cudaMemcpyAsync(tmp, blk, X.stride, cudaMemcpyDeviceToDevice, g->st);
+                    gcuda_op_q4_relayout(tmp, 2 * s.moe_ff, H, blk, g->st);
+                    gcuda_op_q4_relayout(tmp + static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9, H, s.moe_ff, blk + gu_tiled,
+                                         g->st);
+                }
+                // tiles -> R16, the layout the expert kernels read
                 cudaMemcpyAsync(tmp, blk, X.stride, cudaMemcpyDeviceToDevice, g->st);
-                gcuda_op_q4_relayout(tmp, 2 * s.moe_ff, H, blk, g->st);
-                gcuda_op_q4_relayout(tmp + static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9, H, s.moe_ff, blk + gu_tiled, g->st);
+                k_relayout_r16<<<relayout_grid(2 * s.moe_ff / 16 * (H / 64) * 16), 256, 0, g->st>>>(tmp, 2 * s.moe_ff / 16, H, blk);
+                k_relayout_r16<<<relayout_grid(H / 16 * (s.moe_ff / 64) * 16), 256, 0, g->st>>>(tmp + gu_tiled, H / 16, s.moe_ff,
+                                                                                         blk + gu_tiled);
             }
             e = cudaStreamSynchronize(g->st);
             cudaFree(tmp);
             if (e != cudaSuccess) return cuda_fail(g, e, "setup relayout experts");
+            X.tiled = X.r16 = true;
+        }
+        if (s.shared_ff != s.moe_ff)
+            return fail(g, GCUDA_E_ARG, "setup: the shared expert's width must equal the routed experts'");
+        // the shared experts' matrices (read only by the expert kernels in a MoE model) to R16 too, each tensor once
+        std::vector<char> done(g->tensors.size(), 0);
+        auto to_r16 = [&](int id) -> int {
+            const DevTensor *t = tensor(g, id, kQ4Tiled);
+            if (!t || done[static_cast<size_t>(id)]) return GCUDA_OK;
+            done[static_cast<size_t>(id)] = 1;
+            if (t->rows % 16 || t->cols % 64) return fail(g, GCUDA_E_ARG, "setup: a shared expert matrix's shape");
+            uint8_t *tmp = nullptr;
+            cudaError_t e = cudaMalloc(&tmp, t->bytes);
+            if (e != cudaSuccess) return cuda_fail(g, e, "setup cudaMalloc");
+            cudaMemcpyAsync(tmp, t->d, t->bytes, cudaMemcpyDeviceToDevice, g->st);
+            const int64_t tiles = t->rows / 16;
+            k_relayout_r16<<<relayout_grid(tiles * (t->cols / 64) * 16), 256, 0, g->st>>>(
+                tmp, tiles, static_cast<int>(t->cols), static_cast<uint8_t *>(t->d));
+            e = cudaStreamSynchronize(g->st);
+            cudaFree(tmp);
+            return e == cudaSuccess ? GCUDA_OK : cuda_fail(g, e, "setup relayout the shared expert");
+        };
+        for (const gcuda_layer &L : g->layers) {
+            RC_OK(to_r16(L.sh_gate));
+            RC_OK(to_r16(L.sh_up));
+            RC_OK(to_r16(L.sh_down));
+        }
+        if (g->has_mtp) {
+            RC_OK(to_r16(g->mtp_layer.sh_gate));
+            RC_OK(to_r16(g->mtp_layer.sh_up));
+            RC_OK(to_r16(g->mtp_layer.sh_down));
         }
     }
     // state
