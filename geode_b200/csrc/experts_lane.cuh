@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
             tB = kUp ? a.sh_up + j * tb : tA + tb;
             return;
         }
-        const uint8_t *base = a.experts + static_cast<size_t>(global ? R.ex[R.own[m]] : lr.e[m]) * a.stride;
+        const uint8_t *base = a.experts + static_cast<size_t>(global ? R.own_ex[m] : lr.e[m]) * a.stride;
         tA = kUp ? base + j * tb : base + a.down_off + 2 * j * tb;
         tB = kUp ? base + (a.ff / 16 + j) * tb : tA + tb;
     };

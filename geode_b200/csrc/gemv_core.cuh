@@ -430,124 +430,6 @@ __device__ void stream_units(const GetUnit &get, const StreamCtx &c, const Resta
     cp_async_wait<0>();   // (no copy in flight when the warp leaves: the stages are released with the CTA)
 }
 
-// ------------------------------------------------------------------------------------------- warp pairs ----
-// The streaming path for launches with fewer units than warps: the two warps of a pair each take ONE tile of the
-// same two-tile unit (tsel 0: tile A, 1: tile B) through a ring of kPairStages one-tile groups (576 bytes), four groups
-// per iteration (the copies, waits and decodes per byte as stream_units'); at the unit's end the B warp hands its
-// sums to the A warp through xchg (two buffers of 32 lanes) at the pair's named barrier (bar_id, 64 threads) for the
-// epilogue (a swiglu needs both tiles). Needs G % 4 == 0.
-constexpr int kPairStages = 8;
-constexpr int kPairWarps = 24;
-// per warp: 2 KB of scale pairs (four groups), the ring
-__host__ __device__ inline int pair_warp_bytes() { return 2048 + kPairStages * kGroupBytes; }
-
-template <typename GetUnit, typename Epi, typename Prelude>
-__device__ void stream_pairs(const GetUnit &get, const StreamCtx &c, const Epi &epi, const Prelude &prelude, int tsel,
-                             float4 *xchg, int bar_id) {
-    constexpr int S = kPairStages;
-    static_assert(S % 4 == 0, "stages in fours");
-    const int lane = threadIdx.x & 31, gid = lane >> 2, tig = lane & 3;
-    const int G = c.ngroups;
-    // producer: lane l copies code bytes 16 l .. 16 l + 15 of each group, lanes < 4 also 16 scale bytes (512 + 16 l);
-    // one copy group committed per four groups
-    const uint32_t ring_s = smem_addr(c.ring) + lane * 16;
-    uint32_t pdst = ring_s;
-    int pu = 0, pg = 0;
-    const uint8_t *s0 = nullptr;
-    bool p_ok;
-    auto unit_src = [&](int i) {
-        GemvUnit T;
-        p_ok = get(i, T);
-        if (p_ok) s0 = (tsel ? T.w1 : T.w0) + lane * 16;
-    };
-    auto issue4 = [&]() {
-        if (p_ok) {
-            cp_async16(pdst, s0);
-            cp_async16_off<kGroupBytes, kGroupBytes>(pdst, s0);
-            cp_async16_off<2 * kGroupBytes, 2 * kGroupBytes>(pdst, s0);
-            cp_async16_off<3 * kGroupBytes, 3 * kGroupBytes>(pdst, s0);
-            if (lane < 4) {
-                cp_async16_off<512, 512>(pdst, s0);
-                cp_async16_off<kGroupBytes + 512, kGroupBytes + 512>(pdst, s0);
-                cp_async16_off<2 * kGroupBytes + 512, 2 * kGroupBytes + 512>(pdst, s0);
-                cp_async16_off<3 * kGroupBytes + 512, 3 * kGroupBytes + 512>(pdst, s0);
-            }
-            s0 += 4 * kGroupBytes;
-            pg += 4;
-            if (pg == G) {
-                pg = 0;
-                unit_src(++pu);
-            }
-        }
-        cp_async_commit();
-        pdst += 4 * kGroupBytes;
-        if (pdst == ring_s + S * kGroupBytes) pdst = ring_s;
-    };
-    // (get() reads the previous kernel's output: after prelude())
-    prelude();
-    unit_src(0);
-#pragma unroll
-    for (int k = 0; k < S / 4; ++k) issue4();
-    int cu = 0, cg = 0, buf = 0;
-    const uint8_t *st = c.ring;
-    bool c_ok;
-    {
-        GemvUnit U;
-        c_ok = get(0, U);
-    }
-    uint64_t acc[2] = {0, 0};
-    auto chain = [&](int, const uint64_t (&p)[4]) {
-        acc[0] = f2_add(acc[0], p[0]);
-        acc[1] = f2_add(acc[1], p[1]);
-    };
-    const uint8_t *act0 = c.img + gid * c.img_ts + tig * 16;
-    const uint8_t *cs0 = c.img + kMaxTok * c.img_ts + tig * kCsEntry;
-    const uint8_t *ring_end = c.ring + S * kGroupBytes;
-    const int sc_off = (lane >> 4) * kGroupBytes + 512 + 4 * (lane & 15);
-    while (c_ok) {
-        // groups i .. i + 3 (one copy group): S / 4 - 1 copy groups after theirs may still fly
-        cp_async_wait<S / 4 - 1>();
-        __syncwarp();
-        // two decodes serve the four groups: lanes < 16 groups i, i + 2, lanes >= 16 groups i + 1, i + 3
-        decode_scales(*reinterpret_cast<const uint32_t *>(st + sc_off), lane, c.e4p);
-        decode_scales(*reinterpret_cast<const uint32_t *>(st + 2 * kGroupBytes + sc_off), lane, c.e4p + 256);
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-            group_products<true>(ld_shared_v4(st + k * kGroupBytes + lane * 16), make_uint4(0, 0, 0, 0), c.e4p + 128 * k,
-                                 act0 + (cg + k) * 64, cs0 + (cg + k) * 4 * kCsEntry, lane, c.zero, chain);
-        __syncwarp();   // every lane done with the stages and the scale pairs before they are refilled
-        issue4();
-        st += 4 * kGroupBytes;
-        if (st == ring_end) st = c.ring;
-        cg += 4;
-        if (cg == G) {
-            // y = acc * global * 1 (engine/src/kernels.cpp:1320): global / 8 on the 8-fold chain
-            GemvUnit U;
-            get(cu, U);
-            const float gl = __fmul_rn(tsel ? U.g1 : U.g0, 0.125f);
-            float y[4] = {lo_f(acc[0]), hi_f(acc[0]), lo_f(acc[1]), hi_f(acc[1])};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) y[i] = __fmul_rn(y[i], gl);
-            float4 *xb = xchg + buf * 32 + lane;
-            if (tsel) {
-                *xb = make_float4(y[0], y[1], y[2], y[3]);
-                bar_sync_n(bar_id, 64);
-            } else {
-                bar_sync_n(bar_id, 64);
-                const float4 o = *xb;
-                const float y1[4] = {o.x, o.y, o.z, o.w};
-                epi(U, y, y1, gid, tig);
-            }
-            buf ^= 1;   // (the next unit's sums go to the other buffer: the barrier above orders its reuse)
-            acc[0] = acc[1] = 0;
-            cg = 0;
-            c_ok = get(++cu, U);
-        }
-    }
-    cp_async_wait<0>();   // (no copy in flight when the warp leaves)
-}
-
 // ------------------------------------------------------------------------------------------- fan-in ----
 // The path for launches with few units (latency-bound): the whole CTA works on one unit at a time. kFanProducers
 // warps each take one group of a chunk (kFanProducers consecutive groups), multiply it and leave its products in a

@@ -255,288 +255,4 @@ __global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) 
 
 namespace gcu {
 
-// ------------------------------------------------------------------------------------------- the expert GEMVs ----
-// The MoE's routed experts over the union the router picked (engine/src/model.cpp:4496-4543), with the shared expert
-// as one more entry. Units are made on the device from the RouteOut:
-//   kGateUp: per union expert, ff/16 units (gate tile i with up tile i), the shared expert's sff/16 after them;
-//            silu(g) * u quantized into the pick's row of amid (slot t * K + k), or the token's row of shact.
-//            Every unit multiplies h (hq, staged once per CTA).
-//   kDown:   per union expert, hidden/32 units (two down tiles), output rows of eout at the pick's slot; the shared
-//            expert's down units after them into shout. A warp restages its activation image when its expert
-//            changes (the picks' amid rows, or shact).
-// Warps take contiguous ranges of units (so a warp restages rarely).
-enum ExpertPass : int { kGateUp = 0, kDown = 1 };
-
-struct ExpertsArgs {
-    int pass;
-    const RouteOut *route;
-    const uint8_t *experts;     // this layer's tiled expert blocks, expert e at experts + e * stride
-    size_t stride;
-    const float *scales;        // [E][2]
-    const uint8_t *sh_gate, *sh_up, *sh_down;   // the shared expert's tiled matrices
-    float sh_g0, sh_g1, sh_g2;
-    int H, ff, sff, K, n;
-    ActSet hq, amid, shact;     // amid: [n*K][ff], shact: [n][sff]
-    float *eout, *shout;        // [n*K][H], [n][H]
-    int wpu, nslots;            // the launch shape (plan_experts)
-    int blocked;                // down: CTA c takes units [c B, (c + 1) B), B = ceil(units / grid), a warp each
-    uint32_t *status;
-};
-
-// gate_up: the CTA's image of h in front of the warps; down: every warp its own image (the units' activations differ).
-// units: the expected count (the union is known on the device only): n*K picks at most, E experts at most.
-inline bool plan_experts(int pass, int H, int ff, int sff, int E, int K, int n, int sms, GemvShape &r) {
-    const int picks = n * K < E ? n * K : E;
-    if (pass == kGateUp) {
-        // fewer units than a CTA's warps: warp pairs (stream_pairs), each warp one tile of a unit
-        const int pu = picks * (ff / 16) + sff / 16, per_cta = (pu + sms - 1) / sms;
-        if ((H / 64) % 4 == 0 && per_cta >= kStreamMinUnits && per_cta < kDeepWarps)
-            for (int pairs = kPairWarps / 2; pairs >= 4; --pairs) {
-                const size_t smem = static_cast<size_t>(act_smem_bytes(H)) + pairs * 1024 + 2 * pairs * pair_warp_bytes();
-                if (smem <= static_cast<size_t>(kMaxDynSmem)) {
-                    r = GemvShape{2, pairs, H / 64, smem, kPairStages};
-                    return true;
-                }
-            }
-        const int units = picks * (ff / 16) + sff / 16;
-        return plan_gemv(H, H, false, static_cast<size_t>(act_smem_bytes(H)), (units + sms - 1) / sms, r);
-    }
-    const int units = (picks + 1) * (H / 32);
-    // blocked: every CTA's block of consecutive units (at most two experts' worth: B <= H / 32) on one warp each, the
-    // experts' activation images staged once for the CTA - when the worst-case block fits the warps
-    {
-        const int B = (units + sms - 1) / sms, G = ff / 64;
-        const size_t imgs = 2 * static_cast<size_t>(act_smem_bytes(ff));
-        if (G % 2 == 0 && B <= H / 32)
-            for (int w = kStreamWarps; w >= B && w >= 1; --w) {
-                const size_t smem = static_cast<size_t>(w) * stream_warp_bytes(kWideStages, 0) + imgs;
-                if (smem <= static_cast<size_t>(kMaxDynSmem)) {
-                    r = GemvShape{1, w, G, smem, kWideStages, 1};
-                    return true;
-                }
-            }
-    }
-    return plan_gemv(ff, ff, true, 0, (units + sms - 1) / sms, r);
-}
-
-template <int kStages>
-__global__ void __launch_bounds__((kStages ? stream_warps(kStages) : kFanWarps) * 32, 1) k_gemv_experts(ExpertsArgs p) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5;
-    const bool gu = p.pass == kGateUp;
-    // gate_up multiplies hidden-wide h; down multiplies ff-wide (sff for the shared expert) activations
-    const int cols = gu ? p.H : p.ff;
-    const int wpu = p.wpu, sg = (cols / 64) / wpu, nslots = p.nslots;
-    if (!gu && p.sff != p.ff) {
-        // (one K for the whole pass: the shared expert's width must match the routed experts')
-        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(p.status, kErrBadShape);
-    }
-    uint8_t *img = gu ? smem : nullptr;
-    auto prelude = [&]() {
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        asm volatile("griddepcontrol.launch_dependents;");
-        if (gu) {
-            stage_full(p.hq, p.n, img);
-            __syncthreads();
-        }
-    };
-    if (warp >= nslots * wpu) {
-        if (gu) prelude();
-        else asm volatile("griddepcontrol.wait;" ::: "memory");
-        return;
-    }
-    const int slot = warp / wpu;
-    const RouteOut &R = *p.route;
-    int nu = 0, per_ex = 0, total = 0, u0 = 0, u1 = 0;
-    const int all = (1 << p.n) - 1;
-    const size_t tbH = static_cast<size_t>(tile_bytes(p.H)), tbF = static_cast<size_t>(tile_bytes(p.ff)),
-                 tbS = static_cast<size_t>(tile_bytes(p.sff));
-    bool ranged = false;
-    const bool blocked = !gu && p.blocked;
-    int ustep = 1, blk0 = 0, blk1 = 0;   // (blocked: the CTA's units [blk0, blk1))
-    auto range = [&]() {
-        // (read after the dependent-launch wait: the route is the previous kernel's output)
-        nu = R.n_own;   // (this rank's members of the union: all of it on one GPU)
-        per_ex = gu ? p.ff / 16 : p.H / 32;
-        const int sh_units = gu ? p.sff / 16 : p.H / 32;
-        total = nu * per_ex + sh_units;
-        if (blocked) {
-            const int B = (total + gridDim.x - 1) / gridDim.x;
-            blk0 = min(total, blockIdx.x * B);
-            blk1 = min(total, blk0 + B);
-            u0 = blk0 + slot;
-            u1 = blk1;
-            ustep = nslots;
-            ranged = true;
-            return;
-        }
-        // ranges CTA-major (range r on CTA r % grid): a launch with fewer ranges than slots still spreads over every SM
-        const int nslots_all = gridDim.x * nslots, gs = blockIdx.x + gridDim.x * slot;
-        const int per = (total + nslots_all - 1) / nslots_all;
-        u0 = gs * per;
-        u1 = min(total, u0 + per);
-        ranged = true;
-    };
-    auto get = [&](int i, GemvUnit &U) -> bool {
-        if (!ranged) range();
-        const int u = u0 + i * ustep;
-        if (u >= u1) return false;
-        const int s = u / per_ex;
-        const bool shared = s >= nu;
-        const int j = shared ? u - nu * per_ex : u % per_ex;
-        const int su = shared ? 0 : R.own[s];   // the member's index in the union
-        const int e = shared ? 0 : R.ex[su];
-        for (int t = 0; t < kMaxTok; ++t) U.slot[t] = shared ? t : R.slot[su][t];
-        U.tok_mask = shared ? all : R.mask[su];
-        U.act_id = shared ? -1 : s;
-        if (gu) {
-            if (shared) {
-                U.w0 = p.sh_gate + j * tbH;
-                U.w1 = p.sh_up + j * tbH;
-                U.g0 = p.sh_g0;
-                U.g1 = p.sh_g1;
-                U.aq = const_cast<int8_t *>(p.shact.q);
-                U.as = const_cast<float *>(p.shact.scale);
-                U.ab = const_cast<int32_t *>(p.shact.bsum);
-                U.acols = p.sff;
-            } else {
-                const uint8_t *base = p.experts + static_cast<size_t>(e) * p.stride;
-                U.w0 = base + j * tbH;
-                U.w1 = base + (p.ff / 16 + j) * tbH;
-                U.g0 = U.g1 = p.scales[2 * e];
-                U.aq = const_cast<int8_t *>(p.amid.q);
-                U.as = const_cast<float *>(p.amid.scale);
-                U.ab = const_cast<int32_t *>(p.amid.bsum);
-                U.acols = p.ff;
-            }
-            U.arow0 = 16 * j;
-            U.ngroups = p.H / 64;
-            U.mode = kSwiglu;
-            U.act_id = 0;   // every gate_up unit multiplies h
-        } else {
-            if (shared) {
-                U.w0 = p.sh_down + (2 * j) * tbS;
-                U.w1 = U.w0 + tbS;
-                U.g0 = U.g1 = p.sh_g2;
-                U.y0 = p.shout + 32 * j;
-                U.ngroups = p.sff / 64;
-            } else {
-                const uint8_t *base = p.experts + static_cast<size_t>(e) * p.stride + (2 * p.ff / 16) * tbH;
-                U.w0 = base + (2 * j) * tbF;
-                U.w1 = U.w0 + tbF;
-                U.g0 = U.g1 = p.scales[2 * e + 1];
-                U.y0 = p.eout + 32 * j;
-                U.ngroups = p.ff / 64;
-            }
-            U.y1 = U.y0 + 16;
-            U.ystride = p.H;
-            U.mode = kStore;
-        }
-        return true;
-    };
-    int staged = -2, part = 0;
-    uint8_t *own = nullptr;   // the warp's own image (down)
-    auto restage = [&](const GemvUnit &U) {
-        if (gu || U.act_id == staged) return;   // (gate_up: the CTA's image of h, staged in the prelude)
-        __syncwarp();
-        int sel[kMaxTok];
-        for (int t = 0; t < kMaxTok; ++t) sel[t] = t < p.n && ((U.tok_mask >> t) & 1) ? U.slot[t] : -1;
-        stage_slice(U.act_id < 0 ? p.shact : p.amid, sel, part * sg, sg, own);
-        __syncwarp();
-        staged = U.act_id;
-    };
-    auto epi = [](const GemvUnit &U, const float(&y0)[4], const float(&y1)[4], int gid, int tig) {
-        epi_store(U, y0, y1, gid, tig);
-    };
-    if constexpr (kStages == kPairStages) {
-        // gate_up on warp pairs: the image of h, the pairs' exchange buffers (two of 32 float4), per warp the scale
-        // pairs and the ring
-        const size_t front = static_cast<size_t>(act_smem_bytes(p.H)) + static_cast<size_t>(nslots) * 1024;
-        uint8_t *wbase = smem + front + static_cast<size_t>(warp) * pair_warp_bytes();
-        StreamCtx c;
-        c.e4p = reinterpret_cast<float *>(wbase);
-        c.ring = wbase + 2048;
-        c.img = img;
-        c.img_ts = act_tstride(p.H);
-        c.ngroups = cols / 64;
-        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
-        float4 *xchg = reinterpret_cast<float4 *>(smem + act_smem_bytes(p.H)) + slot * 64;
-        if (gu) stream_pairs(get, c, epi, prelude, warp & 1, xchg, 1 + slot);
-    } else if constexpr (kStages > 0) {
-      if (blocked) {
-        // down, blocked: per warp 2 KB of scale pairs and the ring; then two images - the block's first expert and the
-        // next (a block spans two at most). The weights' first copies go out before the images are staged.
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        asm volatile("griddepcontrol.launch_dependents;");
-        range();
-        const size_t swb = static_cast<size_t>(stream_warp_bytes(kStages, 0));
-        uint8_t *wbase = smem + static_cast<size_t>(warp) * swb;
-        uint8_t *imgs = smem + static_cast<size_t>(nslots) * swb;
-        const int ib = act_smem_bytes(p.ff), its = act_tstride(p.ff);
-        const int s_first = blk0 / max(per_ex, 1);
-        StreamCtx c;
-        c.e4p = reinterpret_cast<float *>(wbase);
-        c.ring = wbase + 2048;
-        c.img = imgs + (u0 < u1 ? (u0 / per_ex - s_first) : 0) * ib;
-        c.img_ts = its;
-        c.ngroups = cols / 64;
-        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
-        auto stage_block = [&]() {
-            // half the threads stage the first expert's image, half the second's (if the block reaches it)
-            const int half = blockDim.x / 2, k = threadIdx.x >= half ? 1 : 0;
-            const int s = s_first + k;
-            if (blk0 < blk1 && s * per_ex < blk1) {
-                const bool shared = s >= nu;
-                const int su = shared ? 0 : R.own[s];
-                const int mask = shared ? (1 << p.n) - 1 : R.mask[su];
-                int rows[kMaxTok];
-                for (int t = 0; t < kMaxTok; ++t) rows[t] = t < p.n && ((mask >> t) & 1) ? (shared ? t : R.slot[su][t]) : -1;
-                stage_image(shared ? p.shact : p.amid, [&](int t) { return rows[t]; }, 0, cols / 64, its, imgs + k * ib,
-                            threadIdx.x - k * half, half);
-            }
-            __syncthreads();
-        };
-        stream_units<kStages>(get, c, [](const GemvUnit &) {}, epi, true, stage_block);
-      } else {
-        // per warp: 2 KB of scale pairs, the ring, then (down) the warp's own image of all K
-        uint8_t *wbase = smem + (gu ? act_smem_bytes(p.H) : 0) + static_cast<size_t>(warp) * stream_warp_bytes(kStages, gu ? 0 : sg);
-        uint8_t *own_img = wbase + 2048 + kStages * kStageBytesR;
-        StreamCtx c;
-        c.e4p = reinterpret_cast<float *>(wbase);
-        c.ring = wbase + 2048;
-        c.img = gu ? img : own_img;
-        c.img_ts = gu ? act_tstride(p.H) : slice_tstride(sg);
-        c.ngroups = cols / 64;
-        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(wpu) >> 31);
-        own = gu ? nullptr : own_img;
-        stream_units<kStages>(get, c, restage, epi, false, prelude);
-      }
-    } else {
-        // one image for the CTA: h (gate_up, staged in the prelude), or the unit's picks' rows (down, restaged by the
-        // producers when the expert changes)
-        uint8_t *fimg = smem;
-        FanCtx c;
-        c.img = fimg;
-        c.img_ts = gu ? act_tstride(p.H) : act_tstride(p.ff);
-        c.prod = smem + act_smem_bytes(cols);
-        c.e4p = reinterpret_cast<float *>(c.prod + 2 * kFanSlotBytes);
-        c.xchg = reinterpret_cast<float4 *>(c.prod + 2 * kFanSlotBytes + kFanProducers * 1024);
-        c.ngroups = cols / 64;
-        c.zero = static_cast<uint64_t>(static_cast<uint32_t>(nslots) >> 31);
-        c.half = false;
-        int fan_staged = -2;
-        auto changes = [&](const GemvUnit &U) {
-            if (gu || U.act_id == fan_staged) return false;
-            fan_staged = U.act_id;
-            return true;
-        };
-        auto fan_restage = [&](const GemvUnit &U, int me, int nthr) {
-            stage_image(U.act_id < 0 ? p.shact : p.amid,
-                        [&](int t) { return t < p.n && ((U.tok_mask >> t) & 1) ? static_cast<int>(U.slot[t]) : -1; }, 0,
-                        cols / 64, act_tstride(cols), fimg, me, nthr);
-        };
-        fan_units(get, c, changes, fan_restage, epi, false, prelude);
-    }
-}
-
 }  // namespace gcu

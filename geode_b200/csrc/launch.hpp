@@ -110,11 +110,7 @@ inline int gemv_opt_in() {
         const bool ok = cudaFuncSetAttribute(k_gemv_static<0>, a, kMaxDynSmem) == cudaSuccess &&
                         cudaFuncSetAttribute(k_gemv_static<kWideStages>, a, kMaxDynSmem) == cudaSuccess &&
                         cudaFuncSetAttribute(k_gemv_static<kDeepStages>, a, kMaxDynSmem) == cudaSuccess &&
-                        cudaFuncSetAttribute(k_gemv_static<kSplitStages>, a, kMaxDynSmem) == cudaSuccess &&
-                        cudaFuncSetAttribute(k_gemv_experts<0>, a, kMaxDynSmem) == cudaSuccess &&
-                        cudaFuncSetAttribute(k_gemv_experts<kWideStages>, a, kMaxDynSmem) == cudaSuccess &&
-                        cudaFuncSetAttribute(k_gemv_experts<kDeepStages>, a, kMaxDynSmem) == cudaSuccess &&
-                        cudaFuncSetAttribute(k_gemv_experts<kPairStages>, a, kMaxDynSmem) == cudaSuccess;
+                        cudaFuncSetAttribute(k_gemv_static<kSplitStages>, a, kMaxDynSmem) == cudaSuccess;
         d.gemv_rc[dev] = ok ? static_cast<int>(GCUDA_OK) : static_cast<int>(GCUDA_E_CUDA);
     }
     return d.gemv_rc[dev];

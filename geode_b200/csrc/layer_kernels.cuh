@@ -895,6 +895,7 @@ struct RouteOut {
     // ascending order; n_own == n_union and own[u] == u on one GPU
     int n_own;
     int own[kMaxUnion];
+    int own_ex[kMaxUnion];   // ex[own[m]]: the expert of this rank's m-th member (one load for the expert kernels)
 };
 
 __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict__ logits, int n, int E, int K,
@@ -1038,7 +1039,10 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float *__restrict
             const int u = u0 + lane;
             const bool mine = u < nu && s_ex[u] % ep_world == ep_rank;
             const uint32_t bal = __ballot_sync(0xffffffffu, mine);
-            if (mine) out->own[base + __popc(bal & ((1u << lane) - 1u))] = u;
+            if (mine) {
+                out->own[base + __popc(bal & ((1u << lane) - 1u))] = u;
+                out->own_ex[base + __popc(bal & ((1u << lane) - 1u))] = s_ex[u];
+            }
             base += __popc(bal);
         }
         if (lane == 0) {
