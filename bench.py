@@ -312,7 +312,7 @@ def gemv_roofline(L, peak_gbs, reps: int = 20) -> dict:
 
 KT_NAMES = ["gate_up", "down", "lm_head", "dense"]
 # ncu figures of the dominant kernel, per launch (the capture's command and numbers: this file)
-GATEUP_PROFILE = os.path.join(ROOT, "profiles", "k_gemv_experts_gateup_cfg3.md")
+GATEUP_PROFILE = os.path.join(ROOT, "profiles", "k_experts_lane_gateup_cfg3.md")
 
 
 def profiled_traffic(path: str, blocks: float):
@@ -691,8 +691,8 @@ def main():
     lm_op = gemv_roofline(cuda_lib(), peak)
     kr = kernel_rooflines(be, shape, toks, peak)
     gu = kr["gate_up"]
-    roof = {"kernel": "k_gemv_experts gate_up (the union's routed experts + the shared expert, SwiGLU + quantize "
-                      "epilogue): the step's largest kernel by device time", "bound": "hbm",
+    roof = {"kernel": "k_experts_lane gate_up (the union's routed experts + the shared expert, a lane a weight row, "
+                      "SwiGLU + quantize epilogue): the step's largest kernel by device time", "bound": "hbm",
             "achieved": gu.get("achieved_gbs"), "peak": peak, "unit": "GB/s", "frac": gu.get("frac"),
             "traffic": profiled_traffic(GATEUP_PROFILE, kr["union_per_layer"] + 1), "ms": gu.get("ms_per_launch"),
             "algorithmic_bytes": gu.get("algorithmic_bytes_per_launch"), "launches_per_step": gu["launches_per_step"],
