@@ -159,7 +159,7 @@ struct gcuda {
     uint64_t reject_steps = 0;      // (its Philox sequence index: one per step)
     std::vector<void *> allocs;
     // expert parallelism (gcuda_set_ep): this rank's experts are e % ep_world == ep_rank; the expert outputs meet
-    // through k_ep_exchange (peer stores over NVLink and per-layer flags); NCCL only carries the set-up's handles
+    // through the down kernel's peer stores over NVLink and per-layer flags; NCCL only carries the set-up's handles
     int ep_rank = 0, ep_world = 1;
     ncclComm_t comm = nullptr;
     void *xbuf = nullptr;               // this rank's exchange buffer: flags [n_layers][world] (padded), then eout
@@ -555,6 +555,7 @@ int enqueue_layer(gcuda *g, int n, int l, const gcuda_layer &L, const LayerPlan 
         la.eout = eout_of(g, l);
         la.shout = g->shout;
         la.status = g->d_status;
+        la.world = 1;
         const dim3 lgrid(sm_count()), lblock(kLaneWarps * 32);
         const int su_ = lane_stages(true, n, s.top_k, H, g->lane_avail), sd_ = lane_stages(false, n, s.top_k, s.moe_ff, g->lane_avail);
         if (su_ < 2 || sd_ < 2) return fail(g, GCUDA_E_ARG, "the expert kernels' activation rows leave no room for their rings");
@@ -567,33 +568,23 @@ int enqueue_layer(gcuda *g, int n, int l, const gcuda_layer &L, const LayerPlan 
             LAUNCH_OK(launch_ex(k_experts_lane<true, 1>, lgrid, lblock, smu, g->st, pdl, la));
         if (!kt_mark(g, kKtGateUp, false) || !kt_mark(g, kKtDown, true)) return GCUDA_E_CUDA;
         la.stages = sd_;
+        if (g->ep_world > 1) {
+            // the down kernel stores every owned pick's row into the peers' slots too and meets them at the layer's flags
+            la.rank = g->ep_rank;
+            la.world = g->ep_world;
+            la.layer = l;
+            for (int r = 0; r < kMaxEpWorld; ++r)
+                la.peer_eout[r] = g->peer_eout[r] ? g->peer_eout[r] + static_cast<size_t>(l) * g->eout_stride : nullptr;
+            la.flags = g->xflags;
+            for (int r = 0; r < kMaxEpWorld; ++r) la.peer_flags[r] = g->peer_flags[r];
+            la.epoch = g->ep_epoch;
+            la.count = g->xcount;
+        }
         if ((s.moe_ff / 64) % kLaneStageGroups == 0)
             LAUNCH_OK(launch_ex(k_experts_lane<false, kLaneStageGroups>, lgrid, lblock, smd, g->st, pdl, la));
         else
             LAUNCH_OK(launch_ex(k_experts_lane<false, 1>, lgrid, lblock, smd, g->st, pdl, la));
         if (!kt_mark(g, kKtDown, false)) return GCUDA_E_CUDA;
-        if (g->ep_world > 1) {
-            // every pick's row from the rank that owns its expert, stored here by that rank over NVLink, so the
-            // combine below runs on every rank in rank order as on one GPU
-            ExchangeArgs xa{};
-            xa.eout = eout_of(g, l);
-            for (int r = 0; r < kMaxEpWorld; ++r) {
-                xa.peer_eout[r] = g->peer_eout[r] ? g->peer_eout[r] + static_cast<size_t>(l) * g->eout_stride : nullptr;
-                xa.peer_flags[r] = g->peer_flags[r];
-            }
-            xa.flags = g->xflags;
-            xa.route = g->route;
-            xa.epoch = g->ep_epoch;
-            xa.count = g->xcount;
-            xa.status = g->d_status;
-            xa.n = n;
-            xa.K = s.top_k;
-            xa.H = H;
-            xa.rank = g->ep_rank;
-            xa.world = g->ep_world;
-            xa.layer = l;
-            LAUNCH_OK(launch_ex(k_ep_exchange, dim3(kExchangeCtas), dim3(kExchangeThreads), 0, g->st, false, xa));
-        }
         RC_OK(norm(next_norm, true, next_hf, l));
     }
     return GCUDA_OK;

@@ -1,10 +1,10 @@
-// ep_exchange.cuh - expert parallelism's exchange of the routed experts' outputs over NVLink, without a collective
-// library in the step: every rank's MoE layer computes the picks whose experts it owns (expert e on rank e % world),
-// then k_ep_exchange stores those rows straight into every peer's slot for the layer (peer memory mapped through
-// CUDA IPC at set-up), raises this layer's flag in every peer (the step's epoch, a release store at system scope)
-// and waits, bounded, until every peer's flag for the layer holds the same epoch. The combine that follows reads
-// all the picks' rows from local memory in rank order, as on one GPU, so the step's results equal the one-GPU
-// step's bit for bit.
+// ep_exchange.cuh - expert parallelism's meeting points over NVLink, without a collective library in the step: every
+// rank's MoE layer computes the picks whose experts it owns (expert e on rank e % world), and the down kernel
+// (k_experts_lane) stores those rows straight into every peer's slot for the layer (peer memory mapped through CUDA
+// IPC at set-up), then raises the layer's flag in every peer (the step's epoch, a release store at system scope) and
+// waits, bounded, until every peer's flag for the layer holds the same epoch. The combine that follows reads all the
+// picks' rows from local memory in rank order, as on one GPU, so the step's results equal the one-GPU step's bit for
+// bit. Here: the flags' loads and stores, and the step's start (k_ep_tick).
 //
 // Plain loads and stores on peer memory only: no TMA, no bulk copy, no multicast, no library kernel on peer memory.
 #pragma once
@@ -15,21 +15,7 @@
 namespace gcu {
 
 constexpr int kMaxEpWorld = 8;
-constexpr int kExchangeThreads = 256;
-constexpr int kExchangeCtas = 32;
 constexpr uint32_t kExchangeWaitLimit = 1u << 24;   // polls of a peer's flag before the wait gives up
-
-struct ExchangeArgs {
-    float *eout;                          // this layer's rows [n * K][H] (its own picks computed, the rest to come)
-    float *peer_eout[kMaxEpWorld];        // the peers' slots for this layer (this rank's entry: unused)
-    uint32_t *peer_flags[kMaxEpWorld];    // the peers' flags [n_layers + 2][world]
-    uint32_t *flags;                      // this rank's flags, written by the peers
-    const RouteOut *route;
-    const int *epoch;
-    unsigned int *count;                  // the CTAs' arrival counter (zero between launches)
-    uint32_t *status;
-    int n, K, H, rank, world, layer;
-};
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -66,35 +52,6 @@ __global__ void k_ep_tick(TickArgs a) {
         const uint32_t *f = a.flags + a.row * a.world + s;
         bool ok = false;
         for (uint32_t it = 0; it < kExchangeWaitLimit && !ok; ++it) ok = ld_acquire_sys(f) == ep;
-        if (!ok && a.status) atomicOr(a.status, kErrWaitTimeout);
-    }
-}
-
-__global__ void __launch_bounds__(kExchangeThreads) k_ep_exchange(ExchangeArgs a) {
-    const int P = a.n * a.K, row4 = a.H / 4;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P * row4; i += gridDim.x * blockDim.x) {
-        const int p = i / row4, c = i - p * row4;
-        if (a.route->ids[p] % a.world != a.rank) continue;   // (a peer's pick: the peer sends it)
-        const float4 v = reinterpret_cast<const float4 *>(a.eout + static_cast<size_t>(p) * a.H)[c];
-#pragma unroll
-        for (int s = 0; s < kMaxEpWorld; ++s)
-            if (s < a.world && s != a.rank) reinterpret_cast<float4 *>(a.peer_eout[s] + static_cast<size_t>(p) * a.H)[c] = v;
-    }
-    __threadfence_system();   // (this thread's peer stores, before the arrival below)
-    __syncthreads();
-    __shared__ int last;
-    if (threadIdx.x == 0) last = atomicAdd(a.count, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!last) return;
-    // the last CTA to arrive: every CTA's rows are out; tell the peers, then wait for theirs
-    const uint32_t epoch = static_cast<uint32_t>(*reinterpret_cast<const volatile int *>(a.epoch));
-    if (threadIdx.x == 0) *a.count = 0;
-    const int s = threadIdx.x;
-    if (s < a.world && s != a.rank) st_release_sys(a.peer_flags[s] + a.layer * a.world + a.rank, epoch);
-    if (s < a.world && s != a.rank) {
-        const uint32_t *f = a.flags + a.layer * a.world + s;
-        bool ok = false;
-        for (uint32_t it = 0; it < kExchangeWaitLimit && !ok; ++it) ok = ld_acquire_sys(f) == epoch;
         if (!ok && a.status) atomicOr(a.status, kErrWaitTimeout);
     }
 }

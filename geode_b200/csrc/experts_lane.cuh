@@ -26,6 +26,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "ep_exchange.cuh"
 #include "layer_kernels.cuh"
 
 namespace gcu {
@@ -89,8 +90,17 @@ struct LaneArgs {
     ActSet hq;                // gate_up's input rows
     ActSet amid, shact;       // gate_up's outputs (pick rows, the shared expert's token rows), down's inputs
     float *eout, *shout;      // down's outputs: [n K][H] (pick rows), [n][H]
-    int stages;               // ring stages a warp (lane_stages: as many as the shared memory holds, <= 32)
+    int stages;               // ring stages a warp (lane_stages: as many as the shared memory holds)
     uint32_t *status;
+    // expert parallelism (world > 1), down only: the picks' rows stored into every peer's slot for this layer too
+    // (plain stores over NVLink), then the CTAs' last arrival raises this layer's flag in every peer (the step's
+    // epoch) and waits, bounded, for every peer's - the exchange with no kernel of its own
+    int rank, world, layer;
+    float *peer_eout[kMaxEpWorld];     // the peers' slots for this layer (this rank's entry unused)
+    uint32_t *flags;                   // this rank's flags [n_layers + 2][world], written by the peers
+    uint32_t *peer_flags[kMaxEpWorld];
+    const int *epoch;
+    unsigned int *count;               // the CTAs' arrival counter (zero between launches)
 };
 
 // an image row: the cols int8 codes, then per block of 16 the (scale, bsum) pair
@@ -264,7 +274,8 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
     const int r = lane & 15;
     int st = 0;
     uint32_t ph = 0;   // the consumer's ring slot and its phase parity
-    for (int k = 0;; ++k) {
+    bool failed = false;
+    for (int k = 0; !failed; ++k) {
         const int u = wg + k * NW;
         if (u >= total) break;
         const int m = u / per, j = u - m * per;
@@ -296,13 +307,14 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
         for (int g0 = 0; g0 < G; g0 += gs) {
             const bool ok = mbar_wait_bounded(bars + st, ph, a.status);
             if (!__all_sync(0xffffffffu, ok)) {
-                // (status raised) the copies still in flight land, bounded, before the warp leaves
+                // (status raised) the copies still in flight land, bounded, before the warp stops
                 if (lane == 0)
                     for (int q = 1; q < S; ++q) {
                         const int sq = (st + q) % S;
                         mbar_wait_bounded(bars + sq, sq > st ? ph : ph ^ 1u, nullptr);
                     }
-                return;
+                failed = true;
+                break;
             }
             // the stage's codes and E4M3 scales of this lane's row: gs groups of 4 blocks
             const uint8_t *sbase = ring + st * kLaneStageBytes + (lane >> 4) * sbytes;
@@ -359,6 +371,7 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
                 ph ^= 1u;
             }
         }
+        if (failed) break;
         const float gl = lr.g[m][lane >> 4];
 #pragma unroll
         for (int t = 0; t < kMaxTok; ++t) {
@@ -385,8 +398,33 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
                 }
             } else {
                 float *dst = shared ? a.shout : a.eout;
-                dst[static_cast<size_t>(orow[t]) * a.H + 32 * j + lane] = y;
+                const size_t at = static_cast<size_t>(orow[t]) * a.H + 32 * j + lane;
+                dst[at] = y;
+                if (!shared && a.world > 1) {
+#pragma unroll
+                    for (int s2 = 0; s2 < kMaxEpWorld; ++s2)
+                        if (s2 < a.world && s2 != a.rank) a.peer_eout[s2][at] = y;
+                }
             }
+        }
+    }
+    if (!kUp && a.world > 1) {
+        // every CTA's peer stores out before its arrival; the last to arrive tells the peers and waits for theirs
+        __threadfence_system();
+        __syncthreads();
+        __shared__ int last;
+        if (threadIdx.x == 0) last = atomicAdd(a.count, 1u) == gridDim.x - 1;
+        __syncthreads();
+        if (!last) return;
+        const uint32_t ep = static_cast<uint32_t>(*reinterpret_cast<const volatile int *>(a.epoch));
+        if (threadIdx.x == 0) *a.count = 0;
+        const int s2 = threadIdx.x;
+        if (s2 < a.world && s2 != a.rank) {
+            st_release_sys(a.peer_flags[s2] + a.layer * a.world + a.rank, ep);
+            const uint32_t *f = a.flags + a.layer * a.world + s2;
+            bool ok = false;
+            for (uint32_t it = 0; it < kExchangeWaitLimit && !ok; ++it) ok = ld_acquire_sys(f) == ep;
+            if (!ok && a.status) atomicOr(a.status, kErrWaitTimeout);
         }
     }
 }
