@@ -185,9 +185,13 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
         fence_barrier_init();
     }
     __syncwarp();
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    asm volatile("griddepcontrol.launch_dependents;");
-    // (the route: the previous kernels' output)
+    // gate_up follows the route's kernel directly: the route after the dependent-launch wait. Down follows gate_up,
+    // which passed its own wait only once the route's kernel had finished: down reads the route and starts its
+    // weights' copies before its wait, and only the activation rows (gate_up's output) after it
+    if (kUp) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;");
+    }
     const RouteOut &R = *a.route;
     const int nu = R.n_own;
     const int per = kUp ? a.ff / 16 : a.H / 32;   // units a member
@@ -212,6 +216,7 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
     constexpr int gs = kGS;
     if (G % gs) {
         if (threadIdx.x == 0) atomicOr(a.status, kErrBadShape);
+        if (!kUp) asm volatile("griddepcontrol.wait;" ::: "memory");   // (no kernel ends before its predecessor)
         return;
     }
     const uint32_t sbytes = static_cast<uint32_t>(gs) * kLaneTileGroup;
@@ -264,6 +269,8 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
     if (kUp) {
         lane_stage_rows(a.hq, 0, a.n, img, 0, cols);
     } else {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        asm volatile("griddepcontrol.launch_dependents;");
         lane_stage_rows(a.amid, 0, P, img, 0, cols);
         lane_stage_rows(a.shact, 0, a.n, img, P, cols);
     }
