@@ -185,10 +185,12 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
         fence_barrier_init();
     }
     __syncwarp();
-    // gate_up follows the route's kernel directly: the route after the dependent-launch wait. Down follows gate_up,
-    // which passed its own wait only once the route's kernel had finished: down reads the route and starts its
-    // weights' copies before its wait, and only the activation rows (gate_up's output) after it
+    // gate_up follows the route's kernel directly: the route after the dependent-launch wait; its activation rows
+    // (the norm's, three kernels back, finished before the route's kernel passed its own wait and let this one start)
+    // before it. Down follows gate_up, which passed its own wait only once the route's kernel had finished: down reads
+    // the route and starts its weights' copies before its wait, and only the activation rows (gate_up's output) after
     if (kUp) {
+        lane_stage_rows(a.hq, 0, a.n, img, 0, cols);
         asm volatile("griddepcontrol.wait;" ::: "memory");
         asm volatile("griddepcontrol.launch_dependents;");
     }
@@ -266,9 +268,7 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
             lr.g[m][1] = kUp ? a.sh_g1 : a.sh_g2;
         }
     }
-    if (kUp) {
-        lane_stage_rows(a.hq, 0, a.n, img, 0, cols);
-    } else {
+    if (!kUp) {
         asm volatile("griddepcontrol.wait;" ::: "memory");
         asm volatile("griddepcontrol.launch_dependents;");
         lane_stage_rows(a.amid, 0, P, img, 0, cols);
