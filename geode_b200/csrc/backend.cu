@@ -1016,23 +1016,30 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
             if (X.stride != want) return fail(g, GCUDA_E_ARG, "setup: an expert block of unexpected size");
             if (X.r16) continue;
             uint8_t *tmp = nullptr;
-            cudaError_t e = cudaMalloc(&tmp, X.stride);
+            const size_t all = static_cast<size_t>(X.n) * X.stride;
+            cudaError_t e = cudaMalloc(&tmp, X.tiled ? all : X.stride);
             if (e != cudaSuccess) return cuda_fail(g, e, "setup cudaMalloc");
             const size_t gu_tiled = gcuda_op_q4_tiled_bytes(2 * s.moe_ff, H);
-            for (int i = 0; i < X.n; ++i) {
-                uint8_t *blk = X.d + static_cast<size_t>(i) * X.stride;
-                if (!X.tiled) {   // the pack's rows -> tiles
+            if (!X.tiled) {   // the pack's rows -> tiles, block by block
+                for (int i = 0; i < X.n; ++i) {
+                    uint8_t *blk = X.d + static_cast<size_t>(i) * X.stride;
                     cudaMemcpyAsync(tmp, blk, X.stride, cudaMemcpyDeviceToDevice, g->st);
                     gcuda_op_q4_relayout(tmp, 2 * s.moe_ff, H, blk, g->st);
                     gcuda_op_q4_relayout(tmp + static_cast<size_t>(2 * s.moe_ff) * (H / 16) * 9, H, s.moe_ff, blk + gu_tiled,
                                          g->st);
                 }
-                // tiles -> R16, the layout the expert kernels read
-                cudaMemcpyAsync(tmp, blk, X.stride, cudaMemcpyDeviceToDevice, g->st);
-                k_relayout_r16<<<relayout_grid(2 * s.moe_ff / 16 * (H / 64) * 16), 256, 0, g->st>>>(tmp, 2 * s.moe_ff / 16, H, blk);
-                k_relayout_r16<<<relayout_grid(H / 16 * (s.moe_ff / 64) * 16), 256, 0, g->st>>>(tmp + gu_tiled, H / 16, s.moe_ff,
-                                                                                         blk + gu_tiled);
+                e = cudaStreamSynchronize(g->st);
+                cudaFree(tmp);
+                tmp = nullptr;
+                if (e == cudaSuccess) e = cudaMalloc(&tmp, all);
+                if (e != cudaSuccess) return cuda_fail(g, e, "setup relayout experts");
             }
+            // tiles -> R16, the layout the expert kernels read: every block of the layer in two launches
+            cudaMemcpyAsync(tmp, X.d, all, cudaMemcpyDeviceToDevice, g->st);
+            const int64_t gt = 2 * s.moe_ff / 16, dt = H / 16;
+            k_relayout_r16<<<relayout_grid(gt * (H / 64) * 16 * X.n), 256, 0, g->st>>>(tmp, gt, H, X.d, X.n, X.stride);
+            k_relayout_r16<<<relayout_grid(dt * (s.moe_ff / 64) * 16 * X.n), 256, 0, g->st>>>(tmp + gu_tiled, dt, s.moe_ff,
+                                                                                            X.d + gu_tiled, X.n, X.stride);
             e = cudaStreamSynchronize(g->st);
             cudaFree(tmp);
             if (e != cudaSuccess) return cuda_fail(g, e, "setup relayout experts");

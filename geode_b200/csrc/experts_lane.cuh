@@ -42,16 +42,18 @@ inline dim3 relayout_grid(int64_t items) {
 }
 
 // Tiled (k_relayout_q4's layout) -> R16, one thread a (tile, group, row): the same bytes permuted within each tile
-// group; the scales keep their place.
-__global__ void k_relayout_r16(const uint8_t *__restrict__ tiled, int64_t tiles, int cols, uint8_t *__restrict__ dst) {
+// group; the scales keep their place. `batch` matrices `bstride` bytes apart (a layer's experts at once).
+__global__ void k_relayout_r16(const uint8_t *__restrict__ tiled, int64_t tiles, int cols, uint8_t *__restrict__ dst,
+                               int batch = 1, size_t bstride = 0) {
     const int ng = cols / 64;
-    const int64_t total = tiles * ng * 16;
+    const int64_t per = tiles * ng * 16, total = per * batch;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int r = static_cast<int>(i % 16);
-        const int64_t tg = i / 16;   // tile * ng + group
-        const uint8_t *src = tiled + static_cast<size_t>(tg) * kLaneTileGroup;
-        uint8_t *out = dst + static_cast<size_t>(tg) * kLaneTileGroup;
+        const int64_t bi = i / per, ii = i - bi * per;
+        const int r = static_cast<int>(ii % 16);
+        const int64_t tg = ii / 16;   // tile * ng + group
+        const uint8_t *src = tiled + static_cast<size_t>(bi) * bstride + static_cast<size_t>(tg) * kLaneTileGroup;
+        uint8_t *out = dst + static_cast<size_t>(bi) * bstride + static_cast<size_t>(tg) * kLaneTileGroup;
         // the tiled code of row r, value v (0..63 of the group): lane 4 (r % 8) + (v % 16) / 4, word v / 16, byte v % 4;
         // the low nibble for rows 0..7, the high for 8..15
         auto code = [&](int v) -> uint32_t {
