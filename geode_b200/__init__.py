@@ -43,6 +43,10 @@ def cuda_lib() -> C.CDLL:
         "gcuda_op_q4_umma_bytes": (sz, [i64, i64]),
         "gcuda_op_q4_umma_relayout": (i32, [vp, i64, i64, vp, vp]),
         "gcuda_op_q4_gemm_umma": (i32, [vp, i64, i64, f32, vp, vp, vp, i32, vp, vp]),
+        "gcuda_op_moe_lane_expert_bytes": (sz, [i32, i32]),
+        "gcuda_op_moe_lane_work_bytes": (sz, [i32, i32, i32, i32]),
+        "gcuda_op_moe_lane_relayout": (i32, [vp, sz, i32, i32, i32, vp, vp]),
+        "gcuda_op_moe_lane": (i32, [vp, vp, i32, i32, i32, vp, vp, vp, i32, vp, i32, vp, vp, sz, vp]),
         "gcuda_op_moe_umma_expert_bytes": (sz, [i32, i32]),
         "gcuda_op_moe_umma_work_bytes": (sz, [i32, i32, i32, i32, i32]),
         "gcuda_op_moe_umma_relayout": (i32, [vp, sz, i32, i32, i32, vp, vp]),

@@ -165,7 +165,6 @@ struct gcuda {
     void *xbuf = nullptr;               // this rank's exchange buffer: flags [n_layers][world] (padded), then eout
     uint32_t *xflags = nullptr;
     size_t eout_stride = 0;             // expert parallelism: floats of one layer's slot of eout (a slot per layer)
-    size_t lane_avail = 0;              // the expert kernels' dynamic shared memory (set_attrs)
     int *ep_epoch = nullptr;            // (device) the step's epoch, one per step
     unsigned int *xcount = nullptr;     // (device) the exchange kernel's arrival counter
     void *peer_base[kMaxEpWorld] = {};  // the peers' exchange buffers, mapped here
@@ -556,18 +555,6 @@ int enqueue_layer(gcuda *g, int n, int l, const gcuda_layer &L, const LayerPlan 
         la.shout = g->shout;
         la.status = g->d_status;
         la.world = 1;
-        const dim3 lgrid(sm_count()), lblock(kLaneWarps * 32);
-        const int su_ = lane_stages(true, n, s.top_k, H, g->lane_avail), sd_ = lane_stages(false, n, s.top_k, s.moe_ff, g->lane_avail);
-        if (su_ < 2 || sd_ < 2) return fail(g, GCUDA_E_ARG, "the expert kernels' activation rows leave no room for their rings");
-        if (!kt_mark(g, kKtGateUp, true)) return GCUDA_E_CUDA;
-        la.stages = su_;
-        const size_t smu = lane_smem_bytes(true, n, s.top_k, H, su_), smd = lane_smem_bytes(false, n, s.top_k, s.moe_ff, sd_);
-        if ((H / 64) % kLaneStageGroups == 0)
-            LAUNCH_OK(launch_ex(k_experts_lane<true, kLaneStageGroups>, lgrid, lblock, smu, g->st, pdl, la));
-        else
-            LAUNCH_OK(launch_ex(k_experts_lane<true, 1>, lgrid, lblock, smu, g->st, pdl, la));
-        if (!kt_mark(g, kKtGateUp, false) || !kt_mark(g, kKtDown, true)) return GCUDA_E_CUDA;
-        la.stages = sd_;
         if (g->ep_world > 1) {
             // the down kernel stores every owned pick's row into the peers' slots too and meets them at the layer's flags
             la.rank = g->ep_rank;
@@ -580,11 +567,11 @@ int enqueue_layer(gcuda *g, int n, int l, const gcuda_layer &L, const LayerPlan 
             la.epoch = g->ep_epoch;
             la.count = g->xcount;
         }
-        if ((s.moe_ff / 64) % kLaneStageGroups == 0)
-            LAUNCH_OK(launch_ex(k_experts_lane<false, kLaneStageGroups>, lgrid, lblock, smd, g->st, pdl, la));
-        else
-            LAUNCH_OK(launch_ex(k_experts_lane<false, 1>, lgrid, lblock, smd, g->st, pdl, la));
-        if (!kt_mark(g, kKtDown, false)) return GCUDA_E_CUDA;
+        const int lrc = launch_lane_pair(la, n, s.top_k, H, s.moe_ff, pdl, g->st, [&](int which, bool start) {
+            return kt_mark(g, which == 0 ? kKtGateUp : kKtDown, start);
+        });
+        if (lrc == GCUDA_E_ARG) return fail(g, lrc, "the expert kernels' activation rows leave no room for their rings");
+        if (lrc != GCUDA_OK) return fail(g, lrc, "the expert kernels' launch");
         RC_OK(norm(next_norm, true, next_hf, l));
     }
     return GCUDA_OK;
@@ -667,19 +654,7 @@ int set_attrs(gcuda *g) {
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<256>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<128>())));
     LAUNCH_OK(cudaFuncSetAttribute(k_attn_decode<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(attn_smem_bytes<64>())));
-    // (the expert kernels hold the route in static shared memory: the rest of the CTA's limit is dynamic)
-    for (const void *fn : {reinterpret_cast<const void *>(k_experts_lane<true, kLaneStageGroups>),
-                           reinterpret_cast<const void *>(k_experts_lane<false, kLaneStageGroups>),
-                           reinterpret_cast<const void *>(k_experts_lane<true, 1>),
-                           reinterpret_cast<const void *>(k_experts_lane<false, 1>)}) {
-        cudaFuncAttributes fa{};
-        LAUNCH_OK(cudaFuncGetAttributes(&fa, fn));
-        const int avail = kMaxDynSmem - static_cast<int>(fa.sharedSizeBytes);
-        LAUNCH_OK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, avail));
-        g->lane_avail = static_cast<size_t>(avail);
-    }
-    // (k_route: kMaxTok * E floats, 32 KB at E = 1024, within the default limit; its limit is left as it is, so that
-    // no model lowers it under another caller's needs - attributes last for the process)
+    if (lane_opt_in(nullptr) != GCUDA_OK) return GCUDA_E_CUDA;
     (void)s;
     return GCUDA_OK;
 }

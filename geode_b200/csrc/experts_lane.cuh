@@ -438,4 +438,46 @@ __global__ void __launch_bounds__(kLaneWarps * 32) k_experts_lane(LaneArgs a) {
     }
 }
 
+// A route for ids given directly (the operator gcuda_op_moe_lane): the union of the picks in ascending expert order,
+// each member's pick slots and token mask, every member this rank's. One CTA.
+__global__ void k_route_from_ids(const int *__restrict__ ids, int n, int K, int E, RouteOut *out, uint32_t *status) {
+    __shared__ uint32_t bits[32];
+    __shared__ int mask[kMaxUnion], ex[kMaxUnion];
+    if (threadIdx.x < 32) bits[threadIdx.x] = 0;
+    if (threadIdx.x < kMaxUnion) mask[threadIdx.x] = 0;
+    __syncthreads();
+    const int P = n * K, pk = threadIdx.x;
+    const int e = pk < P ? ids[pk] : -1;
+    if (pk < P && (e < 0 || e >= E || e >= 1024)) atomicOr(status, kErrBadShape);
+    const bool ok = pk < P && e >= 0 && e < E && e < 1024;
+    if (ok) atomicOr(&bits[e >> 5], 1u << (e & 31));
+    __syncthreads();
+    int nu = 0;
+    for (int i = 0; i < 32; ++i) nu += __popc(bits[i]);
+    if (nu > kMaxUnion) {
+        if (threadIdx.x == 0) atomicOr(status, kErrUnion);
+        return;
+    }
+    if (ok) {
+        const int w = e >> 5;
+        int u = __popc(bits[w] & ((1u << (e & 31)) - 1u));
+        for (int i = 0; i < w; ++i) u += __popc(bits[i]);
+        ex[u] = e;
+        out->ex[u] = e;
+        out->slot[u][pk / K] = pk;
+        out->ids[pk] = e;
+        atomicOr(&mask[u], 1 << (pk / K));
+    }
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < nu) {
+        out->mask[threadIdx.x] = mask[threadIdx.x];
+        out->own[threadIdx.x] = threadIdx.x;
+        out->own_ex[threadIdx.x] = ex[threadIdx.x];
+    }
+    if (threadIdx.x == 0) {
+        out->n_union = nu;
+        out->n_own = nu;
+    }
+}
+
 }  // namespace gcu

@@ -32,6 +32,8 @@ struct DeviceState {
     int gemv_rc[kMaxDevices] = {};
     int bf16_rc[kMaxDevices] = {};
     int umma_rc[kMaxDevices] = {};
+    int lane_rc[kMaxDevices] = {};
+    size_t lane_avail[kMaxDevices] = {};   // the expert lane kernels' dynamic shared memory limit
     uint32_t *status[kMaxDevices] = {};
 };
 inline DeviceState &device_state() {

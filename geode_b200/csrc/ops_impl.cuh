@@ -3,6 +3,9 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <functional>
+
 #include "../../include/geode_cuda.h"
 #include "accept.cuh"
 #include "gemv_kernels.cuh"
@@ -10,6 +13,7 @@
 #include "launch.hpp"
 #include "umma_gemm.cuh"
 #include "moe_umma.cuh"
+#include "experts_lane.cuh"
 
 using namespace gcu;
 
@@ -33,6 +37,57 @@ template <int NT>
 constexpr int umma_launch_smem() {
     return static_cast<int>(umma_smem_bytes<NT>()) > kUmmaSmemFloor ? static_cast<int>(umma_smem_bytes<NT>()) : kUmmaSmemFloor;
 }
+// The expert lane kernels' shared-memory opt-in on the current device (the whole limit but their static part), and
+// what it leaves them
+inline int lane_opt_in(size_t *avail) {
+    const int dev = current_device();
+    if (dev < 0) return GCUDA_E_CUDA;
+    DeviceState &d = device_state();
+    std::lock_guard<std::mutex> lock(d.mu);
+    if (!d.lane_rc[dev]) {
+        bool ok = true;
+        size_t least = 0;
+        for (const void *fn : {reinterpret_cast<const void *>(k_experts_lane<true, kLaneStageGroups>),
+                               reinterpret_cast<const void *>(k_experts_lane<false, kLaneStageGroups>),
+                               reinterpret_cast<const void *>(k_experts_lane<true, 1>),
+                               reinterpret_cast<const void *>(k_experts_lane<false, 1>)}) {
+            cudaFuncAttributes fa{};
+            ok = ok && cudaFuncGetAttributes(&fa, fn) == cudaSuccess;
+            const int av = kMaxDynSmem - static_cast<int>(fa.sharedSizeBytes);
+            ok = ok && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, av) == cudaSuccess;
+            least = least == 0 ? static_cast<size_t>(av) : std::min(least, static_cast<size_t>(av));
+        }
+        d.lane_avail[dev] = least;
+        d.lane_rc[dev] = ok ? static_cast<int>(GCUDA_OK) : static_cast<int>(GCUDA_E_CUDA);
+    }
+    if (avail) *avail = d.lane_avail[dev];
+    return d.lane_rc[dev];
+}
+
+// Both expert lane launches of a layer (gate_up, then down) for the route and buffers in `la`
+inline int launch_lane_pair(LaneArgs la, int n, int K, int H, int ff, bool pdl, cudaStream_t st,
+                            const std::function<bool(int, bool)> &mark = nullptr) {
+    size_t avail = 0;
+    if (lane_opt_in(&avail) != GCUDA_OK) return GCUDA_E_CUDA;
+    const dim3 grid(sm_count()), block(kLaneWarps * 32);
+    const int su = lane_stages(true, n, K, H, avail), sd = lane_stages(false, n, K, ff, avail);
+    if (su < 2 || sd < 2) return GCUDA_E_ARG;
+    if (mark && !mark(0, true)) return GCUDA_E_CUDA;
+    la.stages = su;
+    const size_t smu = lane_smem_bytes(true, n, K, H, su), smd = lane_smem_bytes(false, n, K, ff, sd);
+    cudaError_t e = (H / 64) % kLaneStageGroups == 0
+                        ? launch_ex(k_experts_lane<true, kLaneStageGroups>, grid, block, smu, st, pdl, la)
+                        : launch_ex(k_experts_lane<true, 1>, grid, block, smu, st, pdl, la);
+    if (e != cudaSuccess) return GCUDA_E_CUDA;
+    if (mark && (!mark(0, false) || !mark(1, true))) return GCUDA_E_CUDA;
+    la.stages = sd;
+    e = (ff / 64) % kLaneStageGroups == 0 ? launch_ex(k_experts_lane<false, kLaneStageGroups>, grid, block, smd, st, pdl, la)
+                                          : launch_ex(k_experts_lane<false, 1>, grid, block, smd, st, pdl, la);
+    if (e != cudaSuccess) return GCUDA_E_CUDA;
+    if (mark && !mark(1, false)) return GCUDA_E_CUDA;
+    return GCUDA_OK;
+}
+
 inline int umma_opt_in() {
     const int dev = current_device();
     if (dev < 0) return GCUDA_E_CUDA;
@@ -113,6 +168,120 @@ int gcuda_op_moe_umma_relayout(const uint8_t *d_pack, size_t pack_stride, int E,
         count_launch(2);
     }
     return cudaGetLastError() == cudaSuccess ? GCUDA_OK : GCUDA_E_CUDA;
+}
+
+// ---- the verify step's expert kernels (a lane a weight row) as operators ----
+namespace {
+size_t lane_expert_bytes(int H, int ff) {
+    return static_cast<size_t>(2 * ff) * (H / 16) * 9 + static_cast<size_t>(H) * (ff / 16) * 9;
+}
+struct LaneWork {
+    RouteOut *route;
+    int8_t *aq, *sq;
+    float *as, *ss, *shout;
+    int32_t *ab, *sb;
+};
+size_t lane_work_layout(int n, int K, int H, int ff, uint8_t *base, LaneWork *w) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t *p = base ? base + off : nullptr;
+        off += (bytes + 255) / 256 * 256;
+        return p;
+    };
+    const size_t P = static_cast<size_t>(n) * K, nb = static_cast<size_t>(ff / 16);
+    uint8_t *r = take(sizeof(RouteOut)), *aq = take(P * ff), *as = take(P * nb * 4), *ab = take(P * nb * 4);
+    uint8_t *sq = take(static_cast<size_t>(n) * ff), *ss = take(n * nb * 4), *sb = take(n * nb * 4);
+    uint8_t *sh = take(static_cast<size_t>(n) * H * 4);
+    if (w) {
+        w->route = reinterpret_cast<RouteOut *>(r);
+        w->aq = reinterpret_cast<int8_t *>(aq);
+        w->as = reinterpret_cast<float *>(as);
+        w->ab = reinterpret_cast<int32_t *>(ab);
+        w->sq = reinterpret_cast<int8_t *>(sq);
+        w->ss = reinterpret_cast<float *>(ss);
+        w->sb = reinterpret_cast<int32_t *>(sb);
+        w->shout = reinterpret_cast<float *>(sh);
+    }
+    return off;
+}
+}  // namespace
+
+size_t gcuda_op_moe_lane_expert_bytes(int H, int ff) {
+    return H > 0 && ff > 0 && H % 64 == 0 && ff % 64 == 0 ? lane_expert_bytes(H, ff) : 0;
+}
+
+size_t gcuda_op_moe_lane_work_bytes(int n, int K, int H, int ff) {
+    if (n < 1 || n > kMaxTok || K < 1 || K > 8 || H % 64 || ff % 64 || H <= 0 || ff <= 0) return 0;
+    return lane_work_layout(n, K, H, ff, nullptr, nullptr);
+}
+
+int gcuda_op_moe_lane_relayout(const uint8_t *d_pack, size_t pack_stride, int E, int H, int ff, uint8_t *d_out,
+                               void *stream) {
+    const size_t eb = gcuda_op_moe_lane_expert_bytes(H, ff);
+    if (!d_pack || !d_out || eb == 0 || E < 1 || pack_stride < eb || (reinterpret_cast<uintptr_t>(d_out) & 15))
+        return GCUDA_E_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the pack's rows -> tiles (into a temporary), then tiles -> R16 for every block at once
+    uint8_t *tmp = nullptr;
+    if (cudaMalloc(&tmp, static_cast<size_t>(E) * eb) != cudaSuccess) return GCUDA_E_MEMORY;
+    const size_t gu = static_cast<size_t>(2 * ff) * (H / 16) * 9;
+    int rc = GCUDA_OK;
+    for (int e = 0; e < E && rc == GCUDA_OK; ++e) {
+        const uint8_t *src = d_pack + static_cast<size_t>(e) * pack_stride;
+        uint8_t *dst = tmp + static_cast<size_t>(e) * eb;
+        rc = gcuda_op_q4_relayout(src, 2 * static_cast<int64_t>(ff), H, dst, stream);
+        if (rc == GCUDA_OK) rc = gcuda_op_q4_relayout(src + gu, H, ff, dst + gu, stream);
+    }
+    if (rc == GCUDA_OK) {
+        const int64_t gt = 2 * ff / 16, dt = H / 16;
+        k_relayout_r16<<<relayout_grid(gt * (H / 64) * 16 * E), 256, 0, st>>>(tmp, gt, H, d_out, E, eb);
+        k_relayout_r16<<<relayout_grid(dt * (ff / 64) * 16 * E), 256, 0, st>>>(tmp + gu, dt, ff, d_out + gu, E, eb);
+        count_launch(2);
+        if (cudaStreamSynchronize(st) != cudaSuccess) rc = GCUDA_E_CUDA;
+    }
+    cudaFree(tmp);
+    return rc;
+}
+
+int gcuda_op_moe_lane(const uint8_t *d_r16, const float *d_globals, int E, int H, int ff, const int8_t *d_q,
+                      const float *d_scale, const int32_t *d_bsum, int n, const int *d_ids, int K, float *d_out,
+                      void *d_work, size_t work_bytes, void *stream) {
+    const size_t need = gcuda_op_moe_lane_work_bytes(n, K, H, ff);
+    if (!d_r16 || !d_globals || !d_q || !d_scale || !d_bsum || !d_ids || !d_out || !d_work || need == 0 ||
+        work_bytes < need || E < 1 || E > 1024 || (reinterpret_cast<uintptr_t>(d_work) & 255) ||
+        (reinterpret_cast<uintptr_t>(d_r16) & 15) || (reinterpret_cast<uintptr_t>(d_q) & 15))
+        return GCUDA_E_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint32_t *status = device_status();
+    if (!status) return GCUDA_E_CUDA;
+    LaneWork w{};
+    lane_work_layout(n, K, H, ff, static_cast<uint8_t *>(d_work), &w);
+    if (launch_ex(k_route_from_ids, dim3(1), dim3(256), 0, st, false, d_ids, n, K, E, w.route, status) != cudaSuccess)
+        return GCUDA_E_CUDA;
+    const size_t eb = lane_expert_bytes(H, ff), tb = static_cast<size_t>(H / 64) * kLaneTileGroup;
+    LaneArgs la{};
+    la.route = w.route;
+    la.experts = d_r16;
+    la.stride = eb;
+    la.down_off = static_cast<size_t>(2 * ff / 16) * tb;
+    la.globals = d_globals;
+    // (the kernels always run the layer's shared expert too: expert 0's matrices stand in, into a scratch output)
+    la.sh_gate = d_r16;
+    la.sh_up = d_r16 + static_cast<size_t>(ff / 16) * tb;
+    la.sh_down = d_r16 + la.down_off;
+    la.sh_g0 = la.sh_g1 = la.sh_g2 = 1.0f;
+    la.H = H;
+    la.ff = ff;
+    la.K = K;
+    la.n = n;
+    la.hq = ActSet{d_q, d_scale, d_bsum, H, n, H, H / 16};
+    la.amid = ActSet{w.aq, w.as, w.ab, ff, n * K, ff, ff / 16};
+    la.shact = ActSet{w.sq, w.ss, w.sb, ff, n, ff, ff / 16};
+    la.eout = d_out;
+    la.shout = w.shout;
+    la.status = status;
+    la.world = 1;
+    return launch_lane_pair(la, n, K, H, ff, false, st);
 }
 
 int gcuda_op_moe_umma(const uint8_t *d_u, const float *d_globals, int E, int H, int ff, const int8_t *d_q,

@@ -271,6 +271,20 @@ int gcuda_op_q4_gemm_umma(const uint8_t *d_u, int64_t rows, int64_t cols, float 
  * scratch of gcuda_op_moe_umma_work_bytes (256-byte aligned): the picks grouped by expert and the units of the two
  * grouped products are planned on the device. The combine (weights, shared expert) is the caller's. An expert id out
  * of range: its pick is left out and the status word (gcuda_op_status) raised. */
+/* The verify step's expert kernels (a lane a weight row: dp4a on the codes for only the tokens that picked each expert,
+ * the reference's block chain in that lane) for n <= 8 token rows, K <= 8 picks each: every pick p = t * K + k of
+ * expert ids[p] gives d_out row p = W_dn[e] . quant(silu(g) * u), [g | u] = W_gu[e] . quant(h_t) - bit for bit the
+ * reference's per-pick product (engine/src/model.cpp:4496-4543). d_r16: E expert blocks in the kernels' R16 layout,
+ * gcuda_op_moe_lane_expert_bytes(H, ff) apart, made from the pack's blocks by gcuda_op_moe_lane_relayout (which
+ * allocates a temporary and synchronises `stream`); d_q/d_scale/d_bsum: h quantized (gcuda_op_quantize); d_work:
+ * scratch of gcuda_op_moe_lane_work_bytes, 256-byte aligned. At most 64 distinct experts among the picks. */
+size_t gcuda_op_moe_lane_expert_bytes(int H, int ff);
+size_t gcuda_op_moe_lane_work_bytes(int n, int K, int H, int ff);
+int gcuda_op_moe_lane_relayout(const uint8_t *d_pack, size_t pack_stride, int E, int H, int ff, uint8_t *d_out,
+                               void *stream);
+int gcuda_op_moe_lane(const uint8_t *d_r16, const float *d_globals, int E, int H, int ff, const int8_t *d_q,
+                      const float *d_scale, const int32_t *d_bsum, int n, const int *d_ids, int K, float *d_out,
+                      void *d_work, size_t work_bytes, void *stream);
 size_t gcuda_op_moe_umma_expert_bytes(int H, int ff);
 size_t gcuda_op_moe_umma_work_bytes(int n, int K, int E, int H, int ff);
 int gcuda_op_moe_umma_relayout(const uint8_t *d_pack, size_t pack_stride, int E, int H, int ff, uint8_t *d_u,
