@@ -64,7 +64,6 @@ struct GemvShape {
     int wpu, nslots, sg;
     size_t smem;
     int stages = 0;
-    int blocked = 0;   // (expert down) a CTA per block of consecutive units, their experts' images shared
 };
 // The activation image of groups [g0, g0 + ng) of up to kMaxTok vectors (src(t) = the ActSet row of token column t, -1 =
 // zeros), token stride ts: act word (t, gl, tig, j) at t * ts + (gl * 4 + tig) * 16 + 4 j (values 16 (4 g + j) + 4 tig
