@@ -128,6 +128,7 @@ struct gcuda {
     uint64_t graph_kernels[kMaxTok + 1] = {};   // kernels one launch of graph[n] runs
     int pos = 0, last_batch = 0;
     int last_toks[kMaxTok] = {};
+    uint32_t *h_status = nullptr;  // pinned: the status word's copy, read after the step's one synchronization
     StepState *step = nullptr;     // the device-side loop's decision and counters
     double *d_u = nullptr;
     int *d_samples = nullptr;
@@ -697,10 +698,8 @@ int record_graphs(gcuda *g) {
     return GCUDA_OK;
 }
 
-int check_status(gcuda *g) {
-    uint32_t st = 0;
-    LAUNCH_OK(cudaMemcpyAsync(&st, g->d_status, 4, cudaMemcpyDeviceToHost, g->st));
-    LAUNCH_OK(cudaStreamSynchronize(g->st));
+// the status word's verdict once its copy in h_status has landed
+int status_verdict(gcuda *g, uint32_t st) {
     if (st) {
         cudaMemsetAsync(g->d_status, 0, 4, g->st);
         std::string why;
@@ -710,6 +709,12 @@ int check_status(gcuda *g) {
         return fail(g, GCUDA_E_DEVICE, "device status" + why);
     }
     return GCUDA_OK;
+}
+
+int check_status(gcuda *g) {
+    LAUNCH_OK(cudaMemcpyAsync(g->h_status, g->d_status, 4, cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    return status_verdict(g, *g->h_status);
 }
 
 }  // namespace
@@ -756,6 +761,11 @@ gcuda *gcuda_open(int device, char *err, int err_len) {
         gcuda_close(g);
         return nullptr;
     }
+    if (cudaMallocHost(&g->h_status, sizeof(uint32_t)) != cudaSuccess) {
+        put("cudaMallocHost");
+        gcuda_close(g);
+        return nullptr;
+    }
     return g;
 }
 
@@ -776,6 +786,7 @@ void gcuda_close(gcuda *g) {
     for (void *p : g->allocs) cudaFree(p);
     if (g->rej) cudaFree(g->rej);
     if (g->d_seen) cudaFree(g->d_seen);
+    if (g->h_status) cudaFreeHost(g->h_status);
     if (g->ev0) cudaEventDestroy(g->ev0);
     if (g->ev1) cudaEventDestroy(g->ev1);
     for (int r = 0; r < kMaxEpWorld; ++r)
@@ -1192,18 +1203,28 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
     return GCUDA_OK;
 }
 
+namespace {
+// the step's graph for n tokens already in d_toks at the handle's position, and the status word's copy behind it
+int enqueue_verify(gcuda *g, int n) {
+    LAUNCH_OK(cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaEventRecord(g->ev0, g->st));
+    LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
+    count_launch(g->graph_kernels[n]);
+    LAUNCH_OK(cudaEventRecord(g->ev1, g->st));
+    LAUNCH_OK(cudaMemcpyAsync(g->h_status, g->d_status, 4, cudaMemcpyDeviceToHost, g->st));
+    return GCUDA_OK;
+}
+}  // namespace
+
 int gcuda_verify_device(gcuda *g, const int *d_toks, int n) {
     if (!g || !g->ready) return fail(g, GCUDA_E_STATE, "verify before setup");
     if (n < 1 || n > g->sh.max_tokens) return fail(g, GCUDA_E_ARG, "a verified batch of " + std::to_string(n) + " tokens");
     if (g->pos + n > g->sh.context) return fail(g, GCUDA_E_ARG, "the context is full");
     cudaSetDevice(g->device);
     if (d_toks != g->d_toks) LAUNCH_OK(cudaMemcpyAsync(g->d_toks, d_toks, sizeof(int) * n, cudaMemcpyDeviceToDevice, g->st));
-    LAUNCH_OK(cudaMemcpyAsync(g->d_pos, &g->pos, sizeof(int), cudaMemcpyHostToDevice, g->st));
-    LAUNCH_OK(cudaEventRecord(g->ev0, g->st));
-    LAUNCH_OK(cudaGraphLaunch(g->graph[n], g->st));
-    count_launch(g->graph_kernels[n]);
-    LAUNCH_OK(cudaEventRecord(g->ev1, g->st));
-    RC_OK(check_status(g));
+    RC_OK(enqueue_verify(g, n));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    RC_OK(status_verdict(g, *g->h_status));
     cudaEventElapsedTime(&g->last_ms, g->ev0, g->ev1);
     LAUNCH_OK(cudaMemcpy(g->last_toks, g->d_toks, sizeof(int) * n, cudaMemcpyDeviceToHost));
     g->pos += n;
@@ -1221,11 +1242,17 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
         if (toks[t] < 0 || toks[t] >= g->sh.vocab)
             return fail(g, GCUDA_E_ARG, "cannot read the embedding of token " + std::to_string(toks[t]));
     cudaSetDevice(g->device);
+    // the tokens in, the graph, the status word and the outputs back, then one synchronization
     LAUNCH_OK(cudaMemcpyAsync(g->d_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
-    RC_OK(gcuda_verify_device(g, g->d_toks, n));
+    RC_OK(enqueue_verify(g, n));
     if (logits) LAUNCH_OK(cudaMemcpyAsync(logits, g->logits, sizeof(float) * n * g->sh.vocab, cudaMemcpyDeviceToHost, g->st));
     if (hidden) LAUNCH_OK(cudaMemcpyAsync(hidden, g->hid, sizeof(float) * n * g->sh.hidden, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
+    RC_OK(status_verdict(g, *g->h_status));
+    cudaEventElapsedTime(&g->last_ms, g->ev0, g->ev1);
+    std::memcpy(g->last_toks, toks, sizeof(int) * n);
+    g->pos += n;
+    g->last_batch = n;
     return GCUDA_OK;
 }
 
@@ -1432,7 +1459,8 @@ int gcuda_keep(gcuda *g, int kept) {
         LAUNCH_OK(cudaMemcpyAsync(g->conv, g->conv_bk + b * g->conv_n, g->conv_n * sizeof(float), cudaMemcpyDeviceToDevice, g->st));
     if (g->gdn_n)
         LAUNCH_OK(cudaMemcpyAsync(g->gdn, g->gdn_bk + b * g->gdn_n, g->gdn_n * sizeof(float), cudaMemcpyDeviceToDevice, g->st));
-    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    // (no wait: every later use of the states is ordered behind these copies on the handle's stream, and the calls
+    // that hand data to the host synchronize it)
     g->pos -= g->last_batch - kept;
     g->last_batch = 0;
     return GCUDA_OK;

@@ -100,7 +100,8 @@ int gcuda_set_ep(gcuda *g, int rank, int world, const void *id);
  * outside [0, vocab): GCUDA_E_ARG before anything runs, the conversation as it was (engine/src/model.cpp:1551-1555). */
 int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden);
 /* Model::verify_keep (engine/src/model.cpp:1594): keep the first `kept` (1 .. n-1) of the last verified batch - the
- * Gated DeltaNet states as after token kept-1, the position back by n - kept. */
+ * Gated DeltaNet states as after token kept-1, the position back by n - kept. Returns once the states' copies are
+ * queued on the handle's stream (every later call is ordered behind them). */
 int gcuda_keep(gcuda *g, int kept);
 int gcuda_position(gcuda *g);
 
