@@ -73,6 +73,8 @@ def _sig(L):
         "gcuda_sync_step": (i32, [vp, vp, vp, vp]),
         "gcuda_stream": (vp, [vp]),
         "gcuda_set_mtp": (i32, [vp, i32, i32, i32, i32, vp]),
+        "gcuda_set_draft_head": (i32, [vp, i32, vp, i32]),
+        "gcuda_draft_rows": (i32, [vp]),
         "gcuda_draft": (i32, [vp, vp, i32, i32, vp, vp, vp, vp]),
         "gcuda_draft_next": (i32, [vp, i32, i32, vp, vp, vp]),
     }
@@ -85,6 +87,21 @@ def _sig(L):
 
 def _ptr(a: np.ndarray) -> int:
     return a.ctypes.data
+
+
+def draft_vocab(pack_dir: str, vocab: int):
+    """The pack's draft vocabulary (draft_vocab.bin: int32 token ids) as the engine's GPU branch takes it
+    (engine/src/model.cpp:2135-2161): the ids inside the vocabulary in file order, padded to whole tiles of 32 rows
+    with copies of the first; None without the file or a valid id."""
+    path = os.path.join(pack_dir, "draft_vocab.bin")
+    if not os.path.exists(path):
+        return None
+    ids = np.fromfile(path, dtype="<i4")
+    ids = ids[(ids >= 0) & (ids < vocab)]
+    if ids.size == 0:
+        return None
+    pad = (-ids.size) % 32
+    return np.ascontiguousarray(np.concatenate([ids, np.full(pad, ids[0])]).astype(np.int32))
 
 
 class GcudaError(RuntimeError):
@@ -189,6 +206,14 @@ class Backend:
             check(L.gcuda_set_mtp(self.g, q4("mtp.fc.weight"), raw("mtp.pre_fc_norm_embedding.weight"),
                                   raw("mtp.pre_fc_norm_hidden.weight"), raw("mtp.norm.weight"), C.addressof(mt)),
                   "set_mtp")
+            ids = draft_vocab(pack_dir, c["vocab_size"])
+            if ids is not None:
+                hb, ht = tensor_bytes("lm_head.weight")
+                rb = ht["shape"][1] // 16 * 9
+                rows = np.ascontiguousarray(hb.reshape(-1, rb)[ids])
+                dh = check(L.gcuda_adopt_q4(self.g, _ptr(rows), len(ids), ht["shape"][1], rb, ht.get("global", 1.0)),
+                           "draft head")
+                check(L.gcuda_set_draft_head(self.g, dh, _ptr(ids), len(ids)), "set_draft_head")
         eb, et = tensor_bytes("embed_tokens.weight")
         embed = check(L.gcuda_adopt_embedding(self.g, _ptr(eb), et["shape"][0], et["shape"][1], et.get("global", 1.0)), "embed")
         head = q4("lm_head.weight")
@@ -249,11 +274,12 @@ class Backend:
 
     def draft(self, toks, pos: int, hidden=None, logits: bool = False):
         """gcuda_draft: the MTP pass over positions pos.. (toks: the next tokens; hidden: their rows, or None for the
-        last verified batch's); (draft, prob, the last position's logits or None)."""
+        last verified batch's); (draft, prob, the last position's logits or None - over the draft head's rows when the
+        pack has a draft vocabulary, see draft_vocab)."""
         toks = np.ascontiguousarray(np.asarray(toks, dtype=np.int32))
         hd = None if hidden is None else np.ascontiguousarray(hidden, dtype=np.float32)
         d, pr = C.c_int(0), C.c_float(0.0)
-        lg = np.zeros(self.vocab, np.float32) if logits else None
+        lg = np.zeros(self.L.gcuda_draft_rows(self.g), np.float32) if logits else None
         self._rc(self.L.gcuda_draft(self.g, _ptr(toks), len(toks), pos, _ptr(hd) if hd is not None else None,
                                     C.byref(d), C.byref(pr), _ptr(lg) if lg is not None else None), "draft")
         return d.value, pr.value, lg
@@ -261,7 +287,7 @@ class Backend:
     def draft_next(self, tok: int, pos: int, logits: bool = False):
         """gcuda_draft_next: one chained MTP position; (draft, prob, logits or None)."""
         d, pr = C.c_int(0), C.c_float(0.0)
-        lg = np.zeros(self.vocab, np.float32) if logits else None
+        lg = np.zeros(self.L.gcuda_draft_rows(self.g), np.float32) if logits else None
         self._rc(self.L.gcuda_draft_next(self.g, int(tok), pos, C.byref(d), C.byref(pr),
                                          _ptr(lg) if lg is not None else None), "draft_next")
         return d.value, pr.value, lg

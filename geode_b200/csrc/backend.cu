@@ -190,6 +190,10 @@ struct gcuda {
     cudaGraphExec_t mtp_graph[kMaxTok + 1] = {};
     uint64_t mtp_graph_kernels[kMaxTok + 1] = {};
     int mtp_rows = 0;                   // the last pass's rows (a chained draft goes on from row mtp_rows - 1)
+    // the draft head (gcuda_set_draft_head): lm_head's rows of a draft vocabulary, the MTP pass's logits over them
+    int draft_head = -1;
+    std::vector<int> draft_ids;
+    int mtp_vocab = 0;                  // the MTP pass's logits: draft_ids.size(), or the vocabulary
 };
 
 namespace {
@@ -639,12 +643,14 @@ int enqueue_mtp(gcuda *g, int n) {
     last.scale += static_cast<size_t>(n - 1) * (H / 16);
     last.bsum += static_cast<size_t>(n - 1) * (H / 16);
     last.n = 1;
-    RC_OK(launch_units(g, g->mtp_lm_u, static_cast<int>((s.vocab + 31) / 32), last, 1, g->pdl));
+    // (over the draft head's rows when a draft vocabulary is set: d_mtp_draft then holds the row, run_mtp maps it)
+    const int rows = g->mtp_vocab;
+    RC_OK(launch_units(g, g->mtp_lm_u, (rows + 31) / 32, last, 1, g->pdl));
     LAUNCH_OK(launch_ex(k_argmax_rows, dim3(argmax_slices(1, sm_count()), 1), dim3(kArgmaxThreads), 0, g->st, false,
-                        static_cast<const float *>(g->mtp_logits), s.vocab, g->d_mtp_best));
+                        static_cast<const float *>(g->mtp_logits), rows, g->d_mtp_best));
     LAUNCH_OK(launch_ex(k_argmax_finish, dim3(1), dim3(32), 0, g->st, false, g->d_mtp_best, 1, g->d_mtp_draft));
     LAUNCH_OK(launch_ex(k_softmax_at, dim3(kSoftmaxCtas), dim3(kSoftmaxThreads), 0, g->st, false,
-                        static_cast<const float *>(g->mtp_logits), s.vocab, static_cast<const int *>(g->d_mtp_draft),
+                        static_cast<const float *>(g->mtp_logits), rows, static_cast<const int *>(g->d_mtp_draft),
                         g->mtp_part, g->mtp_count, g->mtp_prob));
     return GCUDA_OK;
 }
@@ -1096,7 +1102,8 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
     if (g->ep_world > 1) RC_OK(ep_exchange_setup(g, static_cast<size_t>(T) * K * H));
     if (g->has_mtp &&
         (!act_alloc(g, g->mtp_in, T, 2 * H) || !dalloc(g, &g->mtp_hin, static_cast<size_t>(T) * H) ||
-         !dalloc(g, &g->mtp_hf, static_cast<size_t>(T) * H) || !dalloc(g, &g->mtp_logits, s.vocab) ||
+         !dalloc(g, &g->mtp_hf, static_cast<size_t>(T) * H) ||
+         !dalloc(g, &g->mtp_logits, g->draft_ids.empty() ? s.vocab : g->draft_ids.size()) ||
          !dalloc(g, &g->mtp_prob, 1) || !dalloc(g, &g->mtp_part, kSoftmaxCtas) || !dalloc(g, &g->mtp_count, 1) ||
          !dalloc(g, &g->d_mtp_toks, kMaxTok) || !dalloc(g, &g->d_mtp_pos, 1) || !dalloc(g, &g->d_mtp_draft, 1) ||
          !dalloc(g, &g->d_mtp_best, 1)))
@@ -1189,8 +1196,19 @@ int gcuda_setup(gcuda *g, const gcuda_shape *shape, const gcuda_layer *layers, i
     g->lm_u = static_cast<int>(U.size());
     plain_units(U, *head, g->logits, s.vocab, kStore);
     if (g->has_mtp) {
+        // the MTP pass's head: lm_head, or the draft head (its rows the draft vocabulary's, a multiple of 32)
+        const DevTensor *dh = head;
+        g->mtp_vocab = s.vocab;
+        if (!g->draft_ids.empty()) {
+            dh = q4(g->draft_head);
+            bool ok = dh && dh->rows == static_cast<int64_t>(g->draft_ids.size()) && dh->cols == H &&
+                      dh->global == head->global;
+            for (const int id : g->draft_ids) ok = ok && id >= 0 && id < s.vocab;
+            if (!ok) return fail(g, GCUDA_E_ARG, "setup: the draft head (lm_head's rows of the draft vocabulary)");
+            g->mtp_vocab = static_cast<int>(g->draft_ids.size());
+        }
         g->mtp_lm_u = static_cast<int>(U.size());
-        plain_units(U, *head, g->mtp_logits, s.vocab, kStore);
+        plain_units(U, *dh, g->mtp_logits, g->mtp_vocab, kStore);
     }
     g->n_units = static_cast<int>(U.size());
     if (!dalloc(g, &g->units, U.size())) return GCUDA_E_MEMORY;
@@ -1269,6 +1287,17 @@ int gcuda_set_mtp(gcuda *g, int fc, int pre_e, int pre_h, int norm, const gcuda_
     return GCUDA_OK;
 }
 
+int gcuda_set_draft_head(gcuda *g, int head, const int *ids, int n) {
+    if (!g) return GCUDA_E_ARG;
+    if (g->ready) return fail(g, GCUDA_E_STATE, "set_draft_head: after setup");
+    if (!ids || n < 32 || n % 32) return fail(g, GCUDA_E_ARG, "set_draft_head: a draft vocabulary of whole tiles (32 rows)");
+    g->draft_head = head;
+    g->draft_ids.assign(ids, ids + n);
+    return GCUDA_OK;
+}
+
+int gcuda_draft_rows(gcuda *g) { return g && g->ready && g->has_mtp ? g->mtp_vocab : GCUDA_E_STATE; }
+
 namespace {
 // one MTP pass of n rows (its inputs in place): the captured pass, then the draft, its probability and the logits
 int run_mtp(gcuda *g, int n, int *draft, float *prob, float *logits) {
@@ -1279,8 +1308,13 @@ int run_mtp(gcuda *g, int n, int *draft, float *prob, float *logits) {
     LAUNCH_OK(cudaMemcpyAsync(draft, g->d_mtp_draft, sizeof(int), cudaMemcpyDeviceToHost, g->st));
     if (prob) LAUNCH_OK(cudaMemcpyAsync(prob, g->mtp_prob, sizeof(float), cudaMemcpyDeviceToHost, g->st));
     if (logits)
-        LAUNCH_OK(cudaMemcpyAsync(logits, g->mtp_logits, sizeof(float) * g->sh.vocab, cudaMemcpyDeviceToHost, g->st));
+        LAUNCH_OK(cudaMemcpyAsync(logits, g->mtp_logits, sizeof(float) * g->mtp_vocab, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
+    // a draft head's row -> its token (engine/src/model.cpp:1409, 1473)
+    if (!g->draft_ids.empty()) {
+        if (*draft < 0 || *draft >= static_cast<int>(g->draft_ids.size())) return fail(g, GCUDA_E_DEVICE, "draft: no row");
+        *draft = g->draft_ids[static_cast<size_t>(*draft)];
+    }
     return GCUDA_OK;
 }
 

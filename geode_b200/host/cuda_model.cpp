@@ -4,6 +4,7 @@
 #include <dlfcn.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 
 namespace ghost {
@@ -51,6 +52,7 @@ bool CudaApi::load(const std::string &path, std::string &err) {
     sym(state_put, "gcuda_state_put");
     sym(reset, "gcuda_reset");
     sym(set_mtp, "gcuda_set_mtp");
+    sym(set_draft_head, "gcuda_set_draft_head");
     sym(draft, "gcuda_draft");
     sym(draft_next, "gcuda_draft_next");
     return ok;
@@ -155,6 +157,28 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
             return false;
         if (api_.set_mtp(g_, fc, pre_e, pre_h, mnorm, &mt) != 0) return fail("set_mtp", err);
         has_mtp_ = true;
+        // the draft head (engine/src/model.cpp:2135-2161): draft_vocab.bin's ids inside the vocabulary, padded to whole
+        // tiles of 32 rows with copies of the first, and lm_head's rows of them
+        std::vector<int32_t> ids;
+        if (std::FILE *f = std::fopen((dir + "/draft_vocab.bin").c_str(), "rb")) {
+            const int64_t V = c["vocab_size"].integer();
+            int32_t id;
+            while (std::fread(&id, 4, 1, f) == 1)
+                if (id >= 0 && id < V) ids.push_back(id);
+            std::fclose(f);
+        }
+        if (!ids.empty()) {
+            while (ids.size() % 32) ids.push_back(ids[0]);
+            TensorView lm;
+            if (!pack_.tensor("lm_head.weight", lm, err)) return false;
+            const size_t rb = static_cast<size_t>(lm.cols() / 16) * 9;
+            std::vector<uint8_t> rows(ids.size() * rb);
+            for (size_t r = 0; r < ids.size(); ++r)
+                std::memcpy(rows.data() + r * rb, lm.data + static_cast<size_t>(ids[r]) * rb, rb);
+            const int dh = api_.adopt_q4(g_, rows.data(), static_cast<int64_t>(ids.size()), lm.cols(), rb, lm.global);
+            if (dh < 0 || api_.set_draft_head(g_, dh, ids.data(), static_cast<int>(ids.size())) != 0)
+                return fail("draft head", err);
+        }
     }
     TensorView et;
     if (!pack_.tensor("embed_tokens.weight", et, err)) return false;

@@ -35,6 +35,7 @@ struct CudaApi {
     decltype(&gcuda_state_put) state_put = nullptr;
     decltype(&gcuda_reset) reset = nullptr;
     decltype(&gcuda_set_mtp) set_mtp = nullptr;
+    decltype(&gcuda_set_draft_head) set_draft_head = nullptr;
     decltype(&gcuda_draft) draft = nullptr;
     decltype(&gcuda_draft_next) draft_next = nullptr;
     // path: the library file; empty = libgeode_cuda.so beside this library

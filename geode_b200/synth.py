@@ -222,6 +222,12 @@ class _Writer:
         self.f.close()
 
 
+def write_draft_vocab(pack_dir: str, ids) -> None:
+    """The pack's draft vocabulary: draft_vocab.bin, the token ids as little-endian int32 in order (the file the engine
+    reads for its draft head, engine/src/model.cpp:803-827)."""
+    np.asarray(ids, dtype="<i4").tofile(os.path.join(pack_dir, "draft_vocab.bin"))
+
+
 def write_pack(out_dir: str, shape: ModelShape, seed: int = 0, fill: str = "quantized",
                router_std: float = 0.05, weight_std: float = 0.02, mtp: bool = False, distinct_layers: int = 0) -> Dict:
     """Writes a geode-pack for ``shape`` into out_dir; returns the manifest. fill: "quantized" (N(0, weight_std)

@@ -110,11 +110,21 @@ int gcuda_position(gcuda *g);
  * mtp.norm (f32), and its decoder layer (an attention layer with the model's MLP; routed experts by
  * gcuda_adopt_experts). Before gcuda_setup, which gives the layer its own KV cache of `context` positions. */
 int gcuda_set_mtp(gcuda *g, int fc, int pre_e, int pre_h, int norm, const gcuda_layer *layer);
+/* The draft head (engine/src/model.cpp:803-827, 2135-2161): the pack's draft_vocab.bin tokens ids[0..n) (int32, those
+ * outside the vocabulary left out, then padded to whole tiles of 32 rows with copies of ids[0], as the engine's GPU
+ * branch does - the copies never win the first maximum) and `head`, a q4 tensor of lm_head's rows of those ids in
+ * that order (gcuda_adopt_q4, lm_head's global). The MTP pass then multiplies only these rows: its logits are n wide,
+ * the draft is ids[their first maximum] and prob its softmax probability over the n (copies included). Before
+ * gcuda_setup; n a multiple of 32. */
+int gcuda_set_draft_head(gcuda *g, int head, const int *ids, int n);
+/* The MTP pass's logits per row: n of gcuda_set_draft_head, else the vocabulary (after gcuda_setup). */
+int gcuda_draft_rows(gcuda *g);
 /* Model::draft (engine/src/model.cpp:1295-1446, its GPU branch): the MTP pass over the positions pos .. pos+n-1 of
  * its KV (n <= max_tokens), position i taking the embedding of toks[i] and hidden row i - hidden [n][hidden] on the
  * host, or NULL for the last verified batch's rows (gcuda_verify's `hidden`; n at most that batch's size) - then
  * draft = the first maximum of the last position's logits and prob (NULL: not wanted) its softmax probability
- * (softmax_at, engine/src/model.cpp:1287-1292); logits (NULL: not wanted) gets those vocab logits. */
+ * (softmax_at, engine/src/model.cpp:1287-1292); logits (NULL: not wanted) gets those logits (gcuda_draft_rows of
+ * them: the vocabulary's, or the draft head's rows'). */
 int gcuda_draft(gcuda *g, const int *toks, int n, int pos, const float *hidden, int *draft, float *prob, float *logits);
 /* Model::draft_next (engine/src/model.cpp:1448-1480): one chained MTP position `pos` from the last pass's output row
  * after mtp.norm and the embedding of tok (the draft just made). */

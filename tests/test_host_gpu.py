@@ -265,11 +265,13 @@ def test_host_prefill(env):
     assert np.array_equal(lg2, lg)
 
 
-def test_host_drafts(tmp_path):
+@pytest.mark.parametrize("vocab_file", [False, True])
+def test_host_drafts(tmp_path, vocab_file):
     """ghost_draft / ghost_draft_next through the host (a pack with the MTP layer: CudaModel adopts mtp.* and the
     MTP layer's experts, gcuda_set_mtp) equal the Python binding's gcuda_draft / gcuda_draft_next after the same
     batches - the same kernels on the same bytes, so the same drafts and probabilities bit for bit; the pass's
-    numerics against the oracle are tests/test_mtp_gpu.py's. A pack without the layer refuses to draft."""
+    numerics against the oracle are tests/test_mtp_gpu.py's. With a draft vocabulary (draft_vocab.bin) both sides
+    build the same draft head and every draft is one of its ids. A pack without the layer refuses to draft."""
     if not torch.cuda.is_available():
         pytest.skip("no GPU")
     from geode_b200.backend import Backend
@@ -283,11 +285,16 @@ def test_host_drafts(tmp_path):
     shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
     d = str(tmp_path / "mtp")
     synth.write_pack(d, shape, seed=71, mtp=True)
+    rng = np.random.default_rng(72)
+    ids = None
+    if vocab_file:
+        ids = set(int(i) for i in rng.choice(shape.vocab, 70, replace=False))
+        synth.write_draft_vocab(d, sorted(ids))
     err = C.create_string_buffer(512)
     m = C.c_void_p()
     assert H.ghost_open(d.encode(), 0, shape.ctx, 5, C.byref(m), err, 512) == 0, err.value
     be = Backend(d, context=shape.ctx, max_tokens=5)
-    rng = np.random.default_rng(72)
+    assert be.L.gcuda_draft_rows(be.g) == (96 if vocab_file else shape.vocab)
     try:
         pos = 0
         tok = int(rng.integers(0, shape.vocab))
@@ -301,6 +308,7 @@ def test_host_drafts(tmp_path):
                 err.value
             dp, pp, _ = be.draft(nxt, pos)
             assert (dh.value, np.float32(ph.value)) == (dp, np.float32(pp)), (rep, dh.value, dp, ph.value, pp)
+            assert ids is None or dp in ids
             q = pos + 5
             assert H.ghost_draft_next(m, dh.value, q, C.byref(dh), C.byref(ph), err, 512) == 0, err.value
             dp, pp, _ = be.draft_next(dp, q)

@@ -9,7 +9,11 @@ the dense model with the MTP layer:
   own logits (bit-exact), its probability softmax_at of those logits (rtol 1e-6: the double sum is grouped otherwise);
 - the engine's loop: a verified batch's rows left on the device feed the next pass (hidden NULL);
 - three chained drafts (gcuda_draft_next) from the pass's own output rows, each within the tolerance of the oracle's
-  chain from its own.
+  chain from its own;
+- with a draft vocabulary (draft_vocab.bin, engine/src/model.cpp:803-827, 2135-2161): the pass multiplies only the
+  draft head's rows - the ids inside the vocabulary, padded to whole tiles of 32 with copies of the first - so its
+  logits are the oracle's full logits at those ids (each row's product stands alone) within the tolerance, the draft
+  is the id at their first maximum and the probability softmax_at over the padded rows.
 """
 import numpy as np
 import pytest
@@ -117,4 +121,47 @@ def test_mtp_refusals(tmp_path):
         be.draft(list(range(6)), 0, hidden=np.zeros((6, H), np.float32))      # more rows than max_tokens
     dg, pr, _ = be.draft([1, 2], 0, hidden=np.ones((2, H), np.float32))
     assert 0 <= dg < shape.vocab and 0.0 < pr <= 1.0
+    be.close()
+
+
+@pytest.mark.parametrize("arch", ["qwen35moe", "qwen35"])
+def test_mtp_draft_head(arch, tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from geode_b200.backend import Backend, draft_vocab
+    shape = synth.tiny_shape(arch, n_layers=4, ctx=640)
+    d = str(tmp_path / "pack")
+    synth.write_pack(d, shape, seed=71, mtp=True)
+    V = shape.vocab
+    rng = np.random.default_rng(72)
+    raw_ids = list(rng.choice(V, 100, replace=False)) + [-1, V, V + 7]   # (the last three outside: left out)
+    synth.write_draft_vocab(d, raw_ids)
+    ids = draft_vocab(d, V)
+    assert len(ids) == 128 and list(ids[:100]) == raw_ids[:100] and (ids[100:] == raw_ids[0]).all()
+    ora = op.Oracle(d)
+    st = ora.new_state(shape.ctx)
+    be = Backend(d, context=shape.ctx, max_tokens=5)
+    assert be.L.gcuda_draft_rows(be.g) == 128
+    L = 13
+    prompt = rng.integers(0, V, L).astype(np.int32)
+    hid = np.concatenate([be.verify(prompt[i:i + 5], logits=False, hidden=True)[1] for i in range(0, L, 5)])
+
+    def check(dg, pr, lg, lg_full, what):
+        _close(lg, lg_full[ids], what)
+        best = int(np.argmax(lg))
+        assert dg == int(ids[best]), what
+        assert np.isclose(pr, _softmax_at(lg, best), rtol=1e-6, atol=0), (what, pr, _softmax_at(lg, best))
+
+    for p0 in range(0, L - 1, 5):
+        p1 = min(p0 + 5, L - 1)
+        dg, pr, lg = be.draft(prompt[p0 + 1:p1 + 1], p0, hidden=hid[p0:p1], logits=True)
+        assert lg.shape == (128,)
+        lg_ref, h_ref = ora.forward_mtp(st, prompt[p0 + 1:p1 + 1], hid[p0:p1], p0)
+        check(dg, pr, lg, lg_ref, f"pass at {p0}")
+    q, tok = L - 1, dg
+    for i in range(2):
+        dg, pr, lg = be.draft_next(tok, q, logits=True)
+        lg_ref, h_ref = ora.forward_mtp(st, [tok], h_ref[None], q)
+        check(dg, pr, lg, lg_ref, f"chained draft {i}")
+        tok, q = dg, q + 1
     be.close()
