@@ -127,6 +127,10 @@ struct gcuda {
     cudaGraphExec_t graph[kMaxTok + 1] = {};
     uint64_t graph_kernels[kMaxTok + 1] = {};   // kernels one launch of graph[n] runs
     int pos = 0, last_batch = 0;
+    // hid's rows that hold positions of the conversation (the final norm's rows, the MTP pass's input): the last
+    // verified batch's n, its kept ones after gcuda_keep, 1 after gcuda_put_last_hidden; row hid_rows - 1 is the last
+    // position's (the engine's last_hid_, engine/src/model.cpp:1585, 1602)
+    int hid_rows = 0;
     int last_toks[kMaxTok] = {};
     uint32_t *h_status = nullptr;  // pinned: the status word's copy, read after the step's one synchronization
     StepState *step = nullptr;     // the device-side loop's decision and counters
@@ -1247,6 +1251,7 @@ int gcuda_verify_device(gcuda *g, const int *d_toks, int n) {
     LAUNCH_OK(cudaMemcpy(g->last_toks, g->d_toks, sizeof(int) * n, cudaMemcpyDeviceToHost));
     g->pos += n;
     g->last_batch = n;
+    g->hid_rows = n;
     return GCUDA_OK;
 }
 
@@ -1271,6 +1276,7 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
     std::memcpy(g->last_toks, toks, sizeof(int) * n);
     g->pos += n;
     g->last_batch = n;
+    g->hid_rows = n;
     return GCUDA_OK;
 }
 
@@ -1332,8 +1338,9 @@ int mtp_checks(gcuda *g, const int *toks, int n, int pos, int *draft) {
 
 int gcuda_draft(gcuda *g, const int *toks, int n, int pos, const float *hidden, int *draft, float *prob, float *logits) {
     RC_OK(mtp_checks(g, toks, n, pos, draft));
-    if (!hidden && n > g->last_batch)
-        return fail(g, GCUDA_E_STATE, "draft: the last verified batch has fewer than " + std::to_string(n) + " rows");
+    if (!hidden && n > g->hid_rows)
+        return fail(g, GCUDA_E_STATE, "draft: the device holds fewer than " + std::to_string(n) +
+                                          " hidden rows of the conversation (the last verified batch's, as kept)");
     cudaSetDevice(g->device);
     const size_t rows = static_cast<size_t>(n) * g->sh.hidden * sizeof(float);
     LAUNCH_OK(cudaMemcpyAsync(g->d_mtp_toks, toks, sizeof(int) * n, cudaMemcpyHostToDevice, g->st));
@@ -1497,6 +1504,7 @@ int gcuda_keep(gcuda *g, int kept) {
     // that hand data to the host synchronize it)
     g->pos -= g->last_batch - kept;
     g->last_batch = 0;
+    g->hid_rows = kept;
     return GCUDA_OK;
 }
 
@@ -1510,6 +1518,7 @@ int gcuda_reset(gcuda *g) {
     LAUNCH_OK(cudaStreamSynchronize(g->st));
     g->pos = 0;
     g->last_batch = 0;
+    g->hid_rows = 0;
     g->reject_steps = 0;   // the device-side rejection sampler's Philox sequence starts over with the conversation
     g->mtp_rows = 0;
     return GCUDA_OK;
@@ -1540,8 +1549,9 @@ int gcuda_state_get(gcuda *g, float *conv, float *gdn, int8_t *kv, float *kv_sca
                         gdn[dst] = d[src];
                     }
     }
+    // (the model's attention layers, then the MTP layer's slot when it has one, as the engine's cache orders them)
     const size_t row = g->kvrow, nkv = s.n_kv_heads;
-    for (int a = 0; a < g->n_attn && positions > 0; ++a) {
+    for (int a = 0; a < g->n_attn + (g->has_mtp ? 1 : 0) && positions > 0; ++a) {
         const size_t base = static_cast<size_t>(a) * s.context;
         if (kv) {
             LAUNCH_OK(cudaMemcpy(kv + (static_cast<size_t>(a) * 2 + 0) * positions * row, g->kc + base * row, positions * row, cudaMemcpyDeviceToHost));
@@ -1574,7 +1584,7 @@ int gcuda_state_put(gcuda *g, const float *conv, const float *gdn, const int8_t 
         LAUNCH_OK(cudaMemcpy(g->gdn, d.data(), g->gdn_n * sizeof(float), cudaMemcpyHostToDevice));
     }
     const size_t row = g->kvrow, nkv = s.n_kv_heads;
-    for (int a = 0; a < g->n_attn && pos > 0; ++a) {
+    for (int a = 0; a < g->n_attn + (g->has_mtp ? 1 : 0) && pos > 0; ++a) {
         const size_t base = static_cast<size_t>(a) * s.context;
         if (kv) {
             LAUNCH_OK(cudaMemcpy(g->kc + base * row, kv + (static_cast<size_t>(a) * 2 + 0) * pos * row, pos * row, cudaMemcpyHostToDevice));
@@ -1587,6 +1597,28 @@ int gcuda_state_put(gcuda *g, const float *conv, const float *gdn, const int8_t 
     }
     g->pos = pos;
     g->last_batch = 0;
+    g->hid_rows = 0;
+    return GCUDA_OK;
+}
+
+int gcuda_last_hidden(gcuda *g, float *out) {
+    if (!g || !g->ready || !out) return fail(g, GCUDA_E_ARG, "last_hidden");
+    if (g->hid_rows < 1) return fail(g, GCUDA_E_STATE, "last_hidden: no hidden row of the conversation on the device");
+    cudaSetDevice(g->device);
+    const size_t H = static_cast<size_t>(g->sh.hidden);
+    LAUNCH_OK(cudaMemcpyAsync(out, g->hid + static_cast<size_t>(g->hid_rows - 1) * H, H * sizeof(float),
+                              cudaMemcpyDeviceToHost, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    return GCUDA_OK;
+}
+
+int gcuda_put_last_hidden(gcuda *g, const float *row) {
+    if (!g || !g->ready || !row) return fail(g, GCUDA_E_ARG, "put_last_hidden");
+    if (g->pos < 1) return fail(g, GCUDA_E_STATE, "put_last_hidden: an empty conversation");
+    cudaSetDevice(g->device);
+    LAUNCH_OK(cudaMemcpyAsync(g->hid, row, static_cast<size_t>(g->sh.hidden) * sizeof(float), cudaMemcpyHostToDevice, g->st));
+    LAUNCH_OK(cudaStreamSynchronize(g->st));
+    g->hid_rows = 1;
     return GCUDA_OK;
 }
 
@@ -1616,6 +1648,7 @@ int gcuda_debug_step_eager(gcuda *g, const int *toks, int n, int pdl) {
     RC_OK(check_status(g));
     g->pos += n;
     g->last_batch = n;
+    g->hid_rows = n;
     return GCUDA_OK;
 }
 
@@ -1674,6 +1707,7 @@ int gcuda_debug_trace(gcuda *g, const int *toks, int n, float *x, float *router_
     std::memcpy(g->last_toks, toks, sizeof(int) * n);
     g->pos += n;
     g->last_batch = n;
+    g->hid_rows = n;
     return GCUDA_OK;
 }
 
@@ -1730,6 +1764,7 @@ int gcuda_debug_kernel_times(gcuda *g, const int *toks, int n, int reps, float *
     if (step_ms) *step_ms = total / static_cast<float>(reps);
     if (union_sum) *union_sum = (u1 - u0) / reps;
     g->last_batch = 0;   // (the steps ran at the same position: nothing to accept or keep)
+    g->hid_rows = 0;
     return GCUDA_OK;
 }
 
@@ -1831,6 +1866,7 @@ int gcuda_state_randomize(gcuda *g, int pos, uint64_t seed) {
     LAUNCH_OK(cudaStreamSynchronize(g->st));
     g->pos = pos;
     g->last_batch = 0;
+    g->hid_rows = 0;
     return GCUDA_OK;
 }
 
@@ -1911,6 +1947,7 @@ int gcuda_sync_step(gcuda *g, int *steps, int *union_sum, int *last_kept) {
     if (union_sum) *union_sum = ss.n_union_sum;
     if (last_kept) *last_kept = ss.kept;
     g->last_batch = 0;
+    g->hid_rows = 0;
     return GCUDA_OK;
 }
 

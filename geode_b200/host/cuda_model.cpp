@@ -53,6 +53,8 @@ bool CudaApi::load(const std::string &path, std::string &err) {
     sym(reset, "gcuda_reset");
     sym(set_mtp, "gcuda_set_mtp");
     sym(set_draft_head, "gcuda_set_draft_head");
+    sym(last_hidden, "gcuda_last_hidden");
+    sym(put_last_hidden, "gcuda_put_last_hidden");
     sym(draft, "gcuda_draft");
     sym(draft_next, "gcuda_draft_next");
     return ok;
@@ -214,10 +216,13 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
     vocab_ = s.vocab;
     context_ = s.context;
     dir_ = dir;
-    // what a state of this model holds (engine/src/model.cpp:351-358: the attention layers' KV, the Gated DeltaNet
-    // layers' conv and recurrent states)
+    // what a state of this model holds (engine/src/model.cpp:351-358: the attention layers' KV - the MTP layer's slot
+    // after them when it is bound - the Gated DeltaNet layers' conv and recurrent states; with the MTP layer the last
+    // hidden row too, engine/src/state.cpp:275)
     int n_attn = 0, n_gdn = 0;
     for (int l = 0; l < L; ++l) (types[static_cast<size_t>(l)].text() == "full_attention" ? n_attn : n_gdn)++;
+    if (has_mtp_) ++n_attn;
+    shapes_.mtp = has_mtp_ ? 1u : 0u;
     const uint64_t conv_dim = 2ull * s.gdn_k_heads * s.gdn_k_dim + static_cast<uint64_t>(s.gdn_v_heads) * s.gdn_v_dim;
     shapes_.n_attn = static_cast<uint32_t>(n_attn);
     shapes_.kv_heads = static_cast<uint32_t>(s.n_kv_heads);
@@ -226,7 +231,7 @@ bool CudaModel::open(const std::string &dir, const ModelOptions &opt, std::strin
     shapes_.n_layers = static_cast<uint32_t>(L);
     shapes_.conv_n = static_cast<uint64_t>(n_gdn) * conv_dim * static_cast<uint64_t>(std::max(0, s.conv_kernel - 1));
     shapes_.gdn_n = static_cast<uint64_t>(n_gdn) * s.gdn_v_heads * s.gdn_k_dim * s.gdn_v_dim;
-    text_only_ = !pack_.has("mtp.fc.weight");
+    text_only_ = true;
     const JsonRef tensors = pack_.manifest()["tensors"];
     for (size_t i = 0; i < tensors.size(); ++i)
         if (tensors.key_at(i).substr(0, 7) == "vision.") text_only_ = false;   // (engine/src/vision.cpp's tensors)
@@ -259,7 +264,7 @@ bool CudaModel::save_state(const std::string &path, bool append, int extra, int 
         return false;
     }
     if (!text_only_) {
-        err = "a pack with an MTP layer or a vision encoder: its state holds what this backend does not keep";
+        err = "a pack with a vision encoder: its state holds the images' positions, which this backend does not keep";
         return false;
     }
     const int pos = position();
@@ -269,12 +274,19 @@ bool CudaModel::save_state(const std::string &path, bool append, int extra, int 
     std::vector<float> ks(std::max<size_t>(1, static_cast<size_t>(s.n_attn) * 2 * pos * s.kv_heads));
     code = 7;   // (GHOST_E_BACKEND)
     if (api_.state_get(g_, conv.data(), gdn.data(), kv.data(), ks.data(), pos) != 0) return fail("state_get", err);
+    // the last hidden row when the engine would keep one (an MTP layer, a position, a row on the device)
+    std::vector<float> hid;
+    if (has_mtp_ && pos > 0) {
+        hid.resize(s.hidden);
+        if (api_.last_hidden(g_, hid.data()) != 0) hid.clear();
+    }
     StateMeta m;
     m.position = pos;
     m.extra = extra;
     m.conv_id = conv_id_;
     code = 2;   // (GHOST_E_IO)
-    if (!write_state(path, state_fingerprint(), s, m, conv.data(), gdn.data(), kv.data(), ks.data(), append, err))
+    if (!write_state(path, state_fingerprint(), s, m, conv.data(), gdn.data(), kv.data(), ks.data(),
+                     hid.empty() ? nullptr : hid.data(), append, err))
         return false;
     code = 0;
     return true;
@@ -294,19 +306,20 @@ bool CudaModel::load_state(const std::string &path, int &extra, int &code, std::
         return false;
     };
     if (!text_only_) {
-        err = "a pack with an MTP layer or a vision encoder: its state holds what this backend does not keep";
+        err = "a pack with a vision encoder: its state holds the images' positions, which this backend does not keep";
         return refuse(3);
     }
     StateMeta m;
-    std::vector<float> conv, gdn, ks;
+    std::vector<float> conv, gdn, ks, hid;
     std::vector<int8_t> kv;
-    const StateError e = read_state(path, state_fingerprint(), shapes_, context_, m, conv, gdn, kv, ks, err);
+    const StateError e = read_state(path, state_fingerprint(), shapes_, context_, m, conv, gdn, kv, ks, hid, err);
     if (e != StateError::none) return refuse(e == StateError::format ? 3 : e == StateError::context ? 1 : 2);
     conv.resize(std::max<size_t>(1, conv.size()));
     gdn.resize(std::max<size_t>(1, gdn.size()));
     kv.resize(std::max<size_t>(1, kv.size()));
     ks.resize(std::max<size_t>(1, ks.size()));
-    if (api_.state_put(g_, conv.data(), gdn.data(), kv.data(), ks.data(), m.position) != 0) {
+    if (api_.state_put(g_, conv.data(), gdn.data(), kv.data(), ks.data(), m.position) != 0 ||
+        (has_mtp_ && !hid.empty() && m.position > 0 && api_.put_last_hidden(g_, hid.data()) != 0)) {
         fail("state_put", err);
         return refuse(7);
     }

@@ -36,6 +36,8 @@ struct CudaApi {
     decltype(&gcuda_reset) reset = nullptr;
     decltype(&gcuda_set_mtp) set_mtp = nullptr;
     decltype(&gcuda_set_draft_head) set_draft_head = nullptr;
+    decltype(&gcuda_last_hidden) last_hidden = nullptr;
+    decltype(&gcuda_put_last_hidden) put_last_hidden = nullptr;
     decltype(&gcuda_draft) draft = nullptr;
     decltype(&gcuda_draft_next) draft_next = nullptr;
     // path: the library file; empty = libgeode_cuda.so beside this library
@@ -141,9 +143,10 @@ public:
     // Model::save_state / load_state (engine/src/state.cpp:241-465) in the engine's state file: the device's KV rows
     // and recurrent states through the host (gcuda_state_get / gcuda_state_put), so a state saved by the reference
     // engine (CPU or GPU path) continues here and back. extra: the caller's token passed on but not computed yet.
-    // A failed load leaves the conversation empty (position 0), as the engine's. Packs with an MTP layer or a vision
-    // encoder are refused (their states hold that layer's KV rows and the images' positions, which this backend does
-    // not keep). code: 0, or GHOST_E_IO / GHOST_E_FORMAT / GHOST_E_ARG as include/geode_host.h lists them.
+    // A failed load leaves the conversation empty (position 0), as the engine's. With an MTP layer the file holds that
+    // layer's KV rows and the last hidden row (a load gives the row back to the device for the next draft); packs
+    // with a vision encoder are refused (their states hold the images' positions, which this backend does not keep).
+    // code: 0, or GHOST_E_IO / GHOST_E_FORMAT / GHOST_E_ARG as include/geode_host.h lists them.
     bool save_state(const std::string &path, bool append, int extra, int &code, std::string &err);
     bool load_state(const std::string &path, int &extra, int &code, std::string &err);
     // the shapes the state file records and the fingerprint it carries for this pack
@@ -158,7 +161,7 @@ private:
     int max_tokens_ = 5, vocab_ = 0, last_n_ = 0, context_ = 0;
     std::string dir_;
     StateShapes shapes_;
-    bool text_only_ = true;    // no MTP layer, no vision encoder in the pack
+    bool text_only_ = true;    // no vision encoder in the pack
     bool has_mtp_ = false;     // the MTP layer is on the device (gcuda_set_mtp)
     uint64_t conv_id_ = 0;     // the conversation (new at open and after a failed load; a loaded state's)
 };

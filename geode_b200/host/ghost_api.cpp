@@ -206,6 +206,7 @@ ghost::StateShapes shapes_of(const ghost_state_shapes *s) {
     o.n_layers = s->n_layers;
     o.conv_n = s->conv_n;
     o.gdn_n = s->gdn_n;
+    o.mtp = s->mtp;
     return o;
 }
 int state_code(ghost::StateError e) {
@@ -223,14 +224,14 @@ uint64_t ghost_state_fingerprint(const char *pack_dir, const ghost_state_shapes 
 
 int ghost_state_write(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t position,
                       int32_t extra, uint64_t conv_id, const float *conv, const float *gdn, const int8_t *kv,
-                      const float *kv_scale, int32_t append, char *err, size_t err_len) {
+                      const float *kv_scale, const float *hidden, int32_t append, char *err, size_t err_len) {
     if (!path || !s) return GHOST_E_ARG;
     ghost::StateMeta m;
     m.position = position;
     m.extra = extra;
     m.conv_id = conv_id;
     std::string e;
-    if (!ghost::write_state(path, fingerprint, shapes_of(s), m, conv, gdn, kv, kv_scale, append != 0, e)) {
+    if (!ghost::write_state(path, fingerprint, shapes_of(s), m, conv, gdn, kv, kv_scale, hidden, append != 0, e)) {
         put(e, err, err_len);
         return e.rfind("write_state: bad", 0) == 0 ? GHOST_E_ARG : GHOST_E_IO;
     }
@@ -254,13 +255,14 @@ int ghost_state_peek(const char *path, uint64_t fingerprint, const ghost_state_s
 }
 
 int ghost_state_read(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context, float *conv,
-                     float *gdn, int8_t *kv, float *kv_scale, char *err, size_t err_len) {
+                     float *gdn, int8_t *kv, float *kv_scale, float *hidden, int32_t *has_hidden, char *err,
+                     size_t err_len) {
     if (!path || !s) return GHOST_E_ARG;
     ghost::StateMeta m;
-    std::vector<float> c, g, ks;
+    std::vector<float> c, g, ks, hd;
     std::vector<int8_t> k;
     std::string e;
-    const ghost::StateError r = ghost::read_state(path, fingerprint, shapes_of(s), context, m, c, g, k, ks, e);
+    const ghost::StateError r = ghost::read_state(path, fingerprint, shapes_of(s), context, m, c, g, k, ks, hd, e);
     if (r != ghost::StateError::none) {
         put(e, err, err_len);
         return state_code(r);
@@ -270,6 +272,8 @@ int ghost_state_read(const char *path, uint64_t fingerprint, const ghost_state_s
     if (!g.empty()) std::memcpy(gdn, g.data(), g.size() * sizeof(float));
     if (!k.empty()) std::memcpy(kv, k.data(), k.size());
     if (!ks.empty()) std::memcpy(kv_scale, ks.data(), ks.size() * sizeof(float));
+    if (has_hidden) *has_hidden = hd.empty() ? 0 : 1;
+    if (!hd.empty() && hidden) std::memcpy(hidden, hd.data(), hd.size() * sizeof(float));
     return GHOST_OK;
 }
 

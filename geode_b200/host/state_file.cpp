@@ -251,9 +251,9 @@ uint64_t pack_print(const std::string &pack_dir) {
 
 uint64_t state_fingerprint(uint64_t print, const StateShapes &s) {
     // the engine's list, in its order: version, KV element bytes (1: int8), attention layers, KV heads, row elements,
-    // conv floats, recurrent floats, hidden, layers, an MTP layer (0), a vision encoder (0)
+    // conv floats, recurrent floats, hidden, layers, an MTP layer (0 / 1), a vision encoder (0)
     const uint64_t shapes[] = {kFormatVersion, 1u, s.n_attn, s.kv_heads, s.kv_row, s.conv_n, s.gdn_n, s.hidden,
-                               s.n_layers, 0u, 0u};
+                               s.n_layers, s.mtp ? 1u : 0u, 0u};
     Fnv f;
     f.h = print;
     return f.add(shapes, sizeof shapes).h;
@@ -268,8 +268,8 @@ uint64_t new_conversation_id(const void *salt) {
 }
 
 bool write_state(const std::string &path, uint64_t fingerprint, const StateShapes &s, const StateMeta &m,
-                 const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, bool append,
-                 std::string &err) {
+                 const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, const float *hidden,
+                 bool append, std::string &err) {
     const bool missing = (m.position > 0 && s.n_attn > 0 && (!kv || !kv_scale)) || (s.conv_n && !conv) ||
                          (s.gdn_n && !gdn);
     if (m.position < 0 || missing) {
@@ -291,6 +291,7 @@ bool write_state(const std::string &path, uint64_t fingerprint, const StateShape
     h.kv_heads = s.kv_heads;
     h.kv_row = s.kv_row;
     h.hidden = s.hidden;
+    h.has_hidden = hidden ? 1 : 0;
     h.block = kBlockPositions;
     h.conv_n = s.conv_n;
     h.gdn_n = s.gdn_n;
@@ -329,10 +330,11 @@ bool write_state(const std::string &path, uint64_t fingerprint, const StateShape
     };
     if (!w.ok()) return give_up("open");
 
-    // 1. the fixed part up to the states (gen, empty image slots, a zero hidden row), the states, then - once those
-    //    are on disk - the closing gen, so a reader sees both gens equal only after a finished state write
+    // 1. the fixed part up to the states (gen, empty image slots, the hidden row or zeros), the states, then - once
+    //    those are on disk - the closing gen, so a reader sees both gens equal only after a finished state write
     std::vector<uint8_t> lead(static_cast<size_t>(p.conv - p.gen_lead), 0);
     std::memcpy(lead.data(), &h.gen, sizeof h.gen);
+    if (hidden) std::memcpy(lead.data() + (p.hidden - p.gen_lead), hidden, size_t{s.hidden} * sizeof(float));
     w.put(p.gen_lead, lead.data(), lead.size())
         .put(p.conv, conv, s.conv_n * sizeof(float))
         .put(p.recurrent, gdn, s.gdn_n * sizeof(float))
@@ -385,7 +387,7 @@ StateError peek_state(const std::string &path, uint64_t fingerprint, const State
 
 StateError read_state(const std::string &path, uint64_t fingerprint, const StateShapes &s, int context, StateMeta &m,
                       std::vector<float> &conv, std::vector<float> &gdn, std::vector<int8_t> &kv,
-                      std::vector<float> &kv_scale, std::string &err) {
+                      std::vector<float> &kv_scale, std::vector<float> &hidden, std::string &err) {
     const MappedFile f(path);
     Header h{};
     const StateError e = validate(f, path, fingerprint, s, context, h, err);
@@ -396,6 +398,11 @@ StateError read_state(const std::string &path, uint64_t fingerprint, const State
     gdn.resize(s.gdn_n);
     std::memcpy(conv.data(), f.span(p.conv, s.conv_n * sizeof(float)), s.conv_n * sizeof(float));
     std::memcpy(gdn.data(), f.span(p.recurrent, s.gdn_n * sizeof(float)), s.gdn_n * sizeof(float));
+    hidden.clear();
+    if (h.has_hidden) {
+        hidden.resize(s.hidden);
+        std::memcpy(hidden.data(), f.span(p.hidden, size_t{s.hidden} * sizeof(float)), size_t{s.hidden} * sizeof(float));
+    }
     kv.assign(size_t{s.n_attn} * 2 * P * row, 0);
     kv_scale.assign(size_t{s.n_attn} * 2 * P * heads, 0.0f);
     const size_t B = h.block, blocks = (P + B - 1) / B, bb = static_cast<size_t>(h.block_bytes);

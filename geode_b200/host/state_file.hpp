@@ -18,12 +18,13 @@
 namespace ghost {
 
 // What a state holds, as the engine's fingerprint lists it (engine/src/state.cpp:229-238): the KV element size (1:
-// int8 rows with a scale a position and KV head - the only format this backend keeps), the attention layers, KV
-// heads, row elements, the conv and recurrent state floats, the hidden size, the layers, an MTP layer and a vision
-// encoder (neither: this backend verifies text with the main layers).
+// int8 rows with a scale a position and KV head - the only format this backend keeps), the attention layers (with
+// the MTP layer's slot when there is one, engine/src/model.cpp:354), KV heads, row elements, the conv and recurrent
+// state floats, the hidden size, the layers, an MTP layer, a vision encoder (never: this backend verifies text).
 struct StateShapes {
     uint32_t n_attn = 0, kv_heads = 0, kv_row = 0, hidden = 0, n_layers = 0;
     uint64_t conv_n = 0, gdn_n = 0;
+    uint32_t mtp = 0;
 };
 
 // The conversation around the buffers.
@@ -41,20 +42,22 @@ uint64_t state_fingerprint(uint64_t pack_print, const StateShapes &s);
 uint64_t new_conversation_id(const void *salt);
 
 // Writes the state. kv: [n_attn][2][position][kv_row] int8, kv_scale: [n_attn][2][position][kv_heads] f32 (the
-// gcuda_state_get layouts); conv, gdn: the reference's own buffers. append: as the engine's (falls back to a whole
-// write when the file at path is not an earlier state of this conversation in this shape).
+// gcuda_state_get layouts); conv, gdn: the reference's own buffers; hidden: the last position's row after the final
+// norm (has_hidden, engine/src/state.cpp:275), or NULL for none. append: as the engine's (falls back to a whole write
+// when the file at path is not an earlier state of this conversation in this shape).
 bool write_state(const std::string &path, uint64_t fingerprint, const StateShapes &s, const StateMeta &m,
-                 const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, bool append,
-                 std::string &err);
+                 const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, const float *hidden,
+                 bool append, std::string &err);
 
 // The header of a state file, checked against this model (magic, version, checksum, fingerprint, shapes, the file's
 // length, the fixed part's gen at both ends) and the context (position < context); fills m.
 enum class StateError { none, io, format, context };
 StateError peek_state(const std::string &path, uint64_t fingerprint, const StateShapes &s, int context, StateMeta &m,
                       std::string &err);
-// peek_state, then the buffers (sized for m.position as write_state's).
+// peek_state, then the buffers (sized for m.position as write_state's); hidden: the file's last hidden row, empty
+// when it has none.
 StateError read_state(const std::string &path, uint64_t fingerprint, const StateShapes &s, int context, StateMeta &m,
                       std::vector<float> &conv, std::vector<float> &gdn, std::vector<int8_t> &kv,
-                      std::vector<float> &kv_scale, std::string &err);
+                      std::vector<float> &kv_scale, std::vector<float> &hidden, std::string &err);
 
 }  // namespace ghost

@@ -121,7 +121,8 @@ int gcuda_set_draft_head(gcuda *g, int head, const int *ids, int n);
 int gcuda_draft_rows(gcuda *g);
 /* Model::draft (engine/src/model.cpp:1295-1446, its GPU branch): the MTP pass over the positions pos .. pos+n-1 of
  * its KV (n <= max_tokens), position i taking the embedding of toks[i] and hidden row i - hidden [n][hidden] on the
- * host, or NULL for the last verified batch's rows (gcuda_verify's `hidden`; n at most that batch's size) - then
+ * host, or NULL for the rows the device holds (the last verified batch's, the kept ones after gcuda_keep, or the row
+ * of gcuda_put_last_hidden; n at most their count) - then
  * draft = the first maximum of the last position's logits and prob (NULL: not wanted) its softmax probability
  * (softmax_at, engine/src/model.cpp:1287-1292); logits (NULL: not wanted) gets those logits (gcuda_draft_rows of
  * them: the vocabulary's, or the draft head's rows'). */
@@ -160,10 +161,17 @@ int gcuda_spec_reject(gcuda *g, const float *d_target, const float *d_draft, con
                       const gcuda_sampling *s, uint64_t seed, int *accepted, int *next);
 
 /* The conversation's state to and from the host, in the reference's own buffer layouts (engine/src/model.hpp:548-555):
- * conv [n_gdn][conv_dim][K-1] f32, gdn [n_gdn][nv][dv/16][dk][16] f32, kv [n_attn][2][positions][nkv*hd] int8,
- * kv_scale [n_attn][2][positions][nkv] f32 for positions 0..pos-1; pos the new position (put). */
+ * conv [n_gdn][conv_dim][K-1] f32, gdn [n_gdn][nv][dv/16][dk][16] f32, kv [A][2][positions][nkv*hd] int8,
+ * kv_scale [A][2][positions][nkv] f32 for positions 0..pos-1, A the attention layers and, with an MTP layer, its slot
+ * after them (engine/src/model.cpp:354: the engine counts it among n_attn); pos the new position (put). */
 int gcuda_state_get(gcuda *g, float *conv, float *gdn, int8_t *kv, float *kv_scale, int positions);
 int gcuda_state_put(gcuda *g, const float *conv, const float *gdn, const int8_t *kv, const float *kv_scale, int pos);
+/* The last position's hidden row after the final norm (the engine's last_hid_, which a state file keeps for the MTP
+ * layer, engine/src/state.cpp:275): the last verified batch's row n-1, or kept-1 after gcuda_keep. GCUDA_E_STATE when
+ * the device holds none (after gcuda_reset or gcuda_state_put). gcuda_put_last_hidden: that row given back after a
+ * gcuda_state_put (a loaded state's); a gcuda_draft with hidden NULL and n = 1 then takes it. */
+int gcuda_last_hidden(gcuda *g, float *out);
+int gcuda_put_last_hidden(gcuda *g, const float *row);
 
 /* Device pointers of the last batch's results (the verify step's outputs stay resident): logits [max_tokens][vocab]. */
 const float *gcuda_device_logits(gcuda *g);

@@ -88,7 +88,9 @@ int ghost_pack_summary(const char *dir, char *out, size_t out_len, char *err, si
  * header last; otherwise it is written whole to path.tmp, then renamed over path. ghost_state_load: the saved
  * conversation replaces this one; GHOST_E_FORMAT for another model's / format's / version's or a damaged file,
  * GHOST_E_ARG when it is longer than this model's context, GHOST_E_IO when unreadable or cut short; on failure the
- * conversation is empty. Packs with an MTP layer or a vision encoder: GHOST_E_ARG (save) / GHOST_E_FORMAT (load).
+ * conversation is empty. A pack with an MTP layer keeps that layer's KV rows and the last hidden row in the file (a
+ * load gives the row back to the device, so the next draft can take it); packs with a vision encoder: GHOST_E_ARG
+ * (save) / GHOST_E_FORMAT (load).
  * out_position (may be NULL): the conversation's length in tokens. */
 int ghost_state_save(ghost_model *m, const char *path, int32_t append, int32_t *out_position, char *err,
                      size_t err_len);
@@ -98,24 +100,29 @@ int ghost_state_load(ghost_model *m, const char *path, int32_t *out_position, ch
 int32_t ghost_pending(ghost_model *m);
 
 /* The state file alone, with host buffers (no GPU): what ghost_state_save / ghost_state_load write and read. Shapes:
- * n_attn attention layers, kv_heads, kv_row = kv_heads x head_dim, hidden, n_layers, conv_n and gdn_n floats of the
- * Gated DeltaNet conv and recurrent states. Buffers in the layouts of gcuda_state_get / gcuda_state_put: conv, gdn
- * the engine's own; kv [n_attn][2][position][kv_row] int8, kv_scale [n_attn][2][position][kv_heads] f32. */
+ * n_attn attention layers (with the MTP layer's slot, after them, when the pack has one), kv_heads, kv_row =
+ * kv_heads x head_dim, hidden, n_layers, conv_n and gdn_n floats of the Gated DeltaNet conv and recurrent states, mtp
+ * 1 when the pack has an MTP layer. Buffers in the layouts of gcuda_state_get / gcuda_state_put: conv, gdn the
+ * engine's own; kv [n_attn][2][position][kv_row] int8, kv_scale [n_attn][2][position][kv_heads] f32; hidden the last
+ * position's row after the final norm (the engine keeps it with an MTP layer; write: NULL for none, read: has_hidden
+ * says whether the file holds one). */
 typedef struct {
     uint32_t n_attn, kv_heads, kv_row, hidden, n_layers;
     uint64_t conv_n, gdn_n;
+    uint32_t mtp;
 } ghost_state_shapes;
 /* The fingerprint a state of this pack (geode.json in pack_dir) and these shapes carries (Model::fingerprint). */
 uint64_t ghost_state_fingerprint(const char *pack_dir, const ghost_state_shapes *s);
 int ghost_state_write(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t position,
                       int32_t extra, uint64_t conv_id, const float *conv, const float *gdn, const int8_t *kv,
-                      const float *kv_scale, int32_t append, char *err, size_t err_len);
+                      const float *kv_scale, const float *hidden, int32_t append, char *err, size_t err_len);
 /* The header, checked against the fingerprint, the shapes and context (position < context): position, extra and
  * conversation id out, to size the buffers of ghost_state_read. */
 int ghost_state_peek(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context,
                      int32_t *position, int32_t *extra, uint64_t *conv_id, char *err, size_t err_len);
 int ghost_state_read(const char *path, uint64_t fingerprint, const ghost_state_shapes *s, int32_t context, float *conv,
-                     float *gdn, int8_t *kv, float *kv_scale, char *err, size_t err_len);
+                     float *gdn, int8_t *kv, float *kv_scale, float *hidden, int32_t *has_hidden, char *err,
+                     size_t err_len);
 
 #ifdef __cplusplus
 }

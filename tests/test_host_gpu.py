@@ -168,11 +168,12 @@ def test_host_state_file(env, tmp_path):
     H.ghost_state_fingerprint.restype = C.c_uint64
     H.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
     H.ghost_state_write.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.c_int32, C.c_uint64,
-                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p, C.c_size_t]
+                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_char_p,
+                                    C.c_size_t]
     H.ghost_state_peek.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.POINTER(C.c_int32),
                                    C.POINTER(C.c_int32), C.POINTER(C.c_uint64), C.c_char_p, C.c_size_t]
     H.ghost_state_read.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), C.c_int32, C.c_void_p, C.c_void_p,
-                                   C.c_void_p, C.c_void_p, C.c_char_p, C.c_size_t]
+                                   C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int32), C.c_char_p, C.c_size_t]
     ora = op.Oracle(d)
     c = ora.cfg
     conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
@@ -191,7 +192,7 @@ def test_host_state_file(env, tmp_path):
     else:
         st0, kv0, kvs0 = _state(ora, prompt, shape.ctx)
         assert H.ghost_state_write(a.encode(), fp, C.byref(s), st0.pos, 0, 9, st0.conv.ctypes.data, st0.gdn.ctypes.data,
-                                   kv0.ctypes.data, kvs0.ctypes.data, 0, err, 512) == 0, err.value
+                                   kv0.ctypes.data, kvs0.ctypes.data, None, 0, err, 512) == 0, err.value
     pos = C.c_int32(0)
     assert H.ghost_state_load(m, a.encode(), C.byref(pos), err, 512) == 0, err.value
     assert pos.value == 260 and H.ghost_position(m) == 260 and H.ghost_pending(m) == 0
@@ -227,6 +228,83 @@ def test_host_state_file(env, tmp_path):
     open(str(tmp_path / "bad.state"), "wb").write(bad)
     assert H.ghost_state_load(m, str(tmp_path / "bad.state").encode(), C.byref(pos), err, 512) == 3
     assert H.ghost_position(m) == 0 and H.ghost_pending(m) == -1
+
+
+def test_host_state_file_mtp(tmp_path):
+    """A pack with the MTP layer through ghost_state_save / ghost_state_load: after five verified batches, each with
+    the MTP pass over its rows drafted from the device (hidden NULL), the saved file holds the model's and the MTP layer's KV and the last hidden row, which are the oracle's after the
+    same tokens within the parity tolerance; loaded back, a draft with hidden NULL takes the loaded row and equals
+    the draft made before the save from the file's row, bit for bit (the same kernels on the same state)."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from test_state_file import Shapes, _read
+    H = C.CDLL(HOST_SO)
+    vp, i32 = C.c_void_p, C.c_int32
+    H.ghost_open.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp), C.c_char_p, C.c_size_t]
+    H.ghost_close.argtypes = [vp]
+    H.ghost_position.argtypes = [vp]
+    H.ghost_verify.argtypes = [vp, vp, i32, vp, C.c_char_p, C.c_size_t]
+    H.ghost_draft.argtypes = [vp, vp, i32, i32, vp, C.POINTER(i32), C.POINTER(C.c_float), C.c_char_p, C.c_size_t]
+    H.ghost_state_save.argtypes = [vp, C.c_char_p, i32, C.POINTER(i32), C.c_char_p, C.c_size_t]
+    H.ghost_state_load.argtypes = [vp, C.c_char_p, C.POINTER(i32), C.c_char_p, C.c_size_t]
+    H.ghost_state_fingerprint.restype = C.c_uint64
+    H.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
+    H.ghost_state_peek.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), i32, C.POINTER(i32), C.POINTER(i32),
+                                   C.POINTER(C.c_uint64), C.c_char_p, C.c_size_t]
+    H.ghost_state_read.argtypes = [C.c_char_p, C.c_uint64, C.POINTER(Shapes), i32, vp, vp, vp, vp, vp, C.POINTER(i32),
+                                   C.c_char_p, C.c_size_t]
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d = str(tmp_path / "mtp")
+    synth.write_pack(d, shape, seed=81, mtp=True)
+    ora = op.Oracle(d)
+    c = ora.cfg
+    conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+    A, row = ora.n_attn + 1, c.n_kv_heads * c.head_dim
+    s = Shapes(A, c.n_kv_heads, row, c.hidden, c.n_layers, ora.n_gdn * conv_dim * (c.conv_kernel - 1),
+               ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim, 1)
+    fp = H.ghost_state_fingerprint(d.encode(), C.byref(s))
+    toks = np.random.default_rng(82).integers(0, shape.vocab, 26).astype(np.int32)
+    err = C.create_string_buffer(512)
+    m = C.c_void_p()
+    assert H.ghost_open(d.encode(), 0, shape.ctx, 5, C.byref(m), err, 512) == 0, err.value
+    try:
+        dh, ph = i32(0), C.c_float(0.0)
+        for p0 in range(0, 25, 5):
+            assert H.ghost_verify(m, toks[p0:].ctypes.data_as(vp), 5, None, err, 512) == 0, err.value
+            nxt = np.ascontiguousarray(toks[p0 + 1:p0 + 6])
+            assert H.ghost_draft(m, nxt.ctypes.data_as(vp), 5, p0, None, C.byref(dh), C.byref(ph), err, 512) == 0, \
+                err.value
+        a = str(tmp_path / "a.state")
+        pos = i32(0)
+        assert H.ghost_state_save(m, a.encode(), 0, C.byref(pos), err, 512) == 0, err.value
+        assert pos.value == 25
+        rc, e, got = _read(H, a, fp, s, shape.ctx, with_hidden=True)
+        assert rc == 0, e
+        P, extra, cid, conv, gdn, kv, kvs, hrow = got
+        assert P == 25 and hrow is not None
+        # the oracle after the same tokens (its hidden rows feed its MTP passes)
+        st = ora.new_state(shape.ctx)
+        hid = ora.forward(st, toks[:25], logits=False, hidden=True)["hidden"]
+        span = hid[24].max() - hid[24].min()
+        assert np.abs(hrow - hid[24]).max() <= 1e-2 * span
+        for p0 in range(0, 25, 5):
+            ora.forward_mtp(st, toks[p0 + 1:p0 + 6], hid[p0:p0 + 5], p0, logits=False)
+        kv_o = st.kv.reshape(A - 1, 2, shape.ctx, row)[:, :, :25]
+        assert np.abs(kv[:A - 1].astype(np.int32) - kv_o.astype(np.int32)).max() <= 2
+        mkv_o = st.mtp_kv.reshape(2, shape.ctx, row)[:, :25]
+        assert np.abs(kv[A - 1].astype(np.int32) - mkv_o.astype(np.int32)).max() <= 2
+        # the draft from the file's row, then loaded: the draft from the loaded row (hidden NULL) is the same
+        t25 = np.ascontiguousarray(toks[25:26])
+        d1, p1 = i32(0), C.c_float(0.0)
+        assert H.ghost_draft(m, t25.ctypes.data_as(vp), 1, 24, hrow.ctypes.data_as(vp), C.byref(d1), C.byref(p1), err,
+                             512) == 0, err.value
+        assert H.ghost_state_load(m, a.encode(), C.byref(pos), err, 512) == 0, err.value
+        assert pos.value == 25 and H.ghost_position(m) == 25
+        d2, p2 = i32(0), C.c_float(0.0)
+        assert H.ghost_draft(m, t25.ctypes.data_as(vp), 1, 24, None, C.byref(d2), C.byref(p2), err, 512) == 0, err.value
+        assert (d1.value, np.float32(p1.value)) == (d2.value, np.float32(p2.value))
+    finally:
+        H.ghost_close(m)
 
 
 def test_host_prefill(env):

@@ -165,3 +165,28 @@ def test_mtp_draft_head(arch, tmp_path):
         check(dg, pr, lg, lg_ref, f"chained draft {i}")
         tok, q = dg, q + 1
     be.close()
+
+
+def test_mtp_draft_after_keep(tmp_path):
+    """The engine's loop drafts from the rows a step kept (ghost_draft(..., NULL) after verify_keep): after
+    gcuda_keep(3) of a 5-row batch the device still holds rows 0..2, so a draft over 3 positions with hidden NULL
+    runs, and equals the same draft fed those rows from the host bit for bit; 4 rows are refused."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from geode_b200.backend import Backend, GcudaError
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d = str(tmp_path / "pack")
+    synth.write_pack(d, shape, seed=91, mtp=True)
+    be = Backend(d, context=shape.ctx, max_tokens=5)
+    rng = np.random.default_rng(92)
+    toks = rng.integers(0, shape.vocab, 10).astype(np.int32)
+    be.verify(toks[:5], logits=False)
+    _, hid = be.verify(toks[5:10], logits=False, hidden=True)
+    be.keep(3)
+    nxt = np.array([toks[6], toks[7], int(rng.integers(0, shape.vocab))], np.int32)
+    with pytest.raises(GcudaError):
+        be.draft(np.append(nxt, 1), 5)
+    d0, p0, lg0 = be.draft(nxt, 5, logits=True)
+    d1, p1, lg1 = be.draft(nxt, 5, hidden=hid[:3], logits=True)
+    assert (d0, np.float32(p0)) == (d1, np.float32(p1)) and np.array_equal(lg0, lg1)
+    be.close()

@@ -9,7 +9,9 @@ read, the format behind ghost_state_save / ghost_state_load).
   pack's manifest; made by tests/golden/make_golden.py);
 - round trip, append (in place: the same buffers back, gen 2, the earlier KV blocks kept), and the refusals: a
   damaged header, another model's fingerprint, a file cut short, an interrupted save, a state longer than the
-  context.
+  context;
+- a pack with the MTP layer, pinned to the reference the same way: its file counts the layer's KV slot among the
+  attention layers (after them) and the MTP flag in the fingerprint, and keeps the last hidden row (has_hidden).
 """
 import ctypes as C
 import os
@@ -29,7 +31,7 @@ OK, E_ARG, E_IO, E_FORMAT = 0, 1, 2, 3
 
 class Shapes(C.Structure):
     _fields_ = [("n_attn", C.c_uint32), ("kv_heads", C.c_uint32), ("kv_row", C.c_uint32), ("hidden", C.c_uint32),
-                ("n_layers", C.c_uint32), ("conv_n", C.c_uint64), ("gdn_n", C.c_uint64)]
+                ("n_layers", C.c_uint32), ("conv_n", C.c_uint64), ("gdn_n", C.c_uint64), ("mtp", C.c_uint32)]
 
 
 @pytest.fixture(scope="module")
@@ -40,10 +42,12 @@ def H():
     vp, i32, u64, sz = C.c_void_p, C.c_int32, C.c_uint64, C.c_size_t
     L.ghost_state_fingerprint.restype = u64
     L.ghost_state_fingerprint.argtypes = [C.c_char_p, C.POINTER(Shapes)]
-    L.ghost_state_write.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, i32, u64, vp, vp, vp, vp, i32, C.c_char_p, sz]
+    L.ghost_state_write.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, i32, u64, vp, vp, vp, vp, vp, i32,
+                                    C.c_char_p, sz]
     L.ghost_state_peek.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, C.POINTER(i32), C.POINTER(i32),
                                    C.POINTER(u64), C.c_char_p, sz]
-    L.ghost_state_read.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, vp, vp, vp, vp, C.c_char_p, sz]
+    L.ghost_state_read.argtypes = [C.c_char_p, u64, C.POINTER(Shapes), i32, vp, vp, vp, vp, vp, C.POINTER(i32),
+                                   C.c_char_p, sz]
     return L
 
 
@@ -75,15 +79,16 @@ def _p(a):
     return a.ctypes.data
 
 
-def _write(H, path, fp, s, st, kv, kvs, conv_id=77, extra=-1, append=0):
+def _write(H, path, fp, s, st, kv, kvs, conv_id=77, extra=-1, append=0, hidden=None):
     err = C.create_string_buffer(256)
     rc = H.ghost_state_write(path.encode(), fp, C.byref(s), st.pos, extra, conv_id, _p(st.conv), _p(st.gdn), _p(kv),
-                             _p(kvs), append, err, 256)
+                             _p(kvs), None if hidden is None else _p(hidden), append, err, 256)
     assert rc == OK, err.value
     return rc
 
 
-def _read(H, path, fp, s, context):
+def _read(H, path, fp, s, context, with_hidden=False):
+    """(rc, error, (position, extra, conversation id, conv, gdn, kv, kv scales[, the hidden row or None]))"""
     err = C.create_string_buffer(256)
     pos, extra, cid = C.c_int32(0), C.c_int32(0), C.c_uint64(0)
     rc = H.ghost_state_peek(path.encode(), fp, C.byref(s), context, C.byref(pos), C.byref(extra), C.byref(cid), err, 256)
@@ -94,8 +99,11 @@ def _read(H, path, fp, s, context):
     gdn = np.zeros(max(1, s.gdn_n), np.float32)
     kv = np.zeros((s.n_attn, 2, P, s.kv_row), np.int8)
     kvs = np.zeros((s.n_attn, 2, P, s.kv_heads), np.float32)
-    rc = H.ghost_state_read(path.encode(), fp, C.byref(s), context, _p(conv), _p(gdn), _p(kv), _p(kvs), err, 256)
-    return rc, err.value.decode(), (P, extra.value, cid.value, conv, gdn, kv, kvs)
+    hid, has = np.zeros(s.hidden, np.float32), C.c_int32(-1)
+    rc = H.ghost_state_read(path.encode(), fp, C.byref(s), context, _p(conv), _p(gdn), _p(kv), _p(kvs), _p(hid),
+                            C.byref(has), err, 256)
+    out = (P, extra.value, cid.value, conv, gdn, kv, kvs)
+    return rc, err.value.decode(), out + ((hid if has.value == 1 else None),) if with_hidden else out
 
 
 def test_roundtrip_append_and_refusals(H, model, tmp_path):
@@ -222,6 +230,67 @@ def test_golden_state_file(H, tmp_path):
     assert np.array_equal(kv, kv_o) and np.array_equal(kvs, kvs_o)
     out = str(tmp_path / "again.state")
     err = C.create_string_buffer(256)
-    assert H.ghost_state_write(out.encode(), fp, C.byref(s), P, extra, cid, _p(conv), _p(gdn), _p(kv), _p(kvs), 0, err,
-                               256) == OK, err.value
+    assert H.ghost_state_write(out.encode(), fp, C.byref(s), P, extra, cid, _p(conv), _p(gdn), _p(kv), _p(kvs), None, 0,
+                               err, 256) == OK, err.value
     assert open(out, "rb").read() == state
+
+
+@ref_only
+def test_mtp_state_pinned_to_the_reference(H, tmp_path):
+    """A pack with the MTP layer: the reference (drafting on, so its model binds the layer) after a 40-token prompt and
+    the MTP layer over the prompt's positions saves a file whose KV holds the main attention layers then the MTP
+    layer's slot, and the last position's hidden row; it reads here as the oracle's state after the same prompt and
+    passes (the MTP slot's written rows the oracle's MTP KV) with the reference's own hidden row; written again here
+    from those buffers it is the same bytes; a file written here loads into the reference, whose next MTP position
+    then equals the oracle's bit for bit."""
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d = str(tmp_path / "pack")
+    synth.write_pack(d, shape, seed=9, mtp=True)
+    ora = op.Oracle(d)
+    c = ora.cfg
+    conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+    A, row, heads = ora.n_attn + 1, c.n_kv_heads * c.head_dim, c.n_kv_heads
+    s = Shapes(A, heads, row, c.hidden, c.n_layers, ora.n_gdn * conv_dim * (c.conv_kernel - 1),
+               ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim, 1)
+    s0 = Shapes(A, heads, row, c.hidden, c.n_layers, s.conv_n, s.gdn_n, 0)
+    fp = H.ghost_state_fingerprint(d.encode(), C.byref(s))
+    assert fp != H.ghost_state_fingerprint(d.encode(), C.byref(s0))   # (the MTP flag is in the fingerprint)
+    toks = np.random.default_rng(10).integers(0, shape.vocab, 60).astype(np.int32)
+    P = 40
+    ref = op.Reference(d, ctx=shape.ctx, draft=True)
+    try:
+        ref.forward(toks[:P], all_logits=False)
+        hid = ref.hidden_rows(P)
+        st = ora.new_state(shape.ctx)
+        ora.forward(st, toks[:P], logits=False)
+        for p0 in range(0, P - 1, 5):
+            p1 = min(p0 + 5, P - 1)
+            ref.mtp(toks[p0 + 1:p1 + 1], hid[p0:p1], p0, logits=False)
+            ora.forward_mtp(st, toks[p0 + 1:p1 + 1], hid[p0:p1], p0, logits=False)
+        a = str(tmp_path / "ref.state")
+        ref.save_state(a)
+        rc, e, got = _read(H, a, fp, s, shape.ctx, with_hidden=True)
+        assert rc == OK, e
+        pos, extra, cid, conv, gdn, kv, kvs, hrow = got
+        assert pos == P and extra == 0
+        assert hrow is not None and np.array_equal(hrow, hid[P - 1])
+        assert np.array_equal(conv[:st.conv.size], st.conv) and np.array_equal(gdn[:st.gdn.size], st.gdn)
+        kv_o = st.kv.reshape(A - 1, 2, shape.ctx, row)[:, :, :P]
+        kvs_o = st.kvs.reshape(A - 1, 2, shape.ctx, heads)[:, :, :P]
+        assert np.array_equal(kv[:A - 1], kv_o) and np.array_equal(kvs[:A - 1], kvs_o)
+        # the MTP slot's rows the passes wrote (positions 0 .. P-2; the engine's forward never writes that slot, so the
+        # row at P-1 holds whatever its cache held there - the next MTP pass writes it before anything reads it)
+        assert np.array_equal(kv[A - 1][:, :P - 1], st.mtp_kv.reshape(2, shape.ctx, row)[:, :P - 1])
+        assert np.array_equal(kvs[A - 1][:, :P - 1], st.mtp_kvs.reshape(2, shape.ctx, heads)[:, :P - 1])
+        # written here from those buffers (the reference's conversation id): the same bytes
+        b = str(tmp_path / "ours.state")
+        _write(H, b, fp, s, st, kv, kvs, conv_id=cid, extra=0, hidden=hrow)
+        assert open(a, "rb").read() == open(b, "rb").read()
+        # ours loads into the reference, which drafts the next position as the oracle does
+        ref.load_state(b)
+        assert ref.pos == P
+        lg_r, mh_r = ref.mtp(toks[P:P + 1], hrow[None], P - 1)
+        lg_o, mh_o = ora.forward_mtp(st, toks[P:P + 1], hrow[None], P - 1)
+        assert np.array_equal(lg_r, lg_o) and np.array_equal(mh_r, mh_o)
+    finally:
+        ref.close()
