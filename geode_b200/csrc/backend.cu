@@ -708,8 +708,8 @@ int record_graphs(gcuda *g) {
     return GCUDA_OK;
 }
 
-// the status word's verdict once its copy in h_status has landed
-int status_verdict(gcuda *g, uint32_t st) {
+// the status word's outcome once its copy in h_status has landed
+int status_outcome(gcuda *g, uint32_t st) {
     if (st) {
         cudaMemsetAsync(g->d_status, 0, 4, g->st);
         std::string why;
@@ -724,7 +724,7 @@ int status_verdict(gcuda *g, uint32_t st) {
 int check_status(gcuda *g) {
     LAUNCH_OK(cudaMemcpyAsync(g->h_status, g->d_status, 4, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
-    return status_verdict(g, *g->h_status);
+    return status_outcome(g, *g->h_status);
 }
 
 }  // namespace
@@ -1246,7 +1246,7 @@ int gcuda_verify_device(gcuda *g, const int *d_toks, int n) {
     if (d_toks != g->d_toks) LAUNCH_OK(cudaMemcpyAsync(g->d_toks, d_toks, sizeof(int) * n, cudaMemcpyDeviceToDevice, g->st));
     RC_OK(enqueue_verify(g, n));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
-    RC_OK(status_verdict(g, *g->h_status));
+    RC_OK(status_outcome(g, *g->h_status));
     cudaEventElapsedTime(&g->last_ms, g->ev0, g->ev1);
     LAUNCH_OK(cudaMemcpy(g->last_toks, g->d_toks, sizeof(int) * n, cudaMemcpyDeviceToHost));
     g->pos += n;
@@ -1271,7 +1271,7 @@ int gcuda_verify(gcuda *g, const int *toks, int n, float *logits, float *hidden)
     if (logits) LAUNCH_OK(cudaMemcpyAsync(logits, g->logits, sizeof(float) * n * g->sh.vocab, cudaMemcpyDeviceToHost, g->st));
     if (hidden) LAUNCH_OK(cudaMemcpyAsync(hidden, g->hid, sizeof(float) * n * g->sh.hidden, cudaMemcpyDeviceToHost, g->st));
     LAUNCH_OK(cudaStreamSynchronize(g->st));
-    RC_OK(status_verdict(g, *g->h_status));
+    RC_OK(status_outcome(g, *g->h_status));
     cudaEventElapsedTime(&g->last_ms, g->ev0, g->ev1);
     std::memcpy(g->last_toks, toks, sizeof(int) * n);
     g->pos += n;
