@@ -65,3 +65,21 @@ def test_broken_packs(H, tmp_path):
     open(man, "w").write(json.dumps(m))
     assert H.ghost_pack_summary(d.encode(), out, 512, err, 512) != 0
     assert b"past its file" in err.value
+
+
+def test_draft_vocab(tmp_path):
+    """The draft vocabulary as the engine's GPU branch takes it (engine/src/model.cpp:2135-2161), which the Python
+    binding and the C++ host both follow: the int32 ids inside the vocabulary in file order, padded to whole tiles of
+    32 rows with copies of the first; no file, or no id inside the vocabulary: no draft head."""
+    from geode_b200.backend import draft_vocab
+    d = str(tmp_path)
+    assert draft_vocab(d, 1024) is None
+    synth.write_draft_vocab(d, [-5, 2000])
+    assert draft_vocab(d, 1024) is None
+    synth.write_draft_vocab(d, [7, -1, 1023, 1024, 3] + list(range(100, 130)))
+    ids = draft_vocab(d, 1024)
+    want = [7, 1023, 3] + list(range(100, 130))
+    assert ids.dtype == np.int32 and len(ids) == 64
+    assert list(ids[:len(want)]) == want and (ids[len(want):] == 7).all()
+    synth.write_draft_vocab(d, list(range(64)))
+    assert list(draft_vocab(d, 1024)) == list(range(64))
