@@ -12,11 +12,14 @@ restatement, so tests/test_oracle.py pins the restatement to the reference where
   pack (written by geode_b200/synth.py with the seed stored), every logit and the per-layer trace;
 - state_file.npz: Model::save_state's file (engine/src/state.cpp) after a 20-token prompt on a tiny synthetic pack,
   with that pack's geode.json (the state's fingerprint hashes it) and the shapes the state records;
+- state_file_mtp.npz: the same on a pack with the MTP layer (the model opened with drafting on), after the prompt and
+  the MTP layer over all its positions (the last one fed the token after the prompt): the file with the layer's KV
+  slot and the last hidden row, the reference's hidden rows and that next token;
 - mtp_moe.npz / mtp_dense.npz: the MTP drafting layer (Model::forward_mtp, engine/src/model.cpp:4965-5039) on a tiny
   pack with one: the main model's hidden rows after a prompt, the MTP pass over the prompt's positions (logits and
   normed output of the last), then one chained position fed its own draft.
 
-Run with names (kernels, accept, accept_seen, model, state, mtp) to regenerate only those fixtures.
+Run with names (kernels, accept, accept_seen, model, state, state_mtp, mtp) to regenerate only those fixtures.
 """
 import ctypes as C
 import os
@@ -185,6 +188,31 @@ def state_file(seed=31):
                         manifest=manifest, state=state)
 
 
+def state_file_mtp(seed=33):
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    with tempfile.TemporaryDirectory() as d:
+        synth.write_pack(d, shape, seed=seed, mtp=True)
+        ref = op.Reference(d, threads=1, ctx=shape.ctx, draft=True)
+        toks = np.random.default_rng(seed + 1).integers(0, shape.vocab, 21).astype(np.int32)
+        prompt, nxt = toks[:20], int(toks[20])
+        ref.forward(prompt, all_logits=False)
+        hid = ref.hidden_rows(len(prompt))
+        ref.mtp(np.append(prompt[1:], nxt), hid, 0, logits=False)   # (every position's MTP KV row written)
+        path = os.path.join(d, "s.state")
+        ref.save_state(path)
+        ref.close()
+        ora = op.Oracle(d)
+        c = ora.cfg
+        conv_dim = 2 * c.gdn_k_heads * c.gdn_k_dim + c.gdn_v_heads * c.gdn_v_dim
+        shapes = np.array([ora.n_attn + 1, c.n_kv_heads, c.n_kv_heads * c.head_dim, c.hidden, c.n_layers,
+                           ora.n_gdn * conv_dim * (c.conv_kernel - 1),
+                           ora.n_gdn * c.gdn_v_heads * c.gdn_k_dim * c.gdn_v_dim, 1], np.uint64)
+        manifest = np.frombuffer(open(os.path.join(d, "geode.json"), "rb").read(), np.uint8)
+        state = np.frombuffer(open(path, "rb").read(), np.uint8)
+    np.savez_compressed(os.path.join(OUT, "state_file_mtp.npz"), seed=seed, prompt=prompt, next=nxt, hidden=hid,
+                        shapes=shapes, manifest=manifest, state=state)
+
+
 def mtp(arch, name, seed=41):
     shape = synth.tiny_shape(arch, n_layers=4, ctx=640)
     with tempfile.TemporaryDirectory() as d:
@@ -205,7 +233,7 @@ if __name__ == "__main__":
     if not op.have_reference():
         sys.exit("build the reference first: make -C oracle ref")
     R = op.reference_lib()
-    which = set(sys.argv[1:]) or {"kernels", "accept", "accept_seen", "model", "state", "mtp"}
+    which = set(sys.argv[1:]) or {"kernels", "accept", "accept_seen", "model", "state", "state_mtp", "mtp"}
     if "kernels" in which:
         kernels(R)
     if "accept" in which:
@@ -217,6 +245,8 @@ if __name__ == "__main__":
         model("qwen35", "model_dense")
     if "state" in which:
         state_file()
+    if "state_mtp" in which:
+        state_file_mtp()
     if "mtp" in which:
         mtp("qwen35moe", "mtp_moe")
         mtp("qwen35", "mtp_dense")

@@ -294,3 +294,48 @@ def test_mtp_state_pinned_to_the_reference(H, tmp_path):
         assert np.array_equal(lg_r, lg_o) and np.array_equal(mh_r, mh_o)
     finally:
         ref.close()
+
+
+def test_golden_state_file_mtp(H, tmp_path):
+    """Without the reference build, for a pack with the MTP layer: tests/golden/state_file_mtp.npz holds the file the
+    reference engine (drafting on) saved after a 20-token prompt and the MTP layer over all its positions, with the
+    pack's geode.json and the reference's hidden rows. The fingerprint computed here (the MTP flag in it) equals the
+    file's; the file reads here as the oracle's state after the same prompt and passes - the MTP slot after the model's
+    attention layers - with the reference's last hidden row; written again here, it is the same bytes."""
+    g = np.load(os.path.join(ROOT, "tests", "golden", "state_file_mtp.npz"))
+    state = g["state"].tobytes()
+    d = tmp_path / "pack"
+    d.mkdir()
+    (d / "geode.json").write_bytes(g["manifest"].tobytes())
+    s = Shapes(*[int(x) for x in g["shapes"]])
+    assert s.mtp == 1
+    fp = H.ghost_state_fingerprint(str(d).encode(), C.byref(s))
+    assert fp == int.from_bytes(state[16:24], "little")
+    path = str(tmp_path / "golden.state")
+    open(path, "wb").write(state)
+    rc, e, got = _read(H, path, fp, s, 640, with_hidden=True)
+    assert rc == OK, e
+    P, extra, cid, conv, gdn, kv, kvs, hrow = got
+    prompt, hid = g["prompt"], g["hidden"]
+    assert (P, extra) == (len(prompt), 0)
+    assert hrow is not None and np.array_equal(hrow, hid[-1])
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d2 = str(tmp_path / "again")
+    synth.write_pack(d2, shape, seed=int(g["seed"]), mtp=True)
+    assert open(os.path.join(d2, "geode.json"), "rb").read() == g["manifest"].tobytes()
+    ora = op.Oracle(d2)
+    st = ora.new_state(shape.ctx)
+    ora.forward(st, prompt, logits=False)
+    ora.forward_mtp(st, np.append(prompt[1:], int(g["next"])), hid, 0, logits=False)
+    c = ora.cfg
+    A, row, heads = s.n_attn, c.n_kv_heads * c.head_dim, c.n_kv_heads
+    assert np.array_equal(conv[:st.conv.size], st.conv) and np.array_equal(gdn[:st.gdn.size], st.gdn)
+    assert np.array_equal(kv[:A - 1], st.kv.reshape(A - 1, 2, shape.ctx, row)[:, :, :P])
+    assert np.array_equal(kvs[:A - 1], st.kvs.reshape(A - 1, 2, shape.ctx, heads)[:, :, :P])
+    assert np.array_equal(kv[A - 1], st.mtp_kv.reshape(2, shape.ctx, row)[:, :P])
+    assert np.array_equal(kvs[A - 1], st.mtp_kvs.reshape(2, shape.ctx, heads)[:, :P])
+    out = str(tmp_path / "again.state")
+    err = C.create_string_buffer(256)
+    assert H.ghost_state_write(out.encode(), fp, C.byref(s), P, extra, cid, _p(conv), _p(gdn), _p(kv), _p(kvs),
+                                     _p(hrow), 0, err, 256) == OK, err.value
+    assert open(out, "rb").read() == state
