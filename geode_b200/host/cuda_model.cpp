@@ -360,10 +360,24 @@ bool CudaModel::prefill(const int *toks, int n, std::string &err) {
         err = "prefill: no tokens";
         return false;
     }
+    // with the MTP layer, as the engine's prompt (engine/src/geode.cpp:132-150): after each chunk the layer over the
+    // previous chunk's last position and the chunk's own but its last (each fed the token after it), so its KV holds
+    // every prompt position but the last; that one's row stays for the first draft (gcuda_put_last_hidden: a draft of
+    // the pending token at position n - 1 with hidden NULL takes it). A failed MTP pass only ends them, as there.
+    bool spec = has_mtp_;
+    std::vector<float> prev;
+    const int H = static_cast<int>(shapes_.hidden);
     for (int i = 0; i < n; i += max_tokens_) {
-        const int k = std::min(max_tokens_, n - i);
+        const int k = std::min(max_tokens_, n - i), p0 = position();
         if (api_.verify(g_, toks + i, k, nullptr, nullptr) != 0) return fail("prefill", err);
+        if (!spec) continue;
+        int d = 0;
+        if (!prev.empty() && api_.draft(g_, toks + i, 1, p0 - 1, prev.data(), &d, nullptr, nullptr) != 0) spec = false;
+        if (spec && k > 1 && api_.draft(g_, toks + i + 1, k - 1, p0, nullptr, &d, nullptr, nullptr) != 0) spec = false;
+        prev.resize(static_cast<size_t>(H));
+        if (spec && api_.last_hidden(g_, prev.data()) != 0) spec = false;
     }
+    if (spec && !prev.empty() && api_.put_last_hidden(g_, prev.data()) != 0) return fail("prefill", err);
     last_n_ = 0;   // (nothing to accept or keep: the prompt is all kept)
     return true;
 }

@@ -62,8 +62,10 @@ int ghost_draft_next(ghost_model *m, int32_t tok, int32_t pos, int32_t *draft, f
 int ghost_reset(ghost_model *m, char *err, size_t err_len);
 /* geode_prefill (engine/include/geode/geode.h:166-169): the prompt's n tokens appended to the conversation, nothing
  * generated. It runs through the verify step, max_tokens positions a launch (correct at any length; not a tensor-core
- * prefill). A token id out of range or a prompt past the context: GHOST_E_ARG, the conversation then holds the
- * batches before the failing one. */
+ * prefill). With an MTP layer the layer runs over the prompt's positions too, as the engine's prompt does
+ * (engine/src/geode.cpp:132-150), all but the last, whose row the device keeps for the first draft:
+ * ghost_draft(m, &pending, 1, position - 1, NULL, ...). A token id out of range or a prompt past the context:
+ * GHOST_E_ARG, the conversation then holds the batches before the failing one. */
 int ghost_prefill(ghost_model *m, const int32_t *prompt, int32_t n, char *err, size_t err_len);
 /* Model::verify_keep: keep the first `kept` rows of the last batch (1 <= kept < n; with every row kept, no call) */
 int ghost_keep(ghost_model *m, int32_t kept, char *err, size_t err_len);

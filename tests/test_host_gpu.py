@@ -307,6 +307,60 @@ def test_host_state_file_mtp(tmp_path):
         H.ghost_close(m)
 
 
+def test_host_prefill_mtp(tmp_path):
+    """ghost_prefill on a pack with the MTP layer runs the layer over the prompt as the engine's prompt does
+    (engine/src/geode.cpp:132-150): the first draft afterwards - the pending token at the last position, hidden NULL -
+    equals the Python binding's replay of the same calls bit for bit, and its logits are the oracle's (its MTP passes
+    over every prompt position fed the GPU's hidden rows) within the parity tolerance."""
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    from geode_b200.backend import Backend
+    H = C.CDLL(HOST_SO)
+    vp, i32 = C.c_void_p, C.c_int32
+    H.ghost_open.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp), C.c_char_p, C.c_size_t]
+    H.ghost_close.argtypes = [vp]
+    H.ghost_prefill.argtypes = [vp, vp, i32, C.c_char_p, C.c_size_t]
+    H.ghost_draft.argtypes = [vp, vp, i32, i32, vp, C.POINTER(i32), C.POINTER(C.c_float), C.c_char_p, C.c_size_t]
+    shape = synth.tiny_shape("qwen35moe", n_layers=4, ctx=640)
+    d = str(tmp_path / "mtp")
+    synth.write_pack(d, shape, seed=83, mtp=True)
+    toks = np.random.default_rng(84).integers(0, shape.vocab, 24).astype(np.int32)
+    P = 23
+    err = C.create_string_buffer(512)
+    m = C.c_void_p()
+    assert H.ghost_open(d.encode(), 0, shape.ctx, 5, C.byref(m), err, 512) == 0, err.value
+    try:
+        assert H.ghost_prefill(m, toks.ctypes.data_as(vp), P, err, 512) == 0, err.value
+        dh, ph = i32(0), C.c_float(0.0)
+        nxt = np.ascontiguousarray(toks[P:P + 1])
+        assert H.ghost_draft(m, nxt.ctypes.data_as(vp), 1, P - 1, None, C.byref(dh), C.byref(ph), err, 512) == 0, \
+            err.value
+    finally:
+        H.ghost_close(m)
+    # the same calls through the Python binding
+    be = Backend(d, context=shape.ctx, max_tokens=5)
+    hid = np.zeros((P, shape.hidden), np.float32)
+    for i in range(0, P, 5):
+        k = min(5, P - i)
+        _, hid[i:i + k] = be.verify(toks[i:i + k], logits=False, hidden=True)
+        if i:
+            be.draft(toks[i:i + 1], i - 1, hidden=hid[i - 1:i])
+        if k > 1:
+            be.draft(toks[i + 1:i + k], i)
+    dp, pp, lg = be.draft(nxt, P - 1, hidden=hid[P - 1:P], logits=True)
+    be.close()
+    assert (dh.value, np.float32(ph.value)) == (dp, np.float32(pp)), (dh.value, dp, ph.value, pp)
+    # the oracle: its MTP passes over the prompt's positions with the GPU's rows, then the draft position
+    ora = op.Oracle(d)
+    st = ora.new_state(shape.ctx)
+    ora.forward(st, toks[:P], logits=False)
+    for p0 in range(0, P - 1, 5):
+        p1 = min(p0 + 5, P - 1)
+        ora.forward_mtp(st, toks[p0 + 1:p1 + 1], hid[p0:p1], p0, logits=False)
+    want, _ = ora.forward_mtp(st, nxt, hid[P - 1:P], P - 1)
+    assert np.abs(lg - want).max() <= 1e-2 * (want.max() - want.min())
+
+
 def test_host_prefill(env):
     """ghost_prefill (geode_prefill's counterpart): a 23-token prompt in through the verify step, then a batch whose
     logits match the oracle's after the same prompt within the parity tolerance; a token out of range is refused."""
